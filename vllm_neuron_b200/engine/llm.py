@@ -1,0 +1,132 @@
+"""``LLM``: the offline entry point, with vLLM's constructor arguments and
+``generate`` signature for the supported features."""
+
+from __future__ import annotations
+
+import os
+import socket
+from typing import Sequence
+
+import torch.multiprocessing as mp
+
+from ..config import EngineConfig
+from ..logging_config import init_logger
+from .llm_engine import LLMEngine, _follower_main
+from .sampling_params import RequestOutput, SamplingParams
+
+logger = init_logger(__name__)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+class LLM:
+    """Example::
+
+        llm = LLM(model="/path/to/gpt-oss-120b", tensor_parallel_size=8, max_model_len=8192,
+                  additional_config={"neuron_config": {"quantization": "mxfp4"}})
+        outs = llm.generate(prompt_token_ids=[[1, 2, 3]], sampling_params=SamplingParams(max_tokens=32))
+
+    ``model`` may also be omitted when ``hf_config`` (a config.json dict) is given;
+    ``load_format="dummy"`` initialises random weights.  Under ``torchrun`` (``RANK``
+    and ``WORLD_SIZE`` set) every rank constructs an ``LLM`` with ``spmd=True`` and
+    submits the same requests; otherwise ``tensor_parallel_size > 1`` spawns the
+    follower ranks itself."""
+
+    def __init__(self, model: str | None = None, spmd: bool = False, tokenizer: str | None = None, **kwargs):
+        cfg = EngineConfig.create(model=model, **kwargs)
+        self.cfg = cfg
+        ws = cfg.world_size
+        self._procs = []
+        if spmd or (ws > 1 and "RANK" in os.environ and int(os.environ.get("WORLD_SIZE", "1")) == ws):
+            rank = int(os.environ.get("RANK", "0"))
+            local = int(os.environ.get("LOCAL_RANK", rank))
+            self.engine = LLMEngine(cfg, rank, ws, local, mode="spmd" if ws > 1 else "single")
+        elif ws > 1:
+            port = _free_port()
+            os.environ["MASTER_ADDR"] = "127.0.0.1"
+            os.environ["MASTER_PORT"] = str(port)
+            ctx = mp.get_context("spawn")
+            for r in range(1, ws):
+                p = ctx.Process(target=_follower_main, args=(cfg, r, ws, port), daemon=True)
+                p.start()
+                self._procs.append(p)
+            self.engine = LLMEngine(cfg, 0, ws, 0, mode="driver")
+        else:
+            self.engine = LLMEngine(cfg, 0, 1, 0, mode="single")
+        self._tok = None
+        self._tok_path = tokenizer or model
+        self._counter = 0
+
+    # ----------------------------------------------------------------- tokenizer
+    def get_tokenizer(self):
+        if self._tok is None:
+            if not self._tok_path:
+                raise ValueError("no tokenizer available: pass prompt_token_ids")
+            from transformers import AutoTokenizer
+
+            self._tok = AutoTokenizer.from_pretrained(self._tok_path)
+        return self._tok
+
+    # ------------------------------------------------------------------ generate
+    def generate(self, prompts: Sequence[str] | str | None = None,
+                 sampling_params: SamplingParams | Sequence[SamplingParams] | None = None,
+                 prompt_token_ids: Sequence[Sequence[int]] | None = None, use_tqdm: bool = False,
+                 multi_modal_data: Sequence[dict] | None = None) -> list[RequestOutput]:
+        if prompt_token_ids is None:
+            if prompts is None:
+                raise ValueError("either prompts or prompt_token_ids is required")
+            if isinstance(prompts, str):
+                prompts = [prompts]
+            if prompts and isinstance(prompts[0], dict):  # {"prompt_token_ids": [...]} items
+                prompt_token_ids = [p["prompt_token_ids"] for p in prompts]
+                multi_modal_data = [p.get("multi_modal_data") for p in prompts]
+                prompts = None
+            else:
+                tok = self.get_tokenizer()
+                prompt_token_ids = [tok.encode(p) for p in prompts]
+        n = len(prompt_token_ids)
+        if sampling_params is None:
+            sampling_params = SamplingParams()
+        sps = list(sampling_params) if isinstance(sampling_params, (list, tuple)) else [sampling_params] * n
+        ids = []
+        for i, ptoks in enumerate(prompt_token_ids):
+            rid = f"req-{self._counter}"
+            self._counter += 1
+            mm = multi_modal_data[i] if multi_modal_data else None
+            self.engine.add_request(rid, list(ptoks), sps[i], prompt=prompts[i] if prompts else None,
+                                    mm_inputs=[mm] if mm else None)
+            ids.append(rid)
+        results: dict[str, RequestOutput] = {}
+        while self.engine.has_unfinished_requests():
+            for o in self.engine.step():
+                if o.finished:
+                    results[o.request_id] = o
+        outs = [results[r] for r in ids]
+        if self._tok is not None or (self._tok_path and os.path.exists(os.path.join(self._tok_path,
+                                                                                    "tokenizer.json"))):
+            try:
+                tok = self.get_tokenizer()
+                for o in outs:
+                    o.outputs[0].text = tok.decode(o.outputs[0].token_ids)
+            except Exception:  # noqa: BLE001
+                pass
+        return outs
+
+    def shutdown(self) -> None:
+        self.engine.shutdown()
+        for p in self._procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.terminate()
+        self._procs = []
+
+    def __del__(self):  # pragma: no cover
+        try:
+            if self._procs:
+                self.shutdown()
+        except Exception:
+            pass

@@ -1,0 +1,161 @@
+"""The engine: request intake, scheduling, execution, output assembly.
+
+Multi-GPU execution is SPMD: every rank runs the same scheduler on the same
+request stream and therefore issues the same collectives in the same order (the
+lockstep invariant the reference protects with its DP MAX-reduce,
+``neuron_model_runner.py:2756-2801``).  Three modes:
+* ``single``   one rank;
+* ``driver``   rank 0 of a multi-process group owns the user API and broadcasts
+               new requests / aborts to the followers before every step
+               (CPU gloo group);
+* ``follower`` ranks 1..N-1 of a driver group, looping on :meth:`step`;
+* ``spmd``     every rank is launched externally (torchrun) and receives the same
+               requests itself (used by ``bench.py``).
+"""
+
+from __future__ import annotations
+
+import os
+import time
+import uuid
+from typing import Any
+
+from ..config import EngineConfig
+from ..logging_config import init_logger
+from .block_manager import KVCacheManager
+from .request import Request, RequestStatus
+from .sampling_params import CompletionOutput, RequestOutput, SamplingParams
+from .scheduler import Scheduler
+from .worker import Worker
+
+logger = init_logger(__name__)
+
+
+class LLMEngine:
+    def __init__(self, cfg: EngineConfig, rank: int = 0, world_size: int = 1, local_rank: int = 0,
+                 mode: str = "single"):
+        self.cfg = cfg
+        self.rank, self.world_size, self.mode = rank, world_size, mode
+        self.worker = Worker(cfg, rank, world_size, local_rank)
+        self.worker.init_device()
+        self.worker.load_model()
+        n_blocks = self.worker.determine_num_blocks()
+        self.worker.initialize_cache(n_blocks)
+        self.worker.warmup()
+        self.num_blocks = n_blocks
+        self.kv = KVCacheManager(n_blocks, cfg.block_size, cfg.enable_prefix_caching)
+        k = cfg.speculative_config.num_speculative_tokens if cfg.speculative_config else 0
+        self.scheduler = Scheduler(self.kv, cfg.max_num_seqs, cfg.max_num_batched_tokens, cfg.max_model_len,
+                                   cfg.max_num_prefills_per_step, cfg.enable_chunked_prefill, k)
+        hf = self.worker.hf
+        self.eos_token_id = hf.get("eos_token_id")
+        self._pending: list[tuple] = []
+        self._stopped = False
+        self.proposer = None
+        if cfg.speculative_config is not None:
+            from ..spec_decode.eagle import EagleProposer
+
+            self.proposer = EagleProposer(cfg, self.worker)
+        logger.info("engine ready: rank %d/%d mode=%s kv_blocks=%d", rank, world_size, mode, n_blocks)
+
+    # ------------------------------------------------------------------ intake
+    def add_request(self, request_id: str | None, prompt_token_ids: list[int], sampling_params: SamplingParams,
+                    prompt: str | None = None, mm_inputs: list | None = None,
+                    kv_transfer_params: dict | None = None) -> str:
+        rid = request_id or uuid.uuid4().hex
+        req = Request(rid, list(map(int, prompt_token_ids)), sampling_params, self.eos_token_id, prompt,
+                      mm_inputs=mm_inputs, kv_transfer_params=kv_transfer_params)
+        if self.mode == "driver":
+            self._pending.append(("add", rid, req.prompt_token_ids, sampling_params, prompt, mm_inputs,
+                                  kv_transfer_params))
+        self.scheduler.add_request(req)
+        return rid
+
+    def abort_request(self, request_id: str) -> None:
+        if self.mode == "driver":
+            self._pending.append(("abort", request_id))
+        self.scheduler.abort(request_id)
+
+    def has_unfinished_requests(self) -> bool:
+        return self.scheduler.has_unfinished()
+
+    # -------------------------------------------------------------------- step
+    def _sync_requests(self) -> None:
+        if self.mode not in ("driver", "follower"):
+            return
+        msgs = self.worker.ps.world.broadcast_object(self._pending if self.rank == 0 else None)
+        self._pending = []
+        if self.mode == "follower":
+            for m in msgs:
+                if m[0] == "add":
+                    _, rid, ids, sp, prompt, mm, kvp = m
+                    self.scheduler.add_request(Request(rid, ids, sp, self.eos_token_id, prompt, mm_inputs=mm,
+                                                       kv_transfer_params=kvp))
+                elif m[0] == "abort":
+                    self.scheduler.abort(m[1])
+                elif m[0] == "shutdown":
+                    self._stopped = True
+
+    def step(self) -> list[RequestOutput]:
+        self._sync_requests()
+        if self._stopped:
+            return []
+        so = self.scheduler.schedule()
+        if so.kind == "idle":
+            return []
+        if self.proposer is not None and so.kind == "decode":
+            sampled = self.proposer.execute_with_speculation(so)
+        else:
+            sampled = self.worker.execute_model(so)
+        now = time.monotonic()
+        finished = self.scheduler.update_from_output(so, sampled, now)
+        if self.proposer is not None:
+            self.proposer.propose(so, sampled, self.scheduler)
+        outs = []
+        fin_ids = {r.request_id for r in finished}
+        for s in so.seqs:
+            if s.req_id in sampled or s.req_id in fin_ids:
+                req = s.request
+                outs.append(self._make_output(req, req.status.finished))
+        return outs
+
+    def _make_output(self, req: Request, finished: bool) -> RequestOutput:
+        reason = None
+        if req.status == RequestStatus.FINISHED_STOPPED:
+            reason = "stop"
+        elif req.status == RequestStatus.FINISHED_LENGTH:
+            reason = "length"
+        elif req.status == RequestStatus.FINISHED_ABORTED:
+            reason = "abort"
+        return RequestOutput(req.request_id, req.prompt, req.prompt_token_ids,
+                             [CompletionOutput(0, "", list(req.output_token_ids), reason)], finished,
+                             req.metrics, req.num_cached_tokens)
+
+    # ---------------------------------------------------------------- lifecycle
+    def run_follower(self) -> None:
+        while not self._stopped:
+            self.step()
+
+    def shutdown(self) -> None:
+        if self.mode == "driver" and not self._stopped:
+            self._pending.append(("shutdown",))
+            self._sync_requests()
+        self._stopped = True
+        self.worker.shutdown()
+
+    # -------------------------------------------------------------- statistics
+    def stats(self) -> dict[str, Any]:
+        return {"kv_usage": self.kv.usage, "num_blocks": self.num_blocks,
+                "running": len(self.scheduler.running), "waiting": len(self.scheduler.waiting),
+                "h2d_bytes_last": self.worker.runner.h2d_bytes_last,
+                "d2h_bytes_last": self.worker.runner.d2h_bytes_last}
+
+
+def _follower_main(cfg: EngineConfig, rank: int, world_size: int, master_port: int) -> None:
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(master_port)
+    eng = LLMEngine(cfg, rank, world_size, local_rank=rank, mode="follower")
+    try:
+        eng.run_follower()
+    finally:
+        eng.worker.shutdown()

@@ -1,0 +1,321 @@
+"""Per-step execution: input preparation, model forward, sampling.
+
+Counterpart of the Trainium plugin's ``NeuronModelRunner``
+(``vllm_neuron/vllm/worker/neuron_model_runner.py:378``), designed for CUDA:
+* inputs (token ids, positions, slot mapping, block tables, sequence lengths,
+  sampling parameters) are assembled with numpy in pinned host buffers and copied
+  to persistent device buffers with one async H2D copy each;
+* decode steps replay a CUDA graph captured per ``num_seqs_buckets`` batch size
+  (the counterpart of the reference's per-bucket NEFFs) covering model forward,
+  LM head and sampling; the graph's only host traffic is the inputs and the
+  sampled token ids;
+* prefill steps (including segmented prefill and prefix-cache hits) run eagerly
+  over the flat token batch; attention reads prior context from the paged cache;
+* the KV cache is one (K, V) pair of ``[num_blocks, kv_heads, block_size, head_dim]``
+  tensors per layer (HND, ``vllm/attention/attn.py:27-35``).
+"""
+
+from __future__ import annotations
+
+import hashlib
+import math
+import struct
+import time
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from .. import envs
+from ..config import EngineConfig
+from ..logging_config import init_logger
+from ..metrics import GRAPH_REPLAY_COUNT, NUM_SEQS_PADDING
+from ..nn.sampler import Sampler
+from ..ops.metadata import AttentionMetadata
+from ..utils.bucket_utils import get_bucket_for_count, get_default_num_seqs_buckets, validate_buckets
+from .scheduler import SchedulerOutput
+
+logger = init_logger(__name__)
+
+
+def request_uniform(seed: int, req_id: str, seq: int) -> float:
+    """Deterministic U[0,1) per (seed, request, sample index), identical on every rank."""
+    h = hashlib.blake2b(f"{seed}:{req_id}:{seq}".encode(), digest_size=8).digest()
+    return (struct.unpack("<Q", h)[0] >> 11) * (1.0 / (1 << 53))
+
+
+@dataclass
+class _GraphEntry:
+    graph: torch.cuda.CUDAGraph
+    batch: int
+
+
+class ModelRunner:
+    def __init__(self, cfg: EngineConfig, model: torch.nn.Module, device: torch.device, tp_group,
+                 vocab_size: int):
+        self.cfg = cfg
+        self.model = model
+        self.device = device
+        self.bs = cfg.block_size
+        self.max_model_len = cfg.max_model_len
+        self.max_blocks = math.ceil(cfg.max_model_len / cfg.block_size)
+        nc = cfg.neuron_config
+        buckets = nc.num_seqs_buckets or nc.decode_batch_buckets
+        self.decode_buckets = (validate_buckets("num_seqs_buckets", buckets, cfg.max_num_seqs) if buckets
+                               else get_default_num_seqs_buckets(cfg.max_num_seqs))
+        ods = nc.on_device_sampling_config
+        self.max_top_k = ods.max_top_k if ods is not None else 256
+        self.all_greedy_cfg = bool(ods and ods.all_greedy)
+        lm = model.lm_head
+        self.sampler = Sampler(tp_group, lm.start, vocab_size, self.max_top_k)
+        self.use_graphs = (device.type == "cuda" and not cfg.enforce_eager and not envs.VLLM_B200_DISABLE_CUDA_GRAPHS)
+        self.kv_caches: list[tuple[torch.Tensor, torch.Tensor]] = []
+        self.num_blocks = 0
+        self.graphs: dict[tuple[int, bool], _GraphEntry] = {}
+        self.graph_pool = None
+        self.seed = cfg.seed
+        T = max(cfg.max_num_batched_tokens, cfg.max_num_seqs * (1 + self._num_spec()))
+        B = max(cfg.max_num_seqs, 1)
+        self.max_tokens = T
+        pin = device.type == "cuda"
+        mk = lambda shape, dt: torch.zeros(shape, dtype=dt, pin_memory=pin)  # noqa: E731
+        # pinned host staging buffers
+        self.h_ids = mk(T, torch.int64)
+        self.h_pos = mk(T, torch.int64)
+        self.h_slot = mk(T, torch.int64)
+        self.h_qsl = mk(B + 1, torch.int32)
+        self.h_seqlen = mk(B, torch.int32)
+        self.h_bt = mk((B, self.max_blocks), torch.int32)
+        self.h_lidx = mk(B * (1 + self._num_spec()), torch.int64)
+        self.h_temp = mk(B, torch.float32)
+        self.h_topk = mk(B, torch.int32)
+        self.h_topp = mk(B, torch.float32)
+        self.h_unif = mk(B, torch.float32)
+        self.h_out = mk(B * (1 + self._num_spec()), torch.int64)
+        # persistent device buffers (graph inputs)
+        d = device
+        self.d_ids = torch.zeros(T, dtype=torch.int64, device=d)
+        self.d_pos = torch.zeros(T, dtype=torch.int64, device=d)
+        self.d_slot = torch.full((T,), -1, dtype=torch.int64, device=d)
+        self.d_qsl = torch.zeros(B + 1, dtype=torch.int32, device=d)
+        self.d_seqlen = torch.zeros(B, dtype=torch.int32, device=d)
+        self.d_bt = torch.zeros(B, self.max_blocks, dtype=torch.int32, device=d)
+        self.d_lidx = torch.zeros(B * (1 + self._num_spec()), dtype=torch.int64, device=d)
+        self.d_temp = torch.zeros(B, dtype=torch.float32, device=d)
+        self.d_topk = torch.zeros(B, dtype=torch.int32, device=d)
+        self.d_topp = torch.ones(B, dtype=torch.float32, device=d)
+        self.d_unif = torch.zeros(B, dtype=torch.float32, device=d)
+        self.d_out = torch.zeros(B * (1 + self._num_spec()), dtype=torch.int64, device=d)
+        self.workspace: torch.Tensor | None = None
+        self.h2d_bytes_last = 0
+        self.d2h_bytes_last = 0
+        self.step_count = 0
+
+    def _num_spec(self) -> int:
+        sc = self.cfg.speculative_config
+        return sc.num_speculative_tokens if sc is not None else 0
+
+    # ------------------------------------------------------------------ KV cache
+    def initialize_kv_cache(self, num_blocks: int) -> None:
+        spec = self.model.get_kv_spec()
+        self.kv_caches = []
+        for l in spec.layers:
+            if l.kind != "attention":
+                self.kv_caches.append(None)
+                continue
+            shape = (num_blocks, l.num_kv_heads, self.bs, l.head_dim)
+            self.kv_caches.append((torch.zeros(shape, dtype=l.dtype, device=self.device),
+                                   torch.zeros(shape, dtype=l.dtype, device=self.device)))
+        self.num_blocks = num_blocks
+        # split-KV decode scratch: [B, Hq_local, splits, d + 2] fp32 partials
+        hq = max((getattr(layer, "self_attn", None).nq if hasattr(layer, "self_attn") else 0)
+                 for layer in getattr(self.model, "layers", [])) if hasattr(self.model, "layers") else 0
+        d = max((l.head_dim for l in spec.layers), default=64)
+        if self.device.type == "cuda" and hq:
+            self.workspace = torch.empty(self.cfg.max_num_seqs * max(hq, 1) * self.max_splits(1) * (d + 2),
+                                         dtype=torch.float32, device=self.device)
+        self._hq = hq
+
+    def max_splits(self, batch: int) -> int:
+        return 32
+
+    def num_splits_for(self, batch: int) -> int:
+        """Split-KV factor so that batch x kv_heads x splits covers the SMs ~2 times."""
+        if self.device.type != "cuda":
+            return 1
+        spec = self.model.get_kv_spec()
+        hkv = max(1, max(l.num_kv_heads for l in spec.layers))
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        want = max(1, math.ceil(2 * sms / (batch * hkv)))
+        return int(min(self.max_splits(batch), want))
+
+    # ------------------------------------------------------------------ inputs
+    def _fill_sampling(self, so: SchedulerOutput, B: int) -> bool:
+        all_greedy = True
+        for i, s in enumerate(so.seqs):
+            sp = s.sampling_params
+            t = 0.0 if sp is None else float(sp.temperature)
+            if self.all_greedy_cfg:
+                t = 0.0
+            self.h_temp[i] = t
+            self.h_topk[i] = 0 if sp is None or sp.top_k <= 0 else sp.top_k
+            self.h_topp[i] = 1.0 if sp is None else sp.top_p
+            seed = self.seed if sp is None or sp.seed is None else sp.seed
+            self.h_unif[i] = request_uniform(seed, s.req_id, s.sample_seq) if t > 0 else 0.0
+            all_greedy &= t <= 0
+        n = len(so.seqs)
+        if B > n:
+            self.h_temp[n:B] = 0
+            self.h_topk[n:B] = 0
+            self.h_topp[n:B] = 1
+            self.h_unif[n:B] = 0
+        return all_greedy
+
+    def _prepare(self, so: SchedulerOutput, pad_to: int | None) -> tuple[AttentionMetadata, int, int, bool]:
+        seqs = so.seqs
+        n = len(seqs)
+        B = pad_to or n
+        ids = self.h_ids.numpy()
+        pos = self.h_pos.numpy()
+        slot = self.h_slot.numpy()
+        qsl = self.h_qsl.numpy()
+        sl = self.h_seqlen.numpy()
+        bt = self.h_bt.numpy()
+        lidx = self.h_lidx.numpy()
+        t = 0
+        qsl[0] = 0
+        max_q, max_s = 1, 1
+        n_sel = 0
+        for i, s in enumerate(seqs):
+            k = len(s.token_ids)
+            ids[t:t + k] = s.token_ids
+            p = np.arange(s.start_pos, s.start_pos + k)
+            pos[t:t + k] = p
+            blocks = np.asarray(s.block_ids, dtype=np.int64)
+            slot[t:t + k] = blocks[p // self.bs] * self.bs + p % self.bs
+            nb = len(s.block_ids)
+            bt[i, :nb] = s.block_ids
+            bt[i, nb:] = 0
+            sl[i] = s.seq_len
+            if so.kind == "decode" and s.spec_token_ids:
+                lidx[n_sel:n_sel + k] = np.arange(t, t + k)
+                n_sel += k
+            else:
+                lidx[n_sel] = t + k - 1
+                n_sel += 1
+            t += k
+            qsl[i + 1] = t
+            max_q = max(max_q, k)
+            max_s = max(max_s, s.seq_len)
+        T = t
+        if B > n:  # decode padding rows: no KV write, no keys
+            ids[T:T + (B - n)] = 0
+            pos[T:T + (B - n)] = 0
+            slot[T:T + (B - n)] = -1
+            sl[n:B] = 0
+            bt[n:B] = 0
+            for j in range(n, B):
+                qsl[j + 1] = qsl[j] + 1
+                lidx[n_sel] = T + (j - n)
+                n_sel += 1
+            T += B - n
+        greedy = self._fill_sampling(so, B)
+        # H2D: one async copy per buffer from pinned memory
+        nb_ = 0
+        for h, dv, cnt in ((self.h_ids, self.d_ids, T), (self.h_pos, self.d_pos, T), (self.h_slot, self.d_slot, T),
+                           (self.h_qsl, self.d_qsl, B + 1), (self.h_seqlen, self.d_seqlen, B),
+                           (self.h_lidx, self.d_lidx, n_sel), (self.h_temp, self.d_temp, B),
+                           (self.h_topk, self.d_topk, B), (self.h_topp, self.d_topp, B),
+                           (self.h_unif, self.d_unif, B)):
+            dv[:cnt].copy_(h[:cnt], non_blocking=True)
+            nb_ += cnt * h.element_size()
+        max_nb = max(1, max(math.ceil(s.seq_len / self.bs) for s in seqs)) if seqs else 1
+        self.d_bt[:B, :max_nb].copy_(self.h_bt[:B, :max_nb], non_blocking=True)
+        nb_ += B * max_nb * 4
+        self.h2d_bytes_last = nb_
+        meta = AttentionMetadata(
+            num_tokens=T, num_seqs=B, is_decode=(so.kind == "decode" and max_q == 1),
+            query_start_loc=self.d_qsl[:B + 1], seq_lens=self.d_seqlen[:B], block_tables=self.d_bt[:B],
+            slot_mapping=self.d_slot[:T], logits_indices=self.d_lidx[:n_sel], max_query_len=max_q,
+            max_seq_len=max_s, workspace=self.workspace, num_splits=self.num_splits_for(B))
+        return meta, T, n_sel, greedy
+
+    # ------------------------------------------------------------------ forward
+    def _forward_sample(self, meta: AttentionMetadata, T: int, n_sel: int, greedy: bool) -> torch.Tensor:
+        h = self.model(self.d_ids[:T], self.d_pos[:T], meta, self.kv_caches)
+        hs = h if (meta.is_decode and n_sel == T) else h.index_select(0, meta.logits_indices)
+        logits = self.model.compute_logits(hs)
+        B = meta.num_seqs
+        if n_sel == B:
+            tok = self.sampler(logits, self.d_temp[:B], self.d_topk[:B], self.d_topp[:B], self.d_unif[:B], greedy)
+        else:  # speculative verification: greedy at every position
+            tok = self.sampler.greedy(logits)
+        self.d_out[:n_sel].copy_(tok)
+        self._last_logits = logits
+        return self.d_out[:n_sel]
+
+    @torch.inference_mode()
+    def execute(self, so: SchedulerOutput) -> dict[str, list[int]]:
+        if so.kind == "idle" or not so.seqs:
+            return {}
+        self.step_count += 1
+        n = len(so.seqs)
+        pad_to = None
+        is_plain_decode = so.kind == "decode" and all(len(s.token_ids) == 1 for s in so.seqs)
+        if is_plain_decode:
+            pad_to = get_bucket_for_count(n, self.decode_buckets) if self.use_graphs else n
+            NUM_SEQS_PADDING.labels(model_name=self.cfg.served_model_name or "model").observe(pad_to - n)
+        meta, T, n_sel, greedy = self._prepare(so, pad_to)
+        if is_plain_decode and self.use_graphs:
+            key = (pad_to, greedy)
+            entry = self.graphs.get(key)
+            if entry is None:
+                entry = self._capture(pad_to, greedy, meta, T, n_sel)
+            entry.graph.replay()
+            GRAPH_REPLAY_COUNT.labels(model_name=self.cfg.served_model_name or "model",
+                                      bucket_name=f"decode_b{pad_to}").inc()
+            out_d = self.d_out[:n_sel]
+        else:
+            out_d = self._forward_sample(meta, T, n_sel, greedy)
+        # D2H of the sampled ids (the step's only device->host traffic)
+        self.h_out[:n_sel].copy_(out_d, non_blocking=out_d.is_cuda)
+        if out_d.is_cuda:
+            torch.cuda.current_stream().synchronize()
+        self.d2h_bytes_last = n_sel * 8
+        toks = self.h_out[:n_sel].tolist()
+        res: dict[str, list[int]] = {}
+        if so.kind == "decode" and any(s.spec_token_ids for s in so.seqs):
+            off = 0
+            for s in so.seqs:
+                k = len(s.token_ids)
+                res[s.req_id] = toks[off:off + k]
+                off += k
+            return res
+        for i, s in enumerate(so.seqs):
+            if s.sample:
+                res[s.req_id] = [toks[i]]
+        return res
+
+    def _capture(self, B: int, greedy: bool, meta: AttentionMetadata, T: int, n_sel: int) -> _GraphEntry:
+        t0 = time.time()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):  # warm-up outside the graph (cuBLAS/NCCL init)
+                self._forward_sample(meta, T, n_sel, greedy)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        if self.graph_pool is None:
+            self.graph_pool = torch.cuda.graph_pool_handle()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, pool=self.graph_pool):
+            self._forward_sample(meta, T, n_sel, greedy)
+        torch.cuda.synchronize()
+        e = _GraphEntry(g, B)
+        self.graphs[(B, greedy)] = e
+        logger.info("captured decode graph batch=%d greedy=%s in %.2fs", B, greedy, time.time() - t0)
+        return e
+
+    def release_graphs(self) -> None:
+        self.graphs.clear()
+        self.graph_pool = None

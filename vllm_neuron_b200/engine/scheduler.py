@@ -1,0 +1,248 @@
+"""Continuous-batching scheduler.
+
+Policy (restated from the Trainium plugin's ``NeuronScheduler``,
+``vllm_neuron/vllm/core/scheduler.py:78-906``):
+* a step is either all-prefill or all-decode; while a prefill is pending the decode
+  requests are held back (``scheduler.py:821-854``);
+* at most ``max_num_prefills_per_step`` prompts per prefill step (the reference fixes
+  it at 1, ``:201``; the default here is the same);
+* long prompts are prefilled in segments of at most ``max_num_batched_tokens``
+  (segmented prefill), earlier segments land in the paged cache and later ones
+  attend to them;
+* KV admission control: no new prompt is admitted while the running set could,
+  at worst-case length ``max_model_len``, exhaust the cache (``:556-580``), so decode
+  never preempts decode in steady state; if it still runs out of blocks the newest
+  running request is preempted and recomputed later;
+* decode batches are padded to the ``num_seqs_buckets`` graph sizes by the runner;
+  the padding is recorded in the ``num_seqs_padding`` histogram.
+
+Every rank runs this scheduler on the same inputs and reaches the same decisions,
+which keeps the ranks' collectives in lockstep without broadcasting schedules.
+"""
+
+from __future__ import annotations
+
+import time
+from collections import deque
+from dataclasses import dataclass, field
+
+from ..logging_config import init_logger
+from .block_manager import KVCacheManager
+from .request import Request, RequestStatus
+
+logger = init_logger(__name__)
+
+
+@dataclass
+class ScheduledSeq:
+    req_id: str
+    token_ids: list[int]  # tokens whose K/V are computed this step
+    start_pos: int  # position of token_ids[0]
+    block_ids: list[int]
+    sample: bool  # sample a token after this step
+    spec_token_ids: list[int] = field(default_factory=list)
+    sampling_params: object = None
+    sample_seq: int = 0
+    mm_inputs: list | None = None
+    request: Request | None = None
+
+    @property
+    def seq_len(self) -> int:
+        return self.start_pos + len(self.token_ids)
+
+
+@dataclass
+class SchedulerOutput:
+    kind: str  # "prefill" | "decode" | "idle"
+    seqs: list[ScheduledSeq]
+    preempted: list[str] = field(default_factory=list)
+    finished: list[str] = field(default_factory=list)
+
+    @property
+    def num_tokens(self) -> int:
+        return sum(len(s.token_ids) for s in self.seqs)
+
+
+class Scheduler:
+    def __init__(self, kv: KVCacheManager, max_num_seqs: int, max_num_batched_tokens: int, max_model_len: int,
+                 max_num_prefills_per_step: int = 1, enable_chunked_prefill: bool = True,
+                 num_spec_tokens: int = 0):
+        self.kv = kv
+        self.max_num_seqs = max_num_seqs
+        self.max_num_batched_tokens = max_num_batched_tokens
+        self.max_model_len = max_model_len
+        self.max_prefills = max_num_prefills_per_step
+        self.chunked = enable_chunked_prefill
+        self.num_spec_tokens = num_spec_tokens
+        self.waiting: deque[Request] = deque()
+        self.running: list[Request] = []
+        self.requests: dict[str, Request] = {}
+        blocks_per_max = -(-max_model_len // kv.block_size)
+        self.max_kv_concurrent = max(1, (kv.pool.num_blocks - 1) // blocks_per_max)
+        self._finished_ids: list[str] = []
+
+    # ------------------------------------------------------------------ queue
+    def add_request(self, req: Request) -> None:
+        if req.num_prompt_tokens >= self.max_model_len:
+            raise ValueError(f"prompt of {req.num_prompt_tokens} tokens exceeds max_model_len {self.max_model_len}")
+        if req.num_prompt_tokens == 0:
+            raise ValueError("empty prompt")
+        self.requests[req.request_id] = req
+        self.waiting.append(req)
+
+    def abort(self, req_id: str) -> None:
+        req = self.requests.get(req_id)
+        if req is None or req.status.finished:
+            return
+        req.status = RequestStatus.FINISHED_ABORTED
+        self._finish(req)
+
+    def has_unfinished(self) -> bool:
+        return bool(self.waiting or self.running)
+
+    def _finish(self, req: Request) -> None:
+        if req in self.running:
+            self.running.remove(req)
+        try:
+            self.waiting.remove(req)
+        except ValueError:
+            pass
+        self.kv.free(req)
+        req.metrics.finished_time = time.monotonic()
+        self._finished_ids.append(req.request_id)
+        self.requests.pop(req.request_id, None)
+
+    # --------------------------------------------------------------- schedule
+    def _is_prefill(self, r: Request) -> bool:
+        return r.num_computed_tokens < r.num_prompt_tokens
+
+    def can_admit(self) -> bool:
+        if len(self.running) >= self.max_num_seqs:
+            return False
+        if any(self._is_prefill(r) for r in self.running):
+            return False
+        return len(self.running) < self.max_kv_concurrent
+
+    def schedule(self) -> SchedulerOutput:
+        finished, self._finished_ids = self._finished_ids, []
+        # 1) ongoing segmented prefills first
+        pre = [r for r in self.running if self._is_prefill(r)]
+        # 2) admit new prompts when no prefill is in flight
+        if not pre:
+            admitted = 0
+            while self.waiting and admitted < self.max_prefills and self.can_admit():
+                req = self.waiting[0]
+                blocks, n_cached = self.kv.get_computed_blocks(req)
+                req.num_computed_tokens = n_cached
+                req.num_cached_tokens = n_cached
+                n_new = self._prefill_chunk(req)
+                if not self.kv.allocate_slots(req, n_new, blocks):
+                    req.num_computed_tokens = 0
+                    break
+                self.waiting.popleft()
+                req.status = RequestStatus.RUNNING
+                if req.metrics.first_scheduled_time is None:
+                    req.metrics.first_scheduled_time = time.monotonic()
+                self.running.append(req)
+                pre.append(req)
+                admitted += 1
+                if self._budget_left(pre) <= 0:
+                    break
+        if pre:
+            seqs = []
+            budget = self.max_num_batched_tokens
+            for req in pre:
+                if budget <= 0:
+                    break
+                n = min(self._prefill_chunk(req), budget)
+                if not self.kv.allocate_slots(req, n):
+                    break
+                budget -= n
+                s = req.num_computed_tokens
+                done = s + n >= req.num_tokens
+                seqs.append(ScheduledSeq(req.request_id, req.all_token_ids[s:s + n], s, req.block_ids, done,
+                                         sampling_params=req.sampling_params, sample_seq=req.sample_seq,
+                                         mm_inputs=req.mm_inputs, request=req))
+            if seqs:
+                return SchedulerOutput("prefill", seqs, finished=finished)
+        # 3) decode step over every running request
+        seqs, preempted = [], []
+        k = self.num_spec_tokens
+        running = list(self.running)
+        i = 0
+        while i < len(running):
+            req = running[i]
+            n_new = 1 + len(req.spec_token_ids[:k])
+            if not self.kv.allocate_slots(req, n_new):
+                # preempt the newest request and retry
+                victim = running.pop()
+                self._preempt(victim)
+                preempted.append(victim.request_id)
+                if victim is req:
+                    continue
+                continue
+            i += 1
+        for req in running:
+            spec = req.spec_token_ids[:k]
+            s = req.num_computed_tokens
+            toks = [req.all_token_ids[s]] + spec if s < req.num_tokens else spec
+            seqs.append(ScheduledSeq(req.request_id, toks, s, req.block_ids, True, spec_token_ids=spec,
+                                     sampling_params=req.sampling_params, sample_seq=req.sample_seq, request=req))
+        if not seqs:
+            return SchedulerOutput("idle", [], preempted, finished)
+        return SchedulerOutput("decode", seqs, preempted, finished)
+
+    def _budget_left(self, pre: list[Request]) -> int:
+        return self.max_num_batched_tokens - sum(self._prefill_chunk(r) for r in pre)
+
+    def _prefill_chunk(self, req: Request) -> int:
+        remaining = req.num_tokens - req.num_computed_tokens
+        if self.chunked:
+            return min(remaining, self.max_num_batched_tokens)
+        if remaining > self.max_num_batched_tokens:
+            raise ValueError("prompt exceeds max_num_batched_tokens and chunked prefill is disabled")
+        return remaining
+
+    def _preempt(self, req: Request) -> None:
+        self.running.remove(req)
+        self.kv.free(req)
+        req.num_computed_tokens = 0
+        req.spec_token_ids = []
+        req.status = RequestStatus.PREEMPTED
+        self.waiting.appendleft(req)
+        logger.warning("preempted request %s (KV cache full)", req.request_id)
+
+    # ----------------------------------------------------------------- update
+    def update_from_output(self, out: SchedulerOutput, sampled: dict[str, list[int]],
+                           now: float | None = None) -> list[Request]:
+        """Advance request state after a step.  ``sampled[req_id]`` holds the accepted
+        tokens (1 without speculation; 1..k+1 with).  Returns requests that finished."""
+        now = now or time.monotonic()
+        done = []
+        for s in out.seqs:
+            req = self.requests.get(s.req_id)
+            if req is None:
+                continue
+            if out.kind == "prefill":
+                req.num_computed_tokens += len(s.token_ids)
+            if not s.sample:
+                self.kv.cache_full_blocks(req)
+                continue
+            toks = sampled.get(s.req_id, [])
+            if out.kind == "decode":
+                # tokens computed = the input token + accepted drafts
+                req.num_computed_tokens += max(1, len(toks)) if s.spec_token_ids else 1
+            req.spec_token_ids = []
+            for t in toks:
+                req.output_token_ids.append(int(t))
+                req.sample_seq += 1
+                if req.metrics.first_token_time is None:
+                    req.metrics.first_token_time = now
+                req.metrics.token_times.append(now)
+                if req.check_stop(self.max_model_len):
+                    break
+            self.kv.cache_full_blocks(req)
+            if req.status.finished:
+                done.append(req)
+                self._finish(req)
+        return done

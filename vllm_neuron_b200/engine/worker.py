@@ -1,0 +1,156 @@
+"""One worker per GPU: device and process-group set-up, model load, KV budget,
+warm-up (decode graph capture) and step execution.
+
+Counterpart of ``NeuronWorker`` (``vllm_neuron/vllm/worker/neuron_worker.py:188``):
+* the KV budget is what is left after weights and an activation reserve at the
+  configured ``gpu_memory_utilization``, min-reduced over ranks so every rank
+  allocates the same number of blocks, and must reach ``VLLM_B200_MIN_KV_BUDGET_GIB``
+  (fail fast, ``neuron_worker.py:777-787``);
+* warm-up captures one CUDA graph per decode bucket (``VLLM_B200_SKIP_DECODE_WARMUP``
+  skips it; graphs are then captured lazily on first use).
+"""
+
+from __future__ import annotations
+
+import math
+import os
+import time
+
+import torch
+
+from .. import envs
+from ..config import EngineConfig, load_hf_config
+from ..logging_config import init_logger
+from ..metrics import MODEL_LOAD_SIZE, MODEL_LOAD_TIME, STARTUP_TIME
+from ..models.base import random_init_, random_init_device_
+from ..models.registry import resolve
+from ..parallel import state as pstate
+from .model_runner import ModelRunner
+
+logger = init_logger(__name__)
+
+
+def build_model(cfg: EngineConfig, ps, device: torch.device, hf: dict | None = None):
+    hf = hf if hf is not None else (cfg.hf_config if isinstance(cfg.hf_config, dict) else load_hf_config(cfg.model))
+    model_cls, config_cls = resolve(hf)
+    mcfg = config_cls.from_hf(hf, quantization=cfg.neuron_config.quantization)
+    dtype = torch.bfloat16 if cfg.dtype in ("bfloat16", "bf16", "auto") else (
+        torch.float32 if cfg.dtype in ("float32", "fp32") else torch.float16)
+    kv_dtype = torch.float8_e4m3fn if cfg.kv_dtype_is_fp8 else dtype
+    model = model_cls(mcfg, ps, dtype=dtype, device=device, kv_dtype=kv_dtype)
+    return model, mcfg, hf
+
+
+class Worker:
+    def __init__(self, cfg: EngineConfig, rank: int = 0, world_size: int = 1, local_rank: int = 0):
+        self.cfg = cfg
+        self.rank = rank
+        self.world_size = world_size
+        self.local_rank = local_rank
+        self.device = torch.device("cpu")
+        self.model = None
+        self.runner: ModelRunner | None = None
+        self.ps = None
+
+    def init_device(self) -> None:
+        t0 = time.time()
+        dev = self.cfg.resolve_device()
+        if dev == "cuda":
+            torch.cuda.set_device(self.local_rank)
+            self.device = torch.device("cuda", self.local_rank)
+        pstate.init_distributed_environment(self.world_size, self.rank, local_rank=self.local_rank,
+                                            timeout_s=float(envs.VLLM_B200_BARRIER_TIMEOUT))
+        nc = self.cfg.neuron_config
+        self.ps = pstate.initialize_parallel_state(
+            tp=self.cfg.tensor_parallel_size, dp=self.cfg.data_parallel_size,
+            ep_degree=nc.ep_degree, attention_dp_size=nc.attention_dp_size,
+            embedding_dp_size=nc.embedding_dp_size, lm_head_dp_size=nc.lm_head_dp_size,
+            mlp_dp_size=nc.mlp_dp_size, dcp=self.cfg.decode_context_parallel_size,
+            vision_tp=self.cfg.vision_neuron_config.tp_size, vision_dp=self.cfg.vision_neuron_config.dp_size,
+            timeout_s=float(envs.VLLM_B200_BARRIER_TIMEOUT))
+        if self.device.type == "cuda" and self.world_size > 1 and envs.VLLM_B200_FUSED_COLLECTIVES:
+            from ..parallel.communicator import attach_communicators
+
+            attach_communicators(self.ps, self.device)
+        self._t_start = t0
+
+    def load_model(self) -> None:
+        t0 = time.time()
+        torch.manual_seed(self.cfg.seed)
+        model, mcfg, hf = build_model(self.cfg, self.ps, self.device)
+        if self.cfg.load_format == "dummy" or self.cfg.model is None:
+            if self.device.type == "cuda":
+                random_init_device_(model, self.cfg.seed)
+            else:
+                random_init_(model, self.cfg.seed)
+        else:
+            from ..utils.checkpoints import SafetensorsCheckpoint
+
+            ck = SafetensorsCheckpoint(self.cfg.model)
+            model.load_weights(((k, v.to(self.device) if v.numel() > (1 << 20) else v) for k, v in ck))
+        self.model = model.eval()
+        self.model_cfg = mcfg
+        self.hf = hf
+        nbytes = sum(p.numel() * p.element_size() for p in model.parameters())
+        name = self.cfg.served_model_name or str(self.cfg.model)
+        MODEL_LOAD_TIME.labels(model_name=name).set(time.time() - t0)
+        MODEL_LOAD_SIZE.labels(model_name=name).set(nbytes)
+        vocab = getattr(mcfg, "vocab_size", None) or hf.get("vocab_size")
+        self.runner = ModelRunner(self.cfg, model, self.device, self.ps.tp, vocab)
+        logger.info("rank %d loaded model (%.2f GB) in %.1fs", self.rank, nbytes / 1e9, time.time() - t0)
+
+    def determine_num_blocks(self) -> int:
+        spec = self.model.get_kv_spec()
+        per_block = max(1, spec.bytes_per_block(self.cfg.block_size))
+        need = self.cfg.max_num_seqs * math.ceil(self.cfg.max_model_len / self.cfg.block_size) + 1
+        if self.cfg.num_gpu_blocks_override:
+            n = int(self.cfg.num_gpu_blocks_override)
+        elif self.device.type == "cuda":
+            free, total = torch.cuda.mem_get_info(self.device)
+            used = total - free
+            reserve = (3 << 30) + self.runner.max_tokens * (getattr(self.model_cfg, "hidden_size", 4096) * 64)
+            budget = total * self.cfg.gpu_memory_utilization - used - reserve
+            min_b = envs.VLLM_B200_MIN_KV_BUDGET_GIB * (1 << 30)
+            if budget < min_b:
+                raise RuntimeError(f"KV budget {budget / 2**30:.2f} GiB below the minimum "
+                                   f"{envs.VLLM_B200_MIN_KV_BUDGET_GIB} GiB; lower max_model_len / max_num_seqs "
+                                   "or raise gpu_memory_utilization")
+            n = int(budget // per_block)
+            if not self.cfg.enable_prefix_caching:
+                n = min(n, need)
+        else:
+            n = need
+        if self.world_size > 1:
+            n = -self.ps.world.cpu_all_reduce_max([-n])[0]  # min over ranks
+        return max(n, 2)
+
+    def initialize_cache(self, num_blocks: int) -> None:
+        self.runner.initialize_kv_cache(num_blocks)
+
+    def warmup(self) -> None:
+        t0 = time.time()
+        if self.runner.use_graphs and not envs.VLLM_B200_SKIP_DECODE_WARMUP:
+            from .scheduler import ScheduledSeq, SchedulerOutput
+
+            for B in self.runner.decode_buckets:
+                seqs = [ScheduledSeq(f"__warm{i}", [0], 0, [0], True) for i in range(B)]
+                so = SchedulerOutput("decode", seqs)
+                # writes go to the reserved null block 0 (never read by a live request)
+                self.runner.execute(so)
+        STARTUP_TIME.labels(model_name=self.cfg.served_model_name or str(self.cfg.model)).set(
+            time.time() - getattr(self, "_t_start", t0))
+
+    def execute_model(self, so):
+        return self.runner.execute(so)
+
+    def shutdown(self) -> None:
+        if self.runner is not None:
+            self.runner.release_graphs()
+        pstate.destroy_parallel_state()
+        import torch.distributed as dist
+
+        if dist.is_initialized():
+            try:
+                dist.destroy_process_group()
+            except Exception:  # noqa: BLE001
+                pass

@@ -1,0 +1,362 @@
+"""GPT-OSS (20B / 120B architecture).
+
+Architecture as in the Trainium plugin's ``model/gpt_oss/model_mxfp4.py`` (and HF
+``GptOssForCausalLM``): GQA attention with per-head sink logits (``:360-362``),
+sliding window 128 on even layers (``:267``), YaRN RoPE (``:141-197``), a replicated
+top-k softmax router with bias (``:949-955``), clamped SwiGLU experts with
+interleaved gate/up rows (``:1104,1207-1211``), MXFP4 expert weights from the HF
+``*_blocks`` / ``*_scales`` keys (``:2114-2132``).
+
+B200 design:
+* H stays 2880 (no padding to 3072): 2880 = 90 MX blocks, kernels tile K by 32/64.
+* attention is TP-sharded over the TP group; the fused QKV projection is one GEMM,
+  RoPE + paged-KV write is one kernel, attention reads the paged cache.
+* experts are EP-sharded: rank r owns experts ``[r*E/ep, (r+1)*E/ep)`` with the full
+  intermediate dimension; MXFP4 weights stay packed (the tensor-core operand
+  format) and the MoE output is completed by one all-reduce (decode), as in the
+  reference's ``moe_block_tkg + all_reduce`` path (``model_mxfp4.py:1329-1330``).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Iterable
+
+import torch
+import torch.nn as nn
+
+from .. import ops
+from ..nn.linear import ParallelLMHead, RMSNorm, RowParallelLinear, VocabParallelEmbedding
+from ..ops import reference as ref
+from ..parallel.state import GroupCoordinator, ParallelState
+from .base import KVSpec, LayerSpec, kv_head_sharding
+
+
+@dataclass
+class GptOssConfig:
+    vocab_size: int = 201088
+    hidden_size: int = 2880
+    num_hidden_layers: int = 24
+    num_attention_heads: int = 64
+    num_key_value_heads: int = 8
+    head_dim: int = 64
+    intermediate_size: int = 2880
+    num_local_experts: int = 32
+    num_experts_per_tok: int = 4
+    sliding_window: int = 128
+    layer_types: list | None = None
+    rope_theta: float = 150000.0
+    rope_scaling: dict | None = None
+    rms_norm_eps: float = 1e-5
+    swiglu_limit: float = 7.0
+    swiglu_alpha: float = 1.702
+    attention_bias: bool = True
+    max_position_embeddings: int = 131072
+    quantization: str = "mxfp4"  # mxfp4 | bf16
+    tie_word_embeddings: bool = False
+    eos_token_id: int | list | None = None
+
+    @classmethod
+    def from_hf(cls, d: dict, quantization: str | None = None) -> "GptOssConfig":
+        rope = d.get("rope_scaling") or d.get("rope_parameters")
+        theta = d.get("rope_theta") or (rope or {}).get("rope_theta", 150000.0)
+        q = quantization
+        if q is None:
+            qc = d.get("quantization_config") or {}
+            q = "mxfp4" if qc.get("quant_method") == "mxfp4" else "bf16"
+        n_layers = d["num_hidden_layers"]
+        lt = d.get("layer_types") or [
+            "sliding_attention" if i % 2 == 0 else "full_attention" for i in range(n_layers)
+        ]
+        return cls(vocab_size=d["vocab_size"], hidden_size=d["hidden_size"], num_hidden_layers=n_layers,
+                   num_attention_heads=d["num_attention_heads"], num_key_value_heads=d["num_key_value_heads"],
+                   head_dim=d.get("head_dim") or d["hidden_size"] // d["num_attention_heads"],
+                   intermediate_size=d["intermediate_size"], num_local_experts=d["num_local_experts"],
+                   num_experts_per_tok=d.get("num_experts_per_tok", d.get("experts_per_token", 4)),
+                   sliding_window=d.get("sliding_window", 128), layer_types=lt, rope_theta=theta,
+                   rope_scaling=rope if rope and rope.get("rope_type", rope.get("type")) == "yarn" else None,
+                   rms_norm_eps=d.get("rms_norm_eps", 1e-5), swiglu_limit=d.get("swiglu_limit", 7.0),
+                   attention_bias=d.get("attention_bias", True),
+                   max_position_embeddings=d.get("max_position_embeddings", 131072), quantization=q,
+                   tie_word_embeddings=d.get("tie_word_embeddings", False), eos_token_id=d.get("eos_token_id"))
+
+    def layer_window(self, i: int) -> int | None:
+        lt = self.layer_types or ["sliding_attention" if j % 2 == 0 else "full_attention"
+                                  for j in range(self.num_hidden_layers)]
+        return self.sliding_window if lt[i] == "sliding_attention" else None
+
+    def rope_params(self) -> tuple[torch.Tensor, float]:
+        rs = self.rope_scaling
+        if rs:
+            return ref.yarn_inv_freq(self.head_dim, self.rope_theta, rs.get("factor", 1.0),
+                                     rs.get("original_max_position_embeddings", 4096), rs.get("beta_fast", 32.0),
+                                     rs.get("beta_slow", 1.0), rs.get("truncate", False))
+        return ref.yarn_inv_freq(self.head_dim, self.rope_theta)
+
+
+def _param(shape, dtype, device) -> nn.Parameter:
+    return nn.Parameter(torch.empty(shape, dtype=dtype, device=device), requires_grad=False)
+
+
+class GptOssAttention(nn.Module):
+    def __init__(self, cfg: GptOssConfig, layer_idx: int, tp: GroupCoordinator, dtype, device):
+        super().__init__()
+        self.cfg = cfg
+        self.tp = tp
+        self.layer_idx = layer_idx
+        t, r = tp.world_size, tp.rank_in_group
+        if cfg.num_attention_heads % t:
+            raise ValueError("attention heads must divide by tp")
+        self.nq = cfg.num_attention_heads // t
+        self.kv_start, self.nkv = kv_head_sharding(cfg.num_key_value_heads, t, r)
+        self.d = cfg.head_dim
+        self.window = cfg.layer_window(layer_idx)
+        self.scale = 1.0 / math.sqrt(self.d)
+        qkv_out = (self.nq + 2 * self.nkv) * self.d
+        self.qkv_weight = _param((qkv_out, cfg.hidden_size), dtype, device)
+        self.qkv_bias = _param((qkv_out,), dtype, device) if cfg.attention_bias else None
+        self.sinks = _param((self.nq,), torch.float32, device)
+        self.o_proj = RowParallelLinear(cfg.num_attention_heads * self.d, cfg.hidden_size, tp,
+                                        bias=cfg.attention_bias, dtype=dtype, device=device)
+        self.k_scale = 1.0
+        self.v_scale = 1.0
+
+    # -- weight loading -------------------------------------------------------
+    def load_q_k_v(self, which: str, kind: str, full: torch.Tensor) -> None:
+        d, r = self.d, self.tp.rank_in_group
+        if which == "q":
+            rows = slice(r * self.nq * d, (r + 1) * self.nq * d)
+            dst = slice(0, self.nq * d)
+        else:
+            rows = slice(self.kv_start * d, (self.kv_start + self.nkv) * d)
+            off = self.nq * d if which == "k" else (self.nq + self.nkv) * d
+            dst = slice(off, off + self.nkv * d)
+        if kind == "weight":
+            self.qkv_weight.data[dst].copy_(full[rows].to(self.qkv_weight.dtype))
+        else:
+            self.qkv_bias.data[dst].copy_(full[rows].to(self.qkv_bias.dtype))
+
+    def load_sinks(self, full: torch.Tensor) -> None:
+        r = self.tp.rank_in_group
+        self.sinks.data.copy_(full[r * self.nq:(r + 1) * self.nq].float())
+
+    def forward(self, positions: torch.Tensor, x: torch.Tensor, meta, kv: tuple, cos_sin: torch.Tensor
+                ) -> torch.Tensor:
+        qkv = ops.linear(x, self.qkv_weight, self.qkv_bias)
+        k_cache, v_cache = kv
+        q = ops.rope_and_cache(qkv, positions, cos_sin, k_cache, v_cache, meta.slot_mapping, self.nq, self.nkv,
+                               self.d, self.k_scale, self.v_scale)
+        o = ops.attention(q, k_cache, v_cache, meta, self.scale, self.sinks, self.window, self.k_scale,
+                          self.v_scale)
+        return self.o_proj(o.reshape(o.shape[0], self.nq * self.d))
+
+
+class GptOssExperts(nn.Module):
+    """This rank's experts.  MXFP4: w13 [E_l, 2I, H/2] u8 + s13 [E_l, 2I, H/32] u8,
+    w2 [E_l, H, I/2] + s2 [E_l, H, I/32]; bf16: w13 [E_l, 2I, H], w2 [E_l, H, I]."""
+
+    def __init__(self, cfg: GptOssConfig, ep_rank: int, ep_size: int, dtype, device):
+        super().__init__()
+        E, H, I = cfg.num_local_experts, cfg.hidden_size, cfg.intermediate_size
+        if E % ep_size:
+            raise ValueError(f"{E} experts not divisible by ep {ep_size}")
+        self.E_local = E // ep_size
+        self.offset = ep_rank * self.E_local
+        self.quant = cfg.quantization
+        self.alpha, self.limit = cfg.swiglu_alpha, cfg.swiglu_limit
+        if self.quant == "mxfp4":
+            if H % 32 or I % 32:
+                raise ValueError("MXFP4 needs hidden and intermediate sizes divisible by 32")
+            self.w13 = _param((self.E_local, 2 * I, H // 2), torch.uint8, device)
+            self.s13 = _param((self.E_local, 2 * I, H // 32), torch.uint8, device)
+            self.w2 = _param((self.E_local, H, I // 2), torch.uint8, device)
+            self.s2 = _param((self.E_local, H, I // 32), torch.uint8, device)
+        else:
+            self.w13 = _param((self.E_local, 2 * I, H), dtype, device)
+            self.w2 = _param((self.E_local, H, I), dtype, device)
+        self.b13 = _param((self.E_local, 2 * I), torch.float32, device)
+        self.b2 = _param((self.E_local, H), torch.float32, device)
+
+    def local(self, full: torch.Tensor) -> torch.Tensor:
+        return full[self.offset:self.offset + self.E_local]
+
+    def forward(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        if self.quant == "mxfp4":
+            return ops.moe_mxfp4(x, ids, w, self.w13, self.s13, self.b13, self.w2, self.s2, self.b2, self.offset,
+                                 self.alpha, self.limit)
+        return ops.moe_dense(x, ids, w, self.w13, self.b13, self.w2, self.b2, self.offset, self.alpha, self.limit)
+
+
+class GptOssMLP(nn.Module):
+    def __init__(self, cfg: GptOssConfig, moe_group: GroupCoordinator, dtype, device):
+        super().__init__()
+        self.cfg = cfg
+        self.group = moe_group
+        self.router_weight = _param((cfg.num_local_experts, cfg.hidden_size), dtype, device)
+        self.router_bias = _param((cfg.num_local_experts,), dtype, device)
+        self.experts = GptOssExperts(cfg, moe_group.rank_in_group, moe_group.world_size, dtype, device)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        ids, w = ops.router_topk(x, self.router_weight, self.router_bias, self.cfg.num_experts_per_tok)
+        y = self.experts(x, ids, w)
+        return self.group.all_reduce(y)
+
+
+class GptOssDecoderLayer(nn.Module):
+    def __init__(self, cfg: GptOssConfig, i: int, ps: ParallelState, dtype, device):
+        super().__init__()
+        self.input_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, device=device)
+        self.self_attn = GptOssAttention(cfg, i, ps.tp, dtype, device)
+        self.post_attention_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, device=device)
+        self.mlp = GptOssMLP(cfg, ps.tp, dtype, device)
+
+    def forward(self, positions, h, residual, meta, kv, cos_sin):
+        if residual is None:
+            residual = h
+            x = self.input_layernorm(h)
+        else:
+            x, residual = self.input_layernorm(h, residual)
+        x = self.self_attn(positions, x, meta, kv, cos_sin)
+        x, residual = self.post_attention_layernorm(x, residual)
+        return self.mlp(x), residual
+
+
+class GptOssForCausalLM(nn.Module):
+    """Model entry point used by the runner: ``forward`` returns the hidden states
+    of the tokens selected by ``meta.logits_indices``; ``compute_logits`` returns this
+    rank's vocab shard of the logits."""
+
+    config_class = GptOssConfig
+
+    def __init__(self, cfg: GptOssConfig, ps: ParallelState, dtype=torch.bfloat16, device="cpu",
+                 kv_dtype: torch.dtype | None = None):
+        super().__init__()
+        self.cfg = cfg
+        self.ps = ps
+        self.dtype = dtype
+        self.kv_dtype = kv_dtype or dtype
+        self.embed_tokens = VocabParallelEmbedding(cfg.vocab_size, cfg.hidden_size, ps.tp, dtype, device)
+        self.layers = nn.ModuleList([GptOssDecoderLayer(cfg, i, ps, dtype, device)
+                                     for i in range(cfg.num_hidden_layers)])
+        self.norm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, device=device)
+        self.lm_head = ParallelLMHead(cfg.vocab_size, cfg.hidden_size, ps.tp, dtype, device)
+        inv, af = cfg.rope_params()
+        self.register_buffer("cos_sin", ops.build_cos_sin_cache(inv, min(cfg.max_position_embeddings, 1 << 17),
+                                                                af, device=device), persistent=False)
+        self.aux_hidden_layers: tuple[int, ...] = ()
+
+    # ------------------------------------------------------------------ spec
+    def get_kv_spec(self) -> KVSpec:
+        return KVSpec([LayerSpec(l.self_attn.nkv, self.cfg.head_dim, self.kv_dtype, l.self_attn.window)
+                       for l in self.layers])
+
+    def set_kv_scales(self, k_scale: float, v_scale: float) -> None:
+        for l in self.layers:
+            l.self_attn.k_scale, l.self_attn.v_scale = k_scale, v_scale
+
+    # --------------------------------------------------------------- forward
+    def forward(self, input_ids: torch.Tensor, positions: torch.Tensor, meta, kv_caches: list,
+                inputs_embeds: torch.Tensor | None = None) -> torch.Tensor:
+        h = self.embed_tokens(input_ids) if inputs_embeds is None else inputs_embeds
+        residual = None
+        aux = []
+        for i, layer in enumerate(self.layers):
+            if i in self.aux_hidden_layers:
+                aux.append(h if residual is None else h + residual)
+            h, residual = layer(positions, h, residual, meta, kv_caches[i], self.cos_sin)
+        h, _ = self.norm(h, residual)
+        if self.aux_hidden_layers:
+            self._aux = torch.cat(aux, dim=-1)
+        return h
+
+    def compute_logits(self, h: torch.Tensor) -> torch.Tensor:
+        return self.lm_head(h)
+
+    # ----------------------------------------------------------------- loading
+    def load_weights(self, weights: Iterable[tuple[str, torch.Tensor]]) -> set[str]:
+        """Consume (name, full tensor) pairs in the HF checkpoint naming, including the
+        MXFP4 ``*_blocks``/``*_scales`` expert keys and the bf16 ``gate_up_proj``
+        [E, H, 2I] / ``down_proj`` [E, I, H] layout."""
+        loaded = set()
+        for name, t in weights:
+            n = name[len("model."):] if name.startswith("model.") else name
+            if n == "embed_tokens.weight":
+                self.embed_tokens.weight.weight_loader(self.embed_tokens.weight, t)
+                if self.cfg.tie_word_embeddings:
+                    self.lm_head.weight.weight_loader(self.lm_head.weight, t)
+            elif n in ("lm_head.weight",) or name == "lm_head.weight":
+                self.lm_head.weight.weight_loader(self.lm_head.weight, t)
+            elif n == "norm.weight":
+                self.norm.weight.data.copy_(t.float())
+            elif n.startswith("layers."):
+                parts = n.split(".")
+                li = int(parts[1])
+                rest = ".".join(parts[2:])
+                self._load_layer(self.layers[li], rest, t)
+            else:
+                continue
+            loaded.add(name)
+        return loaded
+
+    def _load_layer(self, layer: GptOssDecoderLayer, rest: str, t: torch.Tensor) -> None:
+        at, mlp = layer.self_attn, layer.mlp
+        ex = mlp.experts
+        if rest in ("input_layernorm.weight", "post_attention_layernorm.weight"):
+            getattr(layer, rest.split(".")[0]).weight.data.copy_(t.float())
+        elif rest.startswith("self_attn.") and rest.split(".")[1] in ("q_proj", "k_proj", "v_proj"):
+            which = rest.split(".")[1][0]
+            at.load_q_k_v(which, rest.split(".")[2], t)
+        elif rest == "self_attn.o_proj.weight":
+            at.o_proj.weight.weight_loader(at.o_proj.weight, t)
+        elif rest == "self_attn.o_proj.bias":
+            at.o_proj.bias.data.copy_(t.to(at.o_proj.bias.dtype))
+        elif rest == "self_attn.sinks":
+            at.load_sinks(t)
+        elif rest == "mlp.router.weight":
+            mlp.router_weight.data.copy_(t.to(mlp.router_weight.dtype))
+        elif rest == "mlp.router.bias":
+            mlp.router_bias.data.copy_(t.to(mlp.router_bias.dtype))
+        elif rest == "mlp.experts.gate_up_proj_bias":
+            ex.b13.data.copy_(ex.local(t).float())
+        elif rest == "mlp.experts.down_proj_bias":
+            ex.b2.data.copy_(ex.local(t).float())
+        elif rest == "mlp.experts.gate_up_proj_blocks":
+            self._load_mx(ex, "13", "blocks", t)
+        elif rest == "mlp.experts.gate_up_proj_scales":
+            self._load_mx(ex, "13", "scales", t)
+        elif rest == "mlp.experts.down_proj_blocks":
+            self._load_mx(ex, "2", "blocks", t)
+        elif rest == "mlp.experts.down_proj_scales":
+            self._load_mx(ex, "2", "scales", t)
+        elif rest == "mlp.experts.gate_up_proj":  # bf16 [E, H, 2I]
+            self._load_dense(ex, "13", ex.local(t).transpose(1, 2))
+        elif rest == "mlp.experts.down_proj":  # bf16 [E, I, H]
+            self._load_dense(ex, "2", ex.local(t).transpose(1, 2))
+        else:
+            raise KeyError(f"unexpected GPT-OSS weight {rest}")
+
+    @staticmethod
+    def _load_mx(ex: GptOssExperts, which: str, kind: str, t: torch.Tensor) -> None:
+        loc = ex.local(t)
+        if ex.quant == "mxfp4":
+            dst = getattr(ex, ("w" if kind == "blocks" else "s") + which)
+            dst.data.copy_(loc.reshape(dst.shape))
+            return
+        # bf16 model served from an MXFP4 checkpoint: dequantise at load time
+        # (``weight_loaders_bf16.py:264``); needs the matching blocks/scales pair.
+        pend = ex.__dict__.setdefault("_pending", {})
+        pend[(which, kind)] = loc
+        if (which, "blocks") in pend and (which, "scales") in pend:
+            b = pend.pop((which, "blocks"))
+            s = pend.pop((which, "scales"))
+            GptOssForCausalLM._load_dense(ex, which, ref.dequant_mxfp4(b.reshape(*b.shape[:2], -1), s))
+
+    @staticmethod
+    def _load_dense(ex: GptOssExperts, which: str, w: torch.Tensor) -> None:
+        if ex.quant == "mxfp4":
+            blocks, scales = ref.quantize_mxfp4(w.float())
+            getattr(ex, "w" + which).data.copy_(blocks)
+            getattr(ex, "s" + which).data.copy_(scales)
+        else:
+            getattr(ex, "w" + which).data.copy_(w.to(getattr(ex, "w" + which).dtype))

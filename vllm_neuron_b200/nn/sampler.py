@@ -1,0 +1,65 @@
+"""Vocab-parallel on-device sampler.
+
+Each TP rank holds logits for its vocab slice.  As in the Trainium plugin's sampler
+(``nn/sampler.py:56-169``, ``functional/topk.py:32-115``, ``functional/argmax.py:26``):
+* greedy batches: local argmax per rank, all-gather of (value, index) pairs, global
+  argmax (ties resolve to the lowest rank, i.e. the lowest token id);
+* otherwise: local top-``max_top_k`` candidates per rank, all-gather, then
+  temperature / top-k / top-p / inverse-CDF draw over the merged candidates.
+The draw uses a per-row uniform supplied by the host, identical on every rank, so
+all ranks produce the same token without a broadcast.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from .. import ops
+from ..parallel.state import GroupCoordinator
+
+
+class Sampler(nn.Module):
+    def __init__(self, group: GroupCoordinator, vocab_start: int, vocab_size: int, max_top_k: int = 256):
+        super().__init__()
+        self.group = group
+        self.vocab_start = vocab_start
+        self.vocab_size = vocab_size
+        self.max_top_k = max_top_k
+
+    def _mask_padding(self, logits: torch.Tensor) -> torch.Tensor:
+        # vocab padding rows (when V % tp != 0) must never win
+        n_valid = self.vocab_size - self.vocab_start
+        if n_valid < logits.shape[1]:
+            logits = logits.clone()
+            logits[:, max(n_valid, 0):] = float("-inf")
+        return logits
+
+    def greedy(self, logits: torch.Tensor) -> torch.Tensor:
+        logits = self._mask_padding(logits)
+        val, idx = ops.argmax(logits)
+        if self.group.world_size == 1:
+            return idx
+        pair = torch.stack([val, (idx + self.vocab_start).to(torch.float32)], dim=-1)  # [B,2]
+        # indices < 2^24 are exact in fp32 (vocab <= 16.7M)
+        allp = self.group.all_gather(pair.unsqueeze(0), dim=0)  # [tp,B,2]
+        best = allp[..., 0].argmax(0)  # first max = lowest rank
+        return allp[..., 1].gather(0, best[None]).squeeze(0).to(torch.int64)
+
+    def forward(self, logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor, top_p: torch.Tensor,
+                uniform: torch.Tensor, all_greedy: bool) -> torch.Tensor:
+        if all_greedy:
+            return self.greedy(logits)
+        logits = self._mask_padding(logits)
+        if self.group.world_size == 1:
+            return ops.sample(logits, temperature, top_k, top_p, uniform, self.max_top_k)
+        K = min(self.max_top_k, logits.shape[1])
+        vals, ids = torch.topk(logits.float(), K, dim=-1)
+        ids = ids + self.vocab_start
+        allv = self.group.all_gather(vals.unsqueeze(0), dim=0)  # [tp,B,K]
+        alli = self.group.all_gather(ids.unsqueeze(0), dim=0)
+        B = logits.shape[0]
+        cand_v = allv.permute(1, 0, 2).reshape(B, -1)
+        cand_i = alli.permute(1, 0, 2).reshape(B, -1)
+        pos = ops.sample(cand_v, temperature, top_k, top_p, uniform, self.max_top_k)
+        return cand_i.gather(1, pos[:, None]).squeeze(1).to(torch.int64)

@@ -1,0 +1,248 @@
+"""Functional op library: hand-written sm_100a kernel on CUDA tensors, PyTorch
+reference otherwise.
+
+This is the B200 counterpart of the Trainium plugin's ``functional`` package
+(``vllm_neuron/functional/__init__.py:42-74``), where each op chose an NKI kernel
+or a PyTorch fallback.  Here the choice is simpler: a CUDA tensor runs the
+compiled kernel (``torch.ops.b200.*``; a missing extension is an error), a CPU
+tensor (or ``VLLM_B200_DISABLE_KERNELS=1``) runs :mod:`.reference`.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+from . import reference as ref
+from ._ext import kernels_enabled, use_kernel  # noqa: F401
+from ._ext import ops as _k
+from .metadata import AttentionMetadata  # noqa: F401
+
+# ---------------------------------------------------------------------------
+# dense layers
+# ---------------------------------------------------------------------------
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None) -> torch.Tensor:
+    """Plain GEMM (cuBLAS on GPU).  Fused GEMM+collective paths live in
+    :mod:`vllm_neuron_b200.parallel.communicator`."""
+    if x.dtype != w.dtype:
+        x = x.to(w.dtype)
+    return F.linear(x, w, b)
+
+
+def embedding(ids: torch.Tensor, w: torch.Tensor, vocab_start: int = 0) -> torch.Tensor:
+    """Rows of ``w`` for ids in ``[vocab_start, vocab_start + rows)``, zero elsewhere."""
+    if use_kernel(w):
+        out = torch.empty(ids.shape[0], w.shape[1], dtype=w.dtype, device=w.device)
+        _k().embedding(out, ids, w, vocab_start)
+        return out
+    local = ids.long() - vocab_start
+    valid = (local >= 0) & (local < w.shape[0])
+    y = w[local.clamp(0, w.shape[0] - 1)]
+    return y * valid[:, None].to(y.dtype)
+
+
+# ---------------------------------------------------------------------------
+# normalisation
+# ---------------------------------------------------------------------------
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    if use_kernel(x):
+        out = torch.empty_like(x)
+        _k().rms_norm(out, x, w, eps)
+        return out
+    return ref.rms_norm(x, w, eps)
+
+
+def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float
+                       ) -> tuple[torch.Tensor, torch.Tensor]:
+    """Returns (norm(x + residual), x + residual).  On GPU the residual buffer is
+    updated in place."""
+    if use_kernel(x):
+        out = torch.empty_like(x)
+        _k().fused_add_rms_norm(out, x, residual, w, eps)
+        return out, residual
+    return ref.fused_add_rms_norm(x, residual, w, eps)
+
+
+# ---------------------------------------------------------------------------
+# rotary + KV cache write
+# ---------------------------------------------------------------------------
+
+
+def rope_and_cache(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor, k_cache: torch.Tensor,
+                   v_cache: torch.Tensor, slot_mapping: torch.Tensor, num_q: int, num_kv: int, head_dim: int,
+                   k_scale: float = 1.0, v_scale: float = 1.0, q_norm_w: torch.Tensor | None = None,
+                   k_norm_w: torch.Tensor | None = None, norm_eps: float = 1e-6,
+                   rotary_dim: int | None = None) -> torch.Tensor:
+    """Apply RoPE to q and k of the fused projection ``qkv [T, (num_q+2*num_kv)*d]``
+    in place, write k and v to the paged cache, return the q view [T, num_q, d].
+
+    ``cos_sin`` [max_pos, rotary_dim] fp32 holds cos in the first half, sin in the
+    second (attention factor folded in).  Optional per-head RMSNorm of q/k before the
+    rotation (Qwen3 QK-norm).  ``rotary_dim`` < d rotates only the leading dims
+    (partial rotary, Qwen3-Next)."""
+    T = qkv.shape[0]
+    rd = rotary_dim or head_dim
+    if use_kernel(qkv):
+        _k().rope_kv_write(qkv, positions, cos_sin, k_cache, v_cache, slot_mapping, num_q, num_kv, head_dim,
+                           rd, k_scale, v_scale, q_norm_w, k_norm_w, norm_eps)
+        return qkv[:, : num_q * head_dim].view(T, num_q, head_dim)
+    q = qkv[:, : num_q * head_dim].view(T, num_q, head_dim)
+    k = qkv[:, num_q * head_dim:(num_q + num_kv) * head_dim].view(T, num_kv, head_dim)
+    v = qkv[:, (num_q + num_kv) * head_dim:].view(T, num_kv, head_dim)
+    if q_norm_w is not None:
+        q.copy_(ref.rms_norm(q, q_norm_w, norm_eps))
+        k.copy_(ref.rms_norm(k, k_norm_w, norm_eps))
+    pos = positions.long()
+    cs = cos_sin[pos]
+    cos, sin = cs[:, : rd // 2], cs[:, rd // 2:]
+    if rd == head_dim:
+        q.copy_(ref.apply_rope(q, cos, sin))
+        k.copy_(ref.apply_rope(k, cos, sin))
+    else:
+        q[..., :rd] = ref.apply_rope(q[..., :rd], cos, sin)
+        k[..., :rd] = ref.apply_rope(k[..., :rd], cos, sin)
+    ref.write_kv_cache(k, v, k_cache, v_cache, slot_mapping, k_scale, v_scale)
+    return q
+
+
+def build_cos_sin_cache(inv_freq: torch.Tensor, max_pos: int, attn_factor: float = 1.0,
+                        device=None) -> torch.Tensor:
+    pos = torch.arange(max_pos, dtype=torch.float32, device=device)
+    cos, sin = ref.rope_cos_sin(pos, inv_freq.to(device), attn_factor)
+    return torch.cat([cos, sin], dim=-1).contiguous()
+
+
+# ---------------------------------------------------------------------------
+# attention
+# ---------------------------------------------------------------------------
+
+
+def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, meta: AttentionMetadata,
+              scale: float, sinks: torch.Tensor | None = None, window: int | None = None,
+              k_scale: float = 1.0, v_scale: float = 1.0, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Attention of this step's queries (already RoPE'd, their K/V already in the
+    cache) over the paged cache.  q [T, Hq, d] (may be a strided view)."""
+    T, Hq, d = q.shape
+    win = int(window or 0)
+    if use_kernel(q):
+        if out is None:
+            out = torch.empty(T, Hq, d, dtype=q.dtype, device=q.device)
+        if meta.is_decode:
+            _k().paged_attention_decode(out, q, k_cache, v_cache, meta.block_tables, meta.seq_lens, sinks, win,
+                                        scale, k_scale, v_scale, meta.workspace, meta.num_splits)
+        else:
+            _k().paged_attention_prefill(out, q, k_cache, v_cache, meta.block_tables, meta.seq_lens,
+                                         meta.query_start_loc, sinks, win, scale, k_scale, v_scale,
+                                         meta.max_query_len)
+        return out
+    o = ref.paged_attention(q, k_cache, v_cache, meta.block_tables, meta.seq_lens, meta.query_start_loc, scale,
+                            sinks, window, k_scale, v_scale)
+    if out is not None:
+        out.copy_(o)
+        return out
+    return o
+
+
+def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens: torch.Tensor, scale: float,
+                     causal: bool = True, max_seqlen: int = 0) -> torch.Tensor:
+    """Self attention over packed sequences without a cache (vision encoder)."""
+    if use_kernel(q):
+        out = torch.empty_like(q)
+        _k().varlen_attention(out, q, k, v, cu_seqlens, scale, causal, int(max_seqlen))
+        return out
+    return ref.prefill_attention(q, k, v, cu_seqlens, scale, None, None, causal)
+
+
+# ---------------------------------------------------------------------------
+# MoE
+# ---------------------------------------------------------------------------
+
+
+def router_topk(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, top_k: int,
+                order: str = "topk_softmax") -> tuple[torch.Tensor, torch.Tensor]:
+    """(topk_ids [T,k] int32, topk_weights [T,k] fp32)."""
+    if use_kernel(x) and order == "topk_softmax" and w.shape[0] <= 1024:
+        logits = F.linear(x.to(w.dtype), w, b).float()
+        ids = torch.empty(x.shape[0], top_k, dtype=torch.int32, device=x.device)
+        wts = torch.empty(x.shape[0], top_k, dtype=torch.float32, device=x.device)
+        _k().topk_softmax(ids, wts, logits)
+        return ids, wts
+    if use_kernel(x):
+        logits = F.linear(x.to(w.dtype), w, b).float()
+        if order == "softmax_topk":
+            wts, ids = torch.topk(torch.softmax(logits, -1), top_k, -1)
+            wts = wts / wts.sum(-1, keepdim=True)
+        else:
+            ids, wts, _ = ref.router_topk(x, w, b, top_k, order)
+        return ids.to(torch.int32), wts
+    ids, wts, _ = ref.router_topk(x, w, b, top_k, order)
+    return ids, wts
+
+
+def moe_mxfp4(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, w13: torch.Tensor,
+              s13: torch.Tensor, b13: torch.Tensor | None, w2: torch.Tensor, s2: torch.Tensor,
+              b2: torch.Tensor | None, expert_offset: int, alpha: float, limit: float,
+              scratch: dict | None = None) -> torch.Tensor:
+    """Routed experts with packed MXFP4 weights.
+
+    w13 [E_local, 2I, H/2] u8 + s13 [E_local, 2I, H/32] (gate/up interleaved rows),
+    w2 [E_local, H, I/2] u8 + s2 [E_local, H, I/32]; biases fp32.  Returns the
+    partial sum over this rank's experts, [T, H] in x.dtype."""
+    if use_kernel(x):
+        out = torch.empty_like(x)
+        _k().moe_mxfp4(out, x, topk_ids, topk_w, w13, s13, b13, w2, s2, b2, expert_offset, alpha, limit)
+        return out
+    E = w13.shape[0]
+    w13f = ref.dequant_mxfp4(w13, s13)
+    w2f = ref.dequant_mxfp4(w2, s2)
+    return ref.moe_experts(x, topk_ids, topk_w, w13f, b13, w2f, b2, alpha, limit, True, expert_offset)
+
+
+def moe_dense(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, w13: torch.Tensor,
+              b13: torch.Tensor | None, w2: torch.Tensor, b2: torch.Tensor | None, expert_offset: int,
+              alpha: float, limit: float | None, interleaved: bool = True, act: str = "swiglu_clamp"
+              ) -> torch.Tensor:
+    """Routed experts with bf16 weights w13 [E, 2I, H], w2 [E, H, I]."""
+    if use_kernel(x):
+        out = torch.empty_like(x)
+        _k().moe_bf16(out, x, topk_ids, topk_w, w13, b13, w2, b2, expert_offset, alpha,
+                      -1.0 if limit is None else float(limit), interleaved, act == "swiglu_clamp")
+        return out
+    return ref.moe_experts(x, topk_ids, topk_w, w13, b13, w2, b2, alpha, limit, interleaved, expert_offset, act)
+
+
+# ---------------------------------------------------------------------------
+# sampling
+# ---------------------------------------------------------------------------
+
+
+def sample(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor, top_p: torch.Tensor,
+           uniform: torch.Tensor, max_top_k: int = 256) -> torch.Tensor:
+    """One token per row.  temperature <= 0 -> greedy.  ``uniform`` [B] in [0,1)
+    drives inverse-CDF sampling so that every TP rank draws the same token."""
+    if use_kernel(logits):
+        out = torch.empty(logits.shape[0], dtype=torch.int64, device=logits.device)
+        _k().sample(out, logits, temperature, top_k, top_p, uniform, max_top_k)
+        return out
+    return ref.sample(logits, temperature, top_k, top_p, max_top_k=max_top_k, uniform=uniform)
+
+
+def argmax(logits: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """(max value fp32 [B], index int64 [B]) per row."""
+    if use_kernel(logits):
+        vals = torch.empty(logits.shape[0], dtype=torch.float32, device=logits.device)
+        idx = torch.empty(logits.shape[0], dtype=torch.int64, device=logits.device)
+        _k().argmax(vals, idx, logits)
+        return vals, idx
+    v, i = logits.float().max(-1)
+    return v, i
+
+
+def softmax_scale(head_dim: int) -> float:
+    return 1.0 / math.sqrt(head_dim)
