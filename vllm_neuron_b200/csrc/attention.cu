@@ -1,0 +1,670 @@
+// Paged attention with sink logits, sliding windows and fp8 KV (decode and prefill),
+// plus contiguous varlen attention (vision encoder).
+//
+// Semantics (restated from the Trainium plugin's PyTorch fallbacks):
+//   * sink logits join the softmax denominator only
+//     (functional/attention/attention_cte.py:163-173, attention_decode.py:707-724);
+//   * query at position p sees keys j with j <= p and, with window W > 0, j > p - W;
+//   * fp8 caches hold k/k_scale, v/v_scale: k_scale is folded into the softmax scale,
+//     v_scale into the output;
+//   * cache layout HND [num_blocks, kv_heads, block_size, d], block_tables [B, max_blocks].
+//
+// Design: FlashAttention-2 style warp tiles on the tensor cores (mma.sync m16n8k16,
+// bf16 in, fp32 accumulate) with cp.async double-buffered K/V tiles of 64 keys in
+// XOR-swizzled shared memory.
+//   decode : one CTA per (split, kv head, sequence); the GQA group of query heads is the
+//            16-row M dimension (group <= 16, zero-padded), each of the 4 warps owns 16
+//            of the 64 keys of a tile and keeps its own online-softmax state; the warps
+//            merge in shared memory, and splits merge in a combine kernel (LSE merge).
+//            M = 8..16 rows is below tcgen05's 64-row minimum, and the kernel is bound by
+//            HBM reads of the cache, so the warp-level MMA is the right unit here.
+//   prefill: one CTA per (64-query tile, query head, sequence), K/V read through the block
+//            table, so chunked prefill and prefix-cache hits need no gather.
+#include "launch.h"
+#include "mma_utils.cuh"
+
+namespace b200 {
+
+constexpr int kKT = 64;  // keys per tile
+constexpr float kLog2e = 1.4426950408889634f;
+
+// ---------------------------------------------------------------------------------------
+// K/V tile loader: 64 keys x D dims into swizzled bf16 shared memory.  For fp8 caches the
+// raw bytes go through a staging buffer and are converted (with the cache scale left to
+// the caller).
+// ---------------------------------------------------------------------------------------
+template <int D>
+struct TileGeom {
+  static constexpr int kChunks = D / 8;  // 16-byte chunks per bf16 row
+  static constexpr int kTileElems = kKT * D;
+};
+
+template <int D, typename CT>
+B200_D void load_kv_tile(__nv_bfloat16* Ks, __nv_bfloat16* Vs, uint8_t* stage, const CT* kc, const CT* vc,
+                         const int* bt_row, int tile_key0, int key_end, int bs, int nkv, int h) {
+  constexpr int C = TileGeom<D>::kChunks;
+  if constexpr (sizeof(CT) == 2) {
+    for (int i = threadIdx.x; i < kKT * C; i += blockDim.x) {
+      const int k = i / C, c = i % C;
+      const int gk = tile_key0 + k;
+      const bool ok = gk < key_end;
+      size_t off = 0;
+      if (ok) {
+        const int blk = bt_row[gk / bs];
+        off = (((size_t)blk * nkv + h) * bs + (gk % bs)) * D + c * 8;
+      }
+      cp_async16(Ks + swz(k, c, C) * 8, kc + off, ok ? 16 : 0);
+      cp_async16(Vs + swz(k, c, C) * 8, vc + off, ok ? 16 : 0);
+    }
+  } else {
+    // fp8: D bytes per row -> D/16 chunks; staged then converted by the caller
+    constexpr int C8 = D / 16;
+    for (int i = threadIdx.x; i < kKT * C8; i += blockDim.x) {
+      const int k = i / C8, c = i % C8;
+      const int gk = tile_key0 + k;
+      const bool ok = gk < key_end;
+      size_t off = 0;
+      if (ok) {
+        const int blk = bt_row[gk / bs];
+        off = (((size_t)blk * nkv + h) * bs + (gk % bs)) * D + c * 16;
+      }
+      cp_async16(stage + (k * D + c * 16), reinterpret_cast<const uint8_t*>(kc) + off, ok ? 16 : 0);
+      cp_async16(stage + kKT * D + (k * D + c * 16), reinterpret_cast<const uint8_t*>(vc) + off, ok ? 16 : 0);
+    }
+  }
+}
+
+template <int D>
+B200_D void convert_fp8_tile(__nv_bfloat16* Ks, __nv_bfloat16* Vs, const uint8_t* stage) {
+  constexpr int C = D / 8;
+  for (int i = threadIdx.x; i < kKT * C; i += blockDim.x) {
+    const int k = i / C, c = i % C;
+#pragma unroll
+    for (int w = 0; w < 2; ++w) {
+      const uint8_t* src = stage + w * kKT * D + k * D + c * 8;
+      __nv_bfloat16* dst = (w == 0 ? Ks : Vs) + swz(k, c, C) * 8;
+      uint2 raw = *reinterpret_cast<const uint2*>(src);
+      const uint8_t* b = reinterpret_cast<const uint8_t*>(&raw);
+      uint32_t packed[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __nv_fp8_e4m3 lo, hi;
+        lo.__x = b[2 * j];
+        hi.__x = b[2 * j + 1];
+        packed[j] = pack_bf16(float(lo), float(hi));
+      }
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<uint4*>(packed);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Decode
+// ---------------------------------------------------------------------------------------
+template <int D, typename T, typename CT>
+__global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const T* __restrict__ q,
+                                                     const CT* __restrict__ kc, const CT* __restrict__ vc,
+                                                     const int* __restrict__ block_tables,
+                                                     const int* __restrict__ seq_lens, const float* __restrict__ sinks,
+                                                     int nq, int nkv, int q_stride, int bs, int max_blocks, int window,
+                                                     float scale_log2, float v_scale, float* __restrict__ ws,
+                                                     int num_splits) {
+  constexpr int C = D / 8;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(smem_raw);            // [2][64*D]
+  __nv_bfloat16* Vs = Ks + 2 * kKT * D;                                      // [2][64*D]
+  uint8_t* stage = reinterpret_cast<uint8_t*>(Vs + 2 * kKT * D);             // fp8 staging [2][64*D]
+
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int G = nq / nkv;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qd = lane & 3, r0 = lane >> 2;
+  const int L = seq_lens[b];
+  const int lo = (window > 0) ? max(0, L - window) : 0;
+  // split the key range [lo, L) by whole cache blocks
+  int key_begin = 0, key_end = 0;
+  if (L > 0) {
+    const int fb = lo / bs, lb = (L - 1) / bs, nb = lb - fb + 1;
+    const int bps = cdiv(nb, num_splits);
+    const int b0 = fb + split * bps, b1 = min(fb + (split + 1) * bps, lb + 1);
+    if (b0 < b1) {
+      key_begin = max(b0 * bs, lo);
+      key_end = min(b1 * bs, L);
+    }
+  }
+  const int* bt_row = block_tables + (size_t)b * max_blocks;
+
+  // Q fragments (A operand, rows = heads of the group)
+  uint32_t qf[D / 16][4];
+  {
+    const T* qb = q + (size_t)b * q_stride + (size_t)(h * G) * D;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+#pragma unroll
+      for (int hv = 0; hv < 2; ++hv) {      // rows r0 / r0+8
+#pragma unroll
+        for (int kh = 0; kh < 2; ++kh) {    // dims lo / hi 8
+          const int row = r0 + hv * 8;
+          const int dim = kk * 16 + kh * 8 + 2 * qd;
+          float a = 0.f, c = 0.f;
+          if (row < G) {
+            a = to_float(qb[(size_t)row * D + dim]);
+            c = to_float(qb[(size_t)row * D + dim + 1]);
+          }
+          qf[kk][kh * 2 + hv] = pack_bf16(a, c);
+        }
+      }
+    }
+  }
+
+  float o[D / 8][4];
+#pragma unroll
+  for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+
+  const int ntiles = key_end > key_begin ? cdiv(key_end - key_begin, kKT) : 0;
+  if (ntiles > 0) {
+    load_kv_tile<D, CT>(Ks, Vs, stage, kc, vc, bt_row, key_begin, key_end, bs, nkv, h);
+    cp_async_commit();
+  }
+  for (int t = 0; t < ntiles; ++t) {
+    const int buf = t & 1;
+    if (t + 1 < ntiles) {
+      load_kv_tile<D, CT>(Ks + (buf ^ 1) * kKT * D, Vs + (buf ^ 1) * kKT * D, stage + (buf ^ 1) * 2 * kKT * D, kc,
+                          vc, bt_row, key_begin + (t + 1) * kKT, key_end, bs, nkv, h);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    __nv_bfloat16* K = Ks + buf * kKT * D;
+    __nv_bfloat16* V = Vs + buf * kKT * D;
+    if constexpr (sizeof(CT) == 1) {
+      convert_fp8_tile<D>(K, V, stage + buf * 2 * kKT * D);
+      __syncthreads();
+    }
+    const int key0 = key_begin + t * kKT + warp * 16;
+    // S = Q K^T for this warp's 16 keys: two n8 tiles
+    float s[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      const int mi = lane >> 3;
+      const int krow = warp * 16 + (mi >> 1) * 8 + (lane & 7);
+      const int kch = kk * 2 + (mi & 1);
+      uint32_t b0, b1, b2, b3;
+      ldmatrix_x4(b0, b1, b2, b3, K + swz(krow, kch, C) * 8);
+      uint32_t bA[2] = {b0, b1}, bB[2] = {b2, b3};
+      mma_bf16_16816(s[0], qf[kk], bA);
+      mma_bf16_16816(s[1], qf[kk], bB);
+    }
+    // mask + online softmax (rows r0 and r0+8)
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = key0 + j * 8 + 2 * qd + (e & 1);
+        float v = s[j][e] * scale_log2;
+        if (key >= key_end) v = -INFINITY;
+        s[j][e] = v;
+        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      }
+    }
+    float corr[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+      const float mnew = fmaxf(m_run[r], mx[r]);
+      corr[r] = (mnew == -INFINITY) ? 1.f : exp2f(m_run[r] - mnew);
+      m_run[r] = mnew;
+    }
+    float rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float mref = m_run[e >> 1];
+        const float p = (mref == -INFINITY) ? 0.f : exp2f(s[j][e] - mref);
+        s[j][e] = p;
+        rs[e >> 1] += p;
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
+      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
+      l_run[r] = l_run[r] * corr[r] + rs[r];
+    }
+#pragma unroll
+    for (int n = 0; n < D / 8; ++n) {
+      o[n][0] *= corr[0];
+      o[n][1] *= corr[0];
+      o[n][2] *= corr[1];
+      o[n][3] *= corr[1];
+    }
+    // O += P V  (P: 16 rows x 16 keys as the A operand)
+    uint32_t pa[4] = {pack_bf16(s[0][0], s[0][1]), pack_bf16(s[0][2], s[0][3]), pack_bf16(s[1][0], s[1][1]),
+                      pack_bf16(s[1][2], s[1][3])};
+#pragma unroll
+    for (int n = 0; n < D / 8; n += 2) {
+      const int mi = lane >> 3;
+      const int vrow = warp * 16 + (mi & 1) * 8 + (lane & 7);
+      const int vch = n + (mi >> 1);
+      uint32_t b0, b1, b2, b3;
+      ldmatrix_x4_trans(b0, b1, b2, b3, V + swz(vrow, vch, C) * 8);
+      uint32_t bA[2] = {b0, b1}, bB[2] = {b2, b3};
+      mma_bf16_16816(o[n], pa, bA);
+      mma_bf16_16816(o[n + 1], pa, bB);
+    }
+    __syncthreads();  // before the next prefetch overwrites this buffer
+  }
+
+  // ---- merge the 4 warps (shared memory reuses the K/V area) ----
+  float* sm_m = reinterpret_cast<float*>(smem_raw);     // [4][16]
+  float* sm_l = sm_m + 4 * 16;                          // [4][16]
+  float* sm_o = sm_l + 4 * 16;                          // [4][16][D]
+  __syncthreads();
+  if (qd == 0) {
+    sm_m[warp * 16 + r0] = m_run[0];
+    sm_m[warp * 16 + r0 + 8] = m_run[1];
+    sm_l[warp * 16 + r0] = l_run[0];
+    sm_l[warp * 16 + r0 + 8] = l_run[1];
+  }
+#pragma unroll
+  for (int n = 0; n < D / 8; ++n) {
+    const int dim = n * 8 + 2 * qd;
+    sm_o[(warp * 16 + r0) * D + dim] = o[n][0];
+    sm_o[(warp * 16 + r0) * D + dim + 1] = o[n][1];
+    sm_o[(warp * 16 + r0 + 8) * D + dim] = o[n][2];
+    sm_o[(warp * 16 + r0 + 8) * D + dim + 1] = o[n][3];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+    const int g = i / D, dim = i % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_m[w * 16 + g]);
+    float l = 0.f, acc = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const float f = exp2f(sm_m[w * 16 + g] - M);
+        l += sm_l[w * 16 + g] * f;
+        acc += sm_o[(w * 16 + g) * D + dim] * f;
+      }
+    }
+    const int head = h * G + g;
+    if (num_splits == 1) {
+      float Mt = M, lt = l, at = acc;
+      if (sinks != nullptr) {
+        const float sk = sinks[head] * kLog2e;
+        const float Mn = fmaxf(Mt, sk);
+        const float f = (Mt == -INFINITY) ? 0.f : exp2f(Mt - Mn);
+        lt = lt * f + exp2f(sk - Mn);
+        at *= f;
+      }
+      const float r = lt > 0.f ? at / lt * v_scale : 0.f;
+      out[(size_t)b * nq * D + (size_t)head * D + dim] = from_float<T>(r);
+    } else {
+      float* w = ws + (((size_t)b * nq + head) * num_splits + split) * (D + 1);
+      w[dim] = l > 0.f ? acc / l : 0.f;
+      if (dim == 0) w[D] = (l > 0.f) ? (M + log2f(l)) : -INFINITY;
+    }
+  }
+}
+
+template <int D, typename T>
+__global__ void decode_combine_kernel(T* __restrict__ out, const float* __restrict__ ws,
+                                      const float* __restrict__ sinks, int nq, int num_splits, float v_scale) {
+  const int head = blockIdx.x, b = blockIdx.y;
+  const float* w = ws + ((size_t)b * nq + head) * num_splits * (D + 1);
+  float M = sinks ? sinks[head] * kLog2e : -INFINITY;
+  for (int s = 0; s < num_splits; ++s) M = fmaxf(M, w[s * (D + 1) + D]);
+  float den = sinks ? exp2f(sinks[head] * kLog2e - M) : 0.f;
+  for (int s = 0; s < num_splits; ++s) {
+    const float ls = w[s * (D + 1) + D];
+    if (ls != -INFINITY) den += exp2f(ls - M);
+  }
+  for (int dim = threadIdx.x; dim < D; dim += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < num_splits; ++s) {
+      const float ls = w[s * (D + 1) + D];
+      if (ls != -INFINITY) acc += w[s * (D + 1) + dim] * exp2f(ls - M);
+    }
+    out[(size_t)b * nq * D + (size_t)head * D + dim] = from_float<T>(den > 0.f ? acc / den * v_scale : 0.f);
+  }
+}
+
+template <int D, typename T, typename CT>
+static int launch_decode(void* out, const void* q, const void* kc, const void* vc, const int* bt, const int* sl,
+                         const float* sinks, int B, int nq, int nkv, int q_stride, int bs, int max_blocks, int window,
+                         float scale, float k_scale, float v_scale, float* ws, int num_splits, cudaStream_t s) {
+  if (B == 0) return 0;
+  if (num_splits > 1 && ws == nullptr) return kBadShape;
+  const size_t smem_tiles = 2 * 2 * kKT * D * sizeof(__nv_bfloat16) + (sizeof(CT) == 1 ? 2 * 2 * kKT * D : 0);
+  const size_t smem_merge = (4 * 16 * 2 + 4 * 16 * D) * sizeof(float);
+  const size_t smem = smem_tiles > smem_merge ? smem_tiles : smem_merge;
+  auto kern = decode_kernel<D, T, CT>;
+  static bool attr_set = false;  // host-side, once per instantiation
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr_set = true;
+  }
+  dim3 grid(num_splits, nkv, B);
+  kern<<<grid, 128, smem, s>>>((T*)out, (const T*)q, (const CT*)kc, (const CT*)vc, bt, sl, sinks, nq, nkv, q_stride,
+                               bs, max_blocks, window, scale * k_scale * kLog2e, v_scale, ws, num_splits);
+  if (num_splits > 1) {
+    decode_combine_kernel<D, T><<<dim3(nq, B), D < 128 ? D : 128, 0, s>>>((T*)out, ws, sinks, nq, num_splits,
+                                                                           v_scale);
+  }
+  return (int)cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------
+// Prefill / chunked prefill over the paged cache, and contiguous varlen attention.
+// ---------------------------------------------------------------------------------------
+struct PagedKV {
+  const int* block_tables;
+  int max_blocks, bs, nkv;
+};
+
+template <int D, int DP, typename T, typename CT, bool kPaged>
+__global__ void __launch_bounds__(128) prefill_kernel(T* __restrict__ out, const T* __restrict__ q,
+                                                      const CT* __restrict__ kc, const CT* __restrict__ vc,
+                                                      PagedKV pk, const int* __restrict__ seq_lens,
+                                                      const int* __restrict__ qsl, const float* __restrict__ sinks,
+                                                      int nq, int nkv, int q_stride, int kv_stride, int window,
+                                                      int causal, float scale_log2, float v_scale) {
+  // DP: head dim padded to a multiple of 16 for the QK^T k-steps (72 -> 80)
+  constexpr int C = DP / 8;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [2][64*DP]
+  __nv_bfloat16* Vs = Ks + 2 * kKT * DP;
+  uint8_t* stage = reinterpret_cast<uint8_t*>(Vs + 2 * kKT * DP);
+
+  const int qt = blockIdx.x, head = blockIdx.y, b = blockIdx.z;
+  const int G = nq / nkv, h = head / G;
+  const int q0 = qsl[b], qlen = qsl[b + 1] - q0;
+  if (qt * 64 >= qlen) return;
+  const int L = kPaged ? seq_lens[b] : qlen;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qd = lane & 3, r0 = lane >> 2;
+  const int pos_base = L - qlen;  // absolute position of query row 0
+  const int row_w = qt * 64 + warp * 16;  // first query row of this warp
+  // key range needed by the CTA
+  const int p_first = pos_base + qt * 64, p_last = pos_base + min(qlen, (qt + 1) * 64) - 1;
+  int key_lo = 0, key_hi = causal ? p_last + 1 : L;
+  if (window > 0) key_lo = max(0, p_first - window + 1);
+  key_lo = (key_lo / kKT) * kKT;
+
+  uint32_t qf[DP / 16][4];
+  {
+#pragma unroll
+    for (int kk = 0; kk < DP / 16; ++kk)
+#pragma unroll
+      for (int hv = 0; hv < 2; ++hv)
+#pragma unroll
+        for (int kh = 0; kh < 2; ++kh) {
+          const int row = row_w + r0 + hv * 8;
+          const int dim = kk * 16 + kh * 8 + 2 * qd;
+          float a = 0.f, c = 0.f;
+          if (row < qlen && dim < D) {
+            const T* qp = q + (size_t)(q0 + row) * q_stride + (size_t)head * D + dim;
+            a = to_float(qp[0]);
+            c = to_float(qp[1]);
+          }
+          qf[kk][kh * 2 + hv] = pack_bf16(a, c);
+        }
+  }
+  float o[DP / 8][4];
+#pragma unroll
+  for (int n = 0; n < DP / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  const int my_p[2] = {pos_base + row_w + r0, pos_base + row_w + r0 + 8};
+
+  auto load_tile = [&](int buf, int key0) {
+    __nv_bfloat16* K = Ks + buf * kKT * DP;
+    __nv_bfloat16* V = Vs + buf * kKT * DP;
+    if constexpr (kPaged) {
+      const int* bt_row = pk.block_tables + (size_t)b * pk.max_blocks;
+      if constexpr (D == DP) {
+        load_kv_tile<D, CT>(K, V, stage + buf * 2 * kKT * D, kc, vc, bt_row, key0, min(key_hi, L), pk.bs, nkv, h);
+      }
+    } else {
+      // contiguous [T, nkv, D] K/V of this sequence; D may be padded to DP with zeros
+      for (int i = threadIdx.x; i < kKT * C; i += blockDim.x) {
+        const int k = i / C, c = i % C;
+        const int gk = key0 + k;
+        const bool ok = gk < L && c * 8 < D;
+        const size_t off = ok ? ((size_t)(q0 + gk) * kv_stride + (size_t)h * D + c * 8) : 0;
+        cp_async16(K + swz(k, c, C) * 8, kc + off, ok ? 16 : 0);
+        cp_async16(V + swz(k, c, C) * 8, vc + off, ok ? 16 : 0);
+      }
+    }
+  };
+
+  const int ntiles = key_hi > key_lo ? cdiv(key_hi - key_lo, kKT) : 0;
+  if (ntiles > 0) {
+    load_tile(0, key_lo);
+    cp_async_commit();
+  }
+  for (int t = 0; t < ntiles; ++t) {
+    const int buf = t & 1;
+    if (t + 1 < ntiles) {
+      load_tile(buf ^ 1, key_lo + (t + 1) * kKT);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    __nv_bfloat16* K = Ks + buf * kKT * DP;
+    __nv_bfloat16* V = Vs + buf * kKT * DP;
+    if constexpr (kPaged && sizeof(CT) == 1) {
+      convert_fp8_tile<D>(K, V, stage + buf * 2 * kKT * D);
+      __syncthreads();
+    }
+    const int key0 = key_lo + t * kKT;
+    // skip tiles entirely outside this warp's visible range
+    // warp-uniform bounds: rows row_w .. row_w+15 sit at positions wp_lo .. wp_hi
+    const int wp_lo = pos_base + row_w, wp_hi = pos_base + row_w + 15;
+    const bool warp_dead = (row_w >= qlen) || (causal && key0 > wp_hi) ||
+                           (window > 0 && key0 + kKT - 1 <= wp_lo - window);
+    if (!warp_dead) {
+      float s[8][4];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < DP / 16; ++kk) {
+#pragma unroll
+        for (int jj = 0; jj < 8; jj += 2) {
+          const int mi = lane >> 3;
+          const int krow = jj * 8 + (mi >> 1) * 8 + (lane & 7);
+          const int kch = kk * 2 + (mi & 1);
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4(b0, b1, b2, b3, K + swz(krow, kch, C) * 8);
+          uint32_t bA[2] = {b0, b1}, bB[2] = {b2, b3};
+          mma_bf16_16816(s[jj], qf[kk], bA);
+          mma_bf16_16816(s[jj + 1], qf[kk], bB);
+        }
+      }
+      float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = key0 + j * 8 + 2 * qd + (e & 1);
+          const int p = my_p[e >> 1];
+          bool ok = key < L;
+          if (causal) ok = ok && key <= p;
+          if (window > 0) ok = ok && key > p - window;
+          const float v = ok ? s[j][e] * scale_log2 : -INFINITY;
+          s[j][e] = v;
+          mx[e >> 1] = fmaxf(mx[e >> 1], v);
+        }
+      float corr[2];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+        const float mnew = fmaxf(m_run[r], mx[r]);
+        corr[r] = (mnew == -INFINITY) ? 1.f : exp2f(m_run[r] - mnew);
+        m_run[r] = mnew;
+      }
+      float rs[2] = {0.f, 0.f};
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float mref = m_run[e >> 1];
+          const float p = (mref == -INFINITY) ? 0.f : exp2f(s[j][e] - mref);
+          s[j][e] = p;
+          rs[e >> 1] += p;
+        }
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
+        rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
+        l_run[r] = l_run[r] * corr[r] + rs[r];
+      }
+#pragma unroll
+      for (int n = 0; n < DP / 8; ++n) {
+        o[n][0] *= corr[0];
+        o[n][1] *= corr[0];
+        o[n][2] *= corr[1];
+        o[n][3] *= corr[1];
+      }
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {  // 64 keys = 4 k16 steps
+        uint32_t pa[4] = {pack_bf16(s[2 * kk][0], s[2 * kk][1]), pack_bf16(s[2 * kk][2], s[2 * kk][3]),
+                          pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]),
+                          pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3])};
+#pragma unroll
+        for (int n = 0; n < DP / 8; n += 2) {
+          const int mi = lane >> 3;
+          const int vrow = kk * 16 + (mi & 1) * 8 + (lane & 7);
+          const int vch = n + (mi >> 1);
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4_trans(b0, b1, b2, b3, V + swz(vrow, vch, C) * 8);
+          uint32_t bA[2] = {b0, b1}, bB[2] = {b2, b3};
+          mma_bf16_16816(o[n], pa, bA);
+          if (n + 1 < DP / 8) mma_bf16_16816(o[n + 1], pa, bB);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  // finalize with the sink
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    float l = l_run[r], M = m_run[r];
+    float f = 1.f;
+    if (sinks != nullptr) {
+      const float sk = sinks[head] * kLog2e;
+      const float Mn = fmaxf(M, sk);
+      f = (M == -INFINITY) ? 0.f : exp2f(M - Mn);
+      l = l * f + exp2f(sk - Mn);
+    }
+    const float inv = l > 0.f ? f / l * v_scale : 0.f;
+    const int row = row_w + r0 + r * 8;
+    if (row < qlen) {
+      T* op = out + (size_t)(q0 + row) * nq * D + (size_t)head * D;
+#pragma unroll
+      for (int n = 0; n < DP / 8; ++n) {
+        const int dim = n * 8 + 2 * qd;
+        if (dim < D) {
+          op[dim] = from_float<T>(o[n][r * 2] * inv);
+          op[dim + 1] = from_float<T>(o[n][r * 2 + 1] * inv);
+        }
+      }
+    }
+  }
+}
+
+template <int D, int DP, typename T, typename CT, bool kPaged>
+static int launch_prefill(void* out, const void* q, const void* kc, const void* vc, PagedKV pk, const int* sl,
+                          const int* qsl, const float* sinks, int B, int nq, int nkv, int q_stride, int kv_stride,
+                          int window, int causal, float scale, float k_scale, float v_scale, int max_q,
+                          cudaStream_t s) {
+  if (B == 0 || max_q == 0) return 0;
+  const size_t smem = 2 * 2 * kKT * DP * sizeof(__nv_bfloat16) + (sizeof(CT) == 1 ? 2 * 2 * kKT * D : 0);
+  auto kern = prefill_kernel<D, DP, T, CT, kPaged>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr_set = true;
+  }
+  dim3 grid(cdiv(max_q, 64), nq, B);
+  kern<<<grid, 128, smem, s>>>((T*)out, (const T*)q, (const CT*)kc, (const CT*)vc, pk, sl, qsl, sinks, nq, nkv,
+                               q_stride, kv_stride, window, causal, scale * k_scale * kLog2e, v_scale);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace b200
+
+using namespace b200;
+
+extern "C" int b200_paged_attention_decode(void* out, const void* q, const void* k_cache, const void* v_cache,
+                                           const int* block_tables, const int* seq_lens, const float* sinks, int B,
+                                           int nq, int nkv, int d, int q_stride, int block_size, int max_blocks,
+                                           int window, float scale, float k_scale, float v_scale, float* workspace,
+                                           int num_splits, int dtype, int cache_dtype, cudaStream_t s) {
+  if (nq % nkv || nq / nkv > 16 || dtype != kBF16) return kBadShape;
+  const bool fp8 = cache_dtype == kFP8E4M3;
+#define DEC(DD)                                                                                                    \
+  return fp8 ? launch_decode<DD, __nv_bfloat16, __nv_fp8_e4m3>(out, q, k_cache, v_cache, block_tables, seq_lens,   \
+                                                                sinks, B, nq, nkv, q_stride, block_size, max_blocks, \
+                                                                window, scale, k_scale, v_scale, workspace,          \
+                                                                num_splits, s)                                       \
+             : launch_decode<DD, __nv_bfloat16, __nv_bfloat16>(out, q, k_cache, v_cache, block_tables, seq_lens,   \
+                                                                sinks, B, nq, nkv, q_stride, block_size, max_blocks, \
+                                                                window, scale, k_scale, v_scale, workspace,          \
+                                                                num_splits, s);
+  if (d == 64) { DEC(64) }
+  if (d == 128) { DEC(128) }
+#undef DEC
+  return kBadShape;
+}
+
+extern "C" int b200_paged_attention_prefill(void* out, const void* q, const void* k_cache, const void* v_cache,
+                                            const int* block_tables, const int* seq_lens, const int* query_start_loc,
+                                            const float* sinks, int B, int T, int nq, int nkv, int d, int q_stride,
+                                            int block_size, int max_blocks, int window, float scale, float k_scale,
+                                            float v_scale, int max_query_len, int dtype, int cache_dtype,
+                                            cudaStream_t s) {
+  if (nq % nkv || dtype != kBF16) return kBadShape;
+  PagedKV pk{block_tables, max_blocks, block_size, nkv};
+  const bool fp8 = cache_dtype == kFP8E4M3;
+#define PRE(DD)                                                                                                     \
+  return fp8 ? launch_prefill<DD, DD, __nv_bfloat16, __nv_fp8_e4m3, true>(                                          \
+                   out, q, k_cache, v_cache, pk, seq_lens, query_start_loc, sinks, B, nq, nkv, q_stride, 0, window,  \
+                   1, scale, k_scale, v_scale, max_query_len, s)                                                     \
+             : launch_prefill<DD, DD, __nv_bfloat16, __nv_bfloat16, true>(                                          \
+                   out, q, k_cache, v_cache, pk, seq_lens, query_start_loc, sinks, B, nq, nkv, q_stride, 0, window,  \
+                   1, scale, k_scale, v_scale, max_query_len, s);
+  if (d == 64) { PRE(64) }
+  if (d == 128) { PRE(128) }
+#undef PRE
+  return kBadShape;
+}
+
+extern "C" int b200_varlen_attention(void* out, const void* q, const void* k, const void* v, const int* cu_seqlens,
+                                     int B, int T, int nq, int nkv, int d, float scale, int causal, int max_seqlen,
+                                     int dtype, cudaStream_t s) {
+  if (nq % nkv || dtype != kBF16) return kBadShape;
+  PagedKV pk{nullptr, 0, 0, nkv};
+#define VAR(DD, DDP)                                                                                           \
+  return launch_prefill<DD, DDP, __nv_bfloat16, __nv_bfloat16, false>(out, q, k, v, pk, nullptr, cu_seqlens,    \
+                                                                      nullptr, B, nq, nkv, nq * DD, nkv * DD, 0, \
+                                                                      causal, scale, 1.f, 1.f, max_seqlen, s);
+  if (d == 64) { VAR(64, 64) }
+  if (d == 72) { VAR(72, 80) }
+  if (d == 80) { VAR(80, 80) }
+  if (d == 128) { VAR(128, 128) }
+#undef VAR
+  return kBadShape;
+}

@@ -1,0 +1,65 @@
+// Shared device helpers for the sm_100a kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define B200_HD __host__ __device__ __forceinline__
+#define B200_D __device__ __forceinline__
+
+namespace b200 {
+
+// Error codes written to device status words by kernels that validate inputs or
+// bound their waits.  A kernel never traps: it records the first error and skips
+// the offending access.
+enum StatusCode : int {
+  kOk = 0,
+  kBadIndex = 1,      // block id / slot / token id out of range
+  kWaitTimeout = 2,   // bounded spin on a flag gave up
+  kBadShape = 3,
+  kBadAlignment = 4,
+};
+
+template <typename T> B200_D float to_float(T v);
+template <> B200_D float to_float<float>(float v) { return v; }
+template <> B200_D float to_float<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <> B200_D float to_float<__half>(__half v) { return __half2float(v); }
+template <> B200_D float to_float<__nv_fp8_e4m3>(__nv_fp8_e4m3 v) { return float(v); }
+
+template <typename T> B200_D T from_float(float v);
+template <> B200_D float from_float<float>(float v) { return v; }
+template <> B200_D __nv_bfloat16 from_float<__nv_bfloat16>(float v) { return __float2bfloat16(v); }
+template <> B200_D __half from_float<__half>(float v) { return __float2half(v); }
+template <> B200_D __nv_fp8_e4m3 from_float<__nv_fp8_e4m3>(float v) { return __nv_fp8_e4m3(v); }
+
+B200_D float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+B200_D float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide sum; `red` must hold >= 32 floats of shared memory.
+B200_D float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  float t = lane < nw ? red[lane] : 0.f;
+  t = warp_sum(t);
+  return t;
+}
+
+B200_HD int cdiv(int a, int b) { return (a + b - 1) / b; }
+
+}  // namespace b200

@@ -1,0 +1,449 @@
+// Mixture-of-experts forward on the Blackwell block-scaled tensor cores.
+//
+// Semantics (restated from functional/moe/moe_cte.py:448 and moe_block_tkg.py:56 of the
+// Trainium plugin): for every route (token t, slot j) whose expert is local,
+//   h   = W13[e] x_t + b13[e]               (gate/up rows interleaved: 2i gate, 2i+1 up)
+//   a_i = min(g_i, L) * sigmoid(alpha * min(g_i, L)) * (clamp(u_i, -L, L) + 1)
+//   y   = (W2[e] a + b2[e]) * w_tj
+//   out_t = sum_j y_tj                        (partial over this rank's experts)
+//
+// Design (B200):
+//   * weights stay in the checkpoint's MX format: e2m1 (or e4m3) values, ue8m0 scale per
+//     32 along K; rows are re-laid out once at load time only to pad K to a multiple of
+//     128 and to put the scales into 128-row x 4-block "atoms" (512 B) that tcgen05.cp
+//     copies straight into tensor memory;
+//   * activations are quantised per route to MXFP8 (e4m3 + ue8m0 per 32) into the same
+//     atom layout, grouped by expert (device-side histogram / scan / scatter: no host sync);
+//   * GEMMs are D[128 weight rows x NT routes] = W . X^T with
+//     tcgen05.mma.kind::mxf8f6f4.block_scale (A = weights, B = routes), fp32 accumulators
+//     in TMEM, operands staged by TMA (128-byte swizzle, no multicast) through an
+//     mbarrier ring, one elected thread issuing MMAs; small N keeps decode weight-streaming
+//     bound, larger N serves prefill;
+//   * epilogues read TMEM with tcgen05.ld: GEMM1 adds the bias and applies the clamped
+//     SwiGLU across the interleaved row pairs; GEMM2 adds the bias, scales by the route
+//     affinity and writes the per-route row; a reduce kernel sums each token's routes.
+#include "launch.h"
+#include "moe.h"
+#include "tcgen05.cuh"
+
+namespace b200 {
+
+constexpr int kSfAtom = 512;  // 128 rows x 4 scale bytes
+
+B200_HD size_t sf_byte(int atom, int kgroups, int row_in_atom, int kb) {
+  // kb = 32-element block index along K; atoms are [atom][kb/4][512]
+  return ((size_t)atom * kgroups + (kb >> 2)) * kSfAtom + (row_in_atom & 31) * 16 + (row_in_atom >> 5) * 4 +
+         (kb & 3);
+}
+
+// ------------------------------------------------------------------------- routing
+__global__ void __launch_bounds__(1024) moe_route_kernel(const int* __restrict__ topk_ids, int TK, int E, int off,
+                                                         int nt, int max_tiles, MoeWorkspace ws) {
+  extern __shared__ int sm[];
+  int* cnt = sm;           // [E]
+  int* cur = sm + E;       // [E]
+  for (int i = threadIdx.x; i < E; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  for (int r = threadIdx.x; r < TK; r += blockDim.x) {
+    const int e = topk_ids[r] - off;
+    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0, abase = 0, ntile = 0;
+    for (int e = 0; e < E; ++e) {
+      ws.offsets[e] = run;
+      ws.atom_base[e] = abase;
+      cur[e] = run;
+      for (int n0 = 0; n0 < cnt[e]; n0 += nt) {
+        if (ntile < max_tiles) {
+          ws.tiles[2 * ntile] = e;
+          ws.tiles[2 * ntile + 1] = n0;
+          ++ntile;
+        }
+      }
+      run += cnt[e];
+      abase += cdiv(cnt[e], 128);
+    }
+    ws.offsets[E] = run;
+    ws.atom_base[E] = abase;
+    *ws.num_tiles = ntile;
+  }
+  __syncthreads();
+  for (int r = threadIdx.x; r < TK; r += blockDim.x) {
+    const int e = topk_ids[r] - off;
+    if (e >= 0 && e < E) ws.row_route[atomicAdd(&cur[e], 1)] = r;
+  }
+}
+
+// ------------------------------------------------------------------ MXFP8 quantise
+// One warp per permuted row.  Source row = x[row_route[r] / k] (gather) or src[r].
+__global__ void __launch_bounds__(128) moe_quant_kernel(uint8_t* __restrict__ q, uint8_t* __restrict__ sf,
+                                                        const __nv_bfloat16* __restrict__ src, int src_ld,
+                                                        const int* __restrict__ row_route, int k_gather,
+                                                        const int* __restrict__ offsets,
+                                                        const int* __restrict__ atom_base, int E, int K, int Kp,
+                                                        int R_max) {
+  const int r = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= R_max || r >= offsets[E]) return;
+  // expert of row r: last e with offsets[e] <= r (binary search)
+  int lo = 0, hi = E;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (offsets[mid] <= r) lo = mid;
+    else hi = mid;
+  }
+  const int e = lo;
+  const int j = r - offsets[e];
+  const int atom = atom_base[e] + (j >> 7), ra = j & 127;
+  const int kgroups = Kp / 128;
+  const int srow = k_gather > 0 ? row_route[r] / k_gather : r;
+  const __nv_bfloat16* s = src + (size_t)srow * src_ld;
+  uint8_t* qr = q + (size_t)r * Kp;
+  for (int kb = lane; kb < Kp / 32; kb += 32) {
+    uint4 o[2];
+    uint8_t scale = 127;
+    if (kb * 32 < K) {
+      float v[32];
+      const uint4* p = reinterpret_cast<const uint4*>(s + kb * 32);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint4 u = p[c];
+        const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[c * 8 + i] = __bfloat162float(hb[i]);
+      }
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+      int ex = 0;  // floor(log2(amax)) - 8 (e4m3 emax), from the exponent bits
+      if (amax > 0.f) {
+        const int be = (int)((__float_as_uint(amax) >> 23) & 0xff);
+        ex = (be == 0 ? -127 : be - 127) - 8;
+        ex = max(-127, min(127, ex));
+      }
+      scale = (uint8_t)(ex + 127);
+      const float inv = exp2f((float)-ex);
+      uint8_t* ob = reinterpret_cast<uint8_t*>(o);
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        const __nv_fp8x2_storage_t pr =
+            __nv_cvt_float2_to_fp8x2(make_float2(v[i] * inv, v[i + 1] * inv), __NV_SATFINITE, __NV_E4M3);
+        ob[i] = (uint8_t)(pr & 0xff);
+        ob[i + 1] = (uint8_t)(pr >> 8);
+      }
+    } else {
+      o[0] = make_uint4(0, 0, 0, 0);
+      o[1] = make_uint4(0, 0, 0, 0);
+    }
+    uint4* qo = reinterpret_cast<uint4*>(qr + kb * 32);
+    qo[0] = o[0];
+    qo[1] = o[1];
+    sf[sf_byte(atom, kgroups, ra, kb)] = scale;
+  }
+}
+
+// ------------------------------------------------------------------------- GEMM
+enum Epi : int { kEpiSwiglu = 0, kEpiDown = 1 };
+
+template <int NT, int STAGES>
+struct GemmSmem {
+  static constexpr int kA = 128 * 128;  // bytes per A stage (padded fp4 or fp8)
+  static constexpr int kB = NT * 128;
+  static constexpr int kOffB = STAGES * kA;
+  static constexpr int kOffSfa = kOffB + STAGES * kB;
+  static constexpr int kOffSfb = kOffSfa + STAGES * kSfAtom;
+  static constexpr int kOffBar = kOffSfb + STAGES * kSfAtom;
+  static constexpr int kBytes = kOffBar + (2 * STAGES + 1) * 8 + 16;
+  static constexpr int kAlloc = kBytes + 1024;  // slack to align the base to 1024
+};
+
+template <int NT, int STAGES, bool A_FP4, int EPI>
+__global__ void __launch_bounds__(128) moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                       const __grid_constant__ CUtensorMap tmB,
+                                                       const uint8_t* __restrict__ sfa,
+                                                       const uint8_t* __restrict__ sfb, MoeWorkspace ws,
+                                                       const float* __restrict__ bias,
+                                                       const float* __restrict__ topk_w, __nv_bfloat16* __restrict__ out,
+                                                       int M, int Kp, int ld_out, float alpha, float limit,
+                                                       int* status) {
+  using L = GemmSmem<NT, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  const int tile = blockIdx.y;
+  if (tile >= *ws.num_tiles) return;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + L::kOffB;
+  uint8_t* sSfa = smem + L::kOffSfa;
+  uint8_t* sSfb = smem + L::kOffSfb;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
+  uint64_t* empty = full + STAGES;
+  uint64_t* done = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mt = blockIdx.x, m0 = mt * 128;
+  const int e = ws.tiles[2 * tile], n0 = ws.tiles[2 * tile + 1];
+  const int row0 = ws.offsets[e] + n0;
+  const int nvalid = min(NT, ws.offsets[e + 1] - ws.offsets[e] - n0);
+  const int atom = ws.atom_base[e] + (n0 >> 7);
+  const int sfb_shift = (n0 & 127) >> 5;  // 32-row groups inside the atom = TMEM columns
+  const int nk = Kp / 128;
+  const int mblk = cdiv(M, 128);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    tc::mbar_init(done, 1);
+    tc::fence_barrier_init();
+    tc::prefetch_tmap(&tmA);
+    tc::prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, 256);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    for (int kt = 0; kt < nk; ++kt) {
+      const int s = kt % STAGES, use = kt / STAGES;
+      if (kt >= STAGES && !tc::mbar_wait(&empty[s], (use - 1) & 1, status)) break;
+      // transaction bytes count the global (packed) size: fp4 tiles are 4 bits/element
+      tc::mbar_arrive_expect_tx(&full[s], (A_FP4 ? L::kA / 2 : L::kA) + L::kB + 2 * kSfAtom);
+      tc::tma_load_3d(sA + s * L::kA, &tmA, kt * 128, m0, e, &full[s]);
+      tc::tma_load_2d(sB + s * L::kB, &tmB, kt * 128, row0, &full[s]);
+      tc::bulk_load(sSfa + s * kSfAtom, sfa + (((size_t)e * mblk + mt) * nk + kt) * kSfAtom, kSfAtom, &full[s]);
+      tc::bulk_load(sSfb + s * kSfAtom, sfb + ((size_t)atom * nk + kt) * kSfAtom, kSfAtom, &full[s]);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    const uint32_t idesc0 = tc::idesc_mxf8f6f4(A_FP4 ? 5 : 0, 0, 128, NT);
+    const uint32_t t_d = tmem, t_sfa = tmem + NT, t_sfb = tmem + NT + 4;
+    bool ok = true;
+    for (int kt = 0; kt < nk; ++kt) {
+      const int s = kt % STAGES, use = kt / STAGES;
+      if (!tc::mbar_wait(&full[s], use & 1, status)) {
+        ok = false;
+        break;
+      }
+      tc::fence_after_sync();
+      tc::utccp_32x128b_warpx4(t_sfa, tc::desc_noswizzle_16b_rows(sSfa + s * kSfAtom));
+      tc::utccp_32x128b_warpx4(t_sfb, tc::desc_noswizzle_16b_rows(sSfb + s * kSfAtom));
+      const uint64_t ad = tc::desc_sw128(sA + s * L::kA);
+      const uint64_t bd = tc::desc_sw128(sB + s * L::kB);
+#pragma unroll
+      for (int kb = 0; kb < 4; ++kb) {
+        tc::mma_mxf8f6f4(t_d, ad + 2 * kb, bd + 2 * kb, tc::idesc_with_sf_ids(idesc0, kb, kb),
+                         t_sfa | ((uint32_t)kb << 30), (t_sfb + sfb_shift) | ((uint32_t)kb << 30),
+                         (kt | kb) != 0 ? 1u : 0u);
+      }
+      tc::mma_commit(&empty[s]);
+    }
+    (void)ok;
+    tc::mma_commit(done);
+  }
+  __syncwarp();
+  // ---------------- epilogue (all 4 warps: TMEM lanes 32w..32w+31) ----------------
+  const bool ok = tc::mbar_wait(done, 0, status);
+  tc::fence_after_sync();
+  if (ok) {
+    const int m = warp * 32 + lane;
+    const int gm = m0 + m;
+    const float b = gm < M ? bias[(size_t)e * M + gm] : 0.f;
+    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+    for (int c = 0; c < NT; c += 32) {
+      if (c >= nvalid) break;
+      uint32_t r[32];
+      tc::tmem_ld_32x32b_x32(lane_addr + c, r);
+      tc::tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int j = c + i;
+        const float v = __uint_as_float(r[i]) + b;
+        if constexpr (EPI == kEpiSwiglu) {
+          const float other = __shfl_xor_sync(0xffffffffu, v, 1);
+          if (!(m & 1) && j < nvalid && gm < M) {
+            float g = v, u = other, a;
+            if (limit > 0.f) {
+              g = fminf(g, limit);
+              u = fminf(fmaxf(u, -limit), limit);
+              a = g / (1.f + __expf(-alpha * g)) * (u + 1.f);
+            } else {
+              a = g / (1.f + __expf(-g)) * u;
+            }
+            out[(size_t)(row0 + j) * ld_out + (gm >> 1)] = __float2bfloat16(a);
+          }
+        } else {
+          if (j < nvalid && gm < M) {
+            const int route = ws.row_route[row0 + j];
+            out[(size_t)route * ld_out + gm] = __float2bfloat16(v * topk_w[route]);
+          }
+        }
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) tc::tmem_dealloc(tmem, 256);
+}
+
+// ------------------------------------------------------------------------- reduce
+__global__ void moe_reduce_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ y,
+                                  const int* __restrict__ topk_ids, int k, int E, int off, int H) {
+  const int t = blockIdx.x;
+  for (int h2 = threadIdx.x; h2 < H / 2; h2 += blockDim.x) {
+    float a0 = 0.f, a1 = 0.f;
+    for (int j = 0; j < k; ++j) {
+      const int e = topk_ids[t * k + j] - off;
+      if (e < 0 || e >= E) continue;
+      const __nv_bfloat162 v = reinterpret_cast<const __nv_bfloat162*>(y + (size_t)(t * k + j) * H)[h2];
+      a0 += __low2float(v);
+      a1 += __high2float(v);
+    }
+    reinterpret_cast<__nv_bfloat162*>(out + (size_t)t * H)[h2] = __floats2bfloat162_rn(a0, a1);
+  }
+}
+
+// ------------------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 3-D weight map [E, rows, Kp] (fp4 packed two per byte, or e4m3), box 128 x 128 x 1.
+static int make_weight_map(CUtensorMap* m, const void* w, int E, int rows, int Kp, bool fp4) {
+  auto enc = get_encode();
+  if (!enc) return kBadShape;
+  const uint64_t row_bytes = fp4 ? (uint64_t)Kp / 2 : (uint64_t)Kp;
+  cuuint64_t dims[3] = {(cuuint64_t)Kp, (cuuint64_t)rows, (cuuint64_t)E};
+  cuuint64_t strides[2] = {row_bytes, row_bytes * rows};
+  cuuint32_t box[3] = {128, 128, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = enc(m, fp4 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, 3,
+                   const_cast<void*>(w), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : 1000 + (int)r;
+}
+
+// 2-D activation map [R, Kp] e4m3, box 128 x NT.
+static int make_act_map(CUtensorMap* m, const void* q, int R, int Kp, int nt) {
+  auto enc = get_encode();
+  if (!enc) return kBadShape;
+  cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)R};
+  cuuint64_t strides[1] = {(cuuint64_t)Kp};
+  cuuint32_t box[2] = {128, (cuuint32_t)nt};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(q), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : 1000 + (int)r;
+}
+
+template <int NT, int STAGES, bool A_FP4, int EPI>
+static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const uint8_t* sfa, const uint8_t* sfb,
+                       const MoeWorkspace& ws, const float* bias, const float* topk_w, void* out, int M, int Kp,
+                       int ld_out, float alpha, float limit, int max_tiles, int* status, cudaStream_t s) {
+  using L = GemmSmem<NT, STAGES>;
+  auto kern = moe_gemm_kernel<NT, STAGES, A_FP4, EPI>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    attr = true;
+  }
+  dim3 grid(cdiv(M, 128), max_tiles);
+  kern<<<grid, 128, L::kAlloc, s>>>(ta, tb, sfa, sfb, ws, bias, topk_w, (__nv_bfloat16*)out, M, Kp, ld_out, alpha,
+                                    limit, status);
+  return (int)cudaGetLastError();
+}
+
+template <int NT, int STAGES, bool A_FP4>
+static int run_gemms(const MoeShape& sh, const void* w13, const uint8_t* sf13, const float* b13, const void* w2,
+                     const uint8_t* sf2w, const float* b2, const float* topk_w, const MoeWorkspace& ws, float alpha,
+                     float limit, int R_max, int max_tiles, int* status, cudaStream_t s) {
+  CUtensorMap ta1, tb1, ta2, tb2;
+  int rc;
+  if ((rc = make_weight_map(&ta1, w13, sh.E_local, 2 * sh.I, sh.K1p, A_FP4))) return rc;
+  if ((rc = make_act_map(&tb1, ws.xq, R_max, sh.K1p, NT))) return rc;
+  if ((rc = make_weight_map(&ta2, w2, sh.E_local, sh.H, sh.K2p, A_FP4))) return rc;
+  if ((rc = make_act_map(&tb2, ws.aq, R_max, sh.K2p, NT))) return rc;
+  rc = launch_gemm<NT, STAGES, A_FP4, kEpiSwiglu>(ta1, tb1, sf13, ws.sf1, ws, b13, topk_w, ws.act, 2 * sh.I,
+                                                  sh.K1p, sh.I, alpha, limit, max_tiles, status, s);
+  if (rc) return rc;
+  moe_quant_kernel<<<cdiv(R_max, 4), 128, 0, s>>>(ws.aq, ws.sf2, (const __nv_bfloat16*)ws.act, sh.I, ws.row_route,
+                                                  0, ws.offsets, ws.atom_base, sh.E_local, sh.I, sh.K2p, R_max);
+  rc = launch_gemm<NT, STAGES, A_FP4, kEpiDown>(ta2, tb2, sf2w, ws.sf2, ws, b2, topk_w, ws.y, sh.H, sh.K2p, sh.H,
+                                                alpha, limit, max_tiles, status, s);
+  return rc;
+}
+
+}  // namespace b200
+
+using namespace b200;
+
+static void ws_sizes(const MoeShape& sh, int64_t* z) {
+  const int64_t R = (int64_t)sh.T * sh.k;
+  const int64_t max_tiles = cdiv((int)R, sh.nt) + sh.E_local;
+  const int64_t atoms = cdiv((int)R, 128) + sh.E_local;
+  z[0] = (sh.E_local + 1) * 4;
+  z[1] = (sh.E_local + 1) * 4;
+  z[2] = sh.E_local * 4;
+  z[3] = R * 4;
+  z[4] = max_tiles * 2 * 4;
+  z[5] = 4;
+  z[6] = R * sh.K1p;
+  z[7] = atoms * (sh.K1p / 128) * kSfAtom;
+  z[8] = R * sh.I * 2;
+  z[9] = R * sh.K2p;
+  z[10] = atoms * (sh.K2p / 128) * kSfAtom;
+  z[11] = R * sh.H * 2;
+}
+
+extern "C" void b200_moe_workspace_sizes(const MoeShape* shape, int64_t* sizes) { ws_sizes(*shape, sizes); }
+
+extern "C" int b200_moe_mx_forward(void* out, const void* x, const int* topk_ids, const float* topk_w,
+                                   const void* w13, const uint8_t* sf13, const float* b13, const void* w2,
+                                   const uint8_t* sf2w, const float* b2, const MoeShape* shape, float alpha,
+                                   float limit, const MoeWorkspace* wsp, int* status, cudaStream_t s) {
+  const MoeShape& sh = *shape;
+  const MoeWorkspace& ws = *wsp;
+  if (sh.T == 0) return 0;
+  if (sh.K1p % 128 || sh.K2p % 128 || sh.H % 2 || sh.I % 32 || sh.H % 32 || sh.E_local > 1024) return kBadShape;
+  if (sh.nt != 32 && sh.nt != 128) return kBadShape;
+  const int R_max = sh.T * sh.k;
+  const int max_tiles = cdiv(R_max, sh.nt) + sh.E_local;
+  moe_route_kernel<<<1, 1024, 2 * sh.E_local * sizeof(int), s>>>(topk_ids, R_max, sh.E_local, sh.expert_offset,
+                                                                 sh.nt, max_tiles, ws);
+  moe_quant_kernel<<<cdiv(R_max, 4), 128, 0, s>>>(ws.xq, ws.sf1, (const __nv_bfloat16*)x, sh.H, ws.row_route,
+                                                  sh.k, ws.offsets, ws.atom_base, sh.E_local, sh.H, sh.K1p, R_max);
+  int rc;
+  if (sh.nt == 32) {
+    rc = sh.a_fp4 ? run_gemms<32, 4, true>(sh, w13, sf13, b13, w2, sf2w, b2, topk_w, ws, alpha, limit, R_max,
+                                           max_tiles, status, s)
+                  : run_gemms<32, 4, false>(sh, w13, sf13, b13, w2, sf2w, b2, topk_w, ws, alpha, limit, R_max,
+                                            max_tiles, status, s);
+  } else {
+    rc = sh.a_fp4 ? run_gemms<128, 4, true>(sh, w13, sf13, b13, w2, sf2w, b2, topk_w, ws, alpha, limit, R_max,
+                                            max_tiles, status, s)
+                  : run_gemms<128, 4, false>(sh, w13, sf13, b13, w2, sf2w, b2, topk_w, ws, alpha, limit, R_max,
+                                             max_tiles, status, s);
+  }
+  if (rc) return rc;
+  moe_reduce_kernel<<<sh.T, 256, 0, s>>>((__nv_bfloat16*)out, (const __nv_bfloat16*)ws.y, topk_ids, sh.k,
+                                         sh.E_local, sh.expert_offset, sh.H);
+  return (int)cudaGetLastError();
+}

@@ -29,6 +29,7 @@ import torch.nn as nn
 from .. import ops
 from ..nn.linear import ParallelLMHead, RMSNorm, RowParallelLinear, VocabParallelEmbedding
 from ..ops import reference as ref
+from ..ops.mx_layout import pad_k, round_up, scales_to_atoms
 from ..parallel.state import GroupCoordinator, ParallelState
 from .base import KVSpec, LayerSpec, kv_head_sharding
 
@@ -165,13 +166,16 @@ class GptOssExperts(nn.Module):
         self.offset = ep_rank * self.E_local
         self.quant = cfg.quantization
         self.alpha, self.limit = cfg.swiglu_alpha, cfg.swiglu_limit
+        self.H, self.I = H, I
         if self.quant == "mxfp4":
             if H % 32 or I % 32:
                 raise ValueError("MXFP4 needs hidden and intermediate sizes divisible by 32")
-            self.w13 = _param((self.E_local, 2 * I, H // 2), torch.uint8, device)
-            self.s13 = _param((self.E_local, 2 * I, H // 32), torch.uint8, device)
-            self.w2 = _param((self.E_local, H, I // 2), torch.uint8, device)
-            self.s2 = _param((self.E_local, H, I // 32), torch.uint8, device)
+            # kernel layout (ops/mx_layout.py): K padded to 128, scales in 512-byte atoms
+            k1, k2 = round_up(H, 128), round_up(I, 128)
+            self.w13 = _param((self.E_local, 2 * I, k1 // 2), torch.uint8, device)
+            self.s13 = _param((self.E_local, -(-2 * I // 128), k1 // 128, 512), torch.uint8, device)
+            self.w2 = _param((self.E_local, H, k2 // 2), torch.uint8, device)
+            self.s2 = _param((self.E_local, -(-H // 128), k2 // 128, 512), torch.uint8, device)
         else:
             self.w13 = _param((self.E_local, 2 * I, H), dtype, device)
             self.w2 = _param((self.E_local, H, I), dtype, device)
@@ -184,7 +188,7 @@ class GptOssExperts(nn.Module):
     def forward(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         if self.quant == "mxfp4":
             return ops.moe_mxfp4(x, ids, w, self.w13, self.s13, self.b13, self.w2, self.s2, self.b2, self.offset,
-                                 self.alpha, self.limit)
+                                 self.alpha, self.limit, self.H, self.I)
         return ops.moe_dense(x, ids, w, self.w13, self.b13, self.w2, self.b2, self.offset, self.alpha, self.limit)
 
 
@@ -339,9 +343,13 @@ class GptOssForCausalLM(nn.Module):
     @staticmethod
     def _load_mx(ex: GptOssExperts, which: str, kind: str, t: torch.Tensor) -> None:
         loc = ex.local(t)
+        K = ex.H if which == "13" else ex.I
         if ex.quant == "mxfp4":
-            dst = getattr(ex, ("w" if kind == "blocks" else "s") + which)
-            dst.data.copy_(loc.reshape(dst.shape))
+            if kind == "blocks":
+                vals = loc.reshape(loc.shape[0], loc.shape[1], -1)
+                getattr(ex, "w" + which).data.copy_(pad_k(vals.to(ex.w13.device), K))
+            else:
+                getattr(ex, "s" + which).data.copy_(scales_to_atoms(loc.to(ex.w13.device), K))
             return
         # bf16 model served from an MXFP4 checkpoint: dequantise at load time
         # (``weight_loaders_bf16.py:264``); needs the matching blocks/scales pair.
@@ -355,8 +363,9 @@ class GptOssForCausalLM(nn.Module):
     @staticmethod
     def _load_dense(ex: GptOssExperts, which: str, w: torch.Tensor) -> None:
         if ex.quant == "mxfp4":
+            K = ex.H if which == "13" else ex.I
             blocks, scales = ref.quantize_mxfp4(w.float())
-            getattr(ex, "w" + which).data.copy_(blocks)
-            getattr(ex, "s" + which).data.copy_(scales)
+            getattr(ex, "w" + which).data.copy_(pad_k(blocks, K))
+            getattr(ex, "s" + which).data.copy_(scales_to_atoms(scales, K))
         else:
             getattr(ex, "w" + which).data.copy_(w.to(getattr(ex, "w" + which).dtype))

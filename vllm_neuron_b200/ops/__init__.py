@@ -20,6 +20,33 @@ from ._ext import kernels_enabled, use_kernel  # noqa: F401
 from ._ext import ops as _k
 from .metadata import AttentionMetadata  # noqa: F401
 
+_STATUS: dict = {}
+
+
+def device_status(device: torch.device) -> torch.Tensor:
+    """Per-device int32 status word that kernels with bounded waits or index checks
+    write (0 = ok; see ``csrc/common.cuh`` StatusCode).  Read it with
+    :func:`check_device_status` between steps."""
+    key = str(device)
+    t = _STATUS.get(key)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=device)
+        _STATUS[key] = t
+    return t
+
+
+def check_device_status(device: torch.device) -> int:
+    """Raise if a kernel on ``device`` recorded an error; returns the code (0)."""
+    t = _STATUS.get(str(device))
+    if t is None:
+        return 0
+    code = int(t.item())
+    if code:
+        t.zero_()
+        names = {1: "index out of range", 2: "device wait timed out", 3: "bad shape", 4: "bad alignment"}
+        raise RuntimeError(f"kernel status {code}: {names.get(code, 'unknown')}")
+    return 0
+
 # ---------------------------------------------------------------------------
 # dense layers
 # ---------------------------------------------------------------------------
@@ -187,20 +214,25 @@ def router_topk(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, top_k:
 
 def moe_mxfp4(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, w13: torch.Tensor,
               s13: torch.Tensor, b13: torch.Tensor | None, w2: torch.Tensor, s2: torch.Tensor,
-              b2: torch.Tensor | None, expert_offset: int, alpha: float, limit: float,
-              scratch: dict | None = None) -> torch.Tensor:
-    """Routed experts with packed MXFP4 weights.
-
-    w13 [E_local, 2I, H/2] u8 + s13 [E_local, 2I, H/32] (gate/up interleaved rows),
-    w2 [E_local, H, I/2] u8 + s2 [E_local, H, I/32]; biases fp32.  Returns the
-    partial sum over this rank's experts, [T, H] in x.dtype."""
-    if use_kernel(x):
-        out = torch.empty_like(x)
-        _k().moe_mxfp4(out, x, topk_ids, topk_w, w13, s13, b13, w2, s2, b2, expert_offset, alpha, limit)
-        return out
+              b2: torch.Tensor | None, expert_offset: int, alpha: float, limit: float, H: int, I: int,
+              status: torch.Tensor | None = None) -> torch.Tensor:
+    """Routed experts with packed MX weights in the kernel layout (``ops/mx_layout.py``):
+    w13 [E_local, 2I, K1p/2] u8 (gate/up interleaved rows) + s13 scale atoms,
+    w2 [E_local, H, K2p/2] u8 + s2 atoms; biases fp32 [E_local, 2I] / [E_local, H].
+    Returns this rank's partial sum over its experts, [T, H] in x.dtype."""
     E = w13.shape[0]
-    w13f = ref.dequant_mxfp4(w13, s13)
-    w2f = ref.dequant_mxfp4(w2, s2)
+    if use_kernel(x) and x.dtype == torch.bfloat16:
+        out = torch.empty_like(x)
+        b13_ = b13 if b13 is not None else torch.zeros(E, 2 * I, dtype=torch.float32, device=x.device)
+        b2_ = b2 if b2 is not None else torch.zeros(E, H, dtype=torch.float32, device=x.device)
+        st = status if status is not None else device_status(x.device)
+        _k().moe_mx(out, x.contiguous(), topk_ids.to(torch.int32).contiguous(), topk_w.float().contiguous(), w13,
+                    s13, b13_, w2, s2, b2_, expert_offset, H, I, True, alpha, limit, st)
+        return out
+    from .mx_layout import atoms_to_scales, unpad_k
+
+    w13f = ref.dequant_mxfp4(unpad_k(w13, H), atoms_to_scales(s13, 2 * I, H))
+    w2f = ref.dequant_mxfp4(unpad_k(w2, I), atoms_to_scales(s2, H, I))
     return ref.moe_experts(x, topk_ids, topk_w, w13f, b13, w2f, b2, alpha, limit, True, expert_offset)
 
 

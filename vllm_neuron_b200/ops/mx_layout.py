@@ -1,0 +1,55 @@
+"""Kernel layout of MX-format (MXFP4 / MXFP8) expert weights.
+
+The checkpoint stores, per expert, ``blocks [rows, K/32, 16]`` (two e2m1 per byte) and
+``scales [rows, K/32]`` (ue8m0).  The tensor-core kernel reads:
+* values ``[E, rows, Kp/2]`` (fp4) or ``[E, rows, Kp]`` (fp8) with K zero-padded to
+  ``Kp = roundup(K, 128)`` (the TMA unpack-to-shared-memory mode for fp4 needs the
+  inner extent to be a multiple of 128 elements);
+* scales in 512-byte atoms ``[E, ceil(rows/128), Kp/128, 512]``: byte
+  ``(r % 32) * 16 + (r // 32) * 4 + j`` of an atom holds the scale of row ``r`` (of 128)
+  and 32-element block ``j`` (of 4); padding scales are 127 (2^0), never NaN.
+Both conversions are exact (pure data movement).
+"""
+
+from __future__ import annotations
+
+import torch
+
+
+def round_up(x: int, m: int) -> int:
+    return (x + m - 1) // m * m
+
+
+def pad_k(values: torch.Tensor, K: int, fp4: bool = True) -> torch.Tensor:
+    """values [..., rows, K/2] (fp4) or [..., rows, K] -> zero-padded along K to Kp."""
+    Kp = round_up(K, 128)
+    width = Kp // 2 if fp4 else Kp
+    cur = values.shape[-1]
+    if cur == width:
+        return values.contiguous()
+    out = torch.zeros(*values.shape[:-1], width, dtype=values.dtype, device=values.device)
+    out[..., :cur] = values
+    return out
+
+
+def scales_to_atoms(scales: torch.Tensor, K: int) -> torch.Tensor:
+    """scales [E, rows, K/32] uint8 -> atoms [E, ceil(rows/128), Kp/128, 512] uint8."""
+    E, R, nb = scales.shape
+    Kp = round_up(K, 128)
+    Rp = round_up(R, 128)
+    full = torch.full((E, Rp, Kp // 32), 127, dtype=torch.uint8, device=scales.device)
+    full[:, :R, :nb] = scales
+    # [E, Rb, 4(r//32), 32(r%32), Kg, 4(j)] -> [E, Rb, Kg, r%32, r//32, j]
+    v = full.view(E, Rp // 128, 4, 32, Kp // 128, 4).permute(0, 1, 4, 3, 2, 5)
+    return v.contiguous().view(E, Rp // 128, Kp // 128, 512)
+
+
+def atoms_to_scales(atoms: torch.Tensor, rows: int, K: int) -> torch.Tensor:
+    E, Rb, Kg, _ = atoms.shape
+    v = atoms.view(E, Rb, Kg, 32, 4, 4).permute(0, 1, 4, 3, 2, 5).contiguous()
+    full = v.view(E, Rb * 128, Kg * 4)
+    return full[:, :rows, : K // 32].contiguous()
+
+
+def unpad_k(values: torch.Tensor, K: int, fp4: bool = True) -> torch.Tensor:
+    return values[..., : (K // 2 if fp4 else K)]
