@@ -381,10 +381,11 @@ __global__ void __launch_bounds__(128) prefill_kernel(T* __restrict__ out, const
                                                       int causal, float scale_log2, float v_scale) {
   // DP: head dim padded to a multiple of 16 for the QK^T k-steps (72 -> 80)
   constexpr int C = DP / 8;
+  constexpr int kTile = kKT * ((C % 8 == 0) ? C : (C | 1)) * 8;  // elements per K or V tile
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [2][64*DP]
-  __nv_bfloat16* Vs = Ks + 2 * kKT * DP;
-  uint8_t* stage = reinterpret_cast<uint8_t*>(Vs + 2 * kKT * DP);
+  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [2][kTile]
+  __nv_bfloat16* Vs = Ks + 2 * kTile;
+  uint8_t* stage = reinterpret_cast<uint8_t*>(Vs + 2 * kTile);
 
   const int qt = blockIdx.x, head = blockIdx.y, b = blockIdx.z;
   const int G = nq / nkv, h = head / G;
@@ -427,8 +428,8 @@ __global__ void __launch_bounds__(128) prefill_kernel(T* __restrict__ out, const
   const int my_p[2] = {pos_base + row_w + r0, pos_base + row_w + r0 + 8};
 
   auto load_tile = [&](int buf, int key0) {
-    __nv_bfloat16* K = Ks + buf * kKT * DP;
-    __nv_bfloat16* V = Vs + buf * kKT * DP;
+    __nv_bfloat16* K = Ks + buf * kTile;
+    __nv_bfloat16* V = Vs + buf * kTile;
     if constexpr (kPaged) {
       const int* bt_row = pk.block_tables + (size_t)b * pk.max_blocks;
       if constexpr (D == DP) {
@@ -462,8 +463,8 @@ __global__ void __launch_bounds__(128) prefill_kernel(T* __restrict__ out, const
       cp_async_wait<0>();
     }
     __syncthreads();
-    __nv_bfloat16* K = Ks + buf * kKT * DP;
-    __nv_bfloat16* V = Vs + buf * kKT * DP;
+    __nv_bfloat16* K = Ks + buf * kTile;
+    __nv_bfloat16* V = Vs + buf * kTile;
     if constexpr (kPaged && sizeof(CT) == 1) {
       convert_fp8_tile<D>(K, V, stage + buf * 2 * kKT * D);
       __syncthreads();
@@ -591,7 +592,8 @@ static int launch_prefill(void* out, const void* q, const void* kc, const void* 
                           int window, int causal, float scale, float k_scale, float v_scale, int max_q,
                           cudaStream_t s) {
   if (B == 0 || max_q == 0) return 0;
-  const size_t smem = 2 * 2 * kKT * DP * sizeof(__nv_bfloat16) + (sizeof(CT) == 1 ? 2 * 2 * kKT * D : 0);
+  const size_t tile = (size_t)kKT * row_stride_chunks(DP / 8) * 8;
+  const size_t smem = 2 * 2 * tile * sizeof(__nv_bfloat16) + (sizeof(CT) == 1 ? 2 * 2 * kKT * D : 0);
   auto kern = prefill_kernel<D, DP, T, CT, kPaged>;
   static bool attr_set = false;
   if (!attr_set) {

@@ -41,9 +41,18 @@ B200_D uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Swizzled offset (in 16-byte chunks) of chunk `c` of row `r` for rows of
-// `chunks_per_row` 16-byte chunks: XOR with the row index mod 8 removes ldmatrix
-// bank conflicts for rows of >= 128 bytes.
-B200_D int swz(int r, int c, int chunks_per_row) { return r * chunks_per_row + (c ^ (r & 7)); }
+// Offset (in 16-byte chunks) of chunk `c` of row `r` in a tile whose rows hold
+// `chunks_per_row` chunks.  Rows of a multiple of 8 chunks use the XOR swizzle (chunk ^
+// row mod 8), which keeps the row length and removes ldmatrix bank conflicts.  Other
+// widths (e.g. head dim 72 padded to 80 = 10 chunks) use an odd row stride instead,
+// `row_stride_chunks(C)`, which is conflict-free for 8-row ldmatrix reads as well; the
+// XOR would push chunks past the end of such rows.
+B200_HD int row_stride_chunks(int chunks_per_row) {
+  return (chunks_per_row % 8 == 0) ? chunks_per_row : (chunks_per_row | 1);
+}
+B200_D int swz(int r, int c, int chunks_per_row) {
+  if (chunks_per_row % 8 == 0) return r * chunks_per_row + (c ^ (r & 7));
+  return r * row_stride_chunks(chunks_per_row) + c;
+}
 
 }  // namespace b200

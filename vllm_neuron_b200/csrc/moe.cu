@@ -30,6 +30,16 @@ namespace b200 {
 
 constexpr int kSfAtom = 512;  // 128 rows x 4 scale bytes
 
+// Self-checks: record (code, where, value) in status[0..2] (first error wins) and let the
+// caller skip the access.  status may be null.
+B200_D void record(int* status, int code, int where, int value) {
+  if (status && atomicCAS(status, 0, code) == 0) {
+    status[1] = where;
+    status[2] = value;
+  }
+}
+B200_D bool misaligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) != 0; }
+
 B200_HD size_t sf_byte(int atom, int kgroups, int row_in_atom, int kb) {
   // kb = 32-element block index along K; atoms are [atom][kb/4][512]
   return ((size_t)atom * kgroups + (kb >> 2)) * kSfAtom + (row_in_atom & 31) * 16 + (row_in_atom >> 5) * 4 +
@@ -63,7 +73,7 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int* __restrict__
         }
       }
       run += cnt[e];
-      abase += cdiv(cnt[e], 128);
+      abase += cdiv(cnt[e], nt);  // one 512-byte scale atom per N tile
     }
     ws.offsets[E] = run;
     ws.atom_base[E] = abase;
@@ -83,10 +93,15 @@ __global__ void __launch_bounds__(128) moe_quant_kernel(uint8_t* __restrict__ q,
                                                         const int* __restrict__ row_route, int k_gather,
                                                         const int* __restrict__ offsets,
                                                         const int* __restrict__ atom_base, int E, int K, int Kp,
-                                                        int R_max) {
+                                                        int R_max, int src_rows, int atoms_max, int nt,
+                                                        int* status) {
   const int r = blockIdx.x * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (r >= R_max || r >= offsets[E]) return;
+  if (offsets[E] > R_max) {
+    if (lane == 0) record(status, kBadIndex, 10, offsets[E]);
+    return;
+  }
   // expert of row r: last e with offsets[e] <= r (binary search)
   int lo = 0, hi = E;
   while (hi - lo > 1) {
@@ -96,11 +111,21 @@ __global__ void __launch_bounds__(128) moe_quant_kernel(uint8_t* __restrict__ q,
   }
   const int e = lo;
   const int j = r - offsets[e];
-  const int atom = atom_base[e] + (j >> 7), ra = j & 127;
+  // every N tile owns a scale atom whose first `nt` rows it uses, so the MMA always reads
+  // the scale factors from the atom's first TMEM columns
+  const int atom = atom_base[e] + j / nt, ra = j % nt;
   const int kgroups = Kp / 128;
   const int srow = k_gather > 0 ? row_route[r] / k_gather : r;
+  if (srow < 0 || srow >= src_rows || atom >= atoms_max) {
+    if (lane == 0) record(status, kBadIndex, 11, srow >= src_rows || srow < 0 ? srow : 100000 + atom);
+    return;
+  }
   const __nv_bfloat16* s = src + (size_t)srow * src_ld;
   uint8_t* qr = q + (size_t)r * Kp;
+  if (misaligned(s, 16) || misaligned(qr, 16)) {
+    if (lane == 0) record(status, kBadAlignment, 12, (int)(reinterpret_cast<uintptr_t>(s) & 0xffff));
+    return;
+  }
   for (int kb = lane; kb < Kp / 32; kb += 32) {
     uint4 o[2];
     uint8_t scale = 127;
@@ -167,12 +192,23 @@ __global__ void __launch_bounds__(128) moe_gemm_kernel(const __grid_constant__ C
                                                        const float* __restrict__ bias,
                                                        const float* __restrict__ topk_w, __nv_bfloat16* __restrict__ out,
                                                        int M, int Kp, int ld_out, float alpha, float limit,
-                                                       int* status) {
+                                                       int E_local, int R_max, int atoms_max, int* status) {
   using L = GemmSmem<NT, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   const int tile = blockIdx.y;
   if (tile >= *ws.num_tiles) return;
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // align the shared-space offset (not the generic address) to 1024 for the 128-byte swizzle
+  const uint32_t raw_off = tc::smem_addr(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_off & 1023u)) & 1023u);
+  {
+    const int e_ = ws.tiles[2 * tile], n0_ = ws.tiles[2 * tile + 1];
+    bool bad = e_ < 0 || e_ >= E_local || n0_ < 0;
+    if (!bad) bad = ws.offsets[e_] + n0_ >= R_max || tile >= atoms_max;
+    if (bad || (tc::smem_addr(smem) & 1023u) != 0) {
+      if (threadIdx.x == 0) record(status, bad ? kBadIndex : kBadAlignment, 20, bad ? e_ : (int)tc::smem_addr(smem));
+      return;
+    }
+  }
   uint8_t* sA = smem;
   uint8_t* sB = smem + L::kOffB;
   uint8_t* sSfa = smem + L::kOffSfa;
@@ -187,8 +223,7 @@ __global__ void __launch_bounds__(128) moe_gemm_kernel(const __grid_constant__ C
   const int e = ws.tiles[2 * tile], n0 = ws.tiles[2 * tile + 1];
   const int row0 = ws.offsets[e] + n0;
   const int nvalid = min(NT, ws.offsets[e + 1] - ws.offsets[e] - n0);
-  const int atom = ws.atom_base[e] + (n0 >> 7);
-  const int sfb_shift = (n0 & 127) >> 5;  // 32-row groups inside the atom = TMEM columns
+  const int atom = tile;  // scale atom of this N tile (tiles are numbered like the atoms)
   const int nk = Kp / 128;
   const int mblk = cdiv(M, 128);
 
@@ -242,7 +277,7 @@ __global__ void __launch_bounds__(128) moe_gemm_kernel(const __grid_constant__ C
 #pragma unroll
       for (int kb = 0; kb < 4; ++kb) {
         tc::mma_mxf8f6f4(t_d, ad + 2 * kb, bd + 2 * kb, tc::idesc_with_sf_ids(idesc0, kb, kb),
-                         t_sfa | ((uint32_t)kb << 30), (t_sfb + sfb_shift) | ((uint32_t)kb << 30),
+                         t_sfa | ((uint32_t)kb << 30), t_sfb | ((uint32_t)kb << 30),
                          (kt | kb) != 0 ? 1u : 0u);
       }
       tc::mma_commit(&empty[s]);
@@ -357,7 +392,8 @@ static int make_act_map(CUtensorMap* m, const void* q, int R, int Kp, int nt) {
 template <int NT, int STAGES, bool A_FP4, int EPI>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const uint8_t* sfa, const uint8_t* sfb,
                        const MoeWorkspace& ws, const float* bias, const float* topk_w, void* out, int M, int Kp,
-                       int ld_out, float alpha, float limit, int max_tiles, int* status, cudaStream_t s) {
+                       int ld_out, float alpha, float limit, int max_tiles, int E_local, int R_max, int atoms_max,
+                       int* status, cudaStream_t s) {
   using L = GemmSmem<NT, STAGES>;
   auto kern = moe_gemm_kernel<NT, STAGES, A_FP4, EPI>;
   static bool attr = false;
@@ -367,14 +403,14 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const uint8
   }
   dim3 grid(cdiv(M, 128), max_tiles);
   kern<<<grid, 128, L::kAlloc, s>>>(ta, tb, sfa, sfb, ws, bias, topk_w, (__nv_bfloat16*)out, M, Kp, ld_out, alpha,
-                                    limit, status);
+                                    limit, E_local, R_max, atoms_max, status);
   return (int)cudaGetLastError();
 }
 
 template <int NT, int STAGES, bool A_FP4>
 static int run_gemms(const MoeShape& sh, const void* w13, const uint8_t* sf13, const float* b13, const void* w2,
                      const uint8_t* sf2w, const float* b2, const float* topk_w, const MoeWorkspace& ws, float alpha,
-                     float limit, int R_max, int max_tiles, int* status, cudaStream_t s) {
+                     float limit, int R_max, int max_tiles, int atoms_max, int* status, cudaStream_t s) {
   CUtensorMap ta1, tb1, ta2, tb2;
   int rc;
   if ((rc = make_weight_map(&ta1, w13, sh.E_local, 2 * sh.I, sh.K1p, A_FP4))) return rc;
@@ -382,12 +418,14 @@ static int run_gemms(const MoeShape& sh, const void* w13, const uint8_t* sf13, c
   if ((rc = make_weight_map(&ta2, w2, sh.E_local, sh.H, sh.K2p, A_FP4))) return rc;
   if ((rc = make_act_map(&tb2, ws.aq, R_max, sh.K2p, NT))) return rc;
   rc = launch_gemm<NT, STAGES, A_FP4, kEpiSwiglu>(ta1, tb1, sf13, ws.sf1, ws, b13, topk_w, ws.act, 2 * sh.I,
-                                                  sh.K1p, sh.I, alpha, limit, max_tiles, status, s);
+                                                  sh.K1p, sh.I, alpha, limit, max_tiles, sh.E_local, R_max, atoms_max,
+                                                  status, s);
   if (rc) return rc;
   moe_quant_kernel<<<cdiv(R_max, 4), 128, 0, s>>>(ws.aq, ws.sf2, (const __nv_bfloat16*)ws.act, sh.I, ws.row_route,
-                                                  0, ws.offsets, ws.atom_base, sh.E_local, sh.I, sh.K2p, R_max);
+                                                  0, ws.offsets, ws.atom_base, sh.E_local, sh.I, sh.K2p, R_max, R_max,
+                                                  atoms_max, NT, status);
   rc = launch_gemm<NT, STAGES, A_FP4, kEpiDown>(ta2, tb2, sf2w, ws.sf2, ws, b2, topk_w, ws.y, sh.H, sh.K2p, sh.H,
-                                                alpha, limit, max_tiles, status, s);
+                                                alpha, limit, max_tiles, sh.E_local, R_max, atoms_max, status, s);
   return rc;
 }
 
@@ -398,7 +436,7 @@ using namespace b200;
 static void ws_sizes(const MoeShape& sh, int64_t* z) {
   const int64_t R = (int64_t)sh.T * sh.k;
   const int64_t max_tiles = cdiv((int)R, sh.nt) + sh.E_local;
-  const int64_t atoms = cdiv((int)R, 128) + sh.E_local;
+  const int64_t atoms = max_tiles;  // one scale atom per N tile
   z[0] = (sh.E_local + 1) * 4;
   z[1] = (sh.E_local + 1) * 4;
   z[2] = sh.E_local * 4;
@@ -428,19 +466,21 @@ extern "C" int b200_moe_mx_forward(void* out, const void* x, const int* topk_ids
   const int max_tiles = cdiv(R_max, sh.nt) + sh.E_local;
   moe_route_kernel<<<1, 1024, 2 * sh.E_local * sizeof(int), s>>>(topk_ids, R_max, sh.E_local, sh.expert_offset,
                                                                  sh.nt, max_tiles, ws);
+  const int atoms_max = max_tiles;
   moe_quant_kernel<<<cdiv(R_max, 4), 128, 0, s>>>(ws.xq, ws.sf1, (const __nv_bfloat16*)x, sh.H, ws.row_route,
-                                                  sh.k, ws.offsets, ws.atom_base, sh.E_local, sh.H, sh.K1p, R_max);
+                                                  sh.k, ws.offsets, ws.atom_base, sh.E_local, sh.H, sh.K1p, R_max,
+                                                  sh.T, atoms_max, sh.nt, status);
   int rc;
   if (sh.nt == 32) {
     rc = sh.a_fp4 ? run_gemms<32, 4, true>(sh, w13, sf13, b13, w2, sf2w, b2, topk_w, ws, alpha, limit, R_max,
-                                           max_tiles, status, s)
+                                           max_tiles, atoms_max, status, s)
                   : run_gemms<32, 4, false>(sh, w13, sf13, b13, w2, sf2w, b2, topk_w, ws, alpha, limit, R_max,
-                                            max_tiles, status, s);
+                                            max_tiles, atoms_max, status, s);
   } else {
     rc = sh.a_fp4 ? run_gemms<128, 4, true>(sh, w13, sf13, b13, w2, sf2w, b2, topk_w, ws, alpha, limit, R_max,
-                                            max_tiles, status, s)
+                                            max_tiles, atoms_max, status, s)
                   : run_gemms<128, 4, false>(sh, w13, sf13, b13, w2, sf2w, b2, topk_w, ws, alpha, limit, R_max,
-                                             max_tiles, status, s);
+                                             max_tiles, atoms_max, status, s);
   }
   if (rc) return rc;
   moe_reduce_kernel<<<sh.T, 256, 0, s>>>((__nv_bfloat16*)out, (const __nv_bfloat16*)ws.y, topk_ids, sh.k,

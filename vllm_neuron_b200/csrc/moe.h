@@ -9,7 +9,7 @@ namespace b200 {
 // All buffers are caller-owned device memory; sizes from moe_workspace_sizes().
 struct MoeWorkspace {
   int* offsets;      // [E_local + 1]   first permuted row of each local expert
-  int* atom_base;    // [E_local + 1]   first 128-row scale atom of each expert
+  int* atom_base;    // [E_local + 1]   first N tile (= scale atom) of each expert
   int* cursor;       // [E_local]       scatter cursors
   int* row_route;    // [R_max]         route id (t*k + j) of each permuted row
   int* tiles;        // [2 * max_tiles] (expert, first row) of each N tile

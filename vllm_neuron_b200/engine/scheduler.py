@@ -117,9 +117,9 @@ class Scheduler:
         return r.num_computed_tokens < r.num_prompt_tokens
 
     def can_admit(self) -> bool:
+        """Room for one more sequence (batch size and worst-case KV capacity).  Whether a
+        segmented prefill from an earlier step is still in flight is checked by the caller."""
         if len(self.running) >= self.max_num_seqs:
-            return False
-        if any(self._is_prefill(r) for r in self.running):
             return False
         return len(self.running) < self.max_kv_concurrent
 

@@ -30,7 +30,7 @@ def device_status(device: torch.device) -> torch.Tensor:
     key = str(device)
     t = _STATUS.get(key)
     if t is None:
-        t = torch.zeros(1, dtype=torch.int32, device=device)
+        t = torch.zeros(4, dtype=torch.int32, device=device)  # code, where, value, spare
         _STATUS[key] = t
     return t
 
@@ -40,11 +40,11 @@ def check_device_status(device: torch.device) -> int:
     t = _STATUS.get(str(device))
     if t is None:
         return 0
-    code = int(t.item())
+    code, where, value, _ = t.tolist()
     if code:
         t.zero_()
         names = {1: "index out of range", 2: "device wait timed out", 3: "bad shape", 4: "bad alignment"}
-        raise RuntimeError(f"kernel status {code}: {names.get(code, 'unknown')}")
+        raise RuntimeError(f"kernel status {code} ({names.get(code, 'unknown')}) at check {where}, value {value}")
     return 0
 
 # ---------------------------------------------------------------------------

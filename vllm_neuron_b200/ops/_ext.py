@@ -64,6 +64,38 @@ def use_kernel(t: torch.Tensor) -> bool:
     return True
 
 
+class _DebugOps:
+    """``VLLM_B200_DEBUG_SYNC=1``: every kernel call synchronises and checks both the
+    CUDA error state and the kernel status word, naming the op that failed."""
+
+    def __getattr__(self, name):
+        fn = getattr(torch.ops.b200, name)
+
+        def call(*args, **kwargs):
+            out = fn(*args, **kwargs)
+            try:
+                torch.cuda.synchronize()
+            except Exception as e:  # noqa: BLE001
+                raise RuntimeError(f"b200::{name} failed: {e}") from e
+            from . import check_device_status
+
+            for a in args:
+                if isinstance(a, torch.Tensor) and a.is_cuda:
+                    try:
+                        check_device_status(a.device)
+                    except RuntimeError as e:
+                        raise RuntimeError(f"b200::{name}: {e}") from e
+                    break
+            return out
+
+        return call
+
+
+_DEBUG = _DebugOps()
+
+
 def ops():
     load()
+    if os.environ.get("VLLM_B200_DEBUG_SYNC", "0") == "1":
+        return _DEBUG
     return torch.ops.b200
