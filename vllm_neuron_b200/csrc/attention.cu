@@ -22,6 +22,7 @@
 //            table, so chunked prefill and prefix-cache hits need no gather.
 #include "launch.h"
 #include "mma_utils.cuh"
+#include "noalloc.h"
 
 namespace b200 {
 
@@ -669,4 +670,79 @@ extern "C" int b200_varlen_attention(void* out, const void* q, const void* k, co
   if (d == 128) { VAR(128, 128) }
 #undef VAR
   return kBadShape;
+}
+
+// =======================================================================================
+// No-allocation entry point for split-KV paged decode attention.
+//
+// This entry point has no counterpart in the reference plugin; it exists for callers of
+// this library that cannot allocate device memory themselves, for example a host runtime
+// written in C that links this library directly but has no allocator handle, or a serving
+// process whose device memory is entirely reserved up front by another component's
+// caching allocator, so that a cudaMalloc here would either fail or force a device-wide
+// synchronisation at a moment the caller cannot afford.  Such callers pass only inputs and
+// outputs; the split-KV partial results live in a fixed array in this library instead of a
+// caller-provided workspace.
+//
+// Limits and contract:
+//   * scratch is a file-scope __device__ array of kNoAllocScratchFloats floats (4 MiB).  Every
+//     GPU that loads this library reserves it until the process exits.  A call needs
+//     B * nq * num_splits * (d + 1) floats when num_splits > 1 (none when num_splits == 1);
+//     larger requests are rejected with kScratchTooSmall and launch nothing.
+//   * the device address of the array is looked up once per device with
+//     cudaGetSymbolAddress, on the first call made while that device is current; issue that
+//     first call before any stream capture on the device.
+//   * all calls share the one array and it keeps whatever the previous call wrote.  Nothing
+//     in it has to start at zero: every partial result the combine step reads is written by
+//     the same call first.  Calls whose kernels overlap on the GPU (different streams, no
+//     ordering between them) race on the array and give wrong results; order them.
+//   * no cudaMalloc, cudaFree or allocating library routine is called.
+// =======================================================================================
+namespace {
+
+constexpr size_t kNoAllocScratchFloats = size_t(1) << 20;
+constexpr int kScratchTooSmall = 5;
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) float g_decode_scratch[kNoAllocScratchFloats];
+
+float* g_scratch_addr[kMaxDevices] = {nullptr};
+
+// Device address of g_decode_scratch for the current device (looked up once per device).
+int scratch_for_current_device(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= kMaxDevices) return kBadShape;
+  float* p = __atomic_load_n(&g_scratch_addr[dev], __ATOMIC_ACQUIRE);
+  if (p == nullptr) {
+    void* addr = nullptr;
+    e = cudaGetSymbolAddress(&addr, g_decode_scratch);
+    if (e != cudaSuccess) return (int)e;
+    p = static_cast<float*>(addr);
+    __atomic_store_n(&g_scratch_addr[dev], p, __ATOMIC_RELEASE);
+  }
+  *out = p;
+  return 0;
+}
+
+}  // namespace
+
+extern "C" int b200_paged_attention_decode_noalloc(void* out, const void* q, const void* k_cache,
+                                                   const void* v_cache, const int* block_tables, const int* seq_lens,
+                                                   const float* sinks, int B, int nq, int nkv, int d, int q_stride,
+                                                   int block_size, int max_blocks, int window, float scale,
+                                                   float k_scale, float v_scale, int num_splits, int dtype,
+                                                   int cache_dtype, cudaStream_t s) {
+  if (num_splits < 1 || B < 0 || nq <= 0 || d <= 0) return kBadShape;
+  const size_t need = num_splits > 1 ? (size_t)B * nq * num_splits * (d + 1) : 0;
+  if (need > kNoAllocScratchFloats) return kScratchTooSmall;
+  float* ws = nullptr;
+  if (num_splits > 1) {
+    const int rc = scratch_for_current_device(&ws);
+    if (rc) return rc;
+  }
+  return b200_paged_attention_decode(out, q, k_cache, v_cache, block_tables, seq_lens, sinks, B, nq, nkv, d,
+                                     q_stride, block_size, max_blocks, window, scale, k_scale, v_scale, ws,
+                                     num_splits, dtype, cache_dtype, s);
 }
