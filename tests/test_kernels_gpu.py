@@ -228,7 +228,7 @@ def _moe_reference(x, ids, wts, w13f, b13, w2f, b2, off, alpha, limit, emulate_f
                                                         (1200, 8, 2880, 2880, 4, 0, 8, 1)])
 def test_moe_mxfp4(T, E, H, I, k, off, E_total, skew):
     """skew=1 concentrates the routing so single experts get several N tiles."""
-    from vllm_neuron_b200.ops.mx_layout import pad_k, scales_to_atoms
+    from vllm_neuron_b200.ops.mx_layout import scales_to_atoms, tile_values
 
     g = torch.Generator(device=DEV).manual_seed(7)
     x = torch.randn(T, H, device=DEV, generator=g).bfloat16()
@@ -245,7 +245,7 @@ def test_moe_mxfp4(T, E, H, I, k, off, E_total, skew):
     v, ids = torch.topk(logits, k, -1)
     wts = torch.softmax(v, -1)
     ids = ids.to(torch.int32)
-    got = ops.moe_mxfp4(x, ids, wts, pad_k(w13, H), scales_to_atoms(s13, H), b13, pad_k(w2, I),
+    got = ops.moe_mxfp4(x, ids, wts, tile_values(w13, H), scales_to_atoms(s13, H), b13, tile_values(w2, I),
                         scales_to_atoms(s2, I), b2, off, 1.702, 7.0, H, I)
     w13f = ref.dequant_mxfp4(w13, s13)
     w2f = ref.dequant_mxfp4(w2, s2)

@@ -3,7 +3,7 @@
 import torch
 
 from vllm_neuron_b200.ops import reference as ref
-from vllm_neuron_b200.ops.mx_layout import atoms_to_scales, pad_k, scales_to_atoms
+from vllm_neuron_b200.ops.mx_layout import atoms_to_scales, pad_k, scales_to_atoms, tile_values, untile_values
 
 
 def test_mxfp4_roundtrip_exact_on_grid():
@@ -134,3 +134,11 @@ def test_yarn_matches_hf():
     inv_hf, af_hf = ROPE_INIT_FUNCTIONS["yarn"](cfg, "cpu")
     inv, af = ref.yarn_inv_freq(64, 150000.0, 32.0, 4096, 32.0, 1.0, False)
     assert torch.allclose(inv, inv_hf.float(), rtol=1e-5) and abs(af - af_hf) < 1e-6
+
+
+def test_value_tiles_roundtrip():
+    v = torch.randint(0, 255, (2, 300, 1440), dtype=torch.uint8)
+    t = tile_values(v, 2880)
+    assert t.shape == (2, 3, 23, 128, 64)
+    assert torch.equal(untile_values(t, 300, 2880), v)
+    assert torch.equal(t[1, 2, 5, 10], v[1, 266, 320:384])  # row 2*128+10, K bytes 5*64..

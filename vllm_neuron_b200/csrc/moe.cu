@@ -47,11 +47,15 @@ B200_HD size_t sf_byte(int atom, int kgroups, int row_in_atom, int kb) {
 }
 
 // ------------------------------------------------------------------------- routing
+// One CTA: histogram of local routes per expert (shared-memory atomics), a block-wide
+// exclusive scan of the counts and of the tile counts (one thread per expert), the tile
+// list written in parallel, then the scatter of route ids into expert order.
 __global__ void __launch_bounds__(1024) moe_route_kernel(const int* __restrict__ topk_ids, int TK, int E, int off,
                                                          int nt, int max_tiles, MoeWorkspace ws) {
   extern __shared__ int sm[];
   int* cnt = sm;           // [E]
-  int* cur = sm + E;       // [E]
+  int* cur = sm + E;       // [E]   scatter cursors
+  __shared__ int warp_tot[2][32];
   for (int i = threadIdx.x; i < E; i += blockDim.x) cnt[i] = 0;
   __syncthreads();
   for (int r = threadIdx.x; r < TK; r += blockDim.x) {
@@ -59,30 +63,63 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int* __restrict__
     if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int run = 0, abase = 0, ntile = 0;
-    for (int e = 0; e < E; ++e) {
-      ws.offsets[e] = run;
-      ws.atom_base[e] = abase;
-      cur[e] = run;
-      for (int n0 = 0; n0 < cnt[e]; n0 += nt) {
-        if (ntile < max_tiles) {
-          ws.tiles[2 * ntile] = e;
-          ws.tiles[2 * ntile + 1] = n0;
-          ++ntile;
-        }
-      }
-      run += cnt[e];
-      abase += cdiv(cnt[e], nt);  // one 512-byte scale atom per N tile
+  // exclusive scan over experts of (rows, tiles); E <= blockDim.x
+  const int e = threadIdx.x;
+  const int lane = e & 31, wid = e >> 5;
+  int v_rows = e < E ? cnt[e] : 0;
+  int v_tiles = e < E ? cdiv(cnt[e], nt) : 0;
+  int a = v_rows, b = v_tiles;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int ya = __shfl_up_sync(0xffffffffu, a, o), yb = __shfl_up_sync(0xffffffffu, b, o);
+    if (lane >= o) {
+      a += ya;
+      b += yb;
     }
-    ws.offsets[E] = run;
-    ws.atom_base[E] = abase;
-    *ws.num_tiles = ntile;
+  }
+  if (lane == 31) {
+    warp_tot[0][wid] = a;
+    warp_tot[1][wid] = b;
+  }
+  __syncthreads();
+  if (wid == 0) {
+    int ta = lane < (int)(blockDim.x >> 5) ? warp_tot[0][lane] : 0;
+    int tb = lane < (int)(blockDim.x >> 5) ? warp_tot[1][lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int ya = __shfl_up_sync(0xffffffffu, ta, o), yb = __shfl_up_sync(0xffffffffu, tb, o);
+      if (lane >= o) {
+        ta += ya;
+        tb += yb;
+      }
+    }
+    warp_tot[0][lane] = ta;  // inclusive prefix of warp totals
+    warp_tot[1][lane] = tb;
+  }
+  __syncthreads();
+  const int base_rows = (wid > 0 ? warp_tot[0][wid - 1] : 0) + a - v_rows;
+  const int base_tiles = (wid > 0 ? warp_tot[1][wid - 1] : 0) + b - v_tiles;
+  if (e < E) {
+    ws.offsets[e] = base_rows;
+    ws.atom_base[e] = base_tiles;  // one 512-byte scale atom per N tile
+    cur[e] = base_rows;
+    for (int t = 0; t < v_tiles; ++t) {
+      const int ti = base_tiles + t;
+      if (ti < max_tiles) {
+        ws.tiles[2 * ti] = e;
+        ws.tiles[2 * ti + 1] = t * nt;
+      }
+    }
+    if (e == E - 1) {
+      ws.offsets[E] = base_rows + v_rows;
+      ws.atom_base[E] = base_tiles + v_tiles;
+      *ws.num_tiles = min(base_tiles + v_tiles, max_tiles);
+    }
   }
   __syncthreads();
   for (int r = threadIdx.x; r < TK; r += blockDim.x) {
-    const int e = topk_ids[r] - off;
-    if (e >= 0 && e < E) ws.row_route[atomicAdd(&cur[e], 1)] = r;
+    const int ee = topk_ids[r] - off;
+    if (ee >= 0 && ee < E) ws.row_route[atomicAdd(&cur[ee], 1)] = r;
   }
 }
 
@@ -95,7 +132,9 @@ __global__ void __launch_bounds__(128) moe_quant_kernel(uint8_t* __restrict__ q,
                                                         const int* __restrict__ atom_base, int E, int K, int Kp,
                                                         int R_max, int src_rows, int atoms_max, int nt,
                                                         int* status) {
-  const int r = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int groups = (Kp / 32 + 31) / 32;  // 32-block groups per row
+  const int gw = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int r = gw / groups, grp = gw % groups;
   const int lane = threadIdx.x & 31;
   if (r >= R_max || r >= offsets[E]) return;
   if (offsets[E] > R_max) {
@@ -126,7 +165,9 @@ __global__ void __launch_bounds__(128) moe_quant_kernel(uint8_t* __restrict__ q,
     if (lane == 0) record(status, kBadAlignment, 12, (int)(reinterpret_cast<uintptr_t>(s) & 0xffff));
     return;
   }
-  for (int kb = lane; kb < Kp / 32; kb += 32) {
+  {
+    const int kb = grp * 32 + lane;
+    if (kb >= Kp / 32) return;
     uint4 o[2];
     uint8_t scale = 127;
     if (kb * 32 < K) {
@@ -170,6 +211,13 @@ __global__ void __launch_bounds__(128) moe_quant_kernel(uint8_t* __restrict__ q,
 }
 
 // ------------------------------------------------------------------------- GEMM
+// Persistent grouped GEMM: one CTA per SM loops over work items (N tile of one expert x
+// 128-row M tile, M fastest so consecutive items share the activation tile in L2).
+//   warp 0 lane 0 : TMA producer through a STAGES-deep shared-memory ring (runs ahead
+//                   across work items);
+//   warp 1        : allocates TMEM; lane 0 issues tcgen05.cp (scale factors) and
+//                   tcgen05.mma into one of two TMEM accumulators;
+//   warps 4..7    : epilogue for TMEM lanes 32*(w%4).., overlapping the next item's MMAs.
 enum Epi : int { kEpiSwiglu = 0, kEpiDown = 1 };
 
 template <int NT, int STAGES>
@@ -180,65 +228,76 @@ struct GemmSmem {
   static constexpr int kOffSfa = kOffB + STAGES * kB;
   static constexpr int kOffSfb = kOffSfa + STAGES * kSfAtom;
   static constexpr int kOffBar = kOffSfb + STAGES * kSfAtom;
-  static constexpr int kBytes = kOffBar + (2 * STAGES + 1) * 8 + 16;
+  static constexpr int kBytes = kOffBar + (2 * STAGES + 4) * 8 + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack to align the base to 1024
+  static constexpr int kTmemNeed = 2 * NT + 8;  // two accumulators + SFA + SFB columns
+  static constexpr uint32_t kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64 : kTmemNeed <= 128 ? 128
+                                        : kTmemNeed <= 256 ? 256 : 512;
 };
 
+struct WorkItem {
+  int e, n0, row0, mt, tile;
+  bool valid;
+};
+
+B200_D WorkItem decode_item(const MoeWorkspace& ws, int w, int mtiles, int E_local, int R_max, int atoms_max) {
+  WorkItem it;
+  it.tile = w / mtiles;
+  it.mt = w % mtiles;
+  it.e = ws.tiles[2 * it.tile];
+  it.n0 = ws.tiles[2 * it.tile + 1];
+  it.valid = it.e >= 0 && it.e < E_local && it.n0 >= 0 && it.tile < atoms_max;
+  it.row0 = it.valid ? ws.offsets[it.e] + it.n0 : 0;
+  it.valid = it.valid && it.row0 < R_max;
+  return it;
+}
+
 template <int NT, int STAGES, bool A_FP4, int EPI>
-__global__ void __launch_bounds__(128) moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
-                                                       const __grid_constant__ CUtensorMap tmB,
-                                                       const uint8_t* __restrict__ sfa,
-                                                       const uint8_t* __restrict__ sfb, MoeWorkspace ws,
-                                                       const float* __restrict__ bias,
-                                                       const float* __restrict__ topk_w, __nv_bfloat16* __restrict__ out,
-                                                       int M, int Kp, int ld_out, float alpha, float limit,
-                                                       int E_local, int R_max, int atoms_max, int* status) {
+__global__ void __launch_bounds__(256, (NT <= 32 ? 2 : 1)) moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                          const __grid_constant__ CUtensorMap tmB,
+                                                          const uint8_t* __restrict__ sfa,
+                                                          const uint8_t* __restrict__ sfb, MoeWorkspace ws,
+                                                          const float* __restrict__ bias,
+                                                          const float* __restrict__ topk_w,
+                                                          __nv_bfloat16* __restrict__ out, int M, int Kp, int ld_out,
+                                                          float alpha, float limit, int E_local, int R_max,
+                                                          int atoms_max, int* status) {
   using L = GemmSmem<NT, STAGES>;
   extern __shared__ uint8_t smem_raw[];
-  const int tile = blockIdx.y;
-  if (tile >= *ws.num_tiles) return;
+  const int mtiles = cdiv(M, 128);
+  const int W = min(*ws.num_tiles, atoms_max) * mtiles;
+  if ((int)blockIdx.x >= W) return;
   // align the shared-space offset (not the generic address) to 1024 for the 128-byte swizzle
   const uint32_t raw_off = tc::smem_addr(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_off & 1023u)) & 1023u);
-  {
-    const int e_ = ws.tiles[2 * tile], n0_ = ws.tiles[2 * tile + 1];
-    bool bad = e_ < 0 || e_ >= E_local || n0_ < 0;
-    if (!bad) bad = ws.offsets[e_] + n0_ >= R_max || tile >= atoms_max;
-    if (bad || (tc::smem_addr(smem) & 1023u) != 0) {
-      if (threadIdx.x == 0) record(status, bad ? kBadIndex : kBadAlignment, 20, bad ? e_ : (int)tc::smem_addr(smem));
-      return;
-    }
-  }
   uint8_t* sA = smem;
   uint8_t* sB = smem + L::kOffB;
   uint8_t* sSfa = smem + L::kOffSfa;
   uint8_t* sSfb = smem + L::kOffSfb;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
   uint64_t* empty = full + STAGES;
-  uint64_t* done = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int mt = blockIdx.x, m0 = mt * 128;
-  const int e = ws.tiles[2 * tile], n0 = ws.tiles[2 * tile + 1];
-  const int row0 = ws.offsets[e] + n0;
-  const int nvalid = min(NT, ws.offsets[e + 1] - ws.offsets[e] - n0);
-  const int atom = tile;  // scale atom of this N tile (tiles are numbered like the atoms)
   const int nk = Kp / 128;
-  const int mblk = cdiv(M, 128);
-
+  const int mblk = mtiles;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       tc::mbar_init(&full[s], 1);
       tc::mbar_init(&empty[s], 1);
     }
-    tc::mbar_init(done, 1);
+    for (int a = 0; a < 2; ++a) {
+      tc::mbar_init(&acc_full[a], 1);
+      tc::mbar_init(&acc_empty[a], 4);  // one arrive per epilogue warp
+    }
     tc::fence_barrier_init();
     tc::prefetch_tmap(&tmA);
     tc::prefetch_tmap(&tmB);
   }
   if (warp == 1) {
-    tc::tmem_alloc(tmem_slot, 256);
+    tc::tmem_alloc(tmem_slot, L::kTmemCols);
     tc::tmem_relinquish();
   }
   tc::fence_before_sync();
@@ -246,104 +305,149 @@ __global__ void __launch_bounds__(128) moe_gemm_kernel(const __grid_constant__ C
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer ----------------
-    for (int kt = 0; kt < nk; ++kt) {
-      const int s = kt % STAGES, use = kt / STAGES;
-      if (kt >= STAGES && !tc::mbar_wait(&empty[s], (use - 1) & 1, status)) break;
-      // transaction bytes count the global (packed) size: fp4 tiles are 4 bits/element
-      tc::mbar_arrive_expect_tx(&full[s], (A_FP4 ? L::kA / 2 : L::kA) + L::kB + 2 * kSfAtom);
-      tc::tma_load_3d(sA + s * L::kA, &tmA, kt * 128, m0, e, &full[s]);
-      tc::tma_load_2d(sB + s * L::kB, &tmB, kt * 128, row0, &full[s]);
-      tc::bulk_load(sSfa + s * kSfAtom, sfa + (((size_t)e * mblk + mt) * nk + kt) * kSfAtom, kSfAtom, &full[s]);
-      tc::bulk_load(sSfb + s * kSfAtom, sfb + ((size_t)atom * nk + kt) * kSfAtom, kSfAtom, &full[s]);
-    }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer ----------------
-    const uint32_t idesc0 = tc::idesc_mxf8f6f4(A_FP4 ? 5 : 0, 0, 128, NT);
-    const uint32_t t_d = tmem, t_sfa = tmem + NT, t_sfb = tmem + NT + 4;
-    bool ok = true;
-    for (int kt = 0; kt < nk; ++kt) {
-      const int s = kt % STAGES, use = kt / STAGES;
-      if (!tc::mbar_wait(&full[s], use & 1, status)) {
-        ok = false;
-        break;
-      }
-      tc::fence_after_sync();
-      tc::utccp_32x128b_warpx4(t_sfa, tc::desc_noswizzle_16b_rows(sSfa + s * kSfAtom));
-      tc::utccp_32x128b_warpx4(t_sfb, tc::desc_noswizzle_16b_rows(sSfb + s * kSfAtom));
-      const uint64_t ad = tc::desc_sw128(sA + s * L::kA);
-      const uint64_t bd = tc::desc_sw128(sB + s * L::kB);
-#pragma unroll
-      for (int kb = 0; kb < 4; ++kb) {
-        tc::mma_mxf8f6f4(t_d, ad + 2 * kb, bd + 2 * kb, tc::idesc_with_sf_ids(idesc0, kb, kb),
-                         t_sfa | ((uint32_t)kb << 30), t_sfb | ((uint32_t)kb << 30),
-                         (kt | kb) != 0 ? 1u : 0u);
-      }
-      tc::mma_commit(&empty[s]);
-    }
-    (void)ok;
-    tc::mma_commit(done);
-  }
-  __syncwarp();
-  // ---------------- epilogue (all 4 warps: TMEM lanes 32w..32w+31) ----------------
-  const bool ok = tc::mbar_wait(done, 0, status);
-  tc::fence_after_sync();
-  if (ok) {
-    const int m = warp * 32 + lane;
-    const int gm = m0 + m;
-    const float b = gm < M ? bias[(size_t)e * M + gm] : 0.f;
-    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-    for (int c = 0; c < NT; c += 32) {
-      if (c >= nvalid) break;
-      uint32_t r[32];
-      tc::tmem_ld_32x32b_x32(lane_addr + c, r);
-      tc::tmem_ld_wait();
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int j = c + i;
-        const float v = __uint_as_float(r[i]) + b;
-        if constexpr (EPI == kEpiSwiglu) {
-          const float other = __shfl_xor_sync(0xffffffffu, v, 1);
-          if (!(m & 1) && j < nvalid && gm < M) {
-            float g = v, u = other, a;
-            if (limit > 0.f) {
-              g = fminf(g, limit);
-              u = fminf(fmaxf(u, -limit), limit);
-              a = g / (1.f + __expf(-alpha * g)) * (u + 1.f);
-            } else {
-              a = g / (1.f + __expf(-g)) * u;
-            }
-            out[(size_t)(row0 + j) * ld_out + (gm >> 1)] = __float2bfloat16(a);
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int it = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < W && ok; w += gridDim.x) {
+        const WorkItem wi = decode_item(ws, w, mtiles, E_local, R_max, atoms_max);
+        if (!wi.valid) {
+          record(status, kBadIndex, 20, wi.e);
+          continue;
+        }
+        for (int kt = 0; kt < nk; ++kt, ++it) {
+          const int s = it % STAGES, use = it / STAGES;
+          if (it >= STAGES && !tc::mbar_wait(&empty[s], (use - 1) & 1, status)) {
+            ok = false;
+            break;
           }
-        } else {
-          if (j < nvalid && gm < M) {
-            const int route = ws.row_route[row0 + j];
-            out[(size_t)route * ld_out + gm] = __float2bfloat16(v * topk_w[route]);
+          // transaction bytes count the global (packed) size: fp4 tiles are 4 bits/element
+          tc::mbar_arrive_expect_tx(&full[s], (A_FP4 ? L::kA / 2 : L::kA) + L::kB + 2 * kSfAtom);
+          // weights are stored as contiguous 128x128 tiles: tile index (e, m tile, k tile)
+          tc::tma_load_3d(sA + s * L::kA, &tmA, 0, 0, ((wi.e * mblk) + wi.mt) * nk + kt, &full[s]);
+          tc::tma_load_2d(sB + s * L::kB, &tmB, kt * 128, wi.row0, &full[s]);
+          tc::bulk_load(sSfa + s * kSfAtom, sfa + (((size_t)wi.e * mblk + wi.mt) * nk + kt) * kSfAtom, kSfAtom,
+                        &full[s]);
+          tc::bulk_load(sSfb + s * kSfAtom, sfb + ((size_t)wi.tile * nk + kt) * kSfAtom, kSfAtom, &full[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      const uint32_t idesc0 = tc::idesc_mxf8f6f4(A_FP4 ? 5 : 0, 0, 128, NT);
+      const uint32_t t_sfa = tmem + 2 * NT, t_sfb = tmem + 2 * NT + 4;
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < W && ok; w += gridDim.x) {
+        const WorkItem wi = decode_item(ws, w, mtiles, E_local, R_max, atoms_max);
+        if (!wi.valid) continue;
+        const int acc = local & 1, ause = local >> 1;
+        if (local >= 2 && !tc::mbar_wait(&acc_empty[acc], (ause - 1) & 1, status)) break;
+        tc::fence_after_sync();
+        const uint32_t t_d = tmem + acc * NT;
+        for (int kt = 0; kt < nk; ++kt, ++it) {
+          const int s = it % STAGES, use = it / STAGES;
+          if (!tc::mbar_wait(&full[s], use & 1, status)) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          tc::utccp_32x128b_warpx4(t_sfa, tc::desc_noswizzle_16b_rows(sSfa + s * kSfAtom));
+          tc::utccp_32x128b_warpx4(t_sfb, tc::desc_noswizzle_16b_rows(sSfb + s * kSfAtom));
+          const uint64_t ad = tc::desc_sw128(sA + s * L::kA);
+          const uint64_t bd = tc::desc_sw128(sB + s * L::kB);
+#pragma unroll
+          for (int kb = 0; kb < 4; ++kb) {
+            tc::mma_mxf8f6f4(t_d, ad + 2 * kb, bd + 2 * kb, tc::idesc_with_sf_ids(idesc0, kb, kb),
+                             t_sfa | ((uint32_t)kb << 30), t_sfb | ((uint32_t)kb << 30), (kt | kb) != 0 ? 1u : 0u);
+          }
+          tc::mma_commit(&empty[s]);
+        }
+        tc::mma_commit(&acc_full[acc]);
+        ++local;
+      }
+    }
+  } else if (warp >= 4) {
+    // ---------------- epilogue ----------------
+    const int ew = warp & 3;
+    const int m = ew * 32 + lane;
+    int local = 0;
+    for (int w = blockIdx.x; w < W; w += gridDim.x) {
+      const WorkItem wi = decode_item(ws, w, mtiles, E_local, R_max, atoms_max);
+      if (!wi.valid) continue;
+      const int acc = local & 1, ause = local >> 1;
+      if (!tc::mbar_wait(&acc_full[acc], ause & 1, status)) break;
+      tc::fence_after_sync();
+      const int nvalid = min(NT, ws.offsets[wi.e + 1] - ws.offsets[wi.e] - wi.n0);
+      const int gm = wi.mt * 128 + m;
+      const float b = gm < M ? bias[(size_t)wi.e * M + gm] : 0.f;
+      const uint32_t lane_addr = tmem + acc * NT + ((uint32_t)(ew * 32) << 16);
+      for (int c = 0; c < NT; c += 16) {
+        if (c >= nvalid) break;
+        uint32_t r[16];
+        tc::tmem_ld_32x32b_x16(lane_addr + c, r);
+        tc::tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int j = c + i;
+          const float v = __uint_as_float(r[i]) + b;
+          if constexpr (EPI == kEpiSwiglu) {
+            const float other = __shfl_xor_sync(0xffffffffu, v, 1);
+            if (!(m & 1) && j < nvalid && gm < M) {
+              float g = v, u = other, a;
+              if (limit > 0.f) {
+                g = fminf(g, limit);
+                u = fminf(fmaxf(u, -limit), limit);
+                a = g / (1.f + __expf(-alpha * g)) * (u + 1.f);
+              } else {
+                a = g / (1.f + __expf(-g)) * u;
+              }
+              out[(size_t)(wi.row0 + j) * ld_out + (gm >> 1)] = __float2bfloat16(a);
+            }
+          } else {
+            if (j < nvalid && gm < M) {
+              const int route = ws.row_route[wi.row0 + j];
+              out[(size_t)route * ld_out + gm] = __float2bfloat16(v * topk_w[route]);
+            }
           }
         }
       }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&acc_empty[acc]);
+      ++local;
     }
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 1) tc::tmem_dealloc(tmem, 256);
+  if (warp == 1) tc::tmem_dealloc(tmem, L::kTmemCols);
 }
 
 // ------------------------------------------------------------------------- reduce
 __global__ void moe_reduce_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ y,
                                   const int* __restrict__ topk_ids, int k, int E, int off, int H) {
   const int t = blockIdx.x;
-  for (int h2 = threadIdx.x; h2 < H / 2; h2 += blockDim.x) {
-    float a0 = 0.f, a1 = 0.f;
-    for (int j = 0; j < k; ++j) {
-      const int e = topk_ids[t * k + j] - off;
-      if (e < 0 || e >= E) continue;
-      const __nv_bfloat162 v = reinterpret_cast<const __nv_bfloat162*>(y + (size_t)(t * k + j) * H)[h2];
-      a0 += __low2float(v);
-      a1 += __high2float(v);
+  int local[16];
+  int nl = 0;
+  for (int j = 0; j < k && j < 16; ++j) {
+    const int e = topk_ids[t * k + j] - off;
+    if (e >= 0 && e < E) local[nl++] = j;
+  }
+  for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int i = 0; i < nl; ++i) {
+      const uint4 u = reinterpret_cast<const uint4*>(y + (size_t)(t * k + local[i]) * H)[c];
+      const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(hb[q]);
     }
-    reinterpret_cast<__nv_bfloat162*>(out + (size_t)t * H)[h2] = __floats2bfloat162_rn(a0, a1);
+    uint4 o;
+    __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&o);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) ob[q] = __float2bfloat16(acc[q]);
+    reinterpret_cast<uint4*>(out + (size_t)t * H)[c] = o;
   }
 }
 
@@ -360,13 +464,14 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
-// 3-D weight map [E, rows, Kp] (fp4 packed two per byte, or e4m3), box 128 x 128 x 1.
-static int make_weight_map(CUtensorMap* m, const void* w, int E, int rows, int Kp, bool fp4) {
+// Weight map over contiguous 128-row x 128-element tiles [n_tiles, 128, 128*bits/8]:
+// one box = one tile = one contiguous 8 KB (fp4) / 16 KB (fp8) run.
+static int make_weight_map(CUtensorMap* m, const void* w, int n_tiles, bool fp4) {
   auto enc = get_encode();
   if (!enc) return kBadShape;
-  const uint64_t row_bytes = fp4 ? (uint64_t)Kp / 2 : (uint64_t)Kp;
-  cuuint64_t dims[3] = {(cuuint64_t)Kp, (cuuint64_t)rows, (cuuint64_t)E};
-  cuuint64_t strides[2] = {row_bytes, row_bytes * rows};
+  const uint64_t row_bytes = fp4 ? 64 : 128;
+  cuuint64_t dims[3] = {128, 128, (cuuint64_t)n_tiles};
+  cuuint64_t strides[2] = {row_bytes, row_bytes * 128};
   cuuint32_t box[3] = {128, 128, 1};
   cuuint32_t es[3] = {1, 1, 1};
   CUresult r = enc(m, fp4 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, 3,
@@ -389,6 +494,17 @@ static int make_act_map(CUtensorMap* m, const void* q, int R, int Kp, int nt) {
   return r == CUDA_SUCCESS ? 0 : 1000 + (int)r;
 }
 
+static int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
 template <int NT, int STAGES, bool A_FP4, int EPI>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const uint8_t* sfa, const uint8_t* sfb,
                        const MoeWorkspace& ws, const float* bias, const float* topk_w, void* out, int M, int Kp,
@@ -401,8 +517,11 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const uint8
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
     attr = true;
   }
-  dim3 grid(cdiv(M, 128), max_tiles);
-  kern<<<grid, 128, L::kAlloc, s>>>(ta, tb, sfa, sfb, ws, bias, topk_w, (__nv_bfloat16*)out, M, Kp, ld_out, alpha,
+  // persistent: one (large tiles) or two (small tiles) CTAs per SM, never more than the
+  // work items
+  const int work = max_tiles * cdiv(M, 128);
+  const int grid = min(num_sms() * (NT <= 32 ? 2 : 1), work);
+  kern<<<grid, 256, L::kAlloc, s>>>(ta, tb, sfa, sfb, ws, bias, topk_w, (__nv_bfloat16*)out, M, Kp, ld_out, alpha,
                                     limit, E_local, R_max, atoms_max, status);
   return (int)cudaGetLastError();
 }
@@ -413,15 +532,15 @@ static int run_gemms(const MoeShape& sh, const void* w13, const uint8_t* sf13, c
                      float limit, int R_max, int max_tiles, int atoms_max, int* status, cudaStream_t s) {
   CUtensorMap ta1, tb1, ta2, tb2;
   int rc;
-  if ((rc = make_weight_map(&ta1, w13, sh.E_local, 2 * sh.I, sh.K1p, A_FP4))) return rc;
+  if ((rc = make_weight_map(&ta1, w13, sh.E_local * cdiv(2 * sh.I, 128) * (sh.K1p / 128), A_FP4))) return rc;
   if ((rc = make_act_map(&tb1, ws.xq, R_max, sh.K1p, NT))) return rc;
-  if ((rc = make_weight_map(&ta2, w2, sh.E_local, sh.H, sh.K2p, A_FP4))) return rc;
+  if ((rc = make_weight_map(&ta2, w2, sh.E_local * cdiv(sh.H, 128) * (sh.K2p / 128), A_FP4))) return rc;
   if ((rc = make_act_map(&tb2, ws.aq, R_max, sh.K2p, NT))) return rc;
   rc = launch_gemm<NT, STAGES, A_FP4, kEpiSwiglu>(ta1, tb1, sf13, ws.sf1, ws, b13, topk_w, ws.act, 2 * sh.I,
                                                   sh.K1p, sh.I, alpha, limit, max_tiles, sh.E_local, R_max, atoms_max,
                                                   status, s);
   if (rc) return rc;
-  moe_quant_kernel<<<cdiv(R_max, 4), 128, 0, s>>>(ws.aq, ws.sf2, (const __nv_bfloat16*)ws.act, sh.I, ws.row_route,
+  moe_quant_kernel<<<cdiv(R_max * cdiv(sh.K2p / 32, 32), 4), 128, 0, s>>>(ws.aq, ws.sf2, (const __nv_bfloat16*)ws.act, sh.I, ws.row_route,
                                                   0, ws.offsets, ws.atom_base, sh.E_local, sh.I, sh.K2p, R_max, R_max,
                                                   atoms_max, NT, status);
   rc = launch_gemm<NT, STAGES, A_FP4, kEpiDown>(ta2, tb2, sf2w, ws.sf2, ws, b2, topk_w, ws.y, sh.H, sh.K2p, sh.H,
@@ -460,30 +579,35 @@ extern "C" int b200_moe_mx_forward(void* out, const void* x, const int* topk_ids
   const MoeShape& sh = *shape;
   const MoeWorkspace& ws = *wsp;
   if (sh.T == 0) return 0;
-  if (sh.K1p % 128 || sh.K2p % 128 || sh.H % 2 || sh.I % 32 || sh.H % 32 || sh.E_local > 1024) return kBadShape;
-  if (sh.nt != 32 && sh.nt != 128) return kBadShape;
+  if (sh.K1p % 128 || sh.K2p % 128 || sh.H % 32 || sh.I % 32 || sh.E_local > 1024 || sh.k > 16) return kBadShape;
+  if (sh.nt != 16 && sh.nt != 32 && sh.nt != 128) return kBadShape;
   const int R_max = sh.T * sh.k;
   const int max_tiles = cdiv(R_max, sh.nt) + sh.E_local;
-  moe_route_kernel<<<1, 1024, 2 * sh.E_local * sizeof(int), s>>>(topk_ids, R_max, sh.E_local, sh.expert_offset,
-                                                                 sh.nt, max_tiles, ws);
+  moe_route_kernel<<<1, 1024, 2 * sh.E_local * sizeof(int), s>>>(topk_ids, R_max, sh.E_local,
+                                                                          sh.expert_offset, sh.nt, max_tiles, ws);
   const int atoms_max = max_tiles;
-  moe_quant_kernel<<<cdiv(R_max, 4), 128, 0, s>>>(ws.xq, ws.sf1, (const __nv_bfloat16*)x, sh.H, ws.row_route,
+  moe_quant_kernel<<<cdiv(R_max * cdiv(sh.K1p / 32, 32), 4), 128, 0, s>>>(ws.xq, ws.sf1, (const __nv_bfloat16*)x, sh.H, ws.row_route,
                                                   sh.k, ws.offsets, ws.atom_base, sh.E_local, sh.H, sh.K1p, R_max,
                                                   sh.T, atoms_max, sh.nt, status);
   int rc;
-  if (sh.nt == 32) {
-    rc = sh.a_fp4 ? run_gemms<32, 4, true>(sh, w13, sf13, b13, w2, sf2w, b2, topk_w, ws, alpha, limit, R_max,
+  if (sh.nt == 16) {
+    rc = sh.a_fp4 ? run_gemms<16, 5, true>(sh, w13, sf13, b13, w2, sf2w, b2, topk_w, ws, alpha, limit, R_max,
                                            max_tiles, atoms_max, status, s)
-                  : run_gemms<32, 4, false>(sh, w13, sf13, b13, w2, sf2w, b2, topk_w, ws, alpha, limit, R_max,
+                  : run_gemms<16, 5, false>(sh, w13, sf13, b13, w2, sf2w, b2, topk_w, ws, alpha, limit, R_max,
+                                            max_tiles, atoms_max, status, s);
+  } else if (sh.nt == 32) {
+    rc = sh.a_fp4 ? run_gemms<32, 5, true>(sh, w13, sf13, b13, w2, sf2w, b2, topk_w, ws, alpha, limit, R_max,
+                                           max_tiles, atoms_max, status, s)
+                  : run_gemms<32, 5, false>(sh, w13, sf13, b13, w2, sf2w, b2, topk_w, ws, alpha, limit, R_max,
                                             max_tiles, atoms_max, status, s);
   } else {
-    rc = sh.a_fp4 ? run_gemms<128, 4, true>(sh, w13, sf13, b13, w2, sf2w, b2, topk_w, ws, alpha, limit, R_max,
+    rc = sh.a_fp4 ? run_gemms<128, 6, true>(sh, w13, sf13, b13, w2, sf2w, b2, topk_w, ws, alpha, limit, R_max,
                                             max_tiles, atoms_max, status, s)
-                  : run_gemms<128, 4, false>(sh, w13, sf13, b13, w2, sf2w, b2, topk_w, ws, alpha, limit, R_max,
+                  : run_gemms<128, 6, false>(sh, w13, sf13, b13, w2, sf2w, b2, topk_w, ws, alpha, limit, R_max,
                                              max_tiles, atoms_max, status, s);
   }
   if (rc) return rc;
-  moe_reduce_kernel<<<sh.T, 256, 0, s>>>((__nv_bfloat16*)out, (const __nv_bfloat16*)ws.y, topk_ids, sh.k,
+  moe_reduce_kernel<<<sh.T, 128, 0, s>>>((__nv_bfloat16*)out, (const __nv_bfloat16*)ws.y, topk_ids, sh.k,
                                          sh.E_local, sh.expert_offset, sh.H);
   return (int)cudaGetLastError();
 }

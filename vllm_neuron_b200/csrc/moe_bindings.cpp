@@ -30,10 +30,15 @@ void moe_mx(Tensor out, Tensor x, Tensor topk_ids, Tensor topk_w, Tensor w13, Te
   sh.K1p = (H + 127) / 128 * 128;
   sh.K2p = (I + 127) / 128 * 128;
   sh.a_fp4 = a_fp4 ? 1 : 0;
-  sh.nt = (sh.T * sh.k <= 2048) ? 32 : 128;
-  const int64_t rowb1 = a_fp4 ? sh.K1p / 2 : sh.K1p, rowb2 = a_fp4 ? sh.K2p / 2 : sh.K2p;
-  TORCH_CHECK(w13.size(1) == 2 * I && w13.size(2) == rowb1, "w13 must be [E, 2I, K1p(/2)]");
-  TORCH_CHECK(w2.size(1) == H && w2.size(2) == rowb2, "w2 must be [E, H, K2p(/2)]");
+  const int routes = sh.T * sh.k;
+  sh.nt = routes <= 512 ? 16 : (routes <= 2048 ? 32 : 128);
+  const int64_t tw = a_fp4 ? 64 : 128;
+  TORCH_CHECK(w13.dim() == 5 && w13.size(1) == (2 * I + 127) / 128 && w13.size(2) == sh.K1p / 128 &&
+                  w13.size(3) == 128 && w13.size(4) == tw && w13.is_contiguous(),
+              "w13 must be contiguous tiles [E, 2I/128, K1p/128, 128, 64 (fp4) | 128 (fp8)]");
+  TORCH_CHECK(w2.dim() == 5 && w2.size(1) == (H + 127) / 128 && w2.size(2) == sh.K2p / 128 && w2.size(3) == 128 &&
+                  w2.size(4) == tw && w2.is_contiguous(),
+              "w2 must be contiguous tiles [E, H/128, K2p/128, 128, 64 | 128]");
   TORCH_CHECK(sf13.numel() == (int64_t)sh.E_local * ((2 * I + 127) / 128) * (sh.K1p / 128) * 512, "sf13 atoms size");
   TORCH_CHECK(sf2.numel() == (int64_t)sh.E_local * ((H + 127) / 128) * (sh.K2p / 128) * 512, "sf2 atoms size");
   TORCH_CHECK(reinterpret_cast<uintptr_t>(w13.data_ptr()) % 32 == 0 && reinterpret_cast<uintptr_t>(w2.data_ptr()) % 32 == 0,

@@ -36,6 +36,66 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(T* __restrict__ out, cons
   for (int i = threadIdx.x; i < H; i += blockDim.x) orow[i] = from_float<T>(srow[i] * inv * w[i]);
 }
 
+// Vector path: bf16 rows with H % 8 == 0, each thread holds up to kMaxVec 16-byte chunks
+// of the row in registers (one read, one write per element).
+constexpr int kMaxVec = 4;
+
+template <bool kAdd>
+__global__ void __launch_bounds__(256) rms_norm_vec_kernel(__nv_bfloat16* __restrict__ out,
+                                                           const __nv_bfloat16* __restrict__ x,
+                                                           __nv_bfloat16* __restrict__ residual,
+                                                           const float* __restrict__ w, int H, float eps) {
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  const int nchunk = H / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * H);
+  uint4* rr = kAdd ? reinterpret_cast<uint4*>(residual + (size_t)row * H) : nullptr;
+  float v[kMaxVec][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+    if (c < nchunk) {
+      uint4 u = xr[c];
+      const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(&u);
+      if (kAdd) {
+        uint4 ru = rr[c];
+        const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&ru);
+        uint4 o;
+        __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&o);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          ob[q] = __float2bfloat16(__bfloat162float(hb[q]) + __bfloat162float(rb[q]));
+          v[i][q] = __bfloat162float(ob[q]);
+        }
+        rr[c] = o;
+      } else {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) v[i][q] = __bfloat162float(hb[q]);
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) ss += v[i][q] * v[i][q];
+    }
+  }
+  const float tot = block_sum(ss, red);
+  const float inv = rsqrtf(tot / (float)H + eps);
+  uint4* orow = reinterpret_cast<uint4*>(out + (size_t)row * H);
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+    if (c < nchunk) {
+      const float4 w0 = reinterpret_cast<const float4*>(w)[2 * c];
+      const float4 w1 = reinterpret_cast<const float4*>(w)[2 * c + 1];
+      const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      uint4 o;
+      __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&o);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) ob[q] = __float2bfloat16(v[i][q] * inv * ww[q]);
+      orow[c] = o;
+    }
+  }
+}
+
 template <typename T>
 static void launch_norm(void* out, const void* x, void* res, const float* w, int rows, int H, float eps,
                         cudaStream_t s) {
@@ -54,6 +114,22 @@ extern "C" int b200_rms_norm(void* out, const void* x, void* residual, const flo
                              float eps, int dtype, cudaStream_t s) {
   using namespace b200;
   if (H > 12288) return kBadShape;  // row staged in <= 48 KB of shared memory
+  const bool aligned = ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(x) |
+                         reinterpret_cast<uintptr_t>(residual) | reinterpret_cast<uintptr_t>(w)) & 15) == 0;
+  if (dtype == kBF16 && H % 8 == 0 && aligned && rows > 0) {
+    const int nchunk = H / 8;
+    int threads = 32;
+    while (threads * kMaxVec < nchunk) threads *= 2;
+    if (threads <= 256) {
+      if (residual)
+        rms_norm_vec_kernel<true><<<rows, threads, 0, s>>>((__nv_bfloat16*)out, (const __nv_bfloat16*)x,
+                                                           (__nv_bfloat16*)residual, w, H, eps);
+      else
+        rms_norm_vec_kernel<false><<<rows, threads, 0, s>>>((__nv_bfloat16*)out, (const __nv_bfloat16*)x, nullptr,
+                                                            w, H, eps);
+      return (int)cudaGetLastError();
+    }
+  }
   switch (dtype) {
     case kBF16: launch_norm<__nv_bfloat16>(out, x, residual, w, rows, H, eps, s); break;
     case kF16: launch_norm<__half>(out, x, residual, w, rows, H, eps, s); break;

@@ -76,6 +76,79 @@ __global__ void __launch_bounds__(256) rope_kv_kernel(T* __restrict__ qkv, const
   }
 }
 
+// Fast path (bf16 q/k/v, full rotary, no QK-norm): one thread per (head, group of 4 rotary
+// pairs); 8-byte vector loads of both halves, 16-byte cos/sin loads, 8-byte cache stores.
+template <typename CT>
+__global__ void __launch_bounds__(256) rope_kv_vec_kernel(__nv_bfloat16* __restrict__ qkv,
+                                                          const int64_t* __restrict__ pos,
+                                                          const float* __restrict__ cos_sin, CT* __restrict__ kc,
+                                                          CT* __restrict__ vc, const int64_t* __restrict__ slots,
+                                                          int nq, int nkv, int d, int stride, int bs, int num_blocks,
+                                                          float inv_ks, float inv_vs, int* status) {
+  const int t = blockIdx.x;
+  const int half = d / 2, g4 = half / 4;  // groups of 4 pairs per head
+  const int64_t p = pos[t];
+  const float* cs = cos_sin + p * d;
+  __nv_bfloat16* row = qkv + (size_t)t * stride;
+  const int64_t slot = slots[t];
+  int64_t blk = slot >= 0 ? slot / bs : -1;
+  const int off = slot >= 0 ? (int)(slot % bs) : 0;
+  if (blk >= num_blocks) {
+    if (status && threadIdx.x == 0) atomicCAS(status, 0, kBadIndex);
+    blk = -1;
+  }
+  const int nrot = (nq + nkv) * g4;
+  const int nv = nkv * (d / 4);
+  for (int i = threadIdx.x; i < nrot + nv; i += blockDim.x) {
+    if (i < nrot) {
+      const int h = i / g4, g = i % g4;
+      __nv_bfloat16* x = row + (size_t)h * d;
+      const uint2 a2 = *reinterpret_cast<const uint2*>(x + 4 * g);
+      const uint2 b2 = *reinterpret_cast<const uint2*>(x + half + 4 * g);
+      const float4 c = *reinterpret_cast<const float4*>(cs + 4 * g);
+      const float4 sn = *reinterpret_cast<const float4*>(cs + half + 4 * g);
+      const __nv_bfloat16* a = reinterpret_cast<const __nv_bfloat16*>(&a2);
+      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&b2);
+      const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
+      float ra[4], rb[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float av = __bfloat162float(a[q]), bv = __bfloat162float(b[q]);
+        ra[q] = av * cc[q] - bv * ss[q];
+        rb[q] = bv * cc[q] + av * ss[q];
+      }
+      uint2 oa, ob;
+      __nv_bfloat16* pa = reinterpret_cast<__nv_bfloat16*>(&oa);
+      __nv_bfloat16* pb = reinterpret_cast<__nv_bfloat16*>(&ob);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        pa[q] = __float2bfloat16(ra[q]);
+        pb[q] = __float2bfloat16(rb[q]);
+      }
+      *reinterpret_cast<uint2*>(x + 4 * g) = oa;
+      *reinterpret_cast<uint2*>(x + half + 4 * g) = ob;
+      if (h >= nq && blk >= 0) {
+        CT* dst = kc + (((size_t)blk * nkv + (h - nq)) * bs + off) * d;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          dst[4 * g + q] = from_float<CT>(__bfloat162float(pa[q]) * inv_ks);
+          dst[half + 4 * g + q] = from_float<CT>(__bfloat162float(pb[q]) * inv_ks);
+        }
+      }
+    } else if (blk >= 0) {
+      const int j = i - nrot, h = j / (d / 4), c4 = j % (d / 4);
+      const __nv_bfloat16* x = row + (size_t)(nq + nkv + h) * d + 4 * c4;
+      CT* dst = vc + (((size_t)blk * nkv + h) * bs + off) * d + 4 * c4;
+      if constexpr (sizeof(CT) == 2) {
+        *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(x);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) dst[q] = from_float<CT>(__bfloat162float(x[q]) * inv_vs);
+      }
+    }
+  }
+}
+
 template <typename T>
 static int launch_rope(void* qkv, const int64_t* pos, const float* cs, void* kc, void* vc, const int64_t* slots,
                        int T_, int nq, int nkv, int d, int rd, int stride, int bs, int nb, float ks, float vs,
@@ -122,6 +195,22 @@ extern "C" int b200_rope_kv_write(void* qkv, const int64_t* positions, const flo
                                   int dtype, int cache_dtype, int* status, cudaStream_t s) {
   using namespace b200;
   if (rotary_dim > d || rotary_dim % 2) return kBadShape;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(cos_sin)) & 15) == 0 &&
+                       (qkv_stride % 8) == 0;
+  if (dtype == kBF16 && rotary_dim == d && d % 8 == 0 && q_norm_w == nullptr && k_norm_w == nullptr && aligned &&
+      T > 0) {
+    const int work = (nq + nkv) * (d / 8) + nkv * (d / 4);
+    const int threads = work >= 256 ? 256 : ((work + 31) / 32) * 32;
+    if (cache_dtype == kFP8E4M3)
+      rope_kv_vec_kernel<__nv_fp8_e4m3><<<T, threads, 0, s>>>(
+          (__nv_bfloat16*)qkv, positions, cos_sin, (__nv_fp8_e4m3*)k_cache, (__nv_fp8_e4m3*)v_cache, slot_mapping, nq,
+          nkv, d, qkv_stride, block_size, num_blocks, 1.f / k_scale, 1.f / v_scale, status);
+    else
+      rope_kv_vec_kernel<__nv_bfloat16><<<T, threads, 0, s>>>(
+          (__nv_bfloat16*)qkv, positions, cos_sin, (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, slot_mapping,
+          nq, nkv, d, qkv_stride, block_size, num_blocks, 1.f, 1.f, status);
+    return (int)cudaGetLastError();
+  }
   switch (dtype) {
     case kBF16:
       return launch_rope<__nv_bfloat16>(qkv, positions, cos_sin, k_cache, v_cache, slot_mapping, T, nq, nkv, d,

@@ -65,54 +65,80 @@ __global__ void topk_softmax_kernel(int* __restrict__ ids, float* __restrict__ w
   }
 }
 
+// argmax: each CTA scans a slice of one row with 16-byte loads and folds its (value,
+// index) into a 64-bit key [order-preserving value bits | ~index] with atomicMax, so the
+// largest value wins and among equal values the lowest index; a second kernel unpacks.
+B200_D uint32_t order_bits(float f) {
+  const uint32_t u = __float_as_uint(f);
+  if (f != f) return 0u;
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+B200_D float from_order_bits(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
 template <typename T>
-__global__ void __launch_bounds__(1024) argmax_kernel(float* __restrict__ vals, int64_t* __restrict__ idx,
-                                                      const T* __restrict__ logits, int V) {
-  const T* row = logits + (size_t)blockIdx.x * V;
+__global__ void __launch_bounds__(256) argmax_partial_kernel(unsigned long long* __restrict__ best,
+                                                             const T* __restrict__ logits, int V, int slice) {
+  const int b = blockIdx.y;
+  const int lo = blockIdx.x * slice, hi = min(V, lo + slice);
+  const T* row = logits + (size_t)b * V;
   float bv = -INFINITY;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float x = to_float(row[i]);
-    if (x > bv) {  // strided scan: first hit per thread is its lowest index
-      bv = x;
-      bi = i;
-    }
-  }
+  constexpr int kVec = 16 / sizeof(T);
+  const bool vec_ok = (reinterpret_cast<uintptr_t>(row) % 16 == 0) && (lo % kVec == 0);
+  if (vec_ok) {
+    const int n_vec = (hi - lo) / kVec;
+    for (int c = threadIdx.x; c < n_vec; c += blockDim.x) {
+      const uint4 u = reinterpret_cast<const uint4*>(row + lo)[c];
+      const T* e = reinterpret_cast<const T*>(&u);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ov > bv || (ov == bv && oi < bi)) {
-      bv = ov;
-      bi = oi;
-    }
-  }
-  __shared__ float sv[32];
-  __shared__ int si[32];
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  if (lane == 0) {
-    sv[wid] = bv;
-    si[wid] = bi;
-  }
-  __syncthreads();
-  if (wid == 0) {
-    const int nw = blockDim.x >> 5;
-    bv = lane < nw ? sv[lane] : -INFINITY;
-    bi = lane < nw ? si[lane] : 0x7fffffff;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
+      for (int q = 0; q < kVec; ++q) {
+        const float x = to_float(e[q]);
+        if (x > bv) {
+          bv = x;
+          bi = lo + c * kVec + q;
+        }
       }
     }
-    if (lane == 0) {
-      vals[blockIdx.x] = bv;
-      idx[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+    for (int i = lo + n_vec * kVec + threadIdx.x; i < hi; i += blockDim.x) {
+      const float x = to_float(row[i]);
+      if (x > bv || (x == bv && i < bi)) {
+        bv = x;
+        bi = i;
+      }
+    }
+  } else {
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+      const float x = to_float(row[i]);
+      if (x > bv) {
+        bv = x;
+        bi = i;
+      }
     }
   }
+  unsigned long long key = bi == 0x7fffffff ? 0ull
+                                            : ((unsigned long long)order_bits(bv) << 32) | (0xffffffffu - (uint32_t)bi);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+    key = other > key ? other : key;
+  }
+  if ((threadIdx.x & 31) == 0 && key != 0ull) atomicMax(best + b, key);
+}
+
+__global__ void argmax_finish_kernel(float* __restrict__ vals, int64_t* __restrict__ idx,
+                                     const unsigned long long* __restrict__ best, int B) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  const unsigned long long k = best[b];
+  if (k == 0ull) {
+    vals[b] = -INFINITY;
+    idx[b] = 0;
+    return;
+  }
+  vals[b] = from_order_bits((uint32_t)(k >> 32));
+  idx[b] = (int64_t)(0xffffffffu - (uint32_t)(k & 0xffffffffu));
 }
 
 B200_D uint32_t order_key(float f) {
@@ -276,12 +302,19 @@ extern "C" int b200_topk_softmax(int* ids, float* weights, const float* logits, 
 
 extern "C" int b200_argmax(float* vals, int64_t* idx, const void* logits, int B, int V, int dtype, cudaStream_t s) {
   if (B == 0) return 0;
+  // the int64 output doubles as the buffer of packed 64-bit keys, unpacked in place
+  unsigned long long* best = reinterpret_cast<unsigned long long*>(idx);
+  cudaError_t e = cudaMemsetAsync(best, 0, sizeof(unsigned long long) * B, s);
+  if (e != cudaSuccess) return (int)e;
+  const int slice = 8192;
+  dim3 grid(cdiv(V, slice), B);
   switch (dtype) {
-    case kBF16: argmax_kernel<__nv_bfloat16><<<B, 1024, 0, s>>>(vals, idx, (const __nv_bfloat16*)logits, V); break;
-    case kF16: argmax_kernel<__half><<<B, 1024, 0, s>>>(vals, idx, (const __half*)logits, V); break;
-    case kF32: argmax_kernel<float><<<B, 1024, 0, s>>>(vals, idx, (const float*)logits, V); break;
+    case kBF16: argmax_partial_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(best, (const __nv_bfloat16*)logits, V, slice); break;
+    case kF16: argmax_partial_kernel<__half><<<grid, 256, 0, s>>>(best, (const __half*)logits, V, slice); break;
+    case kF32: argmax_partial_kernel<float><<<grid, 256, 0, s>>>(best, (const float*)logits, V, slice); break;
     default: return kBadShape;
   }
+  argmax_finish_kernel<<<cdiv(B, 128), 128, 0, s>>>(vals, idx, best, B);
   return (int)cudaGetLastError();
 }
 

@@ -140,13 +140,15 @@ class ModelRunner:
         return 32
 
     def num_splits_for(self, batch: int) -> int:
-        """Split-KV factor so that batch x kv_heads x splits covers the SMs ~2 times."""
+        """Split-KV factor: batch x kv_heads x splits CTAs should cover the SMs about four
+        times (the decode kernel keeps ~3 CTAs resident per SM), so a single long sequence
+        is spread over the whole GPU and a full batch still avoids a thin last wave."""
         if self.device.type != "cuda":
             return 1
         spec = self.model.get_kv_spec()
-        hkv = max(1, max(l.num_kv_heads for l in spec.layers))
+        hkv = max(1, max(l.num_kv_heads for l in spec.layers if l.kind == "attention"))
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-        want = max(1, math.ceil(2 * sms / (batch * hkv)))
+        want = max(1, math.ceil(4 * sms / (batch * hkv)))
         return int(min(self.max_splits(batch), want))
 
     # ------------------------------------------------------------------ inputs

@@ -29,7 +29,7 @@ import torch.nn as nn
 from .. import ops
 from ..nn.linear import ParallelLMHead, RMSNorm, RowParallelLinear, VocabParallelEmbedding
 from ..ops import reference as ref
-from ..ops.mx_layout import pad_k, round_up, scales_to_atoms
+from ..ops.mx_layout import round_up, scales_to_atoms, tile_values, tiled_shape
 from ..parallel.state import GroupCoordinator, ParallelState
 from .base import KVSpec, LayerSpec, kv_head_sharding
 
@@ -170,11 +170,12 @@ class GptOssExperts(nn.Module):
         if self.quant == "mxfp4":
             if H % 32 or I % 32:
                 raise ValueError("MXFP4 needs hidden and intermediate sizes divisible by 32")
-            # kernel layout (ops/mx_layout.py): K padded to 128, scales in 512-byte atoms
+            # kernel layout (ops/mx_layout.py): 128x128 value tiles stored contiguously,
+            # scales in 512-byte atoms
             k1, k2 = round_up(H, 128), round_up(I, 128)
-            self.w13 = _param((self.E_local, 2 * I, k1 // 2), torch.uint8, device)
+            self.w13 = _param(tiled_shape(self.E_local, 2 * I, H), torch.uint8, device)
             self.s13 = _param((self.E_local, -(-2 * I // 128), k1 // 128, 512), torch.uint8, device)
-            self.w2 = _param((self.E_local, H, k2 // 2), torch.uint8, device)
+            self.w2 = _param(tiled_shape(self.E_local, H, I), torch.uint8, device)
             self.s2 = _param((self.E_local, -(-H // 128), k2 // 128, 512), torch.uint8, device)
         else:
             self.w13 = _param((self.E_local, 2 * I, H), dtype, device)
@@ -347,7 +348,7 @@ class GptOssForCausalLM(nn.Module):
         if ex.quant == "mxfp4":
             if kind == "blocks":
                 vals = loc.reshape(loc.shape[0], loc.shape[1], -1)
-                getattr(ex, "w" + which).data.copy_(pad_k(vals.to(ex.w13.device), K))
+                getattr(ex, "w" + which).data.copy_(tile_values(vals.to(ex.w13.device), K))
             else:
                 getattr(ex, "s" + which).data.copy_(scales_to_atoms(loc.to(ex.w13.device), K))
             return
@@ -365,7 +366,7 @@ class GptOssForCausalLM(nn.Module):
         if ex.quant == "mxfp4":
             K = ex.H if which == "13" else ex.I
             blocks, scales = ref.quantize_mxfp4(w.float())
-            getattr(ex, "w" + which).data.copy_(pad_k(blocks, K))
+            getattr(ex, "w" + which).data.copy_(tile_values(blocks, K))
             getattr(ex, "s" + which).data.copy_(scales_to_atoms(scales, K))
         else:
             getattr(ex, "w" + which).data.copy_(w.to(getattr(ex, "w" + which).dtype))

@@ -217,8 +217,9 @@ def moe_mxfp4(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, w13
               b2: torch.Tensor | None, expert_offset: int, alpha: float, limit: float, H: int, I: int,
               status: torch.Tensor | None = None) -> torch.Tensor:
     """Routed experts with packed MX weights in the kernel layout (``ops/mx_layout.py``):
-    w13 [E_local, 2I, K1p/2] u8 (gate/up interleaved rows) + s13 scale atoms,
-    w2 [E_local, H, K2p/2] u8 + s2 atoms; biases fp32 [E_local, 2I] / [E_local, H].
+    w13 tiles [E_local, 2I/128, K1p/128, 128, 64] u8 (gate/up interleaved rows) + s13
+    scale atoms, w2 tiles [E_local, H/128, K2p/128, 128, 64] + s2 atoms; biases fp32
+    [E_local, 2I] / [E_local, H].
     Returns this rank's partial sum over its experts, [T, H] in x.dtype."""
     E = w13.shape[0]
     if use_kernel(x) and x.dtype == torch.bfloat16:
@@ -229,10 +230,10 @@ def moe_mxfp4(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, w13
         _k().moe_mx(out, x.contiguous(), topk_ids.to(torch.int32).contiguous(), topk_w.float().contiguous(), w13,
                     s13, b13_, w2, s2, b2_, expert_offset, H, I, True, alpha, limit, st)
         return out
-    from .mx_layout import atoms_to_scales, unpad_k
+    from .mx_layout import atoms_to_scales, untile_values
 
-    w13f = ref.dequant_mxfp4(unpad_k(w13, H), atoms_to_scales(s13, 2 * I, H))
-    w2f = ref.dequant_mxfp4(unpad_k(w2, I), atoms_to_scales(s2, H, I))
+    w13f = ref.dequant_mxfp4(untile_values(w13, 2 * I, H), atoms_to_scales(s13, 2 * I, H))
+    w2f = ref.dequant_mxfp4(untile_values(w2, H, I), atoms_to_scales(s2, H, I))
     return ref.moe_experts(x, topk_ids, topk_w, w13f, b13, w2f, b2, alpha, limit, True, expert_offset)
 
 

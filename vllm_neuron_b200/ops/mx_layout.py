@@ -1,5 +1,10 @@
 """Kernel layout of MX-format (MXFP4 / MXFP8) expert weights.
 
+Values are stored tile-contiguous: ``[E, ceil(rows/128), Kp/128, 128, 128*bits/8]`` so
+that every (128-row, 128-element) block the tensor cores consume is one contiguous
+8 KB (fp4) or 16 KB (fp8) run in HBM, which the TMA reads in one sweep.  Rows are
+zero-padded to a multiple of 128 and K to ``Kp = roundup(K, 128)``.
+
 The checkpoint stores, per expert, ``blocks [rows, K/32, 16]`` (two e2m1 per byte) and
 ``scales [rows, K/32]`` (ue8m0).  The tensor-core kernel reads:
 * values ``[E, rows, Kp/2]`` (fp4) or ``[E, rows, Kp]`` (fp8) with K zero-padded to
@@ -53,3 +58,28 @@ def atoms_to_scales(atoms: torch.Tensor, rows: int, K: int) -> torch.Tensor:
 
 def unpad_k(values: torch.Tensor, K: int, fp4: bool = True) -> torch.Tensor:
     return values[..., : (K // 2 if fp4 else K)]
+
+
+def tile_values(values: torch.Tensor, K: int, fp4: bool = True) -> torch.Tensor:
+    """values [E, rows, K/2] (fp4) or [E, rows, K] (fp8) -> [E, Rb, Kb, 128, W] with
+    W = 64 (fp4) or 128 (fp8): block (rb, kb) holds rows rb*128.. and K elements kb*128.."""
+    E, R, _ = values.shape
+    padded = pad_k(values, K, fp4)
+    Rp = round_up(R, 128)
+    if Rp != R:
+        z = torch.zeros(E, Rp, padded.shape[-1], dtype=padded.dtype, device=padded.device)
+        z[:, :R] = padded
+        padded = z
+    W = 64 if fp4 else 128
+    Kb = padded.shape[-1] // W
+    return padded.view(E, Rp // 128, 128, Kb, W).permute(0, 1, 3, 2, 4).contiguous()
+
+
+def untile_values(tiled: torch.Tensor, rows: int, K: int, fp4: bool = True) -> torch.Tensor:
+    E, Rb, Kb, _, W = tiled.shape
+    flat = tiled.permute(0, 1, 3, 2, 4).reshape(E, Rb * 128, Kb * W)
+    return flat[:, :rows, : (K // 2 if fp4 else K)].contiguous()
+
+
+def tiled_shape(E: int, rows: int, K: int, fp4: bool = True) -> tuple[int, int, int, int, int]:
+    return (E, -(-rows // 128), round_up(K, 128) // 128, 128, 64 if fp4 else 128)
