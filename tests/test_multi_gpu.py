@@ -1,0 +1,100 @@
+"""Fused NVLink all-reduce (+bias, residual, RMSNorm) on 2 GPUs, against NCCL + the
+unfused ops; eager and inside a CUDA graph.  Skipped with fewer than 2 GPUs."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        import torch.distributed as dist
+
+        from vllm_neuron_b200 import ops
+        from vllm_neuron_b200.parallel import state as ps
+        from vllm_neuron_b200.parallel.communicator import attach_communicators
+
+        torch.cuda.set_device(rank)
+        ps.init_distributed_environment(world, rank, backend="nccl", local_rank=rank, timeout_s=120)
+        st = ps.initialize_parallel_state(tp=world, backend="nccl", timeout_s=120)
+        dev = torch.device("cuda", rank)
+        attach_communicators(st, dev)
+        g = st.tp
+        assert g.communicator is not None
+        errs = []
+        for call in range(5):  # consecutive calls alternate the double-buffered slots
+            torch.manual_seed(100 + call * 7 + rank)
+            T, H = [64, 1, 17, 64, 300][call], 2880
+            x = torch.randn(T, H, device=dev).bfloat16()
+            ref = x.float().clone()
+            dist.all_reduce(ref)
+            got = g.communicator.all_reduce(x)
+            errs.append(("sum", (got.float() - ref).abs().max().item()))
+            torch.manual_seed(999 + call)  # residual / weights identical on all ranks
+            res = torch.randn(T, H, device=dev).bfloat16()
+            w = torch.rand(H, device=dev) + 0.5
+            bias = (torch.randn(H, device=dev) * 0.1).bfloat16()
+            res_ref = res.clone()
+            want, want_res = ops.fused_add_rms_norm((ref.bfloat16() + bias), res_ref, w, 1e-5)
+            out, res_out = g.communicator.all_reduce_add_rmsnorm(x, res, w, 1e-5, bias)
+            errs.append(("norm", (out.float() - want.float()).abs().max().item()))
+            errs.append(("res", (res_out.float() - want_res.float()).abs().max().item()))
+        # CUDA graph: capture two fused calls, replay three times with new inputs
+        x = torch.zeros(64, 2880, device=dev, dtype=torch.bfloat16)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            y1 = g.communicator.all_reduce(x)
+            y2 = g.communicator.all_reduce(y1)
+        torch.cuda.current_stream().wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            y1 = g.communicator.all_reduce(x)
+            y2 = g.communicator.all_reduce(y1)
+        for rep in range(3):
+            x.copy_(torch.full_like(x, float(rank + 1 + rep)))
+            graph.replay()
+            torch.cuda.synchronize()
+            s1 = sum(r + 1 + rep for r in range(world))
+            errs.append(("graph", max((y1.float() - s1).abs().max().item(), (y2.float() - s1 * world).abs().max().item())))
+        torch.cuda.synchronize()
+        st_code = int(ops.device_status(dev)[0].item())
+        del graph
+        ps.destroy_parallel_state()
+        dist.destroy_process_group()
+        q.put((rank, errs, st_code, None))
+    except Exception as e:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, [], -1, traceback.format_exc()))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fused_allreduce_two_gpus():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, errs, code, tb in res:
+        assert tb is None, tb
+        assert code == 0, f"rank {rank} status {code}"
+        for kind, e in errs:
+            tol = {"sum": 0.1, "norm": 0.06, "res": 0.1, "graph": 0.0}[kind]
+            assert e <= tol, f"rank {rank} {kind} err {e}"

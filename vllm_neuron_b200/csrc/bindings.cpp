@@ -188,6 +188,9 @@ void sample(Tensor out, Tensor logits, Tensor temperature, Tensor top_k, Tensor 
 
 void register_moe_ops(torch::Library& m);
 void register_moe_impls(torch::Library& m);
+void register_comm_ops(torch::Library& m);
+void register_comm_impls(torch::Library& m);
+void register_comm_cpu_impls(torch::Library& m);
 
 TORCH_LIBRARY(b200, m) {
   m.def("rms_norm(Tensor(a!) out, Tensor x, Tensor w, float eps) -> ()");
@@ -214,7 +217,11 @@ TORCH_LIBRARY(b200, m) {
       "sample(Tensor(a!) out, Tensor logits, Tensor temperature, Tensor top_k, Tensor top_p, Tensor uniform, "
       "int max_top_k) -> ()");
   register_moe_ops(m);
+  register_comm_ops(m);
 }
+
+// ops without tensor arguments (pointer plumbing) dispatch through CompositeExplicitAutograd
+TORCH_LIBRARY_IMPL(b200, CompositeExplicitAutograd, m) { register_comm_cpu_impls(m); }
 
 TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("rms_norm", &rms_norm);
@@ -228,6 +235,7 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("argmax", &argmax);
   m.impl("sample", &sample);
   register_moe_impls(m);
+  register_comm_impls(m);
 }
 
 // Python module entry so `import vllm_neuron_b200._C` loads the library.

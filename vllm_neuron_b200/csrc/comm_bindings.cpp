@@ -1,0 +1,91 @@
+// torch.ops.b200 registration of the fused NVLink collectives and the IPC plumbing.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+extern "C" {
+int b200_comm_alloc(size_t slot_bytes, void** out);
+int b200_comm_free(void* p);
+int b200_ipc_get_handle(void* p, void* handle64);
+int b200_ipc_open_handle(const void* handle64, void** out);
+int b200_ipc_close(void* p);
+int b200_allreduce_fused(void* const* bases, int rank, int world, size_t slot_bytes, const void* in, void* out,
+                         void* residual, const void* bias, const float* w, float eps, int T, int H, int num_blocks,
+                         int* status, cudaStream_t s);
+}
+
+namespace {
+using at::Tensor;
+
+int64_t comm_alloc(int64_t slot_bytes) {
+  void* p = nullptr;
+  const int rc = b200_comm_alloc((size_t)slot_bytes, &p);
+  TORCH_CHECK(rc == 0, "comm_alloc failed: ", rc);
+  return reinterpret_cast<int64_t>(p);
+}
+
+void comm_free(int64_t p) { b200_comm_free(reinterpret_cast<void*>(p)); }
+
+Tensor ipc_get_handle(int64_t p) {
+  Tensor h = at::empty({64}, at::TensorOptions().dtype(at::kByte));
+  const int rc = b200_ipc_get_handle(reinterpret_cast<void*>(p), h.data_ptr());
+  TORCH_CHECK(rc == 0, "cudaIpcGetMemHandle failed: ", rc);
+  return h;
+}
+
+int64_t ipc_open_handle(Tensor h) {
+  TORCH_CHECK(h.numel() == 64 && h.scalar_type() == at::kByte && !h.is_cuda(), "64-byte CPU handle expected");
+  void* p = nullptr;
+  const int rc = b200_ipc_open_handle(h.contiguous().data_ptr(), &p);
+  TORCH_CHECK(rc == 0, "cudaIpcOpenMemHandle failed: ", rc);
+  return reinterpret_cast<int64_t>(p);
+}
+
+void ipc_close(int64_t p) { b200_ipc_close(reinterpret_cast<void*>(p)); }
+
+void allreduce_fused(at::IntArrayRef bases, int64_t rank, int64_t slot_bytes, Tensor input, Tensor out,
+                     c10::optional<Tensor> residual, c10::optional<Tensor> bias, c10::optional<Tensor> w, double eps,
+                     int64_t num_blocks, c10::optional<Tensor> status) {
+  TORCH_CHECK(input.is_cuda() && input.scalar_type() == at::kBFloat16 && input.is_contiguous(), "bf16 input");
+  TORCH_CHECK(out.is_contiguous() && out.scalar_type() == at::kBFloat16, "bf16 out");
+  TORCH_CHECK(bases.size() >= 1 && bases.size() <= 8, "1..8 ranks");
+  const int H = input.size(-1);
+  const int T = input.numel() / H;
+  void* ptrs[8];
+  for (size_t i = 0; i < bases.size(); ++i) ptrs[i] = reinterpret_cast<void*>(bases[i]);
+  if (w.has_value()) {
+    TORCH_CHECK(residual.has_value() && residual->is_contiguous() && residual->scalar_type() == at::kBFloat16,
+                "fused norm needs a bf16 residual");
+    TORCH_CHECK(w->scalar_type() == at::kFloat, "norm weight fp32");
+  }
+  c10::cuda::CUDAGuard g(input.device());
+  const int rc = b200_allreduce_fused(
+      ptrs, rank, bases.size(), (size_t)slot_bytes, input.data_ptr(), out.data_ptr(),
+      residual.has_value() ? residual->data_ptr() : nullptr, bias.has_value() ? bias->data_ptr() : nullptr,
+      w.has_value() ? w->data_ptr<float>() : nullptr, (float)eps, T, H, num_blocks,
+      status.has_value() ? status->data_ptr<int>() : nullptr, at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(rc == 0, "b200::allreduce_fused failed with code ", rc);
+}
+}  // namespace
+
+void register_comm_ops(torch::Library& m) {
+  m.def("comm_alloc(int slot_bytes) -> int");
+  m.def("comm_free(int ptr) -> ()");
+  m.def("ipc_get_handle(int ptr) -> Tensor");
+  m.def("ipc_open_handle(Tensor handle) -> int");
+  m.def("ipc_close(int ptr) -> ()");
+  m.def(
+      "allreduce_fused(int[] bases, int rank, int slot_bytes, Tensor input, Tensor(a!) out, Tensor(b!)? residual, "
+      "Tensor? bias, Tensor? w, float eps, int num_blocks, Tensor? status) -> ()");
+}
+
+void register_comm_impls(torch::Library& m) { m.impl("allreduce_fused", &allreduce_fused); }
+
+void register_comm_cpu_impls(torch::Library& m) {
+  m.impl("comm_alloc", &comm_alloc);
+  m.impl("comm_free", &comm_free);
+  m.impl("ipc_get_handle", &ipc_get_handle);
+  m.impl("ipc_open_handle", &ipc_open_handle);
+  m.impl("ipc_close", &ipc_close);
+}

@@ -150,7 +150,9 @@ class GptOssAttention(nn.Module):
                                self.d, self.k_scale, self.v_scale)
         o = ops.attention(q, k_cache, v_cache, meta, self.scale, self.sinks, self.window, self.k_scale,
                           self.v_scale)
-        return self.o_proj(o.reshape(o.shape[0], self.nq * self.d))
+        # partial output projection of this rank's heads; the all-reduce, bias, residual add
+        # and the next RMSNorm happen in one fused step in the decoder layer
+        return ops.linear(o.reshape(o.shape[0], self.nq * self.d), self.o_proj.weight, None)
 
 
 class GptOssExperts(nn.Module):
@@ -203,14 +205,21 @@ class GptOssMLP(nn.Module):
         self.experts = GptOssExperts(cfg, moe_group.rank_in_group, moe_group.world_size, dtype, device)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        """This rank's partial MoE output (its experts only); the caller reduces it."""
         ids, w = ops.router_topk(x, self.router_weight, self.router_bias, self.cfg.num_experts_per_tok)
-        y = self.experts(x, ids, w)
-        return self.group.all_reduce(y)
+        return self.experts(x, ids, w)
 
 
 class GptOssDecoderLayer(nn.Module):
+    """Input: the previous layer's MoE partial sum (or the embedding for layer 0).  Each
+    layer boundary is one ``all_reduce_add_rmsnorm``: reduce the partial sums across the
+    group, add bias and residual, normalise."""
+
     def __init__(self, cfg: GptOssConfig, i: int, ps: ParallelState, dtype, device):
         super().__init__()
+        self.eps = cfg.rms_norm_eps
+        self.tp = ps.tp
+        self.moe_group = ps.tp
         self.input_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, device=device)
         self.self_attn = GptOssAttention(cfg, i, ps.tp, dtype, device)
         self.post_attention_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, device=device)
@@ -221,9 +230,10 @@ class GptOssDecoderLayer(nn.Module):
             residual = h
             x = self.input_layernorm(h)
         else:
-            x, residual = self.input_layernorm(h, residual)
-        x = self.self_attn(positions, x, meta, kv, cos_sin)
-        x, residual = self.post_attention_layernorm(x, residual)
+            x, residual = self.moe_group.all_reduce_add_rmsnorm(h, residual, self.input_layernorm.weight, self.eps)
+        a = self.self_attn(positions, x, meta, kv, cos_sin)
+        x, residual = self.tp.all_reduce_add_rmsnorm(a, residual, self.post_attention_layernorm.weight, self.eps,
+                                                     self.self_attn.o_proj.bias)
         return self.mlp(x), residual
 
 
@@ -270,7 +280,7 @@ class GptOssForCausalLM(nn.Module):
             if i in self.aux_hidden_layers:
                 aux.append(h if residual is None else h + residual)
             h, residual = layer(positions, h, residual, meta, kv_caches[i], self.cos_sin)
-        h, _ = self.norm(h, residual)
+        h, _ = self.ps.tp.all_reduce_add_rmsnorm(h, residual, self.norm.weight, self.cfg.rms_norm_eps)
         if self.aux_hidden_layers:
             self._aux = torch.cat(aux, dim=-1)
         return h

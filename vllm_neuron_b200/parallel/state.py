@@ -158,6 +158,21 @@ class GroupCoordinator:
         dist.all_reduce(x, group=self.device_group)
         return x
 
+    def all_reduce_add_rmsnorm(self, x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float,
+                               bias: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """(RMSNorm(sum_ranks(x) + bias + residual) * w, sum + bias + residual).  One fused
+        NVLink kernel when a communicator can take ``x``; otherwise all-reduce then the
+        fused add+norm op."""
+        from .. import ops
+
+        if self.world_size > 1 and self.communicator is not None and self.communicator.can_all_reduce(x):
+            return self.communicator.all_reduce_add_rmsnorm(x, residual, w, eps, bias)
+        if self.world_size > 1:
+            x = self.all_reduce(x)
+        if bias is not None:
+            x = x + bias
+        return ops.fused_add_rms_norm(x, residual, w, eps)
+
     def all_gather(self, x: torch.Tensor, dim: int = 0) -> torch.Tensor:
         if self.world_size == 1:
             return x
