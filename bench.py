@@ -239,8 +239,15 @@ def main() -> None:
             "clocks": clk,
         }
         print(json.dumps(line))
+    # Graphs that captured NCCL calls must be freed before the process group is destroyed,
+    # including the local reference taken above; then leave without interpreter teardown.
+    del graph
     runner.release_graphs()
+    torch.cuda.synchronize()
+    sys.stdout.flush()
     llm.shutdown()
+    sys.stdout.flush()
+    os._exit(0)
 
 
 if __name__ == "__main__":
