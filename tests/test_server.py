@@ -1,0 +1,55 @@
+"""OpenAI-compatible server on the tiny GPT-OSS model (CPU): completions (plain and
+streamed, token-id prompts), models, health, metrics; plus the CLI argument mapping."""
+
+import json
+
+import pytest
+
+from tiny_configs import TINY_GPT_OSS
+
+
+@pytest.fixture(scope="module")
+def client():
+    from fastapi.testclient import TestClient
+
+    from vllm_neuron_b200.engine.async_engine import AsyncLLM
+    from vllm_neuron_b200.entrypoints.openai_server import build_app
+
+    eng = AsyncLLM(hf_config=dict(TINY_GPT_OSS), load_format="dummy", dtype="float32", max_model_len=256,
+                   max_num_seqs=4, max_num_batched_tokens=128, block_size=16, device="cpu",
+                   additional_config={"neuron_config": {"quantization": "bf16"}})
+    with TestClient(build_app(eng, "tiny")) as c:
+        yield c
+    eng.shutdown()
+
+
+def test_health_models_metrics(client):
+    assert client.get("/health").json()["status"] == "ok"
+    assert client.get("/v1/models").json()["data"][0]["id"] == "tiny"
+    assert client.get("/metrics").status_code == 200
+
+
+def test_completion_and_stream_agree(client):
+    body = {"prompt": [5, 6, 7, 8, 9], "max_tokens": 6, "temperature": 0, "ignore_eos": True}
+    r = client.post("/v1/completions", json=body).json()
+    toks = r["choices"][0]["token_ids"]
+    assert len(toks) == 6 and r["usage"]["completion_tokens"] == 6
+    streamed = []
+    with client.stream("POST", "/v1/completions", json=dict(body, stream=True)) as resp:
+        for line in resp.iter_lines():
+            if line.startswith("data:") and not line.endswith("[DONE]"):
+                streamed += json.loads(line[5:])["choices"][0]["token_ids"]
+    assert streamed == toks
+
+
+def test_cli_engine_kwargs():
+    import argparse
+
+    from vllm_neuron_b200.entrypoints import cli
+
+    ap = argparse.ArgumentParser()
+    cli._engine_args(ap)
+    a = ap.parse_args(["/m", "-tp", "8", "--max-num-seqs", "64",
+                       "--additional-config", '{"neuron_config": {"ep_degree": 8}}'])
+    kw = cli.engine_kwargs(a)
+    assert kw["tensor_parallel_size"] == 8 and kw["additional_config"]["neuron_config"]["ep_degree"] == 8

@@ -1,0 +1,101 @@
+"""Asynchronous engine front-end for online serving.
+
+A background thread owns the :class:`LLMEngine` and loops ``step()`` while requests are
+in flight; API handlers submit requests through a thread-safe queue and receive
+per-request outputs on asyncio queues.  This is the role vLLM's AsyncLLM / EngineCore
+play for the Trainium plugin, collapsed into one process since the
+scheduler is deterministic and SPMD across ranks.
+"""
+
+from __future__ import annotations
+
+import asyncio
+import queue
+import threading
+import uuid
+from typing import AsyncIterator
+
+from ..logging_config import init_logger
+from .llm import LLM
+from .sampling_params import RequestOutput, SamplingParams
+
+logger = init_logger(__name__)
+
+
+class AsyncLLM:
+    def __init__(self, **engine_kwargs):
+        self.llm = LLM(**engine_kwargs)
+        self.engine = self.llm.engine
+        self._in: queue.Queue = queue.Queue()
+        self._streams: dict[str, tuple[asyncio.AbstractEventLoop, asyncio.Queue]] = {}
+        self._lock = threading.Lock()
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._loop, name="b200-engine", daemon=True)
+        self._thread.start()
+        self.profiling = False
+
+    def _loop(self) -> None:
+        while not self._stop.is_set():
+            try:
+                while True:
+                    kind, payload = self._in.get_nowait()
+                    if kind == "add":
+                        rid, ids, sp, mm = payload
+                        self.engine.add_request(rid, ids, sp, mm_inputs=mm)
+                    elif kind == "abort":
+                        self.engine.abort_request(payload)
+            except queue.Empty:
+                pass
+            if not self.engine.has_unfinished_requests():
+                try:
+                    kind, payload = self._in.get(timeout=0.05)
+                    self._in.put((kind, payload))
+                except queue.Empty:
+                    pass
+                continue
+            try:
+                outs = self.engine.step()
+            except Exception as e:  # noqa: BLE001
+                logger.exception("engine step failed")
+                with self._lock:
+                    for rid, (loop, q) in list(self._streams.items()):
+                        loop.call_soon_threadsafe(q.put_nowait, e)
+                    self._streams.clear()
+                continue
+            for o in outs:
+                with self._lock:
+                    ent = self._streams.get(o.request_id)
+                if ent is not None:
+                    loop, q = ent
+                    loop.call_soon_threadsafe(q.put_nowait, o)
+                    if o.finished:
+                        with self._lock:
+                            self._streams.pop(o.request_id, None)
+
+    async def generate(self, prompt_token_ids: list[int], sampling_params: SamplingParams,
+                       request_id: str | None = None, mm_inputs: list | None = None) -> AsyncIterator[RequestOutput]:
+        rid = request_id or uuid.uuid4().hex
+        loop = asyncio.get_running_loop()
+        q: asyncio.Queue = asyncio.Queue()
+        with self._lock:
+            self._streams[rid] = (loop, q)
+        self._in.put(("add", (rid, list(prompt_token_ids), sampling_params, mm_inputs)))
+        try:
+            while True:
+                item = await q.get()
+                if isinstance(item, Exception):
+                    raise item
+                yield item
+                if item.finished:
+                    return
+        except asyncio.CancelledError:
+            self._in.put(("abort", rid))
+            raise
+
+    def abort(self, request_id: str) -> None:
+        self._in.put(("abort", request_id))
+
+    def shutdown(self) -> None:
+        self._stop.set()
+        self._thread.join(timeout=10)
+        self.llm.shutdown()

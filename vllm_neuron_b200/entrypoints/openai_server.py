@@ -1,0 +1,154 @@
+"""OpenAI-compatible HTTP server (``/v1/completions``, ``/v1/chat/completions``,
+``/v1/models``, ``/health``, ``/metrics``, ``/start_profile``, ``/stop_profile``).
+
+Request and response bodies follow the OpenAI / vLLM schema for the supported fields.
+Prompts may be text (needs a tokenizer in the model directory) or token-id lists.
+Profiling endpoints map to ``torch.profiler`` with CUDA activities (the Trainium
+plugin mapped them to its device profiler, ``vllm/worker/neuron_profiler.py:52``).
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import time
+import uuid
+
+from fastapi import FastAPI, Request
+from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
+
+from ..engine.async_engine import AsyncLLM
+from ..engine.sampling_params import SamplingParams
+from ..logging_config import init_logger
+
+logger = init_logger(__name__)
+
+
+def _sampling_from(body: dict) -> SamplingParams:
+    return SamplingParams(
+        temperature=float(body.get("temperature", 1.0)), top_p=float(body.get("top_p", 1.0)),
+        top_k=int(body.get("top_k", 0) or 0), max_tokens=int(body.get("max_tokens", 16) or 16),
+        min_tokens=int(body.get("min_tokens", 0) or 0), seed=body.get("seed"),
+        stop_token_ids=body.get("stop_token_ids"), ignore_eos=bool(body.get("ignore_eos", False)))
+
+
+def build_app(engine: AsyncLLM, served_name: str):
+    app = FastAPI(title="vllm_neuron_b200")
+    state = {"prof": None}
+
+    def tokenize(prompt):
+        if isinstance(prompt, list) and prompt and isinstance(prompt[0], int):
+            return prompt, None
+        tok = engine.llm.get_tokenizer()
+        return tok.encode(prompt), prompt
+
+    def detok(ids):
+        try:
+            return engine.llm.get_tokenizer().decode(ids)
+        except Exception:  # noqa: BLE001
+            return ""
+
+    @app.get("/health")
+    async def health():
+        return {"status": "ok"}
+
+    @app.get("/v1/models")
+    async def models():
+        return {"object": "list", "data": [{"id": served_name, "object": "model", "owned_by": "vllm_neuron_b200"}]}
+
+    @app.get("/metrics")
+    async def metrics():
+        from prometheus_client import CONTENT_TYPE_LATEST, generate_latest
+
+        return PlainTextResponse(generate_latest(), media_type=CONTENT_TYPE_LATEST)
+
+    @app.post("/start_profile")
+    async def start_profile():
+        import torch
+
+        prof = torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CPU,
+                                                  torch.profiler.ProfilerActivity.CUDA])
+        prof.__enter__()
+        state["prof"] = prof
+        return {"status": "started"}
+
+    @app.post("/stop_profile")
+    async def stop_profile():
+        prof = state.get("prof")
+        if prof is None:
+            return JSONResponse({"error": "profiler not running"}, status_code=400)
+        prof.__exit__(None, None, None)
+        out = os.environ.get("VLLM_B200_PROFILE_DIR", "/tmp/vllm_b200_profile")
+        os.makedirs(out, exist_ok=True)
+        path = os.path.join(out, f"trace_{int(time.time())}.json")
+        prof.export_chrome_trace(path)
+        state["prof"] = None
+        return {"status": "stopped", "trace": path}
+
+    async def _complete(ids, sp, stream: bool, chat: bool, rid: str):
+        created = int(time.time())
+        obj = "chat.completion" if chat else "text_completion"
+
+        def choice(text, token_ids, finish):
+            if chat:
+                return {"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": finish,
+                        "token_ids": token_ids}
+            return {"index": 0, "text": text, "finish_reason": finish, "token_ids": token_ids}
+
+        if stream:
+            async def gen():
+                sent = 0
+                async for o in engine.generate(ids, sp, rid):
+                    toks = o.outputs[0].token_ids
+                    new = toks[sent:]
+                    sent = len(toks)
+                    delta = detok(new)
+                    ch = ({"index": 0, "delta": {"content": delta}, "finish_reason": o.outputs[0].finish_reason}
+                          if chat else {"index": 0, "text": delta, "finish_reason": o.outputs[0].finish_reason})
+                    ch["token_ids"] = new
+                    yield "data: " + json.dumps({"id": rid, "object": obj + ".chunk", "created": created,
+                                                 "model": served_name, "choices": [ch]}) + "\n\n"
+                yield "data: [DONE]\n\n"
+
+            return StreamingResponse(gen(), media_type="text/event-stream")
+        final = None
+        async for o in engine.generate(ids, sp, rid):
+            final = o
+        toks = final.outputs[0].token_ids
+        return {"id": rid, "object": obj, "created": created, "model": served_name,
+                "choices": [choice(detok(toks), toks, final.outputs[0].finish_reason)],
+                "usage": {"prompt_tokens": len(ids), "completion_tokens": len(toks),
+                          "total_tokens": len(ids) + len(toks)}}
+
+    @app.post("/v1/completions")
+    async def completions(req: Request):
+        body = await req.json()
+        ids, _ = tokenize(body["prompt"])
+        return await _complete(ids, _sampling_from(body), bool(body.get("stream", False)), False,
+                               f"cmpl-{uuid.uuid4().hex}")
+
+    @app.post("/v1/chat/completions")
+    async def chat(req: Request):
+        body = await req.json()
+        msgs = body["messages"]
+        tok = engine.llm.get_tokenizer()
+        if getattr(tok, "chat_template", None):
+            ids = tok.apply_chat_template(msgs, add_generation_prompt=True, tokenize=True)
+        else:
+            ids = tok.encode("\n".join(f"{m['role']}: {m['content']}" for m in msgs) + "\nassistant:")
+        return await _complete(list(ids), _sampling_from(body), bool(body.get("stream", False)), True,
+                               f"chatcmpl-{uuid.uuid4().hex}")
+
+    return app
+
+
+def serve(engine_kwargs: dict, host: str = "127.0.0.1", port: int = 8000, served_name: str | None = None) -> None:
+    import uvicorn
+
+    engine = AsyncLLM(**engine_kwargs)
+    name = served_name or str(engine_kwargs.get("model") or "model")
+    app = build_app(engine, name)
+    try:
+        uvicorn.run(app, host=host, port=port, log_level="warning")
+    finally:
+        engine.shutdown()
