@@ -1,0 +1,73 @@
+"""Llama (dense) and Qwen3 text decoders: greedy tokens vs HF transformers fp32 (CPU),
+TP=1 and TP=2 over gloo."""
+
+import pytest
+import torch
+
+from tiny_configs import workload
+
+
+def _save(model, cfg_dict, path):
+    from vllm_neuron_b200.utils.checkpoints import save_state_dict
+
+    save_state_dict({k: v.detach().clone().contiguous() for k, v in model.state_dict().items()}, str(path), cfg_dict)
+
+
+def _hf_llama():
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    torch.manual_seed(0)
+    cfg = LlamaConfig(vocab_size=2048, hidden_size=128, intermediate_size=256, num_hidden_layers=3,
+                      num_attention_heads=8, num_key_value_heads=2, max_position_embeddings=1024,
+                      rope_theta=500000.0, tie_word_embeddings=False,
+                      rope_scaling={"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
+                                    "high_freq_factor": 4.0, "original_max_position_embeddings": 256})
+    cfg._attn_implementation = "eager"
+    return LlamaForCausalLM(cfg).eval().float(), cfg
+
+
+def _hf_qwen3():
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+
+    torch.manual_seed(0)
+    cfg = Qwen3Config(vocab_size=2048, hidden_size=128, intermediate_size=256, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=2, head_dim=32, max_position_embeddings=1024,
+                      rope_theta=1000000.0, tie_word_embeddings=True)
+    cfg._attn_implementation = "eager"
+    m = Qwen3ForCausalLM(cfg).eval().float()
+    with torch.no_grad():
+        for n, p in m.named_parameters():
+            if "norm" in n:
+                p.copy_(1 + 0.1 * torch.randn_like(p))
+    return m, cfg
+
+
+@pytest.fixture(scope="module", params=["llama", "qwen3"])
+def ckpt(request, tmp_path_factory):
+    m, cfg = _hf_llama() if request.param == "llama" else _hf_qwen3()
+    d = cfg.to_dict()
+    d["architectures"] = ["LlamaForCausalLM"]
+    path = tmp_path_factory.mktemp(request.param)
+    _save(m, d, path)
+    return str(path), m
+
+
+@pytest.mark.parametrize("tp", [1, 2])
+def test_dense_greedy_matches_hf(ckpt, tp):
+    from vllm_neuron_b200 import LLM, SamplingParams
+
+    path, hf = ckpt
+    prompts = workload(n=3, lo=20, hi=60, vocab=2048, seed=5)
+    want = []
+    with torch.no_grad():
+        for p in prompts:
+            g = hf.generate(torch.tensor([p]), max_new_tokens=10, do_sample=False, pad_token_id=0, eos_token_id=None)
+            want.append(g[0, len(p):].tolist())
+    llm = LLM(model=path, dtype="float32", max_model_len=256, max_num_seqs=4, max_num_batched_tokens=128,
+              block_size=16, device="cpu", tensor_parallel_size=tp)
+    try:
+        outs = llm.generate(prompt_token_ids=prompts,
+                            sampling_params=SamplingParams(temperature=0, max_tokens=10, ignore_eos=True))
+    finally:
+        llm.shutdown()
+    assert [o.outputs[0].token_ids for o in outs] == want

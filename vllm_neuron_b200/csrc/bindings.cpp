@@ -60,6 +60,14 @@ void fused_add_rms_norm(Tensor out, Tensor x, Tensor residual, Tensor w, double 
            "fused_add_rms_norm");
 }
 
+void silu_and_mul(Tensor out, Tensor gu) {
+  check_cuda(gu, "gu");
+  TORCH_CHECK(gu.is_contiguous() && out.is_contiguous() && gu.scalar_type() == at::kBFloat16, "bf16 contiguous");
+  const int I = gu.size(-1) / 2;
+  c10::cuda::CUDAGuard g(gu.device());
+  check_rc(b200_silu_and_mul(out.data_ptr(), gu.data_ptr(), gu.numel() / gu.size(-1), I, stream()), "silu_and_mul");
+}
+
 void embedding(Tensor out, Tensor ids, Tensor w, int64_t start) {
   check_cuda(w, "w");
   TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous(), "ids must be contiguous int64");
@@ -196,6 +204,7 @@ TORCH_LIBRARY(b200, m) {
   m.def("rms_norm(Tensor(a!) out, Tensor x, Tensor w, float eps) -> ()");
   m.def("fused_add_rms_norm(Tensor(a!) out, Tensor x, Tensor(b!) residual, Tensor w, float eps) -> ()");
   m.def("embedding(Tensor(a!) out, Tensor ids, Tensor w, int start) -> ()");
+  m.def("silu_and_mul(Tensor(a!) out, Tensor gu) -> ()");
   m.def(
       "rope_kv_write(Tensor(a!) qkv, Tensor positions, Tensor cos_sin, Tensor(b!) k_cache, Tensor(c!) v_cache, "
       "Tensor slots, int nq, int nkv, int d, int rotary_dim, float k_scale, float v_scale, Tensor? q_norm, "
@@ -227,6 +236,7 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("rms_norm", &rms_norm);
   m.impl("fused_add_rms_norm", &fused_add_rms_norm);
   m.impl("embedding", &embedding);
+  m.impl("silu_and_mul", &silu_and_mul);
   m.impl("rope_kv_write", &rope_kv_write);
   m.impl("paged_attention_decode", &paged_attention_decode);
   m.impl("paged_attention_prefill", &paged_attention_prefill);

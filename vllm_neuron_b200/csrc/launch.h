@@ -17,6 +17,8 @@ extern "C" {
 int b200_rms_norm(void* out, const void* x, void* residual, const float* w, int rows, int H, float eps, int dtype,
                   cudaStream_t s);
 
+int b200_silu_and_mul(void* out, const void* gu, int T, int I, cudaStream_t s);
+
 int b200_embedding(void* out, const int64_t* ids, const void* table, int T, int rows, int H, int64_t vocab_start,
                    int dtype, cudaStream_t s);
 

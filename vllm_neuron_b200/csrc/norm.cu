@@ -138,3 +138,40 @@ extern "C" int b200_rms_norm(void* out, const void* x, void* residual, const flo
   }
   return (int)cudaGetLastError();
 }
+
+// silu(gate) * up for [T, 2I] (gate | up halves), bf16, 16-byte vectors when I % 8 == 0.
+namespace b200 {
+__global__ void silu_and_mul_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ gu, int I) {
+  const int t = blockIdx.x;
+  const __nv_bfloat16* g = gu + (size_t)t * 2 * I;
+  const __nv_bfloat16* u = g + I;
+  __nv_bfloat16* o = out + (size_t)t * I;
+  if (I % 8 == 0) {
+    for (int c = threadIdx.x; c < I / 8; c += blockDim.x) {
+      const uint4 gv = reinterpret_cast<const uint4*>(g)[c];
+      const uint4 uv = reinterpret_cast<const uint4*>(u)[c];
+      const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(&gv);
+      const __nv_bfloat16* ub = reinterpret_cast<const __nv_bfloat16*>(&uv);
+      uint4 ov;
+      __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&ov);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float x = __bfloat162float(gb[q]);
+        ob[q] = __float2bfloat16(x / (1.f + __expf(-x)) * __bfloat162float(ub[q]));
+      }
+      reinterpret_cast<uint4*>(o)[c] = ov;
+    }
+  } else {
+    for (int i = threadIdx.x; i < I; i += blockDim.x) {
+      const float x = __bfloat162float(g[i]);
+      o[i] = __float2bfloat16(x / (1.f + __expf(-x)) * __bfloat162float(u[i]));
+    }
+  }
+}
+}  // namespace b200
+
+extern "C" int b200_silu_and_mul(void* out, const void* gu, int T, int I, cudaStream_t s) {
+  if (T == 0) return 0;
+  b200::silu_and_mul_kernel<<<T, 256, 0, s>>>((__nv_bfloat16*)out, (const __nv_bfloat16*)gu, I);
+  return (int)cudaGetLastError();
+}

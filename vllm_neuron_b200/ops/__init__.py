@@ -60,6 +60,32 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None) -> t
     return F.linear(x, w, b)
 
 
+def linear_fp8(x: torch.Tensor, w_fp8: torch.Tensor, w_scale: torch.Tensor, in_scale: torch.Tensor | None,
+               b: torch.Tensor | None = None) -> torch.Tensor:
+    """Static per-tensor FP8 linear (ModelOpt checkpoints, ``model/llama3/quantization.py:176``):
+    y = (q(x / s_in) @ W_fp8^T) * s_in * s_w, q = e4m3 with saturation.  Dynamic per-tensor
+    activation scale when ``in_scale`` is None."""
+    xs = in_scale if in_scale is not None else (x.abs().amax().float().clamp_min(1e-12) / 448.0).reshape(1)
+    xq = (x.float() / xs).clamp(-448, 448).to(torch.float8_e4m3fn)
+    if x.is_cuda and hasattr(torch, "_scaled_mm"):
+        y = torch._scaled_mm(xq, w_fp8.t(), scale_a=xs.float().reshape(()), scale_b=w_scale.float().reshape(()),
+                             out_dtype=torch.bfloat16)
+    else:
+        y = (xq.float() @ w_fp8.float().t()) * (xs.float() * w_scale.float())
+    y = y.to(x.dtype)
+    return y + b if b is not None else y
+
+
+def silu_and_mul(gu: torch.Tensor) -> torch.Tensor:
+    """[T, 2I] (gate | up) -> silu(gate) * up."""
+    if use_kernel(gu) and gu.dtype == torch.bfloat16:
+        out = torch.empty(gu.shape[0], gu.shape[1] // 2, dtype=gu.dtype, device=gu.device)
+        _k().silu_and_mul(out, gu)
+        return out
+    I = gu.shape[-1] // 2
+    return (F.silu(gu[..., :I].float()) * gu[..., I:].float()).to(gu.dtype)
+
+
 def embedding(ids: torch.Tensor, w: torch.Tensor, vocab_start: int = 0) -> torch.Tensor:
     """Rows of ``w`` for ids in ``[vocab_start, vocab_start + rows)``, zero elsewhere."""
     if use_kernel(w):

@@ -23,7 +23,7 @@ from .moe import (  # noqa: F401
 )
 from .mxfp4 import FP4_VALUES, dequant_mxfp4, quantize_mxfp4, quantize_mxfp8, dequant_mxfp8  # noqa: F401
 from .norm import rms_norm, fused_add_rms_norm, rmsnorm_quant_fp8  # noqa: F401
-from .rope import apply_rope, rope_cos_sin, yarn_inv_freq, mrope_cos_sin  # noqa: F401
+from .rope import apply_rope, llama3_inv_freq, mrope_cos_sin, rope_cos_sin, yarn_inv_freq  # noqa: F401
 from .sampling import (  # noqa: F401
     sample,
     greedy,

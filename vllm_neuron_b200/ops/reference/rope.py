@@ -42,6 +42,21 @@ def yarn_inv_freq(head_dim: int, theta: float, factor: float = 1.0, original_max
     return inv.float(), attn_factor
 
 
+def llama3_inv_freq(head_dim: int, theta: float, factor: float, low_freq_factor: float, high_freq_factor: float,
+                    original_max_pos: int) -> torch.Tensor:
+    """Llama 3.x frequency scaling: long wavelengths divided by ``factor``, short ones kept,
+    a smooth interpolation in between (Meta's published Llama 3.1 RoPE recipe)."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+    low_wl = original_max_pos / low_freq_factor
+    high_wl = original_max_pos / high_freq_factor
+    wl = 2 * math.pi / inv
+    scaled = torch.where(wl > low_wl, inv / factor, inv)
+    smooth = (original_max_pos / wl - low_freq_factor) / (high_freq_factor - low_freq_factor)
+    mid = (1 - smooth) * scaled / factor + smooth * scaled
+    is_mid = (wl >= high_wl) & (wl <= low_wl)
+    return torch.where(is_mid, mid, scaled).float()
+
+
 def rope_cos_sin(positions: torch.Tensor, inv_freq: torch.Tensor, attn_factor: float = 1.0,
                  dtype: torch.dtype = torch.float32) -> tuple[torch.Tensor, torch.Tensor]:
     """cos/sin of shape [T, head_dim/2] (half layout)."""
