@@ -41,6 +41,13 @@ class LLMEngine:
         self.worker.load_model()
         n_blocks = self.worker.determine_num_blocks()
         self.worker.initialize_cache(n_blocks)
+        self.proposer = None
+        if cfg.speculative_config is not None:
+            from ..spec_decode.eagle import EagleProposer
+
+            # verification steps carry k+1 tokens per request and run eagerly
+            self.worker.runner.use_graphs = False
+            self.proposer = EagleProposer(cfg, self.worker)
         self.worker.warmup()
         self.num_blocks = n_blocks
         self.kv = KVCacheManager(n_blocks, cfg.block_size, cfg.enable_prefix_caching)
@@ -51,11 +58,6 @@ class LLMEngine:
         self.eos_token_id = hf.get("eos_token_id")
         self._pending: list[tuple] = []
         self._stopped = False
-        self.proposer = None
-        if cfg.speculative_config is not None:
-            from ..spec_decode.eagle import EagleProposer
-
-            self.proposer = EagleProposer(cfg, self.worker)
         logger.info("engine ready: rank %d/%d mode=%s kv_blocks=%d", rank, world_size, mode, n_blocks)
 
     # ------------------------------------------------------------------ intake

@@ -277,13 +277,17 @@ class GptOssForCausalLM(nn.Module):
         residual = None
         aux = []
         for i, layer in enumerate(self.layers):
-            if i in self.aux_hidden_layers:
-                aux.append(h if residual is None else h + residual)
+            if i in self.aux_hidden_layers:  # hidden state entering layer i (reduced partial + residual)
+                aux.append(h if residual is None else self.ps.tp.all_reduce(h.clone()) + residual)
             h, residual = layer(positions, h, residual, meta, kv_caches[i], self.cos_sin)
         h, _ = self.ps.tp.all_reduce_add_rmsnorm(h, residual, self.norm.weight, self.cfg.rms_norm_eps)
-        if self.aux_hidden_layers:
-            self._aux = torch.cat(aux, dim=-1)
+        self._aux = torch.cat(aux, dim=-1) if aux else None
         return h
+
+    def get_eagle3_aux_hidden_state_layers(self) -> tuple[int, ...]:
+        """Low / middle / high layers feeding an EAGLE-3 draft (``model_mxfp4.py:2033-2037``)."""
+        n = self.cfg.num_hidden_layers
+        return (2, n // 2, n - 3) if n >= 8 else (0, n // 2, n - 1)
 
     def compute_logits(self, h: torch.Tensor) -> torch.Tensor:
         return self.lm_head(h)

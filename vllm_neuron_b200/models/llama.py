@@ -238,7 +238,7 @@ class LlamaForCausalLM(nn.Module):
     def get_eagle3_aux_hidden_state_layers(self) -> tuple[int, ...]:
         """Low / middle / high layers whose inputs feed an EAGLE-3 draft model."""
         n = self.cfg.num_hidden_layers
-        return (2, n // 2, n - 3)
+        return (2, n // 2, n - 3) if n >= 8 else (0, n // 2, n - 1)
 
     def forward(self, input_ids, positions, meta, kv_caches, inputs_embeds=None):
         h = self.embed_tokens(input_ids) if inputs_embeds is None else inputs_embeds
