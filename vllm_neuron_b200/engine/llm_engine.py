@@ -54,6 +54,8 @@ class LLMEngine:
         k = cfg.speculative_config.num_speculative_tokens if cfg.speculative_config else 0
         self.scheduler = Scheduler(self.kv, cfg.max_num_seqs, cfg.max_num_batched_tokens, cfg.max_model_len,
                                    cfg.max_num_prefills_per_step, cfg.enable_chunked_prefill, k)
+        if self.worker.runner.encoder_cache is not None:
+            self.scheduler.on_finish.append(self.worker.runner.encoder_cache.release)
         hf = self.worker.hf
         self.eos_token_id = hf.get("eos_token_id")
         self._pending: list[tuple] = []
@@ -65,13 +67,57 @@ class LLMEngine:
                     prompt: str | None = None, mm_inputs: list | None = None,
                     kv_transfer_params: dict | None = None) -> str:
         rid = request_id or uuid.uuid4().hex
-        req = Request(rid, list(map(int, prompt_token_ids)), sampling_params, self.eos_token_id, prompt,
-                      mm_inputs=mm_inputs, kv_transfer_params=kv_transfer_params)
+        req = self._make_request(rid, prompt_token_ids, sampling_params, prompt, mm_inputs, kv_transfer_params)
         if self.mode == "driver":
             self._pending.append(("add", rid, req.prompt_token_ids, sampling_params, prompt, mm_inputs,
                                   kv_transfer_params))
         self.scheduler.add_request(req)
         return rid
+
+    def _make_request(self, rid, prompt_token_ids, sampling_params, prompt, mm_inputs, kv_transfer_params) -> Request:
+        ids = list(map(int, prompt_token_ids))
+        req = Request(rid, ids, sampling_params, self.eos_token_id, prompt, mm_inputs=mm_inputs,
+                      kv_transfer_params=kv_transfer_params)
+        model = self.worker.model
+        if mm_inputs and hasattr(model, "embed_multimodal"):
+            from ..models.qwen3_vl import preprocess_image
+
+            images = []
+            for item in mm_inputs:
+                img = item.get("image") if isinstance(item, dict) else item
+                if img is None:
+                    continue
+                images += list(img) if isinstance(img, (list, tuple)) else [img]
+            img_tok = model.vl_cfg.image_token_id
+            grids = [preprocess_image(torch_image(im), model.vl_cfg.vision)[1] for im in images]
+            counts = [model.num_image_tokens(g) for g in grids]
+            n_ph = sum(1 for t in ids if t == img_tok)
+            out, items, gi, i = [], [], 0, 0
+            if n_ph == len(grids):  # one placeholder per image: expand each to its token count
+                for t in ids:
+                    if t == img_tok:
+                        items.append({"pixels": torch_image(images[gi]), "grid": grids[gi], "offset": len(out),
+                                      "n": counts[gi]})
+                        out += [img_tok] * counts[gi]
+                        gi += 1
+                    else:
+                        out.append(t)
+            elif n_ph == sum(counts):  # already expanded: record where each image starts
+                out = list(ids)
+                while i < len(out):
+                    if out[i] == img_tok:
+                        items.append({"pixels": torch_image(images[gi]), "grid": grids[gi], "offset": i,
+                                      "n": counts[gi]})
+                        i += counts[gi]
+                        gi += 1
+                    else:
+                        i += 1
+            else:
+                raise ValueError(f"prompt has {n_ph} image tokens for {len(grids)} images ({sum(counts)} tokens)")
+            req.prompt_token_ids = out
+            req.mm_items = items
+            req.mrope_positions, req.mrope_delta = model.mrope_positions(out, grids)
+        return req
 
     def abort_request(self, request_id: str) -> None:
         if self.mode == "driver":
@@ -91,8 +137,7 @@ class LLMEngine:
             for m in msgs:
                 if m[0] == "add":
                     _, rid, ids, sp, prompt, mm, kvp = m
-                    self.scheduler.add_request(Request(rid, ids, sp, self.eos_token_id, prompt, mm_inputs=mm,
-                                                       kv_transfer_params=kvp))
+                    self.scheduler.add_request(self._make_request(rid, ids, sp, prompt, mm, kvp))
                 elif m[0] == "abort":
                     self.scheduler.abort(m[1])
                 elif m[0] == "shutdown":
@@ -151,6 +196,23 @@ class LLMEngine:
                 "running": len(self.scheduler.running), "waiting": len(self.scheduler.waiting),
                 "h2d_bytes_last": self.worker.runner.h2d_bytes_last,
                 "d2h_bytes_last": self.worker.runner.d2h_bytes_last}
+
+
+def torch_image(x):
+    """Accept a CHW tensor / HWC numpy array / PIL image; return a CHW float tensor."""
+    import numpy as np
+    import torch
+
+    if isinstance(x, torch.Tensor):
+        t = x.float()
+    else:
+        arr = np.asarray(x)
+        t = torch.from_numpy(arr.copy()).float()
+        if t.dim() == 3 and t.shape[-1] in (1, 3, 4):
+            t = t.permute(2, 0, 1)
+    if t.dim() == 3 and t.shape[0] == 4:
+        t = t[:3]
+    return t
 
 
 def _follower_main(cfg: EngineConfig, rank: int, world_size: int, master_port: int) -> None:

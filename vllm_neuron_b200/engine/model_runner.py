@@ -107,6 +107,16 @@ class ModelRunner:
         self.d_unif = torch.zeros(B, dtype=torch.float32, device=d)
         self.d_out = torch.zeros(B * (1 + self._num_spec()), dtype=torch.int64, device=d)
         self.workspace: torch.Tensor | None = None
+        self.encoder_cache = None
+        if hasattr(model, "embed_multimodal"):
+            from .encoder_cache import EncoderCache
+
+            vc = model.vl_cfg.vision
+            nd = len(vc.deepstack_visual_indexes)
+            ecfg = cfg.vision_neuron_config
+            nblk = ecfg.encoder_cache_num_blocks or min(64, max(4, cfg.max_num_seqs))
+            blk_tok = ecfg.max_vision_seq_len or 4096
+            self.encoder_cache = EncoderCache(nblk, blk_tok, model.cfg.hidden_size * (1 + nd), model.dtype, device)
         self.h2d_bytes_last = 0
         self.d2h_bytes_last = 0
         self.step_count = 0
@@ -188,11 +198,17 @@ class ModelRunner:
         qsl[0] = 0
         max_q, max_s = 1, 1
         n_sel = 0
+        mm_rows: list = []
+        has_mrope = False
         for i, s in enumerate(seqs):
             k = len(s.token_ids)
             ids[t:t + k] = s.token_ids
             p = np.arange(s.start_pos, s.start_pos + k)
-            pos[t:t + k] = p
+            req = s.request
+            delta = req.mrope_delta if req is not None else 0
+            pos[t:t + k] = p + delta if (delta and so.kind == "decode") else p
+            if req is not None and req.mrope_positions is not None and so.kind == "prefill":
+                has_mrope = True
             blocks = np.asarray(s.block_ids, dtype=np.int64)
             slot[t:t + k] = blocks[p // self.bs] * self.bs + p % self.bs
             nb = len(s.block_ids)
@@ -222,6 +238,7 @@ class ModelRunner:
                 n_sel += 1
             T += B - n
         greedy = self._fill_sampling(so, B)
+        extras = self._mm_extras(so) if (has_mrope and self.encoder_cache is not None) else {}
         # H2D: one async copy per buffer from pinned memory
         nb_ = 0
         for h, dv, cnt in ((self.h_ids, self.d_ids, T), (self.h_pos, self.d_pos, T), (self.h_slot, self.d_slot, T),
@@ -239,8 +256,49 @@ class ModelRunner:
             num_tokens=T, num_seqs=B, is_decode=(so.kind == "decode" and max_q == 1),
             query_start_loc=self.d_qsl[:B + 1], seq_lens=self.d_seqlen[:B], block_tables=self.d_bt[:B],
             slot_mapping=self.d_slot[:T], logits_indices=self.d_lidx[:n_sel], max_query_len=max_q,
-            max_seq_len=max_s, workspace=self.workspace, num_splits=self.num_splits_for(B))
+            max_seq_len=max_s, workspace=self.workspace, num_splits=self.num_splits_for(B), extras=extras)
         return meta, T, n_sel, greedy
+
+    def _mm_extras(self, so: SchedulerOutput) -> dict:
+        """Multimodal inputs of a prefill step: image rows from the encoder cache (encoding
+        images on first use), their token indices, and [3, T] multimodal positions."""
+        model = self.model
+        H = model.cfg.hidden_size
+        p3_parts, idx, rows = [], [], []
+        t = 0
+        for s in so.seqs:
+            k = len(s.token_ids)
+            req = s.request
+            p = torch.arange(s.start_pos, s.start_pos + k)
+            if req is not None and req.mrope_positions is not None:
+                P = req.mrope_positions
+                inside = p < P.shape[1]
+                col = torch.where(inside[None], P[:, p.clamp(max=P.shape[1] - 1)], (p + req.mrope_delta)[None])
+                p3_parts.append(col)
+                for it_i, it in enumerate(req.mm_items or []):
+                    lo = max(s.start_pos, it["offset"])
+                    hi = min(s.start_pos + k, it["offset"] + it["n"])
+                    if lo >= hi:
+                        continue
+                    if not self.encoder_cache.has(req.request_id, it_i):
+                        with torch.inference_mode():
+                            mm = model.embed_multimodal(it["pixels"])
+                        fat = torch.cat([mm["embeds"]] + list(mm["deepstack"]), dim=-1)
+                        self.encoder_cache.put(req.request_id, it_i, fat)
+                    r = torch.arange(lo - it["offset"], hi - it["offset"], device=self.device)
+                    rows.append(self.encoder_cache.gather(req.request_id, it_i, r))
+                    idx.append(torch.arange(t + lo - s.start_pos, t + hi - s.start_pos))
+            else:
+                p3_parts.append(p[None].expand(3, k))
+            t += k
+        ex = {"mrope_positions": torch.cat(p3_parts, dim=1).to(self.device)}
+        if rows:
+            fat = torch.cat(rows)
+            nd = (fat.shape[1] // H) - 1
+            ex["mm_embeds"] = fat[:, :H]
+            ex["deepstack"] = [fat[:, (j + 1) * H:(j + 2) * H] for j in range(nd)]
+            ex["mm_index"] = torch.cat(idx).to(self.device)
+        return ex
 
     # ------------------------------------------------------------------ forward
     def _forward_sample(self, meta: AttentionMetadata, T: int, n_sel: int, greedy: bool) -> torch.Tensor:

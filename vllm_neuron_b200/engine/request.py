@@ -42,6 +42,9 @@ class Request:
     metrics: RequestMetrics = field(default_factory=RequestMetrics)
     stop_reason: int | None = None
     sample_seq: int = 0  # deterministic per-request RNG counter
+    mm_items: list | None = None  # [{"pixels", "grid", "offset", "n"}] image placeholders in the prompt
+    mrope_positions: object = None  # [3, prompt_len] multimodal positions (Qwen3-VL)
+    mrope_delta: int = 0  # decode rope position = cache position + delta
 
     def __post_init__(self) -> None:
         self.metrics.arrival_time = self.arrival_time

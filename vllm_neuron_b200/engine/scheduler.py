@@ -80,6 +80,7 @@ class Scheduler:
         blocks_per_max = -(-max_model_len // kv.block_size)
         self.max_kv_concurrent = max(1, (kv.pool.num_blocks - 1) // blocks_per_max)
         self._finished_ids: list[str] = []
+        self.on_finish: list = []  # callbacks(request_id), e.g. encoder-cache release
 
     # ------------------------------------------------------------------ queue
     def add_request(self, req: Request) -> None:
@@ -101,6 +102,8 @@ class Scheduler:
         return bool(self.waiting or self.running)
 
     def _finish(self, req: Request) -> None:
+        for cb in self.on_finish:
+            cb(req.request_id)
         if req in self.running:
             self.running.remove(req)
         try:

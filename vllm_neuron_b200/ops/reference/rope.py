@@ -85,7 +85,7 @@ def mrope_cos_sin(positions_3d: torch.Tensor, inv_freq: torch.Tensor, mrope_sect
     axis = torch.zeros(half, dtype=torch.long)
     if interleaved:
         for a in (1, 2):
-            idx = torch.arange(a, mrope_section[a] * 3, 3)
+            idx = torch.arange(a, min(mrope_section[a] * 3, half), 3)
             axis[idx] = a
     else:
         off = 0
