@@ -50,12 +50,18 @@ class LLMEngine:
             self.proposer = EagleProposer(cfg, self.worker)
         self.worker.warmup()
         self.num_blocks = n_blocks
-        self.kv = KVCacheManager(n_blocks, cfg.block_size, cfg.enable_prefix_caching)
+        hybrid = hasattr(self.worker.model, "get_state_spec")
+        if hybrid and cfg.enable_prefix_caching:
+            logger.info("prefix caching disabled: recurrent (linear-attention) layers keep per-request state")
+        self.kv = KVCacheManager(n_blocks, cfg.block_size, cfg.enable_prefix_caching and not hybrid)
         k = cfg.speculative_config.num_speculative_tokens if cfg.speculative_config else 0
         self.scheduler = Scheduler(self.kv, cfg.max_num_seqs, cfg.max_num_batched_tokens, cfg.max_model_len,
                                    cfg.max_num_prefills_per_step, cfg.enable_chunked_prefill, k)
         if self.worker.runner.encoder_cache is not None:
             self.scheduler.on_finish.append(self.worker.runner.encoder_cache.release)
+        if self.worker.runner.state_caches is not None:
+            self.scheduler.on_finish.append(self.worker.runner.release_state)
+            self.scheduler.on_preempt.append(self.worker.runner.release_state)
         hf = self.worker.hf
         self.eos_token_id = hf.get("eos_token_id")
         self._pending: list[tuple] = []

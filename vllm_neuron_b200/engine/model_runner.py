@@ -117,9 +117,44 @@ class ModelRunner:
             nblk = ecfg.encoder_cache_num_blocks or min(64, max(4, cfg.max_num_seqs))
             blk_tok = ecfg.max_vision_seq_len or 4096
             self.encoder_cache = EncoderCache(nblk, blk_tok, model.cfg.hidden_size * (1 + nd), model.dtype, device)
+        # recurrent-state slots (hybrid linear-attention models): one slot per running
+        # request plus a scratch slot for decode padding rows
+        self.state_caches: list | None = None
+        self.slot_of: dict[str, int] = {}
+        if hasattr(model, "get_state_spec"):
+            S = cfg.max_num_seqs + 1
+            self.state_caches = []
+            for sp in model.get_state_spec():
+                if sp is None:
+                    self.state_caches.append(None)
+                    continue
+                (C, K1), (hv, dk, dv) = sp
+                self.state_caches.append((torch.zeros(S, C, K1, dtype=model.dtype, device=device),
+                                          torch.zeros(S, hv, dk, dv, dtype=torch.float32, device=device)))
+            self.free_slots = list(range(S - 2, -1, -1))
+            self.scratch_slot = S - 1
+            self.h_sslot = mk(B, torch.int32)
+            self.h_sinit = mk(B, torch.int32)
+            self.d_sslot = torch.zeros(B, dtype=torch.int32, device=d)
+            self.d_sinit = torch.zeros(B, dtype=torch.int32, device=d)
         self.h2d_bytes_last = 0
         self.d2h_bytes_last = 0
         self.step_count = 0
+
+    def release_state(self, req_id: str) -> None:
+        """Return a request's recurrent-state slot (request finished or preempted)."""
+        s = self.slot_of.pop(req_id, None)
+        if s is not None:
+            self.free_slots.append(s)
+
+    def _slot_for(self, req_id: str) -> int:
+        s = self.slot_of.get(req_id)
+        if s is None:
+            if not self.free_slots:
+                raise RuntimeError("no free recurrent-state slot (more running requests than max_num_seqs)")
+            s = self.free_slots.pop()
+            self.slot_of[req_id] = s
+        return s
 
     def _num_spec(self) -> int:
         sc = self.cfg.speculative_config
@@ -131,7 +166,7 @@ class ModelRunner:
         self.kv_caches = []
         for l in spec.layers:
             if l.kind != "attention":
-                self.kv_caches.append(None)
+                self.kv_caches.append(self.state_caches[len(self.kv_caches)] if self.state_caches else None)
                 continue
             shape = (num_blocks, l.num_kv_heads, self.bs, l.head_dim)
             self.kv_caches.append((torch.zeros(shape, dtype=l.dtype, device=self.device),
@@ -239,6 +274,18 @@ class ModelRunner:
             T += B - n
         greedy = self._fill_sampling(so, B)
         extras = self._mm_extras(so) if (has_mrope and self.encoder_cache is not None) else {}
+        if self.state_caches is not None:
+            hs, hi = self.h_sslot.numpy(), self.h_sinit.numpy()
+            for i, s in enumerate(seqs):
+                real = s.request is not None
+                hs[i] = self._slot_for(s.req_id) if real else self.scratch_slot
+                hi[i] = 1 if (s.start_pos > 0 or not real) else 0
+            hs[n:B] = self.scratch_slot
+            hi[n:B] = 1
+            self.d_sslot[:B].copy_(self.h_sslot[:B], non_blocking=True)
+            self.d_sinit[:B].copy_(self.h_sinit[:B], non_blocking=True)
+            extras["state_slots"] = self.d_sslot[:B]
+            extras["state_init"] = self.d_sinit[:B]
         # H2D: one async copy per buffer from pinned memory
         nb_ = 0
         for h, dv, cnt in ((self.h_ids, self.d_ids, T), (self.h_pos, self.d_pos, T), (self.h_slot, self.d_slot, T),

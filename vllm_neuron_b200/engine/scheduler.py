@@ -81,6 +81,7 @@ class Scheduler:
         self.max_kv_concurrent = max(1, (kv.pool.num_blocks - 1) // blocks_per_max)
         self._finished_ids: list[str] = []
         self.on_finish: list = []  # callbacks(request_id), e.g. encoder-cache release
+        self.on_preempt: list = []  # callbacks(request_id), e.g. recurrent-state slot release
 
     # ------------------------------------------------------------------ queue
     def add_request(self, req: Request) -> None:
@@ -212,6 +213,8 @@ class Scheduler:
         req.num_computed_tokens = 0
         req.spec_token_ids = []
         req.status = RequestStatus.PREEMPTED
+        for cb in self.on_preempt:
+            cb(req.request_id)
         self.waiting.appendleft(req)
         logger.warning("preempted request %s (KV cache full)", req.request_id)
 

@@ -18,7 +18,8 @@ import torch.nn.functional as F
 from . import reference as ref
 from ._ext import kernels_enabled, use_kernel  # noqa: F401
 from ._ext import ops as _k
-from .metadata import AttentionMetadata  # noqa: F401
+from .metadata import AttentionMetadata
+from .reference import deltanet as ref_dn  # noqa: F401
 
 _STATUS: dict = {}
 
@@ -147,7 +148,7 @@ def rope_and_cache(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Te
         return qkv[:, : num_q * head_dim].view(T, num_q, head_dim)
     q = qkv[:, : num_q * head_dim].view(T, num_q, head_dim)
     k = qkv[:, num_q * head_dim:(num_q + num_kv) * head_dim].view(T, num_kv, head_dim)
-    v = qkv[:, (num_q + num_kv) * head_dim:].view(T, num_kv, head_dim)
+    v = qkv[:, (num_q + num_kv) * head_dim:(num_q + 2 * num_kv) * head_dim].view(T, num_kv, head_dim)
     if q_norm_w is not None:
         q.copy_(ref.rms_norm(q, q_norm_w, norm_eps))
         k.copy_(ref.rms_norm(k, k_norm_w, norm_eps))
@@ -274,6 +275,70 @@ def moe_dense(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, w13
                       -1.0 if limit is None else float(limit), interleaved, act == "swiglu_clamp")
         return out
     return ref.moe_experts(x, topk_ids, topk_w, w13, b13, w2, b2, alpha, limit, interleaved, expert_offset, act)
+
+
+# ---------------------------------------------------------------------------
+# gated DeltaNet (Qwen3-Next linear attention) and gating helpers
+# ---------------------------------------------------------------------------
+
+
+def _state_meta(meta: AttentionMetadata):
+    ex = meta.extras
+    return meta.query_start_loc, ex["state_slots"], ex["state_init"]
+
+
+def causal_conv1d(x: torch.Tensor, w: torch.Tensor, conv_state: torch.Tensor, meta: AttentionMetadata
+                  ) -> torch.Tensor:
+    """Depthwise causal conv (kernel K) + SiLU per sequence, continuing from / updating the
+    per-slot conv state [slots, C, K-1].  x [T, C] may be a row-strided view."""
+    qsl, slots, init = _state_meta(meta)
+    if use_kernel(x):
+        out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+        _k().causal_conv1d(out, x, w, conv_state, qsl, slots, init, int(meta.max_query_len))
+        return out
+    return ref_dn.causal_conv1d(x, w, conv_state, qsl, slots, init)
+
+
+def gated_delta_net(mixed: torch.Tensor, z: torch.Tensor, b: torch.Tensor, a: torch.Tensor, A_log: torch.Tensor,
+                    dt_bias: torch.Tensor, norm_w: torch.Tensor, eps: float, state: torch.Tensor,
+                    meta: AttentionMetadata, nk: int, nv: int, dk: int, dv: int) -> torch.Tensor:
+    """Gated delta rule over the conv output ``mixed`` [T, 2*nk*dk + nv*dv] (q | k | v), with
+    decay/strength from a, b [T, nv], followed by the per-head gated RMSNorm with z
+    [T, nv*dv].  Continues from / updates the per-slot state [slots, nv, dk, dv] fp32.
+    Returns [T, nv*dv] in mixed.dtype."""
+    qsl, slots, init = _state_meta(meta)
+    T = mixed.shape[0]
+    if use_kernel(mixed):
+        out = torch.empty(T, nv * dv, dtype=mixed.dtype, device=mixed.device)
+        _k().gated_delta_net(out, mixed, z, b, a, A_log, dt_bias, norm_w, float(eps), state, qsl, slots, init,
+                             nk, nv, dk, dv, bool(meta.is_decode), int(meta.max_query_len),
+                             meta.extras.get("gdn_workspace"))
+        return out
+    q = mixed[:, :nk * dk].reshape(T, nk, dk)
+    k = mixed[:, nk * dk:2 * nk * dk].reshape(T, nk, dk)
+    v = mixed[:, 2 * nk * dk:].reshape(T, nv, dv)
+    g, beta = ref_dn.gate_and_beta(a, b, A_log, dt_bias)
+    o = ref_dn.gated_delta_rule(q, k, v, g, beta, state, qsl, slots, init)
+    y = ref_dn.gated_rms_norm(o.to(mixed.dtype), z.reshape(T, nv, dv), norm_w, eps)
+    return y.reshape(T, nv * dv)
+
+
+def sigmoid_gate_mul(x: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
+    """x * sigmoid(gate) elementwise (gate may be a row-strided view)."""
+    if use_kernel(x):
+        out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+        _k().sigmoid_gate_mul(out, x, gate)
+        return out
+    return (x.float() * torch.sigmoid(gate.float())).to(x.dtype)
+
+
+def gated_add(x: torch.Tensor, y: torch.Tensor, gate_logit: torch.Tensor) -> torch.Tensor:
+    """x + sigmoid(gate_logit) * y, gate_logit [T, 1] (shared-expert gate)."""
+    if use_kernel(x):
+        out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+        _k().gated_add(out, x, y, gate_logit)
+        return out
+    return (x.float() + torch.sigmoid(gate_logit.float()) * y.float()).to(x.dtype)
 
 
 # ---------------------------------------------------------------------------
