@@ -103,7 +103,7 @@ def _paged_setup(seq_lens, q_lens, nq, nkv, d, bs, dtype=torch.bfloat16, seed=0)
     return q, kc, vc, bt.to(DEV), torch.tensor(seq_lens, dtype=torch.int32, device=DEV), qsl.to(DEV)
 
 
-@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("d", [64, 128, 256])
 @pytest.mark.parametrize("window", [0, 128])
 @pytest.mark.parametrize("splits", [1, 5])
 @pytest.mark.parametrize("fp8", [False, True])
@@ -131,7 +131,7 @@ def test_paged_decode(d, window, splits, fp8):
     _close(got, want, 2e-2, 3e-2, f"decode d={d} w={window} s={splits} fp8={fp8}")
 
 
-@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("d", [64, 128, 256])
 @pytest.mark.parametrize("window", [0, 128])
 def test_paged_prefill(d, window):
     # chunked prefill / prefix hits: queries are the last q_len tokens of each sequence

@@ -629,6 +629,7 @@ extern "C" int b200_paged_attention_decode(void* out, const void* q, const void*
                                                                 num_splits, s);
   if (d == 64) { DEC(64) }
   if (d == 128) { DEC(128) }
+  if (d == 256) { DEC(256) }
 #undef DEC
   return kBadShape;
 }
@@ -651,6 +652,7 @@ extern "C" int b200_paged_attention_prefill(void* out, const void* q, const void
                    1, scale, k_scale, v_scale, max_query_len, s);
   if (d == 64) { PRE(64) }
   if (d == 128) { PRE(128) }
+  if (d == 256) { PRE(256) }
 #undef PRE
   return kBadShape;
 }

@@ -199,6 +199,8 @@ void register_moe_impls(torch::Library& m);
 void register_comm_ops(torch::Library& m);
 void register_comm_impls(torch::Library& m);
 void register_comm_cpu_impls(torch::Library& m);
+void register_deltanet_ops(torch::Library& m);
+void register_deltanet_impls(torch::Library& m);
 
 TORCH_LIBRARY(b200, m) {
   m.def("rms_norm(Tensor(a!) out, Tensor x, Tensor w, float eps) -> ()");
@@ -227,6 +229,7 @@ TORCH_LIBRARY(b200, m) {
       "int max_top_k) -> ()");
   register_moe_ops(m);
   register_comm_ops(m);
+  register_deltanet_ops(m);
 }
 
 // ops without tensor arguments (pointer plumbing) dispatch through CompositeExplicitAutograd
@@ -246,6 +249,7 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("sample", &sample);
   register_moe_impls(m);
   register_comm_impls(m);
+  register_deltanet_impls(m);
 }
 
 // Python module entry so `import vllm_neuron_b200._C` loads the library.

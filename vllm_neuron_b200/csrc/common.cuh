@@ -62,4 +62,14 @@ B200_D float block_sum(float v, float* red) {
 
 B200_HD int cdiv(int a, int b) { return (a + b - 1) / b; }
 
+// Self-checks: record (code, where, value) in status[0..2] (first error wins) and let the
+// caller skip the access.  status may be null.
+B200_D void record(int* status, int code, int where, int value) {
+  if (status && atomicCAS(status, 0, code) == 0) {
+    status[1] = where;
+    status[2] = value;
+  }
+}
+B200_D bool misaligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) != 0; }
+
 }  // namespace b200

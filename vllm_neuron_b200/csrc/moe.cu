@@ -30,15 +30,17 @@ namespace b200 {
 
 constexpr int kSfAtom = 512;  // 128 rows x 4 scale bytes
 
-// Self-checks: record (code, where, value) in status[0..2] (first error wins) and let the
-// caller skip the access.  status may be null.
-B200_D void record(int* status, int code, int where, int value) {
-  if (status && atomicCAS(status, 0, code) == 0) {
-    status[1] = where;
-    status[2] = value;
-  }
-}
-B200_D bool misaligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) != 0; }
+// Weight / activation formats of the grouped GEMM: block-scaled MX (weights e2m1 or e4m3,
+// activations e4m3, ue8m0 scales per 32 along K; tcgen05 kind::mxf8f6f4) or plain bf16
+// (tcgen05 kind::f16).  Every format stages 128-byte K rows per pipeline stage: 128
+// elements of fp8 / unpacked fp4, 64 of bf16.
+enum WFmt : int { kFmtFp4 = 0, kFmtFp8 = 1, kFmtBf16 = 2 };
+template <int FMT>
+struct FmtTraits {
+  static constexpr int kKStage = FMT == kFmtBf16 ? 64 : 128;  // K elements per stage
+  static constexpr bool kScaled = FMT != kFmtBf16;
+};
+
 
 B200_HD size_t sf_byte(int atom, int kgroups, int row_in_atom, int kb) {
   // kb = 32-element block index along K; atoms are [atom][kb/4][512]
@@ -210,6 +212,25 @@ __global__ void __launch_bounds__(128) moe_quant_kernel(uint8_t* __restrict__ q,
   }
 }
 
+// ------------------------------------------------------------------ bf16 gather
+// One warp per permuted row: copy x[row_route[r] / k] (bf16, K elements) to dst row r.
+__global__ void __launch_bounds__(128) moe_gather_kernel(__nv_bfloat16* __restrict__ dst, int ld_dst,
+                                                         const __nv_bfloat16* __restrict__ src, int src_ld,
+                                                         const int* __restrict__ row_route, int k_gather,
+                                                         const int* __restrict__ offsets, int E, int K, int R_max,
+                                                         int src_rows, int* status) {
+  const int r = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (r >= R_max || r >= offsets[E]) return;
+  const int srow = row_route[r] / k_gather;
+  if (srow < 0 || srow >= src_rows) {
+    if (lane == 0) record(status, kBadIndex, 13, srow);
+    return;
+  }
+  const uint4* s4 = reinterpret_cast<const uint4*>(src + (size_t)srow * src_ld);
+  uint4* d4 = reinterpret_cast<uint4*>(dst + (size_t)r * ld_dst);
+  for (int c = lane; c < K / 8; c += 32) d4[c] = s4[c];
+}
+
 // ------------------------------------------------------------------------- GEMM
 // Persistent grouped GEMM: one CTA per SM loops over work items (N tile of one expert x
 // 128-row M tile, M fastest so consecutive items share the activation tile in L2).
@@ -252,7 +273,7 @@ B200_D WorkItem decode_item(const MoeWorkspace& ws, int w, int mtiles, int E_loc
   return it;
 }
 
-template <int NT, int STAGES, bool A_FP4, int EPI>
+template <int NT, int STAGES, int FMT, int EPI>
 __global__ void __launch_bounds__(256, (NT <= 32 ? 2 : 1)) moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                                                           const __grid_constant__ CUtensorMap tmB,
                                                           const uint8_t* __restrict__ sfa,
@@ -281,7 +302,8 @@ __global__ void __launch_bounds__(256, (NT <= 32 ? 2 : 1)) moe_gemm_kernel(const
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nk = Kp / 128;
+  using F = FmtTraits<FMT>;
+  const int nk = Kp / F::kKStage;
   const int mblk = mtiles;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -323,20 +345,24 @@ __global__ void __launch_bounds__(256, (NT <= 32 ? 2 : 1)) moe_gemm_kernel(const
             break;
           }
           // transaction bytes count the global (packed) size: fp4 tiles are 4 bits/element
-          tc::mbar_arrive_expect_tx(&full[s], (A_FP4 ? L::kA / 2 : L::kA) + L::kB + 2 * kSfAtom);
-          // weights are stored as contiguous 128x128 tiles: tile index (e, m tile, k tile)
+          tc::mbar_arrive_expect_tx(&full[s], (FMT == kFmtFp4 ? L::kA / 2 : L::kA) + L::kB +
+                                                  (F::kScaled ? 2 * kSfAtom : 0));
+          // weights are stored as contiguous 128-row x 128-byte tiles: tile index (e, m tile, k tile)
           tc::tma_load_3d(sA + s * L::kA, &tmA, 0, 0, ((wi.e * mblk) + wi.mt) * nk + kt, &full[s]);
-          tc::tma_load_2d(sB + s * L::kB, &tmB, kt * 128, wi.row0, &full[s]);
-          tc::bulk_load(sSfa + s * kSfAtom, sfa + (((size_t)wi.e * mblk + wi.mt) * nk + kt) * kSfAtom, kSfAtom,
-                        &full[s]);
-          tc::bulk_load(sSfb + s * kSfAtom, sfb + ((size_t)wi.tile * nk + kt) * kSfAtom, kSfAtom, &full[s]);
+          tc::tma_load_2d(sB + s * L::kB, &tmB, kt * F::kKStage, wi.row0, &full[s]);
+          if constexpr (F::kScaled) {
+            tc::bulk_load(sSfa + s * kSfAtom, sfa + (((size_t)wi.e * mblk + wi.mt) * nk + kt) * kSfAtom, kSfAtom,
+                          &full[s]);
+            tc::bulk_load(sSfb + s * kSfAtom, sfb + ((size_t)wi.tile * nk + kt) * kSfAtom, kSfAtom, &full[s]);
+          }
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      const uint32_t idesc0 = tc::idesc_mxf8f6f4(A_FP4 ? 5 : 0, 0, 128, NT);
+      const uint32_t idesc0 =
+          F::kScaled ? tc::idesc_mxf8f6f4(FMT == kFmtFp4 ? 5 : 0, 0, 128, NT) : tc::idesc_f16_bf16(128, NT);
       const uint32_t t_sfa = tmem + 2 * NT, t_sfb = tmem + 2 * NT + 4;
       int it = 0, local = 0;
       bool ok = true;
@@ -354,14 +380,21 @@ __global__ void __launch_bounds__(256, (NT <= 32 ? 2 : 1)) moe_gemm_kernel(const
             break;
           }
           tc::fence_after_sync();
-          tc::utccp_32x128b_warpx4(t_sfa, tc::desc_noswizzle_16b_rows(sSfa + s * kSfAtom));
-          tc::utccp_32x128b_warpx4(t_sfb, tc::desc_noswizzle_16b_rows(sSfb + s * kSfAtom));
           const uint64_t ad = tc::desc_sw128(sA + s * L::kA);
           const uint64_t bd = tc::desc_sw128(sB + s * L::kB);
+          if constexpr (F::kScaled) {
+            tc::utccp_32x128b_warpx4(t_sfa, tc::desc_noswizzle_16b_rows(sSfa + s * kSfAtom));
+            tc::utccp_32x128b_warpx4(t_sfb, tc::desc_noswizzle_16b_rows(sSfb + s * kSfAtom));
 #pragma unroll
-          for (int kb = 0; kb < 4; ++kb) {
-            tc::mma_mxf8f6f4(t_d, ad + 2 * kb, bd + 2 * kb, tc::idesc_with_sf_ids(idesc0, kb, kb),
-                             t_sfa | ((uint32_t)kb << 30), t_sfb | ((uint32_t)kb << 30), (kt | kb) != 0 ? 1u : 0u);
+            for (int kb = 0; kb < 4; ++kb) {  // 4 x K=32 per 128-byte stage
+              tc::mma_mxf8f6f4(t_d, ad + 2 * kb, bd + 2 * kb, tc::idesc_with_sf_ids(idesc0, kb, kb),
+                               t_sfa | ((uint32_t)kb << 30), t_sfb | ((uint32_t)kb << 30),
+                               (kt | kb) != 0 ? 1u : 0u);
+            }
+          } else {
+#pragma unroll
+            for (int kb = 0; kb < 4; ++kb)  // 4 x K=16 bf16 per 128-byte stage
+              tc::mma_f16(t_d, ad + 2 * kb, bd + 2 * kb, idesc0, (kt | kb) != 0 ? 1u : 0u);
           }
           tc::mma_commit(&empty[s]);
         }
@@ -466,17 +499,35 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 
 // Weight map over contiguous 128-row x 128-element tiles [n_tiles, 128, 128*bits/8]:
 // one box = one tile = one contiguous 8 KB (fp4) / 16 KB (fp8) run.
-static int make_weight_map(CUtensorMap* m, const void* w, int n_tiles, bool fp4) {
+static int make_weight_map(CUtensorMap* m, const void* w, int n_tiles, int fmt) {
   auto enc = get_encode();
   if (!enc) return kBadShape;
+  const bool fp4 = fmt == kFmtFp4, b16 = fmt == kFmtBf16;
   const uint64_t row_bytes = fp4 ? 64 : 128;
-  cuuint64_t dims[3] = {128, 128, (cuuint64_t)n_tiles};
+  const cuuint64_t row_elems = b16 ? 64 : 128;
+  cuuint64_t dims[3] = {row_elems, 128, (cuuint64_t)n_tiles};
   cuuint64_t strides[2] = {row_bytes, row_bytes * 128};
-  cuuint32_t box[3] = {128, 128, 1};
+  cuuint32_t box[3] = {(cuuint32_t)row_elems, 128, 1};
   cuuint32_t es[3] = {1, 1, 1};
-  CUresult r = enc(m, fp4 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, 3,
+  CUresult r = enc(m, fp4 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B
+                          : (b16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8), 3,
                    const_cast<void*>(w), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : 1000 + (int)r;
+}
+
+// 2-D bf16 activation map: K valid columns (TMA zero-fills beyond), row stride ld elements,
+// box 64 x NT.
+static int make_act_map_bf16(CUtensorMap* m, const void* a, int R, int K, int ld, int nt) {
+  auto enc = get_encode();
+  if (!enc) return kBadShape;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)R};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)nt};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : 1000 + (int)r;
 }
 
@@ -505,13 +556,13 @@ static int num_sms() {
   return n;
 }
 
-template <int NT, int STAGES, bool A_FP4, int EPI>
+template <int NT, int STAGES, int FMT, int EPI>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const uint8_t* sfa, const uint8_t* sfb,
                        const MoeWorkspace& ws, const float* bias, const float* topk_w, void* out, int M, int Kp,
                        int ld_out, float alpha, float limit, int max_tiles, int E_local, int R_max, int atoms_max,
                        int* status, cudaStream_t s) {
   using L = GemmSmem<NT, STAGES>;
-  auto kern = moe_gemm_kernel<NT, STAGES, A_FP4, EPI>;
+  auto kern = moe_gemm_kernel<NT, STAGES, FMT, EPI>;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
@@ -532,20 +583,42 @@ static int run_gemms(const MoeShape& sh, const void* w13, const uint8_t* sf13, c
                      float limit, int R_max, int max_tiles, int atoms_max, int* status, cudaStream_t s) {
   CUtensorMap ta1, tb1, ta2, tb2;
   int rc;
-  if ((rc = make_weight_map(&ta1, w13, sh.E_local * cdiv(2 * sh.I, 128) * (sh.K1p / 128), A_FP4))) return rc;
+  constexpr int FMT = A_FP4 ? kFmtFp4 : kFmtFp8;
+  if ((rc = make_weight_map(&ta1, w13, sh.E_local * cdiv(2 * sh.I, 128) * (sh.K1p / 128), FMT))) return rc;
   if ((rc = make_act_map(&tb1, ws.xq, R_max, sh.K1p, NT))) return rc;
-  if ((rc = make_weight_map(&ta2, w2, sh.E_local * cdiv(sh.H, 128) * (sh.K2p / 128), A_FP4))) return rc;
+  if ((rc = make_weight_map(&ta2, w2, sh.E_local * cdiv(sh.H, 128) * (sh.K2p / 128), FMT))) return rc;
   if ((rc = make_act_map(&tb2, ws.aq, R_max, sh.K2p, NT))) return rc;
-  rc = launch_gemm<NT, STAGES, A_FP4, kEpiSwiglu>(ta1, tb1, sf13, ws.sf1, ws, b13, topk_w, ws.act, 2 * sh.I,
+  rc = launch_gemm<NT, STAGES, FMT, kEpiSwiglu>(ta1, tb1, sf13, ws.sf1, ws, b13, topk_w, ws.act, 2 * sh.I,
                                                   sh.K1p, sh.I, alpha, limit, max_tiles, sh.E_local, R_max, atoms_max,
                                                   status, s);
   if (rc) return rc;
   moe_quant_kernel<<<cdiv(R_max * cdiv(sh.K2p / 32, 32), 4), 128, 0, s>>>(ws.aq, ws.sf2, (const __nv_bfloat16*)ws.act, sh.I, ws.row_route,
                                                   0, ws.offsets, ws.atom_base, sh.E_local, sh.I, sh.K2p, R_max, R_max,
                                                   atoms_max, NT, status);
-  rc = launch_gemm<NT, STAGES, A_FP4, kEpiDown>(ta2, tb2, sf2w, ws.sf2, ws, b2, topk_w, ws.y, sh.H, sh.K2p, sh.H,
-                                                alpha, limit, max_tiles, sh.E_local, R_max, atoms_max, status, s);
+  rc = launch_gemm<NT, STAGES, FMT, kEpiDown>(ta2, tb2, sf2w, ws.sf2, ws, b2, topk_w, ws.y, sh.H, sh.K2p, sh.H,
+                                              alpha, limit, max_tiles, sh.E_local, R_max, atoms_max, status, s);
   return rc;
+}
+
+// bf16 experts: gathered bf16 rows -> GEMM1 (kind::f16) -> SwiGLU (bf16, row stride K2p) ->
+// GEMM2 reading the activations directly.  K1p / K2p are H / I rounded up to 64.
+template <int NT, int STAGES>
+static int run_gemms_bf16(const MoeShape& sh, const void* w13, const float* b13, const void* w2, const float* b2,
+                          const float* topk_w, const MoeWorkspace& ws, float alpha, float limit, int R_max,
+                          int max_tiles, int atoms_max, int* status, cudaStream_t s) {
+  CUtensorMap ta1, tb1, ta2, tb2;
+  int rc;
+  if ((rc = make_weight_map(&ta1, w13, sh.E_local * cdiv(2 * sh.I, 128) * (sh.K1p / 64), kFmtBf16))) return rc;
+  if ((rc = make_act_map_bf16(&tb1, ws.xq, R_max, sh.H, sh.K1p, NT))) return rc;
+  if ((rc = make_weight_map(&ta2, w2, sh.E_local * cdiv(sh.H, 128) * (sh.K2p / 64), kFmtBf16))) return rc;
+  if ((rc = make_act_map_bf16(&tb2, ws.act, R_max, sh.I, sh.K2p, NT))) return rc;
+  rc = launch_gemm<NT, STAGES, kFmtBf16, kEpiSwiglu>(ta1, tb1, nullptr, nullptr, ws, b13, topk_w, ws.act, 2 * sh.I,
+                                                     sh.K1p, sh.K2p, alpha, limit, max_tiles, sh.E_local, R_max,
+                                                     atoms_max, status, s);
+  if (rc) return rc;
+  return launch_gemm<NT, STAGES, kFmtBf16, kEpiDown>(ta2, tb2, nullptr, nullptr, ws, b2, topk_w, ws.y, sh.H, sh.K2p,
+                                                     sh.H, alpha, limit, max_tiles, sh.E_local, R_max, atoms_max,
+                                                     status, s);
 }
 
 }  // namespace b200
@@ -562,9 +635,10 @@ static void ws_sizes(const MoeShape& sh, int64_t* z) {
   z[3] = R * 4;
   z[4] = max_tiles * 2 * 4;
   z[5] = 4;
-  z[6] = R * sh.K1p;
+  const int64_t eb = sh.a_fp4 == 2 ? 2 : 1;  // bf16 experts keep bf16 activations
+  z[6] = R * sh.K1p * eb;
   z[7] = atoms * (sh.K1p / 128) * kSfAtom;
-  z[8] = R * sh.I * 2;
+  z[8] = R * (sh.a_fp4 == 2 ? sh.K2p : sh.I) * 2;
   z[9] = R * sh.K2p;
   z[10] = atoms * (sh.K2p / 128) * kSfAtom;
   z[11] = R * sh.H * 2;
@@ -606,6 +680,38 @@ extern "C" int b200_moe_mx_forward(void* out, const void* x, const int* topk_ids
                   : run_gemms<128, 6, false>(sh, w13, sf13, b13, w2, sf2w, b2, topk_w, ws, alpha, limit, R_max,
                                              max_tiles, atoms_max, status, s);
   }
+  if (rc) return rc;
+  moe_reduce_kernel<<<sh.T, 128, 0, s>>>((__nv_bfloat16*)out, (const __nv_bfloat16*)ws.y, topk_ids, sh.k,
+                                         sh.E_local, sh.expert_offset, sh.H);
+  return (int)cudaGetLastError();
+}
+
+extern "C" int b200_moe_bf16_forward(void* out, const void* x, const int* topk_ids, const float* topk_w,
+                                     const void* w13, const float* b13, const void* w2, const float* b2,
+                                     const MoeShape* shape, float alpha, float limit, const MoeWorkspace* wsp,
+                                     int* status, cudaStream_t s) {
+  const MoeShape& sh = *shape;
+  const MoeWorkspace& ws = *wsp;
+  if (sh.T == 0) return 0;
+  if (sh.K1p % 64 || sh.K2p % 64 || sh.H % 8 || sh.I % 8 || sh.E_local > 1024 || sh.k > 16) return kBadShape;
+  if (sh.nt != 16 && sh.nt != 32 && sh.nt != 128) return kBadShape;
+  const int R_max = sh.T * sh.k;
+  const int max_tiles = cdiv(R_max, sh.nt) + sh.E_local;
+  moe_route_kernel<<<1, 1024, 2 * sh.E_local * sizeof(int), s>>>(topk_ids, R_max, sh.E_local, sh.expert_offset,
+                                                                  sh.nt, max_tiles, ws);
+  moe_gather_kernel<<<cdiv(R_max, 4), 128, 0, s>>>((__nv_bfloat16*)ws.xq, sh.K1p, (const __nv_bfloat16*)x, sh.H,
+                                                   ws.row_route, sh.k, ws.offsets, sh.E_local, sh.H, R_max, sh.T,
+                                                   status);
+  int rc;
+  if (sh.nt == 16)
+    rc = run_gemms_bf16<16, 5>(sh, w13, b13, w2, b2, topk_w, ws, alpha, limit, R_max, max_tiles, max_tiles, status,
+                               s);
+  else if (sh.nt == 32)
+    rc = run_gemms_bf16<32, 5>(sh, w13, b13, w2, b2, topk_w, ws, alpha, limit, R_max, max_tiles, max_tiles, status,
+                               s);
+  else
+    rc = run_gemms_bf16<128, 6>(sh, w13, b13, w2, b2, topk_w, ws, alpha, limit, R_max, max_tiles, max_tiles, status,
+                                s);
   if (rc) return rc;
   moe_reduce_kernel<<<sh.T, 128, 0, s>>>((__nv_bfloat16*)out, (const __nv_bfloat16*)ws.y, topk_ids, sh.k,
                                          sh.E_local, sh.expert_offset, sh.H);

@@ -26,7 +26,7 @@ struct MoeShape {
   int T, k, E_local, expert_offset;
   int H, I;     // hidden, intermediate
   int K1p, K2p; // H and I rounded up to 128
-  int a_fp4;    // 1: weights e2m1 (MXFP4), 0: e4m3 (MXFP8)
+  int a_fp4;    // 1: weights e2m1 (MXFP4), 0: e4m3 (MXFP8), 2: bf16 weights and activations
   int nt;       // N tile (routes per CTA tile): 32 or 128
 };
 
@@ -42,4 +42,11 @@ int b200_moe_mx_forward(void* out, const void* x, const int* topk_ids, const flo
                         const uint8_t* sf13, const float* b13, const void* w2, const uint8_t* sf2w, const float* b2,
                         const b200::MoeShape* shape, float alpha, float limit, const b200::MoeWorkspace* ws,
                         int* status, cudaStream_t s);
+
+// bf16 experts: route -> gather -> GEMM1 (+bias, SwiGLU) -> GEMM2 (+bias, x affinity) -> sum.
+// Weights are 128-row x 64-element tiles [E, ceil(rows/128), Kp/64, 128, 64]; shape.K1p /
+// K2p are H / I rounded up to 64; shape.a_fp4 = 2.
+int b200_moe_bf16_forward(void* out, const void* x, const int* topk_ids, const float* topk_w, const void* w13,
+                          const float* b13, const void* w2, const float* b2, const b200::MoeShape* shape,
+                          float alpha, float limit, const b200::MoeWorkspace* ws, int* status, cudaStream_t s);
 }

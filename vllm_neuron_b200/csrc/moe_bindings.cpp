@@ -73,13 +73,76 @@ void moe_mx(Tensor out, Tensor x, Tensor topk_ids, Tensor topk_w, Tensor w13, Te
                                      &ws, st, at::cuda::getCurrentCUDAStream().stream());
   TORCH_CHECK(rc == 0, "b200::moe_mx failed with code ", rc);
 }
+void moe_bf16(Tensor out, Tensor x, Tensor topk_ids, Tensor topk_w, Tensor w13, Tensor b13, Tensor w2, Tensor b2,
+              int64_t expert_offset, int64_t H, int64_t I, double alpha, double limit, c10::optional<Tensor> status) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "x: contiguous bf16 CUDA");
+  TORCH_CHECK(out.is_contiguous() && out.scalar_type() == at::kBFloat16, "out: contiguous bf16");
+  TORCH_CHECK(topk_ids.scalar_type() == at::kInt && topk_ids.is_contiguous(), "topk_ids: contiguous int32");
+  TORCH_CHECK(topk_w.scalar_type() == at::kFloat && topk_w.is_contiguous(), "topk_w: contiguous fp32");
+  TORCH_CHECK(b13.scalar_type() == at::kFloat && b2.scalar_type() == at::kFloat, "biases fp32");
+  TORCH_CHECK(w13.scalar_type() == at::kBFloat16 && w2.scalar_type() == at::kBFloat16, "bf16 expert weights");
+  TORCH_CHECK(x.size(1) == H && H % 8 == 0 && I % 8 == 0, "H and I must be multiples of 8");
+  b200::MoeShape sh{};
+  sh.T = x.size(0);
+  sh.k = topk_ids.size(1);
+  sh.E_local = w13.size(0);
+  sh.expert_offset = expert_offset;
+  sh.H = H;
+  sh.I = I;
+  sh.K1p = (H + 63) / 64 * 64;
+  sh.K2p = (I + 63) / 64 * 64;
+  sh.a_fp4 = 2;
+  const int routes = sh.T * sh.k;
+  sh.nt = routes <= 512 ? 16 : (routes <= 2048 ? 32 : 128);
+  TORCH_CHECK(w13.dim() == 5 && w13.size(1) == (2 * I + 127) / 128 && w13.size(2) == sh.K1p / 64 &&
+                  w13.size(3) == 128 && w13.size(4) == 64 && w13.is_contiguous(),
+              "w13 must be contiguous bf16 tiles [E, 2I/128, K1p/64, 128, 64]");
+  TORCH_CHECK(w2.dim() == 5 && w2.size(1) == (H + 127) / 128 && w2.size(2) == sh.K2p / 64 && w2.size(3) == 128 &&
+                  w2.size(4) == 64 && w2.is_contiguous(),
+              "w2 must be contiguous bf16 tiles [E, H/128, K2p/64, 128, 64]");
+  int64_t sizes[12];
+  b200_moe_workspace_sizes(&sh, sizes);
+  int64_t offs[12], total = 0;
+  for (int i = 0; i < 12; ++i) {
+    offs[i] = total;
+    total += (sizes[i] + 255) / 256 * 256;
+  }
+  c10::cuda::CUDAGuard g(x.device());
+  Tensor buf = at::empty({total}, x.options().dtype(at::kByte));
+  uint8_t* base = buf.data_ptr<uint8_t>();
+  b200::MoeWorkspace ws{};
+  ws.offsets = reinterpret_cast<int*>(base + offs[0]);
+  ws.atom_base = reinterpret_cast<int*>(base + offs[1]);
+  ws.cursor = reinterpret_cast<int*>(base + offs[2]);
+  ws.row_route = reinterpret_cast<int*>(base + offs[3]);
+  ws.tiles = reinterpret_cast<int*>(base + offs[4]);
+  ws.num_tiles = reinterpret_cast<int*>(base + offs[5]);
+  ws.xq = base + offs[6];
+  ws.sf1 = base + offs[7];
+  ws.act = reinterpret_cast<uint16_t*>(base + offs[8]);
+  ws.aq = base + offs[9];
+  ws.sf2 = base + offs[10];
+  ws.y = reinterpret_cast<uint16_t*>(base + offs[11]);
+  int* st = status.has_value() ? status->data_ptr<int>() : nullptr;
+  const int rc = b200_moe_bf16_forward(out.data_ptr(), x.data_ptr(), topk_ids.data_ptr<int>(),
+                                       topk_w.data_ptr<float>(), w13.data_ptr(), b13.data_ptr<float>(), w2.data_ptr(),
+                                       b2.data_ptr<float>(), &sh, (float)alpha, (float)limit, &ws, st,
+                                       at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(rc == 0, "b200::moe_bf16 failed with code ", rc);
+}
 }  // namespace
 
 void register_moe_ops(torch::Library& m) {
+  m.def(
+      "moe_bf16(Tensor(a!) out, Tensor x, Tensor topk_ids, Tensor topk_w, Tensor w13, Tensor b13, Tensor w2, "
+      "Tensor b2, int expert_offset, int H, int I, float alpha, float limit, Tensor? status) -> ()");
   m.def(
       "moe_mx(Tensor(a!) out, Tensor x, Tensor topk_ids, Tensor topk_w, Tensor w13, Tensor sf13, Tensor b13, "
       "Tensor w2, Tensor sf2, Tensor b2, int expert_offset, int H, int I, bool a_fp4, float alpha, float limit, "
       "Tensor? status) -> ()");
 }
 
-void register_moe_impls(torch::Library& m) { m.impl("moe_mx", &moe_mx); }
+void register_moe_impls(torch::Library& m) {
+  m.impl("moe_mx", &moe_mx);
+  m.impl("moe_bf16", &moe_bf16);
+}

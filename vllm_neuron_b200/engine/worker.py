@@ -88,6 +88,9 @@ class Worker:
 
             ck = SafetensorsCheckpoint(self.cfg.model)
             model.load_weights(((k, v.to(self.device) if v.numel() > (1 << 20) else v) for k, v in ck))
+        for m in model.modules():  # kernel weight layouts (e.g. grouped-GEMM tiles)
+            if hasattr(m, "process_weights_after_loading"):
+                m.process_weights_after_loading()
         self.model = model.eval()
         self.model_cfg = mcfg
         self.hf = hf

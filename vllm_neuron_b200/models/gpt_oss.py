@@ -192,7 +192,16 @@ class GptOssExperts(nn.Module):
         if self.quant == "mxfp4":
             return ops.moe_mxfp4(x, ids, w, self.w13, self.s13, self.b13, self.w2, self.s2, self.b2, self.offset,
                                  self.alpha, self.limit, self.H, self.I)
-        return ops.moe_dense(x, ids, w, self.w13, self.b13, self.w2, self.b2, self.offset, self.alpha, self.limit)
+        return ops.moe_dense(x, ids, w, self.w13, self.b13, self.w2, self.b2, self.offset, self.alpha, self.limit,
+                             True, "swiglu_clamp", self.H, self.I)
+
+    @torch.no_grad()
+    def process_weights_after_loading(self) -> None:
+        """bf16 experts on a GPU: re-lay the weights into the grouped-GEMM tiles."""
+        if self.quant != "mxfp4" and self.w13.is_cuda and self.w13.dim() == 3:
+            t13, t2 = ops.prepare_moe_bf16(self.w13.data, self.w2.data, interleaved=True)
+            self.w13 = nn.Parameter(t13, requires_grad=False)
+            self.w2 = nn.Parameter(t2, requires_grad=False)
 
 
 class GptOssMLP(nn.Module):

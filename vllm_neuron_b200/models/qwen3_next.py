@@ -273,11 +273,20 @@ class SparseMoE(nn.Module):
             p = torch.softmax(ops.linear(x, self.router).float(), -1)
             wts, ids = torch.topk(p, k, -1)
             ids = ids.to(torch.int32)
-        out = ops.moe_dense(x, ids, wts, self.w13, None, self.w2, None, self.e0, 1.0, None, False, "silu")
+        H, I = self.cfg.hidden_size, self.cfg.moe_intermediate_size
+        out = ops.moe_dense(x, ids, wts, self.w13, None, self.w2, None, self.e0, 1.0, None, False, "silu", H, I)
         if self.shared is not None:
             sg = ops.linear(x, self.shared_gate)
             out = ops.gated_add(out, self.shared(x), sg)
         return out
+
+    @torch.no_grad()
+    def process_weights_after_loading(self) -> None:
+        """On a GPU: re-lay the experts into the grouped-GEMM tiles (gate/up interleaved)."""
+        if self.w13.is_cuda and self.w13.dim() == 3:
+            t13, t2 = ops.prepare_moe_bf16(self.w13.data, self.w2.data, interleaved=False)
+            self.w13 = nn.Parameter(t13, requires_grad=False)
+            self.w2 = nn.Parameter(t2, requires_grad=False)
 
 
 @dataclass

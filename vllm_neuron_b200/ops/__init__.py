@@ -266,15 +266,45 @@ def moe_mxfp4(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, w13
 
 def moe_dense(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, w13: torch.Tensor,
               b13: torch.Tensor | None, w2: torch.Tensor, b2: torch.Tensor | None, expert_offset: int,
-              alpha: float, limit: float | None, interleaved: bool = True, act: str = "swiglu_clamp"
-              ) -> torch.Tensor:
-    """Routed experts with bf16 weights w13 [E, 2I, H], w2 [E, H, I]."""
-    if use_kernel(x):
+              alpha: float, limit: float | None, interleaved: bool = True, act: str = "swiglu_clamp",
+              H: int | None = None, I: int | None = None) -> torch.Tensor:
+    """Routed experts with bf16 weights.  Reference layout: w13 [E, 2I, H], w2 [E, H, I]
+    (gate/up interleaved or halves).  Kernel layout (``prepare_moe_bf16``): tiles
+    w13 [E, 2I/128, Hp/64, 128, 64] with gate/up interleaved, w2 [E, H/128, Ip/64, 128, 64];
+    ``H`` and ``I`` must then be given.  ``act``: "swiglu_clamp" (GPT-OSS, alpha/limit) or
+    "silu" (SiLU(gate) * up)."""
+    if w13.dim() == 5:
+        if not use_kernel(x):
+            raise RuntimeError("tiled bf16 expert weights need the CUDA kernels")
+        E = w13.shape[0]
         out = torch.empty_like(x)
-        _k().moe_bf16(out, x, topk_ids, topk_w, w13, b13, w2, b2, expert_offset, alpha,
-                      -1.0 if limit is None else float(limit), interleaved, act == "swiglu_clamp")
+        b13_ = b13 if b13 is not None else _zeros_f32(E * 2 * I, x.device)
+        b2_ = b2 if b2 is not None else _zeros_f32(E * H, x.device)
+        lim = float(limit) if (act == "swiglu_clamp" and limit is not None) else -1.0
+        _k().moe_bf16(out, x.contiguous(), topk_ids.to(torch.int32).contiguous(), topk_w.float().contiguous(), w13,
+                      b13_, w2, b2_, expert_offset, H, I, alpha if act == "swiglu_clamp" else 1.0, lim,
+                      device_status(x.device))
         return out
     return ref.moe_experts(x, topk_ids, topk_w, w13, b13, w2, b2, alpha, limit, interleaved, expert_offset, act)
+
+
+_ZEROS: dict = {}
+
+
+def _zeros_f32(n: int, device) -> torch.Tensor:
+    key = (str(device), n)
+    z = _ZEROS.get(key)
+    if z is None:
+        z = _ZEROS[key] = torch.zeros(n, dtype=torch.float32, device=device)
+    return z
+
+
+def prepare_moe_bf16(w13: torch.Tensor, w2: torch.Tensor, interleaved: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    """Reference-layout bf16 experts -> the kernel's tiled layout (gate/up interleaved)."""
+    from .mx_layout import interleave_gate_up, tile_bf16
+
+    w13i = w13 if interleaved else interleave_gate_up(w13)
+    return tile_bf16(w13i.to(torch.bfloat16)), tile_bf16(w2.to(torch.bfloat16))
 
 
 # ---------------------------------------------------------------------------

@@ -83,3 +83,27 @@ def untile_values(tiled: torch.Tensor, rows: int, K: int, fp4: bool = True) -> t
 
 def tiled_shape(E: int, rows: int, K: int, fp4: bool = True) -> tuple[int, int, int, int, int]:
     return (E, -(-rows // 128), round_up(K, 128) // 128, 128, 64 if fp4 else 128)
+
+
+def tile_bf16(w: torch.Tensor) -> torch.Tensor:
+    """bf16 expert weights [E, rows, K] -> tiles [E, ceil(rows/128), Kp/64, 128, 64] (Kp = K
+    rounded up to 64, rows and K zero-padded): every (128-row, 64-element) block the
+    kind::f16 tensor-core MMA consumes is one contiguous 16 KB run."""
+    E, R, K = w.shape
+    Rp, Kp = round_up(R, 128), round_up(K, 64)
+    full = torch.zeros(E, Rp, Kp, dtype=w.dtype, device=w.device)
+    full[:, :R, :K] = w
+    return full.view(E, Rp // 128, 128, Kp // 64, 64).permute(0, 1, 3, 2, 4).contiguous()
+
+
+def untile_bf16(t: torch.Tensor, rows: int, K: int) -> torch.Tensor:
+    E, Rb, Kb, _, _ = t.shape
+    return t.permute(0, 1, 3, 2, 4).reshape(E, Rb * 128, Kb * 64)[:, :rows, :K]
+
+
+def interleave_gate_up(w13: torch.Tensor) -> torch.Tensor:
+    """[E, 2I, K] with gate rows then up rows -> rows gate0, up0, gate1, up1, ... (the
+    kernels' SwiGLU epilogue pairs adjacent rows)."""
+    E, I2, K = w13.shape
+    I = I2 // 2
+    return torch.stack([w13[:, :I], w13[:, I:]], dim=2).reshape(E, I2, K)
