@@ -5,7 +5,7 @@ recurrent state carried across prefill segments) and preemption-free concurrent 
 import pytest
 import torch
 
-from tiny_configs import workload
+from tiny_configs import hf_torch_path, workload
 
 TINY = dict(vocab_size=2048, hidden_size=128, intermediate_size=256, num_hidden_layers=4, num_attention_heads=4,
             num_key_value_heads=2, head_dim=64, linear_conv_kernel_dim=4, linear_key_head_dim=32,
@@ -22,6 +22,7 @@ def _hf():
     cfg = Qwen3NextConfig(**TINY)
     cfg._attn_implementation = "eager"
     m = Qwen3NextForCausalLM(cfg).eval().float()
+    hf_torch_path(m)
     with torch.no_grad():
         for n, p in m.named_parameters():
             if "norm" in n or n.endswith("dt_bias"):

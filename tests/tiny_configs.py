@@ -20,3 +20,22 @@ def workload(n=16, lo=32, hi=128, vocab=4096, seed=0):
         L = int(torch.randint(lo, hi + 1, (1,), generator=g))
         out.append(torch.randint(0, vocab, (L,), generator=g).tolist())
     return out
+
+
+def hf_torch_path(model) -> None:
+    """Make an HF Qwen3-Next model use its PyTorch gated-DeltaNet path (no Triton kernels
+    from optional packages), so it runs on the CPU as the fp32 oracle."""
+    import torch
+    from transformers.models.qwen3_next import modeling_qwen3_next as mq
+
+    for m in model.modules():
+        if isinstance(m, mq.Qwen3NextGatedDeltaNet):
+            m.causal_conv1d_fn = None
+            m.causal_conv1d_update = mq.torch_causal_conv1d_update
+            m.chunk_gated_delta_rule = mq.torch_chunk_gated_delta_rule
+            m.recurrent_gated_delta_rule = mq.torch_recurrent_gated_delta_rule
+            if not isinstance(m.norm, mq.Qwen3NextRMSNormGated):
+                w = m.norm.weight.detach().float().cpu()
+                m.norm = mq.Qwen3NextRMSNormGated(w.numel(), eps=m.layer_norm_epsilon)
+                with torch.no_grad():
+                    m.norm.weight.copy_(w)

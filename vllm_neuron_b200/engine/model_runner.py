@@ -377,7 +377,12 @@ class ModelRunner:
             key = (pad_to, greedy)
             entry = self.graphs.get(key)
             if entry is None:
+                if self.state_caches is not None:
+                    # capture warm-up runs must not advance live recurrent states
+                    self.d_sslot[:pad_to].fill_(self.scratch_slot)
                 entry = self._capture(pad_to, greedy, meta, T, n_sel)
+                if self.state_caches is not None:
+                    self.d_sslot[:pad_to].copy_(self.h_sslot[:pad_to], non_blocking=True)
             entry.graph.replay()
             GRAPH_REPLAY_COUNT.labels(model_name=self.cfg.served_model_name or "model",
                                       bucket_name=f"decode_b{pad_to}").inc()
