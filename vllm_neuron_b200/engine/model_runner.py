@@ -106,6 +106,10 @@ class ModelRunner:
         self.d_topp = torch.ones(B, dtype=torch.float32, device=d)
         self.d_unif = torch.zeros(B, dtype=torch.float32, device=d)
         self.d_out = torch.zeros(B * (1 + self._num_spec()), dtype=torch.int64, device=d)
+        # per verified position (speculative decoding with sampling)
+        P = B * (1 + self._num_spec())
+        self.h_pos_params = mk((6, P), torch.float32)  # temp, top_k, top_p, draft, u_accept, u_sample
+        self.d_pos_params = torch.zeros(6, P, dtype=torch.float32, device=d)
         self.workspace: torch.Tensor | None = None
         self.encoder_cache = None
         if hasattr(model, "embed_multimodal"):
@@ -218,6 +222,26 @@ class ModelRunner:
             self.h_unif[n:B] = 0
         return all_greedy
 
+    def _fill_spec_sampling(self, so: SchedulerOutput, n_sel: int) -> None:
+        """Per verified position: the request's sampling parameters, the draft token to
+        verify (-1 at the bonus position) and two deterministic uniforms."""
+        hp = self.h_pos_params.numpy()
+        j = 0
+        for i, s in enumerate(so.seqs):
+            k = len(s.token_ids)
+            drafts = list(s.spec_token_ids) + [-1]
+            seed = self.seed if s.sampling_params is None or s.sampling_params.seed is None else \
+                s.sampling_params.seed
+            for p in range(k):
+                hp[0, j] = self.h_temp[i]
+                hp[1, j] = self.h_topk[i]
+                hp[2, j] = self.h_topp[i]
+                hp[3, j] = drafts[p] if p < len(drafts) else -1
+                hp[4, j] = request_uniform(seed, f"{s.req_id}/accept{p}", s.sample_seq)
+                hp[5, j] = request_uniform(seed, f"{s.req_id}/sample{p}", s.sample_seq)
+                j += 1
+        self.d_pos_params[:, :n_sel].copy_(self.h_pos_params[:, :n_sel], non_blocking=True)
+
     def _prepare(self, so: SchedulerOutput, pad_to: int | None) -> tuple[AttentionMetadata, int, int, bool]:
         seqs = so.seqs
         n = len(seqs)
@@ -273,6 +297,8 @@ class ModelRunner:
                 n_sel += 1
             T += B - n
         greedy = self._fill_sampling(so, B)
+        if so.kind == "decode" and n_sel > B and not greedy:
+            self._fill_spec_sampling(so, n_sel)
         extras = self._mm_extras(so) if (has_mrope and self.encoder_cache is not None) else {}
         if self.state_caches is not None:
             hs, hi = self.h_sslot.numpy(), self.h_sinit.numpy()
@@ -355,8 +381,14 @@ class ModelRunner:
         B = meta.num_seqs
         if n_sel == B:
             tok = self.sampler(logits, self.d_temp[:B], self.d_topk[:B], self.d_topp[:B], self.d_unif[:B], greedy)
-        else:  # speculative verification: greedy at every position
+        elif greedy:  # speculative verification, greedy: accept until the first mismatch
             tok = self.sampler.greedy(logits)
+        else:  # speculative verification with sampling: rejection sampling per position
+            from ..spec_decode.rejection_sampler import rejection_sample
+
+            pp = self.d_pos_params[:, :n_sel]
+            cv, ci = self.sampler.candidates(logits)
+            tok, _ = rejection_sample(cv, ci, pp[3].long(), pp[0], pp[1].int(), pp[2], pp[4], pp[5], self.max_top_k)
         self.d_out[:n_sel].copy_(tok)
         self._last_logits = logits
         return self.d_out[:n_sel]

@@ -53,13 +53,22 @@ class Sampler(nn.Module):
         logits = self._mask_padding(logits)
         if self.group.world_size == 1:
             return ops.sample(logits, temperature, top_k, top_p, uniform, self.max_top_k)
+        cand_v, cand_i = self.candidates(logits, masked=True)
+        pos = ops.sample(cand_v, temperature, top_k, top_p, uniform, self.max_top_k)
+        return cand_i.gather(1, pos[:, None]).squeeze(1).to(torch.int64)
+
+    def candidates(self, logits: torch.Tensor, masked: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
+        """Top-``max_top_k`` candidates of every vocab shard, gathered over the TP group:
+        (logits [B, tp*K] fp32, global vocab ids [B, tp*K] int64).  Any top-k / top-p
+        selection over the full vocabulary is contained in this set."""
+        if not masked:
+            logits = self._mask_padding(logits)
         K = min(self.max_top_k, logits.shape[1])
         vals, ids = torch.topk(logits.float(), K, dim=-1)
         ids = ids + self.vocab_start
+        if self.group.world_size == 1:
+            return vals, ids.to(torch.int64)
         allv = self.group.all_gather(vals.unsqueeze(0), dim=0)  # [tp,B,K]
         alli = self.group.all_gather(ids.unsqueeze(0), dim=0)
         B = logits.shape[0]
-        cand_v = allv.permute(1, 0, 2).reshape(B, -1)
-        cand_i = alli.permute(1, 0, 2).reshape(B, -1)
-        pos = ops.sample(cand_v, temperature, top_k, top_p, uniform, self.max_top_k)
-        return cand_i.gather(1, pos[:, None]).squeeze(1).to(torch.int64)
+        return allv.permute(1, 0, 2).reshape(B, -1), alli.permute(1, 0, 2).reshape(B, -1).to(torch.int64)

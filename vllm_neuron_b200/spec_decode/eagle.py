@@ -1,11 +1,12 @@
 """EAGLE-3 proposer (``vllm/spec_decode/eagle.py:31`` of the Trainium plugin).
 
 Per engine step:
-1. target verification: every running request feeds ``[last, d1..dk]``; the target
-   returns its greedy token at each of the k+1 positions; the longest prefix of drafts
-   that matches is accepted plus one bonus token (``nn/rejection_sampler.py:12``
-   semantics: accept until the first mismatch).  Greedy speculation is lossless: the
-   output equals non-speculative greedy decoding exactly.
+1. target verification: every running request feeds ``[last, d1..dk]``; for greedy
+   requests the target returns its argmax at each of the k+1 positions and the longest
+   matching prefix of drafts is accepted plus one bonus token (``nn/rejection_sampler.py:12``
+   semantics: accept until the first mismatch), so the output equals non-speculative greedy
+   decoding exactly; requests that sample are verified by rejection sampling
+   (``spec_decode/rejection_sampler.py``), which keeps their output distribution.
 2. draft catch-up: the draft layer runs over the positions verified in this step, with
    input token = the token at position p+1 and hidden = fc(target aux hidden at p),
    writing its own KV cache (same block tables as the target);
