@@ -1,0 +1,79 @@
+"""MPExecutor (multi-process test harness) on CPU gloo ranks, including host-side failure
+detection: a rank that raises, a rank that exits, a rank that stops answering."""
+
+import os
+import time
+
+import pytest
+import torch
+
+
+def _allreduce(ctx, base):
+    t = torch.tensor([float(base + ctx.rank)])
+    return ctx.ps.tp.all_reduce(t).item()
+
+
+def _make(ctx, scale):
+    return {"w": scale * (ctx.rank + 1)}
+
+
+def _use(ctx):
+    return ctx.obj["w"]
+
+
+def _layout(ctx):
+    return (ctx.ps.tp.world_size, ctx.ps.dp.world_size)
+
+
+def _raise_on_1(ctx):
+    if ctx.rank == 1:
+        raise ValueError("injected failure")
+    return ctx.rank
+
+
+def _exit_on_1(ctx):
+    if ctx.rank == 1:
+        os._exit(3)
+    return ctx.rank
+
+
+def _stall_on_0(ctx):
+    if ctx.rank == 0:
+        time.sleep(30)
+    return ctx.rank
+
+
+def test_executor_run_load_reinit():
+    from vllm_neuron_b200.utils.executor import MPExecutor
+
+    with MPExecutor(world_size=2, tp=2, timeout_s=60) as ex:
+        assert ex.run(_allreduce, 10) == [21.0, 21.0]
+        ex.load(_make, 3)
+        assert ex.run(_use) == [3, 6]
+        assert ex.run(_layout) == [(2, 1), (2, 1)]
+        ex.reinit(tp=1, dp=2)
+        assert ex.run(_layout) == [(1, 2), (1, 2)]
+
+
+def test_executor_reports_rank_exception():
+    from vllm_neuron_b200.utils.executor import MPExecutor, RankError
+
+    with MPExecutor(world_size=2, tp=2, timeout_s=60) as ex:
+        with pytest.raises(RankError) as ei:
+            ex.run(_raise_on_1)
+        assert ei.value.rank == 1 and "injected failure" in str(ei.value)
+        assert ex.run(_layout) == [(2, 1), (2, 1)]  # the pool survives a task error
+
+
+def test_executor_detects_dead_and_stalled_ranks():
+    from vllm_neuron_b200.utils.executor import MPExecutor, RankError
+
+    ex = MPExecutor(world_size=2, tp=2, timeout_s=60)
+    with pytest.raises(RankError) as ei:
+        ex.run(_exit_on_1)
+    assert ei.value.rank == 1 and "exited" in str(ei.value)
+    ex = MPExecutor(world_size=2, tp=2, timeout_s=4)
+    t0 = time.monotonic()
+    with pytest.raises(RankError) as ei:
+        ex.run(_stall_on_0)
+    assert ei.value.rank == 0 and time.monotonic() - t0 < 20

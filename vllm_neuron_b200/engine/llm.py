@@ -4,7 +4,6 @@
 from __future__ import annotations
 
 import os
-import socket
 from typing import Sequence
 
 import torch.multiprocessing as mp
@@ -15,12 +14,6 @@ from .llm_engine import LLMEngine, _follower_main
 from .sampling_params import RequestOutput, SamplingParams
 
 logger = init_logger(__name__)
-
-
-def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
 
 
 class LLM:
@@ -41,14 +34,18 @@ class LLM:
         self.cfg = cfg
         ws = cfg.world_size
         self._procs = []
+        self._rdzv = None
         if spmd or (ws > 1 and "RANK" in os.environ and int(os.environ.get("WORLD_SIZE", "1")) == ws):
             rank = int(os.environ.get("RANK", "0"))
             local = int(os.environ.get("LOCAL_RANK", rank))
             self.engine = LLMEngine(cfg, rank, ws, local, mode="spmd" if ws > 1 else "single")
         elif ws > 1:
-            port = _free_port()
-            os.environ["MASTER_ADDR"] = "127.0.0.1"
-            os.environ["MASTER_PORT"] = str(port)
+            from ..utils.rendezvous import FileRendezvous
+
+            # ranks meet through a private file store: no port to race for
+            self._rdzv = FileRendezvous()
+            self._rdzv.export()
+            port = 0
             ctx = mp.get_context("spawn")
             for r in range(1, ws):
                 p = ctx.Process(target=_follower_main, args=(cfg, r, ws, port), daemon=True)
@@ -123,6 +120,9 @@ class LLM:
             if p.is_alive():
                 p.terminate()
         self._procs = []
+        if getattr(self, "_rdzv", None) is not None:
+            self._rdzv.close()
+            self._rdzv = None
 
     def __del__(self):  # pragma: no cover
         try:

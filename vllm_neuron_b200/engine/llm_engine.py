@@ -221,9 +221,12 @@ def torch_image(x):
     return t
 
 
-def _follower_main(cfg: EngineConfig, rank: int, world_size: int, master_port: int) -> None:
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(master_port)
+def _follower_main(cfg: EngineConfig, rank: int, world_size: int, master_port: int = 0) -> None:
+    """Entry of a follower rank spawned by ``LLM`` (rendezvous through the file store
+    named in the environment; ``master_port`` only for TCP rendezvous)."""
+    if master_port:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(master_port)
     eng = LLMEngine(cfg, rank, world_size, local_rank=rank, mode="follower")
     try:
         eng.run_follower()

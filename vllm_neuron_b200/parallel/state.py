@@ -304,6 +304,10 @@ def init_distributed_environment(world_size: int = 1, rank: int = 0, backend: st
 
     backend = backend or envs.get_dist_backend()
     if init_method is None:
+        from ..utils.rendezvous import init_method_from_env
+
+        init_method = init_method_from_env()  # file store of ranks spawned on this host
+    if init_method is None:
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         os.environ.setdefault("MASTER_PORT", "29533")
         init_method = "env://"
