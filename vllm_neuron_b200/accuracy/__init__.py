@@ -1,1 +1,5 @@
-"""Accuracy toolkit: tolerance checks, logit validation, tensor capture."""
+"""Accuracy toolkit: tolerance checks (two- and three-way), logit validation against a
+reference model, tensor capture / replacement hooks and KV-cache inspection."""
+
+from .logit_validation import compare_logits, validate_greedy_generation, validate_prompt_logits  # noqa: F401
+from .testing import assert_close, assert_close_three_way, compare  # noqa: F401

@@ -184,6 +184,31 @@ class LLMEngine:
                              [CompletionOutput(0, "", list(req.output_token_ids), reason)], finished,
                              req.metrics, req.num_cached_tokens)
 
+    # ------------------------------------------------------------------ scoring
+    def score(self, prompt_token_ids: list[int]) -> "torch.Tensor":
+        """Logits [len(prompt), vocab] of a prompt (teacher forcing), for accuracy tools.
+        Single-rank and SPMD engines only (every rank must call it)."""
+        import torch  # noqa: F401
+
+        from .scheduler import ScheduledSeq, SchedulerOutput
+
+        if self.mode in ("driver", "follower"):
+            raise RuntimeError("score() needs a single-rank or SPMD engine")
+        if self.scheduler.has_unfinished():
+            raise RuntimeError("score() needs an idle engine")
+        ids = list(map(int, prompt_token_ids))
+        req = Request(f"__score_{uuid.uuid4().hex}", ids, SamplingParams(max_tokens=1))
+        if not self.kv.allocate_slots(req, len(ids)):
+            raise RuntimeError("not enough KV blocks to score the prompt")
+        try:
+            seq = ScheduledSeq(req.request_id, ids, 0, list(req.block_ids), False, request=req)
+            vocab = getattr(self.worker.model_cfg, "vocab_size", None) or self.worker.hf["vocab_size"]
+            return self.worker.runner.score(SchedulerOutput("prefill", [seq]), vocab)
+        finally:
+            self.kv.free(req)
+            if self.worker.runner.state_caches is not None:
+                self.worker.runner.release_state(req.request_id)
+
     # ---------------------------------------------------------------- lifecycle
     def run_follower(self) -> None:
         while not self._stopped:

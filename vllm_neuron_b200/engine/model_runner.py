@@ -144,6 +144,21 @@ class ModelRunner:
         self.h2d_bytes_last = 0
         self.d2h_bytes_last = 0
         self.step_count = 0
+        # accuracy tooling: tensor capture / replacement hooks (eager steps only)
+        self.capture = self.replacer = None
+        rank = tp_group.rank_in_group if hasattr(tp_group, "rank_in_group") else 0
+        if nc.tensor_capture is not None and nc.tensor_capture.modules:
+            from ..accuracy.tensor_capture import TensorCapture
+
+            tc = nc.tensor_capture
+            self.capture = TensorCapture(model, tc.modules, tc.capture_dir, rank, tc.capture_filter)
+            self.use_graphs = False
+        if nc.tensor_replacement is not None:
+            from ..accuracy.tensor_replacement import TensorReplacer
+
+            tensors, _ = nc.tensor_replacement.resolve()
+            self.replacer = TensorReplacer(model, tensors)
+            self.use_graphs = False
 
     def release_state(self, req_id: str) -> None:
         """Return a request's recurrent-state slot (request finished or preempted)."""
@@ -421,6 +436,12 @@ class ModelRunner:
             out_d = self.d_out[:n_sel]
         else:
             out_d = self._forward_sample(meta, T, n_sel, greedy)
+        if self.capture is not None:
+            self.capture.flush({"kind": so.kind, "req_ids": [s.req_id for s in so.seqs],
+                                "start_pos": [s.start_pos for s in so.seqs],
+                                "num_tokens": [len(s.token_ids) for s in so.seqs]})
+        if self.replacer is not None:
+            self.replacer.next_step()
         # D2H of the sampled ids (the step's only device->host traffic)
         self.h_out[:n_sel].copy_(out_d, non_blocking=out_d.is_cuda)
         if out_d.is_cuda:
@@ -439,6 +460,18 @@ class ModelRunner:
             if s.sample:
                 res[s.req_id] = [toks[i]]
         return res
+
+    @torch.inference_mode()
+    def score(self, so: SchedulerOutput, vocab_size: int) -> torch.Tensor:
+        """Logits [T, vocab] of every token of a one-sequence prefill step (all TP vocab
+        shards gathered); used by the accuracy tools."""
+        meta, T, _, _ = self._prepare(so, None)
+        h = self.model(self.d_ids[:T], self.d_pos[:T], meta, self.kv_caches)
+        logits = self.model.compute_logits(h).float()
+        g = self.sampler.group
+        if g.world_size > 1:
+            logits = g.all_gather(logits, dim=-1)
+        return logits[:, :vocab_size]
 
     def _capture(self, B: int, greedy: bool, meta: AttentionMetadata, T: int, n_sel: int) -> _GraphEntry:
         t0 = time.time()
