@@ -40,8 +40,8 @@ class AsyncLLM:
                 while True:
                     kind, payload = self._in.get_nowait()
                     if kind == "add":
-                        rid, ids, sp, mm = payload
-                        self.engine.add_request(rid, ids, sp, mm_inputs=mm)
+                        rid, ids, sp, mm, kvp = payload
+                        self.engine.add_request(rid, ids, sp, mm_inputs=mm, kv_transfer_params=kvp)
                     elif kind == "abort":
                         self.engine.abort_request(payload)
             except queue.Empty:
@@ -73,13 +73,14 @@ class AsyncLLM:
                             self._streams.pop(o.request_id, None)
 
     async def generate(self, prompt_token_ids: list[int], sampling_params: SamplingParams,
-                       request_id: str | None = None, mm_inputs: list | None = None) -> AsyncIterator[RequestOutput]:
+                       request_id: str | None = None, mm_inputs: list | None = None,
+                       kv_transfer_params: dict | None = None) -> AsyncIterator[RequestOutput]:
         rid = request_id or uuid.uuid4().hex
         loop = asyncio.get_running_loop()
         q: asyncio.Queue = asyncio.Queue()
         with self._lock:
             self._streams[rid] = (loop, q)
-        self._in.put(("add", (rid, list(prompt_token_ids), sampling_params, mm_inputs)))
+        self._in.put(("add", (rid, list(prompt_token_ids), sampling_params, mm_inputs, kv_transfer_params)))
         try:
             while True:
                 item = await q.get()

@@ -73,6 +73,7 @@ class LLM:
                  sampling_params: SamplingParams | Sequence[SamplingParams] | None = None,
                  prompt_token_ids: Sequence[Sequence[int]] | None = None, use_tqdm: bool = False,
                  multi_modal_data: Sequence[dict] | None = None) -> list[RequestOutput]:
+        kvps = None
         if prompt_token_ids is None:
             if prompts is None:
                 raise ValueError("either prompts or prompt_token_ids is required")
@@ -81,6 +82,7 @@ class LLM:
             if prompts and isinstance(prompts[0], dict):  # {"prompt_token_ids": [...]} items
                 prompt_token_ids = [p["prompt_token_ids"] for p in prompts]
                 multi_modal_data = [p.get("multi_modal_data") for p in prompts]
+                kvps = [p.get("kv_transfer_params") for p in prompts]
                 prompts = None
             else:
                 tok = self.get_tokenizer()
@@ -95,7 +97,8 @@ class LLM:
             self._counter += 1
             mm = multi_modal_data[i] if multi_modal_data else None
             self.engine.add_request(rid, list(ptoks), sps[i], prompt=prompts[i] if prompts else None,
-                                    mm_inputs=[mm] if mm else None)
+                                    mm_inputs=[mm] if mm else None,
+                                    kv_transfer_params=kvps[i] if kvps else None)
             ids.append(rid)
         results: dict[str, RequestOutput] = {}
         while self.engine.has_unfinished_requests():

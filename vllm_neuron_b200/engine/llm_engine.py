@@ -64,6 +64,9 @@ class LLMEngine:
             self.scheduler.on_preempt.append(self.worker.runner.release_state)
         hf = self.worker.hf
         self.eos_token_id = hf.get("eos_token_id")
+        self.connector = None
+        if cfg.kv_transfer_config is not None:
+            self._init_connector(hf)
         self._pending: list[tuple] = []
         self._stopped = False
         logger.info("engine ready: rank %d/%d mode=%s kv_blocks=%d", rank, world_size, mode, n_blocks)
@@ -125,6 +128,22 @@ class LLMEngine:
             req.mrope_positions, req.mrope_delta = model.mrope_positions(out, grids)
         return req
 
+    def _init_connector(self, hf: dict) -> None:
+        from ..kv_transfer import make_connector
+        from ..models.base import kv_head_sharding
+
+        extra = self.cfg.kv_transfer_config.kv_connector_extra_config
+        if not extra.get("engine_id"):
+            eid = uuid.uuid4().hex[:12]
+            if self.world_size > 1:  # every rank of this engine names its transfers alike
+                eid = self.worker.ps.world.broadcast_object(eid)
+            extra["engine_id"] = eid
+        tp = self.worker.ps.tp
+        n_kv = hf.get("num_key_value_heads") or hf.get("num_attention_heads") or 1
+        rng = kv_head_sharding(n_kv, tp.world_size, tp.rank_in_group)
+        self.connector = make_connector(self.cfg, self.worker.runner, tp.rank_in_group, tp.world_size, rng)
+        self.scheduler.connector = self.connector
+
     def abort_request(self, request_id: str) -> None:
         if self.mode == "driver":
             self._pending.append(("abort", request_id))
@@ -154,8 +173,10 @@ class LLMEngine:
         if self._stopped:
             return []
         so = self.scheduler.schedule()
+        failed = [self._make_output(r, True) for r in self.scheduler.failed]
+        self.scheduler.failed = []
         if so.kind == "idle":
-            return []
+            return failed
         if self.proposer is not None and so.kind == "decode":
             sampled = self.proposer.execute_with_speculation(so)
         else:
@@ -170,7 +191,7 @@ class LLMEngine:
             if s.req_id in sampled or s.req_id in fin_ids:
                 req = s.request
                 outs.append(self._make_output(req, req.status.finished))
-        return outs
+        return failed + outs
 
     def _make_output(self, req: Request, finished: bool) -> RequestOutput:
         reason = None
@@ -182,7 +203,7 @@ class LLMEngine:
             reason = "abort"
         return RequestOutput(req.request_id, req.prompt, req.prompt_token_ids,
                              [CompletionOutput(0, "", list(req.output_token_ids), reason)], finished,
-                             req.metrics, req.num_cached_tokens)
+                             req.metrics, req.num_cached_tokens, req.kv_transfer_params_out)
 
     # ------------------------------------------------------------------ scoring
     def score(self, prompt_token_ids: list[int]) -> "torch.Tensor":
@@ -219,6 +240,8 @@ class LLMEngine:
             self._pending.append(("shutdown",))
             self._sync_requests()
         self._stopped = True
+        if self.connector is not None:
+            self.connector.cleanup()
         self.worker.shutdown()
 
     # -------------------------------------------------------------- statistics

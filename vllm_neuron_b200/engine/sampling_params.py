@@ -65,3 +65,4 @@ class RequestOutput:
     finished: bool
     metrics: RequestMetrics | None = None
     num_cached_tokens: int = 0
+    kv_transfer_params: dict | None = None

@@ -82,6 +82,8 @@ class Scheduler:
         self._finished_ids: list[str] = []
         self.on_finish: list = []  # callbacks(request_id), e.g. encoder-cache release
         self.on_preempt: list = []  # callbacks(request_id), e.g. recurrent-state slot release
+        self.connector = None  # KV-transfer connector (disaggregated prefill / decode)
+        self.failed: list[Request] = []  # aborted at admission; the engine reports them
 
     # ------------------------------------------------------------------ queue
     def add_request(self, req: Request) -> None:
@@ -103,6 +105,11 @@ class Scheduler:
         return bool(self.waiting or self.running)
 
     def _finish(self, req: Request) -> None:
+        c = self.connector
+        if (c is not None and c.is_producer and (req.kv_transfer_params or {}).get("do_remote_decode")
+                and req.status != RequestStatus.FINISHED_ABORTED and req.block_ids):
+            # hand the prompt KV to the decode engine before the blocks are freed
+            req.kv_transfer_params_out = c.export(req.request_id, req.block_ids, req.num_prompt_tokens)
         for cb in self.on_finish:
             cb(req.request_id)
         if req in self.running:
@@ -136,13 +143,32 @@ class Scheduler:
             admitted = 0
             while self.waiting and admitted < self.max_prefills and self.can_admit():
                 req = self.waiting[0]
-                blocks, n_cached = self.kv.get_computed_blocks(req)
-                req.num_computed_tokens = n_cached
-                req.num_cached_tokens = n_cached
-                n_new = self._prefill_chunk(req)
-                if not self.kv.allocate_slots(req, n_new, blocks):
+                remote = self._remote_prefill_tokens(req)
+                if remote > 0:
+                    # disaggregated decode: the prompt KV (all but the last token) comes from the
+                    # prefill engine; this engine computes only the last prompt token
                     req.num_computed_tokens = 0
-                    break
+                    if not self.kv.allocate_slots(req, req.num_prompt_tokens):
+                        break
+                    try:
+                        self.connector.load(req.kv_transfer_params, req.block_ids, remote)
+                    except Exception as e:  # noqa: BLE001  (missing / malformed transfer)
+                        logger.error("request %s: KV transfer failed: %s", req.request_id, e)
+                        self.waiting.popleft()
+                        req.status = RequestStatus.FINISHED_ABORTED
+                        self._finish(req)
+                        self.failed.append(req)
+                        continue
+                    req.num_computed_tokens = remote
+                    req.num_cached_tokens = remote
+                else:
+                    blocks, n_cached = self.kv.get_computed_blocks(req)
+                    req.num_computed_tokens = n_cached
+                    req.num_cached_tokens = n_cached
+                    n_new = self._prefill_chunk(req)
+                    if not self.kv.allocate_slots(req, n_new, blocks):
+                        req.num_computed_tokens = 0
+                        break
                 self.waiting.popleft()
                 req.status = RequestStatus.RUNNING
                 if req.metrics.first_scheduled_time is None:
@@ -195,6 +221,12 @@ class Scheduler:
         if not seqs:
             return SchedulerOutput("idle", [], preempted, finished)
         return SchedulerOutput("decode", seqs, preempted, finished)
+
+    def _remote_prefill_tokens(self, req: Request) -> int:
+        p = req.kv_transfer_params or {}
+        if self.connector is None or not self.connector.is_consumer or not p.get("do_remote_prefill"):
+            return 0
+        return max(0, min(int(p.get("num_tokens", 0)), req.num_prompt_tokens) - 1)
 
     def _budget_left(self, pre: list[Request]) -> int:
         return self.max_num_batched_tokens - sum(self._prefill_chunk(r) for r in pre)

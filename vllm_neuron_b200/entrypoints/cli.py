@@ -64,8 +64,17 @@ def main(argv=None) -> None:
     b.add_argument("--random-input-len", type=int, default=1024)
     b.add_argument("--random-output-len", type=int, default=128)
     b.add_argument("--vocab", type=int, default=32000)
+    x = sub.add_parser("disagg-proxy", help="router for one prefill and one decode server")
+    x.add_argument("--prefill", required=True, help="prefill server base URL (kv_producer)")
+    x.add_argument("--decode", required=True, help="decode server base URL (kv_consumer)")
+    x.add_argument("--host", default="127.0.0.1")
+    x.add_argument("--port", type=int, default=8000)
     a = ap.parse_args(argv)
-    if a.cmd == "serve":
+    if a.cmd == "disagg-proxy":
+        from .disagg_proxy import serve_proxy
+
+        serve_proxy(a.prefill, a.decode, a.host, a.port)
+    elif a.cmd == "serve":
         from .openai_server import serve
 
         serve(engine_kwargs(a), a.host, a.port, a.served_model_name)

@@ -85,7 +85,7 @@ def build_app(engine: AsyncLLM, served_name: str):
         state["prof"] = None
         return {"status": "stopped", "trace": path}
 
-    async def _complete(ids, sp, stream: bool, chat: bool, rid: str):
+    async def _complete(ids, sp, stream: bool, chat: bool, rid: str, kvp: dict | None = None):
         created = int(time.time())
         obj = "chat.completion" if chat else "text_completion"
 
@@ -98,7 +98,7 @@ def build_app(engine: AsyncLLM, served_name: str):
         if stream:
             async def gen():
                 sent = 0
-                async for o in engine.generate(ids, sp, rid):
+                async for o in engine.generate(ids, sp, rid, kv_transfer_params=kvp):
                     toks = o.outputs[0].token_ids
                     new = toks[sent:]
                     sent = len(toks)
@@ -112,20 +112,23 @@ def build_app(engine: AsyncLLM, served_name: str):
 
             return StreamingResponse(gen(), media_type="text/event-stream")
         final = None
-        async for o in engine.generate(ids, sp, rid):
+        async for o in engine.generate(ids, sp, rid, kv_transfer_params=kvp):
             final = o
         toks = final.outputs[0].token_ids
-        return {"id": rid, "object": obj, "created": created, "model": served_name,
+        resp = {"id": rid, "object": obj, "created": created, "model": served_name,
                 "choices": [choice(detok(toks), toks, final.outputs[0].finish_reason)],
                 "usage": {"prompt_tokens": len(ids), "completion_tokens": len(toks),
                           "total_tokens": len(ids) + len(toks)}}
+        if final.kv_transfer_params is not None:
+            resp["kv_transfer_params"] = final.kv_transfer_params
+        return resp
 
     @app.post("/v1/completions")
     async def completions(req: Request):
         body = await req.json()
         ids, _ = tokenize(body["prompt"])
         return await _complete(ids, _sampling_from(body), bool(body.get("stream", False)), False,
-                               f"cmpl-{uuid.uuid4().hex}")
+                               f"cmpl-{uuid.uuid4().hex}", body.get("kv_transfer_params"))
 
     @app.post("/v1/chat/completions")
     async def chat(req: Request):

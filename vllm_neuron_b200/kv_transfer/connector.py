@@ -1,0 +1,167 @@
+"""KV-cache connector for disaggregated inference (1 prefill engine, 1 decode engine).
+
+Counterpart of the Trainium plugin's NIXL connector (``vllm/kv_connector/neuron_nixl_connector.py``)
+for engines on one host.  Protocol (vLLM's ``kv_transfer_params``):
+
+* the prefill engine (``kv_role`` producer) gets a request with
+  ``{"do_remote_decode": True}``; when the request finishes (the proxy asks for one token)
+  its prompt KV is exported before the blocks are freed, and the request output carries
+  ``{"do_remote_prefill": True, "transfer_id", "num_tokens", "remote_tp_size", "remote_engine_id"}``;
+* the decode engine (``kv_role`` consumer) gets the request with those params; at admission
+  it allocates blocks for the whole prompt, loads the KV of positions ``[0, num_tokens - 1)``
+  and computes only the last prompt token itself (that step samples the first output token).
+
+Transport ``HostStagedConnector``: each producer rank writes its KV heads of the request (raw
+cache dtype, so the transfer is byte-exact) to one file in a shared store directory
+(``kv_connector_extra_config.store_path``, default a directory under /dev/shm), atomically
+renamed into place; consumer ranks read the files of every producer rank and take the
+global kv heads they own, so producer and consumer may use different TP degrees (the
+reference's head-ratio mapping).  A consumer waits for the files at most ``timeout_s``
+(``kv_connector_extra_config.timeout_s``, default 30 s); a missing or malformed transfer
+raises :class:`KVTransferError`, and the engine aborts that request instead of blocking.  The
+producer removes its exports after ``ttl_s`` (default 600 s).
+"""
+
+from __future__ import annotations
+
+import os
+import time
+
+import torch
+
+from ..logging_config import init_logger
+
+logger = init_logger(__name__)
+
+
+class KVTransferError(RuntimeError):
+    pass
+
+
+class HostStagedConnector:
+    def __init__(self, kv_caches: list, kv_head_range: tuple[int, int], block_size: int, rank: int, tp_size: int,
+                 engine_id: str, role: str, extra: dict | None = None):
+        extra = extra or {}
+        self.store = extra.get("store_path") or os.path.join("/dev/shm" if os.path.isdir("/dev/shm") else "/tmp",
+                                                             "vllm_b200_kv")
+        os.makedirs(self.store, exist_ok=True)
+        self.timeout_s = float(extra.get("timeout_s", 30.0))
+        self.ttl_s = float(extra.get("ttl_s", 600.0))  # exported transfers older than this are removed
+        self.cleanup_on_shutdown = bool(extra.get("cleanup_on_shutdown", False))
+        self.kv = kv_caches
+        self.h0, self.nh = kv_head_range
+        self.bs = block_size
+        self.rank, self.tp = rank, tp_size
+        self.engine_id = engine_id
+        self.role = role
+        self.exported: list[str] = []
+        self.stats = {"exported": 0, "loaded": 0, "failed": 0, "bytes": 0}
+
+    @property
+    def is_producer(self) -> bool:
+        return self.role in ("kv_producer", "kv_both")
+
+    @property
+    def is_consumer(self) -> bool:
+        return self.role in ("kv_consumer", "kv_both")
+
+    def _path(self, transfer_id: str, rank: int) -> str:
+        return os.path.join(self.store, f"{transfer_id}.rank{rank}.pt")
+
+    def _layers(self):
+        return [(i, kv) for i, kv in enumerate(self.kv) if kv is not None]
+
+    # ----------------------------------------------------------------- producer
+    def export(self, request_id: str, block_ids: list[int], num_tokens: int) -> dict:
+        """Write this rank's KV of positions [0, num_tokens) and return the params the
+        decode engine needs."""
+        tid = f"{self.engine_id}-{request_id}"
+        self._gc()
+        nb = -(-num_tokens // self.bs)
+        idx = torch.tensor(block_ids[:nb], dtype=torch.long, device=self.kv[self._layers()[0][0]][0].device)
+        layers = {}
+        for i, (kc, vc) in self._layers():
+            k = kc.index_select(0, idx).permute(0, 2, 1, 3).reshape(nb * self.bs, kc.shape[1], kc.shape[3])
+            v = vc.index_select(0, idx).permute(0, 2, 1, 3).reshape(nb * self.bs, vc.shape[1], vc.shape[3])
+            layers[i] = (k[:num_tokens].cpu().contiguous(), v[:num_tokens].cpu().contiguous())
+            self.stats["bytes"] += layers[i][0].numel() * layers[i][0].element_size() * 2
+        tmp = self._path(tid, self.rank) + f".tmp{os.getpid()}"
+        torch.save({"num_tokens": num_tokens, "heads": (self.h0, self.nh), "layers": layers}, tmp)
+        os.replace(tmp, self._path(tid, self.rank))
+        self.exported.append((tid, time.monotonic()))
+        self.stats["exported"] += 1
+        return {"do_remote_prefill": True, "transfer_id": tid, "num_tokens": num_tokens,
+                "remote_tp_size": self.tp, "remote_engine_id": self.engine_id}
+
+    # ----------------------------------------------------------------- consumer
+    def load(self, params: dict, block_ids: list[int], num_tokens: int) -> None:
+        """Write the remote KV of positions [0, num_tokens) into this engine's blocks."""
+        tid = params.get("transfer_id")
+        ptp = int(params.get("remote_tp_size", 1))
+        if not tid:
+            raise KVTransferError("kv_transfer_params without transfer_id")
+        deadline = time.monotonic() + self.timeout_s
+        paths = [self._path(tid, r) for r in range(ptp)]
+        while not all(os.path.exists(p) for p in paths):
+            if time.monotonic() > deadline:
+                self.stats["failed"] += 1
+                raise KVTransferError(f"KV transfer {tid} not available after {self.timeout_s:.1f}s")
+            time.sleep(0.002)
+        parts = [torch.load(p, weights_only=False) for p in paths]
+        if any(pt["num_tokens"] < num_tokens for pt in parts):
+            raise KVTransferError(f"KV transfer {tid} holds fewer than {num_tokens} tokens")
+        pos = torch.arange(num_tokens)
+        blk = torch.tensor(block_ids, dtype=torch.long)[pos // self.bs]
+        off = pos % self.bs
+        for i, (kc, vc) in self._layers():
+            ks, vs = [], []
+            for h in range(self.h0, self.h0 + self.nh):  # global kv head -> the part that holds it
+                src = next((pt for pt in parts if pt["heads"][0] <= h < pt["heads"][0] + pt["heads"][1]), None)
+                if src is None or i not in src["layers"]:
+                    raise KVTransferError(f"KV transfer {tid}: no data for layer {i} kv head {h}")
+                j = h - src["heads"][0]
+                ks.append(src["layers"][i][0][:num_tokens, j])
+                vs.append(src["layers"][i][1][:num_tokens, j])
+            k = torch.stack(ks, 1).to(kc.device, kc.dtype)
+            v = torch.stack(vs, 1).to(vc.device, vc.dtype)
+            kc[blk.to(kc.device), :, off.to(kc.device)] = k
+            vc[blk.to(vc.device), :, off.to(vc.device)] = v
+        self.stats["loaded"] += 1
+
+    def _gc(self) -> None:
+        now = time.monotonic()
+        keep = []
+        for tid, t in self.exported:
+            if now - t > self.ttl_s:
+                try:
+                    os.remove(self._path(tid, self.rank))
+                except OSError:
+                    pass
+            else:
+                keep.append((tid, t))
+        self.exported = keep
+
+    def cleanup(self) -> None:
+        """Engine shutdown: remove this rank's exports if configured (otherwise they stay
+        for a decode engine that has not read them yet, until ``ttl_s`` on a later run)."""
+        if not self.cleanup_on_shutdown:
+            return
+        for tid, _ in self.exported:
+            try:
+                os.remove(self._path(tid, self.rank))
+            except OSError:
+                pass
+        self.exported = []
+
+
+def make_connector(cfg, runner, rank: int, tp_size: int, kv_head_range: tuple[int, int]):
+    kt = cfg.kv_transfer_config
+    if kt is None:
+        return None
+    name = kt.kv_connector
+    if name not in ("B200IpcConnector", "HostStagedConnector", "NixlConnector", "NeuronNixlConnector"):
+        raise ValueError(f"unsupported kv_connector {name!r}")
+    extra = dict(kt.kv_connector_extra_config or {})
+    engine_id = extra.get("engine_id") or f"eng{os.getpid()}"
+    return HostStagedConnector(runner.kv_caches, kv_head_range, cfg.block_size, rank, tp_size, engine_id,
+                               kt.kv_role, extra)

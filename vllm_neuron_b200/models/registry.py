@@ -15,7 +15,8 @@ _MODELS: dict[str, tuple[str, str, str]] = {
     "Qwen3VLForConditionalGeneration": ("qwen3_vl", "Qwen3VLForConditionalGeneration", "Qwen3VLConfig"),
     "Qwen3NextForCausalLM": ("qwen3_next", "Qwen3NextForCausalLM", "Qwen3NextConfig"),
 }
-_SYNTHETIC = {"SyntheticModel": ("synthetic", "SyntheticModel", "SyntheticConfig")}
+_SYNTHETIC = {"SyntheticModel": ("synthetic", "SyntheticModel", "SyntheticConfig"),
+              "SyntheticNeuronModel": ("synthetic", "SyntheticModel", "SyntheticConfig")}
 
 
 def get_models() -> dict[str, tuple[str, str, str]]:
