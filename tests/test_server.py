@@ -53,3 +53,26 @@ def test_cli_engine_kwargs():
                        "--additional-config", '{"neuron_config": {"ep_degree": 8}}'])
     kw = cli.engine_kwargs(a)
     assert kw["tensor_parallel_size"] == 8 and kw["additional_config"]["neuron_config"]["ep_degree"] == 8
+
+
+def test_profile_endpoints(client, tmp_path, monkeypatch):
+    r = client.post("/start_profile")
+    assert r.json()["status"] == "started"
+    assert client.post("/start_profile").status_code == 400  # already running
+    client.post("/v1/completions", json={"prompt": [5, 6, 7], "max_tokens": 2, "temperature": 0})
+    r = client.post("/stop_profile").json()
+    assert r["status"] == "stopped" and r["steps"] >= 2
+    import os
+
+    assert os.path.exists(r["trace"]) and os.path.exists(r["summary"])
+    assert client.post("/stop_profile").status_code == 400
+
+
+def test_profiler_config_aliases():
+    from vllm_neuron_b200.profiler import ProfilerConfig
+
+    c = ProfilerConfig.from_dict({"activities": ["device_profile", "system_profile"], "output_dir": "/tmp/x",
+                                  "neuron_cores": [0]})
+    assert c.activities == ["cpu", "cuda"] and c.output_dir == "/tmp/x"
+    with pytest.raises(ValueError):
+        ProfilerConfig.from_dict({"activities": ["npu"]})

@@ -224,6 +224,7 @@ class EngineConfig:
     vision_neuron_config: VisionNeuronConfig = field(default_factory=VisionNeuronConfig)
     mm_language_model_only: bool = False
     served_model_name: str | None = None
+    profiler_config: dict | None = None
 
     @classmethod
     def create(cls, **kwargs: Any) -> "EngineConfig":
@@ -239,6 +240,12 @@ class EngineConfig:
             cfg.neuron_config = NeuronConfig.from_dict(extra["neuron_config"])
         if "vision_neuron_config" in extra:
             cfg.vision_neuron_config = VisionNeuronConfig.from_dict(extra["vision_neuron_config"])
+        prof = extra.get("neuron_profiler", extra.get("profiler"))
+        if prof is not None:
+            from .profiler import ProfilerConfig
+
+            ProfilerConfig.from_dict(prof)  # validate early
+            cfg.profiler_config = dict(prof)
         if "mm_language_model_only" in extra:
             cfg.mm_language_model_only = bool(extra["mm_language_model_only"])
         if isinstance(cfg.speculative_config, dict):

@@ -44,6 +44,13 @@ class AsyncLLM:
                         self.engine.add_request(rid, ids, sp, mm_inputs=mm, kv_transfer_params=kvp)
                     elif kind == "abort":
                         self.engine.abort_request(payload)
+                    elif kind == "call":
+                        fn, box, done = payload
+                        try:
+                            box.append(fn(self.engine))
+                        except Exception as e:  # noqa: BLE001
+                            box.append(e)
+                        done.set()
             except queue.Empty:
                 pass
             if not self.engine.has_unfinished_requests():
@@ -92,6 +99,17 @@ class AsyncLLM:
         except asyncio.CancelledError:
             self._in.put(("abort", rid))
             raise
+
+    def call(self, fn, timeout: float = 60.0):
+        """Run ``fn(engine)`` on the engine thread between steps and return its result."""
+        box: list = []
+        done = threading.Event()
+        self._in.put(("call", (fn, box, done)))
+        if not done.wait(timeout):
+            raise RuntimeError("engine did not answer")
+        if isinstance(box[0], Exception):
+            raise box[0]
+        return box[0]
 
     def abort(self, request_id: str) -> None:
         self._in.put(("abort", request_id))

@@ -116,6 +116,13 @@ class LLM:
                 pass
         return outs
 
+    def start_profile(self) -> None:
+        """Record the following engine steps (see ``vllm_neuron_b200.profiler``)."""
+        self.engine.start_profile()
+
+    def stop_profile(self) -> dict:
+        return self.engine.stop_profile()
+
     def shutdown(self) -> None:
         self.engine.shutdown()
         for p in self._procs:

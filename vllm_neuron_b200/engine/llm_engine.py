@@ -64,6 +64,9 @@ class LLMEngine:
             self.scheduler.on_preempt.append(self.worker.runner.release_state)
         hf = self.worker.hf
         self.eos_token_id = hf.get("eos_token_id")
+        from ..profiler import Profiler, ProfilerConfig
+
+        self.profiler = Profiler(ProfilerConfig.from_dict(cfg.profiler_config), rank)
         self.connector = None
         if cfg.kv_transfer_config is not None:
             self._init_connector(hf)
@@ -144,6 +147,16 @@ class LLMEngine:
         self.connector = make_connector(self.cfg, self.worker.runner, tp.rank_in_group, tp.world_size, rng)
         self.scheduler.connector = self.connector
 
+    def start_profile(self) -> None:
+        if self.mode == "driver":
+            self._pending.append(("profile", True))
+        self.profiler.start()
+
+    def stop_profile(self) -> dict:
+        if self.mode == "driver":
+            self._pending.append(("profile", False))
+        return self.profiler.stop()
+
     def abort_request(self, request_id: str) -> None:
         if self.mode == "driver":
             self._pending.append(("abort", request_id))
@@ -165,10 +178,16 @@ class LLMEngine:
                     self.scheduler.add_request(self._make_request(rid, ids, sp, prompt, mm, kvp))
                 elif m[0] == "abort":
                     self.scheduler.abort(m[1])
+                elif m[0] == "profile":
+                    if m[1]:
+                        self.profiler.start()
+                    else:
+                        self.profiler.stop()
                 elif m[0] == "shutdown":
                     self._stopped = True
 
     def step(self) -> list[RequestOutput]:
+        self.profiler.step()
         self._sync_requests()
         if self._stopped:
             return []

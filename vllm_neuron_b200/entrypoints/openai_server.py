@@ -64,26 +64,19 @@ def build_app(engine: AsyncLLM, served_name: str):
 
     @app.post("/start_profile")
     async def start_profile():
-        import torch
-
-        prof = torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CPU,
-                                                  torch.profiler.ProfilerActivity.CUDA])
-        prof.__enter__()
-        state["prof"] = prof
+        try:
+            engine.call(lambda e: e.start_profile())
+        except RuntimeError as e:
+            return JSONResponse({"error": str(e)}, status_code=400)
         return {"status": "started"}
 
     @app.post("/stop_profile")
     async def stop_profile():
-        prof = state.get("prof")
-        if prof is None:
-            return JSONResponse({"error": "profiler not running"}, status_code=400)
-        prof.__exit__(None, None, None)
-        out = os.environ.get("VLLM_B200_PROFILE_DIR", "/tmp/vllm_b200_profile")
-        os.makedirs(out, exist_ok=True)
-        path = os.path.join(out, f"trace_{int(time.time())}.json")
-        prof.export_chrome_trace(path)
-        state["prof"] = None
-        return {"status": "stopped", "trace": path}
+        try:
+            res = engine.call(lambda e: e.stop_profile())
+        except RuntimeError as e:
+            return JSONResponse({"error": str(e)}, status_code=400)
+        return {"status": "stopped", **res}
 
     async def _complete(ids, sp, stream: bool, chat: bool, rid: str, kvp: dict | None = None):
         created = int(time.time())
