@@ -1,0 +1,60 @@
+"""Host utilities: cgroup-aware memory, dtypes, vision block packing, golden cache, topology
+parsing (CPU only)."""
+
+import torch
+
+
+def test_cgroup_memory(tmp_path):
+    from vllm_neuron_b200.utils.memory import get_available_memory_bytes
+
+    cg = tmp_path / "cg"
+    cg.mkdir()
+    (cg / "memory.max").write_text(str(8 << 30))
+    (cg / "memory.current").write_text(str(3 << 30))
+    mi = tmp_path / "meminfo"
+    mi.write_text("MemTotal: 100000000 kB\nMemAvailable: 50000000 kB\n")
+    assert get_available_memory_bytes(str(cg), str(mi)) == 5 << 30
+    (cg / "memory.max").write_text("max")
+    assert get_available_memory_bytes(str(cg), str(mi)) == 50000000 * 1024
+
+
+def test_dtypes():
+    from vllm_neuron_b200.utils.dtype_utils import element_size, to_torch_dtype, ulp
+
+    assert to_torch_dtype("bf16") is torch.bfloat16 and element_size("fp8") == 1
+    assert ulp(1.0, torch.bfloat16) == 2 ** -7
+
+
+def test_vision_packing():
+    from vllm_neuron_b200.utils.vision_utils import pack_sequences
+
+    lens = [900, 300, 700, 100, 2500, 64]
+    blocks = pack_sequences(lens, 1024)
+    assert sorted(i for b in blocks for i in b) == list(range(len(lens)))
+    for b in blocks:
+        assert len(b) == 1 or sum(lens[i] for i in b) <= 1024
+    assert len(blocks) == 4
+
+
+def test_golden_cache(tmp_path, monkeypatch):
+    from vllm_neuron_b200.utils.golden_cache import get_or_compute, golden_key
+
+    monkeypatch.setenv("VLLM_B200_GOLDEN_CACHE", str(tmp_path))
+    calls = []
+    k = golden_key(model="tiny", prompts=[[1, 2]])
+    f = lambda: calls.append(1) or torch.arange(3)  # noqa: E731
+    assert get_or_compute(k, f).tolist() == [0, 1, 2]
+    assert get_or_compute(k, f).tolist() == [0, 1, 2] and len(calls) == 1
+
+
+def test_topology_parse():
+    from vllm_neuron_b200.utils.hardware_config import all_nvlink, parse_topology
+
+    text = ("\tGPU0\tGPU1\tNIC0\tCPU Affinity\tNUMA Affinity\tGPU NUMA ID\n"
+            "GPU0\t X \tNV18\tPIX\t0-55\t0\t\tN/A\n"
+            "GPU1\tNV18\t X \tSYS\t56-111\t1\t\tN/A\n"
+            "NIC0\tPIX\tSYS\t X \n")
+    g = parse_topology(text)
+    assert [x.index for x in g] == [0, 1] and g[0].peer_links == {1: "NV18"}
+    assert g[0].nics == ["NIC0"] and g[1].nics == [] and g[0].numa_node == 0 and g[1].cpu_affinity == "56-111"
+    assert all_nvlink(g)
