@@ -51,16 +51,19 @@ def _hf_greedy(m, prompts, n_new):
     return outs
 
 
-@pytest.mark.parametrize("tp", [1, 2])
-def test_greedy_matches_hf(ckpt, tp):
+@pytest.mark.parametrize("tp,dp", [(1, 1), (2, 1), (1, 2)])
+def test_greedy_matches_hf(ckpt, tp, dp):
+    """dp=2: two data-parallel replicas in lockstep with the experts shared across them
+    (tokens all-gathered / reduce-scattered over DP around the MoE); 5 prompts so one
+    replica runs padding steps while the other still works."""
     from vllm_neuron_b200 import LLM, SamplingParams
 
     path, hf = ckpt
-    prompts = workload(n=4 if tp == 2 else 6)
+    prompts = workload(n=4 if tp == 2 else (5 if dp == 2 else 6))
     n_new = 16
     want = _hf_greedy(hf, prompts, n_new)
     llm = LLM(model=path, dtype="float32", max_model_len=512, max_num_seqs=16, max_num_batched_tokens=256,
-              block_size=16, device="cpu", tensor_parallel_size=tp,
+              block_size=16, device="cpu", tensor_parallel_size=tp, data_parallel_size=dp,
               additional_config={"neuron_config": {"quantization": "bf16"}})
     try:
         outs = llm.generate(prompt_token_ids=prompts,

@@ -42,6 +42,8 @@ class LLMEngine:
         n_blocks = self.worker.determine_num_blocks()
         self.worker.initialize_cache(n_blocks)
         self.proposer = None
+        if cfg.speculative_config is not None and cfg.data_parallel_size > 1:
+            raise ValueError("speculative decoding with data_parallel_size > 1 is not supported")
         if cfg.speculative_config is not None:
             from ..spec_decode.eagle import EagleProposer
 
@@ -72,6 +74,12 @@ class LLMEngine:
             self._init_connector(hf)
         self._pending: list[tuple] = []
         self._stopped = False
+        # data parallelism: requests are dealt round-robin to replicas (same order on every
+        # rank); outputs are exchanged over the DP group every step
+        self.dp = cfg.data_parallel_size
+        self.replica = rank // cfg.tensor_parallel_size
+        self._rr = 0
+        self._remote: set[str] = set()  # unfinished requests owned by other replicas
         logger.info("engine ready: rank %d/%d mode=%s kv_blocks=%d", rank, world_size, mode, n_blocks)
 
     # ------------------------------------------------------------------ intake
@@ -83,8 +91,16 @@ class LLMEngine:
         if self.mode == "driver":
             self._pending.append(("add", rid, req.prompt_token_ids, sampling_params, prompt, mm_inputs,
                                   kv_transfer_params))
-        self.scheduler.add_request(req)
+        self._admit(req)
         return rid
+
+    def _admit(self, req: Request) -> None:
+        owner = self._rr
+        self._rr = (self._rr + 1) % self.dp
+        if owner == self.replica:
+            self.scheduler.add_request(req)
+        else:
+            self._remote.add(req.request_id)
 
     def _make_request(self, rid, prompt_token_ids, sampling_params, prompt, mm_inputs, kv_transfer_params) -> Request:
         ids = list(map(int, prompt_token_ids))
@@ -158,12 +174,13 @@ class LLMEngine:
         return self.profiler.stop()
 
     def abort_request(self, request_id: str) -> None:
+        self._remote.discard(request_id)
         if self.mode == "driver":
             self._pending.append(("abort", request_id))
         self.scheduler.abort(request_id)
 
     def has_unfinished_requests(self) -> bool:
-        return self.scheduler.has_unfinished()
+        return self.scheduler.has_unfinished() or bool(self._remote)
 
     # -------------------------------------------------------------------- step
     def _sync_requests(self) -> None:
@@ -175,7 +192,7 @@ class LLMEngine:
             for m in msgs:
                 if m[0] == "add":
                     _, rid, ids, sp, prompt, mm, kvp = m
-                    self.scheduler.add_request(self._make_request(rid, ids, sp, prompt, mm, kvp))
+                    self._admit(self._make_request(rid, ids, sp, prompt, mm, kvp))
                 elif m[0] == "abort":
                     self.scheduler.abort(m[1])
                 elif m[0] == "profile":
@@ -191,15 +208,47 @@ class LLMEngine:
         self._sync_requests()
         if self._stopped:
             return []
+        if self.dp > 1:
+            return self._step_dp()
         so = self.scheduler.schedule()
         failed = [self._make_output(r, True) for r in self.scheduler.failed]
         self.scheduler.failed = []
         if so.kind == "idle":
             return failed
+        return failed + self._run(so)
+
+    def _step_dp(self) -> list[RequestOutput]:
+        """One lockstep step of a data-parallel replica.  Replicas share the MoE layers'
+        collectives, so every replica runs a step of the same kind with the same padded
+        token count (idle replicas run a padding batch), the counterpart of the reference's
+        per-step MAX-reduce and dummy batches (``neuron_model_runner.py:6524-6821,6968``)."""
+        world = self.worker.ps.world
+        has_work = self.scheduler.has_unfinished()
+        flags = world.cpu_all_reduce_max([int(has_work), int(has_work and self.scheduler.has_prefill_work())])
+        outs: list[RequestOutput] = []
+        if flags[0]:
+            kind = "prefill" if flags[1] else "decode"
+            so = self.scheduler.schedule(kind)
+            outs = [self._make_output(r, True) for r in self.scheduler.failed]
+            self.scheduler.failed = []
+            n_tok = so.num_tokens if so.kind != "idle" else 0
+            mx = world.cpu_all_reduce_max([n_tok, len(so.seqs)])
+            outs += self._run(so, dp_pad=(kind, mx[0], mx[1]))
+        # every replica learns every replica's outputs (TP peers hold identical copies)
+        allouts = [o for lst in self.worker.ps.dp.all_gather_object(outs) for o in lst]
+        for o in allouts:
+            if o.finished:
+                self._remote.discard(o.request_id)
+        return allouts
+
+    def _run(self, so, dp_pad=None) -> list[RequestOutput]:
+        if so.kind == "idle":  # data-parallel padding step
+            self.worker.runner.execute(so, dp_pad=dp_pad)
+            return []
         if self.proposer is not None and so.kind == "decode":
             sampled = self.proposer.execute_with_speculation(so)
         else:
-            sampled = self.worker.execute_model(so)
+            sampled = self.worker.runner.execute(so, dp_pad=dp_pad) if dp_pad else self.worker.execute_model(so)
         now = time.monotonic()
         finished = self.scheduler.update_from_output(so, sampled, now)
         if self.proposer is not None:
@@ -210,7 +259,7 @@ class LLMEngine:
             if s.req_id in sampled or s.req_id in fin_ids:
                 req = s.request
                 outs.append(self._make_output(req, req.status.finished))
-        return failed + outs
+        return outs
 
     def _make_output(self, req: Request, finished: bool) -> RequestOutput:
         reason = None

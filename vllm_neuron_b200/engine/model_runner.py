@@ -257,10 +257,15 @@ class ModelRunner:
                 j += 1
         self.d_pos_params[:, :n_sel].copy_(self.h_pos_params[:, :n_sel], non_blocking=True)
 
-    def _prepare(self, so: SchedulerOutput, pad_to: int | None) -> tuple[AttentionMetadata, int, int, bool]:
+    def _prepare(self, so: SchedulerOutput, pad_to: int | None,
+                 pad_tokens: int | None = None) -> tuple[AttentionMetadata, int, int, bool]:
         seqs = so.seqs
         n = len(seqs)
         B = pad_to or n
+        n_real_tok = sum(len(s.token_ids) for s in seqs)
+        pad_seq = pad_tokens is not None and pad_tokens > n_real_tok
+        if pad_seq:  # one padding sequence (no KV write, not sampled) brings T to pad_tokens
+            B = n + 1
         ids = self.h_ids.numpy()
         pos = self.h_pos.numpy()
         slot = self.h_slot.numpy()
@@ -300,7 +305,17 @@ class ModelRunner:
             max_q = max(max_q, k)
             max_s = max(max_s, s.seq_len)
         T = t
-        if B > n:  # decode padding rows: no KV write, no keys
+        if pad_seq:
+            k = pad_tokens - T
+            ids[T:T + k] = 0
+            pos[T:T + k] = np.arange(k)
+            slot[T:T + k] = -1
+            sl[n] = k
+            bt[n] = 0
+            qsl[n + 1] = T + k
+            max_q, max_s = max(max_q, k), max(max_s, k)
+            T += k
+        elif B > n:  # decode padding rows: no KV write, no keys
             ids[T:T + (B - n)] = 0
             pos[T:T + (B - n)] = 0
             slot[T:T + (B - n)] = -1
@@ -312,7 +327,8 @@ class ModelRunner:
                 n_sel += 1
             T += B - n
         greedy = self._fill_sampling(so, B)
-        if so.kind == "decode" and n_sel > B and not greedy:
+        spec = so.kind == "decode" and any(s.spec_token_ids for s in seqs)
+        if spec and not greedy:
             self._fill_spec_sampling(so, n_sel)
         extras = self._mm_extras(so) if (has_mrope and self.encoder_cache is not None) else {}
         if self.state_caches is not None:
@@ -337,6 +353,8 @@ class ModelRunner:
             dv[:cnt].copy_(h[:cnt], non_blocking=True)
             nb_ += cnt * h.element_size()
         max_nb = max(1, max(math.ceil(s.seq_len / self.bs) for s in seqs)) if seqs else 1
+        if pad_seq:
+            max_nb = max(max_nb, math.ceil(int(sl[n]) / self.bs))
         self.d_bt[:B, :max_nb].copy_(self.h_bt[:B, :max_nb], non_blocking=True)
         nb_ += B * max_nb * 4
         self.h2d_bytes_last = nb_
@@ -345,6 +363,8 @@ class ModelRunner:
             query_start_loc=self.d_qsl[:B + 1], seq_lens=self.d_seqlen[:B], block_tables=self.d_bt[:B],
             slot_mapping=self.d_slot[:T], logits_indices=self.d_lidx[:n_sel], max_query_len=max_q,
             max_seq_len=max_s, workspace=self.workspace, num_splits=self.num_splits_for(B), extras=extras)
+        if spec:
+            extras["spec"] = True
         return meta, T, n_sel, greedy
 
     def _mm_extras(self, so: SchedulerOutput) -> dict:
@@ -391,10 +411,12 @@ class ModelRunner:
     # ------------------------------------------------------------------ forward
     def _forward_sample(self, meta: AttentionMetadata, T: int, n_sel: int, greedy: bool) -> torch.Tensor:
         h = self.model(self.d_ids[:T], self.d_pos[:T], meta, self.kv_caches)
+        if n_sel == 0:  # data-parallel padding step: nothing to sample
+            return self.d_out[:0]
         hs = h if (meta.is_decode and n_sel == T) else h.index_select(0, meta.logits_indices)
         logits = self.model.compute_logits(hs)
-        B = meta.num_seqs
-        if n_sel == B:
+        if not meta.extras.get("spec", False):  # one sampled token per row
+            B = n_sel
             tok = self.sampler(logits, self.d_temp[:B], self.d_topk[:B], self.d_topp[:B], self.d_unif[:B], greedy)
         elif greedy:  # speculative verification, greedy: accept until the first mismatch
             tok = self.sampler.greedy(logits)
@@ -409,17 +431,28 @@ class ModelRunner:
         return self.d_out[:n_sel]
 
     @torch.inference_mode()
-    def execute(self, so: SchedulerOutput) -> dict[str, list[int]]:
-        if so.kind == "idle" or not so.seqs:
+    def execute(self, so: SchedulerOutput, dp_pad: tuple | None = None) -> dict[str, list[int]]:
+        """Run one step.  ``dp_pad = (kind, max_tokens, max_seqs)`` (data parallelism): pad the
+        step to the largest replica's size so the MoE collectives match; an idle ``so``
+        then runs a batch of padding only."""
+        pad_tokens = None
+        if dp_pad is not None:
+            kind, t_max, b_max = dp_pad
+            if so.kind == "idle":
+                so = SchedulerOutput(kind, [])
+            if kind == "prefill":
+                pad_tokens = max(1, t_max)
+        elif so.kind == "idle" or not so.seqs:
             return {}
         self.step_count += 1
         n = len(so.seqs)
         pad_to = None
         is_plain_decode = so.kind == "decode" and all(len(s.token_ids) == 1 for s in so.seqs)
         if is_plain_decode:
-            pad_to = get_bucket_for_count(n, self.decode_buckets) if self.use_graphs else n
+            want = max(n, dp_pad[2]) if dp_pad is not None else n
+            pad_to = get_bucket_for_count(want, self.decode_buckets) if self.use_graphs else want
             NUM_SEQS_PADDING.labels(model_name=self.cfg.served_model_name or "model").observe(pad_to - n)
-        meta, T, n_sel, greedy = self._prepare(so, pad_to)
+        meta, T, n_sel, greedy = self._prepare(so, pad_to, pad_tokens)
         if is_plain_decode and self.use_graphs:
             key = (pad_to, greedy)
             entry = self.graphs.get(key)

@@ -134,12 +134,21 @@ class Scheduler:
             return False
         return len(self.running) < self.max_kv_concurrent
 
-    def schedule(self) -> SchedulerOutput:
+    def has_prefill_work(self) -> bool:
+        """A prefill step would do something now (a segment in flight or an admissible prompt)."""
+        if any(self._is_prefill(r) for r in self.running):
+            return True
+        return bool(self.waiting) and self.can_admit()
+
+    def schedule(self, kind: str | None = None) -> SchedulerOutput:
+        """Next step.  ``kind`` ("prefill" | "decode") restricts the step type; data-parallel
+        replicas use it to run the same kind of step in lockstep (a replica with nothing of
+        that kind gets an idle output and runs a padding batch)."""
         finished, self._finished_ids = self._finished_ids, []
         # 1) ongoing segmented prefills first
-        pre = [r for r in self.running if self._is_prefill(r)]
+        pre = [r for r in self.running if self._is_prefill(r)] if kind != "decode" else []
         # 2) admit new prompts when no prefill is in flight
-        if not pre:
+        if not pre and kind != "decode":
             admitted = 0
             while self.waiting and admitted < self.max_prefills and self.can_admit():
                 req = self.waiting[0]
@@ -195,6 +204,8 @@ class Scheduler:
                                          mm_inputs=req.mm_inputs, request=req))
             if seqs:
                 return SchedulerOutput("prefill", seqs, finished=finished)
+        if kind == "prefill":
+            return SchedulerOutput("idle", [], [], finished)
         # 3) decode step over every running request
         seqs, preempted = [], []
         k = self.num_spec_tokens

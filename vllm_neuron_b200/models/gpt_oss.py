@@ -205,18 +205,28 @@ class GptOssExperts(nn.Module):
 
 
 class GptOssMLP(nn.Module):
-    def __init__(self, cfg: GptOssConfig, moe_group: GroupCoordinator, dtype, device):
+    """Experts are sharded over the whole world (EP = TP x DP).  With data parallelism the
+    tokens of every replica are gathered over the DP group before the experts and the
+    partial outputs reduce-scattered back (cross-DP EP, ``model_mxfp4.py:1361-1453``); the
+    TP partial sum is completed at the next layer boundary."""
+
+    def __init__(self, cfg: GptOssConfig, ps: ParallelState, dtype, device):
         super().__init__()
         self.cfg = cfg
-        self.group = moe_group
+        self.dp = ps.dp
+        ep_rank = ps.dp.rank_in_group * ps.tp.world_size + ps.tp.rank_in_group
+        ep_size = ps.tp.world_size * ps.dp.world_size
         self.router_weight = _param((cfg.num_local_experts, cfg.hidden_size), dtype, device)
         self.router_bias = _param((cfg.num_local_experts,), dtype, device)
-        self.experts = GptOssExperts(cfg, moe_group.rank_in_group, moe_group.world_size, dtype, device)
+        self.experts = GptOssExperts(cfg, ep_rank, ep_size, dtype, device)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         """This rank's partial MoE output (its experts only); the caller reduces it."""
+        if self.dp.world_size > 1:
+            x = self.dp.all_gather(x, dim=0)
         ids, w = ops.router_topk(x, self.router_weight, self.router_bias, self.cfg.num_experts_per_tok)
-        return self.experts(x, ids, w)
+        y = self.experts(x, ids, w)
+        return self.dp.reduce_scatter(y, dim=0) if self.dp.world_size > 1 else y
 
 
 class GptOssDecoderLayer(nn.Module):
@@ -232,7 +242,7 @@ class GptOssDecoderLayer(nn.Module):
         self.input_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, device=device)
         self.self_attn = GptOssAttention(cfg, i, ps.tp, dtype, device)
         self.post_attention_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, device=device)
-        self.mlp = GptOssMLP(cfg, ps.tp, dtype, device)
+        self.mlp = GptOssMLP(cfg, ps, dtype, device)
 
     def forward(self, positions, h, residual, meta, kv, cos_sin):
         if residual is None:

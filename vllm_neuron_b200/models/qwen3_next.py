@@ -247,15 +247,17 @@ class GatedDeltaNet(nn.Module):
 class SparseMoE(nn.Module):
     """Routed experts (EP over the group) + TP-sharded shared expert; returns a partial sum."""
 
-    def __init__(self, cfg: Qwen3NextConfig, group: GroupCoordinator, dtype, device):
+    def __init__(self, cfg: Qwen3NextConfig, ps: ParallelState, dtype, device):
         super().__init__()
         self.cfg = cfg
+        group = ps.tp
         self.group = group
-        E, w = cfg.num_experts, group.world_size
+        self.dp = ps.dp
+        E, w = cfg.num_experts, group.world_size * ps.dp.world_size  # EP over TP x DP
         if E % w:
             raise ValueError(f"experts {E} not divisible by the expert-parallel size {w}")
         self.E_local = E // w
-        self.e0 = group.rank_in_group * self.E_local
+        self.e0 = (ps.dp.rank_in_group * group.world_size + group.rank_in_group) * self.E_local
         H, I = cfg.hidden_size, cfg.moe_intermediate_size
         self.router = _param((E, H), dtype, device)
         self.w13 = _param((self.E_local, 2 * I, H), dtype, device)  # [gate | up] rows
@@ -266,15 +268,18 @@ class SparseMoE(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         k = self.cfg.num_experts_per_tok
+        xr = self.dp.all_gather(x, dim=0) if self.dp.world_size > 1 else x  # cross-DP expert parallelism
         if self.cfg.norm_topk_prob:
             # softmax -> top-k -> renormalise == softmax over the top-k logits
-            ids, wts = ops.router_topk(x, self.router, None, k)
+            ids, wts = ops.router_topk(xr, self.router, None, k)
         else:
-            p = torch.softmax(ops.linear(x, self.router).float(), -1)
+            p = torch.softmax(ops.linear(xr, self.router).float(), -1)
             wts, ids = torch.topk(p, k, -1)
             ids = ids.to(torch.int32)
         H, I = self.cfg.hidden_size, self.cfg.moe_intermediate_size
-        out = ops.moe_dense(x, ids, wts, self.w13, None, self.w2, None, self.e0, 1.0, None, False, "silu", H, I)
+        out = ops.moe_dense(xr, ids, wts, self.w13, None, self.w2, None, self.e0, 1.0, None, False, "silu", H, I)
+        if self.dp.world_size > 1:
+            out = self.dp.reduce_scatter(out, dim=0)
         if self.shared is not None:
             sg = ops.linear(x, self.shared_gate)
             out = ops.gated_add(out, self.shared(x), sg)
@@ -309,7 +314,7 @@ class Qwen3NextDecoderLayer(nn.Module):
             self.linear_attn = GatedDeltaNet(cfg, ps.tp, dtype, device)
         else:
             self.self_attn = GatedAttention(cfg, ps.tp, dtype, device)
-        self.mlp = (SparseMoE(cfg, ps.tp, dtype, device) if cfg.is_moe_layer(i)
+        self.mlp = (SparseMoE(cfg, ps, dtype, device) if cfg.is_moe_layer(i)
                     else DenseMLP(_SharedCfg(cfg.hidden_size, cfg.intermediate_size), ps.tp, dtype, device))
 
     def forward(self, positions, h, residual, meta, cache, cos_sin):

@@ -225,6 +225,13 @@ class GroupCoordinator:
         dist.broadcast_object_list(lst, src=self.ranks[src_in_group], group=self.cpu_group)
         return lst[0]
 
+    def all_gather_object(self, obj: Any) -> list:
+        if self.world_size == 1:
+            return [obj]
+        out: list = [None] * self.world_size
+        dist.all_gather_object(out, obj, group=self.cpu_group)
+        return out
+
     def cpu_all_reduce_max(self, values: list[int]) -> list[int]:
         if self.world_size == 1:
             return list(values)
