@@ -13,7 +13,7 @@ queue:
 
 Failure detection: a task that raises on any rank makes ``run`` raise ``RankError`` with
 the rank and its traceback; a rank process that dies or does not answer within
-``timeout_s`` makes ``run`` raise ``RankError`` as well, after which the pool is torn
+``timeout_s`` (start-up: ``init_timeout_s``) makes ``run`` raise ``RankError`` as well, after which the pool is torn
 down (a fresh executor respawns it).  The ``ctx`` passed to tasks carries ``rank``,
 ``world_size``, ``ps`` (the parallel state), ``device`` and ``obj``.
 """
@@ -95,7 +95,7 @@ def _worker(rank: int, world_size: int, init_method: str, backend: str, layout: 
 
 class MPExecutor:
     def __init__(self, world_size: int, tp: int | None = None, dp: int = 1, backend: str | None = None,
-                 timeout_s: float = 120.0, **layout):
+                 timeout_s: float = 120.0, init_timeout_s: float = 300.0, **layout):
         from .rendezvous import FileRendezvous
 
         self.world_size = world_size
@@ -112,20 +112,21 @@ class MPExecutor:
                        for r in range(world_size)]
         for p in self._procs:
             p.start()
-        self._collect("ready")
+        self._collect("ready", init_timeout_s)
 
     # ------------------------------------------------------------------ internals
-    def _collect(self, expect: str) -> list:
+    def _collect(self, expect: str, timeout_s: float | None = None) -> list:
+        timeout_s = self.timeout_s if timeout_s is None else timeout_s
         out: list = [None] * self.world_size
         seen: set[int] = set()
-        deadline = time.monotonic() + self.timeout_s
+        deadline = time.monotonic() + timeout_s
         errors = []
         while len(seen) < self.world_size:
             left = deadline - time.monotonic()
             if left <= 0:
                 missing = [r for r in range(self.world_size) if r not in seen]
                 self._kill()
-                raise RankError(missing[0] if missing else -1, f"no answer within {self.timeout_s:.0f}s")
+                raise RankError(missing[0] if missing else -1, f"no answer within {timeout_s:.0f}s")
             try:
                 rank, status, payload = self._results.get(timeout=min(0.5, left))
             except queue.Empty:
