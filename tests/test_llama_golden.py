@@ -71,3 +71,36 @@ def test_dense_greedy_matches_hf(ckpt, tp):
     finally:
         llm.shutdown()
     assert [o.outputs[0].token_ids for o in outs] == want
+
+
+def test_sequence_parallel_prefill_counts(ckpt, monkeypatch):
+    """TP=2 prefill steps with an even token count run sequence-parallel layer boundaries
+    (reduce-scatter + sharded residual + all-gather); greedy tokens still match HF."""
+    from vllm_neuron_b200 import LLM, SamplingParams
+    from vllm_neuron_b200.parallel import state as pstate
+
+    calls = {"sp": 0}
+    orig = pstate.GroupCoordinator._sp_add_rmsnorm
+
+    def spy(self, *a, **k):
+        calls["sp"] += 1
+        return orig(self, *a, **k)
+
+    monkeypatch.setattr(pstate.GroupCoordinator, "_sp_add_rmsnorm", spy)
+    path, hf = ckpt
+    prompts = [list(range(10, 40)), list(range(50, 70))]  # 50 tokens in one prefill step
+    want = []
+    with torch.no_grad():
+        for p in prompts:
+            g = hf.generate(torch.tensor([p]), max_new_tokens=4, do_sample=False, pad_token_id=0, eos_token_id=None)
+            want.append(g[0, len(p):].tolist())
+    llm = LLM(model=path, dtype="float32", max_model_len=256, max_num_seqs=4, max_num_batched_tokens=128,
+              block_size=16, device="cpu", tensor_parallel_size=2, spmd=False,
+              additional_config={"neuron_config": {"decode_batch_buckets": [2]}})
+    try:
+        outs = llm.generate(prompt_token_ids=prompts,
+                            sampling_params=SamplingParams(temperature=0, max_tokens=4, ignore_eos=True))
+    finally:
+        llm.shutdown()
+    assert [o.outputs[0].token_ids for o in outs] == want
+    assert calls["sp"] > 0

@@ -409,8 +409,19 @@ class ModelRunner:
         return ex
 
     # ------------------------------------------------------------------ forward
+    def _sp_ok(self, meta: AttentionMetadata, T: int) -> bool:
+        g = self.sampler.group
+        return (not meta.is_decode and g.world_size > 1 and T > g.world_size and T % g.world_size == 0
+                and envs.VLLM_B200_SEQUENCE_PARALLEL and not getattr(self.model, "aux_hidden_layers", ())
+                and "mm_index" not in meta.extras)
+
     def _forward_sample(self, meta: AttentionMetadata, T: int, n_sel: int, greedy: bool) -> torch.Tensor:
-        h = self.model(self.d_ids[:T], self.d_pos[:T], meta, self.kv_caches)
+        g = self.sampler.group
+        g.sp_active = self._sp_ok(meta, T)
+        try:
+            h = self.model(self.d_ids[:T], self.d_pos[:T], meta, self.kv_caches)
+        finally:
+            g.sp_active = False
         if n_sel == 0:  # data-parallel padding step: nothing to sample
             return self.d_out[:0]
         hs = h if (meta.is_decode and n_sel == T) else h.index_select(0, meta.logits_indices)

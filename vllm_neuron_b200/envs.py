@@ -53,6 +53,8 @@ _REGISTRY: dict[str, tuple[Callable[[str], Any], str | None, str | None]] = {
     "VLLM_B200_WORKER_TERMINATION_TIMEOUT": (float, "5", "VLLM_NEURON_WORKER_TERMINATION_TIMEOUT"),
     # Gate the synthetic KV-verification model into the registry (DI tests).
     "VLLM_B200_SYNTHETIC_MODEL": (_bool, "0", "VLLM_NEURON_SYNTHETIC_MODEL"),
+    # sequence parallelism for TP prefill steps (token rows split across TP between blocks)
+    "VLLM_B200_SEQUENCE_PARALLEL": (_bool, "1", None),
     # Directory for golden logits used by accuracy tests.
     "VLLM_B200_GOLDEN_CACHE_DIR": (str, "", "VLLM_NEURON_GOLDEN_CACHE_DIR"),
     # Use the fused in-kernel NVLink collectives (else NCCL).

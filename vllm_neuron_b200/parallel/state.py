@@ -136,6 +136,7 @@ class GroupCoordinator:
     cpu_group: Any = None
     rank: int = 0
     communicator: Any = None  # fused NVLink collectives (parallel.communicator)
+    sp_active: bool = False  # sequence parallelism at layer boundaries (set per prefill step)
 
     @property
     def world_size(self) -> int:
@@ -165,6 +166,8 @@ class GroupCoordinator:
         fused add+norm op."""
         from .. import ops
 
+        if self.sp_active and self.world_size > 1 and x.shape[0] % self.world_size == 0:
+            return self._sp_add_rmsnorm(x, residual, w, eps, bias)
         if self.world_size > 1 and self.communicator is not None and self.communicator.can_all_reduce(x):
             return self.communicator.all_reduce_add_rmsnorm(x, residual, w, eps, bias)
         if self.world_size > 1:
@@ -172,6 +175,22 @@ class GroupCoordinator:
         if bias is not None:
             x = x + bias
         return ops.fused_add_rms_norm(x, residual, w, eps)
+
+    def _sp_add_rmsnorm(self, x, residual, w, eps, bias):
+        """Sequence-parallel layer boundary (prefill): reduce-scatter the partial sums over
+        tokens, add bias and this rank's residual rows, normalise the shard, all-gather the
+        normalised rows for the next GEMM.  The residual stays sharded (T / tp rows)
+        between boundaries (``model_mxfp4.py:464,685``: AG before, RS after each block)."""
+        from .. import ops
+
+        T = x.shape[0]
+        xs = self.reduce_scatter(x, dim=0)
+        if residual.shape[0] == T:  # first boundary after the (replicated) embedding
+            residual = residual.chunk(self.world_size, dim=0)[self.rank_in_group].contiguous()
+        if bias is not None:
+            xs = xs + bias
+        y, r = ops.fused_add_rms_norm(xs, residual, w, eps)
+        return self.all_gather(y, dim=0), r
 
     def all_gather(self, x: torch.Tensor, dim: int = 0) -> torch.Tensor:
         if self.world_size == 1:
