@@ -39,7 +39,7 @@ def test_vision_packing():
 def test_golden_cache(tmp_path, monkeypatch):
     from vllm_neuron_b200.utils.golden_cache import get_or_compute, golden_key
 
-    monkeypatch.setenv("VLLM_B200_GOLDEN_CACHE", str(tmp_path))
+    monkeypatch.setenv("VLLM_B200_GOLDEN_CACHE_DIR", str(tmp_path))
     calls = []
     k = golden_key(model="tiny", prompts=[[1, 2]])
     f = lambda: calls.append(1) or torch.arange(3)  # noqa: E731

@@ -2,8 +2,9 @@
 
 Reference model runs (e.g. HF fp32 generations or logits) are slow; tests and accuracy tools
 key them by a hash of everything that determines them (model config, prompts, generation
-parameters, library versions) and reuse them.  ``VLLM_B200_GOLDEN_CACHE`` sets the directory
-(default ``~/.cache/vllm_b200/golden``); ``VLLM_B200_GOLDEN_CACHE=off`` disables it.
+parameters, library versions) and reuse them.  ``VLLM_B200_GOLDEN_CACHE_DIR`` (alias
+``VLLM_NEURON_GOLDEN_CACHE_DIR``) sets the directory (default ``~/.cache/vllm_b200/golden``);
+the value ``off`` disables the cache.
 """
 
 from __future__ import annotations
@@ -17,8 +18,8 @@ import torch
 
 
 def cache_dir() -> str | None:
-    d = os.environ.get("VLLM_B200_GOLDEN_CACHE", os.path.join(os.path.expanduser("~"), ".cache", "vllm_b200",
-                                                                 "golden"))
+    d = (os.environ.get("VLLM_B200_GOLDEN_CACHE_DIR") or os.environ.get("VLLM_NEURON_GOLDEN_CACHE_DIR")
+         or os.path.join(os.path.expanduser("~"), ".cache", "vllm_b200", "golden"))
     return None if d.lower() in ("off", "0", "none", "") else d
 
 
