@@ -112,6 +112,26 @@ def run_reference(args) -> None:
         print(json.dumps({"impl": "reference", "unavailable": reason or "reference has no CUDA execution path"}))
 
 
+def _profile_replays(graph, n: int) -> tuple[int, int, str]:
+    """Replay the decode graph n times under torch.profiler: (launches of this library's
+    kernels per replay, all kernels per replay, per-kernel table)."""
+    import torch
+
+    acts = [torch.profiler.ProfilerActivity.CUDA]
+    with torch.profiler.profile(activities=acts) as prof:
+        for _ in range(n):
+            graph.replay()
+        torch.cuda.synchronize()
+    ours = total = 0
+    for ev in prof.events():
+        if ev.device_type == torch.autograd.DeviceType.CUDA:
+            total += 1
+            if "b200::" in ev.name:
+                ours += 1
+    table = prof.key_averages().table(sort_by="self_cuda_time_total", row_limit=40)
+    return ours // n, total // n, table
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -122,6 +142,8 @@ def main() -> None:
     ap.add_argument("--concurrency", type=int, default=64)
     ap.add_argument("--prompt-len", type=int, default=2048)
     ap.add_argument("--output-len", type=int, default=512)
+    ap.add_argument("--profile-dir", default=None,
+                    help="also write a per-kernel table of profiled decode-step replays (rank 0)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -216,12 +238,15 @@ def main() -> None:
     value = C * args.steps / (dev_ms / 1000.0)
     e2e_val = C * args.steps / (e2e_wall_ms / 1000.0)
     tpot_ms = e2e_wall_ms / args.steps
-    # kernel launches per decode step (our kernels): per layer rms_norm x2, rope/kv, attention
-    # (+combine when split), moe route, quant x2, gemm x2, reduce, topk; plus final norm, argmax.
-    splits = runner.num_splits_for(C)
-    per_layer = 2 + 1 + 1 + (1 if splits > 1 else 0) + 1 + 6
-    L = hf["num_hidden_layers"]
-    launches = (L * per_layer + 1 + 1 + 1) * args.steps
+    # kernel launches per decode step, counted from one profiled replay after the timed region
+    # (every rank replays so the graphs' collectives stay matched)
+    ours, total, table = _profile_replays(graph, 1 if not args.profile_dir else 5)
+    launches = ours * args.steps
+    if rank == 0 and args.profile_dir:
+        os.makedirs(args.profile_dir, exist_ok=True)
+        with open(os.path.join(args.profile_dir, f"decode_step_kernels_n{N}.txt"), "w") as f:
+            f.write(f"# {ours} launches of this library's kernels, {total} kernels in total, per decode step\n")
+            f.write(table)
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": N, "steps": args.steps,

@@ -161,3 +161,30 @@ def test_qwen3_next_engine_bf16():
             for i, t in enumerate(toks):
                 gap = (logits[i].max() - logits[i, t]).item()
                 assert gap < 0.1 * logits[i].std().item() + 0.05, (i, gap)
+
+
+@pytest.mark.parametrize("T,E,H,I,k", [(7, 16, 512, 256, 4), (64, 64, 2048, 512, 10)])
+def test_moe_mxfp8_experts(T, E, H, I, k):
+    """fp8-checkpoint experts: MXFP8 weights (e4m3 + ue8m0 per 32) on the block-scaled tcgen05
+    GEMM with plain SiLU gating, vs the fp32 reference over the same quantised weights."""
+    from vllm_neuron_b200 import ops
+    from vllm_neuron_b200.ops import reference as ref
+    from vllm_neuron_b200.ops.mx_layout import atoms_to_scales, interleave_gate_up, untile_values
+
+    torch.manual_seed(4)
+    x = torch.randn(T, H, device="cuda").bfloat16()
+    w13 = torch.randn(E, 2 * I, H, device="cuda") / H ** 0.5
+    w2 = torch.randn(E, H, I, device="cuda") / I ** 0.5
+    wts, ids = torch.topk(torch.softmax(torch.randn(T, E, device="cuda"), -1), k, -1)
+    ids = ids.to(torch.int32)
+    t13, s13, t2, s2 = ops.prepare_moe_mxfp8(w13, w2, interleaved=False)
+    b13 = torch.zeros(E, 2 * I, device="cuda")
+    b2 = torch.zeros(E, H, device="cuda")
+    got = ops.moe_mxfp4(x, ids, wts, t13, s13, b13, t2, s2, b2, 0, 1.0, -1.0, H, I, fp4=False)
+    w13q = ref.dequant_mxfp8(untile_values(t13, 2 * I, H, False).view(torch.float8_e4m3fn),
+                             atoms_to_scales(s13, 2 * I, H))
+    w2q = ref.dequant_mxfp8(untile_values(t2, H, I, False).view(torch.float8_e4m3fn), atoms_to_scales(s2, H, I))
+    assert torch.allclose(w13q, interleave_gate_up(w13), atol=0, rtol=0.07)
+    want = ref.moe_experts(x, ids, wts, w13q, None, w2q, None, 1.0, None, True, 0, "silu")
+    rel = (got.float() - want.float()).norm() / want.float().norm()
+    assert rel < 0.05, rel  # activations are MXFP8-quantised inside the kernel

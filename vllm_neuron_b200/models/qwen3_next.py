@@ -265,6 +265,7 @@ class SparseMoE(nn.Module):
         self.shared = DenseMLP(_SharedCfg(H, cfg.shared_expert_intermediate_size), group, dtype, device) \
             if cfg.shared_expert_intermediate_size else None
         self.shared_gate = _param((1, H), dtype, device) if self.shared is not None else None
+        self.mx = None  # MXFP8 kernel tensors (set after loading on a GPU for fp8 checkpoints)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         k = self.cfg.num_experts_per_tok
@@ -277,7 +278,11 @@ class SparseMoE(nn.Module):
             wts, ids = torch.topk(p, k, -1)
             ids = ids.to(torch.int32)
         H, I = self.cfg.hidden_size, self.cfg.moe_intermediate_size
-        out = ops.moe_dense(xr, ids, wts, self.w13, None, self.w2, None, self.e0, 1.0, None, False, "silu", H, I)
+        if self.mx is not None:  # MXFP8 experts (fp8 checkpoints on the GPU)
+            t13, s13, t2, s2, b13, b2 = self.mx
+            out = ops.moe_mxfp4(xr, ids, wts, t13, s13, b13, t2, s2, b2, self.e0, 1.0, -1.0, H, I, fp4=False)
+        else:
+            out = ops.moe_dense(xr, ids, wts, self.w13, None, self.w2, None, self.e0, 1.0, None, False, "silu", H, I)
         if self.dp.world_size > 1:
             out = self.dp.reduce_scatter(out, dim=0)
         if self.shared is not None:
@@ -287,8 +292,19 @@ class SparseMoE(nn.Module):
 
     @torch.no_grad()
     def process_weights_after_loading(self) -> None:
-        """On a GPU: re-lay the experts into the grouped-GEMM tiles (gate/up interleaved)."""
-        if self.w13.is_cuda and self.w13.dim() == 3:
+        """On a GPU: re-lay the experts into the grouped-GEMM tiles (gate/up interleaved); fp8
+        checkpoints become MXFP8 (e4m3 + ue8m0 per 32), bf16 ones stay bf16."""
+        if not (self.w13.is_cuda and self.w13.dim() == 3):
+            return
+        if self.cfg.quantization == "fp8":
+            t13, s13, t2, s2 = ops.prepare_moe_mxfp8(self.w13.data, self.w2.data, interleaved=False)
+            dev = t13.device
+            z13 = torch.zeros(self.E_local, 2 * self.cfg.moe_intermediate_size, dtype=torch.float32, device=dev)
+            z2 = torch.zeros(self.E_local, self.cfg.hidden_size, dtype=torch.float32, device=dev)
+            self.mx = (t13, s13, t2, s2, z13, z2)
+            self.w13 = nn.Parameter(torch.empty(0, device=dev), requires_grad=False)
+            self.w2 = nn.Parameter(torch.empty(0, device=dev), requires_grad=False)
+        else:
             t13, t2 = ops.prepare_moe_bf16(self.w13.data, self.w2.data, interleaved=False)
             self.w13 = nn.Parameter(t13, requires_grad=False)
             self.w2 = nn.Parameter(t2, requires_grad=False)

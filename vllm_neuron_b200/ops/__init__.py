@@ -242,7 +242,7 @@ def router_topk(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, top_k:
 def moe_mxfp4(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, w13: torch.Tensor,
               s13: torch.Tensor, b13: torch.Tensor | None, w2: torch.Tensor, s2: torch.Tensor,
               b2: torch.Tensor | None, expert_offset: int, alpha: float, limit: float, H: int, I: int,
-              status: torch.Tensor | None = None) -> torch.Tensor:
+              status: torch.Tensor | None = None, fp4: bool = True) -> torch.Tensor:
     """Routed experts with packed MX weights in the kernel layout (``ops/mx_layout.py``):
     w13 tiles [E_local, 2I/128, K1p/128, 128, 64] u8 (gate/up interleaved rows) + s13
     scale atoms, w2 tiles [E_local, H/128, K2p/128, 128, 64] + s2 atoms; biases fp32
@@ -255,13 +255,36 @@ def moe_mxfp4(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, w13
         b2_ = b2 if b2 is not None else torch.zeros(E, H, dtype=torch.float32, device=x.device)
         st = status if status is not None else device_status(x.device)
         _k().moe_mx(out, x.contiguous(), topk_ids.to(torch.int32).contiguous(), topk_w.float().contiguous(), w13,
-                    s13, b13_, w2, s2, b2_, expert_offset, H, I, True, alpha, limit, st)
+                    s13, b13_, w2, s2, b2_, expert_offset, H, I, fp4, alpha, limit, st)
         return out
     from .mx_layout import atoms_to_scales, untile_values
 
-    w13f = ref.dequant_mxfp4(untile_values(w13, 2 * I, H), atoms_to_scales(s13, 2 * I, H))
-    w2f = ref.dequant_mxfp4(untile_values(w2, H, I), atoms_to_scales(s2, H, I))
-    return ref.moe_experts(x, topk_ids, topk_w, w13f, b13, w2f, b2, alpha, limit, True, expert_offset)
+    if fp4:
+        w13f = ref.dequant_mxfp4(untile_values(w13, 2 * I, H), atoms_to_scales(s13, 2 * I, H))
+        w2f = ref.dequant_mxfp4(untile_values(w2, H, I), atoms_to_scales(s2, H, I))
+    else:
+        w13f = ref.dequant_mxfp8(untile_values(w13, 2 * I, H, False).view(torch.float8_e4m3fn),
+                                 atoms_to_scales(s13, 2 * I, H))
+        w2f = ref.dequant_mxfp8(untile_values(w2, H, I, False).view(torch.float8_e4m3fn), atoms_to_scales(s2, H, I))
+    act = "swiglu_clamp" if limit is not None and limit > 0 else "silu"
+    return ref.moe_experts(x, topk_ids, topk_w, w13f, b13, w2f, b2, alpha, limit if limit and limit > 0 else None,
+                           True, expert_offset, act)
+
+
+def prepare_moe_mxfp8(w13: torch.Tensor, w2: torch.Tensor, interleaved: bool) -> tuple[torch.Tensor, ...]:
+    """Expert weights (any float dtype) -> MXFP8 kernel layout: e4m3 values with one ue8m0 scale
+    per row and 32 K-elements, tiled [E, rows/128, Kp/128, 128, 128] u8 + 512-byte scale atoms.
+    Used for fp8 checkpoints: block-scaled (128 x 128) fp8 weights are re-expressed with
+    power-of-two scales per 32 elements, which the tensor cores apply in the MMA itself."""
+    from .mx_layout import interleave_gate_up, scales_to_atoms, tile_values
+
+    w13i = w13 if interleaved else interleave_gate_up(w13)
+    out = []
+    for w in (w13i, w2):
+        K = w.shape[-1]
+        q, sc = ref.quantize_mxfp8(w.float())
+        out += [tile_values(q.view(torch.uint8), K, fp4=False), scales_to_atoms(sc, K)]
+    return tuple(out)
 
 
 def moe_dense(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, w13: torch.Tensor,
