@@ -167,8 +167,8 @@ def test_varlen_attention(d, causal):
 @pytest.mark.parametrize("T,E,H,k", [(64, 128, 2880, 4), (300, 128, 2880, 4), (16, 512, 2048, 10),
                                      (600, 128, 2880, 4)])
 def test_router_topk_and_argmax(T, E, H, k):
-    """T <= 512: the fused router kernel (fp32 logits); larger T: GEMM + top-k kernel.  The
-    chosen experts must be a top-k set of the fp32 reference logits up to bf16 rounding."""
+    """GEMM (bf16 logits) + top-k softmax kernel: the chosen experts must be a top-k set of
+    the fp32 reference logits up to bf16 rounding of the logits."""
     torch.manual_seed(5)
     x = torch.randn(T, H, device=DEV, dtype=torch.bfloat16)
     w = torch.randn(E, H, device=DEV, dtype=torch.bfloat16) * 0.02
@@ -179,7 +179,7 @@ def test_router_topk_and_argmax(T, E, H, k):
     got = ref_logits.gather(1, ids.long())
     assert (got >= kth - 0.02).all(), "selected an expert outside the top-k"
     assert (ids.long().sort(-1).values.diff(dim=-1) > 0).all(), "duplicate expert"
-    _close(wt, torch.softmax(got, -1), 2e-3, 2e-3, "router weights")
+    _close(wt, torch.softmax(got, -1), 1e-2, 1e-2, "router weights")
     lg = torch.randn(64, 25136, device=DEV, dtype=torch.bfloat16)
     val, idx = ops.argmax(lg)
     assert torch.equal(idx, lg.float().argmax(-1))

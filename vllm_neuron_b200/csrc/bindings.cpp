@@ -192,26 +192,6 @@ void sample(Tensor out, Tensor logits, Tensor temperature, Tensor top_k, Tensor 
            "sample");
 }
 
-void router_topk(Tensor ids, Tensor weights, Tensor x, Tensor w, c10::optional<Tensor> bias) {
-  check_cuda(x, "x");
-  TORCH_CHECK(x.is_contiguous() && w.is_contiguous() && x.scalar_type() == at::kBFloat16 &&
-                  w.scalar_type() == at::kBFloat16,
-              "router_topk: contiguous bf16 x and weight");
-  TORCH_CHECK(ids.scalar_type() == at::kInt && weights.scalar_type() == at::kFloat && ids.is_contiguous() &&
-                  weights.is_contiguous(),
-              "router_topk: int32 ids, fp32 weights");
-  TORCH_CHECK(x.size(1) == w.size(1), "router_topk: hidden mismatch");
-  const void* b = nullptr;
-  if (bias.has_value()) {
-    TORCH_CHECK(bias->scalar_type() == at::kBFloat16 && bias->numel() == w.size(0), "router_topk: bf16 bias [E]");
-    b = bias->data_ptr();
-  }
-  c10::cuda::CUDAGuard g(x.device());
-  check_rc(b200_router_topk(ids.data_ptr<int>(), weights.data_ptr<float>(), x.data_ptr(), w.data_ptr(), b, x.size(0),
-                            w.size(0), x.size(1), ids.size(1), stream()),
-           "router_topk");
-}
-
 }  // namespace
 
 void register_moe_ops(torch::Library& m);
@@ -243,7 +223,6 @@ TORCH_LIBRARY(b200, m) {
       "varlen_attention(Tensor(a!) out, Tensor q, Tensor k, Tensor v, Tensor cu_seqlens, float scale, bool causal, "
       "int max_seqlen) -> ()");
   m.def("topk_softmax(Tensor(a!) ids, Tensor(b!) weights, Tensor logits) -> ()");
-  m.def("router_topk(Tensor(a!) ids, Tensor(b!) weights, Tensor x, Tensor w, Tensor? bias) -> ()");
   m.def("argmax(Tensor(a!) vals, Tensor(b!) idx, Tensor logits) -> ()");
   m.def(
       "sample(Tensor(a!) out, Tensor logits, Tensor temperature, Tensor top_k, Tensor top_p, Tensor uniform, "
@@ -266,7 +245,6 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("paged_attention_prefill", &paged_attention_prefill);
   m.impl("varlen_attention", &varlen_attention);
   m.impl("topk_softmax", &topk_softmax);
-  m.impl("router_topk", &router_topk);
   m.impl("argmax", &argmax);
   m.impl("sample", &sample);
   register_moe_impls(m);

@@ -46,9 +46,6 @@ int b200_varlen_attention(void* out, const void* q, const void* k, const void* v
 
 int b200_topk_softmax(int* ids, float* weights, const float* logits, int T, int E, int k, cudaStream_t s);
 
-int b200_router_topk(int* ids, float* weights, const void* x, const void* w, const void* bias, int T, int E, int H,
-                     int k, cudaStream_t s);
-
 int b200_argmax(float* vals, int64_t* idx, const void* logits, int B, int V, int dtype, cudaStream_t s);
 
 int b200_sample(int64_t* out, const void* logits, const float* temperature, const int* top_k, const float* top_p,

@@ -221,15 +221,6 @@ def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqle
 def router_topk(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, top_k: int,
                 order: str = "topk_softmax") -> tuple[torch.Tensor, torch.Tensor]:
     """(topk_ids [T,k] int32, topk_weights [T,k] fp32)."""
-    T, H = x.shape
-    if (use_kernel(x) and order == "topk_softmax" and w.shape[0] <= 1024 and T <= 512 and H % 8 == 0
-            and H <= 8192 and top_k <= 16 and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
-            and (b is None or b.dtype == torch.bfloat16)):
-        # decode-sized batches: GEMM + bias + top-k + softmax in one kernel
-        ids = torch.empty(T, top_k, dtype=torch.int32, device=x.device)
-        wts = torch.empty(T, top_k, dtype=torch.float32, device=x.device)
-        _k().router_topk(ids, wts, x.contiguous(), w, b)
-        return ids, wts
     if use_kernel(x) and order == "topk_softmax" and w.shape[0] <= 1024:
         logits = F.linear(x.to(w.dtype), w, b).float()
         ids = torch.empty(x.shape[0], top_k, dtype=torch.int32, device=x.device)
