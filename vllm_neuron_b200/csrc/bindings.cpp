@@ -164,10 +164,12 @@ void varlen_attention(Tensor out, Tensor q, Tensor k, Tensor v, Tensor cu, doubl
 
 void topk_softmax(Tensor ids, Tensor weights, Tensor logits) {
   check_cuda(logits, "logits");
-  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.is_contiguous(), "fp32 contiguous logits");
+  TORCH_CHECK((logits.scalar_type() == at::kFloat || logits.scalar_type() == at::kBFloat16) &&
+                  logits.is_contiguous(),
+              "fp32 / bf16 contiguous logits");
   c10::cuda::CUDAGuard g(logits.device());
-  check_rc(b200_topk_softmax(ids.data_ptr<int>(), weights.data_ptr<float>(), logits.data_ptr<float>(),
-                             logits.size(0), logits.size(1), ids.size(1), stream()),
+  check_rc(b200_topk_softmax(ids.data_ptr<int>(), weights.data_ptr<float>(), logits.data_ptr(), logits.size(0),
+                             logits.size(1), ids.size(1), dt(logits), stream()),
            "topk_softmax");
 }
 

@@ -12,19 +12,20 @@
 
 namespace b200 {
 
-__global__ void topk_softmax_kernel(int* __restrict__ ids, float* __restrict__ w, const float* __restrict__ logits,
+template <typename LT>
+__global__ void topk_softmax_kernel(int* __restrict__ ids, float* __restrict__ w, const LT* __restrict__ logits,
                                     int T, int E, int k) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= T) return;
-  const float* row = logits + (size_t)warp * E;
+  const LT* row = logits + (size_t)warp * E;
   constexpr int kMaxPer = 32;  // E <= 1024
   float v[kMaxPer];
   const int per = (E + 31) / 32;
 #pragma unroll
   for (int i = 0; i < kMaxPer; ++i) {
     const int e = i * 32 + lane;
-    v[i] = (i < per && e < E) ? row[e] : -INFINITY;
+    v[i] = (i < per && e < E) ? to_float(row[e]) : -INFINITY;
   }
   float sel_v[16];
   int sel_i[16];
@@ -291,12 +292,19 @@ __global__ void __launch_bounds__(1024) sample_kernel(int64_t* __restrict__ out,
 
 using namespace b200;
 
-extern "C" int b200_topk_softmax(int* ids, float* weights, const float* logits, int T, int E, int k,
+extern "C" int b200_topk_softmax(int* ids, float* weights, const void* logits, int T, int E, int k, int dtype,
                                  cudaStream_t s) {
   if (E > 1024 || k > 16 || k > E) return kBadShape;
   if (T == 0) return 0;
   const int warps_per_block = 4;
-  topk_softmax_kernel<<<cdiv(T, warps_per_block), 32 * warps_per_block, 0, s>>>(ids, weights, logits, T, E, k);
+  if (dtype == kBF16)
+    topk_softmax_kernel<<<cdiv(T, warps_per_block), 32 * warps_per_block, 0, s>>>(
+        ids, weights, (const __nv_bfloat16*)logits, T, E, k);
+  else if (dtype == kF32)
+    topk_softmax_kernel<<<cdiv(T, warps_per_block), 32 * warps_per_block, 0, s>>>(ids, weights,
+                                                                                 (const float*)logits, T, E, k);
+  else
+    return kBadShape;
   return (int)cudaGetLastError();
 }
 

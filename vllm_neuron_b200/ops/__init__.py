@@ -222,7 +222,9 @@ def router_topk(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, top_k:
                 order: str = "topk_softmax") -> tuple[torch.Tensor, torch.Tensor]:
     """(topk_ids [T,k] int32, topk_weights [T,k] fp32)."""
     if use_kernel(x) and order == "topk_softmax" and w.shape[0] <= 1024:
-        logits = F.linear(x.to(w.dtype), w, b).float()
+        logits = F.linear(x.to(w.dtype), w, b)  # bf16 logits read directly by the top-k kernel
+        if logits.dtype not in (torch.bfloat16, torch.float32):
+            logits = logits.float()
         ids = torch.empty(x.shape[0], top_k, dtype=torch.int32, device=x.device)
         wts = torch.empty(x.shape[0], top_k, dtype=torch.float32, device=x.device)
         _k().topk_softmax(ids, wts, logits)
