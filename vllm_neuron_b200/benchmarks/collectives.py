@@ -1,0 +1,104 @@
+"""Layer-boundary collective microbenchmark (one process per GPU, under torchrun).
+
+    torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m vllm_neuron_b200.benchmarks.collectives
+
+For each token count T (hidden 2880, bf16) it times, with CUDA events after warm-up and as
+the maximum over ranks:
+* ``fused``: the one-shot NVLink all-reduce fused with bias + residual add + RMSNorm
+  (``csrc/comm.cu``), inside a CUDA graph of ``--iters`` back-to-back calls;
+* ``nccl``: NCCL all-reduce followed by the fused add + RMSNorm kernel, same graph setup.
+
+Roofline of the fused path: every rank must read the other ranks' partial rows over NVLink,
+(world - 1) * T * H * 2 bytes, at the measured 770 GB/s per direction, so
+``target_us = bytes / 770e3``; ``frac`` = target / achieved.  One JSON line per (T, path) on
+rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+import torch.distributed as dist
+
+LINK_GBS = 770.0
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--hidden", type=int, default=2880)
+    ap.add_argument("--tokens", default="1,16,64,256")
+    ap.add_argument("--iters", type=int, default=50)
+    a = ap.parse_args()
+    from vllm_neuron_b200 import ops
+    from vllm_neuron_b200.parallel import state as pstate
+    from vllm_neuron_b200.parallel.communicator import attach_communicators
+
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pstate.init_distributed_environment(world, rank, backend="nccl", local_rank=local, timeout_s=120)
+    ps = pstate.initialize_parallel_state(tp=world, timeout_s=120)
+    attach_communicators(ps, dev)
+    tp = ps.tp
+    H = a.hidden
+    w = torch.ones(H, device=dev)
+    for T in [int(t) for t in a.tokens.split(",")]:
+        x = torch.randn(T, H, device=dev).bfloat16()
+        res = torch.randn(T, H, device=dev).bfloat16()
+        bias = torch.zeros(H, device=dev).bfloat16()
+        for path in ("fused", "nccl"):
+            comm = tp.communicator
+
+            def step():
+                if path == "fused":
+                    return comm.all_reduce_add_rmsnorm(x, res, w, 1e-5, bias)
+                y = tp.all_reduce(x.clone()) if comm is None else _nccl(tp, x)
+                return ops.fused_add_rms_norm(y + bias, res, w, 1e-5)
+
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                for _ in range(3):
+                    step()
+            torch.cuda.current_stream().wait_stream(s)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(a.iters):
+                    step()
+            for _ in range(3):
+                g.replay()
+            dist.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            t = torch.tensor([e0.elapsed_time(e1) * 1000.0 / a.iters], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            us = t.item()
+            nbytes = (world - 1) * T * H * 2
+            target = nbytes / (LINK_GBS * 1e3)
+            if rank == 0:
+                print(json.dumps({"path": path, "world": world, "T": T, "H": H, "us": round(us, 2),
+                                  "nvlink_bytes_per_rank": nbytes, "target_us": round(target, 2),
+                                  "frac_of_roofline": round(target / us, 3)}), flush=True)
+            del g
+    torch.cuda.synchronize()
+    pstate.destroy_parallel_state()
+    dist.destroy_process_group()
+
+
+def _nccl(tp, x):
+    y = x.clone()
+    dist.all_reduce(y, group=tp.device_group)
+    return y
+
+
+if __name__ == "__main__":
+    main()
