@@ -1,6 +1,6 @@
 // Fused NVLink collectives for tensor-parallel decode.
 //
-// All-reduce (one-shot) fused with the ops that always follow it in the decoder:
+// All-reduce (one-shot, push) fused with the ops that always follow it in the decoder:
 //   out = RMSNorm(sum_ranks(partial) + bias + residual) * w,  residual <- the pre-norm sum
 // (or plain out = sum when no norm is requested).  This replaces, per layer, NCCL
 // all-reduce + a residual-add/RMSNorm kernel after the attention output projection and
@@ -9,17 +9,22 @@
 //
 // Memory: every rank owns one cudaMalloc'd region, mapped into its peers with CUDA IPC:
 //   [flags: kMaxBlocks x kMaxRanks u32][counters: kMaxBlocks u32][pad][slot 0][slot 1]
+// and each slot holds one receive area per source rank ([world][rows][H] bf16).
 // Protocol per call, independently in every CTA b (so it is CUDA-graph safe and needs no
 // host-side state):
 //   1. epoch = counters[b] + 1; slot = epoch & 1
-//   2. copy this CTA's rows of the local partial into my slot (local stores)
-//   3. __threadfence_system(); for each peer p: st.release.sys peer_p.flags[b][me] = epoch
-//   4. for each peer p: spin (bounded) until ld.acquire.sys my.flags[b][p] >= epoch
-//   5. read the rows from every peer's slot over NVLink (16-byte loads), reduce, add
-//      bias/residual, RMSNorm, store; counters[b] = epoch
-// Double buffering makes the slot written at epoch e disjoint from the one peers may still
-// read at epoch e-1; reuse two calls later is safe because passing barrier e-1 proves every
-// peer has finished epoch e-2 (stream order).  Waits give up after ~2 s and set status.
+//   2. push this CTA's rows of the local partial into every rank's receive area for this
+//      rank (NVLink stores, posted: no round trip); CTA barrier
+//   3. for each peer p: st.release.sys peer_p.flags[b][me] = epoch (the release covers the
+//      CTA's pushes)
+//   4. spin (bounded) on the local flags until every peer's CTA b has pushed (local loads)
+//   5. reduce the rows from the local receive areas (uncached loads), add bias/residual,
+//      RMSNorm, store; counters[b] = epoch
+// Pushing instead of pulling turns the NVLink traffic into posted writes and the waits and
+// reductions into local memory accesses.  Double buffering makes the slot written at epoch e
+// disjoint from the one a peer may still read at epoch e-1; reuse two calls later is safe
+// because passing barrier e-1 proves every peer has finished epoch e-2 (stream order).
+// Waits give up after ~2 s and set status.
 #include "common.cuh"
 #include "launch.h"
 
@@ -76,22 +81,30 @@ __global__ void __launch_bounds__(256) allreduce_fused_kernel(CommPeers peers, c
   __shared__ float red[32];
   __shared__ uint32_t s_epoch;
   const int b = blockIdx.x;
+  // a CTA without rows takes no part (every rank sees the same T, so CTA b's epoch count
+  // stays equal across ranks)
+  if (b >= T) return;
   uint8_t* me = peers.base[peers.rank];
   if (threadIdx.x == 0) s_epoch = counters_of(me)[b] + 1;
   __syncthreads();
   const uint32_t epoch = s_epoch;
   const int slot = epoch & 1;
   const int nchunk = H / 8;
-  // 2. stage my rows into my slot
-  uint4* my_slot = reinterpret_cast<uint4*>(slot_of(me, slot, peers.slot_bytes));
+  const size_t part = peers.slot_bytes / peers.world;  // one source rank's receive area
+  // 2. push my rows into every rank's receive area for me
   for (int r = b; r < T; r += gridDim.x) {
     const uint4* src = reinterpret_cast<const uint4*>(in + (size_t)r * H);
-    for (int c = threadIdx.x; c < nchunk; c += blockDim.x) my_slot[(size_t)r * nchunk + c] = src[c];
+    for (int c = threadIdx.x; c < nchunk; c += blockDim.x) {
+      const uint4 v = src[c];
+      const size_t off = (size_t)peers.rank * part + ((size_t)r * nchunk + c) * 16;
+      for (int p = 0; p < peers.world; ++p)
+        *reinterpret_cast<uint4*>(slot_of(peers.base[p], slot, peers.slot_bytes) + off) = v;
+    }
   }
+  // the release store below is cumulative over the CTA's pushes (ordered by the barrier)
   __syncthreads();
-  // 3. signal every peer, 4. wait for every peer
+  // 3. signal every peer, 4. wait for every peer (local flags)
   if (threadIdx.x < peers.world) {
-    __threadfence_system();
     const int p = threadIdx.x;
     st_release_sys(flags_of(peers.base[p]) + b * kMaxRanks + peers.rank, epoch);
     const uint32_t* f = flags_of(me) + b * kMaxRanks + p;
@@ -120,9 +133,9 @@ __global__ void __launch_bounds__(256) allreduce_fused_kernel(CommPeers peers, c
       if (c < nchunk) {
 #pragma unroll
         for (int q = 0; q < 8; ++q) v[i][q] = 0.f;
+        const uint8_t* mine = slot_of(me, slot, peers.slot_bytes);
         for (int p = 0; p < peers.world; ++p) {
-          const uint8_t* ps = slot_of(peers.base[p], slot, peers.slot_bytes);
-          const uint4 u = ld_volatile_v4(ps + ((size_t)r * nchunk + c) * 16);
+          const uint4 u = ld_volatile_v4(mine + (size_t)p * part + ((size_t)r * nchunk + c) * 16);
           const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(&u);
 #pragma unroll
           for (int q = 0; q < 8; ++q) v[i][q] += __bfloat162float(hb[q]);
@@ -210,7 +223,7 @@ extern "C" int b200_allreduce_fused(void* const* bases, int rank, int world, siz
                                     void* out, void* residual, const void* bias, const float* w, float eps, int T,
                                     int H, int num_blocks, int* status, cudaStream_t s) {
   if (world > kMaxRanks || world < 1 || H % 8 || H > 8192 || T < 0) return kBadShape;
-  if ((size_t)T * H * 2 > slot_bytes) return kBadShape;
+  if ((size_t)T * H * 2 * world > slot_bytes || (slot_bytes / world) % 16) return kBadShape;
   if (num_blocks < 1 || num_blocks > kMaxBlocks) return kBadShape;
   if (T == 0) return 0;
   CommPeers peers{};

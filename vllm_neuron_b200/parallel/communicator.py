@@ -24,7 +24,7 @@ logger = init_logger(__name__)
 
 
 class FusedCommunicator:
-    def __init__(self, group, device: torch.device, max_tokens: int = 512, max_hidden: int = 8192,
+    def __init__(self, group, device: torch.device, max_tokens: int = 256, max_hidden: int = 8192,
                  num_blocks: int = 64):
         from ..ops import _ext
 
@@ -35,7 +35,8 @@ class FusedCommunicator:
         self.world = group.world_size
         self.num_blocks = num_blocks
         self.max_hidden = max_hidden
-        self.slot_bytes = max_tokens * max_hidden * 2
+        # one receive area per source rank in each of the two slots
+        self.slot_bytes = group.world_size * max_tokens * max_hidden * 2
         self.max_elems = max_tokens * max_hidden
         ops = torch.ops.b200
         with torch.cuda.device(device):
