@@ -107,6 +107,7 @@ class KVCacheManager:
         self.pool = BlockPool(num_blocks, enable_caching)
         self.enable_caching = enable_caching
         self._hashes: dict[str, list[bytes]] = {}
+        self._registered: dict[str, int] = {}  # leading blocks already registered per request
 
     # -------------------------------------------------------------- prefix cache
     def _block_hashes(self, req: Request, upto_tokens: int) -> list[bytes]:
@@ -146,6 +147,8 @@ class KVCacheManager:
         return self.pool.num_free - n >= watermark
 
     def allocate_slots(self, req: Request, num_new_tokens: int, computed_blocks: list[int] | None = None) -> bool:
+        if not computed_blocks and req.num_computed_tokens + num_new_tokens <= len(req.block_ids) * self.block_size:
+            return True  # the common decode case: the current block has room
         computed_blocks = computed_blocks or []
         n = self.blocks_needed(req, num_new_tokens, len(computed_blocks))
         # cached blocks taken from the free queue reduce the free count too
@@ -162,15 +165,20 @@ class KVCacheManager:
         """Register blocks that became full after this step's tokens were computed."""
         if not self.enable_caching:
             return
-        n_full = min(req.num_computed_tokens, req.num_tokens) // self.block_size
+        n_full = min(min(req.num_computed_tokens, req.num_tokens) // self.block_size, len(req.block_ids))
+        done = self._registered.get(req.request_id, 0)
+        if n_full <= done:
+            return
         hs = self._block_hashes(req, n_full * self.block_size)
-        for i in range(min(n_full, len(req.block_ids))):
+        for i in range(done, n_full):
             self.pool.register(req.block_ids[i], hs[i])
+        self._registered[req.request_id] = n_full
 
     def free(self, req: Request) -> None:
         self.pool.free_blocks(req.block_ids)
         req.block_ids = []
         self._hashes.pop(req.request_id, None)
+        self._registered.pop(req.request_id, None)
 
     @property
     def usage(self) -> float:

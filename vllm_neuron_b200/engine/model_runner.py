@@ -217,24 +217,28 @@ class ModelRunner:
 
     # ------------------------------------------------------------------ inputs
     def _fill_sampling(self, so: SchedulerOutput, B: int) -> bool:
+        n = len(so.seqs)
+        temp, topk, topp, unif = (self.h_temp.numpy(), self.h_topk.numpy(), self.h_topp.numpy(),
+                                  self.h_unif.numpy())
         all_greedy = True
         for i, s in enumerate(so.seqs):
             sp = s.sampling_params
-            t = 0.0 if sp is None else float(sp.temperature)
-            if self.all_greedy_cfg:
-                t = 0.0
-            self.h_temp[i] = t
-            self.h_topk[i] = 0 if sp is None or sp.top_k <= 0 else sp.top_k
-            self.h_topp[i] = 1.0 if sp is None else sp.top_p
-            seed = self.seed if sp is None or sp.seed is None else sp.seed
-            self.h_unif[i] = request_uniform(seed, s.req_id, s.sample_seq) if t > 0 else 0.0
-            all_greedy &= t <= 0
-        n = len(so.seqs)
+            if sp is None or self.all_greedy_cfg or sp.temperature <= 0:
+                temp[i] = 0.0
+                topk[i] = 0
+                topp[i] = 1.0
+                unif[i] = 0.0
+                continue
+            all_greedy = False
+            temp[i] = sp.temperature
+            topk[i] = sp.top_k if sp.top_k > 0 else 0
+            topp[i] = sp.top_p
+            unif[i] = request_uniform(self.seed if sp.seed is None else sp.seed, s.req_id, s.sample_seq)
         if B > n:
-            self.h_temp[n:B] = 0
-            self.h_topk[n:B] = 0
-            self.h_topp[n:B] = 1
-            self.h_unif[n:B] = 0
+            temp[n:B] = 0
+            topk[n:B] = 0
+            topp[n:B] = 1
+            unif[n:B] = 0
         return all_greedy
 
     def _fill_spec_sampling(self, so: SchedulerOutput, n_sel: int) -> None:
@@ -279,21 +283,36 @@ class ModelRunner:
         n_sel = 0
         mm_rows: list = []
         has_mrope = False
+        bs = self.bs
+        plain_decode = so.kind == "decode" and all(len(x.token_ids) == 1 for x in seqs)
         for i, s in enumerate(seqs):
             k = len(s.token_ids)
+            req = s.request
+            nb = len(s.block_ids)
+            # block-table entries past a sequence's own blocks are never read (its length
+            # bounds every kernel), so rows are not cleared
+            bt[i, :nb] = s.block_ids
+            sl[i] = s.seq_len
+            if plain_decode:  # one token: scalar work only
+                p0 = s.start_pos
+                ids[t] = s.token_ids[0]
+                delta = req.mrope_delta if req is not None else 0
+                pos[t] = p0 + delta
+                slot[t] = s.block_ids[p0 // bs] * bs + p0 % bs
+                lidx[n_sel] = t
+                n_sel += 1
+                t += 1
+                qsl[i + 1] = t
+                max_s = max(max_s, s.seq_len)
+                continue
             ids[t:t + k] = s.token_ids
             p = np.arange(s.start_pos, s.start_pos + k)
-            req = s.request
             delta = req.mrope_delta if req is not None else 0
             pos[t:t + k] = p + delta if (delta and so.kind == "decode") else p
             if req is not None and req.mrope_positions is not None and so.kind == "prefill":
                 has_mrope = True
             blocks = np.asarray(s.block_ids, dtype=np.int64)
-            slot[t:t + k] = blocks[p // self.bs] * self.bs + p % self.bs
-            nb = len(s.block_ids)
-            bt[i, :nb] = s.block_ids
-            bt[i, nb:] = 0
-            sl[i] = s.seq_len
+            slot[t:t + k] = blocks[p // bs] * bs + p % bs
             if so.kind == "decode" and s.spec_token_ids:
                 lidx[n_sel:n_sel + k] = np.arange(t, t + k)
                 n_sel += k

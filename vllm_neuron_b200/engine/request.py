@@ -54,6 +54,10 @@ class Request:
     def all_token_ids(self) -> list[int]:
         return self.prompt_token_ids + self.output_token_ids
 
+    def token_at(self, i: int) -> int:
+        n = len(self.prompt_token_ids)
+        return self.prompt_token_ids[i] if i < n else self.output_token_ids[i - n]
+
     @property
     def num_tokens(self) -> int:
         return len(self.prompt_token_ids) + len(self.output_token_ids)

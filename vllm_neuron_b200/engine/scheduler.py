@@ -226,7 +226,7 @@ class Scheduler:
         for req in running:
             spec = req.spec_token_ids[:k]
             s = req.num_computed_tokens
-            toks = [req.all_token_ids[s]] + spec if s < req.num_tokens else spec
+            toks = [req.token_at(s)] + spec if s < req.num_tokens else spec
             seqs.append(ScheduledSeq(req.request_id, toks, s, req.block_ids, True, spec_token_ids=spec,
                                      sampling_params=req.sampling_params, sample_seq=req.sample_seq, request=req))
         if not seqs:
