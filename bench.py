@@ -10,9 +10,10 @@ All 64 prompts are prefilled through the engine, then decode runs at batch 64:
   (forward + LM head + sampling for 64 sequences) between CUDA events, after W warm-up
   steps; tokens/s = 64 * K / t, t = max over ranks.  Weights (~60 GB) exceed L2, so no
   flush is needed between steps.
-* ``e2e``    the same metric through the public engine API (``LLMEngine.step``): every
-  step schedules, stages its inputs in pinned host memory, copies them H2D, replays the
-  graph and reads the sampled ids back D2H.
+* ``e2e``    the same metric through the public engine API (``LLMEngine.step``, asynchronous
+  scheduling): every step schedules, stages its inputs in pinned host memory, copies them
+  H2D, replays the graph and reads the sampled ids back D2H (the host work of step k+1
+  overlaps step k on the GPU).
 Parallelism for N GPUs: attention TP=N (heads), experts EP=N, one all-reduce after
 attention and one after the MoE per layer (NCCL); total concurrency stays 64 (strong
 scaling).  ``--impl reference`` runs the reference plugin when it can run here.
@@ -165,7 +166,7 @@ def main() -> None:
     t0 = time.time()
     llm = LLM(hf_config=hf, load_format="dummy", dtype="bfloat16", tensor_parallel_size=N,
               max_model_len=max_len, max_num_seqs=C, max_num_batched_tokens=4096, block_size=32,
-              max_num_prefills_per_step=2, spmd=N > 1, seed=0,
+              max_num_prefills_per_step=2, spmd=N > 1, seed=0, async_scheduling=True,
               additional_config={"neuron_config": {"ep_degree": N, "quantization": "mxfp4",
                                                    "num_seqs_buckets": [C]}})
     eng = llm.engine

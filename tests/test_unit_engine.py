@@ -1,5 +1,7 @@
 """Block manager (prefix caching), scheduler policy and request lifecycle."""
 
+import pytest
+
 from vllm_neuron_b200.engine.block_manager import KVCacheManager
 from vllm_neuron_b200.engine.request import Request, RequestStatus
 from vllm_neuron_b200.engine.sampling_params import SamplingParams
@@ -85,3 +87,40 @@ def test_stop_conditions():
     assert not r2.check_stop(100)
     r2.output_token_ids.append(42)
     assert not r2.check_stop(100)
+
+
+@pytest.mark.parametrize("temperature", [0.0, 0.8])
+def test_async_scheduling_matches_sync(temperature):
+    """Asynchronous scheduling (step k+1 staged while step k runs, input tokens taken from
+    the device) produces exactly the tokens of synchronous scheduling, including requests that
+    stop early on a stop token and requests that arrive while others decode."""
+    from vllm_neuron_b200 import LLM, SamplingParams
+    from tiny_configs import TINY_GPT_OSS, workload
+
+    prompts = workload(n=5, lo=8, hi=40)
+    outs = {}
+    for mode in (False, True):
+        llm = LLM(hf_config=dict(TINY_GPT_OSS), load_format="dummy", dtype="float32", max_model_len=256,
+                  max_num_seqs=8, max_num_batched_tokens=128, block_size=16, device="cpu", seed=11,
+                  async_scheduling=mode, additional_config={"neuron_config": {"quantization": "bf16"}})
+        sps = [SamplingParams(temperature=temperature, max_tokens=12 + i, ignore_eos=True, seed=3,
+                              stop_token_ids=[7] if i == 2 else None) for i in range(len(prompts))]
+        eng = llm.engine
+        for i, p in enumerate(prompts[:3]):
+            eng.add_request(f"a{i}", p, sps[i])
+        res = {}
+        steps = 0
+        while eng.has_unfinished_requests():
+            for o in eng.step():
+                if o.finished:
+                    res[o.request_id] = o.outputs[0].token_ids
+            steps += 1
+            if steps == 6:  # late arrivals join while the first requests decode
+                for i, p in enumerate(prompts[3:], start=3):
+                    eng.add_request(f"a{i}", p, sps[i])
+        outs[mode] = res
+        assert eng._inflight is None
+        if mode:
+            assert eng.async_stats["lookahead"] > 10, eng.async_stats
+        llm.shutdown()
+    assert outs[True] == outs[False]

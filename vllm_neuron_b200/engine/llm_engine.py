@@ -80,6 +80,11 @@ class LLMEngine:
         self.replica = rank // cfg.tensor_parallel_size
         self._rr = 0
         self._remote: set[str] = set()  # unfinished requests owned by other replicas
+        # asynchronous scheduling (single rank or SPMD; decode steps with CUDA graphs)
+        self._async = bool(cfg.async_scheduling) and self.dp == 1 and mode in ("single", "spmd") \
+            and self.proposer is None
+        self._inflight = None
+        self.async_stats = {"launched": 0, "lookahead": 0}
         logger.info("engine ready: rank %d/%d mode=%s kv_blocks=%d", rank, world_size, mode, n_blocks)
 
     # ------------------------------------------------------------------ intake
@@ -180,7 +185,7 @@ class LLMEngine:
         self.scheduler.abort(request_id)
 
     def has_unfinished_requests(self) -> bool:
-        return self.scheduler.has_unfinished() or bool(self._remote)
+        return self.scheduler.has_unfinished() or bool(self._remote) or self._inflight is not None
 
     # -------------------------------------------------------------------- step
     def _sync_requests(self) -> None:
@@ -210,12 +215,56 @@ class LLMEngine:
             return []
         if self.dp > 1:
             return self._step_dp()
+        if self._async:
+            return self._step_async()
         so = self.scheduler.schedule()
         failed = [self._make_output(r, True) for r in self.scheduler.failed]
         self.scheduler.failed = []
         if so.kind == "idle":
             return failed
         return failed + self._run(so)
+
+    def _step_async(self) -> list[RequestOutput]:
+        """Asynchronous scheduling (``async_scheduling=True``): while decode step k runs on
+        the GPU, the host schedules and stages step k+1 (its input tokens are step k's sampled
+        ids, taken on the device) and only then waits for step k's ids, appends them and
+        checks stop conditions; outputs therefore trail the GPU by one step.  Anything else
+        (prefill, preemption, a request at its last token) drains the pipeline first and runs
+        synchronously."""
+        runner, sched = self.worker.runner, self.scheduler
+        prev = self._inflight
+        if prev is not None:
+            nxt = sched.schedule_lookahead()
+            cur = None
+            if nxt is not None:
+                cur = runner.launch(nxt, prev)
+                self.async_stats["lookahead"] += 1
+                for s in nxt.seqs:
+                    s.request.num_inflight += 1
+            outs = self._commit(prev)
+            self._inflight = cur
+            return outs
+        so = sched.schedule()
+        failed = [self._make_output(r, True) for r in sched.failed]
+        sched.failed = []
+        if so.kind == "idle":
+            return failed
+        if runner.can_launch_async(so):
+            self._inflight = runner.launch(so)
+            self.async_stats["launched"] += 1
+            for s in so.seqs:
+                s.request.num_inflight += 1
+            return failed
+        return failed + self._run(so)
+
+    def _commit(self, step) -> list[RequestOutput]:
+        sampled = self.worker.runner.commit(step)
+        for s in step.so.seqs:
+            s.request.num_inflight -= 1
+        finished = self.scheduler.update_from_output(step.so, sampled, time.monotonic())
+        fin = {r.request_id for r in finished}
+        return [self._make_output(s.request, s.request.status.finished) for s in step.so.seqs
+                if s.req_id in sampled and (s.req_id in fin or not s.request.status.finished)]
 
     def _step_dp(self) -> list[RequestOutput]:
         """One lockstep step of a data-parallel replica.  Replicas share the MoE layers'

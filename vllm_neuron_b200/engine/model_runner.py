@@ -50,6 +50,22 @@ class _GraphEntry:
     batch: int
 
 
+class _DoneEvent:
+    def synchronize(self) -> None:
+        return None
+
+
+@dataclass
+class AsyncStep:
+    """A launched decode step whose sampled ids are still being copied to the host."""
+
+    so: SchedulerOutput
+    n_sel: int
+    host: torch.Tensor
+    event: object
+    row_of: dict
+
+
 class ModelRunner:
     def __init__(self, cfg: EngineConfig, model: torch.nn.Module, device: torch.device, tp_group,
                  vocab_size: int):
@@ -106,6 +122,13 @@ class ModelRunner:
         self.d_topp = torch.ones(B, dtype=torch.float32, device=d)
         self.d_unif = torch.zeros(B, dtype=torch.float32, device=d)
         self.d_out = torch.zeros(B * (1 + self._num_spec()), dtype=torch.int64, device=d)
+        # asynchronous decode: input rows taken from the previous step's sampled ids, and two
+        # host buffers so one step's D2H never overwrites the ids being read for the last one
+        self.h_src = mk(B, torch.int64)
+        self.d_src = torch.zeros(B, dtype=torch.int64, device=d)
+        self.h_out_async = [mk(B, torch.int64), mk(B, torch.int64)]
+        self._parity = 0
+        self._h2d_done = None
         # per verified position (speculative decoding with sampling)
         P = B * (1 + self._num_spec())
         self.h_pos_params = mk((6, P), torch.float32)  # temp, top_k, top_p, draft, u_accept, u_sample
@@ -263,6 +286,9 @@ class ModelRunner:
 
     def _prepare(self, so: SchedulerOutput, pad_to: int | None,
                  pad_tokens: int | None = None) -> tuple[AttentionMetadata, int, int, bool]:
+        if self._h2d_done is not None:  # an asynchronous step may still be reading the staging buffers
+            self._h2d_done.synchronize()
+            self._h2d_done = None
         seqs = so.seqs
         n = len(seqs)
         B = pad_to or n
@@ -535,6 +561,65 @@ class ModelRunner:
         if g.world_size > 1:
             logits = g.all_gather(logits, dim=-1)
         return logits[:, :vocab_size]
+
+    # ---------------------------------------------------------- async decode steps
+    def can_launch_async(self, so: SchedulerOutput) -> bool:
+        return (so.kind == "decode" and bool(so.seqs) and self.capture is None and self.replacer is None
+                and all(len(s.token_ids) == 1 and not s.spec_token_ids for s in so.seqs))
+
+    def _event(self):
+        if self.device.type == "cuda":
+            ev = torch.cuda.Event()
+            ev.record()
+            return ev
+        return _DoneEvent()
+
+    @torch.inference_mode()
+    def launch(self, so: SchedulerOutput, prev: "AsyncStep | None" = None) -> "AsyncStep":
+        """Start a plain decode step without waiting for it: stage the inputs, take the input
+        token of every sequence that was in ``prev`` from ``prev``'s sampled ids in device
+        memory, replay the decode graph and queue the D2H copy of the sampled ids.
+        ``commit`` waits for it."""
+        self.step_count += 1
+        n = len(so.seqs)
+        pad_to = get_bucket_for_count(n, self.decode_buckets) if self.use_graphs else n
+        NUM_SEQS_PADDING.labels(model_name=self.cfg.served_model_name or "model").observe(pad_to - n)
+        meta, T, n_sel, greedy = self._prepare(so, pad_to)
+        if prev is not None:
+            src = self.h_src.numpy()
+            src[:pad_to] = -1
+            for i, s in enumerate(so.seqs):
+                src[i] = prev.row_of.get(s.req_id, -1)
+            self.d_src[:pad_to].copy_(self.h_src[:pad_to], non_blocking=True)
+            idx = self.d_src[:pad_to]
+            prev_ids = self.d_out[:pad_to].index_select(0, idx.clamp(min=0))
+            self.d_ids[:pad_to] = torch.where(idx >= 0, prev_ids, self.d_ids[:pad_to])
+        self._h2d_done = self._event()  # the staging buffers are free again after this point
+        if self.use_graphs:
+            key = (pad_to, greedy)
+            entry = self.graphs.get(key)
+            if entry is None:
+                if self.state_caches is not None:
+                    self.d_sslot[:pad_to].fill_(self.scratch_slot)
+                entry = self._capture(pad_to, greedy, meta, T, n_sel)
+                if self.state_caches is not None:
+                    self.d_sslot[:pad_to].copy_(self.h_sslot[:pad_to], non_blocking=True)
+            entry.graph.replay()
+            GRAPH_REPLAY_COUNT.labels(model_name=self.cfg.served_model_name or "model",
+                                      bucket_name=f"decode_b{pad_to}").inc()
+        else:
+            self._forward_sample(meta, T, n_sel, greedy)
+        self._parity ^= 1
+        host = self.h_out_async[self._parity]
+        host[:n_sel].copy_(self.d_out[:n_sel], non_blocking=self.device.type == "cuda")
+        ev = self._event()
+        self.d2h_bytes_last = n_sel * 8
+        return AsyncStep(so, n_sel, host, ev, {s.req_id: i for i, s in enumerate(so.seqs)})
+
+    def commit(self, step: "AsyncStep") -> dict[str, list[int]]:
+        step.event.synchronize()
+        toks = step.host[:step.n_sel].tolist()
+        return {s.req_id: [toks[i]] for i, s in enumerate(step.so.seqs) if s.sample}
 
     def _capture(self, B: int, greedy: bool, meta: AttentionMetadata, T: int, n_sel: int) -> _GraphEntry:
         t0 = time.time()

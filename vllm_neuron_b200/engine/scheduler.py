@@ -233,6 +233,29 @@ class Scheduler:
             return SchedulerOutput("idle", [], preempted, finished)
         return SchedulerOutput("decode", seqs, preempted, finished)
 
+    def schedule_lookahead(self) -> SchedulerOutput | None:
+        """Asynchronous scheduling: the next decode step while the previous one is still on
+        the GPU.  Every running request feeds the token that the in-flight step is sampling
+        (the runner takes it from device memory), at position num_computed + num_inflight.
+        Returns None when that is not possible (prefill work waiting, speculation, a request
+        at its token limit, no free KV block): the caller then drains the pipeline."""
+        if self.num_spec_tokens or self.waiting or not self.running:
+            return None
+        seqs = []
+        for req in self.running:
+            if self._is_prefill(req) or req.num_inflight != 1:
+                return None
+            if len(req.output_token_ids) + 1 >= req.max_tokens:
+                return None  # the in-flight token ends this request: nothing to run ahead
+            if not self.kv.allocate_slots(req, 2):  # in-flight token + the new one
+                return None
+            s = req.num_computed_tokens + 1
+            seqs.append(ScheduledSeq(req.request_id, [0], s, req.block_ids, True,
+                                     sampling_params=req.sampling_params, sample_seq=req.sample_seq + 1,
+                                     request=req))
+        finished, self._finished_ids = self._finished_ids, []
+        return SchedulerOutput("decode", seqs, finished=finished)
+
     def _remote_prefill_tokens(self, req: Request) -> int:
         p = req.kv_transfer_params or {}
         if self.connector is None or not self.connector.is_consumer or not p.get("do_remote_prefill"):

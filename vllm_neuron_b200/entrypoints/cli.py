@@ -25,6 +25,8 @@ def _engine_args(ap: argparse.ArgumentParser) -> None:
     ap.add_argument("--gpu-memory-utilization", type=float, default=0.9)
     ap.add_argument("--enable-prefix-caching", action="store_true")
     ap.add_argument("--enforce-eager", action="store_true")
+    ap.add_argument("--async-scheduling", action="store_true",
+                    help="stage decode step k+1 on the host while step k runs on the GPU")
     ap.add_argument("--load-format", default="auto")
     ap.add_argument("--dtype", default="bfloat16")
     ap.add_argument("--seed", type=int, default=0)
@@ -43,7 +45,8 @@ def engine_kwargs(a) -> dict:
               enable_prefix_caching=a.enable_prefix_caching, enforce_eager=a.enforce_eager,
               load_format=a.load_format, dtype=a.dtype, seed=a.seed, speculative_config=a.speculative_config,
               kv_transfer_config=a.kv_transfer_config, additional_config=a.additional_config,
-              served_model_name=a.served_model_name, enable_expert_parallel=a.enable_expert_parallel)
+              served_model_name=a.served_model_name, enable_expert_parallel=a.enable_expert_parallel,
+              async_scheduling=a.async_scheduling)
     if a.hf_config is not None:
         kw["hf_config"] = a.hf_config
         kw["load_format"] = "dummy"
