@@ -184,7 +184,8 @@ def test_moe_mxfp8_experts(T, E, H, I, k):
     w13q = ref.dequant_mxfp8(untile_values(t13, 2 * I, H, False).view(torch.float8_e4m3fn),
                              atoms_to_scales(s13, 2 * I, H))
     w2q = ref.dequant_mxfp8(untile_values(t2, H, I, False).view(torch.float8_e4m3fn), atoms_to_scales(s2, H, I))
-    assert torch.allclose(w13q, interleave_gate_up(w13), atol=0, rtol=0.07)
+    wref = interleave_gate_up(w13)
+    assert (w13q - wref).norm() / wref.norm() < 0.04  # e4m3 with a power-of-two scale per 32
     want = ref.moe_experts(x, ids, wts, w13q, None, w2q, None, 1.0, None, True, 0, "silu")
     rel = (got.float() - want.float()).norm() / want.float().norm()
     assert rel < 0.05, rel  # activations are MXFP8-quantised inside the kernel
