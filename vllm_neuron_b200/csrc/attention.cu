@@ -21,6 +21,7 @@
 //   prefill: one CTA per (64-query tile, query head, sequence), K/V read through the block
 //            table, so chunked prefill and prefix-cache hits need no gather.
 #include "launch.h"
+#include "launch_pdl.h"
 #include "mma_utils.cuh"
 #include "noalloc.h"
 
@@ -110,6 +111,8 @@ __global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const 
                                                      int nq, int nkv, int q_stride, int bs, int max_blocks, int window,
                                                      float scale_log2, float v_scale, float* __restrict__ ws,
                                                      int num_splits) {
+  pdl_wait();  // predecessor output visible (programmatic dependent launch)
+  pdl_trigger();
   constexpr int C = D / 8;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(smem_raw);            // [2][64*D]
@@ -321,6 +324,8 @@ __global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const 
 template <int D, typename T>
 __global__ void decode_combine_kernel(T* __restrict__ out, const float* __restrict__ ws,
                                       const float* __restrict__ sinks, int nq, int num_splits, float v_scale) {
+  pdl_wait();  // predecessor output visible (programmatic dependent launch)
+  pdl_trigger();
   const int head = blockIdx.x, b = blockIdx.y;
   const float* w = ws + ((size_t)b * nq + head) * num_splits * (D + 1);
   float M = sinks ? sinks[head] * kLog2e : -INFINITY;
@@ -356,10 +361,10 @@ static int launch_decode(void* out, const void* q, const void* kc, const void* v
     attr_set = true;
   }
   dim3 grid(num_splits, nkv, B);
-  kern<<<grid, 128, smem, s>>>((T*)out, (const T*)q, (const CT*)kc, (const CT*)vc, bt, sl, sinks, nq, nkv, q_stride,
+  launch_k(kern, dim3(grid), dim3(128), smem, s, (T*)out, (const T*)q, (const CT*)kc, (const CT*)vc, bt, sl, sinks, nq, nkv, q_stride,
                                bs, max_blocks, window, scale * k_scale * kLog2e, v_scale, ws, num_splits);
   if (num_splits > 1) {
-    decode_combine_kernel<D, T><<<dim3(nq, B), D < 128 ? D : 128, 0, s>>>((T*)out, ws, sinks, nq, num_splits,
+    launch_k(decode_combine_kernel<D, T>, dim3(nq, B), dim3(D < 128 ? D : 128), 0, s, (T*)out, ws, sinks, nq, num_splits,
                                                                            v_scale);
   }
   return (int)cudaGetLastError();
@@ -380,6 +385,8 @@ __global__ void __launch_bounds__(128) prefill_kernel(T* __restrict__ out, const
                                                       const int* __restrict__ qsl, const float* __restrict__ sinks,
                                                       int nq, int nkv, int q_stride, int kv_stride, int window,
                                                       int causal, float scale_log2, float v_scale) {
+  pdl_wait();  // predecessor output visible (programmatic dependent launch)
+  pdl_trigger();
   // DP: head dim padded to a multiple of 16 for the QK^T k-steps (72 -> 80)
   constexpr int C = DP / 8;
   constexpr int kTile = kKT * ((C % 8 == 0) ? C : (C | 1)) * 8;  // elements per K or V tile
@@ -602,7 +609,7 @@ static int launch_prefill(void* out, const void* q, const void* kc, const void* 
     attr_set = true;
   }
   dim3 grid(cdiv(max_q, 64), nq, B);
-  kern<<<grid, 128, smem, s>>>((T*)out, (const T*)q, (const CT*)kc, (const CT*)vc, pk, sl, qsl, sinks, nq, nkv,
+  launch_k(kern, dim3(grid), dim3(128), smem, s, (T*)out, (const T*)q, (const CT*)kc, (const CT*)vc, pk, sl, qsl, sinks, nq, nkv,
                                q_stride, kv_stride, window, causal, scale * k_scale * kLog2e, v_scale);
   return (int)cudaGetLastError();
 }

@@ -26,6 +26,7 @@
 // because passing barrier e-1 proves every peer has finished epoch e-2 (stream order).
 // Waits give up after ~2 s and set status.
 #include "common.cuh"
+#include "launch_pdl.h"
 #include "launch.h"
 
 namespace b200 {
@@ -78,6 +79,8 @@ __global__ void __launch_bounds__(256) allreduce_fused_kernel(CommPeers peers, c
                                                               const __nv_bfloat16* __restrict__ bias,
                                                               const float* __restrict__ w, float eps, int T, int H,
                                                               int* status) {
+  pdl_wait();  // predecessor output visible (programmatic dependent launch)
+  pdl_trigger();
   __shared__ float red[32];
   __shared__ uint32_t s_epoch;
   const int b = blockIdx.x;
@@ -232,11 +235,11 @@ extern "C" int b200_allreduce_fused(void* const* bases, int rank, int world, siz
   peers.world = world;
   peers.slot_bytes = slot_bytes;
   if (w != nullptr)
-    allreduce_fused_kernel<true><<<num_blocks, 256, 0, s>>>(peers, (const __nv_bfloat16*)in, (__nv_bfloat16*)out,
+    launch_k(allreduce_fused_kernel<true>, dim3(num_blocks), dim3(256), 0, s, peers, (const __nv_bfloat16*)in, (__nv_bfloat16*)out,
                                                            (__nv_bfloat16*)residual, (const __nv_bfloat16*)bias, w,
                                                            eps, T, H, status);
   else
-    allreduce_fused_kernel<false><<<num_blocks, 256, 0, s>>>(peers, (const __nv_bfloat16*)in, (__nv_bfloat16*)out,
+    launch_k(allreduce_fused_kernel<false>, dim3(num_blocks), dim3(256), 0, s, peers, (const __nv_bfloat16*)in, (__nv_bfloat16*)out,
                                                             nullptr, nullptr, nullptr, eps, T, H, status);
   return (int)cudaGetLastError();
 }

@@ -72,4 +72,13 @@ B200_D void record(int* status, int code, int where, int value) {
 }
 B200_D bool misaligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) != 0; }
 
+// Programmatic dependent launch: kernels of the decode chain are launched with
+// programmatic stream serialisation (launch_k below), so a kernel's CTAs may start while its
+// predecessor is still finishing.  pdl_wait() blocks until the predecessor grid has completed
+// and its memory is visible (a no-op when launched normally); it must precede every read of the
+// predecessor's output.  pdl_trigger() lets the successor grid launch once every CTA of this
+// grid has started and triggered.
+B200_D void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+B200_D void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 }  // namespace b200

@@ -23,6 +23,7 @@
 //     SwiGLU across the interleaved row pairs; GEMM2 adds the bias, scales by the route
 //     affinity and writes the per-route row; a reduce kernel sums each token's routes.
 #include "launch.h"
+#include "launch_pdl.h"
 #include "moe.h"
 #include "tcgen05.cuh"
 
@@ -54,6 +55,8 @@ B200_HD size_t sf_byte(int atom, int kgroups, int row_in_atom, int kb) {
 // list written in parallel, then the scatter of route ids into expert order.
 __global__ void __launch_bounds__(1024) moe_route_kernel(const int* __restrict__ topk_ids, int TK, int E, int off,
                                                          int nt, int max_tiles, MoeWorkspace ws) {
+  pdl_wait();  // predecessor output visible (programmatic dependent launch)
+  pdl_trigger();
   extern __shared__ int sm[];
   int* cnt = sm;           // [E]
   int* cur = sm + E;       // [E]   scatter cursors
@@ -134,6 +137,8 @@ __global__ void __launch_bounds__(128) moe_quant_kernel(uint8_t* __restrict__ q,
                                                         const int* __restrict__ atom_base, int E, int K, int Kp,
                                                         int R_max, int src_rows, int atoms_max, int nt,
                                                         int* status) {
+  pdl_wait();  // predecessor output visible (programmatic dependent launch)
+  pdl_trigger();
   const int groups = (Kp / 32 + 31) / 32;  // 32-block groups per row
   const int gw = blockIdx.x * 4 + (threadIdx.x >> 5);
   const int r = gw / groups, grp = gw % groups;
@@ -219,6 +224,8 @@ __global__ void __launch_bounds__(128) moe_gather_kernel(__nv_bfloat16* __restri
                                                          const int* __restrict__ row_route, int k_gather,
                                                          const int* __restrict__ offsets, int E, int K, int R_max,
                                                          int src_rows, int* status) {
+  pdl_wait();  // predecessor output visible (programmatic dependent launch)
+  pdl_trigger();
   const int r = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (r >= R_max || r >= offsets[E]) return;
   const int srow = row_route[r] / k_gather;
@@ -283,6 +290,8 @@ __global__ void __launch_bounds__(256, (NT <= 32 ? 2 : 1)) moe_gemm_kernel(const
                                                           __nv_bfloat16* __restrict__ out, int M, int Kp, int ld_out,
                                                           float alpha, float limit, int E_local, int R_max,
                                                           int atoms_max, int* status) {
+  pdl_wait();  // predecessor output visible (programmatic dependent launch)
+  pdl_trigger();
   using L = GemmSmem<NT, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   const int mtiles = cdiv(M, 128);
@@ -461,6 +470,8 @@ __global__ void __launch_bounds__(256, (NT <= 32 ? 2 : 1)) moe_gemm_kernel(const
 // ------------------------------------------------------------------------- reduce
 __global__ void moe_reduce_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ y,
                                   const int* __restrict__ topk_ids, int k, int E, int off, int H) {
+  pdl_wait();  // predecessor output visible (programmatic dependent launch)
+  pdl_trigger();
   const int t = blockIdx.x;
   int local[16];
   int nl = 0;
@@ -572,7 +583,7 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const uint8
   // work items
   const int work = max_tiles * cdiv(M, 128);
   const int grid = min(num_sms() * (NT <= 32 ? 2 : 1), work);
-  kern<<<grid, 256, L::kAlloc, s>>>(ta, tb, sfa, sfb, ws, bias, topk_w, (__nv_bfloat16*)out, M, Kp, ld_out, alpha,
+  launch_k(kern, dim3(grid), dim3(256), L::kAlloc, s, ta, tb, sfa, sfb, ws, bias, topk_w, (__nv_bfloat16*)out, M, Kp, ld_out, alpha,
                                     limit, E_local, R_max, atoms_max, status);
   return (int)cudaGetLastError();
 }
@@ -592,7 +603,7 @@ static int run_gemms(const MoeShape& sh, const void* w13, const uint8_t* sf13, c
                                                   sh.K1p, sh.I, alpha, limit, max_tiles, sh.E_local, R_max, atoms_max,
                                                   status, s);
   if (rc) return rc;
-  moe_quant_kernel<<<cdiv(R_max * cdiv(sh.K2p / 32, 32), 4), 128, 0, s>>>(ws.aq, ws.sf2, (const __nv_bfloat16*)ws.act, sh.I, ws.row_route,
+  launch_k(moe_quant_kernel, dim3(cdiv(R_max * cdiv(sh.K2p / 32, 32), 4)), dim3(128), 0, s, ws.aq, ws.sf2, (const __nv_bfloat16*)ws.act, sh.I, ws.row_route,
                                                   0, ws.offsets, ws.atom_base, sh.E_local, sh.I, sh.K2p, R_max, R_max,
                                                   atoms_max, NT, status);
   rc = launch_gemm<NT, STAGES, FMT, kEpiDown>(ta2, tb2, sf2w, ws.sf2, ws, b2, topk_w, ws.y, sh.H, sh.K2p, sh.H,
@@ -657,10 +668,10 @@ extern "C" int b200_moe_mx_forward(void* out, const void* x, const int* topk_ids
   if (sh.nt != 16 && sh.nt != 32 && sh.nt != 128) return kBadShape;
   const int R_max = sh.T * sh.k;
   const int max_tiles = cdiv(R_max, sh.nt) + sh.E_local;
-  moe_route_kernel<<<1, 1024, 2 * sh.E_local * sizeof(int), s>>>(topk_ids, R_max, sh.E_local,
+  launch_k(moe_route_kernel, dim3(1), dim3(1024), 2 * sh.E_local * sizeof(int), s, topk_ids, R_max, sh.E_local,
                                                                           sh.expert_offset, sh.nt, max_tiles, ws);
   const int atoms_max = max_tiles;
-  moe_quant_kernel<<<cdiv(R_max * cdiv(sh.K1p / 32, 32), 4), 128, 0, s>>>(ws.xq, ws.sf1, (const __nv_bfloat16*)x, sh.H, ws.row_route,
+  launch_k(moe_quant_kernel, dim3(cdiv(R_max * cdiv(sh.K1p / 32, 32), 4)), dim3(128), 0, s, ws.xq, ws.sf1, (const __nv_bfloat16*)x, sh.H, ws.row_route,
                                                   sh.k, ws.offsets, ws.atom_base, sh.E_local, sh.H, sh.K1p, R_max,
                                                   sh.T, atoms_max, sh.nt, status);
   int rc;
@@ -681,7 +692,7 @@ extern "C" int b200_moe_mx_forward(void* out, const void* x, const int* topk_ids
                                              max_tiles, atoms_max, status, s);
   }
   if (rc) return rc;
-  moe_reduce_kernel<<<sh.T, 128, 0, s>>>((__nv_bfloat16*)out, (const __nv_bfloat16*)ws.y, topk_ids, sh.k,
+  launch_k(moe_reduce_kernel, dim3(sh.T), dim3(128), 0, s, (__nv_bfloat16*)out, (const __nv_bfloat16*)ws.y, topk_ids, sh.k,
                                          sh.E_local, sh.expert_offset, sh.H);
   return (int)cudaGetLastError();
 }
@@ -697,9 +708,9 @@ extern "C" int b200_moe_bf16_forward(void* out, const void* x, const int* topk_i
   if (sh.nt != 16 && sh.nt != 32 && sh.nt != 128) return kBadShape;
   const int R_max = sh.T * sh.k;
   const int max_tiles = cdiv(R_max, sh.nt) + sh.E_local;
-  moe_route_kernel<<<1, 1024, 2 * sh.E_local * sizeof(int), s>>>(topk_ids, R_max, sh.E_local, sh.expert_offset,
+  launch_k(moe_route_kernel, dim3(1), dim3(1024), 2 * sh.E_local * sizeof(int), s, topk_ids, R_max, sh.E_local, sh.expert_offset,
                                                                   sh.nt, max_tiles, ws);
-  moe_gather_kernel<<<cdiv(R_max, 4), 128, 0, s>>>((__nv_bfloat16*)ws.xq, sh.K1p, (const __nv_bfloat16*)x, sh.H,
+  launch_k(moe_gather_kernel, dim3(cdiv(R_max, 4)), dim3(128), 0, s, (__nv_bfloat16*)ws.xq, sh.K1p, (const __nv_bfloat16*)x, sh.H,
                                                    ws.row_route, sh.k, ws.offsets, sh.E_local, sh.H, R_max, sh.T,
                                                    status);
   int rc;
@@ -713,7 +724,7 @@ extern "C" int b200_moe_bf16_forward(void* out, const void* x, const int* topk_i
     rc = run_gemms_bf16<128, 6>(sh, w13, b13, w2, b2, topk_w, ws, alpha, limit, R_max, max_tiles, max_tiles, status,
                                 s);
   if (rc) return rc;
-  moe_reduce_kernel<<<sh.T, 128, 0, s>>>((__nv_bfloat16*)out, (const __nv_bfloat16*)ws.y, topk_ids, sh.k,
+  launch_k(moe_reduce_kernel, dim3(sh.T), dim3(128), 0, s, (__nv_bfloat16*)out, (const __nv_bfloat16*)ws.y, topk_ids, sh.k,
                                          sh.E_local, sh.expert_offset, sh.H);
   return (int)cudaGetLastError();
 }

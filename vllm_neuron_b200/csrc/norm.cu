@@ -5,6 +5,7 @@
 // r  += x ; out = rms_norm(r)                     (fused_add_rms_norm, r updated in place)
 // Semantics: GptOssRMSNorm (vllm_neuron/model/gpt_oss/model_mxfp4.py:101).
 #include "common.cuh"
+#include "launch_pdl.h"
 #include "launch.h"
 
 namespace b200 {
@@ -13,6 +14,8 @@ template <typename T, bool kAdd>
 __global__ void __launch_bounds__(256) rms_norm_kernel(T* __restrict__ out, const T* __restrict__ x,
                                                        T* __restrict__ residual, const float* __restrict__ w,
                                                        int H, float eps) {
+  pdl_wait();  // predecessor output visible (programmatic dependent launch)
+  pdl_trigger();
   extern __shared__ float srow[];  // H floats (the pre-norm row)
   __shared__ float red[32];
   const int row = blockIdx.x;
@@ -45,6 +48,8 @@ __global__ void __launch_bounds__(256) rms_norm_vec_kernel(__nv_bfloat16* __rest
                                                            const __nv_bfloat16* __restrict__ x,
                                                            __nv_bfloat16* __restrict__ residual,
                                                            const float* __restrict__ w, int H, float eps) {
+  pdl_wait();  // predecessor output visible (programmatic dependent launch)
+  pdl_trigger();
   __shared__ float red[32];
   const int row = blockIdx.x;
   const int nchunk = H / 8;
@@ -103,9 +108,9 @@ static void launch_norm(void* out, const void* x, void* res, const float* w, int
   int threads = H >= 2048 ? 256 : (H >= 512 ? 128 : 64);
   size_t smem = (size_t)H * sizeof(float);
   if (res)
-    rms_norm_kernel<T, true><<<rows, threads, smem, s>>>((T*)out, (const T*)x, (T*)res, w, H, eps);
+    launch_k(rms_norm_kernel<T, true>, dim3(rows), dim3(threads), smem, s, (T*)out, (const T*)x, (T*)res, w, H, eps);
   else
-    rms_norm_kernel<T, false><<<rows, threads, smem, s>>>((T*)out, (const T*)x, nullptr, w, H, eps);
+    launch_k(rms_norm_kernel<T, false>, dim3(rows), dim3(threads), smem, s, (T*)out, (const T*)x, nullptr, w, H, eps);
 }
 
 }  // namespace b200
@@ -122,10 +127,10 @@ extern "C" int b200_rms_norm(void* out, const void* x, void* residual, const flo
     while (threads * kMaxVec < nchunk) threads *= 2;
     if (threads <= 256) {
       if (residual)
-        rms_norm_vec_kernel<true><<<rows, threads, 0, s>>>((__nv_bfloat16*)out, (const __nv_bfloat16*)x,
+        launch_k(rms_norm_vec_kernel<true>, dim3(rows), dim3(threads), 0, s, (__nv_bfloat16*)out, (const __nv_bfloat16*)x,
                                                            (__nv_bfloat16*)residual, w, H, eps);
       else
-        rms_norm_vec_kernel<false><<<rows, threads, 0, s>>>((__nv_bfloat16*)out, (const __nv_bfloat16*)x, nullptr,
+        launch_k(rms_norm_vec_kernel<false>, dim3(rows), dim3(threads), 0, s, (__nv_bfloat16*)out, (const __nv_bfloat16*)x, nullptr,
                                                             w, H, eps);
       return (int)cudaGetLastError();
     }

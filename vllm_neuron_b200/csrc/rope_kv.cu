@@ -9,6 +9,7 @@
 // Semantics: functional/attention/qkv.py:296 (in-kernel cache write) and
 // GptOssRotaryEmbedding (model/gpt_oss/model_mxfp4.py:141-197).
 #include "common.cuh"
+#include "launch_pdl.h"
 #include "launch.h"
 
 namespace b200 {
@@ -21,6 +22,8 @@ __global__ void __launch_bounds__(256) rope_kv_kernel(T* __restrict__ qkv, const
                                                       int num_blocks, float inv_ks, float inv_vs,
                                                       const float* __restrict__ qn, const float* __restrict__ kn,
                                                       float eps, int* status) {
+  pdl_wait();  // predecessor output visible (programmatic dependent launch)
+  pdl_trigger();
   const int t = blockIdx.x;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int64_t p = pos[t];
@@ -85,6 +88,8 @@ __global__ void __launch_bounds__(256) rope_kv_vec_kernel(__nv_bfloat16* __restr
                                                           CT* __restrict__ vc, const int64_t* __restrict__ slots,
                                                           int nq, int nkv, int d, int stride, int bs, int num_blocks,
                                                           float inv_ks, float inv_vs, int* status) {
+  pdl_wait();  // predecessor output visible (programmatic dependent launch)
+  pdl_trigger();
   const int t = blockIdx.x;
   const int half = d / 2, g4 = half / 4;  // groups of 4 pairs per head
   const int64_t p = pos[t];
@@ -156,11 +161,11 @@ static int launch_rope(void* qkv, const int64_t* pos, const float* cs, void* kc,
   if (T_ == 0) return 0;
   const int threads = 128;
   if (cache_dtype == kFP8E4M3) {
-    rope_kv_kernel<T, __nv_fp8_e4m3><<<T_, threads, 0, s>>>((T*)qkv, pos, cs, (__nv_fp8_e4m3*)kc,
+    launch_k(rope_kv_kernel<T, __nv_fp8_e4m3>, dim3(T_), dim3(threads), 0, s, (T*)qkv, pos, cs, (__nv_fp8_e4m3*)kc,
                                                             (__nv_fp8_e4m3*)vc, slots, nq, nkv, d, rd, stride, bs, nb,
                                                             1.f / ks, 1.f / vs, qn, kn, eps, status);
   } else {
-    rope_kv_kernel<T, T><<<T_, threads, 0, s>>>((T*)qkv, pos, cs, (T*)kc, (T*)vc, slots, nq, nkv, d, rd, stride,
+    launch_k(rope_kv_kernel<T, T>, dim3(T_), dim3(threads), 0, s, (T*)qkv, pos, cs, (T*)kc, (T*)vc, slots, nq, nkv, d, rd, stride,
                                                 bs, nb, 1.f, 1.f, qn, kn, eps, status);
   }
   return (int)cudaGetLastError();
@@ -202,11 +207,11 @@ extern "C" int b200_rope_kv_write(void* qkv, const int64_t* positions, const flo
     const int work = (nq + nkv) * (d / 8) + nkv * (d / 4);
     const int threads = work >= 256 ? 256 : ((work + 31) / 32) * 32;
     if (cache_dtype == kFP8E4M3)
-      rope_kv_vec_kernel<__nv_fp8_e4m3><<<T, threads, 0, s>>>(
+      launch_k(rope_kv_vec_kernel<__nv_fp8_e4m3>, dim3(T), dim3(threads), 0, s, 
           (__nv_bfloat16*)qkv, positions, cos_sin, (__nv_fp8_e4m3*)k_cache, (__nv_fp8_e4m3*)v_cache, slot_mapping, nq,
           nkv, d, qkv_stride, block_size, num_blocks, 1.f / k_scale, 1.f / v_scale, status);
     else
-      rope_kv_vec_kernel<__nv_bfloat16><<<T, threads, 0, s>>>(
+      launch_k(rope_kv_vec_kernel<__nv_bfloat16>, dim3(T), dim3(threads), 0, s, 
           (__nv_bfloat16*)qkv, positions, cos_sin, (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, slot_mapping,
           nq, nkv, d, qkv_stride, block_size, num_blocks, 1.f, 1.f, status);
     return (int)cudaGetLastError();

@@ -9,12 +9,15 @@
 //   over order-preserving float bits, then a bitonic sort in shared memory.
 #include "launch.h"
 #include "common.cuh"
+#include "launch_pdl.h"
 
 namespace b200 {
 
 template <typename LT>
 __global__ void topk_softmax_kernel(int* __restrict__ ids, float* __restrict__ w, const LT* __restrict__ logits,
                                     int T, int E, int k) {
+  pdl_wait();  // predecessor output visible (programmatic dependent launch)
+  pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= T) return;
@@ -298,11 +301,11 @@ extern "C" int b200_topk_softmax(int* ids, float* weights, const void* logits, i
   if (T == 0) return 0;
   const int warps_per_block = 4;
   if (dtype == kBF16)
-    topk_softmax_kernel<<<cdiv(T, warps_per_block), 32 * warps_per_block, 0, s>>>(
-        ids, weights, (const __nv_bfloat16*)logits, T, E, k);
+    launch_k(topk_softmax_kernel<__nv_bfloat16>, dim3(cdiv(T, warps_per_block)), dim3(32 * warps_per_block), 0, s,
+             ids, weights, (const __nv_bfloat16*)logits, T, E, k);
   else if (dtype == kF32)
-    topk_softmax_kernel<<<cdiv(T, warps_per_block), 32 * warps_per_block, 0, s>>>(ids, weights,
-                                                                                 (const float*)logits, T, E, k);
+    launch_k(topk_softmax_kernel<float>, dim3(cdiv(T, warps_per_block)), dim3(32 * warps_per_block), 0, s, ids,
+             weights, (const float*)logits, T, E, k);
   else
     return kBadShape;
   return (int)cudaGetLastError();
