@@ -112,7 +112,8 @@ def _attn_decode(args):
     from vllm_neuron_b200 import ops
     from vllm_neuron_b200.ops.metadata import AttentionMetadata
 
-    B, L, hq, hkv, d = args.T or 64, args.L or 2048, 64, 8, 64
+    B, L, d = args.T or 64, args.L or 2048, 64
+    hq, hkv = args.hq or 64, args.hkv or 8
     kc, vc, bt, sl = _paged(B, L, hq, hkv, d)
     q = torch.randn(B, hq, d, device="cuda").bfloat16()
     sms = torch.cuda.get_device_properties(0).multi_processor_count
@@ -190,6 +191,8 @@ def main() -> None:
     ap.add_argument("--E", type=int, default=0, help="experts")
     ap.add_argument("--L", type=int, default=0, help="context / prompt length")
     ap.add_argument("--splits", type=int, default=0, help="split-KV factor for attn_decode (0 = heuristic)")
+    ap.add_argument("--hq", type=int, default=0, help="query heads (attn_decode; default 64)")
+    ap.add_argument("--hkv", type=int, default=0, help="kv heads (attn_decode; default 8)")
     args = ap.parse_args()
     peaks = _peaks()
     flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")  # 256 MB > L2
