@@ -4,7 +4,7 @@
 
 Each op is timed with CUDA events on the launching stream after warm-up, with a write of
 a buffer larger than L2 between timed iterations (so every iteration reads its operands
-from HBM), and reported as one JSON line: median milliseconds, the algorithmic bytes and
+from HBM), and reported as one JSON line: mean milliseconds, the algorithmic bytes and
 FLOPs of one call, achieved GB/s and TFLOP/s, and the fraction of the measured copy
 bandwidth / bf16 GEMM peak (``MEASURED_PEAKS.json`` at the repository root, if present).
 The same command with ``--iters 1 --warmup 1`` is the small case for a profiler capture.
@@ -51,7 +51,9 @@ def _time(fn, iters: int, warmup: int, flush: torch.Tensor) -> float:
         e.record()
         torch.cuda.synchronize()
         times.append(s.elapsed_time(e))
-    return statistics.median(times)
+    # event timestamps on this part tick in ~2 us steps, so a median of short kernels snaps
+    # to the grid; the mean over many iterations (random phase) is not quantised
+    return statistics.fmean(times)
 
 
 def _moe_mxfp4(args):
@@ -117,7 +119,9 @@ def _attn_decode(args):
     kc, vc, bt, sl = _paged(B, L, hq, hkv, d)
     q = torch.randn(B, hq, d, device="cuda").bfloat16()
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    splits = args.splits or min(32, max(1, -(-4 * sms // (B * hkv))))
+    from vllm_neuron_b200.engine.model_runner import decode_splits
+
+    splits = args.splits or decode_splits(B, hkv, sms)
     ws = torch.empty(B * hq * splits * (d + 2), device="cuda")
     qsl = torch.arange(B + 1, dtype=torch.int32, device="cuda")
     meta = AttentionMetadata(B, B, True, qsl, sl, bt, None, None, 1, L, workspace=ws, num_splits=splits)

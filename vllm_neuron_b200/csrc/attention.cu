@@ -103,7 +103,7 @@ B200_D void convert_fp8_tile(__nv_bfloat16* Ks, __nv_bfloat16* Vs, const uint8_t
 // ---------------------------------------------------------------------------------------
 // Decode
 // ---------------------------------------------------------------------------------------
-template <int D, typename T, typename CT>
+template <int D, int S, typename T, typename CT>
 __global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const T* __restrict__ q,
                                                      const CT* __restrict__ kc, const CT* __restrict__ vc,
                                                      const int* __restrict__ block_tables,
@@ -115,9 +115,9 @@ __global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const 
   pdl_trigger();
   constexpr int C = D / 8;
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(smem_raw);            // [2][64*D]
-  __nv_bfloat16* Vs = Ks + 2 * kKT * D;                                      // [2][64*D]
-  uint8_t* stage = reinterpret_cast<uint8_t*>(Vs + 2 * kKT * D);             // fp8 staging [2][64*D]
+  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(smem_raw);            // [S][64*D]
+  __nv_bfloat16* Vs = Ks + S * kKT * D;                                      // [S][64*D]
+  uint8_t* stage = reinterpret_cast<uint8_t*>(Vs + S * kKT * D);             // fp8 staging [S][2][64*D]
 
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int G = nq / nkv;
@@ -166,22 +166,28 @@ __global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const 
   for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
 
+  // S-stage cp.async ring: tiles t+1 .. t+S-1 are in flight while tile t is consumed, so a
+  // CTA with few tiles (a split of a short range) pays one memory latency, not one per tile.
+  // One commit group per tile slot (empty past the end) keeps the group arithmetic uniform.
   const int ntiles = key_end > key_begin ? cdiv(key_end - key_begin, kKT) : 0;
-  if (ntiles > 0) {
-    load_kv_tile<D, CT>(Ks, Vs, stage, kc, vc, bt_row, key_begin, key_end, bs, nkv, h);
+#pragma unroll
+  for (int p = 0; p < S - 1; ++p) {
+    if (p < ntiles)
+      load_kv_tile<D, CT>(Ks + p * kKT * D, Vs + p * kKT * D, stage + p * 2 * kKT * D, kc, vc, bt_row,
+                          key_begin + p * kKT, key_end, bs, nkv, h);
     cp_async_commit();
   }
   for (int t = 0; t < ntiles; ++t) {
-    const int buf = t & 1;
-    if (t + 1 < ntiles) {
-      load_kv_tile<D, CT>(Ks + (buf ^ 1) * kKT * D, Vs + (buf ^ 1) * kKT * D, stage + (buf ^ 1) * 2 * kKT * D, kc,
-                          vc, bt_row, key_begin + (t + 1) * kKT, key_end, bs, nkv, h);
+    const int buf = t % S;
+    cp_async_wait<S - 2>();  // groups 0..t complete: tile t landed
+    __syncthreads();         // ...for every thread; and every warp is done with tile t-1
+    {
+      const int nt = t + S - 1, nb = nt % S;  // refill the slot tile t-1 used
+      if (nt < ntiles)
+        load_kv_tile<D, CT>(Ks + nb * kKT * D, Vs + nb * kKT * D, stage + nb * 2 * kKT * D, kc, vc, bt_row,
+                            key_begin + nt * kKT, key_end, bs, nkv, h);
       cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
     }
-    __syncthreads();
     __nv_bfloat16* K = Ks + buf * kKT * D;
     __nv_bfloat16* V = Vs + buf * kKT * D;
     if constexpr (sizeof(CT) == 1) {
@@ -264,8 +270,8 @@ __global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const 
       mma_bf16_16816(o[n], pa, bA);
       mma_bf16_16816(o[n + 1], pa, bB);
     }
-    __syncthreads();  // before the next prefetch overwrites this buffer
   }
+  cp_async_wait<0>();  // only empty groups can remain; keeps the reuse below obviously safe
 
   // ---- merge the 4 warps (shared memory reuses the K/V area) ----
   float* sm_m = reinterpret_cast<float*>(smem_raw);     // [4][16]
@@ -351,10 +357,15 @@ static int launch_decode(void* out, const void* q, const void* kc, const void* v
                          float scale, float k_scale, float v_scale, float* ws, int num_splits, cudaStream_t s) {
   if (B == 0) return 0;
   if (num_splits > 1 && ws == nullptr) return kBadShape;
-  const size_t smem_tiles = 2 * 2 * kKT * D * sizeof(__nv_bfloat16) + (sizeof(CT) == 1 ? 2 * 2 * kKT * D : 0);
+  // pipeline depth: 3 tile slots for d <= 64 (48 KB of bf16 K/V: four CTAs per SM, so 64
+  // sequences x 8 (kv head, split) CTAs run in one wave), 2 above (the fp8 staging ring
+  // rides on top).  A 4-slot ring measured slower on B200: three CTAs per SM put 512
+  // CTAs into two waves.
+  constexpr int S = D <= 64 ? 3 : 2;
+  const size_t smem_tiles = S * 2 * kKT * D * sizeof(__nv_bfloat16) + (sizeof(CT) == 1 ? S * 2 * kKT * D : 0);
   const size_t smem_merge = (4 * 16 * 2 + 4 * 16 * D) * sizeof(float);
   const size_t smem = smem_tiles > smem_merge ? smem_tiles : smem_merge;
-  auto kern = decode_kernel<D, T, CT>;
+  auto kern = decode_kernel<D, S, T, CT>;
   static bool attr_set = false;  // host-side, once per instantiation
   if (!attr_set) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
