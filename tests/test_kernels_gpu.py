@@ -107,9 +107,10 @@ def _paged_setup(seq_lens, q_lens, nq, nkv, d, bs, dtype=torch.bfloat16, seed=0)
 @pytest.mark.parametrize("window", [0, 128])
 @pytest.mark.parametrize("splits", [1, 5])
 @pytest.mark.parametrize("fp8", [False, True])
-def test_paged_decode(d, window, splits, fp8):
+@pytest.mark.parametrize("heads", [(16, 2), (12, 1), (4, 4)])  # GQA groups 8, 12 (rows 8..15 live), 1
+def test_paged_decode(d, window, splits, fp8, heads):
     seq_lens = [1, 17, 100, 130, 1000, 3001]
-    nq, nkv, bs = 16, 2, 32
+    (nq, nkv), bs = heads, 32
     q, kc, vc, bt, sl, qsl = _paged_setup(seq_lens, [1] * len(seq_lens), nq, nkv, d, bs)
     sinks = torch.randn(nq, device=DEV)
     ks, vs = (0.05, 0.07) if fp8 else (1.0, 1.0)

@@ -43,8 +43,11 @@ struct TileGeom {
 
 template <int D, typename CT>
 B200_D void load_kv_tile(__nv_bfloat16* Ks, __nv_bfloat16* Vs, uint8_t* stage, const CT* kc, const CT* vc,
-                         const int* bt_row, int tile_key0, int key_end, int bs, int nkv, int h) {
+                         const int* bt_row, int tile_key0, int key_end, int bs_log, int nkv, int h) {
+  // block size is a power of two (the engine enforces it): shifts, not integer division,
+  // which would run on the transcendental (XU) pipe that the softmax already saturates
   constexpr int C = TileGeom<D>::kChunks;
+  const int bs_mask = (1 << bs_log) - 1;
   if constexpr (sizeof(CT) == 2) {
     for (int i = threadIdx.x; i < kKT * C; i += blockDim.x) {
       const int k = i / C, c = i % C;
@@ -52,8 +55,8 @@ B200_D void load_kv_tile(__nv_bfloat16* Ks, __nv_bfloat16* Vs, uint8_t* stage, c
       const bool ok = gk < key_end;
       size_t off = 0;
       if (ok) {
-        const int blk = bt_row[gk / bs];
-        off = (((size_t)blk * nkv + h) * bs + (gk % bs)) * D + c * 8;
+        const int blk = bt_row[gk >> bs_log];
+        off = ((((size_t)blk * nkv + h) << bs_log) + (gk & bs_mask)) * D + c * 8;
       }
       cp_async16(Ks + swz(k, c, C) * 8, kc + off, ok ? 16 : 0);
       cp_async16(Vs + swz(k, c, C) * 8, vc + off, ok ? 16 : 0);
@@ -67,8 +70,8 @@ B200_D void load_kv_tile(__nv_bfloat16* Ks, __nv_bfloat16* Vs, uint8_t* stage, c
       const bool ok = gk < key_end;
       size_t off = 0;
       if (ok) {
-        const int blk = bt_row[gk / bs];
-        off = (((size_t)blk * nkv + h) * bs + (gk % bs)) * D + c * 16;
+        const int blk = bt_row[gk >> bs_log];
+        off = ((((size_t)blk * nkv + h) << bs_log) + (gk & bs_mask)) * D + c * 16;
       }
       cp_async16(stage + (k * D + c * 16), reinterpret_cast<const uint8_t*>(kc) + off, ok ? 16 : 0);
       cp_async16(stage + kKT * D + (k * D + c * 16), reinterpret_cast<const uint8_t*>(vc) + off, ok ? 16 : 0);
@@ -137,6 +140,8 @@ __global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const 
     }
   }
   const int* bt_row = block_tables + (size_t)b * max_blocks;
+  const int bs_log = 31 - __clz(bs);
+  const bool hi_rows = G > 8;  // rows r0 + 8 of the 16-row MMA hold real heads
 
   // Q fragments (A operand, rows = heads of the group)
   uint32_t qf[D / 16][4];
@@ -174,7 +179,7 @@ __global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const 
   for (int p = 0; p < S - 1; ++p) {
     if (p < ntiles)
       load_kv_tile<D, CT>(Ks + p * kKT * D, Vs + p * kKT * D, stage + p * 2 * kKT * D, kc, vc, bt_row,
-                          key_begin + p * kKT, key_end, bs, nkv, h);
+                          key_begin + p * kKT, key_end, bs_log, nkv, h);
     cp_async_commit();
   }
   for (int t = 0; t < ntiles; ++t) {
@@ -185,7 +190,7 @@ __global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const 
       const int nt = t + S - 1, nb = nt % S;  // refill the slot tile t-1 used
       if (nt < ntiles)
         load_kv_tile<D, CT>(Ks + nb * kKT * D, Vs + nb * kKT * D, stage + nb * 2 * kKT * D, kc, vc, bt_row,
-                            key_begin + nt * kKT, key_end, bs, nkv, h);
+                            key_begin + nt * kKT, key_end, bs_log, nkv, h);
       cp_async_commit();
     }
     __nv_bfloat16* K = Ks + buf * kKT * D;
@@ -210,44 +215,46 @@ __global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const 
       mma_bf16_16816(s[0], qf[kk], bA);
       mma_bf16_16816(s[1], qf[kk], bB);
     }
-    // mask + online softmax (rows r0 and r0+8)
-    float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int key = key0 + j * 8 + 2 * qd + (e & 1);
-        float v = s[j][e] * scale_log2;
-        if (key >= key_end) v = -INFINITY;
-        s[j][e] = v;
-        mx[e >> 1] = fmaxf(mx[e >> 1], v);
-      }
-    }
-    float corr[2];
+    // mask + online softmax, row r0 (r = 0) and row r0 + 8 (r = 1); with a group of at most
+    // 8 heads the second half is zero padding and skips its exponentials (the XU pipe is the
+    // decode kernel's limiter, ahead of HBM)
+    float corr[2] = {1.f, 1.f};
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
-      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-      const float mnew = fmaxf(m_run[r], mx[r]);
+      if (r == 1 && !hi_rows) {
+        s[0][2] = s[0][3] = s[1][2] = s[1][3] = 0.f;
+        continue;
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+#pragma unroll
+        for (int e2 = 0; e2 < 2; ++e2) {
+          const int key = key0 + j * 8 + 2 * qd + e2;
+          float v = s[j][2 * r + e2] * scale_log2;
+          if (key >= key_end) v = -INFINITY;
+          s[j][2 * r + e2] = v;
+          mx = fmaxf(mx, v);
+        }
+      }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mnew = fmaxf(m_run[r], mx);
       corr[r] = (mnew == -INFINITY) ? 1.f : exp2f(m_run[r] - mnew);
       m_run[r] = mnew;
-    }
-    float rs[2] = {0.f, 0.f};
+      float rs = 0.f;
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
+      for (int j = 0; j < 2; ++j) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float mref = m_run[e >> 1];
-        const float p = (mref == -INFINITY) ? 0.f : exp2f(s[j][e] - mref);
-        s[j][e] = p;
-        rs[e >> 1] += p;
+        for (int e2 = 0; e2 < 2; ++e2) {
+          const float p = (mnew == -INFINITY) ? 0.f : exp2f(s[j][2 * r + e2] - mnew);
+          s[j][2 * r + e2] = p;
+          rs += p;
+        }
       }
-    }
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
-      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
-      l_run[r] = l_run[r] * corr[r] + rs[r];
+      rs += __shfl_xor_sync(0xffffffffu, rs, 1);
+      rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+      l_run[r] = l_run[r] * corr[r] + rs;
     }
 #pragma unroll
     for (int n = 0; n < D / 8; ++n) {
@@ -452,7 +459,8 @@ __global__ void __launch_bounds__(128) prefill_kernel(T* __restrict__ out, const
     if constexpr (kPaged) {
       const int* bt_row = pk.block_tables + (size_t)b * pk.max_blocks;
       if constexpr (D == DP) {
-        load_kv_tile<D, CT>(K, V, stage + buf * 2 * kKT * D, kc, vc, bt_row, key0, min(key_hi, L), pk.bs, nkv, h);
+        load_kv_tile<D, CT>(K, V, stage + buf * 2 * kKT * D, kc, vc, bt_row, key0, min(key_hi, L), 31 - __clz(pk.bs),
+                            nkv, h);
       }
     } else {
       // contiguous [T, nkv, D] K/V of this sequence; D may be padded to DP with zeros
@@ -635,6 +643,7 @@ extern "C" int b200_paged_attention_decode(void* out, const void* q, const void*
                                            int window, float scale, float k_scale, float v_scale, float* workspace,
                                            int num_splits, int dtype, int cache_dtype, cudaStream_t s) {
   if (nq % nkv || nq / nkv > 16 || dtype != kBF16) return kBadShape;
+  if (block_size <= 0 || (block_size & (block_size - 1))) return kBadShape;  // addressed by shifts
   const bool fp8 = cache_dtype == kFP8E4M3;
 #define DEC(DD)                                                                                                    \
   return fp8 ? launch_decode<DD, __nv_bfloat16, __nv_fp8_e4m3>(out, q, k_cache, v_cache, block_tables, seq_lens,   \
@@ -659,6 +668,7 @@ extern "C" int b200_paged_attention_prefill(void* out, const void* q, const void
                                             float v_scale, int max_query_len, int dtype, int cache_dtype,
                                             cudaStream_t s) {
   if (nq % nkv || dtype != kBF16) return kBadShape;
+  if (block_size <= 0 || (block_size & (block_size - 1))) return kBadShape;  // addressed by shifts
   PagedKV pk{block_tables, max_blocks, block_size, nkv};
   const bool fp8 = cache_dtype == kFP8E4M3;
 #define PRE(DD)                                                                                                     \
