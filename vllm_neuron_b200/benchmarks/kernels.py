@@ -2,9 +2,9 @@
 
 ``python -m vllm_neuron_b200.benchmarks.kernels --op moe_mxfp4 --iters 20``
 
-Each op is timed with CUDA events on the launching stream after warm-up, with a write of
+Each op is timed with CUDA events on the launching stream after warm-up, with a read of
 a buffer larger than L2 between timed iterations (so every iteration reads its operands
-from HBM), and reported as one JSON line: mean milliseconds, the algorithmic bytes and
+from HBM and no dirty lines are left to write back inside the timed region), and reported as one JSON line: mean milliseconds, the algorithmic bytes and
 FLOPs of one call, achieved GB/s and TFLOP/s, and the fraction of the measured copy
 bandwidth / bf16 GEMM peak (``MEASURED_PEAKS.json`` at the repository root, if present).
 The same command with ``--iters 1 --warmup 1`` is the small case for a profiler capture.
@@ -44,7 +44,10 @@ def _time(fn, iters: int, warmup: int, flush: torch.Tensor) -> float:
     torch.cuda.synchronize()
     times = []
     for _ in range(iters):
-        flush.add_(1)  # evicts L2 (buffer > 126 MB)
+        # evict L2 by READING a buffer larger than it (126 MB): a write flush leaves ~126 MB
+        # of dirty lines whose write-back then lands inside the timed kernel (~19 us at HBM
+        # speed, most of a small kernel's time); after a read every resident line is clean
+        flush.sum()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         fn()
