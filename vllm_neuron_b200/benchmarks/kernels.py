@@ -38,6 +38,27 @@ def _peaks() -> dict:
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "fallback": True}
 
 
+def _graphed(fn):
+    """Capture ``fn`` into a CUDA graph (as the engine's decode step runs), so the timed
+    region holds device work only: eager launches of a multi-kernel op spend ~20 us of
+    host time per call, more than a small kernel's device time.  Returns (replay, mode)."""
+    try:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        torch.cuda.synchronize()
+        return g.replay, "graph"
+    except Exception:  # an op with a host sync cannot be captured: time it eagerly
+        torch.cuda.synchronize()
+        return fn, "eager"
+
+
 def _time(fn, iters: int, warmup: int, flush: torch.Tensor) -> float:
     for _ in range(warmup):
         fn()
@@ -200,6 +221,7 @@ def main() -> None:
     ap.add_argument("--splits", type=int, default=0, help="split-KV factor for attn_decode (0 = heuristic)")
     ap.add_argument("--hq", type=int, default=0, help="query heads (attn_decode; default 64)")
     ap.add_argument("--hkv", type=int, default=0, help="kv heads (attn_decode; default 8)")
+    ap.add_argument("--eager", action="store_true", help="time eager launches instead of a CUDA-graph replay")
     args = ap.parse_args()
     peaks = _peaks()
     flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")  # 256 MB > L2
@@ -207,16 +229,18 @@ def main() -> None:
     with torch.inference_mode():
         for name in names:
             fn, nbytes, flops, shape = OPS[name](args)
-            ms = _time(fn, args.iters, args.warmup, flush)
+            run, mode = (fn, "eager") if args.eager else _graphed(fn)
+            ms = _time(run, args.iters, args.warmup, flush)
             gbs = nbytes / ms / 1e6
             tfl = flops / ms / 1e9
             print(json.dumps({"op": name, "ms": round(ms, 4), "bytes": int(nbytes), "flops": int(flops),
                               "GB/s": round(gbs, 1), "TFLOP/s": round(tfl, 2),
                               "frac_hbm": round(gbs / peaks["hbm_gbs"], 3),
                               "frac_bf16_peak": round(tfl / peaks["bf16_tflops"], 3),
-                              "peaks": "fallback" if peaks.get("fallback") else "measured", "shape": shape}),
+                              "peaks": "fallback" if peaks.get("fallback") else "measured", "timing": mode,
+                              "shape": shape}),
                   flush=True)
-            del fn
+            del fn, run
             torch.cuda.empty_cache()
 
 
