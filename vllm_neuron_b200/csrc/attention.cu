@@ -143,6 +143,18 @@ __global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const 
   const int bs_log = 31 - __clz(bs);
   const bool hi_rows = G > 8;  // rows r0 + 8 of the 16-row MMA hold real heads
 
+  // S-stage cp.async ring: tiles t+1 .. t+S-1 are in flight while tile t is consumed, so a
+  // CTA with few tiles (a split of a short range) pays one memory latency, not one per tile.
+  // One commit group per tile slot (empty past the end) keeps the group arithmetic uniform.
+  // Issued before the Q fragments are read, so the two memory round trips overlap.
+  const int ntiles = key_end > key_begin ? cdiv(key_end - key_begin, kKT) : 0;
+#pragma unroll
+  for (int p = 0; p < S - 1; ++p) {
+    if (p < ntiles)
+      load_kv_tile<D, CT>(Ks + p * kKT * D, Vs + p * kKT * D, stage + p * 2 * kKT * D, kc, vc, bt_row,
+                          key_begin + p * kKT, key_end, bs_log, nkv, h);
+    cp_async_commit();
+  }
   // Q fragments (A operand, rows = heads of the group)
   uint32_t qf[D / 16][4];
   {
@@ -171,17 +183,6 @@ __global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const 
   for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
 
-  // S-stage cp.async ring: tiles t+1 .. t+S-1 are in flight while tile t is consumed, so a
-  // CTA with few tiles (a split of a short range) pays one memory latency, not one per tile.
-  // One commit group per tile slot (empty past the end) keeps the group arithmetic uniform.
-  const int ntiles = key_end > key_begin ? cdiv(key_end - key_begin, kKT) : 0;
-#pragma unroll
-  for (int p = 0; p < S - 1; ++p) {
-    if (p < ntiles)
-      load_kv_tile<D, CT>(Ks + p * kKT * D, Vs + p * kKT * D, stage + p * 2 * kKT * D, kc, vc, bt_row,
-                          key_begin + p * kKT, key_end, bs_log, nkv, h);
-    cp_async_commit();
-  }
   for (int t = 0; t < ntiles; ++t) {
     const int buf = t % S;
     cp_async_wait<S - 2>();  // groups 0..t complete: tile t landed
@@ -339,22 +340,36 @@ __global__ void decode_combine_kernel(T* __restrict__ out, const float* __restri
                                       const float* __restrict__ sinks, int nq, int num_splits, float v_scale) {
   pdl_wait();  // predecessor output visible (programmatic dependent launch)
   pdl_trigger();
+  // LSE merge of the splits (num_splits <= 32): one warp reads every split's log-sum-exp
+  // at once and turns them into weights, then each thread sums its dims over the splits.
+  // Two dependent memory round trips per CTA instead of one per split and pass.
+  __shared__ float wt[32];
+  __shared__ float scale_s;
   const int head = blockIdx.x, b = blockIdx.y;
   const float* w = ws + ((size_t)b * nq + head) * num_splits * (D + 1);
-  float M = sinks ? sinks[head] * kLog2e : -INFINITY;
-  for (int s = 0; s < num_splits; ++s) M = fmaxf(M, w[s * (D + 1) + D]);
-  float den = sinks ? exp2f(sinks[head] * kLog2e - M) : 0.f;
-  for (int s = 0; s < num_splits; ++s) {
-    const float ls = w[s * (D + 1) + D];
-    if (ls != -INFINITY) den += exp2f(ls - M);
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    const float ls = lane < num_splits ? w[lane * (D + 1) + D] : -INFINITY;
+    float M = ls;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float sk = sinks ? sinks[head] * kLog2e : -INFINITY;
+    M = fmaxf(M, sk);
+    const float e = (ls == -INFINITY) ? 0.f : exp2f(ls - M);
+    float den = e;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+    if (sinks) den += exp2f(sk - M);
+    wt[lane] = e;
+    if (lane == 0) scale_s = den > 0.f ? v_scale / den : 0.f;
   }
+  __syncthreads();
+  const float sc = scale_s;
   for (int dim = threadIdx.x; dim < D; dim += blockDim.x) {
     float acc = 0.f;
-    for (int s = 0; s < num_splits; ++s) {
-      const float ls = w[s * (D + 1) + D];
-      if (ls != -INFINITY) acc += w[s * (D + 1) + dim] * exp2f(ls - M);
-    }
-    out[(size_t)b * nq * D + (size_t)head * D + dim] = from_float<T>(den > 0.f ? acc / den * v_scale : 0.f);
+#pragma unroll 4
+    for (int s = 0; s < num_splits; ++s) acc += w[s * (D + 1) + dim] * wt[s];
+    out[(size_t)b * nq * D + (size_t)head * D + dim] = from_float<T>(acc * sc);
   }
 }
 
@@ -364,6 +379,7 @@ static int launch_decode(void* out, const void* q, const void* kc, const void* v
                          float scale, float k_scale, float v_scale, float* ws, int num_splits, cudaStream_t s) {
   if (B == 0) return 0;
   if (num_splits > 1 && ws == nullptr) return kBadShape;
+  if (num_splits < 1 || num_splits > 32) return kBadShape;  // the combine merges <= 32 splits in one warp
   // pipeline depth: 3 tile slots for d <= 64 (48 KB of bf16 K/V: four CTAs per SM, so 64
   // sequences x 8 (kv head, split) CTAs run in one wave), 2 above (the fp8 staging ring
   // rides on top).  A 4-slot ring measured slower on B200: three CTAs per SM put 512
