@@ -105,7 +105,7 @@ def _paged_setup(seq_lens, q_lens, nq, nkv, d, bs, dtype=torch.bfloat16, seed=0)
 
 @pytest.mark.parametrize("d", [64, 128, 256])
 @pytest.mark.parametrize("window", [0, 128])
-@pytest.mark.parametrize("splits", [1, 5])
+@pytest.mark.parametrize("splits", [1, 4, 5])  # 4: merged in a thread-block cluster; 5: workspace + combine
 @pytest.mark.parametrize("fp8", [False, True])
 @pytest.mark.parametrize("heads", [(16, 2), (12, 1), (4, 4)])  # GQA groups 8, 12 (rows 8..15 live), 1
 def test_paged_decode(d, window, splits, fp8, heads):

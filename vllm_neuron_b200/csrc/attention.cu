@@ -20,6 +20,8 @@
 //            HBM reads of the cache, so the warp-level MMA is the right unit here.
 //   prefill: one CTA per (64-query tile, query head, sequence), K/V read through the block
 //            table, so chunked prefill and prefix-cache hits need no gather.
+#include <cooperative_groups.h>
+
 #include "launch.h"
 #include "launch_pdl.h"
 #include "mma_utils.cuh"
@@ -113,7 +115,7 @@ __global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const 
                                                      const int* __restrict__ seq_lens, const float* __restrict__ sinks,
                                                      int nq, int nkv, int q_stride, int bs, int max_blocks, int window,
                                                      float scale_log2, float v_scale, float* __restrict__ ws,
-                                                     int num_splits) {
+                                                     int num_splits, int cluster_merge) {
   pdl_wait();  // predecessor output visible (programmatic dependent launch)
   pdl_trigger();
   constexpr int C = D / 8;
@@ -285,6 +287,8 @@ __global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const 
   float* sm_m = reinterpret_cast<float*>(smem_raw);     // [4][16]
   float* sm_l = sm_m + 4 * 16;                          // [4][16]
   float* sm_o = sm_l + 4 * 16;                          // [4][16][D]
+  float* part_o = sm_o + 4 * 16 * D;                    // [16][D]  this split's normalised output
+  float* part_lse = part_o + 16 * D;                    // [16]     and its log2-sum-exp
   __syncthreads();
   if (qd == 0) {
     sm_m[warp * 16 + r0] = m_run[0];
@@ -316,7 +320,10 @@ __global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const 
       }
     }
     const int head = h * G + g;
-    if (num_splits == 1) {
+    if (cluster_merge) {
+      part_o[i] = l > 0.f ? acc / l : 0.f;
+      if (dim == 0) part_lse[g] = (l > 0.f) ? (M + log2f(l)) : -INFINITY;
+    } else if (num_splits == 1) {
       float Mt = M, lt = l, at = acc;
       if (sinks != nullptr) {
         const float sk = sinks[head] * kLog2e;
@@ -332,6 +339,45 @@ __global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const 
       w[dim] = l > 0.f ? acc / l : 0.f;
       if (dim == 0) w[D] = (l > 0.f) ? (M + log2f(l)) : -INFINITY;
     }
+  }
+  if (cluster_merge) {
+    // Split merge inside the cluster (the splits of one (sequence, kv head) are the CTAs
+    // of one cluster): every CTA publishes its partial in its own shared memory, then CTA
+    // r merges outputs r, r + S, ... reading the peers' partials over distributed shared
+    // memory.  No workspace round trip through L2 and no second kernel.
+    namespace cg = cooperative_groups;
+    cg::cluster_group cl = cg::this_cluster();
+    cl.sync();  // every split's partial is visible cluster-wide
+    const float* peer_o[8];
+    const float* peer_lse[8];
+#pragma unroll
+    for (int sp = 0; sp < 8; ++sp) {
+      if (sp < num_splits) {
+        peer_o[sp] = cl.map_shared_rank(part_o, sp);
+        peer_lse[sp] = cl.map_shared_rank(part_lse, sp);
+      }
+    }
+    for (int i = split * blockDim.x + threadIdx.x; i < G * D; i += num_splits * blockDim.x) {
+      const int g = i / D, dim = i % D, head = h * G + g;
+      float lse[8];
+      float M = sinks ? sinks[head] * kLog2e : -INFINITY;
+#pragma unroll
+      for (int sp = 0; sp < 8; ++sp) {
+        lse[sp] = sp < num_splits ? peer_lse[sp][g] : -INFINITY;
+        M = fmaxf(M, lse[sp]);
+      }
+      float den = (sinks && M != -INFINITY) ? exp2f(sinks[head] * kLog2e - M) : 0.f, acc = 0.f;
+#pragma unroll
+      for (int sp = 0; sp < 8; ++sp) {
+        if (sp < num_splits && lse[sp] != -INFINITY) {
+          const float e = exp2f(lse[sp] - M);
+          den += e;
+          acc += e * peer_o[sp][i];
+        }
+      }
+      out[(size_t)b * nq * D + (size_t)head * D + dim] = from_float<T>(den > 0.f ? acc / den * v_scale : 0.f);
+    }
+    cl.sync();  // keep this CTA's shared memory alive until every peer has read it
   }
 }
 
@@ -373,20 +419,33 @@ __global__ void decode_combine_kernel(T* __restrict__ out, const float* __restri
   }
 }
 
+// VLLM_B200_DECODE_CLUSTER=0 sends every split count through the workspace + combine path.
+inline bool decode_cluster_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("VLLM_B200_DECODE_CLUSTER");
+    v = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 template <int D, typename T, typename CT>
 static int launch_decode(void* out, const void* q, const void* kc, const void* vc, const int* bt, const int* sl,
                          const float* sinks, int B, int nq, int nkv, int q_stride, int bs, int max_blocks, int window,
                          float scale, float k_scale, float v_scale, float* ws, int num_splits, cudaStream_t s) {
   if (B == 0) return 0;
-  if (num_splits > 1 && ws == nullptr) return kBadShape;
   if (num_splits < 1 || num_splits > 32) return kBadShape;  // the combine merges <= 32 splits in one warp
+  // 2, 4 or 8 splits merge inside a thread-block cluster; other counts go through the
+  // workspace and the combine kernel
+  const bool cluster = (num_splits == 2 || num_splits == 4 || num_splits == 8) && decode_cluster_enabled();
+  if (num_splits > 1 && !cluster && ws == nullptr) return kBadShape;
   // pipeline depth: 3 tile slots for d <= 64 (48 KB of bf16 K/V: four CTAs per SM, so 64
   // sequences x 8 (kv head, split) CTAs run in one wave), 2 above (the fp8 staging ring
   // rides on top).  A 4-slot ring measured slower on B200: three CTAs per SM put 512
   // CTAs into two waves.
   constexpr int S = D <= 64 ? 3 : 2;
   const size_t smem_tiles = S * 2 * kKT * D * sizeof(__nv_bfloat16) + (sizeof(CT) == 1 ? S * 2 * kKT * D : 0);
-  const size_t smem_merge = (4 * 16 * 2 + 4 * 16 * D) * sizeof(float);
+  const size_t smem_merge = (4 * 16 * 2 + 4 * 16 * D + 16 * D + 16) * sizeof(float);
   const size_t smem = smem_tiles > smem_merge ? smem_tiles : smem_merge;
   auto kern = decode_kernel<D, S, T, CT>;
   static bool attr_set = false;  // host-side, once per instantiation
@@ -395,8 +454,14 @@ static int launch_decode(void* out, const void* q, const void* kc, const void* v
     attr_set = true;
   }
   dim3 grid(num_splits, nkv, B);
+  if (cluster) {
+    launch_kc(kern, grid, dim3(128), smem, s, (unsigned)num_splits, (T*)out, (const T*)q, (const CT*)kc,
+              (const CT*)vc, bt, sl, sinks, nq, nkv, q_stride, bs, max_blocks, window, scale * k_scale * kLog2e,
+              v_scale, ws, num_splits, 1);
+    return (int)cudaGetLastError();
+  }
   launch_k(kern, dim3(grid), dim3(128), smem, s, (T*)out, (const T*)q, (const CT*)kc, (const CT*)vc, bt, sl, sinks, nq, nkv, q_stride,
-                               bs, max_blocks, window, scale * k_scale * kLog2e, v_scale, ws, num_splits);
+                               bs, max_blocks, window, scale * k_scale * kLog2e, v_scale, ws, num_splits, 0);
   if (num_splits > 1) {
     launch_k(decode_combine_kernel<D, T>, dim3(nq, B), dim3(D < 128 ? D : 128), 0, s, (T*)out, ws, sinks, nq, num_splits,
                                                                            v_scale);
