@@ -68,7 +68,7 @@ def test_group_rank_math():
     assert cols[0] == [0, 8, 16, 24] and cols[7] == [7, 15, 23, 31]
     assert ps.build_inter_node_peer_group_ranks(16, 2)[3] == [3, 11]
     kv, heads = ps.build_dcp_group_ranks(8, 8, 2)
-    assert kv[0] == [0, 4] and heads[0] == [0, 1, 2, 3]
+    assert kv == [[0, 1], [2, 3], [4, 5], [6, 7]] and heads == [[0, 2, 4, 6], [1, 3, 5, 7]]
     with pytest.raises(ValueError):
         ps.build_component_tp_group_ranks(16, 8, 4)
 

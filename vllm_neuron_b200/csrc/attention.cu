@@ -31,6 +31,31 @@ namespace b200 {
 
 constexpr int kKT = 64;  // keys per tile
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// Decode context parallelism: the tokens of a sequence are dealt to the ``size`` ranks of a
+// DCP group one cache block at a time (token t lives on rank (t / bs) % size), and every rank
+// stores its share densely in the same virtual blocks: local token u of block-table entry
+// u / bs.  A shard computes attention over its own tokens and writes (normalised output,
+// natural-log LSE) without sinks; the group merges the shards.
+struct CpArgs {
+  int rank, size;  // size 1: no context parallelism
+  float* lse;      // [tokens, nq] partial log-sum-exp; nullptr: plain attention (sinks applied)
+};
+
+// number of this rank's tokens among global positions [0, x)
+B200_D int cp_count_local(int x, int bs_log, CpArgs cp) {
+  if (cp.size == 1) return x;
+  const int span = cp.size << bs_log;
+  const int full = x / span, rem = x - full * span;
+  return (full << bs_log) + min(max(rem - (cp.rank << bs_log), 0), 1 << bs_log);
+}
+
+// global position of this rank's local token u
+B200_D int cp_global_pos(int u, int bs_log, CpArgs cp) {
+  if (cp.size == 1) return u;
+  return ((((u >> bs_log) * cp.size) + cp.rank) << bs_log) + (u & ((1 << bs_log) - 1));
+}
 
 // ---------------------------------------------------------------------------------------
 // K/V tile loader: 64 keys x D dims into swizzled bf16 shared memory.  For fp8 caches the
@@ -115,7 +140,7 @@ __global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const 
                                                      const int* __restrict__ seq_lens, const float* __restrict__ sinks,
                                                      int nq, int nkv, int q_stride, int bs, int max_blocks, int window,
                                                      float scale_log2, float v_scale, float* __restrict__ ws,
-                                                     int num_splits, int cluster_merge) {
+                                                     int num_splits, int cluster_merge, CpArgs cp) {
   pdl_wait();  // predecessor output visible (programmatic dependent launch)
   pdl_trigger();
   constexpr int C = D / 8;
@@ -128,8 +153,11 @@ __global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const 
   const int G = nq / nkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qd = lane & 3, r0 = lane >> 2;
-  const int L = seq_lens[b];
-  const int lo = (window > 0) ? max(0, L - window) : 0;
+  const int bs_log = 31 - __clz(bs);
+  // this rank's key range [lo, L) in local token indices (the window is in global positions)
+  const int Lg = seq_lens[b];
+  const int L = cp_count_local(Lg, bs_log, cp);
+  const int lo = (window > 0) ? cp_count_local(max(0, Lg - window), bs_log, cp) : 0;
   // split the key range [lo, L) by whole cache blocks
   int key_begin = 0, key_end = 0;
   if (L > 0) {
@@ -142,7 +170,6 @@ __global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const 
     }
   }
   const int* bt_row = block_tables + (size_t)b * max_blocks;
-  const int bs_log = 31 - __clz(bs);
   const bool hi_rows = G > 8;  // rows r0 + 8 of the 16-row MMA hold real heads
 
   // S-stage cp.async ring: tiles t+1 .. t+S-1 are in flight while tile t is consumed, so a
@@ -334,6 +361,7 @@ __global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const 
       }
       const float r = lt > 0.f ? at / lt * v_scale : 0.f;
       out[(size_t)b * nq * D + (size_t)head * D + dim] = from_float<T>(r);
+      if (cp.lse != nullptr && dim == 0) cp.lse[(size_t)b * nq + head] = lt > 0.f ? (Mt + log2f(lt)) * kLn2 : -INFINITY;
     } else {
       float* w = ws + (((size_t)b * nq + head) * num_splits + split) * (D + 1);
       w[dim] = l > 0.f ? acc / l : 0.f;
@@ -376,6 +404,7 @@ __global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const 
         }
       }
       out[(size_t)b * nq * D + (size_t)head * D + dim] = from_float<T>(den > 0.f ? acc / den * v_scale : 0.f);
+      if (cp.lse != nullptr && dim == 0) cp.lse[(size_t)b * nq + head] = den > 0.f ? (M + log2f(den)) * kLn2 : -INFINITY;
     }
     cl.sync();  // keep this CTA's shared memory alive until every peer has read it
   }
@@ -383,7 +412,8 @@ __global__ void __launch_bounds__(128) decode_kernel(T* __restrict__ out, const 
 
 template <int D, typename T>
 __global__ void decode_combine_kernel(T* __restrict__ out, const float* __restrict__ ws,
-                                      const float* __restrict__ sinks, int nq, int num_splits, float v_scale) {
+                                      const float* __restrict__ sinks, int nq, int num_splits, float v_scale,
+                                      float* __restrict__ lse_out) {
   pdl_wait();  // predecessor output visible (programmatic dependent launch)
   pdl_trigger();
   // LSE merge of the splits (num_splits <= 32): one warp reads every split's log-sum-exp
@@ -408,6 +438,7 @@ __global__ void decode_combine_kernel(T* __restrict__ out, const float* __restri
     if (sinks) den += exp2f(sk - M);
     wt[lane] = e;
     if (lane == 0) scale_s = den > 0.f ? v_scale / den : 0.f;
+    if (lane == 0 && lse_out != nullptr) lse_out[(size_t)b * nq + head] = den > 0.f ? (M + log2f(den)) * kLn2 : -INFINITY;
   }
   __syncthreads();
   const float sc = scale_s;
@@ -432,7 +463,8 @@ inline bool decode_cluster_enabled() {
 template <int D, typename T, typename CT>
 static int launch_decode(void* out, const void* q, const void* kc, const void* vc, const int* bt, const int* sl,
                          const float* sinks, int B, int nq, int nkv, int q_stride, int bs, int max_blocks, int window,
-                         float scale, float k_scale, float v_scale, float* ws, int num_splits, cudaStream_t s) {
+                         float scale, float k_scale, float v_scale, float* ws, int num_splits, CpArgs cp,
+                         cudaStream_t s) {
   if (B == 0) return 0;
   if (num_splits < 1 || num_splits > 32) return kBadShape;  // the combine merges <= 32 splits in one warp
   // 2, 4 or 8 splits merge inside a thread-block cluster; other counts go through the
@@ -457,14 +489,14 @@ static int launch_decode(void* out, const void* q, const void* kc, const void* v
   if (cluster) {
     launch_kc(kern, grid, dim3(128), smem, s, (unsigned)num_splits, (T*)out, (const T*)q, (const CT*)kc,
               (const CT*)vc, bt, sl, sinks, nq, nkv, q_stride, bs, max_blocks, window, scale * k_scale * kLog2e,
-              v_scale, ws, num_splits, 1);
+              v_scale, ws, num_splits, 1, cp);
     return (int)cudaGetLastError();
   }
-  launch_k(kern, dim3(grid), dim3(128), smem, s, (T*)out, (const T*)q, (const CT*)kc, (const CT*)vc, bt, sl, sinks, nq, nkv, q_stride,
-                               bs, max_blocks, window, scale * k_scale * kLog2e, v_scale, ws, num_splits, 0);
+  launch_k(kern, dim3(grid), dim3(128), smem, s, (T*)out, (const T*)q, (const CT*)kc, (const CT*)vc, bt, sl, sinks,
+           nq, nkv, q_stride, bs, max_blocks, window, scale * k_scale * kLog2e, v_scale, ws, num_splits, 0, cp);
   if (num_splits > 1) {
-    launch_k(decode_combine_kernel<D, T>, dim3(nq, B), dim3(D < 128 ? D : 128), 0, s, (T*)out, ws, sinks, nq, num_splits,
-                                                                           v_scale);
+    launch_k(decode_combine_kernel<D, T>, dim3(nq, B), dim3(D < 128 ? D : 128), 0, s, (T*)out, ws, sinks, nq,
+             num_splits, v_scale, cp.lse);
   }
   return (int)cudaGetLastError();
 }
@@ -483,7 +515,7 @@ __global__ void __launch_bounds__(128) prefill_kernel(T* __restrict__ out, const
                                                       PagedKV pk, const int* __restrict__ seq_lens,
                                                       const int* __restrict__ qsl, const float* __restrict__ sinks,
                                                       int nq, int nkv, int q_stride, int kv_stride, int window,
-                                                      int causal, float scale_log2, float v_scale) {
+                                                      int causal, float scale_log2, float v_scale, CpArgs cp) {
   pdl_wait();  // predecessor output visible (programmatic dependent launch)
   pdl_trigger();
   // DP: head dim padded to a multiple of 16 for the QK^T k-steps (72 -> 80)
@@ -498,15 +530,17 @@ __global__ void __launch_bounds__(128) prefill_kernel(T* __restrict__ out, const
   const int G = nq / nkv, h = head / G;
   const int q0 = qsl[b], qlen = qsl[b + 1] - q0;
   if (qt * 64 >= qlen) return;
-  const int L = kPaged ? seq_lens[b] : qlen;
+  const int L = kPaged ? seq_lens[b] : qlen;  // global sequence length
+  const int bs_log = kPaged ? 31 - __clz(pk.bs) : 0;
+  const int L_loc = kPaged ? cp_count_local(L, bs_log, cp) : L;  // this rank's cached tokens
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qd = lane & 3, r0 = lane >> 2;
   const int pos_base = L - qlen;  // absolute position of query row 0
   const int row_w = qt * 64 + warp * 16;  // first query row of this warp
-  // key range needed by the CTA
+  // key range needed by the CTA, in local token indices
   const int p_first = pos_base + qt * 64, p_last = pos_base + min(qlen, (qt + 1) * 64) - 1;
-  int key_lo = 0, key_hi = causal ? p_last + 1 : L;
-  if (window > 0) key_lo = max(0, p_first - window + 1);
+  int key_lo = 0, key_hi = causal ? cp_count_local(p_last + 1, bs_log, cp) : L_loc;
+  if (window > 0) key_lo = cp_count_local(max(0, p_first - window + 1), bs_log, cp);
   key_lo = (key_lo / kKT) * kKT;
 
   uint32_t qf[DP / 16][4];
@@ -540,8 +574,8 @@ __global__ void __launch_bounds__(128) prefill_kernel(T* __restrict__ out, const
     if constexpr (kPaged) {
       const int* bt_row = pk.block_tables + (size_t)b * pk.max_blocks;
       if constexpr (D == DP) {
-        load_kv_tile<D, CT>(K, V, stage + buf * 2 * kKT * D, kc, vc, bt_row, key0, min(key_hi, L), 31 - __clz(pk.bs),
-                            nkv, h);
+        load_kv_tile<D, CT>(K, V, stage + buf * 2 * kKT * D, kc, vc, bt_row, key0, min(key_hi, L_loc), bs_log, nkv,
+                            h);
       }
     } else {
       // contiguous [T, nkv, D] K/V of this sequence; D may be padded to DP with zeros
@@ -581,8 +615,9 @@ __global__ void __launch_bounds__(128) prefill_kernel(T* __restrict__ out, const
     // skip tiles entirely outside this warp's visible range
     // warp-uniform bounds: rows row_w .. row_w+15 sit at positions wp_lo .. wp_hi
     const int wp_lo = pos_base + row_w, wp_hi = pos_base + row_w + 15;
-    const bool warp_dead = (row_w >= qlen) || (causal && key0 > wp_hi) ||
-                           (window > 0 && key0 + kKT - 1 <= wp_lo - window);
+    const int kp_first = cp_global_pos(key0, bs_log, cp), kp_last = cp_global_pos(key0 + kKT - 1, bs_log, cp);
+    const bool warp_dead = (row_w >= qlen) || (causal && kp_first > wp_hi) ||
+                           (window > 0 && kp_last <= wp_lo - window);
     if (!warp_dead) {
       float s[8][4];
 #pragma unroll
@@ -607,10 +642,11 @@ __global__ void __launch_bounds__(128) prefill_kernel(T* __restrict__ out, const
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int key = key0 + j * 8 + 2 * qd + (e & 1);
+          const int kp = cp_global_pos(key, bs_log, cp);
           const int p = my_p[e >> 1];
-          bool ok = key < L;
-          if (causal) ok = ok && key <= p;
-          if (window > 0) ok = ok && key > p - window;
+          bool ok = key < L_loc;
+          if (causal) ok = ok && kp <= p;
+          if (window > 0) ok = ok && kp > p - window;
           const float v = ok ? s[j][e] * scale_log2 : -INFINITY;
           s[j][e] = v;
           mx[e >> 1] = fmaxf(mx[e >> 1], v);
@@ -680,6 +716,8 @@ __global__ void __launch_bounds__(128) prefill_kernel(T* __restrict__ out, const
     }
     const float inv = l > 0.f ? f / l * v_scale : 0.f;
     const int row = row_w + r0 + r * 8;
+    if (cp.lse != nullptr && row < qlen && qd == 0)
+      cp.lse[(size_t)(q0 + row) * nq + head] = l > 0.f ? (M + log2f(l)) * kLn2 : -INFINITY;
     if (row < qlen) {
       T* op = out + (size_t)(q0 + row) * nq * D + (size_t)head * D;
 #pragma unroll
@@ -698,7 +736,7 @@ template <int D, int DP, typename T, typename CT, bool kPaged>
 static int launch_prefill(void* out, const void* q, const void* kc, const void* vc, PagedKV pk, const int* sl,
                           const int* qsl, const float* sinks, int B, int nq, int nkv, int q_stride, int kv_stride,
                           int window, int causal, float scale, float k_scale, float v_scale, int max_q,
-                          cudaStream_t s) {
+                          CpArgs cp, cudaStream_t s) {
   if (B == 0 || max_q == 0) return 0;
   const size_t tile = (size_t)kKT * row_stride_chunks(DP / 8) * 8;
   const size_t smem = 2 * 2 * tile * sizeof(__nv_bfloat16) + (sizeof(CT) == 1 ? 2 * 2 * kKT * D : 0);
@@ -710,7 +748,7 @@ static int launch_prefill(void* out, const void* q, const void* kc, const void* 
   }
   dim3 grid(cdiv(max_q, 64), nq, B);
   launch_k(kern, dim3(grid), dim3(128), smem, s, (T*)out, (const T*)q, (const CT*)kc, (const CT*)vc, pk, sl, qsl, sinks, nq, nkv,
-                               q_stride, kv_stride, window, causal, scale * k_scale * kLog2e, v_scale);
+           q_stride, kv_stride, window, causal, scale * k_scale * kLog2e, v_scale, cp);
   return (int)cudaGetLastError();
 }
 
@@ -718,27 +756,73 @@ static int launch_prefill(void* out, const void* q, const void* kc, const void* 
 
 using namespace b200;
 
-extern "C" int b200_paged_attention_decode(void* out, const void* q, const void* k_cache, const void* v_cache,
-                                           const int* block_tables, const int* seq_lens, const float* sinks, int B,
-                                           int nq, int nkv, int d, int q_stride, int block_size, int max_blocks,
-                                           int window, float scale, float k_scale, float v_scale, float* workspace,
-                                           int num_splits, int dtype, int cache_dtype, cudaStream_t s) {
+static int paged_decode(void* out, const void* q, const void* k_cache, const void* v_cache, const int* block_tables,
+                        const int* seq_lens, const float* sinks, int B, int nq, int nkv, int d, int q_stride,
+                        int block_size, int max_blocks, int window, float scale, float k_scale, float v_scale,
+                        float* workspace, int num_splits, CpArgs cp, int dtype, int cache_dtype, cudaStream_t s) {
   if (nq % nkv || nq / nkv > 16 || dtype != kBF16) return kBadShape;
+  if (cp.size < 1 || cp.rank < 0 || cp.rank >= cp.size || (cp.size > 1 && (cp.lse == nullptr || sinks != nullptr)))
+    return kBadShape;  // a shard writes its LSE and leaves the sinks to the merge
   if (block_size <= 0 || (block_size & (block_size - 1))) return kBadShape;  // addressed by shifts
   const bool fp8 = cache_dtype == kFP8E4M3;
 #define DEC(DD)                                                                                                    \
   return fp8 ? launch_decode<DD, __nv_bfloat16, __nv_fp8_e4m3>(out, q, k_cache, v_cache, block_tables, seq_lens,   \
                                                                 sinks, B, nq, nkv, q_stride, block_size, max_blocks, \
                                                                 window, scale, k_scale, v_scale, workspace,          \
-                                                                num_splits, s)                                       \
+                                                                num_splits, cp, s)                                   \
              : launch_decode<DD, __nv_bfloat16, __nv_bfloat16>(out, q, k_cache, v_cache, block_tables, seq_lens,   \
                                                                 sinks, B, nq, nkv, q_stride, block_size, max_blocks, \
                                                                 window, scale, k_scale, v_scale, workspace,          \
-                                                                num_splits, s);
+                                                                num_splits, cp, s);
   if (d == 64) { DEC(64) }
   if (d == 128) { DEC(128) }
   if (d == 256) { DEC(256) }
 #undef DEC
+  return kBadShape;
+}
+
+extern "C" int b200_paged_attention_decode(void* out, const void* q, const void* k_cache, const void* v_cache,
+                                           const int* block_tables, const int* seq_lens, const float* sinks, int B,
+                                           int nq, int nkv, int d, int q_stride, int block_size, int max_blocks,
+                                           int window, float scale, float k_scale, float v_scale, float* workspace,
+                                           int num_splits, int dtype, int cache_dtype, cudaStream_t s) {
+  return paged_decode(out, q, k_cache, v_cache, block_tables, seq_lens, sinks, B, nq, nkv, d, q_stride, block_size,
+                      max_blocks, window, scale, k_scale, v_scale, workspace, num_splits, CpArgs{0, 1, nullptr},
+                      dtype, cache_dtype, s);
+}
+
+extern "C" int b200_paged_attention_decode_cp(void* out, float* lse, const void* q, const void* k_cache,
+                                              const void* v_cache, const int* block_tables, const int* seq_lens,
+                                              int B, int nq, int nkv, int d, int q_stride, int block_size,
+                                              int max_blocks, int window, float scale, float k_scale, float v_scale,
+                                              float* workspace, int num_splits, int cp_rank, int cp_size, int dtype,
+                                              int cache_dtype, cudaStream_t s) {
+  return paged_decode(out, q, k_cache, v_cache, block_tables, seq_lens, nullptr, B, nq, nkv, d, q_stride,
+                      block_size, max_blocks, window, scale, k_scale, v_scale, workspace, num_splits,
+                      CpArgs{cp_rank, cp_size, lse}, dtype, cache_dtype, s);
+}
+
+static int paged_prefill(void* out, const void* q, const void* k_cache, const void* v_cache, const int* block_tables,
+                         const int* seq_lens, const int* query_start_loc, const float* sinks, int B, int nq, int nkv,
+                         int d, int q_stride, int block_size, int max_blocks, int window, float scale, float k_scale,
+                         float v_scale, int max_query_len, CpArgs cp, int dtype, int cache_dtype, cudaStream_t s) {
+  if (nq % nkv || dtype != kBF16) return kBadShape;
+  if (cp.size < 1 || cp.rank < 0 || cp.rank >= cp.size || (cp.size > 1 && (cp.lse == nullptr || sinks != nullptr)))
+    return kBadShape;
+  if (block_size <= 0 || (block_size & (block_size - 1))) return kBadShape;  // addressed by shifts
+  PagedKV pk{block_tables, max_blocks, block_size, nkv};
+  const bool fp8 = cache_dtype == kFP8E4M3;
+#define PRE(DD)                                                                                                     \
+  return fp8 ? launch_prefill<DD, DD, __nv_bfloat16, __nv_fp8_e4m3, true>(                                          \
+                   out, q, k_cache, v_cache, pk, seq_lens, query_start_loc, sinks, B, nq, nkv, q_stride, 0, window,  \
+                   1, scale, k_scale, v_scale, max_query_len, cp, s)                                                 \
+             : launch_prefill<DD, DD, __nv_bfloat16, __nv_bfloat16, true>(                                          \
+                   out, q, k_cache, v_cache, pk, seq_lens, query_start_loc, sinks, B, nq, nkv, q_stride, 0, window,  \
+                   1, scale, k_scale, v_scale, max_query_len, cp, s);
+  if (d == 64) { PRE(64) }
+  if (d == 128) { PRE(128) }
+  if (d == 256) { PRE(256) }
+#undef PRE
   return kBadShape;
 }
 
@@ -748,22 +832,21 @@ extern "C" int b200_paged_attention_prefill(void* out, const void* q, const void
                                             int block_size, int max_blocks, int window, float scale, float k_scale,
                                             float v_scale, int max_query_len, int dtype, int cache_dtype,
                                             cudaStream_t s) {
-  if (nq % nkv || dtype != kBF16) return kBadShape;
-  if (block_size <= 0 || (block_size & (block_size - 1))) return kBadShape;  // addressed by shifts
-  PagedKV pk{block_tables, max_blocks, block_size, nkv};
-  const bool fp8 = cache_dtype == kFP8E4M3;
-#define PRE(DD)                                                                                                     \
-  return fp8 ? launch_prefill<DD, DD, __nv_bfloat16, __nv_fp8_e4m3, true>(                                          \
-                   out, q, k_cache, v_cache, pk, seq_lens, query_start_loc, sinks, B, nq, nkv, q_stride, 0, window,  \
-                   1, scale, k_scale, v_scale, max_query_len, s)                                                     \
-             : launch_prefill<DD, DD, __nv_bfloat16, __nv_bfloat16, true>(                                          \
-                   out, q, k_cache, v_cache, pk, seq_lens, query_start_loc, sinks, B, nq, nkv, q_stride, 0, window,  \
-                   1, scale, k_scale, v_scale, max_query_len, s);
-  if (d == 64) { PRE(64) }
-  if (d == 128) { PRE(128) }
-  if (d == 256) { PRE(256) }
-#undef PRE
-  return kBadShape;
+  (void)T;
+  return paged_prefill(out, q, k_cache, v_cache, block_tables, seq_lens, query_start_loc, sinks, B, nq, nkv, d,
+                       q_stride, block_size, max_blocks, window, scale, k_scale, v_scale, max_query_len,
+                       CpArgs{0, 1, nullptr}, dtype, cache_dtype, s);
+}
+
+extern "C" int b200_paged_attention_prefill_cp(void* out, float* lse, const void* q, const void* k_cache,
+                                               const void* v_cache, const int* block_tables, const int* seq_lens,
+                                               const int* query_start_loc, int B, int nq, int nkv, int d,
+                                               int q_stride, int block_size, int max_blocks, int window, float scale,
+                                               float k_scale, float v_scale, int max_query_len, int cp_rank,
+                                               int cp_size, int dtype, int cache_dtype, cudaStream_t s) {
+  return paged_prefill(out, q, k_cache, v_cache, block_tables, seq_lens, query_start_loc, nullptr, B, nq, nkv, d,
+                       q_stride, block_size, max_blocks, window, scale, k_scale, v_scale, max_query_len,
+                       CpArgs{cp_rank, cp_size, lse}, dtype, cache_dtype, s);
 }
 
 extern "C" int b200_varlen_attention(void* out, const void* q, const void* k, const void* v, const int* cu_seqlens,
@@ -774,7 +857,8 @@ extern "C" int b200_varlen_attention(void* out, const void* q, const void* k, co
 #define VAR(DD, DDP)                                                                                           \
   return launch_prefill<DD, DDP, __nv_bfloat16, __nv_bfloat16, false>(out, q, k, v, pk, nullptr, cu_seqlens,    \
                                                                       nullptr, B, nq, nkv, nq * DD, nkv * DD, 0, \
-                                                                      causal, scale, 1.f, 1.f, max_seqlen, s);
+                                                                      causal, scale, 1.f, 1.f, max_seqlen,      \
+                                                                      CpArgs{0, 1, nullptr}, s);
   if (d == 64) { VAR(64, 64) }
   if (d == 72) { VAR(72, 80) }
   if (d == 80) { VAR(80, 80) }

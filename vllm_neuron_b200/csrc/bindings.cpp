@@ -150,6 +150,57 @@ void paged_attention_prefill(Tensor out, Tensor q, Tensor k_cache, Tensor v_cach
            "paged_attention_prefill");
 }
 
+void paged_attention_decode_cp(Tensor out, Tensor lse, Tensor q, Tensor k_cache, Tensor v_cache,
+                               Tensor block_tables, Tensor seq_lens, int64_t window, double scale, double k_scale,
+                               double v_scale, c10::optional<Tensor> workspace, int64_t num_splits, int64_t cp_rank,
+                               int64_t cp_size) {
+  check_cuda(q, "q");
+  const int64_t d = q.size(2);
+  check_q(q, d);
+  TORCH_CHECK(out.is_contiguous() && lse.is_contiguous() && lse.scalar_type() == at::kFloat, "out / lse");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt, "int32 tables");
+  TORCH_CHECK(block_tables.stride(1) == 1, "block_tables rows must be contiguous");
+  const int B = seq_lens.size(0);
+  TORCH_CHECK(q.size(0) == B, "decode expects one query token per sequence");
+  const int nq = q.size(1), nkv = k_cache.size(1);
+  TORCH_CHECK(lse.numel() >= (int64_t)B * nq, "lse too small");
+  float* ws = nullptr;
+  if (num_splits > 1 && workspace.has_value()) {
+    TORCH_CHECK(workspace->numel() >= (int64_t)B * nq * num_splits * (d + 1), "workspace too small");
+    ws = workspace->data_ptr<float>();
+  }
+  c10::cuda::CUDAGuard g(q.device());
+  check_rc(b200_paged_attention_decode_cp(out.data_ptr(), lse.data_ptr<float>(), q.data_ptr(), k_cache.data_ptr(),
+                                          v_cache.data_ptr(), block_tables.data_ptr<int>(), seq_lens.data_ptr<int>(),
+                                          B, nq, nkv, d, q.stride(0), k_cache.size(2), block_tables.stride(0), window,
+                                          (float)scale, (float)k_scale, (float)v_scale, ws, num_splits, cp_rank,
+                                          cp_size, dt(q), dt(k_cache), stream()),
+           "paged_attention_decode_cp");
+}
+
+void paged_attention_prefill_cp(Tensor out, Tensor lse, Tensor q, Tensor k_cache, Tensor v_cache,
+                                Tensor block_tables, Tensor seq_lens, Tensor qsl, int64_t window, double scale,
+                                double k_scale, double v_scale, int64_t max_query_len, int64_t cp_rank,
+                                int64_t cp_size) {
+  check_cuda(q, "q");
+  const int64_t d = q.size(2);
+  check_q(q, d);
+  TORCH_CHECK(out.is_contiguous() && lse.is_contiguous() && lse.scalar_type() == at::kFloat, "out / lse");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt &&
+                  qsl.scalar_type() == at::kInt,
+              "int32 metadata");
+  TORCH_CHECK(lse.numel() >= q.size(0) * q.size(1), "lse too small");
+  const int B = seq_lens.size(0);
+  c10::cuda::CUDAGuard g(q.device());
+  check_rc(b200_paged_attention_prefill_cp(out.data_ptr(), lse.data_ptr<float>(), q.data_ptr(), k_cache.data_ptr(),
+                                           v_cache.data_ptr(), block_tables.data_ptr<int>(),
+                                           seq_lens.data_ptr<int>(), qsl.data_ptr<int>(), B, q.size(1),
+                                           k_cache.size(1), d, q.stride(0), k_cache.size(2), block_tables.stride(0),
+                                           window, (float)scale, (float)k_scale, (float)v_scale, max_query_len,
+                                           cp_rank, cp_size, dt(q), dt(k_cache), stream()),
+           "paged_attention_prefill_cp");
+}
+
 void varlen_attention(Tensor out, Tensor q, Tensor k, Tensor v, Tensor cu, double scale, bool causal,
                       int64_t max_seqlen) {
   check_cuda(q, "q");
@@ -222,6 +273,14 @@ TORCH_LIBRARY(b200, m) {
       "Tensor seq_lens, Tensor query_start_loc, Tensor? sinks, int window, float scale, float k_scale, "
       "float v_scale, int max_query_len) -> ()");
   m.def(
+      "paged_attention_decode_cp(Tensor(a!) out, Tensor(b!) lse, Tensor q, Tensor k_cache, Tensor v_cache, "
+      "Tensor block_tables, Tensor seq_lens, int window, float scale, float k_scale, float v_scale, "
+      "Tensor? workspace, int num_splits, int cp_rank, int cp_size) -> ()");
+  m.def(
+      "paged_attention_prefill_cp(Tensor(a!) out, Tensor(b!) lse, Tensor q, Tensor k_cache, Tensor v_cache, "
+      "Tensor block_tables, Tensor seq_lens, Tensor query_start_loc, int window, float scale, float k_scale, "
+      "float v_scale, int max_query_len, int cp_rank, int cp_size) -> ()");
+  m.def(
       "varlen_attention(Tensor(a!) out, Tensor q, Tensor k, Tensor v, Tensor cu_seqlens, float scale, bool causal, "
       "int max_seqlen) -> ()");
   m.def("topk_softmax(Tensor(a!) ids, Tensor(b!) weights, Tensor logits) -> ()");
@@ -245,6 +304,8 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("rope_kv_write", &rope_kv_write);
   m.impl("paged_attention_decode", &paged_attention_decode);
   m.impl("paged_attention_prefill", &paged_attention_prefill);
+  m.impl("paged_attention_decode_cp", &paged_attention_decode_cp);
+  m.impl("paged_attention_prefill_cp", &paged_attention_prefill_cp);
   m.impl("varlen_attention", &varlen_attention);
   m.impl("topk_softmax", &topk_softmax);
   m.impl("argmax", &argmax);

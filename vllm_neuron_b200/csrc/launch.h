@@ -40,6 +40,23 @@ int b200_paged_attention_prefill(void* out, const void* q, const void* k_cache, 
                                  int block_size, int max_blocks, int window, float scale, float k_scale,
                                  float v_scale, int max_query_len, int dtype, int cache_dtype, cudaStream_t s);
 
+// Decode context parallelism: attention of one DCP shard (rank ``cp_rank`` of ``cp_size``)
+// over the tokens it holds (token t on rank (t / block_size) % cp_size, stored densely in the
+// same virtual blocks).  seq_lens are global lengths; windows are in global positions.  Writes
+// the shard's normalised output and its natural-log LSE [tokens, nq] (-inf: no visible key);
+// sinks join in the merge.
+int b200_paged_attention_decode_cp(void* out, float* lse, const void* q, const void* k_cache, const void* v_cache,
+                                   const int* block_tables, const int* seq_lens, int B, int nq, int nkv, int d,
+                                   int q_stride, int block_size, int max_blocks, int window, float scale,
+                                   float k_scale, float v_scale, float* workspace, int num_splits, int cp_rank,
+                                   int cp_size, int dtype, int cache_dtype, cudaStream_t s);
+
+int b200_paged_attention_prefill_cp(void* out, float* lse, const void* q, const void* k_cache, const void* v_cache,
+                                    const int* block_tables, const int* seq_lens, const int* query_start_loc, int B,
+                                    int nq, int nkv, int d, int q_stride, int block_size, int max_blocks, int window,
+                                    float scale, float k_scale, float v_scale, int max_query_len, int cp_rank,
+                                    int cp_size, int dtype, int cache_dtype, cudaStream_t s);
+
 int b200_varlen_attention(void* out, const void* q, const void* k, const void* v, const int* cu_seqlens, int B,
                           int T, int nq, int nkv, int d, float scale, int causal, int max_seqlen, int dtype,
                           cudaStream_t s);

@@ -55,7 +55,10 @@ class LLMEngine:
         hybrid = hasattr(self.worker.model, "get_state_spec")
         if hybrid and cfg.enable_prefix_caching:
             logger.info("prefix caching disabled: recurrent (linear-attention) layers keep per-request state")
-        self.kv = KVCacheManager(n_blocks, cfg.block_size, cfg.enable_prefix_caching and not hybrid)
+        # with decode context parallelism a block-table entry covers block_size tokens on each
+        # of the dcp ranks
+        self.kv = KVCacheManager(n_blocks, cfg.block_size * cfg.decode_context_parallel_size,
+                                 cfg.enable_prefix_caching and not hybrid)
         k = cfg.speculative_config.num_speculative_tokens if cfg.speculative_config else 0
         self.scheduler = Scheduler(self.kv, cfg.max_num_seqs, cfg.max_num_batched_tokens, cfg.max_model_len,
                                    cfg.max_num_prefills_per_step, cfg.enable_chunked_prefill, k)
@@ -71,6 +74,8 @@ class LLMEngine:
         self.profiler = Profiler(ProfilerConfig.from_dict(cfg.profiler_config), rank)
         self.connector = None
         if cfg.kv_transfer_config is not None:
+            if cfg.decode_context_parallel_size > 1:
+                raise ValueError("KV transfer with decode context parallelism is not supported")
             self._init_connector(hf)
         self._pending: list[tuple] = []
         self._stopped = False

@@ -74,13 +74,20 @@ class AsyncStep:
 
 class ModelRunner:
     def __init__(self, cfg: EngineConfig, model: torch.nn.Module, device: torch.device, tp_group,
-                 vocab_size: int):
+                 vocab_size: int, cp_group=None):
         self.cfg = cfg
         self.model = model
         self.device = device
         self.bs = cfg.block_size
+        # decode context parallelism: a virtual block of bs * cp tokens is dealt to the cp
+        # ranks bs tokens each (token t on rank (t // bs) % cp, at local index
+        # (t // (bs * cp)) * bs + t % bs of the block)
+        self.cp_group = cp_group if (cp_group is not None and cp_group.world_size > 1) else None
+        self.cp = self.cp_group.world_size if self.cp_group is not None else 1
+        self.cp_rank = self.cp_group.rank_in_group if self.cp_group is not None else 0
+        self.vbs = self.bs * self.cp
         self.max_model_len = cfg.max_model_len
-        self.max_blocks = math.ceil(cfg.max_model_len / cfg.block_size)
+        self.max_blocks = math.ceil(cfg.max_model_len / self.vbs)
         nc = cfg.neuron_config
         buckets = nc.num_seqs_buckets or nc.decode_batch_buckets
         self.decode_buckets = (validate_buckets("num_seqs_buckets", buckets, cfg.max_num_seqs) if buckets
@@ -225,7 +232,8 @@ class ModelRunner:
                  for layer in getattr(self.model, "layers", [])) if hasattr(self.model, "layers") else 0
         d = max((l.head_dim for l in spec.layers), default=64)
         if self.device.type == "cuda" and hq:
-            self.workspace = torch.empty(self.cfg.max_num_seqs * max(hq, 1) * self.max_splits(1) * (d + 2),
+            # with DCP every rank attends the query heads of its whole DCP group
+            self.workspace = torch.empty(self.cfg.max_num_seqs * max(hq, 1) * self.cp * self.max_splits(1) * (d + 2),
                                          dtype=torch.float32, device=self.device)
         self._hq = hq
 
@@ -317,7 +325,7 @@ class ModelRunner:
         n_sel = 0
         mm_rows: list = []
         has_mrope = False
-        bs = self.bs
+        bs, vbs, cp, cpr = self.bs, self.vbs, self.cp, self.cp_rank
         plain_decode = so.kind == "decode" and all(len(x.token_ids) == 1 for x in seqs)
         for i, s in enumerate(seqs):
             k = len(s.token_ids)
@@ -332,7 +340,7 @@ class ModelRunner:
                 ids[t] = s.token_ids[0]
                 delta = req.mrope_delta if req is not None else 0
                 pos[t] = p0 + delta
-                slot[t] = s.block_ids[p0 // bs] * bs + p0 % bs
+                slot[t] = s.block_ids[p0 // vbs] * bs + p0 % bs if (p0 // bs) % cp == cpr else -1
                 lidx[n_sel] = t
                 n_sel += 1
                 t += 1
@@ -346,7 +354,10 @@ class ModelRunner:
             if req is not None and req.mrope_positions is not None and so.kind == "prefill":
                 has_mrope = True
             blocks = np.asarray(s.block_ids, dtype=np.int64)
-            slot[t:t + k] = blocks[p // bs] * bs + p % bs
+            if cp == 1:
+                slot[t:t + k] = blocks[p // bs] * bs + p % bs
+            else:  # only the owning DCP rank writes a token
+                slot[t:t + k] = np.where((p // bs) % cp == cpr, blocks[p // vbs] * bs + p % bs, -1)
             if so.kind == "decode" and s.spec_token_ids:
                 lidx[n_sel:n_sel + k] = np.arange(t, t + k)
                 n_sel += k
@@ -405,9 +416,9 @@ class ModelRunner:
                            (self.h_unif, self.d_unif, B)):
             dv[:cnt].copy_(h[:cnt], non_blocking=True)
             nb_ += cnt * h.element_size()
-        max_nb = max(1, max(math.ceil(s.seq_len / self.bs) for s in seqs)) if seqs else 1
+        max_nb = max(1, max(math.ceil(s.seq_len / vbs) for s in seqs)) if seqs else 1
         if pad_seq:
-            max_nb = max(max_nb, math.ceil(int(sl[n]) / self.bs))
+            max_nb = max(max_nb, math.ceil(int(sl[n]) / vbs))
         self.d_bt[:B, :max_nb].copy_(self.h_bt[:B, :max_nb], non_blocking=True)
         nb_ += B * max_nb * 4
         self.h2d_bytes_last = nb_
@@ -415,7 +426,8 @@ class ModelRunner:
             num_tokens=T, num_seqs=B, is_decode=(so.kind == "decode" and max_q == 1),
             query_start_loc=self.d_qsl[:B + 1], seq_lens=self.d_seqlen[:B], block_tables=self.d_bt[:B],
             slot_mapping=self.d_slot[:T], logits_indices=self.d_lidx[:n_sel], max_query_len=max_q,
-            max_seq_len=max_s, workspace=self.workspace, num_splits=self.num_splits_for(B), extras=extras)
+            max_seq_len=max_s, workspace=self.workspace, num_splits=self.num_splits_for(B), extras=extras,
+            cp_group=self.cp_group)
         if spec:
             extras["spec"] = True
         return meta, T, n_sel, greedy

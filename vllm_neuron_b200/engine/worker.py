@@ -99,13 +99,33 @@ class Worker:
         MODEL_LOAD_TIME.labels(model_name=name).set(time.time() - t0)
         MODEL_LOAD_SIZE.labels(model_name=name).set(nbytes)
         vocab = getattr(mcfg, "vocab_size", None) or hf.get("vocab_size")
-        self.runner = ModelRunner(self.cfg, model, self.device, self.ps.tp, vocab)
+        dcp = self.cfg.decode_context_parallel_size
+        if dcp > 1:
+            self._check_dcp(mcfg, hf, dcp)
+        self.runner = ModelRunner(self.cfg, model, self.device, self.ps.tp, vocab,
+                                  cp_group=self.ps.dcp_kv if dcp > 1 else None)
         logger.info("rank %d loaded model (%.2f GB) in %.1fs", self.rank, nbytes / 1e9, time.time() - t0)
+
+    def _check_dcp(self, mcfg, hf: dict, dcp: int) -> None:
+        """DCP groups are runs of ``dcp`` consecutive TP ranks, which share a KV head under
+        the TP sharding exactly when ``(tp // kv_heads) % dcp == 0`` (``platform.py:579-620``
+        states the same condition as kv_heads < tp, dcp <= tp / kv_heads)."""
+        tp = self.cfg.tensor_parallel_size
+        hkv = getattr(mcfg, "num_key_value_heads", None) or hf.get("num_key_value_heads")
+        if hasattr(self.model, "get_state_spec"):
+            raise ValueError("decode context parallelism does not apply to recurrent (linear-attention) layers")
+        if self.cfg.speculative_config is not None:
+            raise ValueError("decode context parallelism with speculative decoding is not supported")
+        if not hkv or hkv * dcp > tp or (tp // hkv) % dcp:
+            raise ValueError(f"decode_context_parallel_size {dcp} needs (tp // kv_heads) % dcp == 0 "
+                             f"(tp={tp}, kv_heads={hkv})")
 
     def determine_num_blocks(self) -> int:
         spec = self.model.get_kv_spec()
         per_block = max(1, spec.bytes_per_block(self.cfg.block_size))
-        need = self.cfg.max_num_seqs * math.ceil(self.cfg.max_model_len / self.cfg.block_size) + 1
+        # a (virtual) block of a DCP rank holds block_size of its group's bs * dcp tokens
+        vbs = self.cfg.block_size * self.cfg.decode_context_parallel_size
+        need = self.cfg.max_num_seqs * math.ceil(self.cfg.max_model_len / vbs) + 1
         if self.cfg.num_gpu_blocks_override:
             n = int(self.cfg.num_gpu_blocks_override)
         elif self.device.type == "cuda":

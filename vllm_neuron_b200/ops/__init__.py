@@ -184,6 +184,14 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, met
     cache) over the paged cache.  q [T, Hq, d] (may be a strided view)."""
     T, Hq, d = q.shape
     win = int(window or 0)
+    if meta.cp_group is not None:  # decode context parallelism: shard attention + merge over the group
+        from ..parallel.dcp import dcp_attention
+
+        o = dcp_attention(q, k_cache, v_cache, meta, scale, sinks, window, k_scale, v_scale)
+        if out is not None:
+            out.copy_(o)
+            return out
+        return o
     if use_kernel(q):
         if out is None:
             out = torch.empty(T, Hq, d, dtype=q.dtype, device=q.device)
@@ -201,6 +209,32 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, met
         out.copy_(o)
         return out
     return o
+
+
+def attention_shard(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, meta: AttentionMetadata,
+                    scale: float, window: int | None, k_scale: float, v_scale: float, cp_rank: int,
+                    cp_size: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Attention of one decode-context-parallel shard over the tokens its cache holds
+    (token t lives on rank ``(t // block_size) % cp_size``).  Returns the shard's normalised
+    output [T, Hq, d] and natural-log LSE [T, Hq] fp32 (-inf where it holds no visible key);
+    no sinks (they join once, in the merge)."""
+    T, Hq, d = q.shape
+    win = int(window or 0)
+    if use_kernel(q):
+        out = torch.empty(T, Hq, d, dtype=q.dtype, device=q.device)
+        lse = torch.empty(T, Hq, dtype=torch.float32, device=q.device)
+        if meta.is_decode:
+            _k().paged_attention_decode_cp(out, lse, q, k_cache, v_cache, meta.block_tables, meta.seq_lens, win,
+                                           scale, k_scale, v_scale, meta.workspace, meta.num_splits, cp_rank,
+                                           cp_size)
+        else:
+            _k().paged_attention_prefill_cp(out, lse, q, k_cache, v_cache, meta.block_tables, meta.seq_lens,
+                                            meta.query_start_loc, win, scale, k_scale, v_scale,
+                                            meta.max_query_len, cp_rank, cp_size)
+        return out, lse
+    o, lse = ref.paged_attention(q, k_cache, v_cache, meta.block_tables, meta.seq_lens, meta.query_start_loc, scale,
+                                 None, window, k_scale, v_scale, return_lse=True, cp_rank=cp_rank, cp_size=cp_size)
+    return o, lse.transpose(0, 1).contiguous()
 
 
 def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens: torch.Tensor, scale: float,

@@ -34,3 +34,6 @@ class AttentionMetadata:
     workspace: torch.Tensor | None = None
     num_splits: int = 1
     extras: dict = field(default_factory=dict)
+    # decode context parallelism: the DCP group (ranks that hold the same KV heads and
+    # split the tokens of every sequence block by block); None without DCP
+    cp_group: object = None

@@ -12,6 +12,9 @@ from .attention import (  # noqa: F401
     write_kv_cache,
     gather_kv_from_cache,
     lse_merge,
+    cp_count_local,
+    cp_global_pos,
+    cp_slot_mapping,
 )
 from .moe import (  # noqa: F401
     clamped_swiglu,

@@ -94,16 +94,18 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
                     seq_lens: torch.Tensor, query_start_loc: torch.Tensor, scale: float,
                     sinks: torch.Tensor | None = None, sliding_window: int | None = None,
                     k_scale: float = 1.0, v_scale: float = 1.0, return_lse: bool = False,
-                    context_start: torch.Tensor | None = None):
+                    cp_rank: int = 0, cp_size: int = 1):
     """Attention of new queries over a paged KV cache that already holds them.
 
     Sequence b owns query rows ``query_start_loc[b]:query_start_loc[b+1]`` (decode: 1
     row) at positions ``seq_lens[b] - q_len + i`` and attends keys ``[0, seq_lens[b])``
     causally.  This one definition covers decode (``attention_decode.py:354``),
     segmented/chunked prefill and prefix-cache hits (``attention_segmented_cte.py:103``).
-    ``context_start`` (optional, per sequence) is the absolute position of the first
-    cached key, for DCP shards that hold an interleaved subset (positions are then
-    ``context_start + i*stride``; stride support lives in the DCP op)."""
+    With ``cp_size > 1`` the cache is one decode-context-parallel shard: it holds the
+    tokens t with ``(t // block_size) % cp_size == cp_rank``, densely, and the result is
+    that shard's partial (sinks must be None; they join in :func:`lse_merge`).  Sequence
+    lengths and windows stay global (``neuron_model_runner.py:279-328`` deals tokens the
+    same way with ``cp_kv_cache_interleave_size = block_size``)."""
     out = torch.zeros(q.shape, dtype=torch.float32, device=q.device)
     lse = torch.full((q.shape[1], q.shape[0]), float("-inf"), dtype=torch.float32, device=q.device)
     qs = query_start_loc.tolist()
@@ -113,14 +115,46 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
         if e == s or sl[b] == 0:
             continue
         L = sl[b]
-        k, v = gather_kv_from_cache(k_cache, v_cache, block_tables[b], L, k_scale, v_scale)
-        kpos = torch.arange(L, device=q.device)
+        bs = k_cache.shape[2]
+        n_loc = cp_count_local(L, bs, cp_rank, cp_size)
+        if n_loc == 0:
+            continue
+        k, v = gather_kv_from_cache(k_cache, v_cache, block_tables[b], n_loc, k_scale, v_scale)
+        kpos = cp_global_pos(torch.arange(n_loc, device=q.device), bs, cp_rank, cp_size)
         qpos = torch.arange(L - (e - s), L, device=q.device)
         o, l = _attend(q[s:e], k, v, qpos, kpos, scale, sinks, sliding_window, True)
         out[s:e] = o
         lse[:, s:e] = l
     out = out.to(q.dtype)
     return (out, lse) if return_lse else out
+
+
+def cp_count_local(x: int, block_size: int, cp_rank: int, cp_size: int) -> int:
+    """How many of the global positions [0, x) belong to DCP rank ``cp_rank``."""
+    if cp_size == 1:
+        return x
+    span = block_size * cp_size
+    full, rem = divmod(x, span)
+    return full * block_size + min(max(rem - cp_rank * block_size, 0), block_size)
+
+
+def cp_global_pos(u, block_size: int, cp_rank: int, cp_size: int):
+    """Global position of local token ``u`` (int or tensor) on DCP rank ``cp_rank``."""
+    if cp_size == 1:
+        return u
+    return ((u // block_size) * cp_size + cp_rank) * block_size + u % block_size
+
+
+def cp_slot_mapping(positions: torch.Tensor, block_tables: torch.Tensor, req_index: torch.Tensor,
+                    block_size: int, cp_rank: int, cp_size: int) -> torch.Tensor:
+    """Cache slots of new tokens on DCP rank ``cp_rank``: the owner writes token t at local
+    index ``(t // (bs * cp)) * bs + t % bs`` of virtual block ``t // (bs * cp)``; every
+    other rank gets -1 (skip)."""
+    span = block_size * cp_size
+    blk = block_tables[req_index.long(), (positions // span).long()].long()
+    own = (positions // block_size) % cp_size == cp_rank
+    slot = blk * block_size + positions % block_size
+    return torch.where(own, slot, torch.full_like(slot, -1))
 
 
 def write_kv_cache(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,

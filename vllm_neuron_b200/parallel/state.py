@@ -96,17 +96,20 @@ def build_dp_column_group_ranks(world_size: int, tp: int, attention_dp: int) -> 
 
 
 def build_dcp_group_ranks(world_size: int, tp: int, dcp: int) -> tuple[list[list[int]], list[list[int]]]:
-    """Decode context parallel.  Within each TP group, ranks ``j, j+tp/dcp, ...`` hold
-    the same KV heads and split the tokens (KV group); the complementary rows shard
-    heads (``neuron_parallel_state.py:361-414``)."""
+    """Decode context parallel.  KV groups are runs of ``dcp`` consecutive ranks of a TP
+    group: TP shards KV heads contiguously (rank r holds head r // (tp / kv_heads) when
+    TP exceeds the head count), so consecutive ranks hold the same KV head and split its
+    tokens.  Head groups take one rank from each run (stride ``dcp``) and shard the heads.
+    The reference strides its KV groups instead (``neuron_parallel_state.py:361-414``)
+    because it also re-orders the head sharding under DCP; here the TP sharding is kept."""
     if tp % dcp:
         raise ValueError(f"dcp ({dcp}) must divide tp ({tp})")
     kv_groups, head_groups = [], []
     for base in range(0, world_size, tp):
         ranks = list(range(base, base + tp))
-        rows, cols = build_2d_mesh(ranks, tp // dcp, dcp)
-        kv_groups.extend(cols)
-        head_groups.extend(rows)
+        rows, cols = build_2d_mesh(ranks, dcp, tp // dcp)
+        kv_groups.extend(rows)
+        head_groups.extend(cols)
     return kv_groups, head_groups
 
 
