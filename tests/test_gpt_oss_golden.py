@@ -51,19 +51,32 @@ def _hf_greedy(m, prompts, n_new):
     return outs
 
 
-@pytest.mark.parametrize("tp,dp", [(1, 1), (2, 1), (1, 2)])
-def test_greedy_matches_hf(ckpt, tp, dp):
+@pytest.mark.parametrize("tp,dp,a2a", [(1, 1, None), (2, 1, None), (1, 2, None), (1, 2, "naive"),
+                                       (2, 1, "naive")])
+def test_greedy_matches_hf(ckpt, tp, dp, a2a, monkeypatch):
     """dp=2: two data-parallel replicas in lockstep with the experts shared across them
     (tokens all-gathered / reduce-scattered over DP around the MoE); 5 prompts so one
-    replica runs padding steps while the other still works."""
+    replica runs padding steps while the other still works.  a2a: the EP all-to-all
+    (each token sent only to the ranks owning its experts; under TP each rank sends a
+    slice and the outputs are partial sums)."""
     from vllm_neuron_b200 import LLM, SamplingParams
+    from vllm_neuron_b200.parallel import all2all
 
+    calls = {"n": 0}
+    orig = all2all.EpAll2All.dispatch
+
+    def spy(self, *a, **k):
+        calls["n"] += 1
+        return orig(self, *a, **k)
+
+    monkeypatch.setattr(all2all.EpAll2All, "dispatch", spy)
     path, hf = ckpt
     prompts = workload(n=4 if tp == 2 else (5 if dp == 2 else 6))
     n_new = 16
     want = _hf_greedy(hf, prompts, n_new)
     llm = LLM(model=path, dtype="float32", max_model_len=512, max_num_seqs=16, max_num_batched_tokens=256,
               block_size=16, device="cpu", tensor_parallel_size=tp, data_parallel_size=dp,
+              all2all_backend=a2a or "allgather_reducescatter", spmd=not a2a,
               additional_config={"neuron_config": {"quantization": "bf16"}})
     try:
         outs = llm.generate(prompt_token_ids=prompts,
@@ -72,3 +85,4 @@ def test_greedy_matches_hf(ckpt, tp, dp):
         llm.shutdown()
     got = [o.outputs[0].token_ids for o in outs]
     assert got == want
+    assert (calls["n"] > 0) == bool(a2a)

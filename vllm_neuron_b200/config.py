@@ -205,6 +205,11 @@ class EngineConfig:
     data_parallel_size: int = 1
     decode_context_parallel_size: int = 1
     enable_expert_parallel: bool = False
+    # EP token exchange of MoE layers under data parallelism: "allgather_reducescatter"
+    # (gather every replica's tokens, reduce-scatter the outputs) or an all-to-all that
+    # sends each token only to the ranks owning its experts: "neuron" / "b200" (fused NVLink
+    # kernels on GPU), "naive" (collective all-to-all)
+    all2all_backend: str = "allgather_reducescatter"
     max_model_len: int = 8192
     max_num_seqs: int = 64
     max_num_batched_tokens: int = 4096
@@ -285,6 +290,10 @@ class EngineConfig:
         nc = self.neuron_config
         if nc.ep_degree > 1 and self.world_size % nc.ep_degree:
             raise ValueError(f"world size {self.world_size} must be divisible by ep_degree {nc.ep_degree}")
+        from .parallel.all2all import A2A_BACKENDS
+
+        if self.all2all_backend not in A2A_BACKENDS:
+            raise ValueError(f"all2all_backend must be one of {A2A_BACKENDS}, got {self.all2all_backend!r}")
         if self.decode_context_parallel_size > 1 and self.tensor_parallel_size % self.decode_context_parallel_size:
             raise ValueError("decode_context_parallel_size must divide tensor_parallel_size")
         if self.kv_cache_dtype not in ("auto", "bf16", "bfloat16", "fp8", "fp8_e4m3"):

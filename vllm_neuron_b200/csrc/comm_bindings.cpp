@@ -13,6 +13,12 @@ int b200_ipc_close(void* p);
 int b200_allreduce_fused(void* const* bases, int rank, int world, size_t slot_bytes, const void* in, void* out,
                          void* residual, const void* bias, const float* w, float eps, int T, int H, int num_blocks,
                          int* status, cudaStream_t s);
+int b200_ep_dispatch(void* const* bases, int rank, int world, size_t slot_bytes, int cpd, int T, int Tc, int H, int k,
+                     int E_local, int t_begin, int t_end, const void* x, const int* ids, const float* w, void* x_recv,
+                     int* ids_recv, float* w_recv, int* send_idx, int* status, cudaStream_t s);
+int b200_ep_combine(void* const* bases, int rank, int world, size_t slot_bytes, int cpd, int T, int Tc, int H, int k,
+                    const void* y_recv, const int* ids_recv, const int* send_idx, void* out, int* status,
+                    cudaStream_t s);
 }
 
 namespace {
@@ -67,6 +73,51 @@ void allreduce_fused(at::IntArrayRef bases, int64_t rank, int64_t slot_bytes, Te
       status.has_value() ? status->data_ptr<int>() : nullptr, at::cuda::getCurrentCUDAStream().stream());
   TORCH_CHECK(rc == 0, "b200::allreduce_fused failed with code ", rc);
 }
+void ep_dispatch(at::IntArrayRef bases, int64_t rank, int64_t slot_bytes, int64_t cpd, int64_t Tc, int64_t E_local,
+                 int64_t t_begin, int64_t t_end, Tensor x, Tensor ids, Tensor w, Tensor x_recv, Tensor ids_recv,
+                 Tensor w_recv, Tensor send_idx, c10::optional<Tensor> status) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 2, "bf16 x [T, H]");
+  TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous() && w.scalar_type() == at::kFloat &&
+                  w.is_contiguous(),
+              "int32 ids / fp32 weights [T, k]");
+  const int T = x.size(0), H = x.size(1), k = ids.size(1), world = bases.size();
+  TORCH_CHECK(ids.size(0) == T && w.size(0) == T && w.size(1) == k, "ids / weights shape");
+  TORCH_CHECK(x_recv.is_contiguous() && x_recv.numel() >= (int64_t)world * T * H && ids_recv.is_contiguous() &&
+                  ids_recv.numel() >= (int64_t)world * T * k && w_recv.is_contiguous() &&
+                  w_recv.numel() >= (int64_t)world * T * k && send_idx.is_contiguous() &&
+                  send_idx.numel() >= (int64_t)T * world,
+              "receive buffers too small");
+  TORCH_CHECK(world >= 1 && world <= 8, "1..8 ranks");
+  void* ptrs[8];
+  for (int i = 0; i < world; ++i) ptrs[i] = reinterpret_cast<void*>(bases[i]);
+  c10::cuda::CUDAGuard g(x.device());
+  const int rc = b200_ep_dispatch(ptrs, rank, world, (size_t)slot_bytes, cpd, T, Tc, H, k, E_local, t_begin, t_end,
+                                  x.data_ptr(), ids.data_ptr<int>(), w.data_ptr<float>(), x_recv.data_ptr(),
+                                  ids_recv.data_ptr<int>(), w_recv.data_ptr<float>(), send_idx.data_ptr<int>(),
+                                  status.has_value() ? status->data_ptr<int>() : nullptr,
+                                  at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(rc == 0, "b200::ep_dispatch failed with code ", rc);
+}
+
+void ep_combine(at::IntArrayRef bases, int64_t rank, int64_t slot_bytes, int64_t cpd, int64_t Tc, Tensor y_recv,
+                Tensor ids_recv, Tensor send_idx, Tensor out, c10::optional<Tensor> status) {
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.dim() == 2,
+              "bf16 out [T, H]");
+  TORCH_CHECK(y_recv.scalar_type() == at::kBFloat16 && y_recv.is_contiguous(), "bf16 expert outputs");
+  const int T = out.size(0), H = out.size(1), world = bases.size();
+  const int k = ids_recv.size(-1);
+  TORCH_CHECK(y_recv.numel() >= (int64_t)world * T * H && ids_recv.numel() >= (int64_t)world * T * k &&
+                  send_idx.numel() >= (int64_t)T * world,
+              "buffers too small");
+  void* ptrs[8];
+  for (int i = 0; i < world; ++i) ptrs[i] = reinterpret_cast<void*>(bases[i]);
+  c10::cuda::CUDAGuard g(out.device());
+  const int rc = b200_ep_combine(ptrs, rank, world, (size_t)slot_bytes, cpd, T, Tc, H, k, y_recv.data_ptr(),
+                                 ids_recv.data_ptr<int>(), send_idx.data_ptr<int>(), out.data_ptr(),
+                                 status.has_value() ? status->data_ptr<int>() : nullptr,
+                                 at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(rc == 0, "b200::ep_combine failed with code ", rc);
+}
 }  // namespace
 
 void register_comm_ops(torch::Library& m) {
@@ -78,9 +129,20 @@ void register_comm_ops(torch::Library& m) {
   m.def(
       "allreduce_fused(int[] bases, int rank, int slot_bytes, Tensor input, Tensor(a!) out, Tensor(b!)? residual, "
       "Tensor? bias, Tensor? w, float eps, int num_blocks, Tensor? status) -> ()");
+  m.def(
+      "ep_dispatch(int[] bases, int rank, int slot_bytes, int cpd, int Tc, int E_local, int t_begin, int t_end, "
+      "Tensor x, Tensor ids, Tensor w, Tensor(a!) x_recv, Tensor(b!) ids_recv, Tensor(c!) w_recv, "
+      "Tensor(d!) send_idx, Tensor? status) -> ()");
+  m.def(
+      "ep_combine(int[] bases, int rank, int slot_bytes, int cpd, int Tc, Tensor y_recv, Tensor ids_recv, "
+      "Tensor send_idx, Tensor(a!) out, Tensor? status) -> ()");
 }
 
-void register_comm_impls(torch::Library& m) { m.impl("allreduce_fused", &allreduce_fused); }
+void register_comm_impls(torch::Library& m) {
+  m.impl("allreduce_fused", &allreduce_fused);
+  m.impl("ep_dispatch", &ep_dispatch);
+  m.impl("ep_combine", &ep_combine);
+}
 
 void register_comm_cpu_impls(torch::Library& m) {
   m.impl("comm_alloc", &comm_alloc);

@@ -99,12 +99,27 @@ class Worker:
         MODEL_LOAD_TIME.labels(model_name=name).set(time.time() - t0)
         MODEL_LOAD_SIZE.labels(model_name=name).set(nbytes)
         vocab = getattr(mcfg, "vocab_size", None) or hf.get("vocab_size")
+        self._attach_all2all(model, mcfg)
         dcp = self.cfg.decode_context_parallel_size
         if dcp > 1:
             self._check_dcp(mcfg, hf, dcp)
         self.runner = ModelRunner(self.cfg, model, self.device, self.ps.tp, vocab,
                                   cp_group=self.ps.dcp_kv if dcp > 1 else None)
         logger.info("rank %d loaded model (%.2f GB) in %.1fs", self.rank, nbytes / 1e9, time.time() - t0)
+
+    def _attach_all2all(self, model, mcfg) -> None:
+        """One EP all-to-all object (over the world group) shared by every MoE layer that
+        supports it, when ``all2all_backend`` selects one and experts span several ranks."""
+        from ..parallel.all2all import make_ep_all2all
+
+        layers = [m for m in model.modules() if hasattr(m, "a2a") and hasattr(m, "experts")]
+        if not layers or self.cfg.all2all_backend == "allgather_reducescatter" or self.ps.world.world_size == 1:
+            return
+        a2a = make_ep_all2all(self.cfg.all2all_backend, self.ps.world, self.device, mcfg.hidden_size,
+                              mcfg.num_experts_per_tok, max_tokens=min(256, self.cfg.max_num_seqs))
+        for m in layers:
+            m.a2a = a2a
+        self.a2a = a2a
 
     def _check_dcp(self, mcfg, hf: dict, dcp: int) -> None:
         """DCP groups are runs of ``dcp`` consecutive TP ranks, which share a KV head under

@@ -17,6 +17,10 @@ def _engine_args(ap: argparse.ArgumentParser) -> None:
     ap.add_argument("--tensor-parallel-size", "-tp", type=int, default=1)
     ap.add_argument("--data-parallel-size", "-dp", type=int, default=1)
     ap.add_argument("--enable-expert-parallel", action="store_true")
+    ap.add_argument("--decode-context-parallel-size", "-dcp", type=int, default=1)
+    ap.add_argument("--all2all-backend", default="allgather_reducescatter",
+                    choices=["allgather_reducescatter", "naive", "neuron", "b200"],
+                    help="MoE token exchange under data parallelism (neuron / b200: fused NVLink all-to-all)")
     ap.add_argument("--max-model-len", type=int, default=8192)
     ap.add_argument("--max-num-seqs", type=int, default=64)
     ap.add_argument("--max-num-batched-tokens", type=int, default=4096)
@@ -46,7 +50,8 @@ def engine_kwargs(a) -> dict:
               load_format=a.load_format, dtype=a.dtype, seed=a.seed, speculative_config=a.speculative_config,
               kv_transfer_config=a.kv_transfer_config, additional_config=a.additional_config,
               served_model_name=a.served_model_name, enable_expert_parallel=a.enable_expert_parallel,
-              async_scheduling=a.async_scheduling)
+              async_scheduling=a.async_scheduling, decode_context_parallel_size=a.decode_context_parallel_size,
+              all2all_backend=a.all2all_backend)
     if a.hf_config is not None:
         kw["hf_config"] = a.hf_config
         kw["load_format"] = "dummy"

@@ -214,14 +214,28 @@ class GptOssMLP(nn.Module):
         super().__init__()
         self.cfg = cfg
         self.dp = ps.dp
+        self.tp = ps.tp
         ep_rank = ps.dp.rank_in_group * ps.tp.world_size + ps.tp.rank_in_group
         ep_size = ps.tp.world_size * ps.dp.world_size
         self.router_weight = _param((cfg.num_local_experts, cfg.hidden_size), dtype, device)
         self.router_bias = _param((cfg.num_local_experts,), dtype, device)
         self.experts = GptOssExperts(cfg, ep_rank, ep_size, dtype, device)
+        # EP all-to-all (``parallel/all2all.py``), attached by the worker when
+        # ``all2all_backend`` asks for one; None: all-gather / reduce-scatter over DP
+        self.a2a = None
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         """This rank's partial MoE output (its experts only); the caller reduces it."""
+        if self.a2a is not None:
+            # route the local tokens; each TP rank sends its slice to the expert owners
+            # and gets their outputs back (zeros outside the slice: a TP partial sum)
+            from ..parallel.all2all import ep_slice
+
+            T = x.shape[0]
+            ids, w = ops.router_topk(x, self.router_weight, self.router_bias, self.cfg.num_experts_per_tok)
+            t0, t1 = ep_slice(T, self.tp.rank_in_group, self.tp.world_size)
+            xr, ir, wr = self.a2a.dispatch(x, ids, w, self.experts.E_local, t0, t1)
+            return self.a2a.combine(self.experts(xr, ir, wr), T)
         if self.dp.world_size > 1:
             x = self.dp.all_gather(x, dim=0)
         ids, w = ops.router_topk(x, self.router_weight, self.router_bias, self.cfg.num_experts_per_tok)
