@@ -103,3 +103,114 @@ def test_fused_allreduce_two_gpus():
             if e > tol:
                 bad.append(f"rank {rank} {kind} err {e}")
     assert not bad, bad
+
+
+def _mock_experts(x, ids, w, E_local, offset):
+    """Stand-in expert layer: sum over this rank's routes of w * (expert id + 1) * x."""
+    local = (ids >= offset) & (ids < offset + E_local)
+    scale = torch.where(local, w * (ids.float() + 1), torch.zeros_like(w)).sum(-1, keepdim=True)
+    return torch.where(scale != 0, x.float() * scale, torch.zeros_like(scale)).bfloat16()
+
+
+def _a2a_worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        import torch.distributed as dist
+
+        from vllm_neuron_b200 import ops
+        from vllm_neuron_b200.parallel import state as ps
+        from vllm_neuron_b200.parallel.all2all import EpAll2All, FusedEpAll2All
+
+        torch.cuda.set_device(rank)
+        ps.init_distributed_environment(world, rank, backend="nccl", local_rank=rank, timeout_s=120)
+        st = ps.initialize_parallel_state(tp=world, backend="nccl", timeout_s=120)
+        dev = torch.device("cuda", rank)
+        H, k, E = 2880, 4, 16
+        E_local = E // world
+        fused = FusedEpAll2All(st.world, dev, H, k, max_tokens=256)
+        coll = EpAll2All(st.world, H, k)
+        errs = []
+
+        def case(T, t0, t1, seed):
+            torch.manual_seed(seed + rank)
+            x = torch.randn(T, H, device=dev).bfloat16()
+            ids = torch.stack([torch.randperm(E, device=dev)[:k] for _ in range(T)]).to(torch.int32) \
+                if T else torch.zeros(0, k, dtype=torch.int32, device=dev)
+            w = torch.rand(T, k, device=dev)
+            want = x.float() * (w * (ids.float() + 1)).sum(-1, keepdim=True)
+            want[:t0] = 0
+            want[t1:] = 0
+            outs = []
+            for a in (fused, coll):
+                xr, ir, wr = a.dispatch(x, ids, w, E_local, t0, t1)
+                yr = _mock_experts(xr, ir, wr, E_local, rank * E_local)
+                outs.append(a.combine(yr, T).float())
+            scale = want.abs().max().item() + 1e-6
+            errs.append(("fused", T, (outs[0] - want).abs().max().item() / scale))
+            errs.append(("coll", T, (outs[1] - want).abs().max().item() / scale))
+
+        # consecutive calls alternate the double-buffered slots; slices as under TP = 2
+        for i, (T, sl) in enumerate([(64, None), (1, None), (17, (0, 9)), (64, (32, 64)), (256, None), (5, None)]):
+            t0, t1 = sl if sl else (0, T)
+            case(T, t0, t1, 100 + 7 * i)
+        # CUDA graph: dispatch + experts + combine captured once, replayed with new tokens
+        T = 64
+        x = torch.zeros(T, H, device=dev, dtype=torch.bfloat16)
+        ids = torch.zeros(T, k, device=dev, dtype=torch.int32)
+        w = torch.zeros(T, k, device=dev)
+
+        def step():
+            xr, ir, wr = fused.dispatch(x, ids, w, E_local, 0, T)
+            return fused.combine(_mock_experts(xr, ir, wr, E_local, rank * E_local), T)
+
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            step()
+        torch.cuda.current_stream().wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = step()
+        for rep in range(3):
+            torch.manual_seed(500 + rep + rank)
+            x.copy_(torch.randn(T, H, device=dev).bfloat16())
+            ids.copy_(torch.stack([torch.randperm(E, device=dev)[:k] for _ in range(T)]).to(torch.int32))
+            w.copy_(torch.rand(T, k, device=dev))
+            graph.replay()
+            torch.cuda.synchronize()
+            want = x.float() * (w * (ids.float() + 1)).sum(-1, keepdim=True)
+            errs.append(("graph", T, (out.float() - want).abs().max().item() / (want.abs().max().item() + 1e-6)))
+        torch.cuda.synchronize()
+        st_code = int(ops.device_status(dev)[0].item())
+        del graph
+        fused.close()
+        ps.destroy_parallel_state()
+        dist.destroy_process_group()
+        q.put((rank, errs, st_code, None))
+    except Exception:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, [], -1, traceback.format_exc()))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fused_ep_all2all_two_gpus():
+    """Fused NVLink dispatch / combine against the math and against the collective
+    all-to-all, over consecutive calls (slot alternation), TP-style slices and a CUDA graph."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_a2a_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    bad = []
+    for rank, errs, code, tb in res:
+        assert tb is None, tb
+        assert code == 0, f"rank {rank} status {code}"
+        for kind, T, e in errs:
+            if e > 2e-2:  # bf16 expert outputs summed over two ranks
+                bad.append(f"rank {rank} {kind} T={T} rel err {e}")
+    assert not bad, bad
