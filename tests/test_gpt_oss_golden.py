@@ -76,7 +76,7 @@ def test_greedy_matches_hf(ckpt, tp, dp, a2a, monkeypatch):
     want = _hf_greedy(hf, prompts, n_new)
     llm = LLM(model=path, dtype="float32", max_model_len=512, max_num_seqs=16, max_num_batched_tokens=256,
               block_size=16, device="cpu", tensor_parallel_size=tp, data_parallel_size=dp,
-              all2all_backend=a2a or "allgather_reducescatter", spmd=not a2a,
+              all2all_backend=a2a or "allgather_reducescatter",
               additional_config={"neuron_config": {"quantization": "bf16"}})
     try:
         outs = llm.generate(prompt_token_ids=prompts,

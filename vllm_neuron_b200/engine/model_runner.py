@@ -74,7 +74,7 @@ class AsyncStep:
 
 class ModelRunner:
     def __init__(self, cfg: EngineConfig, model: torch.nn.Module, device: torch.device, tp_group,
-                 vocab_size: int, cp_group=None):
+                 vocab_size: int, cp_group=None, sampling_groups=None):
         self.cfg = cfg
         self.model = model
         self.device = device
@@ -96,7 +96,7 @@ class ModelRunner:
         self.max_top_k = ods.max_top_k if ods is not None else 256
         self.all_greedy_cfg = bool(ods and ods.all_greedy)
         lm = model.lm_head
-        self.sampler = Sampler(tp_group, lm.start, vocab_size, self.max_top_k)
+        self.sampler = Sampler(tp_group, lm.start, vocab_size, self.max_top_k, sampling_groups)
         self.use_graphs = (device.type == "cuda" and not cfg.enforce_eager and not envs.VLLM_B200_DISABLE_CUDA_GRAPHS)
         self.kv_caches: list[tuple[torch.Tensor, torch.Tensor]] = []
         self.num_blocks = 0

@@ -67,7 +67,7 @@ class Worker:
             embedding_dp_size=nc.embedding_dp_size, lm_head_dp_size=nc.lm_head_dp_size,
             mlp_dp_size=nc.mlp_dp_size, dcp=self.cfg.decode_context_parallel_size,
             vision_tp=self.cfg.vision_neuron_config.tp_size, vision_dp=self.cfg.vision_neuron_config.dp_size,
-            timeout_s=float(envs.VLLM_B200_BARRIER_TIMEOUT))
+            timeout_s=float(envs.VLLM_B200_BARRIER_TIMEOUT), sampling_dp=self._sampling_dp())
         if self.device.type == "cuda" and self.world_size > 1 and envs.VLLM_B200_FUSED_COLLECTIVES:
             from ..parallel.communicator import attach_communicators
 
@@ -103,9 +103,15 @@ class Worker:
         dcp = self.cfg.decode_context_parallel_size
         if dcp > 1:
             self._check_dcp(mcfg, hf, dcp)
+        sdp = self._sampling_dp()
         self.runner = ModelRunner(self.cfg, model, self.device, self.ps.tp, vocab,
-                                  cp_group=self.ps.dcp_kv if dcp > 1 else None)
+                                  cp_group=self.ps.dcp_kv if dcp > 1 else None,
+                                  sampling_groups=(self.ps.sampling_a2a, self.ps.sampling_gather) if sdp > 1 else None)
         logger.info("rank %d loaded model (%.2f GB) in %.1fs", self.rank, nbytes / 1e9, time.time() - t0)
+
+    def _sampling_dp(self) -> int:
+        ods = self.cfg.neuron_config.on_device_sampling_config
+        return ods.sampling_dp_degree if ods is not None else 1
 
     def _attach_all2all(self, model, mcfg) -> None:
         """One EP all-to-all object (over the world group) shared by every MoE layer that

@@ -20,12 +20,15 @@ from ..parallel.state import GroupCoordinator
 
 
 class Sampler(nn.Module):
-    def __init__(self, group: GroupCoordinator, vocab_start: int, vocab_size: int, max_top_k: int = 256):
+    def __init__(self, group: GroupCoordinator, vocab_start: int, vocab_size: int, max_top_k: int = 256,
+                 sampling_groups: tuple[GroupCoordinator, GroupCoordinator] | None = None):
         super().__init__()
         self.group = group
         self.vocab_start = vocab_start
         self.vocab_size = vocab_size
         self.max_top_k = max_top_k
+        # sampling DP: (all-to-all group of consecutive TP ranks, gather group across them)
+        self.sdp = sampling_groups if (sampling_groups and sampling_groups[0].world_size > 1) else None
 
     def _mask_padding(self, logits: torch.Tensor) -> torch.Tensor:
         # vocab padding rows (when V % tp != 0) must never win
@@ -63,6 +66,8 @@ class Sampler(nn.Module):
         selection over the full vocabulary is contained in this set."""
         if not masked:
             logits = self._mask_padding(logits)
+        if self.sdp is not None:
+            return self._candidates_sdp(logits)
         K = min(self.max_top_k, logits.shape[1])
         vals, ids = torch.topk(logits.float(), K, dim=-1)
         ids = ids + self.vocab_start
@@ -72,3 +77,30 @@ class Sampler(nn.Module):
         alli = self.group.all_gather(ids.unsqueeze(0), dim=0)
         B = logits.shape[0]
         return allv.permute(1, 0, 2).reshape(B, -1), alli.permute(1, 0, 2).reshape(B, -1).to(torch.int64)
+
+    def _candidates_sdp(self, logits: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """Sampling DP (``functional/topk.py:130``, ``sampling.py:106-161``): an all-to-all
+        inside each group of ``s`` consecutive TP ranks swaps batch for vocab, so a rank
+        holds B/s rows over the s vocab shards of its group; one top-K over that span; the
+        candidates are gathered over the ranks holding the other spans and then over the
+        row chunks.  The candidate set per row is (tp/s)*K instead of tp*K and contains the
+        same global top-K."""
+        a2a, gat = self.sdp
+        s = a2a.world_size
+        B, Vl = logits.shape
+        Bp = -(-B // s) * s
+        x = logits.float()
+        if Bp != B:
+            x = torch.cat([x, torch.full((Bp - B, Vl), float("-inf"), device=x.device)], 0)
+        span = a2a.all_to_all(x, scatter_dim=0, gather_dim=1)  # [Bp/s, s*Vl]
+        K = min(self.max_top_k, span.shape[1])
+        vals, ids = torch.topk(span, K, dim=-1)
+        ids = ids + (self.vocab_start - a2a.rank_in_group * Vl)  # first vocab id of the group's span
+        allv = gat.all_gather(vals.unsqueeze(0), dim=0)  # [tp/s, Bp/s, K]
+        alli = gat.all_gather(ids.unsqueeze(0), dim=0)
+        rows = Bp // s
+        cv = allv.permute(1, 0, 2).reshape(rows, -1)
+        ci = alli.permute(1, 0, 2).reshape(rows, -1)
+        cv = a2a.all_gather(cv, dim=0)[:B]  # row chunks back in order
+        ci = a2a.all_gather(ci, dim=0)[:B]
+        return cv, ci.to(torch.int64)

@@ -222,10 +222,12 @@ class GroupCoordinator:
         ``gather_dim`` (``functional/collectives/all_to_all.py:12``)."""
         if self.world_size == 1:
             return x
-        chunks = [c.contiguous() for c in torch.chunk(x, self.world_size, dim=scatter_dim)]
-        outs = [torch.empty_like(chunks[0]) for _ in range(self.world_size)]
-        dist.all_to_all(outs, chunks, group=self.device_group)
-        return torch.cat(outs, dim=gather_dim)
+        if x.shape[scatter_dim] % self.world_size:
+            raise ValueError(f"all_to_all dim {x.shape[scatter_dim]} not divisible by {self.world_size}")
+        send = torch.stack(torch.chunk(x, self.world_size, dim=scatter_dim)).contiguous()
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=self.device_group)
+        return torch.cat(list(recv.unbind(0)), dim=gather_dim)
 
     def all_to_all_v(self, x: torch.Tensor, send_counts: list[int], recv_counts: list[int]) -> torch.Tensor:
         if self.world_size == 1:
@@ -295,6 +297,11 @@ class ParallelState:
     vision_tp: GroupCoordinator
     vision_dp: GroupCoordinator
     degrees: dict = field(default_factory=dict)
+    # sampling DP within each TP group: all-to-all groups of ``sampling_dp`` consecutive
+    # ranks (batch <-> vocab) and gather groups across them (``neuron_parallel_state.py:
+    # 170-187,464-492``)
+    sampling_a2a: GroupCoordinator | None = None
+    sampling_gather: GroupCoordinator | None = None
 
 
 _STATE: ParallelState | None = None
@@ -352,7 +359,8 @@ def init_distributed_environment(world_size: int = 1, rank: int = 0, backend: st
 def initialize_parallel_state(tp: int = 1, dp: int = 1, ep_degree: int = 1, attention_dp_size: int = 1,
                               embedding_dp_size: int = 1, lm_head_dp_size: int = 1, mlp_dp_size: int = 1,
                               dcp: int = 1, vision_tp: int | None = None, vision_dp: int | None = None,
-                              backend: str | None = None, timeout_s: float = 1800.0) -> ParallelState:
+                              backend: str | None = None, timeout_s: float = 1800.0,
+                              sampling_dp: int = 1) -> ParallelState:
     """Build every group (``initialize_neuron_parallel_state``, ``neuron_parallel_state.py:863``)."""
     global _STATE
     from .. import envs
@@ -375,10 +383,11 @@ def initialize_parallel_state(tp: int = 1, dp: int = 1, ep_degree: int = 1, atte
 
     degrees = dict(world=world_size, tp=tp, dp=dp, ep=ep_degree, attention_dp=attention_dp_size,
                    embedding_dp=embedding_dp_size, lm_head_dp=lm_head_dp_size, mlp_dp=mlp_dp_size,
-                   dcp=dcp, vision_tp=vtp, vision_dp=vdp)
+                   dcp=dcp, vision_tp=vtp, vision_dp=vdp, sampling_dp=sampling_dp)
     if world_size == 1:
         g = {k: _single(k) for k in ("world", "tp", "dp", "ep", "ep_tp", "moe", "attn_tp", "attn_dp", "dcp_kv",
-                                     "dcp_head", "embedding", "lm_head", "mlp", "vision_tp", "vision_dp")}
+                                     "dcp_head", "embedding", "lm_head", "mlp", "vision_tp", "vision_dp",
+                                     "sampling_a2a", "sampling_gather")}
         _STATE = ParallelState(**g, degrees=degrees)
         return _STATE
 
@@ -406,13 +415,19 @@ def initialize_parallel_state(tp: int = 1, dp: int = 1, ep_degree: int = 1, atte
     vtp_rows, vdp_cols = build_2d_mesh(list(range(world_size)), vtp, vdp)
     vtp_g = _new_groups("vision_tp", vtp_rows, rank, backend, to)
     vdp_g = _new_groups("vision_dp", vdp_cols, rank, backend, to)
+    s_rows, s_cols = build_sampling_dp_meshes(tp, sampling_dp)
+    bases = range(0, world_size, tp)
+    sa2a_g = _new_groups("sampling_a2a", [[b + r for r in row] for b in bases for row in s_rows], rank, backend, to)
+    sgat_g = _new_groups("sampling_gather", [[b + r for r in col] for b in bases for col in s_cols], rank, backend,
+                         to)
     # With EP the MoE output is completed by an all-reduce over every rank that
     # holds a slice of the experts for these tokens: the whole world when the
     # tokens are replicated across DP (wide EP), else the TP group.
     moe_g = world_g if ep_degree > 1 else mlp_g
     _STATE = ParallelState(world=world_g, tp=tp_g, dp=dp_g, ep=ep_g, ep_tp=eptp_g, moe=moe_g, attn_tp=attn_tp_g,
                            attn_dp=attn_dp_g, dcp_kv=dcp_kv_g, dcp_head=dcp_head_g, embedding=emb_g,
-                           lm_head=lmh_g, mlp=mlp_g, vision_tp=vtp_g, vision_dp=vdp_g, degrees=degrees)
+                           lm_head=lmh_g, mlp=mlp_g, vision_tp=vtp_g, vision_dp=vdp_g, degrees=degrees,
+                           sampling_a2a=sa2a_g, sampling_gather=sgat_g)
     logger.info("parallel state: %s", degrees)
     return _STATE
 
