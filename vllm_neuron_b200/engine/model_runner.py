@@ -96,7 +96,13 @@ class ModelRunner:
         self.max_top_k = ods.max_top_k if ods is not None else 256
         self.all_greedy_cfg = bool(ods and ods.all_greedy)
         lm = model.lm_head
-        self.sampler = Sampler(tp_group, lm.start, vocab_size, self.max_top_k, sampling_groups)
+        self.tp_group = tp_group
+        # lm_head DP: the head is sharded over a TP x DP supergroup and the rows to sample
+        # are gathered over its DP ranks (``_sample_lm_dp``); the sampler reduces over the
+        # supergroup
+        self.lm_dp = getattr(lm, "dp_group", None)
+        self.sampler = Sampler(lm.group if self.lm_dp is not None else tp_group, lm.start, vocab_size,
+                               self.max_top_k, sampling_groups)
         self.use_graphs = (device.type == "cuda" and not cfg.enforce_eager and not envs.VLLM_B200_DISABLE_CUDA_GRAPHS)
         self.kv_caches: list[tuple[torch.Tensor, torch.Tensor]] = []
         self.num_blocks = 0
@@ -475,18 +481,20 @@ class ModelRunner:
 
     # ------------------------------------------------------------------ forward
     def _sp_ok(self, meta: AttentionMetadata, T: int) -> bool:
-        g = self.sampler.group
+        g = self.tp_group
         return (not meta.is_decode and g.world_size > 1 and T > g.world_size and T % g.world_size == 0
                 and envs.VLLM_B200_SEQUENCE_PARALLEL and not getattr(self.model, "aux_hidden_layers", ())
                 and "mm_index" not in meta.extras)
 
     def _forward_sample(self, meta: AttentionMetadata, T: int, n_sel: int, greedy: bool) -> torch.Tensor:
-        g = self.sampler.group
+        g = self.tp_group
         g.sp_active = self._sp_ok(meta, T)
         try:
             h = self.model(self.d_ids[:T], self.d_pos[:T], meta, self.kv_caches)
         finally:
             g.sp_active = False
+        if self.lm_dp is not None:
+            return self._sample_lm_dp(h, meta, T, n_sel)
         if n_sel == 0:  # data-parallel padding step: nothing to sample
             return self.d_out[:0]
         hs = h if (meta.is_decode and n_sel == T) else h.index_select(0, meta.logits_indices)
@@ -504,6 +512,25 @@ class ModelRunner:
             tok, _ = rejection_sample(cv, ci, pp[3].long(), pp[0], pp[1].int(), pp[2], pp[4], pp[5], self.max_top_k)
         self.d_out[:n_sel].copy_(tok)
         self._last_logits = logits
+        return self.d_out[:n_sel]
+
+    def _sample_lm_dp(self, h: torch.Tensor, meta: AttentionMetadata, T: int, n_sel: int) -> torch.Tensor:
+        """lm_head DP (``model_mxfp4.py:1928-2001``): every DP replica of the supergroup pads
+        its rows to R (the decode batch, equal across replicas in lockstep; max_num_seqs for
+        prefill), the rows and their sampling parameters are gathered, the supergroup computes
+        the vocab-sharded logits and samples all of them (rows with temperature <= 0 greedily),
+        and each replica keeps its own tokens.  Runs on padding-only steps too, since the
+        collectives must match."""
+        dpg = self.lm_dp
+        R = n_sel if meta.is_decode else self.cfg.max_num_seqs
+        hs = h if (meta.is_decode and n_sel == T) else h.index_select(0, meta.logits_indices)
+        if hs.shape[0] < R:
+            hs = torch.cat([hs, hs.new_zeros(R - hs.shape[0], hs.shape[1])])
+        logits = self.model.compute_logits(dpg.all_gather(hs, dim=0))
+        prm = [dpg.all_gather(t[:R], dim=0) for t in (self.d_temp, self.d_topk, self.d_topp, self.d_unif)]
+        tok = self.sampler(logits, *prm, False)
+        j = dpg.rank_in_group
+        self.d_out[:n_sel].copy_(tok[j * R:j * R + n_sel])
         return self.d_out[:n_sel]
 
     @torch.inference_mode()
@@ -576,6 +603,8 @@ class ModelRunner:
         shards gathered); used by the accuracy tools."""
         meta, T, _, _ = self._prepare(so, None)
         h = self.model(self.d_ids[:T], self.d_pos[:T], meta, self.kv_caches)
+        if self.lm_dp is not None:
+            raise NotImplementedError("score() with lm_head data parallelism")
         logits = self.model.compute_logits(h).float()
         g = self.sampler.group
         if g.world_size > 1:

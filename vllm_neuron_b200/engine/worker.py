@@ -99,6 +99,9 @@ class Worker:
         MODEL_LOAD_TIME.labels(model_name=name).set(time.time() - t0)
         MODEL_LOAD_SIZE.labels(model_name=name).set(nbytes)
         vocab = getattr(mcfg, "vocab_size", None) or hf.get("vocab_size")
+        nc = self.cfg.neuron_config
+        if max(nc.embedding_dp_size, nc.lm_head_dp_size, nc.mlp_dp_size) > 1 and self.cfg.speculative_config:
+            raise ValueError("component data parallelism with speculative decoding is not supported")
         self._attach_all2all(model, mcfg)
         dcp = self.cfg.decode_context_parallel_size
         if dcp > 1:

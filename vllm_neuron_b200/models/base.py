@@ -32,6 +32,13 @@ class KVSpec:
         return tot
 
 
+def component(ps, name: str) -> dict:
+    """Constructor kwargs ``group`` / ``dp_group`` of an embedding or LM head under
+    component DP (the TP group and no DP gather unless the component's DP degree is > 1)."""
+    g, dp_g = ps.component(name)
+    return {"group": g, "dp_group": dp_g}
+
+
 def kv_head_sharding(num_kv_heads: int, tp: int, tp_rank: int) -> tuple[int, int]:
     """(first kv head, number of kv heads) held by ``tp_rank``.  When TP exceeds
     the KV head count, KV heads are replicated (``model_mxfp4.py:306-313``)."""

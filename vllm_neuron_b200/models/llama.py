@@ -26,7 +26,7 @@ from .. import ops
 from ..nn.linear import ParallelLMHead, RMSNorm, VocabParallelEmbedding, shard_range
 from ..ops import reference as ref
 from ..parallel.state import GroupCoordinator, ParallelState
-from .base import KVSpec, LayerSpec, kv_head_sharding
+from .base import KVSpec, LayerSpec, component, kv_head_sharding
 
 
 @dataclass
@@ -151,10 +151,17 @@ class DenseAttention(nn.Module):
 
 
 class DenseMLP(nn.Module):
-    def __init__(self, cfg: LlamaConfig, tp: GroupCoordinator, dtype, device, intermediate: int | None = None):
+    """Gate/up column-parallel, down row-parallel; returns the partial sum over ``tp``.  With
+    MLP DP (``dp_group``) ``tp`` is a TP x DP supergroup: the rows of the supergroup's DP
+    replicas are gathered, run through the supergroup's shards, and reduce-scattered back,
+    leaving each replica a partial sum over its own TP group."""
+
+    def __init__(self, cfg: LlamaConfig, tp: GroupCoordinator, dtype, device, intermediate: int | None = None,
+                 dp_group: GroupCoordinator | None = None):
         super().__init__()
         I = intermediate or cfg.intermediate_size
         self.tp = tp
+        self.dp_group = dp_group
         self.I_local = I // tp.world_size
         fp8 = cfg.quantization == "fp8"
         self.gate_up = Linear(2 * self.I_local, cfg.hidden_size, cfg.mlp_bias, dtype, device, fp8)
@@ -179,6 +186,9 @@ class DenseMLP(nn.Module):
         tgt.data[off:off + self.I_local].copy_(full[s:e].to(tgt.dtype))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.dp_group is not None:
+            xa = self.dp_group.all_gather(x, dim=0)
+            return self.dp_group.reduce_scatter(self.down(ops.silu_and_mul(self.gate_up(xa)), with_bias=False), dim=0)
         return self.down(ops.silu_and_mul(self.gate_up(x)), with_bias=False)  # partial sum
 
 
@@ -190,7 +200,8 @@ class DenseDecoderLayer(nn.Module):
         self.input_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, device=device)
         self.self_attn = DenseAttention(cfg, i, ps.tp, dtype, device, sliding_window)
         self.post_attention_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, device=device)
-        self.mlp = DenseMLP(cfg, ps.tp, dtype, device)
+        mlp_g, mlp_dp = ps.component("mlp")
+        self.mlp = DenseMLP(cfg, mlp_g, dtype, device, dp_group=mlp_dp)
 
     def forward(self, positions, h, residual, meta, kv, cos_sin, in_bias=None):
         """``h``: the embedding (layer 0) or the previous layer's MLP partial sum, whose
@@ -216,11 +227,13 @@ class LlamaForCausalLM(nn.Module):
         self.ps = ps
         self.dtype = dtype
         self.kv_dtype = kv_dtype or dtype
-        self.embed_tokens = VocabParallelEmbedding(cfg.vocab_size, cfg.hidden_size, ps.tp, dtype, device)
+        self.embed_tokens = VocabParallelEmbedding(cfg.vocab_size, cfg.hidden_size, dtype=dtype, device=device,
+                                                   **component(ps, "embedding"))
         self.layers = nn.ModuleList([DenseDecoderLayer(cfg, i, ps, dtype, device)
                                      for i in range(cfg.num_hidden_layers)])
         self.norm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, device=device)
-        self.lm_head = ParallelLMHead(cfg.vocab_size, cfg.hidden_size, ps.tp, dtype, device)
+        self.lm_head = ParallelLMHead(cfg.vocab_size, cfg.hidden_size, dtype=dtype, device=device,
+                                      **component(ps, "lm_head"))
         inv, af = cfg.inv_freq()
         self.register_buffer("cos_sin", ops.build_cos_sin_cache(inv, min(cfg.max_position_embeddings, 1 << 17), af,
                                                                 device=device), persistent=False)

@@ -38,7 +38,7 @@ from .. import ops
 from ..nn.linear import ParallelLMHead, RMSNorm, VocabParallelEmbedding, shard_range
 from ..ops import reference as ref
 from ..parallel.state import GroupCoordinator, ParallelState
-from .base import KVSpec, LayerSpec, kv_head_sharding
+from .base import KVSpec, LayerSpec, component, kv_head_sharding
 from .llama import DenseMLP, Linear
 
 
@@ -357,11 +357,13 @@ class Qwen3NextForCausalLM(nn.Module):
         self.ps = ps
         self.dtype = dtype
         self.kv_dtype = kv_dtype or dtype
-        self.embed_tokens = VocabParallelEmbedding(cfg.vocab_size, cfg.hidden_size, ps.tp, dtype, device)
+        self.embed_tokens = VocabParallelEmbedding(cfg.vocab_size, cfg.hidden_size, dtype=dtype, device=device,
+                                                   **component(ps, "embedding"))
         self.layers = nn.ModuleList([Qwen3NextDecoderLayer(cfg, i, ps, dtype, device)
                                      for i in range(cfg.num_hidden_layers)])
         self.norm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, device=device)
-        self.lm_head = ParallelLMHead(cfg.vocab_size, cfg.hidden_size, ps.tp, dtype, device)
+        self.lm_head = ParallelLMHead(cfg.vocab_size, cfg.hidden_size, dtype=dtype, device=device,
+                                      **component(ps, "lm_head"))
         inv, af = ref.yarn_inv_freq(cfg.rotary_dim, cfg.rope_theta)
         self.register_buffer("cos_sin", ops.build_cos_sin_cache(inv, min(cfg.max_position_embeddings, 1 << 17), af,
                                                                 device=device), persistent=False)

@@ -96,9 +96,16 @@ class RowParallelLinear(nn.Module):
 
 
 class VocabParallelEmbedding(nn.Module):
-    def __init__(self, vocab: int, hidden: int, group: GroupCoordinator, dtype=torch.bfloat16, device=None):
+    """Vocab-sharded embedding.  With embedding DP (``dp_group``) the table is sharded over a
+    TP x DP supergroup (``group``): the token ids of the supergroup's DP replicas are gathered,
+    looked up, reduced over the supergroup, and each replica keeps its own rows
+    (``model_mxfp4.py:1718-1733``).  Every replica must bring the same token count."""
+
+    def __init__(self, vocab: int, hidden: int, group: GroupCoordinator, dtype=torch.bfloat16, device=None,
+                 dp_group: GroupCoordinator | None = None):
         super().__init__()
         self.group = group
+        self.dp_group = dp_group
         self.vocab = vocab
         self.vocab_padded = ((vocab + group.world_size - 1) // group.world_size) * group.world_size
         self.per = self.vocab_padded // group.world_size
@@ -114,6 +121,10 @@ class VocabParallelEmbedding(nn.Module):
             param.data[: e - s].copy_(full[s:e].to(param.dtype))
 
     def forward(self, ids: torch.Tensor, sequence_parallel: bool = False) -> torch.Tensor:
+        if self.dp_group is not None:
+            T = ids.shape[0]
+            y = self.group.all_reduce(ops.embedding(self.dp_group.all_gather(ids, dim=0), self.weight, self.start))
+            return y[self.dp_group.rank_in_group * T:(self.dp_group.rank_in_group + 1) * T]
         if self.group.world_size == 1:
             return ops.embedding(ids, self.weight, 0)
         y = ops.embedding(ids, self.weight, self.start)
@@ -127,9 +138,13 @@ class ParallelLMHead(nn.Module):
     sampler works on the shards (distributed top-k / argmax) so the full logits
     are only gathered when requested (``nn/cpl.py:141``)."""
 
-    def __init__(self, vocab: int, hidden: int, group: GroupCoordinator, dtype=torch.bfloat16, device=None):
+    def __init__(self, vocab: int, hidden: int, group: GroupCoordinator, dtype=torch.bfloat16, device=None,
+                 dp_group: GroupCoordinator | None = None):
         super().__init__()
         self.group = group
+        # lm_head DP: ``group`` is a TP x DP supergroup; the runner gathers the rows to sample
+        # over ``dp_group`` and keeps its own tokens (``model_mxfp4.py:1928-2001``)
+        self.dp_group = dp_group
         self.vocab = vocab
         self.vocab_padded = ((vocab + group.world_size - 1) // group.world_size) * group.world_size
         self.per = self.vocab_padded // group.world_size

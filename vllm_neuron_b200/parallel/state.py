@@ -83,6 +83,17 @@ def build_component_tp_group_ranks(world_size: int, tp: int, dp_component: int) 
     return out
 
 
+def build_component_dp_group_ranks(world_size: int, tp: int, dp_component: int) -> list[list[int]]:
+    """Inside every component supergroup, the ranks at the same TP position (one per DP
+    replica of the supergroup): the group over which a component-DP module gathers its
+    input rows (``model_mxfp4.py:1484-1501`` transitions between these states)."""
+    out = []
+    for sg in build_component_tp_group_ranks(world_size, tp, dp_component):
+        for t in range(tp):
+            out.append([sg[d * tp + t] for d in range(dp_component)])
+    return out
+
+
 def build_dp_column_group_ranks(world_size: int, tp: int, attention_dp: int) -> list[list[int]]:
     """Attention-DP columns: same TP position across ``attention_dp`` consecutive DP replicas."""
     dp = world_size // tp
@@ -302,6 +313,18 @@ class ParallelState:
     # 170-187,464-492``)
     sampling_a2a: GroupCoordinator | None = None
     sampling_gather: GroupCoordinator | None = None
+    # component DP: the DP ranks of an embedding / lm_head / mlp supergroup
+    embedding_dp: GroupCoordinator | None = None
+    lm_head_dp: GroupCoordinator | None = None
+    mlp_dp: GroupCoordinator | None = None
+
+    def component(self, name: str) -> tuple[GroupCoordinator, GroupCoordinator | None]:
+        """(sharding group, DP gather group or None) of the "embedding", "lm_head" or "mlp"
+        component: the TP group unless its component-DP degree is above 1."""
+        dp_g = getattr(self, name + "_dp")
+        if dp_g is None or dp_g.world_size == 1:
+            return self.tp, None
+        return getattr(self, name), dp_g
 
 
 _STATE: ParallelState | None = None
@@ -387,7 +410,7 @@ def initialize_parallel_state(tp: int = 1, dp: int = 1, ep_degree: int = 1, atte
     if world_size == 1:
         g = {k: _single(k) for k in ("world", "tp", "dp", "ep", "ep_tp", "moe", "attn_tp", "attn_dp", "dcp_kv",
                                      "dcp_head", "embedding", "lm_head", "mlp", "vision_tp", "vision_dp",
-                                     "sampling_a2a", "sampling_gather")}
+                                     "sampling_a2a", "sampling_gather", "embedding_dp", "lm_head_dp", "mlp_dp")}
         _STATE = ParallelState(**g, degrees=degrees)
         return _STATE
 
@@ -409,6 +432,12 @@ def initialize_parallel_state(tp: int = 1, dp: int = 1, ep_degree: int = 1, atte
     lmh_g = _new_groups("lm_head", build_component_tp_group_ranks(world_size, tp, lm_head_dp_size), rank,
                         backend, to)
     mlp_g = _new_groups("mlp", build_component_tp_group_ranks(world_size, tp, mlp_dp_size), rank, backend, to)
+    emb_dp_g = _new_groups("embedding_dp", build_component_dp_group_ranks(world_size, tp, embedding_dp_size), rank,
+                           backend, to)
+    lmh_dp_g = _new_groups("lm_head_dp", build_component_dp_group_ranks(world_size, tp, lm_head_dp_size), rank,
+                           backend, to)
+    mlp_dp_g = _new_groups("mlp_dp", build_component_dp_group_ranks(world_size, tp, mlp_dp_size), rank, backend,
+                           to)
     kv_rows, head_rows = build_dcp_group_ranks(world_size, tp, dcp)
     dcp_kv_g = _new_groups("dcp_kv", kv_rows, rank, backend, to)
     dcp_head_g = _new_groups("dcp_head", head_rows, rank, backend, to)
@@ -427,7 +456,8 @@ def initialize_parallel_state(tp: int = 1, dp: int = 1, ep_degree: int = 1, atte
     _STATE = ParallelState(world=world_g, tp=tp_g, dp=dp_g, ep=ep_g, ep_tp=eptp_g, moe=moe_g, attn_tp=attn_tp_g,
                            attn_dp=attn_dp_g, dcp_kv=dcp_kv_g, dcp_head=dcp_head_g, embedding=emb_g,
                            lm_head=lmh_g, mlp=mlp_g, vision_tp=vtp_g, vision_dp=vdp_g, degrees=degrees,
-                           sampling_a2a=sa2a_g, sampling_gather=sgat_g)
+                           sampling_a2a=sa2a_g, sampling_gather=sgat_g, embedding_dp=emb_dp_g,
+                           lm_head_dp=lmh_dp_g, mlp_dp=mlp_dp_g)
     logger.info("parallel state: %s", degrees)
     return _STATE
 
