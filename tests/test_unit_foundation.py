@@ -85,3 +85,22 @@ def test_single_rank_parallel_state():
     st = ps.initialize_parallel_state()
     assert st.tp.world_size == 1 and st.tp.all_reduce is not None
     ps.destroy_parallel_state()
+
+
+def test_attention_backend_spec():
+    from vllm_neuron_b200.ops.metadata import AttentionMetadata, B200AttentionBackend as B
+    from vllm_neuron_b200.platform import B200Platform
+
+    assert B.get_kv_cache_shape(10, 32, 8, 64) == (2, 10, 8, 32, 64)  # K/V x HND
+    assert B.get_metadata_cls() is AttentionMetadata
+    B.validate(32, 128)
+    with pytest.raises(ValueError):
+        B.validate(24, 64)
+    with pytest.raises(ValueError):
+        B.validate(32, 96)
+    assert B200Platform.get_attn_backend_cls() == "vllm_neuron_b200.ops.metadata.B200AttentionBackend"
+
+
+def test_component_dp_group_math():
+    assert ps.build_component_dp_group_ranks(8, 2, 2) == [[0, 2], [1, 3], [4, 6], [5, 7]]
+    assert ps.build_component_dp_group_ranks(4, 1, 4) == [[0, 1, 2, 3]]

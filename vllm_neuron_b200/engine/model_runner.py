@@ -31,7 +31,7 @@ from ..config import EngineConfig
 from ..logging_config import init_logger
 from ..metrics import GRAPH_REPLAY_COUNT, NUM_SEQS_PADDING
 from ..nn.sampler import Sampler
-from ..ops.metadata import AttentionMetadata
+from ..ops.metadata import AttentionMetadata, B200AttentionBackend
 from ..utils.bucket_utils import get_bucket_for_count, get_default_num_seqs_buckets, validate_buckets
 from .scheduler import SchedulerOutput
 
@@ -229,7 +229,7 @@ class ModelRunner:
             if l.kind != "attention":
                 self.kv_caches.append(self.state_caches[len(self.kv_caches)] if self.state_caches else None)
                 continue
-            shape = (num_blocks, l.num_kv_heads, self.bs, l.head_dim)
+            shape = B200AttentionBackend.get_kv_cache_shape(num_blocks, self.bs, l.num_kv_heads, l.head_dim)[1:]
             self.kv_caches.append((torch.zeros(shape, dtype=l.dtype, device=self.device),
                                    torch.zeros(shape, dtype=l.dtype, device=self.device)))
         self.num_blocks = num_blocks

@@ -37,3 +37,38 @@ class AttentionMetadata:
     # decode context parallelism: the DCP group (ranks that hold the same KV heads and
     # split the tokens of every sequence block by block); None without DCP
     cp_group: object = None
+
+
+class B200AttentionBackend:
+    """Stateless description of the paged-attention backend (the reference's
+    ``NeuronAttentionBackend``, ``vllm/attention/attn.py:7``): one K and one V cache per
+    attention layer in the HND layout ``[num_blocks, kv_heads, block_size, head_size]``
+    (the reference stacks them as ``(2, ...)``, ``attn.py:27-35``), read by
+    ``csrc/attention.cu`` through block tables.  Block sizes are powers of two (the kernels
+    address blocks with shifts); head sizes are the ones the kernels are built for."""
+
+    name = "B200_PAGED"
+    supported_head_sizes = (64, 128, 256)
+
+    @staticmethod
+    def get_name() -> str:
+        return B200AttentionBackend.name
+
+    @staticmethod
+    def get_metadata_cls() -> type:
+        return AttentionMetadata
+
+    @staticmethod
+    def get_kv_cache_shape(num_blocks: int, block_size: int, num_kv_heads: int, head_size: int) -> tuple:
+        return (2, num_blocks, num_kv_heads, block_size, head_size)
+
+    @staticmethod
+    def get_supported_head_sizes() -> tuple:
+        return B200AttentionBackend.supported_head_sizes
+
+    @staticmethod
+    def validate(block_size: int, head_size: int) -> None:
+        if block_size <= 0 or block_size & (block_size - 1):
+            raise ValueError(f"block_size must be a power of two, got {block_size}")
+        if head_size not in B200AttentionBackend.supported_head_sizes:
+            raise ValueError(f"head size {head_size} not in {B200AttentionBackend.supported_head_sizes}")

@@ -34,6 +34,10 @@ def _make_platform():
         default_block_size = 32
 
         @classmethod
+        def get_attn_backend_cls(cls, *args, **kwargs) -> str:  # ``platform.py:663`` of the reference
+            return "vllm_neuron_b200.ops.metadata.B200AttentionBackend"
+
+        @classmethod
         def check_and_update_config(cls, vllm_config) -> None:
             from .config import NeuronConfig
 
