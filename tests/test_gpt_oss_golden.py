@@ -51,14 +51,16 @@ def _hf_greedy(m, prompts, n_new):
     return outs
 
 
-@pytest.mark.parametrize("tp,dp,a2a", [(1, 1, None), (2, 1, None), (1, 2, None), (1, 2, "naive"),
-                                       (2, 1, "naive")])
-def test_greedy_matches_hf(ckpt, tp, dp, a2a, monkeypatch):
+@pytest.mark.parametrize("tp,dp,a2a,adp", [(1, 1, None, 1), (2, 1, None, 1), (1, 2, None, 1), (1, 2, "naive", 1),
+                                           (2, 1, "naive", 1), (1, 2, None, 2), (2, 2, None, 2)])
+def test_greedy_matches_hf(ckpt, tp, dp, a2a, adp, monkeypatch):
     """dp=2: two data-parallel replicas in lockstep with the experts shared across them
     (tokens all-gathered / reduce-scattered over DP around the MoE); 5 prompts so one
     replica runs padding steps while the other still works.  a2a: the EP all-to-all
     (each token sent only to the ranks owning its experts; under TP each rank sends a
-    slice and the outputs are partial sums)."""
+    slice and the outputs are partial sums).  adp: attention DP (the model runs on every
+    replica's tokens over the TP x DP supergroup; attention per replica after a batch <-> heads
+    all-to-all)."""
     from vllm_neuron_b200 import LLM, SamplingParams
     from vllm_neuron_b200.parallel import all2all
 
@@ -70,6 +72,16 @@ def test_greedy_matches_hf(ckpt, tp, dp, a2a, monkeypatch):
         return orig(self, *a, **k)
 
     monkeypatch.setattr(all2all.EpAll2All, "dispatch", spy)
+    from vllm_neuron_b200.parallel import state as pstate
+
+    a2a_calls = {"n": 0}
+    orig_a2a = pstate.GroupCoordinator.all_to_all
+
+    def spy_a2a(self, *a, **k):
+        a2a_calls["n"] += 1
+        return orig_a2a(self, *a, **k)
+
+    monkeypatch.setattr(pstate.GroupCoordinator, "all_to_all", spy_a2a)
     path, hf = ckpt
     prompts = workload(n=4 if tp == 2 else (5 if dp == 2 else 6))
     n_new = 16
@@ -77,7 +89,7 @@ def test_greedy_matches_hf(ckpt, tp, dp, a2a, monkeypatch):
     llm = LLM(model=path, dtype="float32", max_model_len=512, max_num_seqs=16, max_num_batched_tokens=256,
               block_size=16, device="cpu", tensor_parallel_size=tp, data_parallel_size=dp,
               all2all_backend=a2a or "allgather_reducescatter",
-              additional_config={"neuron_config": {"quantization": "bf16"}})
+              additional_config={"neuron_config": {"quantization": "bf16", "attention_dp_size": adp}})
     try:
         outs = llm.generate(prompt_token_ids=prompts,
                             sampling_params=SamplingParams(temperature=0, max_tokens=n_new, ignore_eos=True))
@@ -86,3 +98,4 @@ def test_greedy_matches_hf(ckpt, tp, dp, a2a, monkeypatch):
     got = [o.outputs[0].token_ids for o in outs]
     assert got == want
     assert (calls["n"] > 0) == bool(a2a)
+    assert (a2a_calls["n"] > 0) == (adp > 1)  # batch <-> heads exchange around attention

@@ -17,6 +17,7 @@ Counterpart of the Trainium plugin's ``NeuronModelRunner``
 
 from __future__ import annotations
 
+import dataclasses
 import hashlib
 import math
 import struct
@@ -101,6 +102,9 @@ class ModelRunner:
         # are gathered over its DP ranks (``_sample_lm_dp``); the sampler reduces over the
         # supergroup
         self.lm_dp = getattr(lm, "dp_group", None)
+        # attention DP: the model runs on the tokens of every replica of its supergroup
+        # (gathered here), attention per replica inside the model
+        self.adp = getattr(model, "attention_dp", None)
         self.sampler = Sampler(lm.group if self.lm_dp is not None else tp_group, lm.start, vocab_size,
                                self.max_top_k, sampling_groups)
         self.use_graphs = (device.type == "cuda" and not cfg.enforce_eager and not envs.VLLM_B200_DISABLE_CUDA_GRAPHS)
@@ -482,7 +486,7 @@ class ModelRunner:
     # ------------------------------------------------------------------ forward
     def _sp_ok(self, meta: AttentionMetadata, T: int) -> bool:
         g = self.tp_group
-        return (not meta.is_decode and g.world_size > 1 and T > g.world_size and T % g.world_size == 0
+        return (not meta.is_decode and g.world_size > 1 and self.adp is None and T > g.world_size and T % g.world_size == 0
                 and envs.VLLM_B200_SEQUENCE_PARALLEL and not getattr(self.model, "aux_hidden_layers", ())
                 and "mm_index" not in meta.extras)
 
@@ -490,7 +494,10 @@ class ModelRunner:
         g = self.tp_group
         g.sp_active = self._sp_ok(meta, T)
         try:
-            h = self.model(self.d_ids[:T], self.d_pos[:T], meta, self.kv_caches)
+            if self.adp is not None:
+                h = self._forward_attention_dp(meta, T)
+            else:
+                h = self.model(self.d_ids[:T], self.d_pos[:T], meta, self.kv_caches)
         finally:
             g.sp_active = False
         if self.lm_dp is not None:
@@ -513,6 +520,19 @@ class ModelRunner:
         self.d_out[:n_sel].copy_(tok)
         self._last_logits = logits
         return self.d_out[:n_sel]
+
+    def _forward_attention_dp(self, meta: AttentionMetadata, T: int) -> torch.Tensor:
+        """Attention DP: gather the token ids and positions of the a replicas (every replica
+        brings T rows in lockstep), give the model a slot mapping that writes only this
+        replica's rows, and keep this replica's rows of the output."""
+        adp = self.adp
+        a, j = adp.world_size, adp.rank_in_group
+        ids = adp.all_gather(self.d_ids[:T], dim=0)
+        pos = adp.all_gather(self.d_pos[:T], dim=0)
+        slots = torch.full((a * T,), -1, dtype=meta.slot_mapping.dtype, device=meta.slot_mapping.device)
+        slots[j * T:(j + 1) * T] = meta.slot_mapping[:T]
+        h = self.model(ids, pos, dataclasses.replace(meta, slot_mapping=slots), self.kv_caches)
+        return h[j * T:(j + 1) * T]
 
     def _sample_lm_dp(self, h: torch.Tensor, meta: AttentionMetadata, T: int, n_sel: int) -> torch.Tensor:
         """lm_head DP (``model_mxfp4.py:1928-2001``): every DP replica of the supergroup pads

@@ -102,6 +102,14 @@ class Worker:
         nc = self.cfg.neuron_config
         if max(nc.embedding_dp_size, nc.lm_head_dp_size, nc.mlp_dp_size) > 1 and self.cfg.speculative_config:
             raise ValueError("component data parallelism with speculative decoding is not supported")
+        if nc.attention_dp_size > 1:
+            if not hasattr(model, "attention_dp"):
+                raise ValueError(f"attention_dp_size > 1 is not supported for {type(model).__name__}")
+            if (nc.attention_dp_size != self.cfg.data_parallel_size or self.cfg.speculative_config
+                    or self.cfg.decode_context_parallel_size > 1
+                    or max(nc.embedding_dp_size, nc.lm_head_dp_size, nc.mlp_dp_size) > 1):
+                raise ValueError("attention_dp_size must equal data_parallel_size, without speculative decoding, "
+                                 "DCP or component DP")
         self._attach_all2all(model, mcfg)
         dcp = self.cfg.decode_context_parallel_size
         if dcp > 1:

@@ -100,32 +100,72 @@ def _param(shape, dtype, device) -> nn.Parameter:
     return nn.Parameter(torch.empty(shape, dtype=dtype, device=device), requires_grad=False)
 
 
+def _attention_dp(ps: ParallelState) -> GroupCoordinator | None:
+    """The attention-DP group (DP replicas at one TP position) when attention DP is on."""
+    g = getattr(ps, "attn_dp", None)
+    return g if (g is not None and g.world_size > 1) else None
+
+
+def _single_group() -> GroupCoordinator:
+    from ..parallel.state import _single
+
+    return _single("dp")
+
+
 class GptOssAttention(nn.Module):
-    def __init__(self, cfg: GptOssConfig, layer_idx: int, tp: GroupCoordinator, dtype, device):
+    """GQA with sinks over the paged cache; q heads and the o_proj input columns sharded
+    over ``tp``.
+
+    Attention DP (``adp``, ``attention_decode.py:530-563,756-765``, ``model_mxfp4.py:274-339``):
+    ``tp`` is then a supergroup of a = adp.world_size DP replicas x TP ranks that holds the
+    tokens of all a replicas.  The q projection is sharded over the supergroup, the member at
+    TP position t of replica j taking q shard t * a + j, so the a members at position t hold
+    together exactly the heads of plain TP rank t; K/V are projected with TP rank t's kv
+    heads.  An all-to-all over ``adp`` swaps batch for heads: each rank attends its own
+    replica's tokens (own KV cache and metadata) with TP rank t's heads, and the reverse
+    all-to-all returns its q shard for every token to the o_proj.  KV heads never move."""
+
+    def __init__(self, cfg: GptOssConfig, layer_idx: int, tp: GroupCoordinator, dtype, device,
+                 adp: GroupCoordinator | None = None):
         super().__init__()
         self.cfg = cfg
         self.tp = tp
+        self.adp = adp
         self.layer_idx = layer_idx
         t, r = tp.world_size, tp.rank_in_group
         if cfg.num_attention_heads % t:
             raise ValueError("attention heads must divide by tp")
         self.nq = cfg.num_attention_heads // t
-        self.kv_start, self.nkv = kv_head_sharding(cfg.num_key_value_heads, t, r)
+        if adp is None:
+            self.q_shard = r
+            self.kv_start, self.nkv = kv_head_sharding(cfg.num_key_value_heads, t, r)
+            self.head0, self.nq_attn = r * self.nq, self.nq
+        else:
+            a, j = adp.world_size, adp.rank_in_group
+            tp_plain = t // a
+            tpos = r % tp_plain
+            self.q_shard = tpos * a + j
+            self.kv_start, self.nkv = kv_head_sharding(cfg.num_key_value_heads, tp_plain, tpos)
+            self.nq_attn = cfg.num_attention_heads // tp_plain
+            self.head0 = tpos * self.nq_attn
         self.d = cfg.head_dim
         self.window = cfg.layer_window(layer_idx)
         self.scale = 1.0 / math.sqrt(self.d)
         qkv_out = (self.nq + 2 * self.nkv) * self.d
         self.qkv_weight = _param((qkv_out, cfg.hidden_size), dtype, device)
         self.qkv_bias = _param((qkv_out,), dtype, device) if cfg.attention_bias else None
-        self.sinks = _param((self.nq,), torch.float32, device)
+        self.sinks = _param((self.nq_attn,), torch.float32, device)
         self.o_proj = RowParallelLinear(cfg.num_attention_heads * self.d, cfg.hidden_size, tp,
                                         bias=cfg.attention_bias, dtype=dtype, device=device)
+        if adp is not None:  # o_proj input columns follow the q shard, not the group rank
+            qs, w = self.q_shard, self.nq * self.d
+            self.o_proj.weight.weight_loader = lambda p, full: p.data.copy_(full[:, qs * w:(qs + 1) * w].to(p.dtype))
         self.k_scale = 1.0
         self.v_scale = 1.0
 
     # -- weight loading -------------------------------------------------------
     def load_q_k_v(self, which: str, kind: str, full: torch.Tensor) -> None:
-        d, r = self.d, self.tp.rank_in_group
+        d, r = self.d, self.q_shard
         if which == "q":
             rows = slice(r * self.nq * d, (r + 1) * self.nq * d)
             dst = slice(0, self.nq * d)
@@ -139,17 +179,22 @@ class GptOssAttention(nn.Module):
             self.qkv_bias.data[dst].copy_(full[rows].to(self.qkv_bias.dtype))
 
     def load_sinks(self, full: torch.Tensor) -> None:
-        r = self.tp.rank_in_group
-        self.sinks.data.copy_(full[r * self.nq:(r + 1) * self.nq].float())
+        self.sinks.data.copy_(full[self.head0:self.head0 + self.nq_attn].float())
 
     def forward(self, positions: torch.Tensor, x: torch.Tensor, meta, kv: tuple, cos_sin: torch.Tensor
                 ) -> torch.Tensor:
         qkv = ops.linear(x, self.qkv_weight, self.qkv_bias)
         k_cache, v_cache = kv
+        # under attention DP the slot mapping covers every replica's rows (-1 outside this
+        # replica's), so only this replica's K/V reach its cache
         q = ops.rope_and_cache(qkv, positions, cos_sin, k_cache, v_cache, meta.slot_mapping, self.nq, self.nkv,
                                self.d, self.k_scale, self.v_scale)
+        if self.adp is not None:
+            q = self.adp.all_to_all(q.contiguous(), scatter_dim=0, gather_dim=1)  # own rows, TP-rank heads
         o = ops.attention(q, k_cache, v_cache, meta, self.scale, self.sinks, self.window, self.k_scale,
                           self.v_scale)
+        if self.adp is not None:
+            o = self.adp.all_to_all(o, scatter_dim=1, gather_dim=0)  # every row, this rank's q shard
         # partial output projection of this rank's heads; the all-reduce, bias, residual add
         # and the next RMSNorm happen in one fused step in the decoder layer
         return ops.linear(o.reshape(o.shape[0], self.nq * self.d), self.o_proj.weight, None)
@@ -210,11 +255,13 @@ class GptOssMLP(nn.Module):
     partial outputs reduce-scattered back (cross-DP EP, ``model_mxfp4.py:1361-1453``); the
     TP partial sum is completed at the next layer boundary."""
 
-    def __init__(self, cfg: GptOssConfig, ps: ParallelState, dtype, device):
+    def __init__(self, cfg: GptOssConfig, ps: ParallelState, dtype, device, rows_group: GroupCoordinator | None = None):
         super().__init__()
         self.cfg = cfg
-        self.dp = ps.dp
-        self.tp = ps.tp
+        # rows are replicated over ``tp`` (the attention-DP supergroup when set: every DP
+        # replica's tokens are already there, so no gather over DP)
+        self.dp = ps.dp if rows_group is None else _single_group()
+        self.tp = rows_group or ps.tp
         ep_rank = ps.dp.rank_in_group * ps.tp.world_size + ps.tp.rank_in_group
         ep_size = ps.tp.world_size * ps.dp.world_size
         self.router_weight = _param((cfg.num_local_experts, cfg.hidden_size), dtype, device)
@@ -252,11 +299,14 @@ class GptOssDecoderLayer(nn.Module):
         super().__init__()
         self.eps = cfg.rms_norm_eps
         self.tp = ps.tp
-        self.moe_group = ps.tp
+        adp = _attention_dp(ps)
+        if adp is not None:  # every layer boundary reduces over the attention-DP supergroup
+            self.tp = ps.attn_tp
+        self.moe_group = self.tp
         self.input_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, device=device)
-        self.self_attn = GptOssAttention(cfg, i, ps.tp, dtype, device)
+        self.self_attn = GptOssAttention(cfg, i, self.tp, dtype, device, adp)
         self.post_attention_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, device=device)
-        self.mlp = GptOssMLP(cfg, ps, dtype, device)
+        self.mlp = GptOssMLP(cfg, ps, dtype, device, rows_group=ps.attn_tp if adp is not None else None)
 
     def forward(self, positions, h, residual, meta, kv, cos_sin):
         if residual is None:
@@ -284,13 +334,20 @@ class GptOssForCausalLM(nn.Module):
         self.ps = ps
         self.dtype = dtype
         self.kv_dtype = kv_dtype or dtype
+        adp = _attention_dp(ps)
+        # the group whose ranks hold the same rows (TP, or the attention-DP supergroup)
+        self.tp = ps.attn_tp if adp is not None else ps.tp
+        emb = {"group": self.tp, "dp_group": None} if adp is not None else component(ps, "embedding")
         self.embed_tokens = VocabParallelEmbedding(cfg.vocab_size, cfg.hidden_size, dtype=dtype, device=device,
-                                                   **component(ps, "embedding"))
+                                                   **emb)
         self.layers = nn.ModuleList([GptOssDecoderLayer(cfg, i, ps, dtype, device)
                                      for i in range(cfg.num_hidden_layers)])
         self.norm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, device=device)
-        self.lm_head = ParallelLMHead(cfg.vocab_size, cfg.hidden_size, dtype=dtype, device=device,
-                                      **component(ps, "lm_head"))
+        # under attention DP the head is sharded over the supergroup and the runner samples
+        # every replica's rows (as with lm_head DP)
+        lmh = {"group": self.tp, "dp_group": adp} if adp is not None else component(ps, "lm_head")
+        self.lm_head = ParallelLMHead(cfg.vocab_size, cfg.hidden_size, dtype=dtype, device=device, **lmh)
+        self.attention_dp = adp
         inv, af = cfg.rope_params()
         self.register_buffer("cos_sin", ops.build_cos_sin_cache(inv, min(cfg.max_position_embeddings, 1 << 17),
                                                                 af, device=device), persistent=False)
@@ -313,9 +370,9 @@ class GptOssForCausalLM(nn.Module):
         aux = []
         for i, layer in enumerate(self.layers):
             if i in self.aux_hidden_layers:  # hidden state entering layer i (reduced partial + residual)
-                aux.append(h if residual is None else self.ps.tp.all_reduce(h.clone()) + residual)
+                aux.append(h if residual is None else self.tp.all_reduce(h.clone()) + residual)
             h, residual = layer(positions, h, residual, meta, kv_caches[i], self.cos_sin)
-        h, _ = self.ps.tp.all_reduce_add_rmsnorm(h, residual, self.norm.weight, self.cfg.rms_norm_eps)
+        h, _ = self.tp.all_reduce_add_rmsnorm(h, residual, self.norm.weight, self.cfg.rms_norm_eps)
         self._aux = torch.cat(aux, dim=-1) if aux else None
         return h
 

@@ -94,7 +94,7 @@ def attach_communicators(ps, device) -> None:
     """Create fused communicators for the groups whose all-reduces sit on the decode hot
     path (TP, and the MoE group when it differs).  Collective: every rank calls it."""
     seen = {}
-    for name in ("tp", "moe", "world"):
+    for name in ("tp", "moe", "world", "attn_tp"):
         g = getattr(ps, name)
         if g.world_size <= 1 or g.world_size > 8:
             continue
