@@ -7,9 +7,12 @@
 //   inverse-CDF draw with a host-supplied uniform; temperature <= 0 is greedy
 //   (functional/sampling.py:21).  The top-K candidates come from a 4-pass radix select
 //   over order-preserving float bits, then a bitonic sort in shared memory.
+#include <cooperative_groups.h>
+
 #include "launch.h"
 #include "common.cuh"
 #include "launch_pdl.h"
+#include "mma_utils.cuh"
 
 namespace b200 {
 
@@ -67,6 +70,132 @@ __global__ void topk_softmax_kernel(int* __restrict__ ids, float* __restrict__ w
       w[(size_t)warp * k + j] = __expf(sel_v[j] - m) / s;
     }
   }
+}
+
+// ---------------------------------------------------------------------------------------
+// Router: logits = x W^T (+ bias) and the top-k softmax of each token in one launch.
+// A thread-block cluster of CL CTAs covers the E experts of a 16-token tile, EN = E / CL
+// experts per CTA.  In each CTA the 4 warps split K and run warp-level bf16 MMAs
+// (m16n8k16; 16 tokens are below tcgen05's 64-row minimum and the GEMM is a 0.7 MB weight
+// read), their fp32 partial tiles are summed in shared memory, and after a cluster barrier
+// CTA r selects the experts of tokens r, r + CL, ... reading every CTA's logits over
+// distributed shared memory.  Same selection and softmax as topk_softmax_kernel, on fp32
+// logits.  Replaces a library GEMM launch + the top-k launch on the decode hot path.
+// ---------------------------------------------------------------------------------------
+template <int EN>
+__global__ void __launch_bounds__(128) router_topk_kernel(int* __restrict__ ids, float* __restrict__ wts,
+                                                          const __nv_bfloat16* __restrict__ x,
+                                                          const __nv_bfloat16* __restrict__ W,
+                                                          const __nv_bfloat16* __restrict__ bias, int T, int H, int E,
+                                                          int k) {
+  pdl_wait();
+  pdl_trigger();
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  const int CL = (int)cl.num_blocks();
+  const int r = (int)cl.block_rank();
+  __shared__ float part[4][16][EN];
+  __shared__ float lg[16][EN];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int m0 = blockIdx.y * 16, n0 = r * EN;
+  constexpr int NT = EN / 8;
+  float acc[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+  const int ksteps = H / 16;
+  const int per = (ksteps + 3) / 4;
+  const int kb = warp * per, ke = min(ksteps, kb + per);
+  const bool r0ok = m0 + g < T, r1ok = m0 + g + 8 < T;
+  const __nv_bfloat16* xr0 = x + (size_t)(m0 + g) * H + 2 * t4;
+  const __nv_bfloat16* xr1 = x + (size_t)(m0 + g + 8) * H + 2 * t4;
+#pragma unroll 4
+  for (int ks = kb; ks < ke; ++ks) {
+    const int k0 = ks * 16;
+    uint32_t a[4];
+    a[0] = r0ok ? *reinterpret_cast<const uint32_t*>(xr0 + k0) : 0u;
+    a[1] = r1ok ? *reinterpret_cast<const uint32_t*>(xr1 + k0) : 0u;
+    a[2] = r0ok ? *reinterpret_cast<const uint32_t*>(xr0 + k0 + 8) : 0u;
+    a[3] = r1ok ? *reinterpret_cast<const uint32_t*>(xr1 + k0 + 8) : 0u;
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      const __nv_bfloat16* wr = W + (size_t)(n0 + n * 8 + g) * H + k0 + 2 * t4;
+      uint32_t b[2] = {*reinterpret_cast<const uint32_t*>(wr), *reinterpret_cast<const uint32_t*>(wr + 8)};
+      mma_bf16_16816(acc[n], a, b);
+    }
+  }
+  // C fragment: rows g / g + 8, columns 2 * t4, 2 * t4 + 1 of each n8 tile
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    part[warp][g][n * 8 + 2 * t4] = acc[n][0];
+    part[warp][g][n * 8 + 2 * t4 + 1] = acc[n][1];
+    part[warp][g + 8][n * 8 + 2 * t4] = acc[n][2];
+    part[warp][g + 8][n * 8 + 2 * t4 + 1] = acc[n][3];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 16 * EN; i += blockDim.x) {
+    const int row = i / EN, col = i % EN;
+    float v = part[0][row][col] + part[1][row][col] + part[2][row][col] + part[3][row][col];
+    if (bias != nullptr) v += __bfloat162float(bias[n0 + col]);
+    lg[row][col] = v;
+  }
+  cl.sync();  // every CTA's logits are visible cluster-wide
+  // top-k: warp w of CTA r takes token rows r + CL * (w + 4 * i) of the tile
+  for (int row = r + CL * warp; row < 16; row += CL * 4) {
+    const int tok = m0 + row;
+    if (tok >= T) break;
+    constexpr int kMaxPer = 32;  // E <= 1024
+    float v[kMaxPer];
+    const int per_lane = (E + 31) / 32;
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+      const int e = i * 32 + lane;
+      if (i < per_lane && e < E) {
+        const float* peer = cl.map_shared_rank(&lg[0][0], e / EN);
+        v[i] = peer[row * EN + e % EN];
+      } else {
+        v[i] = -INFINITY;
+      }
+    }
+    float sel_v[16];
+    int sel_i[16];
+    for (int j = 0; j < k; ++j) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int i = 0; i < kMaxPer; ++i) {
+        const int e = i * 32 + lane;
+        if (i < per_lane && e < E && (v[i] > bv || (v[i] == bv && e < bi))) {
+          bv = v[i];
+          bi = e;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      sel_v[j] = bv;
+      sel_i[j] = bi;
+#pragma unroll
+      for (int i = 0; i < kMaxPer; ++i)
+        if (i * 32 + lane == bi) v[i] = -INFINITY;
+    }
+    if (lane == 0) {
+      const float m = sel_v[0];
+      float sum = 0.f;
+      for (int j = 0; j < k; ++j) sum += __expf(sel_v[j] - m);
+      for (int j = 0; j < k; ++j) {
+        ids[(size_t)tok * k + j] = sel_i[j];
+        wts[(size_t)tok * k + j] = __expf(sel_v[j] - m) / sum;
+      }
+    }
+  }
+  cl.sync();  // peers' shared memory stays alive until every CTA has read it
 }
 
 // argmax: each CTA scans a slice of one row with 16-byte loads and folds its (value,
@@ -309,6 +438,42 @@ extern "C" int b200_topk_softmax(int* ids, float* weights, const void* logits, i
   else
     return kBadShape;
   return (int)cudaGetLastError();
+}
+
+extern "C" int b200_router_topk(int* ids, float* weights, const void* x, const void* w, const void* bias, int T,
+                                int H, int E, int k, cudaStream_t s) {
+  // CL CTAs per cluster cover E = CL * EN experts, EN in {16, 32, 64}, CL <= 8
+  if (T < 0 || H % 16 || k < 1 || k > 16 || k > E || E > 1024) return kBadShape;
+  if (T == 0) return 0;
+  int EN = 0;
+  for (int en : {16, 32, 64})
+    if (E % en == 0 && E / en <= 8) {
+      EN = en;
+      break;
+    }
+  if (EN == 0) return kBadShape;
+  const int CL = E / EN;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(CL, cdiv(T, 16));
+  cfg.blockDim = dim3(128);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CL;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  const __nv_bfloat16* xb = (const __nv_bfloat16*)x;
+  const __nv_bfloat16* wb = (const __nv_bfloat16*)w;
+  const __nv_bfloat16* bb = (const __nv_bfloat16*)bias;
+  cudaError_t e;
+  if (EN == 16) e = cudaLaunchKernelEx(&cfg, router_topk_kernel<16>, ids, weights, xb, wb, bb, T, H, E, k);
+  else if (EN == 32) e = cudaLaunchKernelEx(&cfg, router_topk_kernel<32>, ids, weights, xb, wb, bb, T, H, E, k);
+  else e = cudaLaunchKernelEx(&cfg, router_topk_kernel<64>, ids, weights, xb, wb, bb, T, H, E, k);
+  return (int)e;
 }
 
 extern "C" int b200_argmax(float* vals, int64_t* idx, const void* logits, int B, int V, int dtype, cudaStream_t s) {
