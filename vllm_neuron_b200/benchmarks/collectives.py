@@ -1,6 +1,10 @@
-"""Layer-boundary collective microbenchmark (one process per GPU, under torchrun).
+"""Collective microbenchmarks (one process per GPU, under torchrun).
 
     torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m vllm_neuron_b200.benchmarks.collectives
+    torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m vllm_neuron_b200.benchmarks.collectives --op ep
+
+``--op ep`` times the EP all-to-all (see ``_ep``); the default is the layer-boundary
+all-reduce:
 
 For each token count T (hidden 2880, bf16) it times, with CUDA events after warm-up and as
 the maximum over ranks:
@@ -26,10 +30,84 @@ import torch.distributed as dist
 LINK_GBS = 770.0
 
 
+def _ep(a, rank, world, dev, ps) -> None:
+    """EP all-to-all: fused NVLink dispatch + combine (identity experts) in a CUDA graph of
+    ``--iters`` calls, and the collective (NCCL) all-to-all baseline timed eagerly.  Roofline:
+    the rows that must leave this rank (each token once to every other rank owning one of its
+    top-k experts, H bf16 + k ids / weights) and come back (H bf16), over 770 GB/s."""
+    from vllm_neuron_b200.parallel.all2all import EpAll2All, FusedEpAll2All
+
+    H, k, E = a.hidden, 4, a.experts
+    E_local = E // world
+    fused = FusedEpAll2All(ps.world, dev, H, k, max_tokens=256)
+    coll = EpAll2All(ps.world, H, k)
+    for T in [int(t) for t in a.tokens.split(",")]:
+        torch.manual_seed(1000 + rank)
+        x = torch.randn(T, H, device=dev).bfloat16()
+        ids = torch.stack([torch.randperm(E, device=dev)[:k] for _ in range(T)]).to(torch.int32)
+        w = torch.rand(T, k, device=dev)
+        owners = (ids // E_local).long()
+        remote = sum(int(((owners == d).any(1)).sum()) for d in range(world) if d != rank)
+        nbytes = remote * (H * 2 + 8 * k) + remote * H * 2
+        t_max = torch.tensor([float(nbytes)], device=dev)
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+        nbytes = int(t_max.item())
+        res = {}
+        for path, a2a in (("fused", fused), ("nccl", coll)):
+            def step():
+                xr, ir, wr = a2a.dispatch(x, ids, w, E_local, 0, T)
+                return a2a.combine(xr, T)
+
+            for _ in range(3):
+                step()
+            torch.cuda.synchronize()
+            if path == "fused":
+                g = torch.cuda.CUDAGraph()
+                s = torch.cuda.Stream()
+                s.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(s):
+                    step()
+                torch.cuda.current_stream().wait_stream(s)
+                with torch.cuda.graph(g):
+                    for _ in range(a.iters):
+                        step()
+                g.replay()
+                run = g.replay
+                n = a.iters
+            else:
+                run = step
+                n = 1
+            dist.barrier()
+            torch.cuda.synchronize()
+            times = []
+            for _ in range(5 if path == "fused" else a.iters):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                run()
+                e1.record()
+                torch.cuda.synchronize()
+                times.append(e0.elapsed_time(e1) * 1000.0 / n)
+            t = torch.tensor([sum(times) / len(times)], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            res[path] = t.item()
+            if path == "fused":
+                del g
+        target = nbytes / (LINK_GBS * 1e3)
+        if rank == 0:
+            for path, us in res.items():
+                print(json.dumps({"op": "ep_dispatch_combine", "path": path, "world": world, "T": T, "H": H,
+                                  "E": E, "k": k, "us": round(us, 2), "nvlink_bytes_per_rank": nbytes,
+                                  "target_us": round(target, 2), "frac_of_roofline": round(target / us, 3)}),
+                      flush=True)
+    fused.close()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
+    ap.add_argument("--op", choices=["allreduce", "ep"], default="allreduce")
     ap.add_argument("--hidden", type=int, default=2880)
     ap.add_argument("--tokens", default="1,16,64,256")
+    ap.add_argument("--experts", type=int, default=128)
     ap.add_argument("--iters", type=int, default=50)
     a = ap.parse_args()
     from vllm_neuron_b200 import ops
@@ -42,6 +120,12 @@ def main() -> None:
     dev = torch.device("cuda", local)
     pstate.init_distributed_environment(world, rank, backend="nccl", local_rank=local, timeout_s=120)
     ps = pstate.initialize_parallel_state(tp=world, timeout_s=120)
+    if a.op == "ep":
+        _ep(a, rank, world, dev, ps)
+        torch.cuda.synchronize()
+        pstate.destroy_parallel_state()
+        dist.destroy_process_group()
+        return
     attach_communicators(ps, dev)
     tp = ps.tp
     H = a.hidden
