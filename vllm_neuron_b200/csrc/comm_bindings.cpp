@@ -13,6 +13,11 @@ int b200_ipc_close(void* p);
 int b200_allreduce_fused(void* const* bases, int rank, int world, size_t slot_bytes, const void* in, void* out,
                          void* residual, const void* bias, const float* w, float eps, int T, int H, int num_blocks,
                          int* status, cudaStream_t s);
+int b200_kv_export(void* dst, const int64_t* kptr, const int64_t* vptr, int n_layers, const int* blocks, int T, int nh,
+                   int row_bytes, int bs, cudaStream_t s);
+int b200_kv_import(const void* const* part_base, const int* part_h0, const int* part_nh, int n_parts,
+                   const int64_t* kptr, const int64_t* vptr, int n_layers, const int* blocks, int T, int src_T, int h0,
+                   int nh, int row_bytes, int bs, int* status, cudaStream_t s);
 int b200_ep_dispatch(void* const* bases, int rank, int world, size_t slot_bytes, int cpd, int T, int Tc, int H, int k,
                      int E_local, int t_begin, int t_end, const void* x, const int* ids, const float* w, void* x_recv,
                      int* ids_recv, float* w_recv, int* send_idx, int* status, cudaStream_t s);
@@ -73,6 +78,45 @@ void allreduce_fused(at::IntArrayRef bases, int64_t rank, int64_t slot_bytes, Te
       status.has_value() ? status->data_ptr<int>() : nullptr, at::cuda::getCurrentCUDAStream().stream());
   TORCH_CHECK(rc == 0, "b200::allreduce_fused failed with code ", rc);
 }
+void kv_export(int64_t dst, Tensor kptr, Tensor vptr, Tensor blocks, int64_t num_tokens, int64_t nh,
+               int64_t row_bytes, int64_t bs) {
+  TORCH_CHECK(kptr.is_cuda() && kptr.scalar_type() == at::kLong && vptr.scalar_type() == at::kLong &&
+                  kptr.numel() == vptr.numel(),
+              "device int64 layer pointer tables");
+  TORCH_CHECK(blocks.is_cuda() && blocks.scalar_type() == at::kInt && blocks.is_contiguous(), "int32 blocks");
+  TORCH_CHECK(blocks.numel() * bs >= num_tokens, "too few blocks for the tokens");
+  c10::cuda::CUDAGuard g(kptr.device());
+  const int rc = b200_kv_export(reinterpret_cast<void*>(dst), kptr.data_ptr<int64_t>(), vptr.data_ptr<int64_t>(),
+                                kptr.numel(), blocks.data_ptr<int>(), num_tokens, nh, row_bytes, bs,
+                                at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(rc == 0, "b200::kv_export failed with code ", rc);
+}
+
+void kv_import(at::IntArrayRef part_base, at::IntArrayRef part_h0, at::IntArrayRef part_nh, Tensor kptr,
+               Tensor vptr, Tensor blocks, int64_t num_tokens, int64_t src_tokens, int64_t h0, int64_t nh,
+               int64_t row_bytes, int64_t bs, c10::optional<Tensor> status) {
+  TORCH_CHECK(kptr.is_cuda() && kptr.scalar_type() == at::kLong && vptr.scalar_type() == at::kLong &&
+                  kptr.numel() == vptr.numel(),
+              "device int64 layer pointer tables");
+  TORCH_CHECK(blocks.is_cuda() && blocks.scalar_type() == at::kInt && blocks.is_contiguous(), "int32 blocks");
+  TORCH_CHECK(blocks.numel() * bs >= num_tokens, "too few blocks for the tokens");
+  const int n = part_base.size();
+  TORCH_CHECK(n >= 1 && n <= 8 && (int)part_h0.size() == n && (int)part_nh.size() == n, "1..8 producer parts");
+  const void* bases[8];
+  int ph0[8], pnh[8];
+  for (int i = 0; i < n; ++i) {
+    bases[i] = reinterpret_cast<const void*>(part_base[i]);
+    ph0[i] = part_h0[i];
+    pnh[i] = part_nh[i];
+  }
+  c10::cuda::CUDAGuard g(kptr.device());
+  const int rc = b200_kv_import(bases, ph0, pnh, n, kptr.data_ptr<int64_t>(), vptr.data_ptr<int64_t>(), kptr.numel(),
+                                blocks.data_ptr<int>(), num_tokens, src_tokens, h0, nh, row_bytes, bs,
+                                status.has_value() ? status->data_ptr<int>() : nullptr,
+                                at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(rc == 0, "b200::kv_import failed with code ", rc);
+}
+
 void ep_dispatch(at::IntArrayRef bases, int64_t rank, int64_t slot_bytes, int64_t cpd, int64_t Tc, int64_t E_local,
                  int64_t t_begin, int64_t t_end, Tensor x, Tensor ids, Tensor w, Tensor x_recv, Tensor ids_recv,
                  Tensor w_recv, Tensor send_idx, c10::optional<Tensor> status) {
@@ -134,6 +178,12 @@ void register_comm_ops(torch::Library& m) {
       "Tensor x, Tensor ids, Tensor w, Tensor(a!) x_recv, Tensor(b!) ids_recv, Tensor(c!) w_recv, "
       "Tensor(d!) send_idx, Tensor? status) -> ()");
   m.def(
+      "kv_export(int dst, Tensor kptr, Tensor vptr, Tensor blocks, int num_tokens, int nh, int row_bytes, "
+      "int bs) -> ()");
+  m.def(
+      "kv_import(int[] part_base, int[] part_h0, int[] part_nh, Tensor kptr, Tensor vptr, Tensor blocks, "
+      "int num_tokens, int src_tokens, int h0, int nh, int row_bytes, int bs, Tensor? status) -> ()");
+  m.def(
       "ep_combine(int[] bases, int rank, int slot_bytes, int cpd, int Tc, Tensor y_recv, Tensor ids_recv, "
       "Tensor send_idx, Tensor(a!) out, Tensor? status) -> ()");
 }
@@ -142,6 +192,8 @@ void register_comm_impls(torch::Library& m) {
   m.impl("allreduce_fused", &allreduce_fused);
   m.impl("ep_dispatch", &ep_dispatch);
   m.impl("ep_combine", &ep_combine);
+  m.impl("kv_export", &kv_export);
+  m.impl("kv_import", &kv_import);
 }
 
 void register_comm_cpu_impls(torch::Library& m) {

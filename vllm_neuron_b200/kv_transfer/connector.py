@@ -54,6 +54,7 @@ class HostStagedConnector:
         self.rank, self.tp = rank, tp_size
         self.engine_id = engine_id
         self.role = role
+        self.extra = extra
         self.exported: list[str] = []
         self.stats = {"exported": 0, "loaded": 0, "failed": 0, "bytes": 0}
 
@@ -154,6 +155,167 @@ class HostStagedConnector:
         self.exported = []
 
 
+class B200IpcConnector(HostStagedConnector):
+    """Device-to-device transport for engines on one host (``csrc/kv_transfer.cu``).
+
+    Every producer rank owns a device pool (``pool_mb``, default 1024 MB) shared by CUDA IPC;
+    its handle is published once in the store directory.  ``export`` gathers the request's KV
+    of positions [0, num_tokens) from the paged cache into a free range of the pool (one
+    kernel), waits for it, and writes a small metadata file (offset, tokens, heads, layers).
+    ``load`` maps the producer ranks' pools (once per producer rank), copies the rows of the
+    kv heads this rank owns straight into its blocks (one kernel, peer loads), waits for it and
+    leaves an acknowledgement file; the producer reuses a pool range once it is acknowledged
+    or older than ``ttl_s``.  When the pool has no free range, or either side runs on the CPU,
+    the transfer falls back to the host-staged files of :class:`HostStagedConnector` (the
+    params carry the transport)."""
+
+    def __init__(self, *args, **kwargs):
+        super().__init__(*args, **kwargs)
+        layers = self._layers()
+        kc0 = self.kv[layers[0][0]][0]
+        self.device = kc0.device
+        self.row_bytes = kc0.shape[3] * kc0.element_size()
+        self.kptr = torch.tensor([kc.data_ptr() for _, (kc, _) in layers], dtype=torch.int64, device=self.device)
+        self.vptr = torch.tensor([vc.data_ptr() for _, (_, vc) in layers], dtype=torch.int64, device=self.device)
+        self.layer_ids = [i for i, _ in layers]
+        self.pool = None
+        self.pool_bytes = int(float(self.extra.get("pool_mb", 1024)) * (1 << 20)) // 256 * 256
+        self.ranges: list[tuple[str, int, int, float]] = []  # (transfer id, offset, size, created)
+        self._peers: dict[tuple[str, int], int] = {}
+        from ..ops import device_status
+
+        self.status = device_status(self.device)
+        if self.is_producer and self.pool_bytes > 0:
+            ops = torch.ops.b200
+            # comm_alloc(n) allocates a 64 KB header + 2 n bytes; the pool starts after the header
+            self.pool = ops.comm_alloc(self.pool_bytes // 2 + 256)
+            self.pool0 = self.pool + 64 * 1024
+            h = ops.ipc_get_handle(self.pool).numpy().tobytes()
+            tmp = self._pool_path(self.engine_id, self.rank) + f".tmp{os.getpid()}"
+            with open(tmp, "wb") as f:
+                f.write(h)
+            os.replace(tmp, self._pool_path(self.engine_id, self.rank))
+
+    def _pool_path(self, engine_id: str, rank: int) -> str:
+        return os.path.join(self.store, f"{engine_id}.rank{rank}.pool")
+
+    def _meta_path(self, tid: str, rank: int) -> str:
+        return os.path.join(self.store, f"{tid}.rank{rank}.ipc")
+
+    def _ack_path(self, tid: str, rank: int) -> str:
+        return os.path.join(self.store, f"{tid}.rank{rank}.ack")
+
+    # ----------------------------------------------------------------- producer
+    def _reserve(self, need: int) -> int | None:
+        """First-fit range of the pool after dropping acknowledged / expired ranges."""
+        now = time.monotonic()
+        keep = []
+        for tid, off, size, t in self.ranges:
+            if os.path.exists(self._ack_path(tid, self.rank)) or now - t > self.ttl_s:
+                for p in (self._ack_path(tid, self.rank), self._meta_path(tid, self.rank)):
+                    try:
+                        os.remove(p)
+                    except OSError:
+                        pass
+            else:
+                keep.append((tid, off, size, t))
+        self.ranges = sorted(keep, key=lambda r: r[1])
+        cur = 0
+        for _, off, size, _ in self.ranges:
+            if off - cur >= need:
+                return cur
+            cur = off + size
+        return cur if self.pool_bytes - cur >= need else None
+
+    def export(self, request_id: str, block_ids: list[int], num_tokens: int) -> dict:
+        need = (2 * len(self.layer_ids) * num_tokens * self.nh * self.row_bytes + 255) // 256 * 256
+        off = self._reserve(need) if self.pool is not None else None
+        if off is None:
+            return {**super().export(request_id, block_ids, num_tokens), "transport": "host"}
+        tid = f"{self.engine_id}-{request_id}"
+        nb = -(-num_tokens // self.bs)
+        blocks = torch.tensor(block_ids[:nb], dtype=torch.int32, device=self.device)
+        torch.ops.b200.kv_export(self.pool0 + off, self.kptr, self.vptr, blocks, num_tokens, self.nh,
+                                 self.row_bytes, self.bs)
+        torch.cuda.current_stream(self.device).synchronize()  # the consumer reads from another process
+        self.ranges.append((tid, off, need, time.monotonic()))
+        meta = {"offset": off, "num_tokens": num_tokens, "heads": (self.h0, self.nh), "layers": self.layer_ids,
+                "row_bytes": self.row_bytes}
+        tmp = self._meta_path(tid, self.rank) + f".tmp{os.getpid()}"
+        torch.save(meta, tmp)
+        os.replace(tmp, self._meta_path(tid, self.rank))
+        self.stats["exported"] += 1
+        self.stats["bytes"] += need
+        return {"do_remote_prefill": True, "transfer_id": tid, "num_tokens": num_tokens,
+                "remote_tp_size": self.tp, "remote_engine_id": self.engine_id, "transport": "ipc"}
+
+    # ----------------------------------------------------------------- consumer
+    def _peer(self, engine_id: str, rank: int, deadline: float) -> int:
+        key = (engine_id, rank)
+        if key not in self._peers:
+            path = self._pool_path(engine_id, rank)
+            while not os.path.exists(path):
+                if time.monotonic() > deadline:
+                    raise KVTransferError(f"no KV pool published by {engine_id} rank {rank}")
+                time.sleep(0.002)
+            with open(path, "rb") as f:
+                h = f.read()
+            self._peers[key] = torch.ops.b200.ipc_open_handle(torch.frombuffer(bytearray(h), dtype=torch.uint8))
+        return self._peers[key]
+
+    def load(self, params: dict, block_ids: list[int], num_tokens: int) -> None:
+        if params.get("transport") != "ipc" or self.device.type != "cuda":
+            return super().load(params, block_ids, num_tokens)
+        tid = params.get("transfer_id")
+        ptp = int(params.get("remote_tp_size", 1))
+        eng = params.get("remote_engine_id")
+        if not tid or not eng:
+            raise KVTransferError("kv_transfer_params without transfer_id / remote_engine_id")
+        deadline = time.monotonic() + self.timeout_s
+        paths = [self._meta_path(tid, r) for r in range(ptp)]
+        while not all(os.path.exists(p) for p in paths):
+            if time.monotonic() > deadline:
+                self.stats["failed"] += 1
+                raise KVTransferError(f"KV transfer {tid} not available after {self.timeout_s:.1f}s")
+            time.sleep(0.002)
+        metas = [torch.load(p, weights_only=False) for p in paths]
+        for m in metas:
+            if m["num_tokens"] < num_tokens or m["layers"] != self.layer_ids or m["row_bytes"] != self.row_bytes:
+                raise KVTransferError(f"KV transfer {tid}: layout does not match this engine")
+        need_heads = range(self.h0, self.h0 + self.nh)
+        if not all(any(m["heads"][0] <= h < m["heads"][0] + m["heads"][1] for m in metas) for h in need_heads):
+            raise KVTransferError(f"KV transfer {tid}: kv heads {self.h0}..{self.h0 + self.nh - 1} missing")
+        bases = [self._peer(eng, r, deadline) + 64 * 1024 + m["offset"] for r, m in enumerate(metas)]
+        if any(m["num_tokens"] != metas[0]["num_tokens"] for m in metas):
+            raise KVTransferError(f"KV transfer {tid}: producer ranks disagree on the token count")
+        nb = -(-num_tokens // self.bs)
+        blocks = torch.tensor(block_ids[:nb], dtype=torch.int32, device=self.device)
+        torch.ops.b200.kv_import(bases, [m["heads"][0] for m in metas], [m["heads"][1] for m in metas], self.kptr,
+                                 self.vptr, blocks, num_tokens, metas[0]["num_tokens"], self.h0, self.nh,
+                                 self.row_bytes, self.bs, self.status)
+        torch.cuda.current_stream(self.device).synchronize()  # the producer may reuse the range after the ack
+        for r in range(ptp):
+            with open(self._ack_path(tid, r), "w"):
+                pass
+        self.stats["loaded"] += 1
+        self.stats["bytes"] += sum(2 * len(self.layer_ids) * num_tokens * m["heads"][1] * self.row_bytes
+                                   for m in metas)
+
+    def cleanup(self) -> None:
+        super().cleanup()
+        ops = torch.ops.b200
+        try:
+            torch.cuda.synchronize(self.device)
+            for p in self._peers.values():
+                ops.ipc_close(p)
+            self._peers = {}
+            if self.pool is not None:
+                ops.comm_free(self.pool)
+                self.pool = None
+        except Exception:  # noqa: BLE001
+            pass
+
+
 def make_connector(cfg, runner, rank: int, tp_size: int, kv_head_range: tuple[int, int]):
     kt = cfg.kv_transfer_config
     if kt is None:
@@ -163,5 +325,9 @@ def make_connector(cfg, runner, rank: int, tp_size: int, kv_head_range: tuple[in
         raise ValueError(f"unsupported kv_connector {name!r}")
     extra = dict(kt.kv_connector_extra_config or {})
     engine_id = extra.get("engine_id") or f"eng{os.getpid()}"
-    return HostStagedConnector(runner.kv_caches, kv_head_range, cfg.block_size, rank, tp_size, engine_id,
-                               kt.kv_role, extra)
+    kv0 = next((kv for kv in runner.kv_caches if kv is not None), None)
+    on_gpu = kv0 is not None and kv0[0].is_cuda
+    # the NIXL names select the device transport: same-host engines, peer memory instead of
+    # a network fabric
+    cls = B200IpcConnector if (on_gpu and name != "HostStagedConnector") else HostStagedConnector
+    return cls(runner.kv_caches, kv_head_range, cfg.block_size, rank, tp_size, engine_id, kt.kv_role, extra)
