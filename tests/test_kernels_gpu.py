@@ -167,7 +167,8 @@ def test_varlen_attention(d, causal):
 
 @pytest.mark.parametrize("T,E,H,k", [(64, 128, 2880, 4), (300, 128, 2880, 4), (16, 512, 2048, 10),
                                      (600, 128, 2880, 4), (1, 32, 2880, 4), (5, 64, 2048, 8), (40, 8, 256, 2)])
-def test_router_topk_and_argmax(T, E, H, k):
+@pytest.mark.parametrize("fused", [False, True])
+def test_router_topk_and_argmax(T, E, H, k, fused):
     """Router logits + top-k softmax (the fused cluster kernel for E a multiple of 16 up to
     512; GEMM + top-k kernel otherwise): the chosen experts must be a top-k set of the fp32
     reference logits up to bf16 rounding of the logits."""
@@ -175,7 +176,7 @@ def test_router_topk_and_argmax(T, E, H, k):
     x = torch.randn(T, H, device=DEV, dtype=torch.bfloat16)
     w = torch.randn(E, H, device=DEV, dtype=torch.bfloat16) * 0.02
     b = torch.randn(E, device=DEV, dtype=torch.bfloat16) * 0.02
-    ids, wt = ops.router_topk(x, w, b, k)
+    ids, wt = ops.router_topk(x, w, b, k, fused=fused)
     ref_logits = x.float() @ w.float().t() + b.float()
     kth = ref_logits.topk(k, -1).values[:, -1:]
     got = ref_logits.gather(1, ids.long())

@@ -13,7 +13,7 @@ Shapes (defaults are the GPT-OSS-120B decode step at concurrency 64 and the Qwen
 layer shapes at TP=4):
   moe_mxfp4    T=64 tokens x top-4 over 128 MXFP4 experts, H = I = 2880 (one MoE layer)
   moe_bf16     T=64, 16 bf16 experts, H = I = 2880
-  router       T=64 tokens x 128 experts, H = 2880: fused logits + top-4 softmax kernel
+  router       T=64 tokens x 128 experts, H = 2880: fused logits + top-4 softmax cluster kernel
                (router_unfused: library GEMM + top-k kernel, for comparison)
   attn_decode  B=64 sequences x 2048 context, 64 q / 8 kv heads, d=64, bf16 paged cache
   attn_prefill 1 x 2048-token prompt, 64 q / 8 kv heads, d=64

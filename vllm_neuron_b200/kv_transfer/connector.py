@@ -171,6 +171,9 @@ class B200IpcConnector(HostStagedConnector):
 
     def __init__(self, *args, **kwargs):
         super().__init__(*args, **kwargs)
+        from ..ops import _ext
+
+        _ext.load()
         layers = self._layers()
         kc0 = self.kv[layers[0][0]][0]
         self.device = kc0.device
