@@ -167,16 +167,14 @@ def test_varlen_attention(d, causal):
 
 @pytest.mark.parametrize("T,E,H,k", [(64, 128, 2880, 4), (300, 128, 2880, 4), (16, 512, 2048, 10),
                                      (600, 128, 2880, 4), (1, 32, 2880, 4), (5, 64, 2048, 8), (40, 8, 256, 2)])
-@pytest.mark.parametrize("fused", [False, True])
-def test_router_topk_and_argmax(T, E, H, k, fused):
-    """Router logits + top-k softmax (the fused cluster kernel for E a multiple of 16 up to
-    512; GEMM + top-k kernel otherwise): the chosen experts must be a top-k set of the fp32
-    reference logits up to bf16 rounding of the logits."""
+def test_router_topk_and_argmax(T, E, H, k):
+    """GEMM (bf16 logits) + top-k softmax kernel: the chosen experts must be a top-k set of
+    the fp32 reference logits up to bf16 rounding of the logits."""
     torch.manual_seed(5)
     x = torch.randn(T, H, device=DEV, dtype=torch.bfloat16)
     w = torch.randn(E, H, device=DEV, dtype=torch.bfloat16) * 0.02
     b = torch.randn(E, device=DEV, dtype=torch.bfloat16) * 0.02
-    ids, wt = ops.router_topk(x, w, b, k, fused=fused)
+    ids, wt = ops.router_topk(x, w, b, k)
     ref_logits = x.float() @ w.float().t() + b.float()
     kth = ref_logits.topk(k, -1).values[:, -1:]
     got = ref_logits.gather(1, ids.long())

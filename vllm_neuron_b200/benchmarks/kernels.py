@@ -13,8 +13,6 @@ Shapes (defaults are the GPT-OSS-120B decode step at concurrency 64 and the Qwen
 layer shapes at TP=4):
   moe_mxfp4    T=64 tokens x top-4 over 128 MXFP4 experts, H = I = 2880 (one MoE layer)
   moe_bf16     T=64, 16 bf16 experts, H = I = 2880
-  router       T=64 tokens x 128 experts, H = 2880: fused logits + top-4 softmax cluster kernel
-               (router_unfused: library GEMM + top-k kernel, for comparison)
   attn_decode  B=64 sequences x 2048 context, 64 q / 8 kv heads, d=64, bf16 paged cache
   attn_prefill 1 x 2048-token prompt, 64 q / 8 kv heads, d=64
   gdn_prefill  8192-token prompt, 4 key / 8 value heads of 128 (Qwen3-Next TP=4)
@@ -202,26 +200,7 @@ def _gdn(args, decode: bool):
     return fn, nbytes, flops, {"T": T, "B": B, "nk": nk, "nv": nv, "d": d}
 
 
-def _router(args, fused: bool):
-    from vllm_neuron_b200 import ops
-
-    T, E, H, k = args.T or 64, args.E or 128, 2880, 4
-    x = torch.randn(T, H, device="cuda").bfloat16()
-    w = (torch.randn(E, H, device="cuda") * 0.02).bfloat16()
-    b = (torch.randn(E, device="cuda") * 0.02).bfloat16()
-    ids = torch.empty(T, k, dtype=torch.int32, device="cuda")
-    wts = torch.empty(T, k, dtype=torch.float32, device="cuda")
-    if fused:
-        fn = lambda: ops._k().router_topk(ids, wts, x, w, b)  # noqa: E731
-    else:  # library GEMM (bf16 logits) + top-k kernel
-        fn = lambda: ops._k().topk_softmax(ids, wts, torch.nn.functional.linear(x, w, b))  # noqa: E731
-    nbytes = E * H * 2 + T * H * 2
-    return fn, nbytes, 2 * T * E * H, {"T": T, "E": E, "H": H, "k": k}
-
-
 OPS = {
-    "router": lambda a: _router(a, True),
-    "router_unfused": lambda a: _router(a, False),
     "moe_mxfp4": _moe_mxfp4,
     "moe_bf16": _moe_bf16,
     "attn_decode": _attn_decode,

@@ -213,22 +213,6 @@ void varlen_attention(Tensor out, Tensor q, Tensor k, Tensor v, Tensor cu, doubl
            "varlen_attention");
 }
 
-void router_topk(Tensor ids, Tensor weights, Tensor x, Tensor w, c10::optional<Tensor> bias) {
-  check_cuda(x, "x");
-  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && x.is_contiguous() &&
-                  w.is_contiguous() && x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1),
-              "bf16 x [T, H] and router weight [E, H]");
-  TORCH_CHECK(!bias.has_value() || (bias->scalar_type() == at::kBFloat16 && bias->is_contiguous()), "bf16 bias");
-  TORCH_CHECK(ids.scalar_type() == at::kInt && weights.scalar_type() == at::kFloat && ids.is_contiguous() &&
-                  weights.is_contiguous(),
-              "int32 ids / fp32 weights");
-  c10::cuda::CUDAGuard g(x.device());
-  check_rc(b200_router_topk(ids.data_ptr<int>(), weights.data_ptr<float>(), x.data_ptr(), w.data_ptr(),
-                            bias.has_value() ? bias->data_ptr() : nullptr, x.size(0), x.size(1), w.size(0),
-                            ids.size(1), stream()),
-           "router_topk");
-}
-
 void topk_softmax(Tensor ids, Tensor weights, Tensor logits) {
   check_cuda(logits, "logits");
   TORCH_CHECK((logits.scalar_type() == at::kFloat || logits.scalar_type() == at::kBFloat16) &&
@@ -300,7 +284,6 @@ TORCH_LIBRARY(b200, m) {
       "varlen_attention(Tensor(a!) out, Tensor q, Tensor k, Tensor v, Tensor cu_seqlens, float scale, bool causal, "
       "int max_seqlen) -> ()");
   m.def("topk_softmax(Tensor(a!) ids, Tensor(b!) weights, Tensor logits) -> ()");
-  m.def("router_topk(Tensor(a!) ids, Tensor(b!) weights, Tensor x, Tensor w, Tensor? bias) -> ()");
   m.def("argmax(Tensor(a!) vals, Tensor(b!) idx, Tensor logits) -> ()");
   m.def(
       "sample(Tensor(a!) out, Tensor logits, Tensor temperature, Tensor top_k, Tensor top_p, Tensor uniform, "
@@ -325,7 +308,6 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("paged_attention_prefill_cp", &paged_attention_prefill_cp);
   m.impl("varlen_attention", &varlen_attention);
   m.impl("topk_softmax", &topk_softmax);
-  m.impl("router_topk", &router_topk);
   m.impl("argmax", &argmax);
   m.impl("sample", &sample);
   register_moe_impls(m);

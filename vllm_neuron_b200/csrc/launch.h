@@ -61,10 +61,6 @@ int b200_varlen_attention(void* out, const void* q, const void* k, const void* v
                           int T, int nq, int nkv, int d, float scale, int causal, int max_seqlen, int dtype,
                           cudaStream_t s);
 
-// router logits x W^T (+ bias) fused with the top-k softmax (bf16 x / W / bias, H % 64 == 0,
-// E = CL * EN with EN in {16, 32, 64} and CL <= 8)
-int b200_router_topk(int* ids, float* weights, const void* x, const void* w, const void* bias, int T, int H, int E,
-                     int k, cudaStream_t s);
 int b200_topk_softmax(int* ids, float* weights, const void* logits, int T, int E, int k, int dtype, cudaStream_t s);
 
 int b200_argmax(float* vals, int64_t* idx, const void* logits, int B, int V, int dtype, cudaStream_t s);

@@ -7,12 +7,9 @@
 //   inverse-CDF draw with a host-supplied uniform; temperature <= 0 is greedy
 //   (functional/sampling.py:21).  The top-K candidates come from a 4-pass radix select
 //   over order-preserving float bits, then a bitonic sort in shared memory.
-#include <cooperative_groups.h>
-
 #include "launch.h"
 #include "common.cuh"
 #include "launch_pdl.h"
-#include "mma_utils.cuh"
 
 namespace b200 {
 
@@ -70,172 +67,6 @@ __global__ void topk_softmax_kernel(int* __restrict__ ids, float* __restrict__ w
       w[(size_t)warp * k + j] = __expf(sel_v[j] - m) / s;
     }
   }
-}
-
-// ---------------------------------------------------------------------------------------
-// Router: logits = x W^T (+ bias) and the top-k softmax of each token in one launch.
-// A thread-block cluster of CL CTAs covers the E experts of a 16-token tile, EN = E / CL
-// experts per CTA.  K streams through shared memory in 64-wide slabs on a kRouterStages-deep
-// cp.async ring (x tile and W slice of a slab: 16 + EN rows of 128 B, padded to 144 B so the
-// fragment loads hit distinct banks); in each slab the 8 warps take the 4 k16 steps x the n8
-// tiles with warp-level bf16 MMAs (m16n8k16: 16 tokens are below tcgen05's 64-row minimum and
-// the GEMM is a 0.7 MB weight read).  The per-k-step partial tiles are summed in shared
-// memory, and after a cluster barrier CTA r selects the experts of tokens r, r + CL, ...,
-// reading every CTA's logits over distributed shared memory.  Same selection and softmax as
-// topk_softmax_kernel, on fp32 logits.
-// ---------------------------------------------------------------------------------------
-constexpr int kRouterKC = 64;                 // K elements per slab
-constexpr int kRouterRow = kRouterKC + 8;     // padded row, bf16 elements (144 B)
-constexpr int kRouterStages = 8;
-
-template <int EN>
-__global__ void __launch_bounds__(256) router_topk_kernel(int* __restrict__ ids, float* __restrict__ wts,
-                                                          const __nv_bfloat16* __restrict__ x,
-                                                          const __nv_bfloat16* __restrict__ W,
-                                                          const __nv_bfloat16* __restrict__ bias, int T, int H, int E,
-                                                          int k) {
-  pdl_wait();
-  pdl_trigger();
-  namespace cg = cooperative_groups;
-  cg::cluster_group cl = cg::this_cluster();
-  const int CL = (int)cl.num_blocks();
-  const int r = (int)cl.block_rank();
-  extern __shared__ __align__(128) uint8_t router_smem[];
-  __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(router_smem);  // [S][16 + EN][kRouterRow]
-  __shared__ float part[4][16][EN];
-  __shared__ float lg[16][EN];
-  constexpr int ROWS = 16 + EN;
-  constexpr int NT = EN / 8;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t4 = lane & 3;
-  const int ks = warp & 3;  // k16 step of every slab this warp computes
-  const int m0 = blockIdx.y * 16, n0 = r * EN;
-  const int nslab = H / kRouterKC;
-
-  auto load = [&](int slab, int buf) {
-    __nv_bfloat16* st = ring + (size_t)buf * ROWS * kRouterRow;
-    const int k0 = slab * kRouterKC;
-    for (int i = threadIdx.x; i < ROWS * 8; i += blockDim.x) {
-      const int row = i >> 3, c = i & 7;
-      const __nv_bfloat16* src;
-      int bytes = 16;
-      if (row < 16) {
-        const int tok = m0 + row;
-        bytes = tok < T ? 16 : 0;
-        src = x + (size_t)(tok < T ? tok : 0) * H + k0 + c * 8;
-      } else {
-        src = W + (size_t)(n0 + row - 16) * H + k0 + c * 8;
-      }
-      cp_async16(st + row * kRouterRow + c * 8, src, bytes);
-    }
-  };
-
-  float acc[NT][4];
-#pragma unroll
-  for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
-#pragma unroll
-  for (int p = 0; p < kRouterStages - 1; ++p) {
-    if (p < nslab) load(p, p);
-    cp_async_commit();
-  }
-  for (int sl = 0; sl < nslab; ++sl) {
-    cp_async_wait<kRouterStages - 2>();
-    __syncthreads();  // slab sl landed for every thread; every warp is done with slab sl - 1
-    {
-      const int nx = sl + kRouterStages - 1;
-      if (nx < nslab) load(nx, nx % kRouterStages);
-      cp_async_commit();
-    }
-    const __nv_bfloat16* st = ring + (size_t)(sl % kRouterStages) * ROWS * kRouterRow;
-    const int kc = ks * 16 + 2 * t4;
-    uint32_t a[4];
-    a[0] = *reinterpret_cast<const uint32_t*>(st + g * kRouterRow + kc);
-    a[1] = *reinterpret_cast<const uint32_t*>(st + (g + 8) * kRouterRow + kc);
-    a[2] = *reinterpret_cast<const uint32_t*>(st + g * kRouterRow + kc + 8);
-    a[3] = *reinterpret_cast<const uint32_t*>(st + (g + 8) * kRouterRow + kc + 8);
-#pragma unroll
-    for (int n = 0; n < NT; ++n) {
-      if ((n & 1) != (warp >> 2)) continue;  // warps 0-3 even n8 tiles, warps 4-7 odd ones
-      const __nv_bfloat16* wr = st + (16 + n * 8 + g) * kRouterRow + kc;
-      uint32_t b[2] = {*reinterpret_cast<const uint32_t*>(wr), *reinterpret_cast<const uint32_t*>(wr + 8)};
-      mma_bf16_16816(acc[n], a, b);
-    }
-  }
-  cp_async_wait<0>();
-  // C fragment: rows g / g + 8, columns 2 * t4, 2 * t4 + 1 of each n8 tile; warps ks and
-  // ks + 4 own disjoint tiles, so part[ks] is written once per element
-#pragma unroll
-  for (int n = 0; n < NT; ++n) {
-    if ((n & 1) != (warp >> 2)) continue;
-    part[ks][g][n * 8 + 2 * t4] = acc[n][0];
-    part[ks][g][n * 8 + 2 * t4 + 1] = acc[n][1];
-    part[ks][g + 8][n * 8 + 2 * t4] = acc[n][2];
-    part[ks][g + 8][n * 8 + 2 * t4 + 1] = acc[n][3];
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < 16 * EN; i += blockDim.x) {
-    const int row = i / EN, col = i % EN;
-    float v = part[0][row][col] + part[1][row][col] + part[2][row][col] + part[3][row][col];
-    if (bias != nullptr) v += __bfloat162float(bias[n0 + col]);
-    lg[row][col] = v;
-  }
-  cl.sync();  // every CTA's logits are visible cluster-wide
-  // top-k: warp w of CTA r takes token rows r + CL * (w + 8 * i) of the tile
-  for (int row = r + CL * warp; row < 16; row += CL * 8) {
-    const int tok = m0 + row;
-    if (tok >= T) break;
-    constexpr int kMaxPer = 32;  // E <= 1024
-    float v[kMaxPer];
-    const int per_lane = (E + 31) / 32;
-#pragma unroll
-    for (int i = 0; i < kMaxPer; ++i) {
-      const int e = i * 32 + lane;
-      if (i < per_lane && e < E) {
-        const float* peer = cl.map_shared_rank(&lg[0][0], e / EN);
-        v[i] = peer[row * EN + e % EN];
-      } else {
-        v[i] = -INFINITY;
-      }
-    }
-    float sel_v[16];
-    int sel_i[16];
-    for (int j = 0; j < k; ++j) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
-#pragma unroll
-      for (int i = 0; i < kMaxPer; ++i) {
-        const int e = i * 32 + lane;
-        if (i < per_lane && e < E && (v[i] > bv || (v[i] == bv && e < bi))) {
-          bv = v[i];
-          bi = e;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) {
-          bv = ov;
-          bi = oi;
-        }
-      }
-      sel_v[j] = bv;
-      sel_i[j] = bi;
-#pragma unroll
-      for (int i = 0; i < kMaxPer; ++i)
-        if (i * 32 + lane == bi) v[i] = -INFINITY;
-    }
-    if (lane == 0) {
-      const float m = sel_v[0];
-      float sum = 0.f;
-      for (int j = 0; j < k; ++j) sum += __expf(sel_v[j] - m);
-      for (int j = 0; j < k; ++j) {
-        ids[(size_t)tok * k + j] = sel_i[j];
-        wts[(size_t)tok * k + j] = __expf(sel_v[j] - m) / sum;
-      }
-    }
-  }
-  cl.sync();  // peers' shared memory stays alive until every CTA has read it
 }
 
 // argmax: each CTA scans a slice of one row with 16-byte loads and folds its (value,
@@ -478,50 +309,6 @@ extern "C" int b200_topk_softmax(int* ids, float* weights, const void* logits, i
   else
     return kBadShape;
   return (int)cudaGetLastError();
-}
-
-extern "C" int b200_router_topk(int* ids, float* weights, const void* x, const void* w, const void* bias, int T,
-                                int H, int E, int k, cudaStream_t s) {
-  // CL CTAs per cluster cover E = CL * EN experts, EN in {16, 32, 64}, CL <= 8; K in 64-wide slabs
-  if (T < 0 || H % kRouterKC || k < 1 || k > 16 || k > E || E > 1024) return kBadShape;
-  if (T == 0) return 0;
-  int EN = 0;
-  for (int en : {16, 32, 64})
-    if (E % en == 0 && E / en <= 8) {
-      EN = en;
-      break;
-    }
-  if (EN == 0) return kBadShape;
-  const int CL = E / EN;
-  const size_t smem = (size_t)kRouterStages * (16 + EN) * kRouterRow * sizeof(__nv_bfloat16);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(CL, cdiv(T, 16));
-  cfg.blockDim = dim3(256);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = CL;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  const __nv_bfloat16* xb = (const __nv_bfloat16*)x;
-  const __nv_bfloat16* wb = (const __nv_bfloat16*)w;
-  const __nv_bfloat16* bb = (const __nv_bfloat16*)bias;
-  auto run = [&](auto kern) -> int {
-    static bool attr_set = false;  // host-side, once per instantiation
-    if (!attr_set) {
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      attr_set = true;
-    }
-    return (int)cudaLaunchKernelEx(&cfg, kern, ids, weights, xb, wb, bb, T, H, E, k);
-  };
-  if (EN == 16) return run(router_topk_kernel<16>);
-  if (EN == 32) return run(router_topk_kernel<32>);
-  return run(router_topk_kernel<64>);
 }
 
 extern "C" int b200_argmax(float* vals, int64_t* idx, const void* logits, int B, int V, int dtype, cudaStream_t s) {

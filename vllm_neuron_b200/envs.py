@@ -57,8 +57,6 @@ _REGISTRY: dict[str, tuple[Callable[[str], Any], str | None, str | None]] = {
     "VLLM_B200_SEQUENCE_PARALLEL": (_bool, "1", None),
     # Directory for golden logits used by accuracy tests.
     "VLLM_B200_GOLDEN_CACHE_DIR": (str, "", "VLLM_NEURON_GOLDEN_CACHE_DIR"),
-    # Router logits + top-k in one cluster kernel (else library GEMM + top-k kernel).
-    "VLLM_B200_FUSED_ROUTER": (_bool, "0", None),
     # Use the fused in-kernel NVLink collectives (else NCCL).
     "VLLM_B200_FUSED_COLLECTIVES": (_bool, "1", None),
     # Spin-wait bound (iterations) for device-side flag waits in fused collectives.

@@ -15,7 +15,6 @@ import math
 import torch
 import torch.nn.functional as F
 
-from .. import envs
 from . import reference as ref
 from ._ext import kernels_enabled, use_kernel  # noqa: F401
 from ._ext import ops as _k
@@ -254,18 +253,8 @@ def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqle
 
 
 def router_topk(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, top_k: int,
-                order: str = "topk_softmax", fused: bool | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+                order: str = "topk_softmax") -> tuple[torch.Tensor, torch.Tensor]:
     """(topk_ids [T,k] int32, topk_weights [T,k] fp32)."""
-    E, H = w.shape
-    fused_router = fused if fused is not None else envs.VLLM_B200_FUSED_ROUTER
-    if (fused_router and use_kernel(x) and order == "topk_softmax" and w.dtype == torch.bfloat16 and H % 64 == 0
-            and (b is None or b.dtype == torch.bfloat16) and top_k <= 16
-            and any(E % en == 0 and E // en <= 8 for en in (16, 32, 64))):
-        # one launch: tensor-core logits of a 16-token tile per cluster, top-k over DSMEM
-        ids = torch.empty(x.shape[0], top_k, dtype=torch.int32, device=x.device)
-        wts = torch.empty(x.shape[0], top_k, dtype=torch.float32, device=x.device)
-        _k().router_topk(ids, wts, x.to(w.dtype).contiguous(), w.contiguous(), b)
-        return ids, wts
     if use_kernel(x) and order == "topk_softmax" and w.shape[0] <= 1024:
         logits = F.linear(x.to(w.dtype), w, b)  # bf16 logits read directly by the top-k kernel
         if logits.dtype not in (torch.bfloat16, torch.float32):
