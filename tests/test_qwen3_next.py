@@ -46,8 +46,9 @@ def ckpt(tmp_path_factory):
     return str(path), m
 
 
-@pytest.mark.parametrize("tp,chunk,dp", [(1, 256, 1), (1, 24, 1), (2, 256, 1), (1, 24, 2)])
-def test_qwen3_next_greedy_matches_hf(ckpt, tp, chunk, dp):
+@pytest.mark.parametrize("tp,chunk,dp,a2a", [(1, 256, 1, None), (1, 24, 1, None), (2, 256, 1, None),
+                                             (1, 24, 2, None), (1, 24, 2, "naive"), (2, 256, 1, "naive")])
+def test_qwen3_next_greedy_matches_hf(ckpt, tp, chunk, dp, a2a):
     from vllm_neuron_b200 import LLM, SamplingParams
 
     path, hf = ckpt
@@ -58,7 +59,8 @@ def test_qwen3_next_greedy_matches_hf(ckpt, tp, chunk, dp):
             g = hf.generate(torch.tensor([p]), max_new_tokens=8, do_sample=False, pad_token_id=0, eos_token_id=None)
             want.append(g[0, len(p):].tolist())
     llm = LLM(model=path, dtype="float32", max_model_len=256, max_num_seqs=4, max_num_batched_tokens=chunk,
-              block_size=16, device="cpu", tensor_parallel_size=tp, data_parallel_size=dp)
+              block_size=16, device="cpu", tensor_parallel_size=tp, data_parallel_size=dp,
+              all2all_backend=a2a or "allgather_reducescatter")
     try:
         outs = llm.generate(prompt_token_ids=prompts,
                             sampling_params=SamplingParams(temperature=0, max_tokens=8, ignore_eos=True))

@@ -129,7 +129,7 @@ class Worker:
         supports it, when ``all2all_backend`` selects one and experts span several ranks."""
         from ..parallel.all2all import make_ep_all2all
 
-        layers = [m for m in model.modules() if hasattr(m, "a2a") and hasattr(m, "experts")]
+        layers = [m for m in model.modules() if hasattr(m, "a2a")]
         if not layers or self.cfg.all2all_backend == "allgather_reducescatter" or self.ps.world.world_size == 1:
             return
         a2a = make_ep_all2all(self.cfg.all2all_backend, self.ps.world, self.device, mcfg.hidden_size,

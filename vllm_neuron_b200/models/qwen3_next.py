@@ -266,25 +266,43 @@ class SparseMoE(nn.Module):
             if cfg.shared_expert_intermediate_size else None
         self.shared_gate = _param((1, H), dtype, device) if self.shared is not None else None
         self.mx = None  # MXFP8 kernel tensors (set after loading on a GPU for fp8 checkpoints)
+        # EP all-to-all (``parallel/all2all.py``), attached by the worker when
+        # ``all2all_backend`` asks for one; None: all-gather / reduce-scatter over DP
+        self.a2a = None
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def _route(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         k = self.cfg.num_experts_per_tok
-        xr = self.dp.all_gather(x, dim=0) if self.dp.world_size > 1 else x  # cross-DP expert parallelism
         if self.cfg.norm_topk_prob:
             # softmax -> top-k -> renormalise == softmax over the top-k logits
-            ids, wts = ops.router_topk(xr, self.router, None, k)
-        else:
-            p = torch.softmax(ops.linear(xr, self.router).float(), -1)
-            wts, ids = torch.topk(p, k, -1)
-            ids = ids.to(torch.int32)
+            return ops.router_topk(x, self.router, None, k)
+        p = torch.softmax(ops.linear(x, self.router).float(), -1)
+        wts, ids = torch.topk(p, k, -1)
+        return ids.to(torch.int32), wts
+
+    def _experts(self, x: torch.Tensor, ids: torch.Tensor, wts: torch.Tensor) -> torch.Tensor:
         H, I = self.cfg.hidden_size, self.cfg.moe_intermediate_size
         if self.mx is not None:  # MXFP8 experts (fp8 checkpoints on the GPU)
             t13, s13, t2, s2, b13, b2 = self.mx
-            out = ops.moe_mxfp4(xr, ids, wts, t13, s13, b13, t2, s2, b2, self.e0, 1.0, -1.0, H, I, fp4=False)
+            return ops.moe_mxfp4(x, ids, wts, t13, s13, b13, t2, s2, b2, self.e0, 1.0, -1.0, H, I, fp4=False)
+        return ops.moe_dense(x, ids, wts, self.w13, None, self.w2, None, self.e0, 1.0, None, False, "silu", H, I)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.a2a is not None:
+            # each TP rank sends its slice of the local tokens to the expert owners; zeros
+            # outside the slice keep the output a TP partial sum
+            from ..parallel.all2all import ep_slice
+
+            T = x.shape[0]
+            ids, wts = self._route(x)
+            t0, t1 = ep_slice(T, self.group.rank_in_group, self.group.world_size)
+            xr, ir, wr = self.a2a.dispatch(x, ids, wts, self.E_local, t0, t1)
+            out = self.a2a.combine(self._experts(xr, ir, wr), T)
         else:
-            out = ops.moe_dense(xr, ids, wts, self.w13, None, self.w2, None, self.e0, 1.0, None, False, "silu", H, I)
-        if self.dp.world_size > 1:
-            out = self.dp.reduce_scatter(out, dim=0)
+            xr = self.dp.all_gather(x, dim=0) if self.dp.world_size > 1 else x  # cross-DP expert parallelism
+            ids, wts = self._route(xr)
+            out = self._experts(xr, ids, wts)
+            if self.dp.world_size > 1:
+                out = self.dp.reduce_scatter(out, dim=0)
         if self.shared is not None:
             sg = ops.linear(x, self.shared_gate)
             out = ops.gated_add(out, self.shared(x), sg)
