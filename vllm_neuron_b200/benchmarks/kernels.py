@@ -17,6 +17,7 @@ layer shapes at TP=4):
   attn_prefill 1 x 2048-token prompt, 64 q / 8 kv heads, d=64
   gdn_prefill  8192-token prompt, 4 key / 8 value heads of 128 (Qwen3-Next TP=4)
   gdn_decode   64 sequences, 8 value heads of 128
+  kv_transfer  one 2048-token GPT-OSS-120B request: device export + import (disaggregated serving)
 """
 
 from __future__ import annotations
@@ -200,7 +201,44 @@ def _gdn(args, decode: bool):
     return fn, nbytes, flops, {"T": T, "B": B, "nk": nk, "nv": nv, "d": d}
 
 
+def _kv_transfer(args):
+    """Device KV transfer of one request (disaggregated serving): export from a paged cache
+    into a device pool + import into another cache (same GPU here; the decode engine reads the
+    pool over NVLink when it sits on another GPU).  GPT-OSS-120B shape at TP=1: 36 layers,
+    8 kv heads of 64, 2048 tokens, bf16."""
+    from vllm_neuron_b200.ops import _ext
+
+    _ext.load()
+    ops = torch.ops.b200
+    L, T, nh, d, bs = 36, args.L or 2048, 8, 64, 32
+    nb = T // bs
+    dev = "cuda"
+    src = [(torch.randn(nb + 1, nh, bs, d, device=dev).bfloat16(), torch.randn(nb + 1, nh, bs, d, device=dev).bfloat16())
+           for _ in range(L)]
+    dst = [(torch.zeros_like(k), torch.zeros_like(v)) for k, v in src]
+    kp = torch.tensor([k.data_ptr() for k, _ in src], dtype=torch.int64, device=dev)
+    vp = torch.tensor([v.data_ptr() for _, v in src], dtype=torch.int64, device=dev)
+    kq = torch.tensor([k.data_ptr() for k, _ in dst], dtype=torch.int64, device=dev)
+    vq = torch.tensor([v.data_ptr() for _, v in dst], dtype=torch.int64, device=dev)
+    blocks = torch.randperm(nb, device=dev).to(torch.int32) + 1
+    region = 2 * L * T * nh * d * 2
+    pool = ops.comm_alloc(region // 2 + 256)
+    base = pool + 64 * 1024
+    row = d * 2
+
+    def fn():
+        ops.kv_export(base, kp, vp, blocks, T, nh, row, bs)
+        ops.kv_import([base], [0], [nh], kq, vq, blocks, T, T, 0, nh, row, bs, None)
+
+    fn()
+    torch.cuda.synchronize()
+    k0 = src[5][0][blocks.long()].permute(0, 2, 1, 3)
+    assert torch.equal(k0, dst[5][0][blocks.long()].permute(0, 2, 1, 3)), "kv transfer mismatch"
+    return fn, 4 * region, 0, {"layers": L, "tokens": T, "kv_heads": nh, "d": d, "request_bytes": region}
+
+
 OPS = {
+    "kv_transfer": _kv_transfer,
     "moe_mxfp4": _moe_mxfp4,
     "moe_bf16": _moe_bf16,
     "attn_decode": _attn_decode,
