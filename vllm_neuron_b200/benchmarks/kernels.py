@@ -226,7 +226,9 @@ def _kv_transfer(args):
     base = pool + 64 * 1024
     row = d * 2
 
-    def fn():
+    keep = (src, dst)  # the pointer tables hold raw addresses: the caches must outlive fn
+
+    def fn(_keep=keep):
         ops.kv_export(base, kp, vp, blocks, T, nh, row, bs)
         ops.kv_import([base], [0], [nh], kq, vq, blocks, T, T, 0, nh, row, bs, None)
 
