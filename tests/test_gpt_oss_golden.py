@@ -51,16 +51,18 @@ def _hf_greedy(m, prompts, n_new):
     return outs
 
 
-@pytest.mark.parametrize("tp,dp,a2a,adp", [(1, 1, None, 1), (2, 1, None, 1), (1, 2, None, 1), (1, 2, "naive", 1),
-                                           (2, 1, "naive", 1), (1, 2, None, 2), (2, 2, None, 2)])
-def test_greedy_matches_hf(ckpt, tp, dp, a2a, adp, monkeypatch):
+@pytest.mark.parametrize("tp,dp,a2a,adp,dcp", [(1, 1, None, 1, 1), (2, 1, None, 1, 1), (1, 2, None, 1, 1),
+                                               (1, 2, "naive", 1, 1), (2, 1, "naive", 1, 1), (1, 2, None, 2, 1),
+                                               (2, 2, None, 2, 1), (4, 1, None, 1, 2)])
+def test_greedy_matches_hf(ckpt, tp, dp, a2a, adp, dcp, monkeypatch):
     """dp=2: two data-parallel replicas in lockstep with the experts shared across them
     (tokens all-gathered / reduce-scattered over DP around the MoE); 5 prompts so one
     replica runs padding steps while the other still works.  a2a: the EP all-to-all
     (each token sent only to the ranks owning its experts; under TP each rank sends a
     slice and the outputs are partial sums).  adp: attention DP (the model runs on every
     replica's tokens over the TP x DP supergroup; attention per replica after a batch <-> heads
-    all-to-all)."""
+    all-to-all).  dcp: decode context parallelism (the two TP ranks that replicate a kv head
+    split its tokens; sinks join the LSE merge once, windows are in global positions)."""
     from vllm_neuron_b200 import LLM, SamplingParams
     from vllm_neuron_b200.parallel import all2all
 
@@ -83,12 +85,12 @@ def test_greedy_matches_hf(ckpt, tp, dp, a2a, adp, monkeypatch):
 
     monkeypatch.setattr(pstate.GroupCoordinator, "all_to_all", spy_a2a)
     path, hf = ckpt
-    prompts = workload(n=4 if tp == 2 else (5 if dp == 2 else 6))
+    prompts = workload(n=4 if tp >= 2 else (5 if dp == 2 else 6))
     n_new = 16
     want = _hf_greedy(hf, prompts, n_new)
     llm = LLM(model=path, dtype="float32", max_model_len=512, max_num_seqs=16, max_num_batched_tokens=256,
               block_size=16, device="cpu", tensor_parallel_size=tp, data_parallel_size=dp,
-              all2all_backend=a2a or "allgather_reducescatter",
+              all2all_backend=a2a or "allgather_reducescatter", decode_context_parallel_size=dcp,
               additional_config={"neuron_config": {"quantization": "bf16", "attention_dp_size": adp}})
     try:
         outs = llm.generate(prompt_token_ids=prompts,
