@@ -76,17 +76,22 @@ class EpAll2All:
         return out
 
     def dispatch(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, E_local: int, t0: int, t1: int):
-        T, W = x.shape[0], self.world
+        # no host synchronisation (CUDA-graph safe): every (token, rank) pair is scattered,
+        # pairs that send nothing land in a dummy row T that is dropped
+        T, W, k = x.shape[0], self.world, ids.shape[1]
         send_idx = compact(ids, E_local, W, t0, t1)
         self._send_idx = send_idx
-        sx = torch.zeros(W, T, x.shape[1], dtype=x.dtype, device=x.device)
-        sid = torch.full((W, T, ids.shape[1]), -1, dtype=torch.int32, device=x.device)
-        sw = torch.zeros(W, T, ids.shape[1], dtype=torch.float32, device=x.device)
-        t_idx, d_idx = torch.nonzero(send_idx >= 0, as_tuple=True)
-        p = send_idx[t_idx, d_idx].long()
-        sx[d_idx, p] = x[t_idx]
-        sid[d_idx, p] = ids[t_idx].to(torch.int32)
-        sw[d_idx, p] = w[t_idx].float()
+        row = torch.where(send_idx >= 0, send_idx, torch.full_like(send_idx, T)).long()  # [T, W]
+        flat = (torch.arange(W, device=x.device) * (T + 1)).unsqueeze(0) + row  # [T, W]
+        flat = flat.reshape(-1)
+        sx = torch.zeros(W * (T + 1), x.shape[1], dtype=x.dtype, device=x.device)
+        sid = torch.full((W * (T + 1), k), -1, dtype=torch.int32, device=x.device)
+        sw = torch.zeros(W * (T + 1), k, dtype=torch.float32, device=x.device)
+        sx.index_copy_(0, flat, x.unsqueeze(1).expand(T, W, x.shape[1]).reshape(T * W, -1))
+        sid.index_copy_(0, flat, ids.to(torch.int32).unsqueeze(1).expand(T, W, k).reshape(T * W, k))
+        sw.index_copy_(0, flat, w.float().unsqueeze(1).expand(T, W, k).reshape(T * W, k))
+        # drop the dummy rows; rows no token was sent to keep their -1 ids
+        sx, sid, sw = (t.view(W, T + 1, -1)[:, :T] for t in (sx, sid, sw))
         rx, rid, rw = self._a2a(sx), self._a2a(sid), self._a2a(sw)
         return rx.view(W * T, -1), rid.view(W * T, -1), rw.view(W * T, -1)
 
@@ -94,10 +99,10 @@ class EpAll2All:
         W = self.world
         back = self._a2a(y_recv.view(W, T, -1))  # back[d, i]: rank d's output for my row i to d
         send_idx = self._send_idx
-        out = torch.zeros(T, y_recv.shape[-1], dtype=torch.float32, device=y_recv.device)
-        t_idx, d_idx = torch.nonzero(send_idx >= 0, as_tuple=True)
-        out.index_add_(0, t_idx, back[d_idx, send_idx[t_idx, d_idx].long()].float())
-        return out.to(y_recv.dtype)
+        valid = send_idx >= 0  # [T, W]
+        d_idx = torch.arange(W, device=back.device).unsqueeze(0).expand(T, W)
+        rows = back[d_idx, send_idx.clamp(min=0).long()].float()  # [T, W, H]
+        return (rows * valid.unsqueeze(-1)).sum(1).to(y_recv.dtype)
 
 
 class FusedEpAll2All:
