@@ -1,0 +1,110 @@
+"""Structured outputs on CPU: a tiny random Llama with a word-level tokenizer saved next to it;
+every constrained request's text must satisfy its regex / choice / grammar, at TP=1 and TP=2
+(gloo), greedy and sampled; constrained requests are refused when the feature is off."""
+
+import json
+import re
+
+import pytest
+import torch
+
+V = 512
+TOKS = [str(d) for d in range(10)] + list('{}":, ') + [chr(ord("a") + i) for i in range(26)] + ["true", "false", "null"]
+TOKS += [f"<x{i}>" for i in range(V - len(TOKS) - 2)] + ["<unk>", "</s>"]
+EOS = V - 1
+
+
+@pytest.fixture(scope="module")
+def ckpt(tmp_path_factory):
+    from tokenizers import Tokenizer, models
+    from transformers import LlamaConfig, LlamaForCausalLM, PreTrainedTokenizerFast
+
+    from vllm_neuron_b200.utils.checkpoints import save_state_dict
+
+    path = tmp_path_factory.mktemp("so")
+    torch.manual_seed(0)
+    cfg = LlamaConfig(vocab_size=V, hidden_size=64, intermediate_size=128, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=256,
+                      tie_word_embeddings=False, eos_token_id=EOS)
+    m = LlamaForCausalLM(cfg).eval().float()
+    d = cfg.to_dict()
+    d["architectures"] = ["LlamaForCausalLM"]
+    save_state_dict({k: v.detach().clone().contiguous() for k, v in m.state_dict().items()}, str(path), d)
+    tk = Tokenizer(models.WordLevel({t: i for i, t in enumerate(TOKS)}, unk_token="<unk>"))
+    PreTrainedTokenizerFast(tokenizer_object=tk, eos_token="</s>", unk_token="<unk>").save_pretrained(str(path))
+    return str(path)
+
+
+def _text(ids):
+    return "".join(TOKS[i] for i in ids if i != EOS)
+
+
+def _llm(path, tp=1, enabled=True):
+    from vllm_neuron_b200 import LLM
+
+    return LLM(model=path, dtype="float32", max_model_len=128, max_num_seqs=4, max_num_batched_tokens=64,
+               block_size=16, device="cpu", tensor_parallel_size=tp,
+               additional_config={"neuron_config": {"enable_structured_outputs": enabled}})
+
+
+CASES = [({"regex": "[a-c]{3}[0-9]{2}"}, lambda s: re.fullmatch("[a-c]{3}[0-9]{2}", s)),
+         ({"choice": ["yes", "no", "maybe"]}, lambda s: s in ("yes", "no", "maybe")),
+         ({"grammar": 'root ::= "{" [a-z] ":" [0-9] "}"'}, lambda s: re.fullmatch(r"\{[a-z]:[0-9]\}", s))]
+
+
+@pytest.mark.parametrize("tp", [1, 2])
+def test_constrained_outputs_follow_their_grammar(ckpt, tp):
+    from vllm_neuron_b200 import SamplingParams
+
+    llm = _llm(ckpt, tp)
+    prompts = [[11, 12, 13, 14, 20 + i] for i in range(len(CASES) * 2)]
+    params = []
+    for i in range(len(prompts)):
+        so, _ = CASES[i % len(CASES)]
+        params.append(SamplingParams(temperature=0 if i < len(CASES) else 0.9, seed=i, max_tokens=32,
+                                     structured_outputs=so))
+    try:
+        outs = llm.generate(prompt_token_ids=prompts, sampling_params=params)
+        free = llm.generate(prompt_token_ids=[prompts[0]],
+                            sampling_params=SamplingParams(temperature=0, max_tokens=8, ignore_eos=True))
+    finally:
+        llm.shutdown()
+    for i, o in enumerate(outs):
+        text = _text(o.outputs[0].token_ids)
+        assert CASES[i % len(CASES)][1](text), (i, text, o.outputs[0].token_ids)
+        assert o.outputs[0].finish_reason == "stop", o.outputs[0].finish_reason
+    assert len(free[0].outputs[0].token_ids) == 8  # an unconstrained request in the same engine
+
+
+def test_refused_when_disabled(ckpt):
+    from vllm_neuron_b200 import SamplingParams
+
+    llm = _llm(ckpt, enabled=False)
+    try:
+        with pytest.raises(ValueError, match="structured outputs are disabled"):
+            llm.generate(prompt_token_ids=[[1, 2, 3]],
+                         sampling_params=SamplingParams(max_tokens=4, structured_outputs={"regex": "a+"}))
+    finally:
+        llm.shutdown()
+
+
+def test_json_schema_bitmask():
+    import xgrammar as xgr
+
+    from vllm_neuron_b200.engine.structured_output import (StructuredOutputManager, StructuredOutputsParams,
+                                                            mask_logits)
+
+    mgr = StructuredOutputManager(xgr.TokenizerInfo(TOKS, stop_token_ids=[EOS]))
+    schema = {"type": "object", "properties": {"a": {"type": "integer"}}, "required": ["a"]}
+    m = mgr.matcher(StructuredOutputsParams.from_any({"json": json.dumps(schema)}))
+    for t in '{"a":12}':  # drive the matcher through a valid document, token by token
+        bm = mgr.bitmask([m])
+        logits = mask_logits(torch.zeros(1, V), bm, 0)
+        assert torch.isfinite(logits[0, TOKS.index(t)]), t
+        assert m.accept_token(TOKS.index(t))
+    bm = mgr.bitmask([m, None])
+    allowed = torch.isfinite(mask_logits(torch.zeros(2, V), bm, 0))
+    assert allowed[0, EOS] and not allowed[0, TOKS.index("a")]
+    assert allowed[1].all()  # rows without a grammar are unconstrained
+    # a vocabulary shard (TP): ids [256, 512) see the same bits
+    assert torch.equal(torch.isfinite(mask_logits(torch.zeros(2, 256), bm, 256)), allowed[:, 256:])

@@ -86,7 +86,9 @@ class LLMEngine:
         self._rr = 0
         self._remote: set[str] = set()  # unfinished requests owned by other replicas
         # asynchronous scheduling (single rank or SPMD; decode steps with CUDA graphs)
+        # (grammar masks need step k's token before step k + 1 is staged: no lookahead then)
         self._async = bool(cfg.async_scheduling) and self.dp == 1 and mode in ("single", "spmd") \
+            and not cfg.neuron_config.enable_structured_outputs \
             and self.proposer is None
         self._inflight = None
         self.async_stats = {"launched": 0, "lookahead": 0}
@@ -112,10 +114,34 @@ class LLMEngine:
         else:
             self._remote.add(req.request_id)
 
+    def structured_output_manager(self):
+        """Grammar compiler over this model's vocabulary (built on the first constrained
+        request from the model's tokenizer, or set by the caller as ``so_manager``).
+        Constrained requests are refused unless ``enable_structured_outputs`` is on, as in the
+        reference (``vllm/platform.py:396-435``)."""
+        if not self.cfg.neuron_config.enable_structured_outputs:
+            raise ValueError("structured outputs are disabled: set neuron_config.enable_structured_outputs")
+        if self.cfg.speculative_config is not None:
+            raise ValueError("structured outputs with speculative decoding are not supported")
+        if getattr(self, "so_manager", None) is None:
+            from transformers import AutoTokenizer
+
+            from .structured_output import StructuredOutputManager
+
+            if self.cfg.model is None:
+                raise ValueError("structured outputs need a tokenizer: load a model directory or set so_manager")
+            tok = AutoTokenizer.from_pretrained(self.cfg.model)
+            vocab = getattr(self.worker.model_cfg, "vocab_size", None) or self.worker.hf.get("vocab_size")
+            self.so_manager = StructuredOutputManager.from_tokenizer(tok, vocab)
+        return self.so_manager
+
     def _make_request(self, rid, prompt_token_ids, sampling_params, prompt, mm_inputs, kv_transfer_params) -> Request:
         ids = list(map(int, prompt_token_ids))
         req = Request(rid, ids, sampling_params, self.eos_token_id, prompt, mm_inputs=mm_inputs,
                       kv_transfer_params=kv_transfer_params)
+        so = getattr(sampling_params, "structured_outputs", None)
+        if so is not None:
+            req.grammar = self.structured_output_manager().matcher(so)
         model = self.worker.model
         if mm_inputs and hasattr(model, "embed_multimodal"):
             from ..models.qwen3_vl import preprocess_image

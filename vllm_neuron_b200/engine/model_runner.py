@@ -402,6 +402,7 @@ class ModelRunner:
             T += B - n
         greedy = self._fill_sampling(so, B)
         spec = so.kind == "decode" and any(s.spec_token_ids for s in seqs)
+        extras_so = self._grammar_mask(seqs, n_sel) if not spec else None
         if spec and not greedy:
             self._fill_spec_sampling(so, n_sel)
         extras = self._mm_extras(so) if (has_mrope and self.encoder_cache is not None) else {}
@@ -440,7 +441,21 @@ class ModelRunner:
             cp_group=self.cp_group)
         if spec:
             extras["spec"] = True
+        if extras_so is not None:
+            extras["token_bitmask"] = extras_so
         return meta, T, n_sel, greedy
+
+    def _grammar_mask(self, seqs, n_sel: int) -> torch.Tensor | None:
+        """Packed allowed-token bitmask [n_sel, words] of this step's sampled rows (one row per
+        sequence, in order; rows of unconstrained sequences and padding allow everything), or
+        None when no sequence carries a grammar."""
+        if not any(s.request is not None and s.request.grammar is not None for s in seqs):
+            return None
+        from .structured_output import fill_bitmask
+
+        matchers = [s.request.grammar if s.request is not None else None for s in seqs]
+        matchers += [None] * (n_sel - len(matchers))
+        return fill_bitmask(matchers[:n_sel], self.sampler.vocab_size).to(self.device)
 
     def _mm_extras(self, so: SchedulerOutput) -> dict:
         """Multimodal inputs of a prefill step: image rows from the encoder cache (encoding
@@ -506,6 +521,10 @@ class ModelRunner:
             return self.d_out[:0]
         hs = h if (meta.is_decode and n_sel == T) else h.index_select(0, meta.logits_indices)
         logits = self.model.compute_logits(hs)
+        if "token_bitmask" in meta.extras:  # structured outputs: this shard's disallowed ids -> -inf
+            from .structured_output import mask_logits
+
+            logits = mask_logits(logits, meta.extras["token_bitmask"], self.sampler.vocab_start)
         if not meta.extras.get("spec", False):  # one sampled token per row
             B = n_sel
             tok = self.sampler(logits, self.d_temp[:B], self.d_topk[:B], self.d_topp[:B], self.d_unif[:B], greedy)
@@ -547,6 +566,8 @@ class ModelRunner:
         if hs.shape[0] < R:
             hs = torch.cat([hs, hs.new_zeros(R - hs.shape[0], hs.shape[1])])
         logits = self.model.compute_logits(dpg.all_gather(hs, dim=0))
+        if "token_bitmask" in meta.extras:
+            raise NotImplementedError("structured outputs with lm_head / attention data parallelism")
         prm = [dpg.all_gather(t[:R], dim=0) for t in (self.d_temp, self.d_topk, self.d_topp, self.d_unif)]
         tok = self.sampler(logits, *prm, False)
         j = dpg.rank_in_group
@@ -576,7 +597,7 @@ class ModelRunner:
             pad_to = get_bucket_for_count(want, self.decode_buckets) if self.use_graphs else want
             NUM_SEQS_PADDING.labels(model_name=self.cfg.served_model_name or "model").observe(pad_to - n)
         meta, T, n_sel, greedy = self._prepare(so, pad_to, pad_tokens)
-        if is_plain_decode and self.use_graphs:
+        if is_plain_decode and self.use_graphs and "token_bitmask" not in meta.extras:
             key = (pad_to, greedy)
             entry = self.graphs.get(key)
             if entry is None:

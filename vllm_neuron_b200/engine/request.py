@@ -47,6 +47,7 @@ class Request:
     mrope_delta: int = 0  # decode rope position = cache position + delta
     kv_transfer_params_out: dict | None = None  # set by a KV-producer engine when the request finishes
     num_inflight: int = 0  # decode steps launched whose token is not yet known (async scheduling)
+    grammar: object = None  # structured-output matcher (xgrammar), fed every sampled token
 
     def __post_init__(self) -> None:
         self.metrics.arrival_time = self.arrival_time

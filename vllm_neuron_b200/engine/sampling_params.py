@@ -20,6 +20,9 @@ class SamplingParams:
     ignore_eos: bool = False
     logprobs: int | None = None
     detokenize: bool = False
+    # grammar constraint (``engine/structured_output.py``): a StructuredOutputsParams or a
+    # dict with one of json / regex / choice / grammar / json_object
+    structured_outputs: object = None
 
     def __post_init__(self) -> None:
         if self.temperature < 0:
@@ -32,6 +35,10 @@ class SamplingParams:
             raise ValueError("max_tokens must be >= 1")
         if self.n != 1:
             raise ValueError("n > 1 is not supported")
+        if self.structured_outputs is not None:
+            from .structured_output import StructuredOutputsParams
+
+            self.structured_outputs = StructuredOutputsParams.from_any(self.structured_outputs)
 
     @property
     def greedy(self) -> bool:

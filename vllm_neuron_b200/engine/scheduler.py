@@ -313,6 +313,10 @@ class Scheduler:
                 req.metrics.token_times.append(now)
                 if req.check_stop(self.max_model_len):
                     break
+                if req.grammar is not None:  # structured output: advance the grammar
+                    if not req.grammar.accept_token(int(t)) or req.grammar.is_terminated():
+                        req.status = RequestStatus.FINISHED_STOPPED
+                        break
             self.kv.cache_full_blocks(req)
             if req.status.finished:
                 done.append(req)
