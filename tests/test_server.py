@@ -76,3 +76,19 @@ def test_profiler_config_aliases():
     assert c.activities == ["cpu", "cuda"] and c.output_dir == "/tmp/x"
     with pytest.raises(ValueError):
         ProfilerConfig.from_dict({"activities": ["npu"]})
+
+
+def test_structured_output_request_fields():
+    from vllm_neuron_b200.entrypoints.openai_server import _sampling_from
+
+    def so(body):
+        p = _sampling_from(body).structured_outputs
+        return None if p is None else (p.json, p.regex, p.choice, p.grammar, p.json_object)
+
+    assert so({}) is None
+    assert so({"response_format": {"type": "json_object"}}) == (None, None, None, None, True)
+    schema = {"type": "object"}
+    assert so({"response_format": {"type": "json_schema", "json_schema": {"name": "x", "schema": schema}}})[0] == schema
+    assert so({"guided_regex": "a+"})[1] == "a+"
+    assert so({"guided_choice": ["a", "b"]})[2] == ["a", "b"]
+    assert so({"structured_outputs": {"grammar": 'root ::= "x"'}})[3] == 'root ::= "x"'

@@ -24,12 +24,31 @@ from ..logging_config import init_logger
 logger = init_logger(__name__)
 
 
+def _structured_from(body: dict) -> dict | None:
+    """OpenAI ``response_format`` (json_object / json_schema) and vLLM's ``structured_outputs``
+    / ``guided_json`` / ``guided_regex`` / ``guided_choice`` / ``guided_grammar`` fields."""
+    if body.get("structured_outputs"):
+        return dict(body["structured_outputs"])
+    rf = body.get("response_format") or {}
+    if rf.get("type") == "json_object":
+        return {"json_object": True}
+    if rf.get("type") == "json_schema":
+        js = rf.get("json_schema") or {}
+        return {"json": js.get("schema", js)}
+    for key, field in (("guided_json", "json"), ("guided_regex", "regex"), ("guided_choice", "choice"),
+                       ("guided_grammar", "grammar")):
+        if body.get(key) is not None:
+            return {field: body[key]}
+    return None
+
+
 def _sampling_from(body: dict) -> SamplingParams:
     return SamplingParams(
         temperature=float(body.get("temperature", 1.0)), top_p=float(body.get("top_p", 1.0)),
         top_k=int(body.get("top_k", 0) or 0), max_tokens=int(body.get("max_tokens", 16) or 16),
         min_tokens=int(body.get("min_tokens", 0) or 0), seed=body.get("seed"),
-        stop_token_ids=body.get("stop_token_ids"), ignore_eos=bool(body.get("ignore_eos", False)))
+        stop_token_ids=body.get("stop_token_ids"), ignore_eos=bool(body.get("ignore_eos", False)),
+        structured_outputs=_structured_from(body))
 
 
 def build_app(engine: AsyncLLM, served_name: str):
