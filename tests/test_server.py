@@ -92,3 +92,16 @@ def test_structured_output_request_fields():
     assert so({"guided_regex": "a+"})[1] == "a+"
     assert so({"guided_choice": ["a", "b"]})[2] == ["a", "b"]
     assert so({"structured_outputs": {"grammar": 'root ::= "x"'}})[3] == 'root ::= "x"'
+
+
+def test_logprobs_request_and_payload():
+    from vllm_neuron_b200.entrypoints.openai_server import _logprobs_from, _logprobs_payload
+
+    assert _logprobs_from({}) is None and _logprobs_from({"logprobs": 2}) == 2
+    assert _logprobs_from({"logprobs": True, "top_logprobs": 3}) == 3
+    detok = lambda ids: "".join(chr(97 + i) for i in ids)  # noqa: E731
+    entries = [{1: -0.1, 2: -2.0}, {0: -0.5}]
+    comp = _logprobs_payload([1, 0], entries, detok, chat=False)
+    assert comp["tokens"] == ["b", "a"] and comp["token_logprobs"] == [-0.1, -0.5]
+    chat = _logprobs_payload([1, 0], entries, detok, chat=True)
+    assert chat["content"][0]["top_logprobs"] == [{"token": "c", "logprob": -2.0}]

@@ -1,6 +1,7 @@
 """Block manager (prefix caching), scheduler policy and request lifecycle."""
 
 import pytest
+import torch
 
 from vllm_neuron_b200.engine.block_manager import KVCacheManager
 from vllm_neuron_b200.engine.request import Request, RequestStatus
@@ -124,3 +125,41 @@ def test_async_scheduling_matches_sync(temperature):
             assert eng.async_stats["lookahead"] > 10, eng.async_stats
         llm.shutdown()
     assert outs[True] == outs[False]
+
+
+@pytest.mark.parametrize("tp", [1, 2])
+def test_logprobs_match_reference(tmp_path, tp):
+    """Top-N logprobs of the raw logits and the sampled token's logprob, over the vocab shards
+    (TP=2 gathers them), against HF transformers' log-softmax at every generated position."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from vllm_neuron_b200 import LLM, SamplingParams
+    from vllm_neuron_b200.utils.checkpoints import save_state_dict
+
+    torch.manual_seed(0)
+    cfg = LlamaConfig(vocab_size=1001, hidden_size=64, intermediate_size=128, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=256,
+                      tie_word_embeddings=False)
+    cfg._attn_implementation = "eager"
+    hf = LlamaForCausalLM(cfg).eval().float()
+    d = cfg.to_dict()
+    d["architectures"] = ["LlamaForCausalLM"]
+    save_state_dict({k: v.detach().clone().contiguous() for k, v in hf.state_dict().items()}, str(tmp_path), d)
+    prompt = [5, 17, 300, 42, 7, 999]
+    llm = LLM(model=str(tmp_path), dtype="float32", max_model_len=128, max_num_seqs=2, max_num_batched_tokens=64,
+              block_size=16, device="cpu", tensor_parallel_size=tp)
+    try:
+        out = llm.generate(prompt_token_ids=[prompt],
+                           sampling_params=SamplingParams(temperature=0.7, seed=3, max_tokens=5, ignore_eos=True,
+                                                          logprobs=3))[0].outputs[0]
+    finally:
+        llm.shutdown()
+    assert len(out.logprobs) == len(out.token_ids) == 5
+    ids = torch.tensor([prompt + out.token_ids[:-1]])
+    with torch.no_grad():
+        lp = torch.log_softmax(hf(ids).logits[0, len(prompt) - 1:].float(), -1)
+    for j, (t, entry) in enumerate(zip(out.token_ids, out.logprobs)):
+        assert abs(entry[t] - lp[j, t].item()) < 1e-3
+        top = lp[j].topk(3)
+        for v, i in zip(top.values.tolist(), top.indices.tolist()):
+            assert abs(entry[i] - v) < 1e-3, (j, i, entry)

@@ -139,6 +139,13 @@ class LLMEngine:
         ids = list(map(int, prompt_token_ids))
         req = Request(rid, ids, sampling_params, self.eos_token_id, prompt, mm_inputs=mm_inputs,
                       kv_transfer_params=kv_transfer_params)
+        n_lp = sampling_params.logprobs
+        if n_lp is not None:
+            limit = self.cfg.neuron_config.max_logprobs or 20
+            if n_lp < 0 or n_lp > limit:
+                raise ValueError(f"logprobs must be in [0, {limit}] (neuron_config.max_logprobs)")
+            if self.proposer is not None:
+                raise ValueError("logprobs with speculative decoding are not supported")
         so = getattr(sampling_params, "structured_outputs", None)
         if so is not None:
             req.grammar = self.structured_output_manager().matcher(so)
@@ -329,6 +336,10 @@ class LLMEngine:
             sampled = self.proposer.execute_with_speculation(so)
         else:
             sampled = self.worker.runner.execute(so, dp_pad=dp_pad) if dp_pad else self.worker.execute_model(so)
+            for rid, entry in getattr(self.worker.runner, "last_logprobs", {}).items():
+                req = self.scheduler.requests.get(rid)
+                if req is not None:
+                    req.logprobs.append(entry)
         now = time.monotonic()
         finished = self.scheduler.update_from_output(so, sampled, now)
         if self.proposer is not None:
@@ -350,7 +361,9 @@ class LLMEngine:
         elif req.status == RequestStatus.FINISHED_ABORTED:
             reason = "abort"
         return RequestOutput(req.request_id, req.prompt, req.prompt_token_ids,
-                             [CompletionOutput(0, "", list(req.output_token_ids), reason)], finished,
+                             [CompletionOutput(0, "", list(req.output_token_ids), reason,
+                                               list(req.logprobs) if req.sampling_params.logprobs is not None
+                                               else None)], finished,
                              req.metrics, req.num_cached_tokens, req.kv_transfer_params_out)
 
     # ------------------------------------------------------------------ scoring

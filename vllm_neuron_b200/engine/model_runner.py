@@ -443,6 +443,11 @@ class ModelRunner:
             extras["spec"] = True
         if extras_so is not None:
             extras["token_bitmask"] = extras_so
+        if not spec:
+            lp = [s.request.sampling_params.logprobs for s in seqs
+                  if s.request is not None and s.request.sampling_params.logprobs is not None]
+            if lp:
+                extras["logprobs_k"] = max(lp)
         return meta, T, n_sel, greedy
 
     def _grammar_mask(self, seqs, n_sel: int) -> torch.Tensor | None:
@@ -521,6 +526,7 @@ class ModelRunner:
             return self.d_out[:0]
         hs = h if (meta.is_decode and n_sel == T) else h.index_select(0, meta.logits_indices)
         logits = self.model.compute_logits(hs)
+        raw = logits
         if "token_bitmask" in meta.extras:  # structured outputs: this shard's disallowed ids -> -inf
             from .structured_output import mask_logits
 
@@ -538,7 +544,34 @@ class ModelRunner:
             tok, _ = rejection_sample(cv, ci, pp[3].long(), pp[0], pp[1].int(), pp[2], pp[4], pp[5], self.max_top_k)
         self.d_out[:n_sel].copy_(tok)
         self._last_logits = logits
+        if "logprobs_k" in meta.extras:
+            self._last_lp = self._logprobs(raw, tok, int(meta.extras["logprobs_k"]))
         return self.d_out[:n_sel]
+
+    def _logprobs(self, logits: torch.Tensor, tok: torch.Tensor, k: int):
+        """Log-probabilities of the raw model logits (before temperature, top-k/p and grammar
+        masks, as vLLM reports them) over the vocabulary shards of the sampler group: the
+        sampled token's and the top ``k`` (ids, values).  Returns host lists per row."""
+        g = self.sampler.group
+        lf = self.sampler._mask_padding(logits.float())
+        lse = torch.logsumexp(lf, -1)
+        start = self.sampler.vocab_start
+        V = lf.shape[1]
+        inside = (tok >= start) & (tok < start + V)
+        t_logit = torch.where(inside, lf.gather(1, (tok - start).clamp(0, V - 1).long()[:, None]).squeeze(1),
+                              torch.full_like(lse, float("-inf")))
+        kk = min(k, V) if k > 0 else 0
+        vals, ids = (torch.topk(lf, kk, -1) if kk else (lf[:, :0], lf[:, :0].long()))
+        ids = ids + start
+        if g.world_size > 1:
+            lse = torch.logsumexp(g.all_gather(lse.unsqueeze(0), dim=0), 0)
+            t_logit = g.all_gather(t_logit.unsqueeze(0), dim=0).amax(0)
+            if kk:
+                av = g.all_gather(vals.unsqueeze(0), dim=0).permute(1, 0, 2).reshape(lf.shape[0], -1)
+                ai = g.all_gather(ids.unsqueeze(0), dim=0).permute(1, 0, 2).reshape(lf.shape[0], -1)
+                vals, pos = torch.topk(av, min(k, av.shape[1]), -1)
+                ids = ai.gather(1, pos)
+        return ((t_logit - lse).tolist(), (vals - lse[:, None]).tolist(), ids.tolist())
 
     def _forward_attention_dp(self, meta: AttentionMetadata, T: int) -> torch.Tensor:
         """Attention DP: gather the token ids and positions of the a replicas (every replica
@@ -597,7 +630,8 @@ class ModelRunner:
             pad_to = get_bucket_for_count(want, self.decode_buckets) if self.use_graphs else want
             NUM_SEQS_PADDING.labels(model_name=self.cfg.served_model_name or "model").observe(pad_to - n)
         meta, T, n_sel, greedy = self._prepare(so, pad_to, pad_tokens)
-        if is_plain_decode and self.use_graphs and "token_bitmask" not in meta.extras:
+        if (is_plain_decode and self.use_graphs and "token_bitmask" not in meta.extras
+                and "logprobs_k" not in meta.extras):
             key = (pad_to, greedy)
             entry = self.graphs.get(key)
             if entry is None:
@@ -633,9 +667,16 @@ class ModelRunner:
                 res[s.req_id] = toks[off:off + k]
                 off += k
             return res
+        lp = self.__dict__.pop("_last_lp", None)
+        self.last_logprobs = {}
         for i, s in enumerate(so.seqs):
             if s.sample:
                 res[s.req_id] = [toks[i]]
+                if lp is not None and s.request is not None and s.request.sampling_params.logprobs is not None:
+                    n = s.request.sampling_params.logprobs
+                    entry = {int(t): float(v) for t, v in zip(lp[2][i][:n], lp[1][i][:n])}
+                    entry[int(toks[i])] = float(lp[0][i])
+                    self.last_logprobs[s.req_id] = entry
         return res
 
     @torch.inference_mode()
@@ -655,7 +696,9 @@ class ModelRunner:
     # ---------------------------------------------------------- async decode steps
     def can_launch_async(self, so: SchedulerOutput) -> bool:
         return (so.kind == "decode" and bool(so.seqs) and self.capture is None and self.replacer is None
-                and all(len(s.token_ids) == 1 and not s.spec_token_ids for s in so.seqs))
+                and all(len(s.token_ids) == 1 and not s.spec_token_ids for s in so.seqs)
+                and not any(s.request is not None and (s.request.sampling_params.logprobs is not None
+                                                       or s.request.grammar is not None) for s in so.seqs))
 
     def _event(self):
         if self.device.type == "cuda":

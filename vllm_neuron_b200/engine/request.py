@@ -48,6 +48,7 @@ class Request:
     kv_transfer_params_out: dict | None = None  # set by a KV-producer engine when the request finishes
     num_inflight: int = 0  # decode steps launched whose token is not yet known (async scheduling)
     grammar: object = None  # structured-output matcher (xgrammar), fed every sampled token
+    logprobs: list = field(default_factory=list)  # per output token {token id: logprob} (SamplingParams.logprobs)
 
     def __post_init__(self) -> None:
         self.metrics.arrival_time = self.arrival_time

@@ -48,7 +48,28 @@ def _sampling_from(body: dict) -> SamplingParams:
         top_k=int(body.get("top_k", 0) or 0), max_tokens=int(body.get("max_tokens", 16) or 16),
         min_tokens=int(body.get("min_tokens", 0) or 0), seed=body.get("seed"),
         stop_token_ids=body.get("stop_token_ids"), ignore_eos=bool(body.get("ignore_eos", False)),
-        structured_outputs=_structured_from(body))
+        structured_outputs=_structured_from(body), logprobs=_logprobs_from(body))
+
+
+def _logprobs_from(body: dict) -> int | None:
+    """completions: ``logprobs: N``; chat: ``logprobs: true`` + ``top_logprobs: N``."""
+    lp = body.get("logprobs")
+    if lp is True:
+        return int(body.get("top_logprobs") or 0)
+    if lp is None or lp is False:
+        return None
+    return int(lp)
+
+
+def _logprobs_payload(token_ids, entries, detok, chat: bool) -> dict | None:
+    if entries is None:
+        return None
+    if chat:
+        return {"content": [{"token": detok([t]), "logprob": e.get(t),
+                             "top_logprobs": [{"token": detok([i]), "logprob": v} for i, v in e.items() if i != t]}
+                            for t, e in zip(token_ids, entries)]}
+    return {"tokens": [detok([t]) for t in token_ids], "token_logprobs": [e.get(t) for t, e in zip(token_ids, entries)],
+            "top_logprobs": [{detok([i]): v for i, v in e.items()} for e in entries]}
 
 
 def build_app(engine: AsyncLLM, served_name: str):
@@ -127,8 +148,10 @@ def build_app(engine: AsyncLLM, served_name: str):
         async for o in engine.generate(ids, sp, rid, kv_transfer_params=kvp):
             final = o
         toks = final.outputs[0].token_ids
+        ch = choice(detok(toks), toks, final.outputs[0].finish_reason)
+        ch["logprobs"] = _logprobs_payload(toks, final.outputs[0].logprobs, detok, chat)
         resp = {"id": rid, "object": obj, "created": created, "model": served_name,
-                "choices": [choice(detok(toks), toks, final.outputs[0].finish_reason)],
+                "choices": [ch],
                 "usage": {"prompt_tokens": len(ids), "completion_tokens": len(toks),
                           "total_tokens": len(ids) + len(toks)}}
         if final.kv_transfer_params is not None:
