@@ -108,3 +108,28 @@ def test_json_schema_bitmask():
     assert allowed[1].all()  # rows without a grammar are unconstrained
     # a vocabulary shard (TP): ids [256, 512) see the same bits
     assert torch.equal(torch.isfinite(mask_logits(torch.zeros(2, 256), bm, 256)), allowed[:, 256:])
+
+
+@pytest.mark.parametrize("include", [False, True])
+def test_stop_strings_cut_generation(ckpt, include):
+    from transformers import AutoTokenizer
+
+    from vllm_neuron_b200 import SamplingParams
+
+    tok = AutoTokenizer.from_pretrained(ckpt)
+    llm = _llm(ckpt, enabled=False)
+    prompt = [11, 12, 13, 14, 30]
+    try:
+        full = llm.generate(prompt_token_ids=[prompt],
+                            sampling_params=SamplingParams(temperature=0, max_tokens=20, ignore_eos=True))[0]
+        ids = full.outputs[0].token_ids
+        text = tok.decode(ids, skip_special_tokens=True)
+        stop = tok.decode(ids[4:6], skip_special_tokens=True)
+        cut = llm.generate(prompt_token_ids=[prompt],
+                           sampling_params=SamplingParams(temperature=0, max_tokens=20, ignore_eos=True, stop=[stop],
+                                                          include_stop_str_in_output=include))[0].outputs[0]
+    finally:
+        llm.shutdown()
+    p = text.find(stop)
+    assert cut.finish_reason == "stop" and len(cut.token_ids) <= 6
+    assert cut.text == text[:p + (len(stop) if include else 0)]

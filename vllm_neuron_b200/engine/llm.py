@@ -111,7 +111,8 @@ class LLM:
             try:
                 tok = self.get_tokenizer()
                 for o in outs:
-                    o.outputs[0].text = tok.decode(o.outputs[0].token_ids)
+                    if not isinstance(o.outputs[0].stop_reason, str):  # a stop string already cut the text
+                        o.outputs[0].text = tok.decode(o.outputs[0].token_ids)
             except Exception:  # noqa: BLE001
                 pass
         return outs

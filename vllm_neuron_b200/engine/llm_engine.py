@@ -31,6 +31,28 @@ from .worker import Worker
 logger = init_logger(__name__)
 
 
+def make_stop_checker(tok, stops: list[str], include: bool):
+    """Callable(request) -> True once the decoded output contains a stop string; it sets the
+    request's ``stop_reason`` (the string) and ``stop_text`` (the output cut before it, or after
+    it with ``include``).  Only the new tail of the text is searched each step."""
+    longest = max(len(x) for x in stops)
+
+    def check(req) -> bool:
+        text = tok.decode(req.output_token_ids, skip_special_tokens=True)
+        start = max(0, getattr(req, "_stop_scanned", 0) - longest)
+        req._stop_scanned = len(text)
+        hits = [(text.find(x, start), x) for x in stops]
+        hits = [(p, x) for p, x in hits if p >= 0]
+        if not hits:
+            return False
+        p, x = min(hits)
+        req.stop_reason = x
+        req.stop_text = text[:p + (len(x) if include else 0)]
+        return True
+
+    return check
+
+
 class LLMEngine:
     def __init__(self, cfg: EngineConfig, rank: int = 0, world_size: int = 1, local_rank: int = 0,
                  mode: str = "single"):
@@ -124,16 +146,22 @@ class LLMEngine:
         if self.cfg.speculative_config is not None:
             raise ValueError("structured outputs with speculative decoding are not supported")
         if getattr(self, "so_manager", None) is None:
-            from transformers import AutoTokenizer
-
             from .structured_output import StructuredOutputManager
 
-            if self.cfg.model is None:
-                raise ValueError("structured outputs need a tokenizer: load a model directory or set so_manager")
-            tok = AutoTokenizer.from_pretrained(self.cfg.model)
             vocab = getattr(self.worker.model_cfg, "vocab_size", None) or self.worker.hf.get("vocab_size")
-            self.so_manager = StructuredOutputManager.from_tokenizer(tok, vocab)
+            self.so_manager = StructuredOutputManager.from_tokenizer(self.tokenizer(), vocab)
         return self.so_manager
+
+    def tokenizer(self):
+        """The model directory's tokenizer (loaded on first use: stop strings, structured
+        outputs); a caller may set ``engine.hf_tokenizer`` instead."""
+        if getattr(self, "hf_tokenizer", None) is None:
+            from transformers import AutoTokenizer
+
+            if self.cfg.model is None:
+                raise ValueError("stop strings / structured outputs need a tokenizer: load a model directory")
+            self.hf_tokenizer = AutoTokenizer.from_pretrained(self.cfg.model)
+        return self.hf_tokenizer
 
     def _make_request(self, rid, prompt_token_ids, sampling_params, prompt, mm_inputs, kv_transfer_params) -> Request:
         ids = list(map(int, prompt_token_ids))
@@ -149,6 +177,9 @@ class LLMEngine:
         so = getattr(sampling_params, "structured_outputs", None)
         if so is not None:
             req.grammar = self.structured_output_manager().matcher(so)
+        if sampling_params.stop:
+            req.stop_checker = make_stop_checker(self.tokenizer(), sampling_params.stop,
+                                                 sampling_params.include_stop_str_in_output)
         model = self.worker.model
         if mm_inputs and hasattr(model, "embed_multimodal"):
             from ..models.qwen3_vl import preprocess_image
@@ -361,9 +392,9 @@ class LLMEngine:
         elif req.status == RequestStatus.FINISHED_ABORTED:
             reason = "abort"
         return RequestOutput(req.request_id, req.prompt, req.prompt_token_ids,
-                             [CompletionOutput(0, "", list(req.output_token_ids), reason,
+                             [CompletionOutput(0, req.stop_text or "", list(req.output_token_ids), reason,
                                                list(req.logprobs) if req.sampling_params.logprobs is not None
-                                               else None)], finished,
+                                               else None, req.stop_reason)], finished,
                              req.metrics, req.num_cached_tokens, req.kv_transfer_params_out)
 
     # ------------------------------------------------------------------ scoring

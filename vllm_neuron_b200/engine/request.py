@@ -40,7 +40,7 @@ class Request:
     num_cached_tokens: int = 0  # prefix-cache hit length at first schedule
     spec_token_ids: list[int] = field(default_factory=list)
     metrics: RequestMetrics = field(default_factory=RequestMetrics)
-    stop_reason: int | None = None
+    stop_reason: int | str | None = None
     sample_seq: int = 0  # deterministic per-request RNG counter
     mm_items: list | None = None  # [{"pixels", "grid", "offset", "n"}] image placeholders in the prompt
     mrope_positions: object = None  # [3, prompt_len] multimodal positions (Qwen3-VL)
@@ -49,6 +49,8 @@ class Request:
     num_inflight: int = 0  # decode steps launched whose token is not yet known (async scheduling)
     grammar: object = None  # structured-output matcher (xgrammar), fed every sampled token
     logprobs: list = field(default_factory=list)  # per output token {token id: logprob} (SamplingParams.logprobs)
+    stop_checker: object = None  # stop strings: callable(request) -> True when one appeared
+    stop_text: str | None = None  # output text cut at the stop string that ended the request
 
     def __post_init__(self) -> None:
         self.metrics.arrival_time = self.arrival_time

@@ -23,6 +23,10 @@ class SamplingParams:
     # grammar constraint (``engine/structured_output.py``): a StructuredOutputsParams or a
     # dict with one of json / regex / choice / grammar / json_object
     structured_outputs: object = None
+    # stop strings: generation ends when the decoded output contains one (the text is cut
+    # before it unless include_stop_str_in_output)
+    stop: list[str] | str | None = None
+    include_stop_str_in_output: bool = False
 
     def __post_init__(self) -> None:
         if self.temperature < 0:
@@ -35,6 +39,10 @@ class SamplingParams:
             raise ValueError("max_tokens must be >= 1")
         if self.n != 1:
             raise ValueError("n > 1 is not supported")
+        if isinstance(self.stop, str):
+            self.stop = [self.stop]
+        if self.stop is not None:
+            self.stop = [x for x in self.stop if x]
         if self.structured_outputs is not None:
             from .structured_output import StructuredOutputsParams
 
@@ -52,6 +60,7 @@ class CompletionOutput:
     token_ids: list[int]
     finish_reason: str | None = None
     logprobs: list | None = None
+    stop_reason: int | str | None = None  # the stop token id or stop string that ended the request
 
 
 @dataclass

@@ -317,6 +317,9 @@ class Scheduler:
                     if not req.grammar.accept_token(int(t)) or req.grammar.is_terminated():
                         req.status = RequestStatus.FINISHED_STOPPED
                         break
+                if req.stop_checker is not None and req.stop_checker(req):  # a stop string appeared
+                    req.status = RequestStatus.FINISHED_STOPPED
+                    break
             self.kv.cache_full_blocks(req)
             if req.status.finished:
                 done.append(req)

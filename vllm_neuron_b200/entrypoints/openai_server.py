@@ -48,7 +48,8 @@ def _sampling_from(body: dict) -> SamplingParams:
         top_k=int(body.get("top_k", 0) or 0), max_tokens=int(body.get("max_tokens", 16) or 16),
         min_tokens=int(body.get("min_tokens", 0) or 0), seed=body.get("seed"),
         stop_token_ids=body.get("stop_token_ids"), ignore_eos=bool(body.get("ignore_eos", False)),
-        structured_outputs=_structured_from(body), logprobs=_logprobs_from(body))
+        structured_outputs=_structured_from(body), logprobs=_logprobs_from(body), stop=body.get("stop"),
+        include_stop_str_in_output=bool(body.get("include_stop_str_in_output", False)))
 
 
 def _logprobs_from(body: dict) -> int | None:
@@ -148,7 +149,8 @@ def build_app(engine: AsyncLLM, served_name: str):
         async for o in engine.generate(ids, sp, rid, kv_transfer_params=kvp):
             final = o
         toks = final.outputs[0].token_ids
-        ch = choice(detok(toks), toks, final.outputs[0].finish_reason)
+        c0 = final.outputs[0]
+        ch = choice(c0.text if isinstance(c0.stop_reason, str) else detok(toks), toks, c0.finish_reason)
         ch["logprobs"] = _logprobs_payload(toks, final.outputs[0].logprobs, detok, chat)
         resp = {"id": rid, "object": obj, "created": created, "model": served_name,
                 "choices": [ch],
