@@ -133,3 +133,27 @@ def test_proxy_routes_prefill_then_decode(tmp_path):
     finally:
         pe.shutdown()
         de.shutdown()
+
+
+def test_decode_bench_connector_skips_prefill(tmp_path):
+    """Decode-only benchmarking: every prompt is admitted as prefilled (its KV filled with
+    noise), so each request computes only its last prompt token and then decodes."""
+    from vllm_neuron_b200 import LLM, SamplingParams
+
+    llm = LLM(hf_config={"architectures": ["LlamaForCausalLM"], "vocab_size": 512, "hidden_size": 64,
+                         "intermediate_size": 128, "num_hidden_layers": 2, "num_attention_heads": 4,
+                         "num_key_value_heads": 2, "max_position_embeddings": 256},
+              load_format="dummy", dtype="float32", max_model_len=256, max_num_seqs=4, max_num_batched_tokens=256,
+              block_size=16, device="cpu",
+              kv_transfer_config={"kv_connector": "NeuronDecodeBenchConnector", "kv_role": "kv_consumer"})
+    prompts = [list(range(1, 100)), list(range(5, 40))]
+    try:
+        outs = llm.generate(prompt_token_ids=prompts,
+                            sampling_params=SamplingParams(temperature=0, max_tokens=5, ignore_eos=True))
+        st = llm.engine.connector.stats
+    finally:
+        llm.shutdown()
+    for o, p in zip(outs, prompts):
+        assert len(o.outputs[0].token_ids) == 5
+        assert o.num_cached_tokens == len(p) - 1
+    assert st["loaded"] == 2

@@ -258,6 +258,8 @@ class Scheduler:
 
     def _remote_prefill_tokens(self, req: Request) -> int:
         p = req.kv_transfer_params or {}
+        if self.connector is not None and getattr(self.connector, "prefill_all", False):
+            return max(0, req.num_prompt_tokens - 1)  # decode benchmarking: every prompt counts as prefilled
         if self.connector is None or not self.connector.is_consumer or not p.get("do_remote_prefill"):
             return 0
         return max(0, min(int(p.get("num_tokens", 0)), req.num_prompt_tokens) - 1)

@@ -319,14 +319,58 @@ class B200IpcConnector(HostStagedConnector):
             pass
 
 
+class DecodeBenchConnector:
+    """Decode-only benchmarking (the reference's ``NeuronDecodeBenchConnector``,
+    ``vllm/kv_connector/neuron_decode_bench_connector.py``): every request is admitted as if
+    its prompt had been prefilled elsewhere, so the engine runs no prefill and the first step of
+    a request is a one-token decode.  ``load`` writes normal noise (``fill_mean``, ``fill_std``;
+    default 0, 1) into the request's cache blocks on the device so attention reads finite values;
+    the decode cost does not depend on the values.  ``fill: false`` leaves the blocks as they
+    are."""
+
+    prefill_all = True
+    is_producer = False
+    is_consumer = True
+
+    def __init__(self, kv_caches: list, block_size: int, extra: dict | None = None):
+        extra = extra or {}
+        self.kv = kv_caches
+        self.bs = block_size
+        self.fill = bool(extra.get("fill", True))
+        self.mean = float(extra.get("fill_mean", 0.0))
+        self.std = float(extra.get("fill_std", 1.0))
+        self.stats = {"exported": 0, "loaded": 0, "failed": 0, "bytes": 0}
+
+    def export(self, request_id: str, block_ids: list[int], num_tokens: int) -> dict:
+        return {}
+
+    def load(self, params: dict, block_ids: list[int], num_tokens: int) -> None:
+        self.stats["loaded"] += 1
+        if not self.fill or num_tokens <= 0:
+            return
+        nb = -(-num_tokens // self.bs)
+        for kv in self.kv:
+            if not isinstance(kv, tuple):
+                continue
+            for c in kv:
+                idx = torch.tensor(block_ids[:nb], dtype=torch.long, device=c.device)
+                noise = torch.randn((nb,) + tuple(c.shape[1:]), device=c.device) * self.std + self.mean
+                c.index_copy_(0, idx, noise.to(c.dtype))
+
+    def cleanup(self) -> None:
+        return None
+
+
 def make_connector(cfg, runner, rank: int, tp_size: int, kv_head_range: tuple[int, int]):
     kt = cfg.kv_transfer_config
     if kt is None:
         return None
     name = kt.kv_connector
+    extra = dict(kt.kv_connector_extra_config or {})
+    if name in ("DecodeBenchConnector", "NeuronDecodeBenchConnector"):
+        return DecodeBenchConnector(runner.kv_caches, cfg.block_size, extra)
     if name not in ("B200IpcConnector", "HostStagedConnector", "NixlConnector", "NeuronNixlConnector"):
         raise ValueError(f"unsupported kv_connector {name!r}")
-    extra = dict(kt.kv_connector_extra_config or {})
     engine_id = extra.get("engine_id") or f"eng{os.getpid()}"
     kv0 = next((kv for kv in runner.kv_caches if kv is not None), None)
     on_gpu = kv0 is not None and kv0[0].is_cuda
