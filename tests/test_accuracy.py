@@ -91,3 +91,34 @@ def test_kv_gather_matches_reference_write():
     ref.write_kv_cache(k, v, kc, vc, slots)
     gk, gv = gather_request_kv(kc, vc, blocks, L)
     assert compare_kv(gk, k)["max_abs"] == 0 and compare_kv(gv, v)["first_bad_position"] is None
+
+
+def test_tensor_compare_three_way_and_captures(tmp_path):
+    import os
+
+    from vllm_neuron_b200.accuracy.report import export_html, export_json
+    from vllm_neuron_b200.accuracy.tensor_compare import (align_shapes, bhattacharyya, compare_captures,
+                                                          compare_tensors, compare_tensors_three_way, report)
+    from vllm_neuron_b200.accuracy.tensor_histogram import TensorHistogram, box_table
+
+    torch.manual_seed(0)
+    ref = torch.randn(64, 128)
+    bf = ref.bfloat16().float()  # same-precision baseline
+    good = ref.bfloat16().float() + 1e-4 * torch.randn_like(ref)
+    bad = ref + 0.3 * torch.randn_like(ref)
+    assert compare_tensors(good, ref, "good").passed and not compare_tensors(bad, ref, "bad").passed
+    assert compare_tensors_three_way(good, bf, ref).passed and not compare_tensors_three_way(bad, bf, ref).passed
+    assert bhattacharyya(ref, ref) > 0.999 and bhattacharyya(ref, ref + 100) < 0.01
+    a, b = align_shapes(torch.zeros(1, 8, 4), torch.zeros(6, 4))  # padded capture vs real rows
+    assert a.shape == b.shape == (6, 4)
+    for d, t in (("a", good), ("b", ref)):
+        os.makedirs(tmp_path / d)
+        torch.save({"meta": {}, "tensors": {"layers.0": t, "norm": t * 2}}, tmp_path / d / "step_00000_rank0.pt")
+    res, agg = compare_captures(str(tmp_path / "a"), str(tmp_path / "b"))
+    assert agg.n == 2 and agg.n_failed == 0 and "2/2 passed" in report(res, agg)
+    export_json(res, str(tmp_path / "r.json"))
+    export_html(res, str(tmp_path / "r.html"))
+    assert "<table>" in open(tmp_path / "r.html").read()
+    h = TensorHistogram(torch.tensor([0.0, 1.0, 3.0, float("nan"), -0.25]), "x")
+    assert h.nan == 1 and h.zeros == 1 and h.buckets == {-2: 1, 0: 1, 1: 1}
+    assert "x" in h.render() and "p99" in box_table([h])

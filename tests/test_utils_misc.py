@@ -1,6 +1,7 @@
 """Host utilities: cgroup-aware memory, dtypes, vision block packing, golden cache, topology
 parsing (CPU only)."""
 
+import pytest
 import torch
 
 
@@ -58,3 +59,37 @@ def test_topology_parse():
     assert [x.index for x in g] == [0, 1] and g[0].peer_links == {1: "NV18"}
     assert g[0].nics == ["NIC0"] and g[1].nics == [] and g[0].numa_node == 0 and g[1].cpu_affinity == "56-111"
     assert all_nvlink(g)
+
+
+def test_device_allocator_contiguous_and_reclaims(tmp_path):
+    import json
+
+    from vllm_neuron_b200.utils.device_allocator import DeviceAllocator
+
+    state = str(tmp_path / "dev.json")
+    with open(state, "w") as f:
+        json.dump({"0": 2 ** 22 + 12345}, f)  # a dead owner: reclaimed
+    a = DeviceAllocator(4, state)
+    assert a.acquire(2) == [0, 1]
+    b = DeviceAllocator(4, state)
+    assert b.acquire(2) == [2, 3]
+    with pytest.raises(TimeoutError):
+        DeviceAllocator(4, state).acquire(1, timeout_s=0.2, poll_s=0.05)
+    a.release()
+    assert DeviceAllocator(4, state).acquire(2) == [0, 1]
+
+
+def test_spec_decode_utils():
+    import torch
+
+    from vllm_neuron_b200.utils.spec_decode_utils import (compute_token_indices_to_sample, extract_next_token_ids,
+                                                          replicate_per_seq_rows)
+
+    last, cnt = extract_next_token_ids(torch.tensor([[10, 20, -1], [5, -1, -1], [7, 99999, 3]]), 32000)
+    assert last.tolist() == [20, 5, 7] and cnt.tolist() == [2, 1, 1]
+    last, cnt = extract_next_token_ids([[1, 2], [3]], 100)
+    assert last.tolist() == [2, 3] and cnt.tolist() == [2, 1]
+    idx = compute_token_indices_to_sample(torch.tensor([3, 7]), torch.tensor([3, 0]), torch.tensor([2, 1]))
+    assert idx.tolist() == [1, 7]
+    r = replicate_per_seq_rows(torch.tensor([[1.0, 2.0], [3.0, 4.0]]), 3)
+    assert torch.equal(r, torch.tensor([[1.0, 2.0]] * 3 + [[3.0, 4.0]] * 3))
