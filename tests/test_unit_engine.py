@@ -163,3 +163,25 @@ def test_logprobs_match_reference(tmp_path, tp):
         top = lp[j].topk(3)
         for v, i in zip(top.values.tolist(), top.indices.tolist()):
             assert abs(entry[i] - v) < 1e-3, (j, i, entry)
+
+
+def test_parallel_sampling_n(tmp_path):
+    """n > 1: n completions per prompt with distinct samples; greedy children agree."""
+    from vllm_neuron_b200 import LLM, SamplingParams
+
+    llm = LLM(hf_config={"architectures": ["LlamaForCausalLM"], "vocab_size": 512, "hidden_size": 64,
+                         "intermediate_size": 128, "num_hidden_layers": 2, "num_attention_heads": 4,
+                         "num_key_value_heads": 2, "max_position_embeddings": 256},
+              load_format="dummy", dtype="float32", max_model_len=256, max_num_seqs=8, max_num_batched_tokens=256,
+              block_size=16, device="cpu", enable_prefix_caching=True)
+    try:
+        outs = llm.generate(prompt_token_ids=[[1, 2, 3, 4], [9, 8]],
+                            sampling_params=[SamplingParams(n=4, temperature=1.0, seed=1, max_tokens=8,
+                                                            ignore_eos=True),
+                                             SamplingParams(n=2, temperature=0, max_tokens=8, ignore_eos=True)])
+    finally:
+        llm.shutdown()
+    assert [len(o.outputs) for o in outs] == [4, 2]
+    assert [c.index for c in outs[0].outputs] == [0, 1, 2, 3]
+    assert len({tuple(c.token_ids) for c in outs[0].outputs}) > 1
+    assert outs[1].outputs[0].token_ids == outs[1].outputs[1].token_ids

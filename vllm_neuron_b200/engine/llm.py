@@ -16,6 +16,20 @@ from .sampling_params import RequestOutput, SamplingParams
 logger = init_logger(__name__)
 
 
+def merge_samples(request_id: str, outs: list[RequestOutput]) -> RequestOutput:
+    """One RequestOutput with the n completions of a prompt (index = sample number)."""
+    if len(outs) == 1:
+        return outs[0]
+    first = outs[0]
+    comps = []
+    for j, o in enumerate(outs):
+        c = o.outputs[0]
+        c.index = j
+        comps.append(c)
+    return RequestOutput(request_id, first.prompt, first.prompt_token_ids, comps, all(o.finished for o in outs),
+                         first.metrics, first.num_cached_tokens, first.kv_transfer_params)
+
+
 class LLM:
     """Example::
 
@@ -91,28 +105,33 @@ class LLM:
         if sampling_params is None:
             sampling_params = SamplingParams()
         sps = list(sampling_params) if isinstance(sampling_params, (list, tuple)) else [sampling_params] * n
-        ids = []
+        ids = []  # per prompt: the request ids of its n samples
         for i, ptoks in enumerate(prompt_token_ids):
             rid = f"req-{self._counter}"
             self._counter += 1
             mm = multi_modal_data[i] if multi_modal_data else None
-            self.engine.add_request(rid, list(ptoks), sps[i], prompt=prompts[i] if prompts else None,
-                                    mm_inputs=[mm] if mm else None,
-                                    kv_transfer_params=kvps[i] if kvps else None)
-            ids.append(rid)
+            # parallel sampling: n child requests of one prompt (their request-keyed uniforms
+            # differ, and with prefix caching they share the prompt's KV blocks)
+            children = [rid] if sps[i].n == 1 else [f"{rid}#{j}" for j in range(sps[i].n)]
+            for cid in children:
+                self.engine.add_request(cid, list(ptoks), sps[i], prompt=prompts[i] if prompts else None,
+                                        mm_inputs=[mm] if mm else None,
+                                        kv_transfer_params=kvps[i] if kvps else None)
+            ids.append(children)
         results: dict[str, RequestOutput] = {}
         while self.engine.has_unfinished_requests():
             for o in self.engine.step():
                 if o.finished:
                     results[o.request_id] = o
-        outs = [results[r] for r in ids]
+        outs = [merge_samples(rid[0].split("#")[0], [results[c] for c in rid]) for rid in ids]
         if self._tok is not None or (self._tok_path and os.path.exists(os.path.join(self._tok_path,
                                                                                     "tokenizer.json"))):
             try:
                 tok = self.get_tokenizer()
                 for o in outs:
-                    if not isinstance(o.outputs[0].stop_reason, str):  # a stop string already cut the text
-                        o.outputs[0].text = tok.decode(o.outputs[0].token_ids)
+                    for c in o.outputs:
+                        if not isinstance(c.stop_reason, str):  # a stop string already cut the text
+                            c.text = tok.decode(c.token_ids)
             except Exception:  # noqa: BLE001
                 pass
         return outs

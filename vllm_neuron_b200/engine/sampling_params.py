@@ -37,8 +37,8 @@ class SamplingParams:
             raise ValueError("top_k must be -1, 0 or positive")
         if self.max_tokens is not None and self.max_tokens < 1:
             raise ValueError("max_tokens must be >= 1")
-        if self.n != 1:
-            raise ValueError("n > 1 is not supported")
+        if self.n < 1:
+            raise ValueError("n must be >= 1")
         if isinstance(self.stop, str):
             self.stop = [self.stop]
         if self.stop is not None:

@@ -9,6 +9,7 @@ plugin mapped them to its device profiler, ``vllm/worker/neuron_profiler.py:52``
 
 from __future__ import annotations
 
+import asyncio
 import json
 import os
 import time
@@ -49,6 +50,7 @@ def _sampling_from(body: dict) -> SamplingParams:
         min_tokens=int(body.get("min_tokens", 0) or 0), seed=body.get("seed"),
         stop_token_ids=body.get("stop_token_ids"), ignore_eos=bool(body.get("ignore_eos", False)),
         structured_outputs=_structured_from(body), logprobs=_logprobs_from(body), stop=body.get("stop"),
+        n=int(body.get("n", 1) or 1),
         include_stop_str_in_output=bool(body.get("include_stop_str_in_output", False)))
 
 
@@ -129,6 +131,8 @@ def build_app(engine: AsyncLLM, served_name: str):
                         "token_ids": token_ids}
             return {"index": 0, "text": text, "finish_reason": finish, "token_ids": token_ids}
 
+        if stream and sp.n > 1:
+            return JSONResponse({"error": "n > 1 is not supported with stream=true"}, status_code=400)
         if stream:
             async def gen():
                 sent = 0
@@ -145,6 +149,25 @@ def build_app(engine: AsyncLLM, served_name: str):
                 yield "data: [DONE]\n\n"
 
             return StreamingResponse(gen(), media_type="text/event-stream")
+        if sp.n > 1:  # parallel sampling: n child requests, one choice each
+            async def one(j):
+                last = None
+                async for o in engine.generate(ids, sp, f"{rid}#{j}", kv_transfer_params=kvp):
+                    last = o
+                return last
+
+            finals = await asyncio.gather(*[one(j) for j in range(sp.n)])
+            chs = []
+            for j, f in enumerate(finals):
+                c = f.outputs[0]
+                ch = choice(c.text if isinstance(c.stop_reason, str) else detok(c.token_ids), c.token_ids,
+                            c.finish_reason)
+                ch["index"] = j
+                ch["logprobs"] = _logprobs_payload(c.token_ids, c.logprobs, detok, chat)
+                chs.append(ch)
+            n_out = sum(len(f.outputs[0].token_ids) for f in finals)
+            return {"id": rid, "object": obj, "created": created, "model": served_name, "choices": chs,
+                    "usage": {"prompt_tokens": len(ids), "completion_tokens": n_out, "total_tokens": len(ids) + n_out}}
         final = None
         async for o in engine.generate(ids, sp, rid, kv_transfer_params=kvp):
             final = o
