@@ -77,3 +77,34 @@ def test_executor_detects_dead_and_stalled_ranks():
     with pytest.raises(RankError) as ei:
         ex.run(_stall_on_0)
     assert ei.value.rank == 0 and time.monotonic() - t0 < 20
+
+
+def _ep_a2a_case(ctx, T, t0, t1):
+    from vllm_neuron_b200.parallel.all2all import EpAll2All
+
+    W, H, k, E = ctx.ps.world.world_size, 16, 2, 8
+    E_local = E // W
+    g = torch.Generator().manual_seed(10 + ctx.rank)
+    x = torch.randn(T, H, generator=g)
+    ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32)
+    w = torch.rand(T, k, generator=g)
+    a2a = EpAll2All(ctx.ps.world, H, k)
+    xr, ir, wr = a2a.dispatch(x, ids, w, E_local, t0, t1)
+    off = ctx.rank * E_local
+    local = (ir >= off) & (ir < off + E_local)
+    yr = xr * torch.where(local, wr * (ir.float() + 1), torch.zeros_like(wr)).sum(-1, keepdim=True)
+    out = a2a.combine(yr, T)
+    want = x * (w * (ids.float() + 1)).sum(-1, keepdim=True)
+    want[:t0] = 0
+    want[t1:] = 0
+    return (out - want).abs().max().item()
+
+
+def test_collective_all2all_matches_math():
+    """The collective EP all-to-all (gloo): dispatch to expert owners, per-rank experts,
+    combine; whole batch and a TP-style slice."""
+    from vllm_neuron_b200.utils.executor import MPExecutor
+
+    with MPExecutor(world_size=2, tp=2, timeout_s=120) as ex:
+        assert max(ex.run(_ep_a2a_case, 9, 0, 9)) < 1e-5
+        assert max(ex.run(_ep_a2a_case, 9, 2, 6)) < 1e-5
