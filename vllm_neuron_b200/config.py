@@ -90,6 +90,9 @@ class NeuronConfig:
     embedding_dp_size: int = 1
     lm_head_dp_size: int = 1
     mlp_dp_size: int = 1
+    # accepted for compatibility: with decode_context_parallel_size > 1 every prefill chunk
+    # already attends through the DCP shards (queries gathered, LSE merge), so there is no
+    # separate prefill DCP mode to switch on
     apply_prefill_dcp: bool = False
     on_device_sampling_config: OnDeviceSamplingConfig | None = field(default_factory=OnDeviceSamplingConfig)
     max_logprobs: int = 0
