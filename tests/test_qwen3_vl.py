@@ -92,10 +92,10 @@ def test_vl_generation_through_engine():
 
     cfg = dict(HF_KW)
     cfg["architectures"] = ["Qwen3VLForConditionalGeneration"]
-    img = torch.rand(3, 64, 96) * 255
+    img = torch.rand(3, 128, 160) * 255  # grid 8 x 10 patches: 20 merged tokens at prompt rows 3..22
     prompt = [5, 6, 1001, 1000, 1002, 7, 8, 9]
     outs = []
-    for chunk in (16, 256):  # 16: the 24 image tokens span two prefill segments
+    for chunk in (16, 256):  # 16: the image tokens span two prefill segments
         llm = LLM(hf_config=cfg, load_format="dummy", dtype="float32", max_model_len=256, max_num_seqs=2,
                   max_num_batched_tokens=chunk, block_size=16, device="cpu", seed=1)
         o = llm.generate([{"prompt_token_ids": prompt, "multi_modal_data": {"image": img}}],
@@ -104,3 +104,30 @@ def test_vl_generation_through_engine():
         assert llm.engine.worker.runner.encoder_cache.num_free == llm.engine.worker.runner.encoder_cache.buf.shape[0]
         llm.shutdown()
     assert outs[0] == outs[1] and len(outs[0]) == 6
+
+
+def test_vl_oversized_image_refused_at_request_time():
+    """An image with more vision tokens than the configured maximum (largest
+    num_vision_tokens_buckets entry) is refused by add_request with a ValueError before any
+    scheduling; a smaller image on the same engine still runs and frees its cache blocks."""
+    import pytest
+
+    from vllm_neuron_b200 import LLM, SamplingParams
+
+    cfg = dict(HF_KW)
+    cfg["architectures"] = ["Qwen3VLForConditionalGeneration"]
+    llm = LLM(hf_config=cfg, load_format="dummy", dtype="float32", max_model_len=256, max_num_seqs=2,
+              max_num_batched_tokens=256, block_size=16, device="cpu", seed=1,
+              additional_config={"vision_neuron_config": {"num_vision_tokens_buckets": [4]}})
+    assert llm.engine.max_embeds_per_image() == 4
+    prompt = [5, 6, 1001, 1000, 1002, 7, 8, 9]
+    big = torch.rand(3, 64, 96) * 255  # grid 4 x 6 patches: 6 merged tokens
+    with pytest.raises(ValueError, match="exceeds the maximum"):
+        llm.generate([{"prompt_token_ids": prompt, "multi_modal_data": {"image": big}}],
+                     SamplingParams(temperature=0, max_tokens=2))
+    assert not llm.engine.has_unfinished_requests()
+    small = torch.rand(3, 64, 64) * 255  # grid 4 x 4 patches: 4 merged tokens
+    o = llm.generate([{"prompt_token_ids": prompt, "multi_modal_data": {"image": small}}],
+                     SamplingParams(temperature=0, max_tokens=2, ignore_eos=True))
+    assert len(o[0].outputs[0].token_ids) == 2
+    llm.shutdown()

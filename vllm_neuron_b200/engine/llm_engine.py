@@ -163,6 +163,17 @@ class LLMEngine:
             self.hf_tokenizer = AutoTokenizer.from_pretrained(self.cfg.model)
         return self.hf_tokenizer
 
+    def max_embeds_per_image(self) -> int | None:
+        """Largest image (in merged vision tokens) a request may carry: the largest
+        ``num_vision_tokens_buckets`` entry when buckets are configured, else what the whole
+        encoder cache holds.  None for text-only models."""
+        ec = getattr(self.worker.runner, "encoder_cache", None)
+        if ec is None:
+            return None
+        cap = ec.buf.shape[0] * ec.block_size
+        buckets = self.cfg.vision_neuron_config.num_vision_tokens_buckets
+        return min(cap, max(buckets)) if buckets else cap
+
     def _make_request(self, rid, prompt_token_ids, sampling_params, prompt, mm_inputs, kv_transfer_params) -> Request:
         ids = list(map(int, prompt_token_ids))
         req = Request(rid, ids, sampling_params, self.eos_token_id, prompt, mm_inputs=mm_inputs,
@@ -193,6 +204,14 @@ class LLMEngine:
             img_tok = model.vl_cfg.image_token_id
             grids = [preprocess_image(torch_image(im), model.vl_cfg.vision)[1] for im in images]
             counts = [model.num_image_tokens(g) for g in grids]
+            cap = self.max_embeds_per_image()
+            for n in counts:
+                if cap is not None and n > cap:
+                    # refused before scheduling, so an oversized image never reaches the encoder
+                    # cache mid-step (vllm_neuron/vllm/platform.py:396 validate_request)
+                    raise ValueError(f"an image in this request produces {n} embedding tokens, which exceeds the "
+                                     f"maximum of the vision encoder cache ({cap}); reduce the image resolution "
+                                     f"or raise vision_neuron_config.max_vision_seq_len / num_vision_tokens_buckets")
             n_ph = sum(1 for t in ids if t == img_tok)
             out, items, gi, i = [], [], 0, 0
             if n_ph == len(grids):  # one placeholder per image: expand each to its token count
