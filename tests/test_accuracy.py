@@ -122,3 +122,142 @@ def test_tensor_compare_three_way_and_captures(tmp_path):
     h = TensorHistogram(torch.tensor([0.0, 1.0, 3.0, float("nan"), -0.25]), "x")
     assert h.nan == 1 and h.zeros == 1 and h.buckets == {-2: 1, 0: 1, 1: 1}
     assert "x" in h.render() and "p99" in box_table([h])
+
+
+def _hf_greedy_fn(hf, n_new):
+    """generate_fn over an HF model: greedy continuation of every sequence, logits [n, B, V]."""
+    base = {}
+
+    def fn(ids):
+        base.setdefault("n", len(ids[0]))
+        n = n_new - (len(ids[0]) - base["n"])
+        rows = []
+        with torch.no_grad():
+            for x in ids:
+                seq, out = list(x), []
+                for _ in range(n):
+                    lg = hf(torch.tensor([seq])).logits[0, -1].float()
+                    out.append(lg)
+                    seq.append(int(lg.argmax()))
+                rows.append(torch.stack(out))
+        return torch.stack(rows, 1)
+
+    return fn
+
+
+def test_debug_logits_dump_matches_hf(llama, tmp_path):
+    """neuron_config.debug_logits_dir: one file per sampling step; rows at positions
+    prompt_len - 1 ... carry the decode path's full-vocab logits (chunked prefill writes no
+    partial-chunk rows), equal to the HF model's teacher-forced logits."""
+    from vllm_neuron_b200 import LLM, SamplingParams
+    from vllm_neuron_b200.engine.debug_logits import read_debug_logits, stack_debug_logits
+
+    path, hf = llama
+    d = str(tmp_path / "logits")
+    llm = LLM(model=path, dtype="float32", max_model_len=256, max_num_seqs=2, max_num_batched_tokens=16,
+              block_size=16, device="cpu", additional_config={"neuron_config": {"debug_logits_dir": d}})
+    try:
+        prompts = [[5, 9, 100, 7, 3], list(range(20, 45))]  # the second prefills in two chunks
+        outs = llm.generate(prompt_token_ids=prompts,
+                            sampling_params=SamplingParams(temperature=0, max_tokens=4, ignore_eos=True))
+    finally:
+        llm.shutdown()
+    got = read_debug_logits(d)
+    assert [sorted(v) for _, v in sorted(got.items())] == [[4, 5, 6, 7], [24, 25, 26, 27]]
+    lg = stack_debug_logits(d)
+    assert lg.shape[:2] == (4, 2)
+    for b, (p, o) in enumerate(zip(prompts, outs)):
+        toks = list(o.outputs[0].token_ids)
+        assert lg[:, b].argmax(-1).tolist() == toks
+        with torch.no_grad():
+            want = hf(torch.tensor([p + toks])).logits[0, len(p) - 1:len(p) + 3].float()
+        assert torch.allclose(lg[:, b], want, atol=1e-4), (lg[:, b] - want).abs().max()
+
+
+def test_logit_validation_tiers_divergence_three_way():
+    """Teacher-forced validator on synthetic logits: identical logits pass; a constant offset is
+    removed; noise beyond the top-5 tier fails; a flipped near-tie within one bf16 ULP passes
+    and is re-prompted with the teacher token; three-way metrics against fp32 logits."""
+    from vllm_neuron_b200.accuracy.logit_validation import check_token_logits, logit_validation, ulp
+
+    assert ulp(19.0) == 0.125 and ulp(1.0, 23) == 2.0 ** -23
+    torch.manual_seed(0)
+    S, B, V = 6, 2, 64
+    exp = torch.randn(S, B, V) * 4
+    calls = []
+
+    def fn_from(actual):
+        def fn(ids):
+            done = len(ids[0]) - 3
+            calls.append(done)
+            return actual[done:]
+        return fn
+
+    ids = [[1, 2, 3], [4, 5, 6]]
+    assert logit_validation(ids, fn_from(exp.clone()), exp).passed
+    assert ids == [[1, 2, 3], [4, 5, 6]]  # caller's lists untouched
+    assert logit_validation(ids, fn_from(exp + 2.5), exp).passed  # constant offset removed
+    noisy = exp.clone()
+    top = exp[3, 1].topk(2).indices
+    noisy[3, 1, top[1]] -= 0.5  # the second-best entry off by 0.5 / max|e| ~ 5%: over the top-5 tier
+    r = logit_validation(ids, fn_from(noisy), exp)
+    assert not r.passed and [(t.batch, t.index) for t in r.failures()] == [(1, 3)]
+    # a near-tie flipped by less than one bf16 ULP: divergent but in bounds
+    tie = exp.clone()
+    w = exp[2, 0].argmax()
+    other = (w + 1) % V
+    tie[2, 0, other] = tie[2, 0, w] + ulp(float(tie[2, 0, w])) / 4
+    exp2 = tie.clone()
+    exp2[2, 0, other] = tie[2, 0, w] - ulp(float(tie[2, 0, w])) / 4
+    calls.clear()
+    r = logit_validation(ids, fn_from(tie), exp2)
+    assert r.passed and sum(t.divergence for t in r.tokens[0]) == 1
+    assert calls == [0, 3]  # re-prompted after the divergent position
+    # a flip by many ULPs fails
+    far = exp.clone()
+    far[2, 0, other] = far[2, 0, w] + 1.0
+    assert not logit_validation(ids, fn_from(far), exp).passed
+    # three-way: target error like the expected tensor's own error vs fp32 -> metrics pass
+    fp32 = exp.clone()
+    low = fp32.bfloat16().float()
+    tgt = (fp32 + 1e-3 * torch.randn_like(fp32)).bfloat16().float()
+    r = logit_validation(ids, fn_from(tgt), low, baseline_logits=fp32)
+    tw = [t.three_way for row in r.tokens for t in row]
+    assert all(m is not None for m in tw) and sum(m["passed"] for m in tw) >= len(tw) // 2
+    c = check_token_logits(exp[0, 0], exp[0, 0], actual_token=int(exp[0, 0].argmax()))
+    assert c.passed and not c.divergence and c.shift == pytest.approx(0.0, abs=1e-5)
+
+
+def test_multi_prompt_and_engine_generate_fn(llama, tmp_path):
+    """Engine (real decode path via its logit dumps) against HF fp32 with teacher forcing,
+    over two prompts, with HF in float64 as the three-way baseline; and one prompt replicated
+    to a batch of three."""
+    import copy
+
+    from vllm_neuron_b200 import LLM
+    from vllm_neuron_b200.accuracy import make_engine_generate_fn, multi_prompt_logit_validation
+
+    path, hf = llama
+    hf64 = copy.deepcopy(hf).double()
+    d = str(tmp_path / "dbg")
+    llm = LLM(model=path, dtype="float32", max_model_len=256, max_num_seqs=4, max_num_batched_tokens=64,
+              block_size=16, device="cpu", additional_config={"neuron_config": {"debug_logits_dir": d}})
+    try:
+        prompts = [[[5, 9, 100, 7, 3]], [list(range(30, 50)), list(range(60, 70))]]
+        expected = [_hf_greedy_fn(hf, 5)(p) for p in prompts]
+        fp64 = [_hf_greedy_fn(hf64, 5)(p).float() for p in prompts]
+        for p, e in zip(prompts, expected):  # engine vs HF fp32: two-way
+            r = multi_prompt_logit_validation([p], make_engine_generate_fn(llm, 5, d), [e])
+            assert r.passed, r.per_prompt[0].summary()
+        r = multi_prompt_logit_validation(prompts, make_engine_generate_fn(llm, 5, d), expected,
+                                          prompts_baseline_logits=fp64)
+        assert r.passed, [x.summary() for x in r.per_prompt]
+        agg = r.aggregate
+        assert set(agg) >= {"pp_static_0.03", "pp_max_linf_1.5x", "agg_bc", "agg_sigma_ratio", "per_token_bc"}
+        assert len(agg["per_token_bc"]) == 5 and 0 < agg["agg_sigma_ratio"] < float("inf")
+        rep = multi_prompt_logit_validation([prompts[0]], make_engine_generate_fn(llm, 5, d), [expected[0]],
+                                            replicate_to_batch_size=3)
+        assert rep.passed and len(rep.per_prompt[0].tokens) == 3
+    finally:
+        llm.shutdown()
+

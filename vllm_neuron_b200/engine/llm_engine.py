@@ -86,6 +86,9 @@ class LLMEngine:
                                    cfg.max_num_prefills_per_step, cfg.enable_chunked_prefill, k)
         if self.worker.runner.encoder_cache is not None:
             self.scheduler.on_finish.append(self.worker.runner.encoder_cache.release)
+        if self.worker.runner.debug_logits is not None:
+            self.worker.runner.debug_logits.replica = rank // cfg.tensor_parallel_size
+            self.scheduler.on_finish.append(self.worker.runner.debug_logits.release)
         if self.worker.runner.state_caches is not None:
             self.scheduler.on_finish.append(self.worker.runner.release_state)
             self.scheduler.on_preempt.append(self.worker.runner.release_state)

@@ -188,6 +188,13 @@ class ModelRunner:
             self.d_sslot = torch.zeros(B, dtype=torch.int32, device=d)
             self.d_sinit = torch.zeros(B, dtype=torch.int32, device=d)
         self.h2d_bytes_last = 0
+        self.debug_logits = None
+        if nc.debug_logits_dir:
+            if self.lm_dp is not None:
+                raise NotImplementedError("debug_logits_dir with lm_head data parallelism")
+            from .debug_logits import DebugLogitsWriter
+
+            self.debug_logits = DebugLogitsWriter(nc.debug_logits_dir, self.sampler.group, vocab_size)
         self.d2h_bytes_last = 0
         self.step_count = 0
         # accuracy tooling: tensor capture / replacement hooks (eager steps only)
@@ -448,6 +455,8 @@ class ModelRunner:
                   if s.request is not None and s.request.sampling_params.logprobs is not None]
             if lp:
                 extras["logprobs_k"] = max(lp)
+        if self.debug_logits is not None:
+            extras["debug_logits"] = True
         return meta, T, n_sel, greedy
 
     def _grammar_mask(self, seqs, n_sel: int) -> torch.Tensor | None:
@@ -544,6 +553,8 @@ class ModelRunner:
             tok, _ = rejection_sample(cv, ci, pp[3].long(), pp[0], pp[1].int(), pp[2], pp[4], pp[5], self.max_top_k)
         self.d_out[:n_sel].copy_(tok)
         self._last_logits = logits
+        if "debug_logits" in meta.extras:
+            self._last_raw = raw
         if "logprobs_k" in meta.extras:
             self._last_lp = self._logprobs(raw, tok, int(meta.extras["logprobs_k"]))
         return self.d_out[:n_sel]
@@ -631,7 +642,7 @@ class ModelRunner:
             NUM_SEQS_PADDING.labels(model_name=self.cfg.served_model_name or "model").observe(pad_to - n)
         meta, T, n_sel, greedy = self._prepare(so, pad_to, pad_tokens)
         if (is_plain_decode and self.use_graphs and "token_bitmask" not in meta.extras
-                and "logprobs_k" not in meta.extras):
+                and "logprobs_k" not in meta.extras and "debug_logits" not in meta.extras):
             key = (pad_to, greedy)
             entry = self.graphs.get(key)
             if entry is None:
@@ -659,6 +670,9 @@ class ModelRunner:
             torch.cuda.current_stream().synchronize()
         self.d2h_bytes_last = n_sel * 8
         toks = self.h_out[:n_sel].tolist()
+        raw = self.__dict__.pop("_last_raw", None)
+        if raw is not None:
+            self.debug_logits.write(so, raw, toks)
         res: dict[str, list[int]] = {}
         if so.kind == "decode" and any(s.spec_token_ids for s in so.seqs):
             off = 0
@@ -696,6 +710,7 @@ class ModelRunner:
     # ---------------------------------------------------------- async decode steps
     def can_launch_async(self, so: SchedulerOutput) -> bool:
         return (so.kind == "decode" and bool(so.seqs) and self.capture is None and self.replacer is None
+                and self.debug_logits is None
                 and all(len(s.token_ids) == 1 and not s.spec_token_ids for s in so.seqs)
                 and not any(s.request is not None and (s.request.sampling_params.logprobs is not None
                                                        or s.request.grammar is not None) for s in so.seqs))
