@@ -261,3 +261,46 @@ def test_multi_prompt_and_engine_generate_fn(llama, tmp_path):
     finally:
         llm.shutdown()
 
+
+
+def test_kv_snapshot_matches_hf_cache(llama):
+    """The engine's KV of a finished request (snapshot taken before its blocks are freed)
+    equals the HF model's cache on prompt + output[:-1]; three-way against HF float64 with
+    per-layer error-distribution overlap and the cross-prompt aggregates."""
+    import copy
+
+    from vllm_neuron_b200 import LLM, SamplingParams
+    from vllm_neuron_b200.accuracy.kv_cache_analysis import (KVSnapshot, aggregate_kv_bc_across_prompts,
+                                                             combined_bc_per_layer, compare_kv_caches,
+                                                             extract_hf_kv, kv_report)
+
+    path, hf = llama
+    hf64 = copy.deepcopy(hf).double()
+    llm = LLM(model=path, dtype="float32", max_model_len=256, max_num_seqs=2, max_num_batched_tokens=16,
+              block_size=16, device="cpu")
+    try:
+        prompts = [[5, 9, 100, 7, 3], list(range(20, 45))]
+        with KVSnapshot(llm.engine) as snap:
+            outs = llm.generate(prompt_token_ids=prompts,
+                                sampling_params=SamplingParams(temperature=0, max_tokens=4, ignore_eos=True))
+        assert len(snap.kv) == 2
+        raws = []
+        for p, o in zip(prompts, outs):
+            seq = p + list(o.outputs[0].token_ids)[:-1]
+            ours = snap.kv[o.request_id]
+            want = extract_hf_kv(hf, seq)
+            assert set(ours) == set(want) and ours["layers.0.self_attn"][0].shape == want["layers.0.self_attn"][0].shape
+            res = compare_kv_caches(want, ours)
+            assert len(res) == len(seq)
+            worst = max(m.k_linf for tok in res for hm in tok.values() for m in hm)
+            assert worst < 1e-4, kv_report(res)
+            res3, raw = compare_kv_caches(want, ours, baseline=extract_hf_kv(hf64, seq), return_raw_errors=True)
+            assert "layers.0.self_attn._bc" in res3[0]
+            raws.append(raw)
+        agg = aggregate_kv_bc_across_prompts(raws, [len(p) for p in prompts])
+        assert sorted(agg) == [0, 1, 2] and all(0.0 <= m.k_bc <= 1.0 for r in agg.values() for m in r.values())
+        comb = combined_bc_per_layer(raws)
+        assert sorted(comb) == sorted(snap.kv[outs[0].request_id])
+        assert "layers.1.self_attn" in kv_report(res)
+    finally:
+        llm.shutdown()

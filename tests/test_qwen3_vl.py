@@ -131,3 +131,33 @@ def test_vl_oversized_image_refused_at_request_time():
                      SamplingParams(temperature=0, max_tokens=2, ignore_eos=True))
     assert len(o[0].outputs[0].token_ids) == 2
     llm.shutdown()
+
+
+def test_encoder_cache_snapshot_matches_hf(models, tmp_path):
+    """The engine's cached vision-encoder rows of each image (embedding + deepstack features)
+    equal HF's vision tower outputs for the same preprocessing."""
+    from vllm_neuron_b200 import LLM, SamplingParams
+    from vllm_neuron_b200.accuracy.encoder_cache_analysis import (EncoderSnapshot, compare_encoder_caches_by_index,
+                                                                  encoder_report, extract_hf_encoder_outputs)
+
+    hf, ours = models
+    cfg = dict(HF_KW)
+    cfg["architectures"] = ["Qwen3VLForConditionalGeneration"]
+    llm = LLM(hf_config=cfg, load_format="dummy", dtype="float32", max_model_len=256, max_num_seqs=2,
+              max_num_batched_tokens=256, block_size=16, device="cpu", seed=1)
+    try:
+        model = llm.engine.worker.model
+        model.load_state_dict(ours.state_dict(), strict=False)
+        imgs = [torch.rand(3, 64, 96) * 255, torch.rand(3, 96, 64) * 255]
+        prompt = [5, 1001, 1000, 1002, 1001, 1000, 1002, 7]
+        with EncoderSnapshot(llm.engine) as snap:
+            o = llm.generate([{"prompt_token_ids": prompt, "multi_modal_data": {"image": imgs}}],
+                             SamplingParams(temperature=0, max_tokens=2, ignore_eos=True))
+        rid = o[0].request_id
+        got = [snap.items[(rid, 0)], snap.items[(rid, 1)]]
+        want = extract_hf_encoder_outputs(hf, imgs, ours.vl_cfg.vision)
+        res = compare_encoder_caches_by_index(want, got)
+        assert all(m.linf < 1e-4 and m.cos_sim > 0.99999 for m in res), encoder_report(res)
+        assert [m.num_tokens for m in res] == [6, 6]
+    finally:
+        llm.shutdown()
