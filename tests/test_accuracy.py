@@ -304,3 +304,39 @@ def test_kv_snapshot_matches_hf_cache(llama):
         assert "layers.1.self_attn" in kv_report(res)
     finally:
         llm.shutdown()
+
+
+def test_tensor_io_layout_and_hf_capture_alignment(llama, tmp_path):
+    """Engine captures converted to the dp<N>/<pass>/<module>/rank<r>.pt layout, written and
+    read back, then matched pass by pass (prefill, and decode by position) with an HF capture of
+    the same prompt: every module output agrees."""
+    from vllm_neuron_b200 import LLM, SamplingParams
+    from vllm_neuron_b200.accuracy import tensor_io
+    from vllm_neuron_b200.accuracy.tensor_alignment_utils import (align_and_truncate_hidden, count_real_tokens,
+                                                                  match_passes, slice_token)
+
+    path, hf = llama
+    cap = str(tmp_path / "steps")
+    nc = {"tensor_capture": {"modules": ["layers.0-1.mlp"], "capture_dir": cap}}
+    llm = LLM(model=path, dtype="float32", max_model_len=128, max_num_seqs=1, block_size=16, device="cpu",
+              additional_config={"neuron_config": nc})
+    prompt = [4, 5, 6, 7, 8]
+    llm.generate(prompt_token_ids=[prompt], sampling_params=SamplingParams(temperature=0, max_tokens=3,
+                                                                           ignore_eos=True))
+    llm.shutdown()
+    ours = tensor_io.from_capture_steps(cap)
+    assert [p.dir_name for p in ours] == ["prefill_s5_0", "decode_b1_1", "decode_b1_2"]
+    assert ours[1].metadata.positions == [5]
+    tensor_io.write(str(tmp_path / "io" / "dp0"), ours)
+    back = tensor_io.read(str(tmp_path / "io"))
+    assert [p.dir_name for p in back] == [p.dir_name for p in ours]
+    assert torch.equal(back[0].tensors["layers.0.mlp"][0], ours[0].tensors["layers.0.mlp"][0])
+    ref = tensor_io.capture_hf(hf, prompt, {"model.layers.0.mlp": "layers.0.mlp", "model.layers.1.mlp": "layers.1.mlp"},
+                               max_new_tokens=4)
+    pairs = match_passes(ref, back)
+    assert len(pairs) == 3  # HF decoded one extra step: dropped
+    for r, t in pairs:
+        for name in ("layers.0.mlp", "layers.1.mlp"):
+            (a, b), same = align_and_truncate_hidden(r.tensors[name][0], t.tensors[name][0])
+            assert same and torch.allclose(a, b, atol=1e-4), (r.dir_name, name, (a - b).abs().max())
+    assert count_real_tokens([0, 1, 2, 2, 2]) == 3 and slice_token(torch.zeros(1, 5, 8), 2).shape == (1, 1, 8)
