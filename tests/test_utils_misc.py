@@ -93,3 +93,44 @@ def test_spec_decode_utils():
     assert idx.tolist() == [1, 7]
     r = replicate_per_seq_rows(torch.tensor([[1.0, 2.0], [3.0, 4.0]]), 3)
     assert torch.equal(r, torch.tensor([[1.0, 2.0]] * 3 + [[3.0, 4.0]] * 3))
+
+
+def test_kv_cache_dtype_names_and_fp8_bound():
+    import torch
+
+    from vllm_neuron_b200.utils.dtype_utils import FP8_CLAMP_MAX, kv_cache_dtype_str_to_dtype
+
+    assert FP8_CLAMP_MAX == float(torch.finfo(torch.float8_e4m3fn).max)
+    assert kv_cache_dtype_str_to_dtype("auto", torch.bfloat16) == torch.bfloat16
+    assert kv_cache_dtype_str_to_dtype("fp8_e4m3", torch.bfloat16) == torch.float8_e4m3fn
+    with pytest.raises(ValueError, match="unsupported kv_cache_dtype"):
+        kv_cache_dtype_str_to_dtype("int4", torch.bfloat16)
+
+
+def test_bind_to_gpu_numa_with_fake_sysfs(tmp_path):
+    """NUMA pinning reads the GPU's PCI numa_node and the node's CPU list from sysfs (a fake
+    tree here) and never widens the process's allowed CPUs."""
+    import os
+
+    from vllm_neuron_b200.utils.hardware_config import bind_to_gpu_numa, parse_cpulist, pci_numa_node
+
+    assert parse_cpulist("0-3,8,10-11\n") == {0, 1, 2, 3, 8, 10, 11}
+    before = os.sched_getaffinity(0)
+    bus = "0000:1b:00.0"
+    (tmp_path / "bus/pci/devices" / bus).mkdir(parents=True)
+    (tmp_path / "bus/pci/devices" / bus / "numa_node").write_text("1\n")
+    (tmp_path / "devices/system/node/node1").mkdir(parents=True)
+    allowed = sorted(before)
+    (tmp_path / "devices/system/node/node1/cpulist").write_text(f"{allowed[0]},{max(allowed) + 1000}\n")
+    assert pci_numa_node(bus, str(tmp_path)) == 1
+    try:
+        cpus = bind_to_gpu_numa(0, bus, str(tmp_path))
+        assert cpus == {allowed[0]} and os.sched_getaffinity(0) == {allowed[0]}
+    finally:
+        for tid in os.listdir("/proc/self/task"):
+            try:
+                os.sched_setaffinity(int(tid), before)
+            except OSError:
+                pass
+    (tmp_path / "bus/pci/devices" / bus / "numa_node").write_text("-1\n")
+    assert bind_to_gpu_numa(0, bus, str(tmp_path)) is None and os.sched_getaffinity(0) == before

@@ -25,6 +25,7 @@ from ..metrics import MODEL_LOAD_SIZE, MODEL_LOAD_TIME, STARTUP_TIME
 from ..models.base import random_init_, random_init_device_
 from ..models.registry import resolve
 from ..parallel import state as pstate
+from ..utils.dtype_utils import kv_cache_dtype_str_to_dtype
 from .model_runner import ModelRunner
 
 logger = init_logger(__name__)
@@ -36,7 +37,8 @@ def build_model(cfg: EngineConfig, ps, device: torch.device, hf: dict | None = N
     mcfg = config_cls.from_hf(hf, quantization=cfg.neuron_config.quantization)
     dtype = torch.bfloat16 if cfg.dtype in ("bfloat16", "bf16", "auto") else (
         torch.float32 if cfg.dtype in ("float32", "fp32") else torch.float16)
-    kv_dtype = torch.float8_e4m3fn if cfg.kv_dtype_is_fp8 else dtype
+    # fp8 names select the e4m3fn cache; the 16-bit names keep the model's dtype
+    kv_dtype = kv_cache_dtype_str_to_dtype(cfg.kv_cache_dtype, dtype) if cfg.kv_dtype_is_fp8 else dtype
     model = model_cls(mcfg, ps, dtype=dtype, device=device, kv_dtype=kv_dtype)
     return model, mcfg, hf
 
@@ -58,6 +60,12 @@ class Worker:
         if dev == "cuda":
             torch.cuda.set_device(self.local_rank)
             self.device = torch.device("cuda", self.local_rank)
+            if envs.VLLM_B200_CPU_AFFINITY:
+                from ..utils.hardware_config import bind_to_gpu_numa
+
+                cpus = bind_to_gpu_numa(self.local_rank)
+                logger.info("rank %d pinned to %s CPUs of its GPU's NUMA node", self.rank,
+                            len(cpus) if cpus else "no (node unknown)")
         pstate.init_distributed_environment(self.world_size, self.rank, local_rank=self.local_rank,
                                             timeout_s=float(envs.VLLM_B200_BARRIER_TIMEOUT))
         nc = self.cfg.neuron_config

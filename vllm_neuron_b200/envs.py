@@ -63,6 +63,8 @@ _REGISTRY: dict[str, tuple[Callable[[str], Any], str | None, str | None]] = {
     "VLLM_B200_DEVICE_WAIT_LIMIT": (int, "20000000", None),
     # Prometheus multiprocess directory (set automatically when unset).
     "PROMETHEUS_MULTIPROC_DIR": (str, "", None),
+    # Pin each rank's threads to the CPUs of its GPU's NUMA node.
+    "VLLM_B200_CPU_AFFINITY": (_bool, "0", None),
     # Bidirectional KV transfer for disaggregated serving.
     "VLLM_B200_BIDIRECTIONAL_KV": (_bool, "0", "VLLM_NEURON_BIDIRECTIONAL_KV"),
 }

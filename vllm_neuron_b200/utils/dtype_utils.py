@@ -1,4 +1,9 @@
-"""dtype names and properties (``utils/dtype_utils.py`` of the Trainium plugin)."""
+"""dtype names and properties (``utils/dtype_utils.py`` of the Trainium plugin:
+``FP8_CLAMP_MAX`` ``:17-41``, ``kv_cache_dtype_str_to_dtype`` ``:44``).
+
+B200 tensor cores and conversions use the OCP e4m3fn format (no infinities), whose largest
+finite value is 448; that is the clamp bound for every fp8 quantisation here (KV cache,
+activations), with no per-chip variant."""
 
 from __future__ import annotations
 
@@ -47,3 +52,20 @@ def ulp(value: float, dt) -> float:
     if value == 0:
         return float(torch.finfo(to_torch_dtype(dt)).tiny)
     return 2.0 ** (math.floor(math.log2(abs(value))) - mantissa_bits(dt))
+
+
+FP8_CLAMP_MAX: float = 448.0
+QUANTIZED_KV_CACHE_DTYPES = ("fp8", "fp8_e4m3")
+_KV_DTYPES = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16, "bf16": torch.bfloat16,
+              "fp8": torch.float8_e4m3fn, "fp8_e4m3": torch.float8_e4m3fn}
+
+
+def kv_cache_dtype_str_to_dtype(kv_cache_dtype: str, model_dtype) -> torch.dtype:
+    """``--kv-cache-dtype`` value -> storage dtype of the paged KV cache; ``auto`` keeps the
+    model's dtype and the fp8 names map to ``torch.float8_e4m3fn`` (dequantised with the
+    per-layer k / v scales inside the attention kernels)."""
+    if kv_cache_dtype == "auto":
+        return to_torch_dtype(model_dtype)
+    if kv_cache_dtype not in _KV_DTYPES:
+        raise ValueError(f"unsupported kv_cache_dtype {kv_cache_dtype!r}; supported: 'auto', {sorted(_KV_DTYPES)}")
+    return _KV_DTYPES[kv_cache_dtype]
