@@ -192,7 +192,11 @@ class Worker:
 
     def warmup(self) -> None:
         t0 = time.time()
-        if self.runner.use_graphs and not envs.VLLM_B200_SKIP_DECODE_WARMUP:
+        kv = self.cfg.kv_transfer_config
+        # a prefill-only server (KV producer) never decodes, so it captures no decode graphs
+        # (vllm/worker/neuron_worker.py:957-962); a bucket reached anyway is captured on first use
+        producer_only = kv is not None and kv.kv_role == "kv_producer"
+        if self.runner.use_graphs and not envs.VLLM_B200_SKIP_DECODE_WARMUP and not producer_only:
             from .scheduler import ScheduledSeq, SchedulerOutput
 
             for B in self.runner.decode_buckets:

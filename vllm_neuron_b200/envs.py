@@ -46,7 +46,8 @@ _REGISTRY: dict[str, tuple[Callable[[str], Any], str | None, str | None]] = {
     "VLLM_B200_BARRIER_TIMEOUT": (int, "3600", "VLLM_NEURON_BARRIER_TIMEOUT"),
     # Minimum KV-cache budget in GiB; below it the worker fails fast.
     "VLLM_B200_MIN_KV_BUDGET_GIB": (float, "1.0", "VLLM_NEURON_MIN_KV_BUDGET_GIB"),
-    # Skip warm-up (graph capture) of prefill / decode buckets.
+    # Skip warm-up (graph capture) of the decode buckets.  Prefill runs eagerly (no per-bucket
+    # graphs), so the prefill switch is accepted for compatibility and has nothing to skip.
     "VLLM_B200_SKIP_PREFILL_WARMUP": (_bool, "0", "VLLM_NEURON_SKIP_PREFILL_WARMUP"),
     "VLLM_B200_SKIP_DECODE_WARMUP": (_bool, "0", "VLLM_NEURON_SKIP_DECODE_WARMUP"),
     # Seconds a worker gets between SIGTERM and SIGKILL at shutdown.
