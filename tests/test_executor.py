@@ -108,3 +108,26 @@ def test_collective_all2all_matches_math():
     with MPExecutor(world_size=2, tp=2, timeout_s=120) as ex:
         assert max(ex.run(_ep_a2a_case, 9, 0, 9)) < 1e-5
         assert max(ex.run(_ep_a2a_case, 9, 2, 6)) < 1e-5
+
+
+def _lockstep(ctx, skew_rank, skew, tag_rank):
+    """Every rank reduces once; ``skew_rank`` claims a later step, ``tag_rank`` another call site."""
+    step = 7 + (skew if ctx.rank == skew_rank else 0)
+    tag = 2 if ctx.rank == tag_rank else 1
+    try:
+        return ("ok", ctx.ps.world.lockstep_all_reduce_max([ctx.rank * 10, 5], step, tag))
+    except RuntimeError as e:
+        return ("tripped", str(e))
+
+
+def test_dp_lockstep_tripwire_fires_on_every_rank():
+    """A replica one step ahead, or at a different reduce, makes every rank raise; aligned
+    ranks get the plain MAX-reduce."""
+    from vllm_neuron_b200.utils.executor import MPExecutor
+
+    with MPExecutor(world_size=2, tp=1, dp=2, timeout_s=60) as ex:
+        assert ex.run(_lockstep, -1, 0, -1) == [("ok", [10, 5]), ("ok", [10, 5])]
+        res = ex.run(_lockstep, 1, 1, -1)  # rank 1 skipped a step
+        assert [r[0] for r in res] == ["tripped", "tripped"] and "steps 7..8" in res[0][1]
+        res = ex.run(_lockstep, -1, 0, 0)  # rank 0 at the token-count reduce, rank 1 at the flags reduce
+        assert [r[0] for r in res] == ["tripped", "tripped"] and "call sites 1..2" in res[1][1]

@@ -109,6 +109,7 @@ class LLMEngine:
         self.dp = cfg.data_parallel_size
         self.replica = rank // cfg.tensor_parallel_size
         self._rr = 0
+        self._dp_step = 0  # data-parallel lockstep counter (checked every step)
         self._remote: set[str] = set()  # unfinished requests owned by other replicas
         # asynchronous scheduling (single rank or SPMD; decode steps with CUDA graphs)
         # (grammar masks need step k's token before step k + 1 is staged: no lookahead then)
@@ -363,8 +364,10 @@ class LLMEngine:
         token count (idle replicas run a padding batch), the counterpart of the reference's
         per-step MAX-reduce and dummy batches (``neuron_model_runner.py:6524-6821,6968``)."""
         world = self.worker.ps.world
+        self._dp_step += 1
         has_work = self.scheduler.has_unfinished()
-        flags = world.cpu_all_reduce_max([int(has_work), int(has_work and self.scheduler.has_prefill_work())])
+        flags = world.lockstep_all_reduce_max([int(has_work), int(has_work and self.scheduler.has_prefill_work())],
+                                              self._dp_step, 1)
         outs: list[RequestOutput] = []
         if flags[0]:
             kind = "prefill" if flags[1] else "decode"
@@ -372,7 +375,7 @@ class LLMEngine:
             outs = [self._make_output(r, True) for r in self.scheduler.failed]
             self.scheduler.failed = []
             n_tok = so.num_tokens if so.kind != "idle" else 0
-            mx = world.cpu_all_reduce_max([n_tok, len(so.seqs)])
+            mx = world.lockstep_all_reduce_max([n_tok, len(so.seqs)], self._dp_step, 2)
             outs += self._run(so, dp_pad=(kind, mx[0], mx[1]))
         # every replica learns every replica's outputs (TP peers hold identical copies)
         allouts = [o for lst in self.worker.ps.dp.all_gather_object(outs) for o in lst]

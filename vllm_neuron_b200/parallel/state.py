@@ -274,6 +274,19 @@ class GroupCoordinator:
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.cpu_group)
         return t.tolist()
 
+    def lockstep_all_reduce_max(self, values: list[int], step: int, tag: int) -> list[int]:
+        """``cpu_all_reduce_max`` that also proves every rank is at the same ``step`` and the
+        same call site (``tag``): both ride along as (x, -x) pairs, whose MAX-reduce gives the
+        largest and the smallest value.  A rank that skipped or repeated a step, or reached a
+        different reduce, makes every rank raise instead of silently mixing one call's values
+        with another's (the reference's data-parallel padding tripwire,
+        ``neuron_model_runner.py:2765-2791``)."""
+        out = self.cpu_all_reduce_max([step, -step, tag, -tag] + list(values))
+        if out[0] != -out[1] or out[2] != -out[3]:
+            raise RuntimeError(f"lockstep violated on rank {self.rank_in_group}: steps {-out[1]}..{out[0]}, "
+                               f"call sites {-out[3]}..{out[2]} (this rank: step {step}, site {tag})")
+        return out[4:]
+
     def barrier(self, timeout_s: float | None = None) -> None:
         """Barrier on the CPU group with a timeout (``neuron_parallel_state.py:1289-1325``)."""
         if self.world_size == 1:
