@@ -134,3 +134,14 @@ def test_bind_to_gpu_numa_with_fake_sysfs(tmp_path):
                 pass
     (tmp_path / "bus/pci/devices" / bus / "numa_node").write_text("-1\n")
     assert bind_to_gpu_numa(0, bus, str(tmp_path)) is None and os.sched_getaffinity(0) == before
+
+
+def test_device_offset_moves_every_rank(monkeypatch):
+    """VLLM_B200_DEVICE_OFFSET shifts the GPU of every rank (rank r -> GPU offset + r)."""
+    from vllm_neuron_b200.config import EngineConfig
+    from vllm_neuron_b200.engine.worker import Worker
+
+    cfg = EngineConfig.create(model=None, device="cpu")
+    assert Worker(cfg, rank=1, world_size=4, local_rank=1).device_index == 1
+    monkeypatch.setenv("VLLM_B200_DEVICE_OFFSET", "4")
+    assert Worker(cfg, rank=1, world_size=4, local_rank=1).device_index == 5

@@ -49,6 +49,9 @@ class Worker:
         self.rank = rank
         self.world_size = world_size
         self.local_rank = local_rank
+        # GPU of this rank: local rank + VLLM_B200_DEVICE_OFFSET, so two servers that both see every
+        # GPU of the host (CUDA IPC between them needs that) can still sit on disjoint GPUs
+        self.device_index = local_rank + envs.VLLM_B200_DEVICE_OFFSET
         self.device = torch.device("cpu")
         self.model = None
         self.runner: ModelRunner | None = None
@@ -58,15 +61,15 @@ class Worker:
         t0 = time.time()
         dev = self.cfg.resolve_device()
         if dev == "cuda":
-            torch.cuda.set_device(self.local_rank)
-            self.device = torch.device("cuda", self.local_rank)
+            torch.cuda.set_device(self.device_index)
+            self.device = torch.device("cuda", self.device_index)
             if envs.VLLM_B200_CPU_AFFINITY:
                 from ..utils.hardware_config import bind_to_gpu_numa
 
-                cpus = bind_to_gpu_numa(self.local_rank)
+                cpus = bind_to_gpu_numa(self.device_index)
                 logger.info("rank %d pinned to %s CPUs of its GPU's NUMA node", self.rank,
                             len(cpus) if cpus else "no (node unknown)")
-        pstate.init_distributed_environment(self.world_size, self.rank, local_rank=self.local_rank,
+        pstate.init_distributed_environment(self.world_size, self.rank, local_rank=self.device_index,
                                             timeout_s=float(envs.VLLM_B200_BARRIER_TIMEOUT))
         nc = self.cfg.neuron_config
         self.ps = pstate.initialize_parallel_state(

@@ -64,6 +64,8 @@ _REGISTRY: dict[str, tuple[Callable[[str], Any], str | None, str | None]] = {
     "VLLM_B200_DEVICE_WAIT_LIMIT": (int, "20000000", None),
     # Prometheus multiprocess directory (set automatically when unset).
     "PROMETHEUS_MULTIPROC_DIR": (str, "", None),
+    # First GPU index of this engine (rank r uses GPU offset + r).
+    "VLLM_B200_DEVICE_OFFSET": (int, "0", None),
     # Pin each rank's threads to the CPUs of its GPU's NUMA node.
     "VLLM_B200_CPU_AFFINITY": (_bool, "0", None),
     # Bidirectional KV transfer for disaggregated serving.
