@@ -161,3 +161,35 @@ def test_encoder_cache_snapshot_matches_hf(models, tmp_path):
         assert [m.num_tokens for m in res] == [6, 6]
     finally:
         llm.shutdown()
+
+
+def test_vl_interfaces_and_vision_warmup():
+    """Qwen3-VL declares the optional capabilities (spatial merge, pixel budget, M-RoPE,
+    vision warm-up); with num_vision_tokens_buckets set, start-up runs the encoder once per
+    bucket on synthetic inputs that produce exactly that many tokens."""
+    from vllm_neuron_b200 import LLM
+    from vllm_neuron_b200.models.interfaces import (SupportsMaxPixels, SupportsMRoPE, SupportsSpatialMerge,
+                                                    SupportsVisionWarmup)
+    from vllm_neuron_b200.models.qwen3_vl import Qwen3VLForConditionalGeneration as VL
+
+    cfg = dict(HF_KW)
+    cfg["architectures"] = ["Qwen3VLForConditionalGeneration"]
+    assert VL.get_vision_token_merge_factor(cfg) == 4
+    assert VL.get_max_pixels_token_count(cfg, 64 * 96) == 24
+    llm = LLM(hf_config=cfg, load_format="dummy", dtype="float32", max_model_len=256, max_num_seqs=2,
+              max_num_batched_tokens=256, block_size=16, device="cpu", seed=1,
+              additional_config={"vision_neuron_config": {"num_vision_tokens_buckets": [4, 8]}})
+    try:
+        model = llm.engine.worker.model
+        for proto in (SupportsVisionWarmup, SupportsSpatialMerge, SupportsMaxPixels, SupportsMRoPE):
+            assert isinstance(model, proto)
+        assert llm.engine.worker.vision_warmups == 2
+        inp = model.build_vision_synthetic_inputs(8, None, torch.device("cpu"))
+        with torch.no_grad():
+            emb, deep = model.visual(inp["patches"], inp["grids"])
+        assert emb.shape[0] == 8 and len(deep) == 2
+        ids = [5, 1000, 1000, 1000, 1000, 7]
+        p, delta = model.get_mrope_input_positions(ids, [(1, 4, 4)])
+        assert p.shape == (3, 6) and delta == int(p.max()) + 1 - 6
+    finally:
+        llm.shutdown()

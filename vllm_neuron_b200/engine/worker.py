@@ -207,6 +207,18 @@ class Worker:
                 so = SchedulerOutput("decode", seqs)
                 # writes go to the reserved null block 0 (never read by a live request)
                 self.runner.execute(so)
+        buckets = self.cfg.vision_neuron_config.num_vision_tokens_buckets
+        if buckets:
+            from ..models.interfaces import SupportsVisionWarmup
+
+            if isinstance(self.model, SupportsVisionWarmup):
+                # one encoder pass per configured image size, so the first requests do not pay
+                # for lazy initialisation (vllm/worker/neuron_worker.py:907 vision warm-up)
+                with torch.inference_mode():
+                    for b in sorted(set(buckets)):
+                        inp = self.model.build_vision_synthetic_inputs(b, self.cfg.vision_neuron_config, self.device)
+                        self.model.visual(inp["patches"], inp["grids"])
+                self.vision_warmups = len(set(buckets))
         STARTUP_TIME.labels(model_name=self.cfg.served_model_name or str(self.cfg.model)).set(
             time.time() - getattr(self, "_t_start", t0))
 

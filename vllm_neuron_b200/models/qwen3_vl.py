@@ -271,6 +271,37 @@ class Qwen3VLForConditionalGeneration(LlamaForCausalLM):
         emb, deep = self.visual(patches.to(dev), [grid])
         return {"embeds": emb, "deepstack": deep, "grid": grid}
 
+    # ------------------------------------------------ capabilities (models/interfaces.py)
+    @classmethod
+    def get_vision_token_merge_factor(cls, hf_config) -> int:
+        """Raw patches per embedding token: spatial_merge_size squared."""
+        from .interfaces import _vision_cfg
+
+        m = int(_vision_cfg(hf_config).get("spatial_merge_size", 2))
+        return m * m
+
+    @classmethod
+    def get_max_pixels_token_count(cls, hf_config, max_pixels: int) -> int:
+        """Raw (pre-merge) patches of an image of ``max_pixels`` pixels: one patch per
+        patch_size x patch_size pixels."""
+        from .interfaces import _vision_cfg
+
+        p = int(_vision_cfg(hf_config).get("patch_size", 16))
+        return max(1, int(max_pixels) // (p * p))
+
+    def build_vision_synthetic_inputs(self, bucket: int, vision_neuron_config, device) -> dict:
+        """Zero patches of a one-frame grid (merge x bucket*merge patches) that the encoder
+        turns into exactly ``bucket`` embedding tokens."""
+        vc = self.vl_cfg.vision
+        m, p = vc.spatial_merge_size, vc.patch_size
+        grid = (1, m, int(bucket) * m)
+        dim = vc.in_channels * vc.temporal_patch_size * p * p
+        return {"patches": torch.zeros(m * m * int(bucket), dim, dtype=torch.float32, device=device),
+                "grids": [grid]}
+
+    def get_mrope_input_positions(self, token_ids: list[int], grids: list) -> tuple[torch.Tensor, int]:
+        return self.mrope_positions(token_ids, grids)
+
     def num_image_tokens(self, grid) -> int:
         t, h, w = grid
         m = self.vl_cfg.vision.spatial_merge_size
