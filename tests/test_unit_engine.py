@@ -123,6 +123,11 @@ def test_async_scheduling_matches_sync(temperature):
         assert eng._inflight is None
         if mode:
             assert eng.async_stats["lookahead"] > 10, eng.async_stats
+            assert eng.async_stats["sync_fallback"] > 0  # prefills run synchronously
+            from prometheus_client import REGISTRY
+
+            got = REGISTRY.get_sample_value("vllm_b200:async_steps_total", {"model_name": "model", "mode": "lookahead"})
+            assert got is not None and got >= eng.async_stats["lookahead"]
         llm.shutdown()
     assert outs[True] == outs[False]
 

@@ -117,7 +117,7 @@ class LLMEngine:
             and not cfg.neuron_config.enable_structured_outputs \
             and self.proposer is None
         self._inflight = None
-        self.async_stats = {"launched": 0, "lookahead": 0}
+        self.async_stats = {"launched": 0, "lookahead": 0, "sync_fallback": 0}
         logger.info("engine ready: rank %d/%d mode=%s kv_blocks=%d", rank, world_size, mode, n_blocks)
 
     # ------------------------------------------------------------------ intake
@@ -330,7 +330,7 @@ class LLMEngine:
             cur = None
             if nxt is not None:
                 cur = runner.launch(nxt, prev)
-                self.async_stats["lookahead"] += 1
+                self._count_async("lookahead")
                 for s in nxt.seqs:
                     s.request.num_inflight += 1
             outs = self._commit(prev)
@@ -343,11 +343,20 @@ class LLMEngine:
             return failed
         if runner.can_launch_async(so):
             self._inflight = runner.launch(so)
-            self.async_stats["launched"] += 1
+            self._count_async("launched")
             for s in so.seqs:
                 s.request.num_inflight += 1
             return failed
+        self._count_async("sync_fallback")
         return failed + self._run(so)
+
+    def _count_async(self, mode: str) -> None:
+        """Async vs synchronous-fallback step counters (reference:
+        ``neuron_model_runner.py:709-710``, ``neuron_worker.py:1881-1897``)."""
+        from ..metrics import ASYNC_STEPS
+
+        self.async_stats[mode] += 1
+        ASYNC_STEPS.labels(model_name=self.cfg.served_model_name or "model", mode=mode).inc()
 
     def _commit(self, step) -> list[RequestOutput]:
         sampled = self.worker.runner.commit(step)

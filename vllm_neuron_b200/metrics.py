@@ -63,4 +63,8 @@ COMPILATION_TIME = _make("g", "vllm_b200:compilation_time_seconds", "Graph captu
 STARTUP_TIME = _make("g", "vllm_b200:startup_time_seconds", "Worker start-up time", ("model_name",))
 MODEL_LOAD_TIME = _make("g", "vllm_b200:model_load_time_seconds", "Weight load time", ("model_name",))
 MODEL_LOAD_SIZE = _make("g", "vllm_b200:model_load_size_bytes", "Bytes of weights loaded", ("model_name",))
+ASYNC_STEPS = _make(
+    "c", "vllm_b200:async_steps", "Engine steps under asynchronous scheduling by how they ran: launched (pipeline "
+    "started), lookahead (scheduled while the previous step ran), sync_fallback (drained and run synchronously)",
+    ("model_name", "mode"))
 NVLINK_BYTES = _make("c", "vllm_b200:nvlink_bytes", "Bytes moved by fused collectives", ("model_name", "op"))
