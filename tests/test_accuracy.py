@@ -340,3 +340,30 @@ def test_tensor_io_layout_and_hf_capture_alignment(llama, tmp_path):
             (a, b), same = align_and_truncate_hidden(r.tensors[name][0], t.tensors[name][0])
             assert same and torch.allclose(a, b, atol=1e-4), (r.dir_name, name, (a - b).abs().max())
     assert count_real_tokens([0, 1, 2, 2, 2]) == 3 and slice_token(torch.zeros(1, 5, 8), 2).shape == (1, 1, 8)
+
+
+def test_deterministic_replay_bitwise(llama, tmp_path):
+    """Two fresh engines given the same seeded sampled workload produce the same tokens and
+    bitwise-identical logit dumps (a replay check for races in the step pipeline)."""
+    from vllm_neuron_b200 import LLM, SamplingParams
+    from vllm_neuron_b200.engine.debug_logits import read_debug_logits
+
+    path, _ = llama
+    runs = []
+    for i in range(2):
+        d = str(tmp_path / f"run{i}")
+        llm = LLM(model=path, dtype="float32", max_model_len=256, max_num_seqs=4, max_num_batched_tokens=32,
+                  block_size=16, device="cpu", seed=3, additional_config={"neuron_config": {"debug_logits_dir": d}})
+        try:
+            outs = llm.generate(prompt_token_ids=[[5, 9, 100, 7, 3], list(range(20, 60)), [11] * 12],
+                                sampling_params=SamplingParams(temperature=0.9, top_p=0.9, top_k=40, max_tokens=6,
+                                                               ignore_eos=True, seed=17))
+        finally:
+            llm.shutdown()
+        runs.append(([o.outputs[0].token_ids for o in outs], read_debug_logits(d)))
+    (t0, l0), (t1, l1) = runs
+    assert t0 == t1
+    assert sorted(l0) == sorted(l1)
+    for b in l0:
+        assert sorted(l0[b]) == sorted(l1[b])
+        assert all(torch.equal(l0[b][p], l1[b][p]) for p in l0[b])
