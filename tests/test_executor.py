@@ -131,3 +131,42 @@ def test_dp_lockstep_tripwire_fires_on_every_rank():
         assert [r[0] for r in res] == ["tripped", "tripped"] and "steps 7..8" in res[0][1]
         res = ex.run(_lockstep, -1, 0, 0)  # rank 0 at the token-count reduce, rank 1 at the flags reduce
         assert [r[0] for r in res] == ["tripped", "tripped"] and "call sites 1..2" in res[1][1]
+
+
+def _shard_sum(ctx, shard):
+    return float(shard.sum()) + 1000 * ctx.rank
+
+
+def _where(ctx):
+    return (ctx.nnodes, ctx.node_rank, ctx.local_rank)
+
+
+def _matmul(ctx, n):
+    a = torch.randn(n, n)
+    return float((a @ a).sum() * 0)
+
+
+def test_executor_per_rank_inputs_nodes_profile_and_pool(tmp_path):
+    """Per-rank arguments, simulated nodes, per-rank Chrome traces, and the pooled executor
+    that a second request with another layout reuses (re-laid-out, same processes)."""
+    from vllm_neuron_b200.utils.executor import MPExecutor
+
+    with MPExecutor(world_size=4, tp=2, dp=2, nnodes=2, timeout_s=60) as ex:
+        x = torch.arange(8.0)
+        assert ex.run_per_rank(_shard_sum, [(c,) for c in x.chunk(4)]) == [1.0, 1005.0, 2009.0, 3013.0]
+        assert ex.run(_where) == [(2, 0, 0), (2, 0, 1), (2, 1, 0), (2, 1, 1)]
+        ex.start_profile(str(tmp_path / "prof"))
+        ex.run(_matmul, 64)
+        paths = ex.stop_profile()
+        assert [os.path.basename(p) for p in paths] == [f"trace_rank{r}.json" for r in range(4)]
+        assert all(os.path.getsize(p) > 0 for p in paths)
+        with pytest.raises(ValueError):
+            ex.run_per_rank(_shard_sum, [(x,)])
+    try:
+        a = MPExecutor.shared(2, tp=2)
+        pids = [p.pid for p in a._procs]
+        b = MPExecutor.shared(2, tp=1, dp=2)
+        assert b is a and [p.pid for p in b._procs] == pids
+        assert b.run(_layout) == [(1, 2), (1, 2)]
+    finally:
+        MPExecutor.shutdown_shared()

@@ -8,8 +8,20 @@ queue:
 
 * ``run(fn, *args)``      call ``fn(ctx, *args)`` on every rank, return the per-rank results;
 * ``load(factory, *args)`` build a per-rank object (kept in ``ctx.obj``) for later ``run`` calls;
+* ``run_per_rank(fn, [args_0, args_1, ...])`` call ``fn(ctx, *args_r)`` with each rank's own
+  arguments (e.g. the shard of an input that rank r owns);
 * ``reinit(tp=, dp=, ...)`` rebuild the parallel state with another layout (same world);
+* ``start_profile(dir)`` / ``stop_profile()`` record every rank with ``torch.profiler`` (CPU, and
+  CUDA activity on GPU ranks) and write one Chrome trace per rank
+  (reference: ``utils/executor.py:618-732``);
 * ``shutdown()``          stop the pool.
+
+``MPExecutor.shared(world_size, **layout)`` returns a pooled executor that later calls with the
+same world size reuse (re-laid-out with ``reinit`` when the layout differs), so a test suite
+pays for process start-up and rendezvous once per world size (``_WorkerPool``, reference
+``utils/executor.py:100``).  ``nnodes`` simulates a multi-node job on one host: ranks are dealt
+to nodes in contiguous blocks and ``ctx.node_rank`` / ``ctx.local_rank`` / ``ctx.nnodes`` tell a
+task where its rank sits.
 
 Failure detection: a task that raises on any rank makes ``run`` raise ``RankError`` with
 the rank and its traceback; a rank process that dies or does not answer within
@@ -44,16 +56,44 @@ class RankContext:
     device: Any = None
     obj: Any = None
     store: dict = field(default_factory=dict)
+    nnodes: int = 1
+    node_rank: int = 0
+    local_rank: int = 0
+    profiler: Any = None
+
+
+def _start_profile(ctx: RankContext, out_dir: str) -> None:
+    import torch
+
+    acts = [torch.profiler.ProfilerActivity.CPU]
+    if ctx.device is not None and ctx.device.type == "cuda":
+        acts.append(torch.profiler.ProfilerActivity.CUDA)
+    ctx.store["profile_dir"] = out_dir
+    ctx.profiler = torch.profiler.profile(activities=acts, record_shapes=True)
+    ctx.profiler.__enter__()
+
+
+def _stop_profile(ctx: RankContext) -> str | None:
+    if ctx.profiler is None:
+        return None
+    ctx.profiler.__exit__(None, None, None)
+    out_dir = ctx.store.pop("profile_dir")
+    os.makedirs(out_dir, exist_ok=True)
+    path = os.path.join(out_dir, f"trace_rank{ctx.rank}.json")
+    ctx.profiler.export_chrome_trace(path)
+    ctx.profiler = None
+    return path
 
 
 def _worker(rank: int, world_size: int, init_method: str, backend: str, layout: dict, tasks, results,
-            timeout_s: float) -> None:
+            timeout_s: float, nnodes: int = 1) -> None:
     import torch
     import torch.distributed as dist
 
     from ..parallel import state as pstate
 
-    ctx = RankContext(rank, world_size)
+    per_node = world_size // nnodes
+    ctx = RankContext(rank, world_size, nnodes=nnodes, node_rank=rank // per_node, local_rank=rank % per_node)
     try:
         if backend == "nccl":
             torch.cuda.set_device(rank)
@@ -75,6 +115,14 @@ def _worker(rank: int, world_size: int, init_method: str, backend: str, layout: 
             if kind == "run":
                 fn, args, kwargs = payload
                 out = fn(ctx, *args, **kwargs)
+            elif kind == "run_per_rank":
+                fn, per_rank, kwargs = payload
+                out = fn(ctx, *per_rank[rank], **kwargs)
+            elif kind == "start_profile":
+                _start_profile(ctx, payload)
+                out = None
+            elif kind == "stop_profile":
+                out = _stop_profile(ctx)
             elif kind == "load":
                 factory, args, kwargs = payload
                 ctx.obj = factory(ctx, *args, **kwargs)
@@ -94,21 +142,28 @@ def _worker(rank: int, world_size: int, init_method: str, backend: str, layout: 
 
 
 class MPExecutor:
+    _pool: dict = {}
+
     def __init__(self, world_size: int, tp: int | None = None, dp: int = 1, backend: str | None = None,
-                 timeout_s: float = 120.0, init_timeout_s: float = 300.0, **layout):
+                 timeout_s: float = 120.0, init_timeout_s: float = 300.0, nnodes: int = 1, **layout):
         from .rendezvous import FileRendezvous
 
+        if nnodes < 1 or world_size % nnodes:
+            raise ValueError(f"world_size {world_size} is not a multiple of nnodes {nnodes}")
         self.world_size = world_size
+        self.nnodes = nnodes
         self.timeout_s = timeout_s
         self.backend = backend or ("nccl" if os.environ.get("VLLM_B200_EXECUTOR_GPU") == "1" else "gloo")
         lay = dict(tp=tp or world_size // dp, dp=dp)
         lay.update(layout)
+        self.layout = lay
         self._rdzv = FileRendezvous()
         ctx = mp.get_context("spawn")
         self._results = ctx.Queue()
         self._tasks = [ctx.Queue() for _ in range(world_size)]
         self._procs = [ctx.Process(target=_worker, args=(r, world_size, self._rdzv.init_method, self.backend, lay,
-                                                         self._tasks[r], self._results, timeout_s), daemon=True)
+                                                         self._tasks[r], self._results, timeout_s, nnodes),
+                                  daemon=True)
                        for r in range(world_size)]
         for p in self._procs:
             p.start()
@@ -168,9 +223,53 @@ class MPExecutor:
         self._send("load", (factory, args, kwargs))
         self._collect("ok")
 
+    def run_per_rank(self, fn: Callable, per_rank_args: list, **kwargs) -> list:
+        if len(per_rank_args) != self.world_size:
+            raise ValueError(f"{len(per_rank_args)} argument sets for {self.world_size} ranks")
+        per_rank = [tuple(a) if isinstance(a, (tuple, list)) else (a,) for a in per_rank_args]
+        self._send("run_per_rank", (fn, per_rank, kwargs))
+        return self._collect("ok")
+
     def reinit(self, **layout) -> None:
         self._send("reinit", layout)
         self._collect("ok")
+        self.layout = dict(layout)
+
+    def start_profile(self, out_dir: str) -> None:
+        self._send("start_profile", out_dir)
+        self._collect("ok")
+
+    def stop_profile(self) -> list:
+        """Per-rank Chrome trace paths."""
+        self._send("stop_profile", None)
+        return self._collect("ok")
+
+    @classmethod
+    def shared(cls, world_size: int, tp: int | None = None, dp: int = 1, **layout) -> "MPExecutor":
+        """A pooled executor per (world size, backend); reused and re-laid-out across calls.
+        ``shutdown_shared()`` (also run at interpreter exit) stops them."""
+        lay = dict(tp=tp or world_size // dp, dp=dp)
+        lay.update(layout)
+        backend = "nccl" if os.environ.get("VLLM_B200_EXECUTOR_GPU") == "1" else "gloo"
+        ex = cls._pool.get((world_size, backend))
+        if ex is not None and not ex._procs:
+            ex = None
+        if ex is None:
+            if not cls._pool:
+                import atexit
+
+                atexit.register(cls.shutdown_shared)
+            ex = cls(world_size, backend=backend, **lay)
+            cls._pool[(world_size, backend)] = ex
+        elif ex.layout != lay:
+            ex.reinit(**lay)
+        return ex
+
+    @classmethod
+    def shutdown_shared(cls) -> None:
+        for ex in list(cls._pool.values()):
+            ex.shutdown()
+        cls._pool.clear()
 
     def shutdown(self) -> None:
         if not self._procs:
