@@ -170,3 +170,50 @@ def test_executor_per_rank_inputs_nodes_profile_and_pool(tmp_path):
         assert b.run(_layout) == [(1, 2), (1, 2)]
     finally:
         MPExecutor.shutdown_shared()
+
+
+def _hier_case(ctx, T, H):
+    """Flat vs two-hop all-to-all of the same per-rank data, and EP dispatch + combine through
+    both exchanges (experts: a fixed per-expert scale)."""
+    import torch.distributed as dist
+
+    from vllm_neuron_b200.parallel.all2all import EpAll2All, hierarchical_all_to_all
+
+    ps = ctx.ps
+    W = ps.world.world_size
+    g = torch.Generator().manual_seed(100 + ctx.rank)
+    t = torch.randn(W, T, H, generator=g)
+    flat = torch.empty_like(t)
+    dist.all_to_all_single(flat, t, group=ps.world.device_group)
+    hier = hierarchical_all_to_all(t, ps.node, ps.inter_node)
+    exact = bool(torch.equal(flat, hier))
+    E_local, k = 2, 2
+    x = torch.randn(T, H, generator=g)
+    ids = torch.stack([torch.randperm(E_local * W, generator=g)[:k] for _ in range(T)])
+    w = torch.rand(T, k, generator=g)
+    outs = []
+    for a2a in (EpAll2All(ps.world, H, k), EpAll2All(ps.world, H, k, (ps.node, ps.inter_node))):
+        rx, rid, rw = a2a.dispatch(x, ids, w, E_local, 0, T)
+        lo = ctx.rank * E_local
+        y = torch.zeros_like(rx)
+        for j in range(k):
+            e = rid[:, j].long()
+            mine = (e >= lo) & (e < lo + E_local)
+            y += torch.where(mine[:, None], rx * (1.0 + e[:, None].float()) * rw[:, j:j + 1], torch.zeros_like(rx))
+        outs.append(a2a.combine(y, T))
+    want = sum(x * (1.0 + ids[:, j:j + 1].float()) * w[:, j:j + 1] for j in range(k))
+    return exact, float((outs[0] - outs[1]).abs().max()), float((outs[1] - want).abs().max()), ps.degrees["nnodes"]
+
+
+def test_hierarchical_all_to_all_two_nodes():
+    """Two simulated nodes of two ranks: the node and positional-peer groups exist, the two-hop
+    exchange equals the flat one bit for bit, and the EP all-to-all gives the same combined
+    output through either."""
+    from vllm_neuron_b200.parallel.state import build_node_group_ranks
+    from vllm_neuron_b200.utils.executor import MPExecutor
+
+    assert build_node_group_ranks(16, 2) == ([list(range(8)), list(range(8, 16))],
+                                             [[i, i + 8] for i in range(8)])
+    with MPExecutor(world_size=4, tp=4, nnodes=2, timeout_s=120) as ex:
+        for exact, d_paths, d_math, nn in ex.run(_hier_case, 5, 16):
+            assert exact and d_paths < 1e-6 and d_math < 1e-4 and nn == 2

@@ -144,7 +144,7 @@ class Worker:
         if not layers or self.cfg.all2all_backend == "allgather_reducescatter" or self.ps.world.world_size == 1:
             return
         a2a = make_ep_all2all(self.cfg.all2all_backend, self.ps.world, self.device, mcfg.hidden_size,
-                              mcfg.num_experts_per_tok, max_tokens=min(256, self.cfg.max_num_seqs))
+                              mcfg.num_experts_per_tok, max_tokens=min(256, self.cfg.max_num_seqs), ps=self.ps)
         for m in layers:
             m.a2a = a2a
         self.a2a = a2a

@@ -21,7 +21,12 @@ Semantics shared by both implementations here:
 
 ``FusedEpAll2All`` does this with the push kernels of ``csrc/ep_a2a.cu`` over NVLink peer
 memory (no host round trip, CUDA-graph safe).  ``EpAll2All`` is the collective baseline: a
-dense equal-split ``all_to_all`` of the same padded layout (NCCL on GPU, gloo on CPU).
+dense equal-split ``all_to_all`` of the same padded layout (NCCL on GPU, gloo on CPU).  In a
+multi-node job it exchanges in two hops (``hierarchical_all_to_all``): first within each node,
+to the local rank at the destination's local position, then between those positional peers
+across nodes, so every row crosses the inter-node network once and the many small per-rank
+messages become one message per node pair and local position (the reference's inter-node
+positional peer groups, ``parallel/neuron_parallel_state.py:280``).
 """
 
 from __future__ import annotations
@@ -55,22 +60,46 @@ def compact(ids: torch.Tensor, E_local: int, world: int, t0: int, t1: int) -> to
     return torch.where(hit, pos, torch.full_like(pos, -1)).to(torch.int32)
 
 
+def hierarchical_all_to_all(t: torch.Tensor, node_group, peer_group) -> torch.Tensor:
+    """Equal-split all-to-all of ``t`` [W, ...] (row d goes to rank d; ranks node-major,
+    ``W = nodes x P``) in two hops; the result equals the flat exchange: row s holds what
+    rank s sent here.  Hop 1 (``node_group``, P ranks): rows for (any node, local l) go to
+    local rank l.  Hop 2 (``peer_group``, one rank per node at the same local position):
+    rows for node n go to that node's peer."""
+    P, N = node_group.world_size, peer_group.world_size
+    W = t.shape[0]
+    if W != N * P:
+        raise ValueError(f"{W} rows for {N} nodes x {P} ranks")
+    rest = tuple(t.shape[1:])
+    # [dest node, dest local, ...] -> [dest local, dest node, ...]: one chunk per local peer
+    send1 = t.reshape((N, P) + rest).transpose(0, 1).contiguous()
+    recv1 = torch.empty_like(send1)  # [src local, dest node, ...]
+    dist.all_to_all_single(recv1, send1, group=node_group.device_group)
+    send2 = recv1.transpose(0, 1).contiguous()  # [dest node, src local, ...]
+    recv2 = torch.empty_like(send2)  # [src node, src local, ...]
+    dist.all_to_all_single(recv2, send2, group=peer_group.device_group)
+    return recv2.reshape((W,) + rest)
+
+
 class EpAll2All:
     """Collective baseline: every rank sends T padded rows to every rank."""
 
     fused = False
 
-    def __init__(self, group, hidden: int, top_k: int):
+    def __init__(self, group, hidden: int, top_k: int, hierarchy: tuple | None = None):
         self.group = group
         self.world = group.world_size
         self.rank = group.rank_in_group
         self.H, self.k = hidden, top_k
+        self.hierarchy = hierarchy  # (node group, positional peer group) of a multi-node job
         self._send_idx: torch.Tensor | None = None
 
     def can(self, T: int) -> bool:
         return True
 
     def _a2a(self, t: torch.Tensor) -> torch.Tensor:
+        if self.hierarchy is not None:
+            return hierarchical_all_to_all(t, *self.hierarchy)
         out = torch.empty_like(t)
         dist.all_to_all_single(out, t.contiguous(), group=self.group.device_group)
         return out
@@ -187,13 +216,20 @@ class FusedEpAll2All:
         self._opened = []
 
 
-def make_ep_all2all(backend: str, group, device: torch.device, hidden: int, top_k: int, max_tokens: int = 256):
+def make_ep_all2all(backend: str, group, device: torch.device, hidden: int, top_k: int, max_tokens: int = 256,
+                    ps=None):
     """The all-to-all object for ``all2all_backend`` (None: all-gather / reduce-scatter path).
-    Collective when it builds the fused path: every rank of ``group`` calls it."""
+    Collective when it builds the fused path: every rank of ``group`` calls it.  ``ps``: the
+    parallel state; in a multi-node job whose EP group is the whole world the collective path
+    exchanges hierarchically."""
     if backend not in A2A_BACKENDS:
         raise ValueError(f"all2all_backend must be one of {A2A_BACKENDS}, got {backend!r}")
     if backend == "allgather_reducescatter" or group.world_size == 1:
         return None
-    if backend in ("neuron", "b200") and device.type == "cuda" and group.world_size <= 8:
+    multi_node = ps is not None and getattr(ps, "nnodes", 1) > 1 and ps.node is not None
+    if backend in ("neuron", "b200") and device.type == "cuda" and group.world_size <= 8 and not multi_node:
         return FusedEpAll2All(group, device, hidden, top_k, max_tokens)
-    return EpAll2All(group, hidden, top_k)
+    hier = None
+    if multi_node and list(group.ranks) == list(range(ps.world.world_size)):
+        hier = (ps.node, ps.inter_node)
+    return EpAll2All(group, hidden, top_k, hier)

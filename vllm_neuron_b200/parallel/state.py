@@ -330,6 +330,12 @@ class ParallelState:
     embedding_dp: GroupCoordinator | None = None
     lm_head_dp: GroupCoordinator | None = None
     mlp_dp: GroupCoordinator | None = None
+    # multi-node jobs: the ranks of this node, and the ranks at this rank's local position on
+    # every node (``_build_inter_node_positional_peer_group_ranks``,
+    # ``neuron_parallel_state.py:280``); both None on one node
+    nnodes: int = 1
+    node: GroupCoordinator | None = None
+    inter_node: GroupCoordinator | None = None
 
     def component(self, name: str) -> tuple[GroupCoordinator, GroupCoordinator | None]:
         """(sharding group, DP gather group or None) of the "embedding", "lm_head" or "mlp"
@@ -392,11 +398,27 @@ def init_distributed_environment(world_size: int = 1, rank: int = 0, backend: st
     dist.init_process_group(**kw)
 
 
+def build_node_group_ranks(world_size: int, nnodes: int) -> tuple[list[list[int]], list[list[int]]]:
+    """(ranks of each node, positional peers): ranks are dealt to nodes in contiguous blocks;
+    peer group l holds local position l of every node."""
+    if nnodes < 1 or world_size % nnodes:
+        raise ValueError(f"world size {world_size} not divisible by nnodes {nnodes}")
+    per = world_size // nnodes
+    return ([[n * per + l for l in range(per)] for n in range(nnodes)],
+            [[n * per + l for n in range(nnodes)] for l in range(per)])
+
+
+def _default_nnodes(world_size: int) -> int:
+    """Nodes of a torchrun job (``LOCAL_WORLD_SIZE`` ranks per node), else one."""
+    local = int(os.environ.get("LOCAL_WORLD_SIZE", "0") or 0)
+    return world_size // local if local > 0 and world_size % local == 0 else 1
+
+
 def initialize_parallel_state(tp: int = 1, dp: int = 1, ep_degree: int = 1, attention_dp_size: int = 1,
                               embedding_dp_size: int = 1, lm_head_dp_size: int = 1, mlp_dp_size: int = 1,
                               dcp: int = 1, vision_tp: int | None = None, vision_dp: int | None = None,
                               backend: str | None = None, timeout_s: float = 1800.0,
-                              sampling_dp: int = 1) -> ParallelState:
+                              sampling_dp: int = 1, nnodes: int | None = None) -> ParallelState:
     """Build every group (``initialize_neuron_parallel_state``, ``neuron_parallel_state.py:863``)."""
     global _STATE
     from .. import envs
@@ -466,11 +488,18 @@ def initialize_parallel_state(tp: int = 1, dp: int = 1, ep_degree: int = 1, atte
     # holds a slice of the experts for these tokens: the whole world when the
     # tokens are replicated across DP (wide EP), else the TP group.
     moe_g = world_g if ep_degree > 1 else mlp_g
+    nn = nnodes if nnodes is not None else _default_nnodes(world_size)
+    node_g = inter_g = None
+    if nn > 1:
+        node_rows, peer_rows = build_node_group_ranks(world_size, nn)
+        node_g = _new_groups("node", node_rows, rank, backend, to)
+        inter_g = _new_groups("inter_node", peer_rows, rank, backend, to)
+    degrees["nnodes"] = nn
     _STATE = ParallelState(world=world_g, tp=tp_g, dp=dp_g, ep=ep_g, ep_tp=eptp_g, moe=moe_g, attn_tp=attn_tp_g,
                            attn_dp=attn_dp_g, dcp_kv=dcp_kv_g, dcp_head=dcp_head_g, embedding=emb_g,
                            lm_head=lmh_g, mlp=mlp_g, vision_tp=vtp_g, vision_dp=vdp_g, degrees=degrees,
                            sampling_a2a=sa2a_g, sampling_gather=sgat_g, embedding_dp=emb_dp_g,
-                           lm_head_dp=lmh_dp_g, mlp_dp=mlp_dp_g)
+                           lm_head_dp=lmh_dp_g, mlp_dp=mlp_dp_g, nnodes=nn, node=node_g, inter_node=inter_g)
     logger.info("parallel state: %s", degrees)
     return _STATE
 

@@ -102,7 +102,7 @@ def _worker(rank: int, world_size: int, init_method: str, backend: str, layout: 
             ctx.device = torch.device("cpu")
         pstate.init_distributed_environment(world_size, rank, backend=backend, init_method=init_method,
                                             local_rank=rank, timeout_s=timeout_s)
-        ctx.ps = pstate.initialize_parallel_state(backend=backend, timeout_s=timeout_s, **layout)
+        ctx.ps = pstate.initialize_parallel_state(backend=backend, timeout_s=timeout_s, nnodes=nnodes, **layout)
         results.put((rank, "ready", None))
     except Exception:  # noqa: BLE001
         results.put((rank, "error", traceback.format_exc()))
@@ -129,7 +129,8 @@ def _worker(rank: int, world_size: int, init_method: str, backend: str, layout: 
                 out = None
             elif kind == "reinit":
                 pstate.destroy_parallel_state()
-                ctx.ps = pstate.initialize_parallel_state(backend=backend, timeout_s=timeout_s, **payload)
+                ctx.ps = pstate.initialize_parallel_state(backend=backend, timeout_s=timeout_s, nnodes=nnodes,
+                                                          **payload)
                 out = None
             else:
                 raise ValueError(f"unknown task {kind}")
