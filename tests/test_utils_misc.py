@@ -145,3 +145,18 @@ def test_device_offset_moves_every_rank(monkeypatch):
     assert Worker(cfg, rank=1, world_size=4, local_rank=1).device_index == 1
     monkeypatch.setenv("VLLM_B200_DEVICE_OFFSET", "4")
     assert Worker(cfg, rank=1, world_size=4, local_rank=1).device_index == 5
+
+
+def test_cross_node_loopback_master_addr_refused(monkeypatch):
+    """Several nodes (LOCAL_WORLD_SIZE below the world size) with a loopback MASTER_ADDR are
+    refused before any rendezvous; one node, or a routable address, passes."""
+    from vllm_neuron_b200.parallel.state import validate_master_addr
+
+    monkeypatch.setenv("LOCAL_WORLD_SIZE", "4")
+    monkeypatch.setenv("MASTER_ADDR", "127.0.0.1")
+    with pytest.raises(ValueError, match="loopback"):
+        validate_master_addr(8)
+    validate_master_addr(4)  # one node
+    validate_master_addr(8, "file:///tmp/x")  # not an env:// rendezvous
+    monkeypatch.setenv("MASTER_ADDR", "10.1.2.3")
+    validate_master_addr(8)

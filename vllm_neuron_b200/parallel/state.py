@@ -386,6 +386,7 @@ def init_distributed_environment(world_size: int = 1, rank: int = 0, backend: st
 
         init_method = init_method_from_env()  # file store of ranks spawned on this host
     if init_method is None:
+        validate_master_addr(world_size)
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         os.environ.setdefault("MASTER_PORT", "29533")
         init_method = "env://"
@@ -396,6 +397,26 @@ def init_distributed_environment(world_size: int = 1, rank: int = 0, backend: st
     if backend == "nccl":
         kw["device_id"] = torch.device("cuda", local_rank)
     dist.init_process_group(**kw)
+
+
+_LOOPBACK = ("127.0.0.1", "localhost", "::1", "0.0.0.0")
+
+
+def validate_master_addr(world_size: int, init_method: str | None = None) -> None:
+    """A job spread over several nodes cannot rendezvous on a loopback address: the ranks of
+    the other nodes would each wait on their own host until the timeout.  Raise a clear error
+    instead (``validate_cross_node_master_addr``, ``vllm/worker/neuron_worker.py:56``).  Only
+    ``env://`` rendezvous is checked; the nodes come from ``LOCAL_WORLD_SIZE``."""
+    if _default_nnodes(world_size) <= 1:
+        return
+    if init_method not in (None, "env://"):
+        return
+    addr = os.environ.get("MASTER_ADDR", "127.0.0.1")
+    if addr in _LOOPBACK:
+        raise ValueError(f"{_default_nnodes(world_size)} nodes ({world_size} ranks, LOCAL_WORLD_SIZE="
+                         f"{os.environ.get('LOCAL_WORLD_SIZE')}) but MASTER_ADDR={addr!r} is a loopback address; "
+                         "set MASTER_ADDR (torchrun --master-addr / --rdzv-endpoint) to the head node's address "
+                         "on every node")
 
 
 def build_node_group_ranks(world_size: int, nnodes: int) -> tuple[list[list[int]], list[list[int]]]:
