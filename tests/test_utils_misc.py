@@ -160,3 +160,43 @@ def test_cross_node_loopback_master_addr_refused(monkeypatch):
     validate_master_addr(8, "file:///tmp/x")  # not an env:// rendezvous
     monkeypatch.setenv("MASTER_ADDR", "10.1.2.3")
     validate_master_addr(8)
+
+
+def _quick(ready):
+    ready.set()
+
+
+def _ignores_sigterm(ready):
+    import signal
+    import time
+
+    signal.signal(signal.SIGTERM, signal.SIG_IGN)
+    ready.set()
+    time.sleep(60)
+
+
+def _sleeps(ready):
+    import time
+
+    ready.set()
+    time.sleep(60)
+
+
+def test_stop_workers_escalates_to_sigkill():
+    """A worker that exits is joined; one that hangs gets SIGTERM; one that ignores SIGTERM is
+    killed after the termination timeout."""
+    import multiprocessing as mp
+    import time
+
+    from vllm_neuron_b200.engine.llm import stop_workers
+
+    ctx = mp.get_context("spawn")
+    events = [ctx.Event() for _ in range(3)]
+    procs = [ctx.Process(target=f, args=(e,), daemon=True) for f, e in zip((_quick, _sleeps, _ignores_sigterm), events)]
+    for p in procs:
+        p.start()
+    assert all(e.wait(60) for e in events)
+    procs[0].join(30)
+    t0 = time.monotonic()
+    assert stop_workers(procs, grace_s=1.0, term_timeout_s=1.0) == ["exited", "terminated", "killed"]
+    assert time.monotonic() - t0 < 15 and not any(p.is_alive() for p in procs)

@@ -16,6 +16,38 @@ from .sampling_params import RequestOutput, SamplingParams
 logger = init_logger(__name__)
 
 
+def stop_workers(procs: list, grace_s: float = 30.0, term_timeout_s: float | None = None) -> list[str]:
+    """Stop worker processes that were told to shut down: wait up to ``grace_s`` (in total) for
+    them to exit, send SIGTERM to the ones still running, and SIGKILL whatever is left after
+    ``term_timeout_s`` (default ``VLLM_B200_WORKER_TERMINATION_TIMEOUT``), so a wedged worker
+    cannot hold the shutdown (the reference patches the same SIGTERM -> SIGKILL escalation,
+    ``vllm/platform.py:783``).  Returns how each process ended ("exited", "terminated",
+    "killed")."""
+    import time
+
+    from .. import envs
+
+    if term_timeout_s is None:
+        term_timeout_s = float(envs.VLLM_B200_WORKER_TERMINATION_TIMEOUT)
+    deadline = time.monotonic() + grace_s
+    how = ["exited"] * len(procs)
+    for p in procs:
+        p.join(timeout=max(0.0, deadline - time.monotonic()))
+    for i, p in enumerate(procs):
+        if p.is_alive():
+            p.terminate()
+            how[i] = "terminated"
+    deadline = time.monotonic() + term_timeout_s
+    for i, p in enumerate(procs):
+        if how[i] == "terminated":
+            p.join(timeout=max(0.0, deadline - time.monotonic()))
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=5)
+                how[i] = "killed"
+    return how
+
+
 def merge_samples(request_id: str, outs: list[RequestOutput]) -> RequestOutput:
     """One RequestOutput with the n completions of a prompt (index = sample number)."""
     if len(outs) == 1:
@@ -145,10 +177,7 @@ class LLM:
 
     def shutdown(self) -> None:
         self.engine.shutdown()
-        for p in self._procs:
-            p.join(timeout=30)
-            if p.is_alive():
-                p.terminate()
+        stop_workers(self._procs)
         self._procs = []
         if getattr(self, "_rdzv", None) is not None:
             self._rdzv.close()
