@@ -157,3 +157,45 @@ def test_decode_bench_connector_skips_prefill(tmp_path):
         assert len(o.outputs[0].token_ids) == 5
         assert o.num_cached_tokens == len(p) - 1
     assert st["loaded"] == 2
+
+
+def test_bidirectional_kv_multi_turn(tmp_path, monkeypatch):
+    """Two conversation turns over 1P1D with decode -> prefill KV: after turn 1 the decode
+    engine exports the conversation so far; turn 2's prefill engine (kv_both) loads that prefix
+    (checked byte-exact by the synthetic model) and computes only the new tokens, then hands the
+    whole prompt to the decode engine.  A transfer whose tokens do not match the prompt is
+    ignored and the prompt computed locally."""
+    from vllm_neuron_b200 import SamplingParams
+    from vllm_neuron_b200.models.synthetic import TOKEN_EMPTY, TOKEN_SUCCESS
+
+    monkeypatch.setenv("VLLM_B200_BIDIRECTIONAL_KV", "1")
+    store = str(tmp_path / "kv")
+    sp1 = SamplingParams(temperature=0, max_tokens=1, ignore_eos=True)
+    sp4 = SamplingParams(temperature=0, max_tokens=4, ignore_eos=True)
+    prefill, decode = _llm("kv_both", store), _llm("kv_consumer", store)
+    try:
+        turn1 = list(range(1, 30))
+        p1 = prefill.generate([{"prompt_token_ids": turn1, "kv_transfer_params": {"do_remote_decode": True}}], sp1)
+        assert p1[0].outputs[0].token_ids == [TOKEN_EMPTY]
+        d1 = decode.generate([{"prompt_token_ids": turn1, "kv_transfer_params": p1[0].kv_transfer_params}], sp4)
+        out1 = list(d1[0].outputs[0].token_ids)
+        assert out1 == [TOKEN_SUCCESS] * 4
+        back = d1[0].kv_transfer_params
+        assert back and back["do_remote_prefill"] and back["num_tokens"] == len(turn1) + 3
+        # turn 2: the conversation so far plus the user's new tokens
+        turn2 = turn1 + out1 + [11, 12, 13, 14, 15]
+        p2 = prefill.generate([{"prompt_token_ids": turn2, "kv_transfer_params": {**back, "do_remote_decode": True}}],
+                              sp1)
+        assert p2[0].num_cached_tokens == len(turn1) + 3  # the prefix came from the decode engine
+        assert p2[0].outputs[0].token_ids == [TOKEN_SUCCESS]  # and it verified byte-exact
+        assert prefill.engine.connector.stats["loaded"] == 1
+        d2 = decode.generate([{"prompt_token_ids": turn2, "kv_transfer_params": p2[0].kv_transfer_params}], sp4)
+        assert d2[0].outputs[0].token_ids == [TOKEN_SUCCESS] * 4
+        # a prompt that does not extend the transferred conversation ignores the transfer
+        other = [7] * 40
+        p3 = prefill.generate([{"prompt_token_ids": other, "kv_transfer_params": {**back, "do_remote_decode": True}}],
+                              sp1)
+        assert p3[0].num_cached_tokens == 0 and prefill.engine.connector.stats["loaded"] == 1
+    finally:
+        prefill.shutdown()
+        decode.shutdown()

@@ -33,6 +33,16 @@ from .request import Request, RequestStatus
 logger = init_logger(__name__)
 
 
+def token_hash(tokens) -> str:
+    """Fingerprint of a token sequence carried with a KV transfer, so the receiver can check
+    that the KV belongs to its prompt's prefix."""
+    import hashlib
+
+    import numpy as np
+
+    return hashlib.sha1(np.asarray(list(tokens), dtype=np.int64).tobytes()).hexdigest()
+
+
 @dataclass
 class ScheduledSeq:
     req_id: str
@@ -83,6 +93,10 @@ class Scheduler:
         self.on_finish: list = []  # callbacks(request_id), e.g. encoder-cache release
         self.on_preempt: list = []  # callbacks(request_id), e.g. recurrent-state slot release
         self.connector = None  # KV-transfer connector (disaggregated prefill / decode)
+        # decode -> prefill KV for multi-turn chats (VLLM_B200_BIDIRECTIONAL_KV)
+        from .. import envs
+
+        self.bidirectional_kv = bool(envs.VLLM_B200_BIDIRECTIONAL_KV)
         self.failed: list[Request] = []  # aborted at admission; the engine reports them
 
     # ------------------------------------------------------------------ queue
@@ -106,10 +120,21 @@ class Scheduler:
 
     def _finish(self, req: Request) -> None:
         c = self.connector
-        if (c is not None and c.is_producer and (req.kv_transfer_params or {}).get("do_remote_decode")
-                and req.status != RequestStatus.FINISHED_ABORTED and req.block_ids):
+        p = req.kv_transfer_params or {}
+        ok = req.status != RequestStatus.FINISHED_ABORTED and bool(req.block_ids)
+        if c is not None and c.is_producer and p.get("do_remote_decode") and ok:
             # hand the prompt KV to the decode engine before the blocks are freed
             req.kv_transfer_params_out = c.export(req.request_id, req.block_ids, req.num_prompt_tokens)
+            req.kv_transfer_params_out["token_hash"] = token_hash(req.prompt_token_ids)
+        elif (c is not None and c.is_consumer and p.get("do_remote_prefill") and ok and self.bidirectional_kv
+              and req.num_computed_tokens > 0):
+            # bidirectional KV (decode -> prefill): the conversation so far (prompt and output,
+            # every token whose KV is written) goes back, so the next turn's prefill engine loads
+            # it instead of recomputing it
+            n = req.num_computed_tokens
+            out = c.export(req.request_id + "-d2p", req.block_ids, n)
+            out["token_hash"] = token_hash((list(req.prompt_token_ids) + list(req.output_token_ids))[:n])
+            req.kv_transfer_params_out = out
         for cb in self.on_finish:
             cb(req.request_id)
         if req in self.running:
@@ -257,12 +282,25 @@ class Scheduler:
         return SchedulerOutput("decode", seqs, finished=finished)
 
     def _remote_prefill_tokens(self, req: Request) -> int:
+        """Prompt positions whose KV comes from the remote engine: all but the last prompt
+        token when the transfer covers the whole prompt (prefill -> decode), the transferred
+        prefix when it is a shorter conversation prefix (decode -> prefill, the next turn's
+        prompt extends it).  A transfer whose token hash does not match this prompt's prefix,
+        or shorter than ``remote_pull_threshold`` tokens, is ignored (computed locally)."""
         p = req.kv_transfer_params or {}
         if self.connector is not None and getattr(self.connector, "prefill_all", False):
             return max(0, req.num_prompt_tokens - 1)  # decode benchmarking: every prompt counts as prefilled
         if self.connector is None or not self.connector.is_consumer or not p.get("do_remote_prefill"):
             return 0
-        return max(0, min(int(p.get("num_tokens", 0)), req.num_prompt_tokens) - 1)
+        n = min(int(p.get("num_tokens", 0)), req.num_prompt_tokens)
+        if "token_hash" in p and token_hash(req.prompt_token_ids[:n]) != p["token_hash"]:
+            logger.warning("request %s: transferred KV is for other tokens; computing the prompt here",
+                           req.request_id)
+            return 0
+        threshold = int((getattr(self.connector, "extra", None) or {}).get("remote_pull_threshold", 0))
+        if n < max(threshold, 1):
+            return 0
+        return max(0, min(n, req.num_prompt_tokens - 1))
 
     def _budget_left(self, pre: list[Request]) -> int:
         return self.max_num_batched_tokens - sum(self._prefill_chunk(r) for r in pre)

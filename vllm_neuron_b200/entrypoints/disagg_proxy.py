@@ -7,6 +7,12 @@ For every ``/v1/completions`` request it
 2. forwards the original request to the decode server with the ``kv_transfer_params`` the
    prefill server returned (the decode engine loads the KV and generates), streaming or not.
 
+Multi-turn chats with bidirectional KV (``VLLM_B200_BIDIRECTIONAL_KV=1`` on both servers, the
+prefill server in ``kv_role: kv_both``): the decode server's (non-streaming) response carries
+``kv_transfer_params`` for the conversation so far; a client that sends them back with the next
+turn's request makes the prefill server load that prefix from the decode server instead of
+recomputing it (the reference proxy relays the decode side's block ids the same way).
+
 ``vllm-b200 disagg-proxy --prefill http://127.0.0.1:8100 --decode http://127.0.0.1:8200 --port 8000``
 """
 
@@ -35,7 +41,8 @@ def build_proxy(prefill_url: str, decode_url: str, post: PostFn | None = None) -
     stats = {"requests": 0, "transfers": 0}
 
     async def _prefill(body: dict) -> dict:
-        pb = dict(body, max_tokens=1, stream=False, kv_transfer_params={"do_remote_decode": True})
+        prev = body.get("kv_transfer_params") or {}  # a previous turn's decode -> prefill transfer
+        pb = dict(body, max_tokens=1, stream=False, kv_transfer_params={**prev, "do_remote_decode": True})
         resp = await post(prefill_url.rstrip("/") + "/v1/completions", pb)
         kvp = resp.get("kv_transfer_params")
         if not kvp:
