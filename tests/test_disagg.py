@@ -199,3 +199,35 @@ def test_bidirectional_kv_multi_turn(tmp_path, monkeypatch):
     finally:
         prefill.shutdown()
         decode.shutdown()
+
+
+def test_streamed_response_carries_kv_transfer_params(tmp_path):
+    """A prefill server's streamed completion ends with a chunk that carries the
+    kv_transfer_params (non-streamed: in the response body)."""
+    import json
+
+    from fastapi.testclient import TestClient
+
+    from vllm_neuron_b200.engine.async_engine import AsyncLLM
+    from vllm_neuron_b200.entrypoints.openai_server import build_app
+
+    store = str(tmp_path / "kv")
+    eng = AsyncLLM(hf_config=dict(SYN), load_format="dummy", dtype="bfloat16", max_model_len=256, max_num_seqs=4,
+                   max_num_batched_tokens=256, block_size=16, device="cpu",
+                   kv_transfer_config={"kv_connector": "HostStagedConnector", "kv_role": "kv_producer",
+                                       "kv_connector_extra_config": {"store_path": store}})
+    try:
+        with TestClient(build_app(eng, "syn")) as c:
+            body = {"model": "syn", "prompt": list(range(1, 30)), "max_tokens": 1, "temperature": 0,
+                    "kv_transfer_params": {"do_remote_decode": True}}
+            plain = c.post("/v1/completions", json=body).json()
+            assert plain["kv_transfer_params"]["do_remote_prefill"]
+            chunks = []
+            with c.stream("POST", "/v1/completions", json=dict(body, stream=True)) as resp:
+                for line in resp.iter_lines():
+                    if line.startswith("data: {"):
+                        chunks.append(json.loads(line[6:]))
+            assert chunks and chunks[-1]["kv_transfer_params"]["do_remote_prefill"]
+            assert all("kv_transfer_params" not in ch for ch in chunks[:-1])
+    finally:
+        eng.shutdown()

@@ -144,8 +144,13 @@ def build_app(engine: AsyncLLM, served_name: str):
                     ch = ({"index": 0, "delta": {"content": delta}, "finish_reason": o.outputs[0].finish_reason}
                           if chat else {"index": 0, "text": delta, "finish_reason": o.outputs[0].finish_reason})
                     ch["token_ids"] = new
-                    yield "data: " + json.dumps({"id": rid, "object": obj + ".chunk", "created": created,
-                                                 "model": served_name, "choices": [ch]}) + "\n\n"
+                    chunk = {"id": rid, "object": obj + ".chunk", "created": created, "model": served_name,
+                             "choices": [ch]}
+                    if o.finished and o.kv_transfer_params is not None:
+                        # disaggregated serving: the final chunk carries the transfer parameters
+                        # (e.g. decode -> prefill KV of a multi-turn chat)
+                        chunk["kv_transfer_params"] = o.kv_transfer_params
+                    yield "data: " + json.dumps(chunk) + "\n\n"
                 yield "data: [DONE]\n\n"
 
             return StreamingResponse(gen(), media_type="text/event-stream")
