@@ -2,21 +2,32 @@
 
 ``python bench.py --gpus N --steps K --warmup W`` (N > 1 under torch.distributed.run).
 
-Workload (BASELINE.json config 3 shape): 64 concurrent requests of 2048 synthetic
-random prompt tokens, random-init weights of the GPT-OSS-120B architecture (36 layers,
-hidden 2880, 64 q / 8 kv heads of 64, 128 experts top-4, MXFP4 experts, bf16 rest).
-All 64 prompts are prefilled through the engine, then decode runs at batch 64:
-* ``value``  device-timed decode throughput: K replays of the captured decode step
-  (forward + LM head + sampling for 64 sequences) between CUDA events, after W warm-up
-  steps; tokens/s = 64 * K / t, t = max over ranks.  Weights (~60 GB) exceed L2, so no
-  flush is needed between steps.
-* ``e2e``    the same metric through the public engine API (``LLMEngine.step``, asynchronous
-  scheduling): every step schedules, stages its inputs in pinned host memory, copies them
-  H2D, replays the graph and reads the sampled ids back D2H (the host work of step k+1
-  overlaps step k on the GPU).
-Parallelism for N GPUs: attention TP=N (heads), experts EP=N, one all-reduce after
-attention and one after the MoE per layer (NCCL); total concurrency stays 64 (strong
-scaling).  ``--impl reference`` runs the reference plugin when it can run here.
+Workload (BASELINE.json config 3 shape): a closed serving loop that keeps 64 requests in
+flight, the way ``vllm bench serve --max-concurrency 64`` drives a server.  Every request has
+2048 synthetic random prompt tokens and generates 512 tokens (greedy, ignore EOS); weights are
+random-init with the GPT-OSS-120B architecture (36 layers, hidden 2880, 64 q / 8 kv heads of
+64, 128 experts top-4, MXFP4 experts, bf16 rest).  When a request finishes, a new one is
+submitted at once, so the engine alternates one 2048-token prefill (admission of the
+replacement) with about eight decode steps at batch 64: the steady state of serving at
+concurrency 64, whose output rate is the headline metric.  The 64 first requests get staggered
+output lengths (8, 16, ..., 512 tokens) so that completions are evenly spread from the start.
+
+A benchmark *step* is one serving period of that steady state: from one completion to the
+next (the replacement's prefill plus the decode steps until the next request finishes).
+W periods are run untimed, then K periods are timed:
+* ``value``  output tokens of the K periods / device time, where device time is the sum of
+  every engine step's GPU span (CUDA events recorded around each step's H2D staging, forward,
+  sampling and D2H enqueue; host gaps between steps excluded), max over ranks.  The weights
+  (~60 GB) and KV cache exceed L2 many times over every step, so no flush is needed.
+* ``e2e``    the same output tokens / wall-clock time of the same window through the public
+  engine API (``LLMEngine.add_request`` / ``LLMEngine.step``): scheduling, pinned-memory H2D
+  of every step's inputs, the forward, and the D2H read of the sampled ids, max over ranks.
+* ``config.ttft_p50_ms`` / ``tpot_p50_ms``: medians over the requests of the window (arrival
+  to first token; per-request mean interval between later tokens).  ``decode_only_tok_s``:
+  K x 8 replays of the captured batch-64 decode graph between CUDA events (no prefill).
+Parallelism for N GPUs: attention TP=N (heads), experts EP=N; each layer boundary is one
+fused NVLink all-reduce + residual + RMSNorm kernel; total concurrency stays 64 (strong
+scaling).  ``--impl reference`` reports why the reference plugin cannot run here.
 """
 
 from __future__ import annotations
@@ -105,7 +116,7 @@ def run_reference(args) -> None:
     try:
         import vllm_neuron.functional  # noqa: F401
     except Exception as e:  # noqa: BLE001
-        reason = (f"reference installs from /root/reference but cannot run on B200: "
+        reason = (f"the reference installs (baseline/_ref) but cannot run on B200: "
                   f"importing vllm_neuron.functional fails ({type(e).__name__}: {e}); it targets AWS Trainium "
                   f"(NKI kernels, neuronx-cc) and sets CUDA_VISIBLE_DEVICES='' at import")
     rank = int(os.environ.get("RANK", "0"))
@@ -113,15 +124,13 @@ def run_reference(args) -> None:
         print(json.dumps({"impl": "reference", "unavailable": reason or "reference has no CUDA execution path"}))
 
 
-def _profile_replays(graph, n: int) -> tuple[int, int, str]:
-    """Replay the decode graph n times under torch.profiler: (launches of this library's
-    kernels per replay, all kernels per replay, per-kernel table)."""
+def _count_our_kernels(fn) -> tuple[int, int, str]:
+    """Run ``fn`` under torch.profiler (CUDA activity): (launches of this library's kernels,
+    all kernel launches, per-kernel table)."""
     import torch
 
-    acts = [torch.profiler.ProfilerActivity.CUDA]
-    with torch.profiler.profile(activities=acts) as prof:
-        for _ in range(n):
-            graph.replay()
+    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+        fn()
         torch.cuda.synchronize()
     ours = total = 0
     for ev in prof.events():
@@ -130,21 +139,81 @@ def _profile_replays(graph, n: int) -> tuple[int, int, str]:
             if "b200::" in ev.name:
                 ours += 1
     table = prof.key_averages().table(sort_by="self_cuda_time_total", row_limit=40)
-    return ours // n, total // n, table
+    return ours, total, table
+
+
+class ClosedLoop:
+    """Keeps ``C`` requests in flight through the public engine API: every finished request
+    is replaced by a new prompt at once.  Records arrival / token timestamps per request."""
+
+    def __init__(self, eng, vocab: int, C: int, P: int, O: int, seed: int = 1234):
+        import torch
+
+        from vllm_neuron_b200 import SamplingParams
+
+        self.eng, self.C, self.P, self.O = eng, C, P, O
+        self.SamplingParams = SamplingParams
+        self.g = torch.Generator().manual_seed(seed)
+        self.vocab = vocab
+        self.n_added = 0
+        self.arrival: dict[str, float] = {}
+        self.first: dict[str, float] = {}
+        self.seen: dict[str, int] = {}
+        self.tok_times: dict[str, list[float]] = {}
+        self.completions = 0
+
+    def add(self, max_tokens: int) -> None:
+        import torch
+
+        rid = f"bench-{self.n_added}"
+        self.n_added += 1
+        prompt = torch.randint(0, self.vocab - 1000, (self.P,), generator=self.g).tolist()
+        self.eng.add_request(rid, prompt, self.SamplingParams(temperature=0.0, max_tokens=max_tokens, ignore_eos=True))
+        self.arrival[rid] = time.perf_counter()
+        self.seen[rid] = 0
+
+    def fill(self) -> None:
+        """C requests with staggered output lengths (O/C, 2 O/C, ..., O): completions are evenly
+        spread from the first decode step on, as in the steady state."""
+        for i in range(self.C):
+            self.add(max(1, (i + 1) * self.O // self.C))
+
+    def step(self, record: bool) -> tuple[int, int]:
+        """One engine step; returns (new output tokens, completions).  Replaces finished requests."""
+        outs = self.eng.step()
+        now = time.perf_counter()
+        new_tok = done = 0
+        for o in outs:
+            rid = o.request_id
+            n = len(o.outputs[0].token_ids)
+            k = n - self.seen.get(rid, 0)
+            if k > 0:
+                new_tok += k
+                self.seen[rid] = n
+                if rid not in self.first:
+                    self.first[rid] = now
+                if record:
+                    self.tok_times.setdefault(rid, []).extend([now] * k)
+            if o.finished:
+                done += 1
+        self.completions += done
+        for _ in range(done):
+            self.add(self.O)
+        return new_tok, done
 
 
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=20, help="timed serving periods")
+    ap.add_argument("--warmup", type=int, default=5, help="untimed serving periods")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--model", default="gpt-oss-120b", choices=["gpt-oss-120b", "gpt-oss-20b"])
     ap.add_argument("--concurrency", type=int, default=64)
     ap.add_argument("--prompt-len", type=int, default=2048)
     ap.add_argument("--output-len", type=int, default=512)
     ap.add_argument("--profile-dir", default=None,
-                    help="also write a per-kernel table of profiled decode-step replays (rank 0)")
+                    help="also write a per-kernel table of one profiled serving period (rank 0)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -155,14 +224,14 @@ def main() -> None:
     import torch
     import torch.distributed as dist
 
-    from vllm_neuron_b200 import LLM, SamplingParams
+    from vllm_neuron_b200 import LLM
 
     N = args.gpus
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     hf = GPT_OSS_120B if args.model == "gpt-oss-120b" else GPT_OSS_20B
-    C, P = args.concurrency, args.prompt_len
-    max_len = P + args.output_len + 64
+    C, P, O = args.concurrency, args.prompt_len, args.output_len
+    max_len = P + O + 64
     t0 = time.time()
     llm = LLM(hf_config=hf, load_format="dummy", dtype="bfloat16", tensor_parallel_size=N,
               max_model_len=max_len, max_num_seqs=C, max_num_batched_tokens=4096, block_size=32,
@@ -170,110 +239,131 @@ def main() -> None:
               additional_config={"neuron_config": {"ep_degree": N, "quantization": "mxfp4",
                                                    "num_seqs_buckets": [C]}})
     eng = llm.engine
+    runner = eng.worker.runner
     torch.cuda.synchronize()
     t_load = time.time() - t0
-    g = torch.Generator().manual_seed(1234)
-    prompts = [torch.randint(0, hf["vocab_size"] - 1000, (P,), generator=g).tolist() for _ in range(C)]
-    sp = SamplingParams(temperature=0.0, max_tokens=args.output_len, ignore_eos=True)
-    # ---- prefill all requests (TTFT per request from engine metrics) ----
-    for i, p in enumerate(prompts):
-        eng.add_request(f"bench-{i}", p, sp)
-    t_pf = time.time()
-    while any(r.num_computed_tokens < r.num_prompt_tokens for r in eng.scheduler.requests.values()):
-        eng.step()
-    torch.cuda.synchronize()
-    t_prefill = time.time() - t_pf
-    ttfts = sorted((r.metrics.first_token_time - r.metrics.arrival_time) for r in eng.scheduler.requests.values())
-    ttft_p50 = ttfts[len(ttfts) // 2]
-    runner = eng.worker.runner
-    if rank == 0:
-        print(f"# load {t_load:.1f}s prefill {t_prefill:.2f}s ({C * P / t_prefill:.0f} tok/s) ttft_p50 "
-              f"{ttft_p50 * 1000:.1f} ms", file=sys.stderr)
 
     def barrier():
         if dist.is_initialized():
             dist.barrier()
         torch.cuda.synchronize()
 
-    # ---- e2e through the public API: LLMEngine.step() (schedule, pinned H2D, replay, D2H) ----
-    for _ in range(args.warmup):
-        eng.step()
+    loop = ClosedLoop(eng, hf["vocab_size"], C, P, O)
+    # ---- fill: C prompts prefilled back to back (the burst at the start of a serving run) ----
+    loop.fill()
+    t_pf = time.time()
+    while any(r.num_computed_tokens < r.num_prompt_tokens for r in eng.scheduler.requests.values()):
+        loop.step(False)
+    torch.cuda.synchronize()
+    t_fill = time.time() - t_pf
+    if rank == 0:
+        print(f"# load {t_load:.1f}s, fill prefill of {C}x{P} tokens {t_fill:.2f}s ({C * P / t_fill:.0f} tok/s)",
+              file=sys.stderr)
+
+    def run_periods(n: int, record: bool) -> tuple[int, list[int], list[int]]:
+        """Steps until ``n`` more requests completed: (output tokens, h2d bytes, d2h bytes per step)."""
+        tok, h2d, d2h = 0, [], []
+        target = loop.completions + n
+        while loop.completions < target:
+            t, _ = loop.step(record)
+            tok += t
+            h2d.append(runner.h2d_bytes_last)
+            d2h.append(runner.d2h_bytes_last)
+        return tok, h2d, d2h
+
+    # ---- warm-up periods (decode graph capture happens in the first decode step) ----
+    run_periods(args.warmup, False)
     clocks = ClockSampler(local)
     barrier()
     clocks.start()
-    h2d, d2h = [], []
-    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    w0 = time.perf_counter()
-    s_ev.record()
-    for _ in range(args.steps):
-        outs = eng.step()
-        h2d.append(runner.h2d_bytes_last)
-        d2h.append(runner.d2h_bytes_last)
-    e_ev.record()
-    barrier()
-    e2e_wall = time.perf_counter() - w0
-    e2e_ms = s_ev.elapsed_time(e_ev)
-    # ---- device-timed decode step: replay the captured decode graph K times ----
-    key = next(k for k in runner.graphs if k[0] == C) if runner.graphs else None
-    if key is None:
-        raise SystemExit("decode graph for the benchmark batch was not captured")
-    graph = runner.graphs[key].graph
-    for _ in range(args.warmup):
-        graph.replay()
-    barrier()
-    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s2.record()
-    for _ in range(args.steps):
-        graph.replay()
-    e2.record()
-    barrier()
-    dev_ms = s2.elapsed_time(e2)
+    # ---- timed window: K serving periods through the public engine API ----
+    runner.step_spans = []
+    window_start = time.perf_counter()
+    arrivals_before = loop.n_added
+    tokens, h2d, d2h = run_periods(args.steps, True)
+    wall_s = time.perf_counter() - window_start
+    torch.cuda.synchronize()
+    spans = runner.step_spans
+    runner.step_spans = None
+    dev_ms = sum(a.elapsed_time(b) for a, b in spans)
+    n_engine_steps = len(h2d)
+    # TTFT of the requests that arrived in the window and got their first token in it
+    window_ids = [f"bench-{i}" for i in range(arrivals_before, loop.n_added)]
+    ttfts = sorted(loop.first[r] - loop.arrival[r] for r in window_ids if r in loop.first)
+    # TPOT: per request, mean interval between its tokens after the first one seen in the window
+    tpots = []
+    for rid, ts in loop.tok_times.items():
+        if len(ts) >= 3:
+            tpots.append((ts[-1] - ts[0]) / (len(ts) - 1))
+    tpots.sort()
+    # ---- secondary: decode-only graph replays (device-timed, no prefill) ----
+    key = next((k for k in runner.graphs if k[0] == C), None)
+    dec_ms = float("nan")
+    n_dec = 8 * args.steps
+    if key is not None:
+        graph = runner.graphs[key].graph
+        for _ in range(3):
+            graph.replay()
+        barrier()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(n_dec):
+            graph.replay()
+        e2.record()
+        barrier()
+        dec_ms = s2.elapsed_time(e2)
+        del graph
     clk = clocks.stop()
-    tms = torch.tensor([dev_ms, e2e_ms, max(e2e_wall * 1000, e2e_ms)], dtype=torch.float64)
+    tms = torch.tensor([dev_ms, wall_s * 1000.0, dec_ms if key is not None else 0.0], dtype=torch.float64)
     if dist.is_initialized():
         t = tms.cuda()
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         tms = t.cpu()
-    dev_ms, e2e_ms, e2e_wall_ms = tms.tolist()
-    ms_step = dev_ms / args.steps
-    value = C * args.steps / (dev_ms / 1000.0)
-    e2e_val = C * args.steps / (e2e_wall_ms / 1000.0)
-    tpot_ms = e2e_wall_ms / args.steps
-    # kernel launches per decode step, counted from one profiled replay after the timed region
-    # (every rank replays so the graphs' collectives stay matched)
-    ours, total, table = _profile_replays(graph, 1 if not args.profile_dir else 5)
+    dev_ms, wall_ms, dec_ms = tms.tolist()
+    # ---- kernel launches of this library per serving period (one profiled period after timing;
+    # every rank runs it so the collectives stay matched) ----
+    ours, total, table = _count_our_kernels(lambda: run_periods(1, False))
     launches = ours * args.steps
     if rank == 0 and args.profile_dir:
         os.makedirs(args.profile_dir, exist_ok=True)
-        with open(os.path.join(args.profile_dir, f"decode_step_kernels_n{N}.txt"), "w") as f:
-            f.write(f"# {ours} launches of this library's kernels, {total} kernels in total, per decode step\n")
+        with open(os.path.join(args.profile_dir, f"serving_period_kernels_n{N}.txt"), "w") as f:
+            f.write(f"# one serving period: {ours} launches of this library's kernels, {total} kernels in total\n")
             f.write(table)
+    value = tokens / (dev_ms / 1000.0)
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": N, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16 (experts MXFP4 weights, MXFP8 activations)",
+            "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16 (experts MXFP4 weights, MXFP8 activations)",
             "data": "synthetic random prompt tokens; random-init weights (GPT-OSS-120B architecture)",
-            "config": {"model": args.model, "global_batch": C, "seq_len": P, "output_len": args.output_len,
-                       "parallelism": f"tp{N}-ep{N}" if N > 1 else "single", "phase": "decode at concurrency "
-                       f"{C} after prefilling {C}x{P} tokens", "l2": "weights per step (~60 GB) exceed L2; no flush",
-                       "ttft_p50_ms": round(ttft_p50 * 1000, 2), "tpot_p50_ms": round(tpot_ms, 3),
-                       "prefill_tok_s": round(C * P / t_prefill, 1)},
-            "e2e": {"value": round(e2e_val, 2), "unit": "tokens/s", "api": "LLMEngine.step",
+            "config": {"model": args.model, "global_batch": C, "seq_len": P, "output_len": O,
+                       "parallelism": f"tp{N}-ep{N}" if N > 1 else "single",
+                       "phase": f"steady-state closed loop at concurrency {C}: each step is one serving period "
+                                f"(a finished request replaced by a new {P}-token prompt, its prefill, and the "
+                                f"decode steps until the next completion)",
+                       "l2": "weights (~60 GB) and KV exceed L2 every engine step; no flush",
+                       "output_tokens": tokens, "engine_steps": n_engine_steps,
+                       "ttft_p50_ms": round(1000 * ttfts[len(ttfts) // 2], 2) if ttfts else None,
+                       "tpot_p50_ms": round(1000 * tpots[len(tpots) // 2], 3) if tpots else None,
+                       "requests_in_window": len(ttfts),
+                       "decode_only_tok_s": round(C * n_dec / (dec_ms / 1000.0), 1) if key is not None else None,
+                       "fill_prefill_tok_s": round(C * P / t_fill, 1)},
+            "e2e": {"value": round(tokens / (wall_ms / 1000.0), 2), "unit": "tokens/s",
+                    "api": "LLMEngine.add_request + LLMEngine.step (closed loop, wall clock)",
                     "h2d_bytes_per_step": int(statistics.mean(h2d)), "d2h_bytes_per_step": int(statistics.mean(d2h))},
             "gpu_launches": launches,
             "clocks": clk,
         }
         print(json.dumps(line))
-    # Graphs that captured NCCL calls must be freed before the process group is destroyed,
-    # including the local reference taken above; then leave without interpreter teardown.
-    del graph
+        sys.stdout.flush()
+    # Graphs that captured NCCL calls are freed before the process group is destroyed
+    # (worker shutdown releases them, then destroys the groups); then a normal exit.
     runner.release_graphs()
     torch.cuda.synchronize()
-    sys.stdout.flush()
     llm.shutdown()
-    sys.stdout.flush()
-    os._exit(0)
+    if dist.is_initialized():
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":

@@ -5,6 +5,8 @@ request within the connector timeout instead of blocking the engine."""
 
 import os
 
+import time
+
 import pytest
 
 SYN = {"architectures": ["SyntheticModel"], "num_hidden_layers": 3, "num_key_value_heads": 4, "head_dim": 16,
@@ -177,10 +179,16 @@ def test_bidirectional_kv_multi_turn(tmp_path, monkeypatch):
         turn1 = list(range(1, 30))
         p1 = prefill.generate([{"prompt_token_ids": turn1, "kv_transfer_params": {"do_remote_decode": True}}], sp1)
         assert p1[0].outputs[0].token_ids == [TOKEN_EMPTY]
-        d1 = decode.generate([{"prompt_token_ids": turn1, "kv_transfer_params": p1[0].kv_transfer_params}], sp4)
+        # without ``return_kv`` the decode engine exports nothing when the request finishes
+        d0 = decode.generate([{"prompt_token_ids": turn1, "kv_transfer_params": p1[0].kv_transfer_params}], sp4)
+        assert not d0[0].kv_transfer_params and decode.engine.connector.stats["exported"] == 0
+        p1 = prefill.generate([{"prompt_token_ids": turn1, "kv_transfer_params": {"do_remote_decode": True}}], sp1)
+        d1 = decode.generate([{"prompt_token_ids": turn1,
+                               "kv_transfer_params": {**p1[0].kv_transfer_params, "return_kv": True}}], sp4)
         out1 = list(d1[0].outputs[0].token_ids)
         assert out1 == [TOKEN_SUCCESS] * 4
         back = d1[0].kv_transfer_params
+        assert decode.engine.connector.exported[-1][1] - time.monotonic() <= 60.0  # the short return TTL
         assert back and back["do_remote_prefill"] and back["num_tokens"] == len(turn1) + 3
         # turn 2: the conversation so far plus the user's new tokens
         turn2 = turn1 + out1 + [11, 12, 13, 14, 15]

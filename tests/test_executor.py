@@ -217,3 +217,13 @@ def test_hierarchical_all_to_all_two_nodes():
     with MPExecutor(world_size=4, tp=4, nnodes=2, timeout_s=120) as ex:
         for exact, d_paths, d_math, nn in ex.run(_hier_case, 5, 16):
             assert exact and d_paths < 1e-6 and d_math < 1e-4 and nn == 2
+
+
+def test_hierarchical_all_to_all_one_rank_per_node():
+    """Two simulated nodes of one rank each: the node groups have a single rank, so the
+    in-node hop is skipped and the exchange still equals the flat one."""
+    from vllm_neuron_b200.utils.executor import MPExecutor
+
+    with MPExecutor(world_size=2, tp=2, nnodes=2, timeout_s=120) as ex:
+        for exact, d_paths, d_math, nn in ex.run(_hier_case, 3, 8):
+            assert exact and d_paths < 1e-6 and d_math < 1e-4 and nn == 2

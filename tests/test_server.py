@@ -19,6 +19,7 @@ def client():
                    max_num_seqs=4, max_num_batched_tokens=128, block_size=16, device="cpu",
                    additional_config={"neuron_config": {"quantization": "bf16"}})
     with TestClient(build_app(eng, "tiny")) as c:
+        c.b200_engine = eng
         yield c
     eng.shutdown()
 
@@ -56,6 +57,7 @@ def test_cli_engine_kwargs():
 
 
 def test_profile_endpoints(client, tmp_path, monkeypatch):
+    monkeypatch.setattr(client.b200_engine.engine.profiler.cfg, "output_dir", str(tmp_path))
     r = client.post("/start_profile")
     assert r.json()["status"] == "started"
     assert client.post("/start_profile").status_code == 400  # already running
@@ -65,6 +67,7 @@ def test_profile_endpoints(client, tmp_path, monkeypatch):
     import os
 
     assert os.path.exists(r["trace"]) and os.path.exists(r["summary"])
+    assert os.path.dirname(r["trace"]) == str(tmp_path)
     assert client.post("/stop_profile").status_code == 400
 
 

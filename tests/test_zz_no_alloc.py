@@ -5,7 +5,8 @@ process whose device memory another allocator has already reserved) use
 ``b200_paged_attention_decode_noalloc``: it takes only inputs and outputs and keeps its
 split-KV partials in a fixed array inside the library.  This test checks its output against
 the regular entry point (``torch.ops.b200.paged_attention_decode`` with a caller-provided
-workspace) on two calls in a row, and that an oversized request is refused.  The file is
+workspace) on two calls in a row that both use the shared array, and that oversized or
+malformed requests are refused.  The file is
 named so that pytest collects it last."""
 
 import ctypes
@@ -17,7 +18,8 @@ import torch
 pytestmark = pytest.mark.gpu
 
 DEV = "cuda"
-SCRATCH_TOO_SMALL = 5
+SCRATCH_TOO_SMALL = 1005  # kScratchTooSmall (csrc/common.cuh)
+BAD_SHAPE = 1003  # kBadShape
 
 
 def _lib():
@@ -32,10 +34,10 @@ def _lib():
     return fn
 
 
-def _case(seed):
+def _case(seed, seq_lens=(1, 40, 700, 2049, 5000), nq=16, nkv=2):
     g = torch.Generator(device="cpu").manual_seed(seed)
-    seq_lens = [1, 40, 700, 2049, 5000]
-    B, nq, nkv, d, bs = len(seq_lens), 16, 2, 64, 32
+    seq_lens = list(seq_lens)
+    B, d, bs = len(seq_lens), 64, 32
     max_blocks = max(math.ceil(s / bs) for s in seq_lens)
     nb = sum(math.ceil(s / bs) for s in seq_lens) + 1
     perm = torch.randperm(nb - 1, generator=g) + 1
@@ -61,10 +63,14 @@ def _call(fn, out, q, kc, vc, bt, sl, sinks, splits, window, scale):
 
 
 def test_noalloc_matches_workspace_entry_point_twice():
+    """Two calls in a row whose split counts (5, then 3) both merge through the shared
+    scratch array, with different shapes, so the second call runs on whatever the first
+    one left there."""
     fn = _lib()
     scale = 64 ** -0.5
-    for call, (seed, splits, window) in enumerate([(0, 8, 0), (1, 5, 128)]):
-        q, kc, vc, bt, sl, sinks = _case(seed)
+    cases = [(0, 5, 0, (1, 40, 700, 2049, 5000), 16, 2), (1, 3, 128, (3000, 17, 260), 8, 1)]
+    for call, (seed, splits, window, lens, nq, nkv) in enumerate(cases):
+        q, kc, vc, bt, sl, sinks = _case(seed, lens, nq, nkv)
         B, nq, d = q.shape
         ws = torch.empty(B * nq * splits * (d + 1), device=DEV)
         want = torch.empty_like(q)
@@ -75,6 +81,19 @@ def test_noalloc_matches_workspace_entry_point_twice():
         torch.cuda.synchronize()
         err = (got.float() - want.float()).abs().max().item()
         assert err <= 1e-2, f"call {call}: max abs difference {err}"
+
+
+def test_noalloc_rejects_bad_shape():
+    fn = _lib()
+    q, kc, vc, bt, sl, sinks = _case(3)
+    out = torch.empty_like(q)
+    B, nq, d = q.shape
+    stream = torch.cuda.current_stream().cuda_stream
+    for nkv in (0, 3):  # no kv heads; query heads not a multiple of the kv heads
+        rc = fn(out.data_ptr(), q.data_ptr(), kc.data_ptr(), vc.data_ptr(), bt.data_ptr(), sl.data_ptr(),
+                sinks.data_ptr(), B, nq, nkv, d, q.stride(0), kc.shape[2], bt.stride(0), 0, 0.125, 1.0, 1.0, 5,
+                2, 2, stream)
+        assert rc == BAD_SHAPE
 
 
 def test_noalloc_rejects_oversized_request():

@@ -882,8 +882,11 @@ extern "C" int b200_varlen_attention(void* out, const void* q, const void* k, co
 // Limits and contract:
 //   * scratch is a file-scope __device__ array of kNoAllocScratchFloats floats (4 MiB).  Every
 //     GPU that loads this library reserves it until the process exits.  A call needs
-//     B * nq * num_splits * (d + 1) floats when num_splits > 1 (none when num_splits == 1);
-//     larger requests are rejected with kScratchTooSmall and launch nothing.
+//     B * nq * num_splits * (d + 1) floats when its splits merge through the scratch (any
+//     count above 1 except 2, 4 and 8, which merge inside a thread-block cluster, unless
+//     VLLM_B200_DECODE_CLUSTER=0); a call that needs more is rejected with kScratchTooSmall
+//     (1005) and launches nothing.  Bad shapes (including nkv <= 0 or nq % nkv != 0) return
+//     kBadShape (1003).
 //   * the device address of the array is looked up once per device with
 //     cudaGetSymbolAddress, on the first call made while that device is current; issue that
 //     first call before any stream capture on the device.
@@ -896,7 +899,6 @@ extern "C" int b200_varlen_attention(void* out, const void* q, const void* k, co
 namespace {
 
 constexpr size_t kNoAllocScratchFloats = size_t(1) << 20;
-constexpr int kScratchTooSmall = 5;
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) float g_decode_scratch[kNoAllocScratchFloats];
@@ -929,11 +931,14 @@ extern "C" int b200_paged_attention_decode_noalloc(void* out, const void* q, con
                                                    int block_size, int max_blocks, int window, float scale,
                                                    float k_scale, float v_scale, int num_splits, int dtype,
                                                    int cache_dtype, cudaStream_t s) {
-  if (num_splits < 1 || B < 0 || nq <= 0 || d <= 0) return kBadShape;
-  const size_t need = num_splits > 1 ? (size_t)B * nq * num_splits * (d + 1) : 0;
+  if (num_splits < 1 || B < 0 || nq <= 0 || d <= 0 || nkv <= 0 || nq % nkv) return kBadShape;
+  // 2, 4 or 8 splits merge inside a thread-block cluster and touch no scratch
+  const bool cluster = (num_splits == 2 || num_splits == 4 || num_splits == 8) && decode_cluster_enabled();
+  const bool uses_scratch = num_splits > 1 && !cluster;
+  const size_t need = uses_scratch ? (size_t)B * nq * num_splits * (d + 1) : 0;
   if (need > kNoAllocScratchFloats) return kScratchTooSmall;
   float* ws = nullptr;
-  if (num_splits > 1) {
+  if (uses_scratch) {
     const int rc = scratch_for_current_device(&ws);
     if (rc) return rc;
   }

@@ -24,7 +24,7 @@
 // reductions into local memory accesses.  Double buffering makes the slot written at epoch e
 // disjoint from the one a peer may still read at epoch e-1; reuse two calls later is safe
 // because passing barrier e-1 proves every peer has finished epoch e-2 (stream order).
-// Waits give up after ~2 s and set status.
+// Waits give up after `wait_ns` (2 s by default) and set status to kWaitTimeout.
 #include "common.cuh"
 #include "launch_pdl.h"
 #include "launch.h"
@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(256) allreduce_fused_kernel(CommPeers peers, c
                                                               __nv_bfloat16* __restrict__ residual,
                                                               const __nv_bfloat16* __restrict__ bias,
                                                               const float* __restrict__ w, float eps, int T, int H,
-                                                              int* status) {
+                                                              unsigned long long wait_ns, int* status) {
   pdl_wait();  // predecessor output visible (programmatic dependent launch)
   pdl_trigger();
   __shared__ float red[32];
@@ -116,7 +116,7 @@ __global__ void __launch_bounds__(256) allreduce_fused_kernel(CommPeers peers, c
       for (uint32_t i = 1;; ++i) {
         if (ld_acquire_sys(f) >= epoch) break;
         if ((i & 255) == 0) {
-          if (now_ns() - t0 > 2000000000ull) {
+          if (now_ns() - t0 > wait_ns) {
             if (status) atomicCAS(status, 0, kWaitTimeout);
             break;
           }
@@ -222,9 +222,11 @@ extern "C" int b200_ipc_open_handle(const void* handle64, void** out) {
 
 extern "C" int b200_ipc_close(void* p) { return (int)cudaIpcCloseMemHandle(p); }
 
+// wait_ns: limit of each CTA's wait for its peers (0 = kDefaultWaitNs).
 extern "C" int b200_allreduce_fused(void* const* bases, int rank, int world, size_t slot_bytes, const void* in,
                                     void* out, void* residual, const void* bias, const float* w, float eps, int T,
-                                    int H, int num_blocks, int* status, cudaStream_t s) {
+                                    int H, int num_blocks, unsigned long long wait_ns, int* status, cudaStream_t s) {
+  if (wait_ns == 0) wait_ns = kDefaultWaitNs;
   if (world > kMaxRanks || world < 1 || H % 8 || H > 8192 || T < 0) return kBadShape;
   if ((size_t)T * H * 2 * world > slot_bytes || (slot_bytes / world) % 16) return kBadShape;
   if (num_blocks < 1 || num_blocks > kMaxBlocks) return kBadShape;
@@ -237,9 +239,9 @@ extern "C" int b200_allreduce_fused(void* const* bases, int rank, int world, siz
   if (w != nullptr)
     launch_k(allreduce_fused_kernel<true>, dim3(num_blocks), dim3(256), 0, s, peers, (const __nv_bfloat16*)in, (__nv_bfloat16*)out,
                                                            (__nv_bfloat16*)residual, (const __nv_bfloat16*)bias, w,
-                                                           eps, T, H, status);
+                                                           eps, T, H, wait_ns, status);
   else
     launch_k(allreduce_fused_kernel<false>, dim3(num_blocks), dim3(256), 0, s, peers, (const __nv_bfloat16*)in, (__nv_bfloat16*)out,
-                                                            nullptr, nullptr, nullptr, eps, T, H, status);
+                                                            nullptr, nullptr, nullptr, eps, T, H, wait_ns, status);
   return (int)cudaGetLastError();
 }

@@ -14,15 +14,26 @@
 namespace b200 {
 
 // Error codes written to device status words by kernels that validate inputs or
-// bound their waits.  A kernel never traps: it records the first error and skips
-// the offending access.
+// bound their waits, and returned by the extern "C" entry points.  A kernel never
+// traps: it records the first error and skips the offending access.
+//
+// Return-code ranges of every entry point (disjoint, so a caller can tell them apart):
+//   0              success
+//   1 .. 999       a cudaError_t from the launch or a runtime call
+//   1001 .. 1099   a StatusCode below (validation or bounded-wait failure)
+//   2000 + r       cuTensorMapEncodeTiled failed with CUresult r
 enum StatusCode : int {
   kOk = 0,
-  kBadIndex = 1,      // block id / slot / token id out of range
-  kWaitTimeout = 2,   // bounded spin on a flag gave up
-  kBadShape = 3,
-  kBadAlignment = 4,
+  kBadIndex = 1001,         // block id / slot / token id out of range
+  kWaitTimeout = 1002,      // bounded spin on a flag gave up
+  kBadShape = 1003,
+  kBadAlignment = 1004,
+  kScratchTooSmall = 1005,  // a fixed-size scratch array cannot hold the request
 };
+constexpr int kTensorMapErrorBase = 2000;
+// Default limit of a bounded device-side wait (ns): long enough for any peer that is
+// alive, short enough that a dead peer surfaces as kWaitTimeout instead of a hang.
+constexpr unsigned long long kDefaultWaitNs = 2000000000ull;
 
 template <typename T> B200_D float to_float(T v);
 template <> B200_D float to_float<float>(float v) { return v; }

@@ -84,13 +84,13 @@ B200_D uint64_t ep_now_ns() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
-// bounded wait (~2 s) for *f >= epoch; on timeout sets the status word and gives up
+// bounded wait (kDefaultWaitNs) for *f >= epoch; on timeout sets the status word and gives up
 B200_D void ep_wait(const uint32_t* f, uint32_t epoch, int* status) {
   if (ep_ld_acquire(f) >= epoch) return;
   const uint64_t t0 = ep_now_ns();
   for (uint32_t i = 1;; ++i) {
     if (ep_ld_acquire(f) >= epoch) return;
-    if ((i & 255) == 0 && ep_now_ns() - t0 > 2000000000ull) {
+    if ((i & 255) == 0 && ep_now_ns() - t0 > kDefaultWaitNs) {
       if (status) atomicCAS(status, 0, kWaitTimeout);
       return;
     }

@@ -524,7 +524,7 @@ static int make_weight_map(CUtensorMap* m, const void* w, int n_tiles, int fmt) 
                           : (b16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8), 3,
                    const_cast<void*>(w), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? 0 : 1000 + (int)r;
+  return r == CUDA_SUCCESS ? 0 : kTensorMapErrorBase + (int)r;
 }
 
 // 2-D bf16 activation map: K valid columns (TMA zero-fills beyond), row stride ld elements,
@@ -539,7 +539,7 @@ static int make_act_map_bf16(CUtensorMap* m, const void* a, int R, int K, int ld
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a), dims, strides, box, es,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? 0 : 1000 + (int)r;
+  return r == CUDA_SUCCESS ? 0 : kTensorMapErrorBase + (int)r;
 }
 
 // 2-D activation map [R, Kp] e4m3, box 128 x NT.
@@ -553,7 +553,7 @@ static int make_act_map(CUtensorMap* m, const void* q, int R, int Kp, int nt) {
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(q), dims, strides, box, es,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? 0 : 1000 + (int)r;
+  return r == CUDA_SUCCESS ? 0 : kTensorMapErrorBase + (int)r;
 }
 
 static int num_sms() {

@@ -45,7 +45,7 @@ B200_D uint64_t globaltimer_ns() {
 }
 // Bounded wait: gives up after ~`limit_ns` (default 2 s) or as soon as another CTA has
 // recorded an error in *status; records kWaitTimeout and returns false.
-B200_D bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, uint64_t limit_ns = 2000000000ull) {
+B200_D bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, uint64_t limit_ns = kDefaultWaitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {

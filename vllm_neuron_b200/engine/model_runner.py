@@ -197,6 +197,11 @@ class ModelRunner:
             self.debug_logits = DebugLogitsWriter(nc.debug_logits_dir, self.sampler.group, vocab_size)
         self.d2h_bytes_last = 0
         self.step_count = 0
+        # optional device timing of every step: a list that receives one (start, end) pair of
+        # CUDA events per step, recorded around the step's GPU work (H2D staging, forward,
+        # sampling, D2H enqueue); None = off.  Benchmarks sum the spans for the device time
+        # of a serving window without the host gaps between steps.
+        self.step_spans: list | None = None
         # accuracy tooling: tensor capture / replacement hooks (eager steps only)
         self.capture = self.replacer = None
         rank = tp_group.rank_in_group if hasattr(tp_group, "rank_in_group") else 0
@@ -633,6 +638,7 @@ class ModelRunner:
         elif so.kind == "idle" or not so.seqs:
             return {}
         self.step_count += 1
+        span0 = self._span_start()
         n = len(so.seqs)
         pad_to = None
         is_plain_decode = so.kind == "decode" and all(len(s.token_ids) == 1 for s in so.seqs)
@@ -666,6 +672,7 @@ class ModelRunner:
             self.replacer.next_step()
         # D2H of the sampled ids (the step's only device->host traffic)
         self.h_out[:n_sel].copy_(out_d, non_blocking=out_d.is_cuda)
+        self._span_end(span0)
         if out_d.is_cuda:
             torch.cuda.current_stream().synchronize()
         self.d2h_bytes_last = n_sel * 8
@@ -715,6 +722,19 @@ class ModelRunner:
                 and not any(s.request is not None and (s.request.sampling_params.logprobs is not None
                                                        or s.request.grammar is not None) for s in so.seqs))
 
+    def _span_start(self):
+        if self.step_spans is None or self.device.type != "cuda":
+            return None
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        return ev
+
+    def _span_end(self, start) -> None:
+        if start is not None and self.step_spans is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.step_spans.append((start, ev))
+
     def _event(self):
         if self.device.type == "cuda":
             ev = torch.cuda.Event()
@@ -729,6 +749,7 @@ class ModelRunner:
         memory, replay the decode graph and queue the D2H copy of the sampled ids.
         ``commit`` waits for it."""
         self.step_count += 1
+        span0 = self._span_start()
         n = len(so.seqs)
         pad_to = get_bucket_for_count(n, self.decode_buckets) if self.use_graphs else n
         NUM_SEQS_PADDING.labels(model_name=self.cfg.served_model_name or "model").observe(pad_to - n)
@@ -760,6 +781,7 @@ class ModelRunner:
         self._parity ^= 1
         host = self.h_out_async[self._parity]
         host[:n_sel].copy_(self.d_out[:n_sel], non_blocking=self.device.type == "cuda")
+        self._span_end(span0)
         ev = self._event()
         self.d2h_bytes_last = n_sel * 8
         return AsyncStep(so, n_sel, host, ev, {s.req_id: i for i, s in enumerate(so.seqs)})

@@ -126,13 +126,17 @@ class Scheduler:
             # hand the prompt KV to the decode engine before the blocks are freed
             req.kv_transfer_params_out = c.export(req.request_id, req.block_ids, req.num_prompt_tokens)
             req.kv_transfer_params_out["token_hash"] = token_hash(req.prompt_token_ids)
-        elif (c is not None and c.is_consumer and p.get("do_remote_prefill") and ok and self.bidirectional_kv
-              and req.num_computed_tokens > 0):
+        elif (c is not None and c.is_consumer and p.get("do_remote_prefill") and p.get("return_kv") and ok
+              and self.bidirectional_kv and req.num_computed_tokens > 0):
             # bidirectional KV (decode -> prefill): the conversation so far (prompt and output,
             # every token whose KV is written) goes back, so the next turn's prefill engine loads
-            # it instead of recomputing it
+            # it instead of recomputing it.  Only requests that ask for it (``return_kv``: the
+            # client expects another turn) pay for the export, which copies every layer's KV of
+            # the conversation (device pool, or device -> host + a file when the pool is absent
+            # or full) on the scheduler thread; the export expires after the connector's
+            # ``return_ttl_s`` (60 s by default) instead of its ``ttl_s``.
             n = req.num_computed_tokens
-            out = c.export(req.request_id + "-d2p", req.block_ids, n)
+            out = c.export(req.request_id + "-d2p", req.block_ids, n, ttl_s=getattr(c, "return_ttl_s", None))
             out["token_hash"] = token_hash((list(req.prompt_token_ids) + list(req.output_token_ids))[:n])
             req.kv_transfer_params_out = out
         for cb in self.on_finish:

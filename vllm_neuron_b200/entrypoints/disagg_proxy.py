@@ -8,10 +8,12 @@ For every ``/v1/completions`` request it
    prefill server returned (the decode engine loads the KV and generates), streaming or not.
 
 Multi-turn chats with bidirectional KV (``VLLM_B200_BIDIRECTIONAL_KV=1`` on both servers, the
-prefill server in ``kv_role: kv_both``): the decode server's (non-streaming) response carries
-``kv_transfer_params`` for the conversation so far; a client that sends them back with the next
-turn's request makes the prefill server load that prefix from the decode server instead of
-recomputing it (the reference proxy relays the decode side's block ids the same way).
+prefill server in ``kv_role: kv_both``): a request whose ``kv_transfer_params`` carry
+``"return_kv": true`` (the client expects another turn) makes the decode server export the
+conversation when it finishes, and its (non-streaming) response carries ``kv_transfer_params``
+for it; a client that sends them back with the next turn's request makes the prefill server
+load that prefix from the decode server instead of recomputing it (the reference proxy relays
+the decode side's block ids the same way).  Requests without the flag export nothing.
 
 ``vllm-b200 disagg-proxy --prefill http://127.0.0.1:8100 --decode http://127.0.0.1:8200 --port 8000``
 """
@@ -62,7 +64,8 @@ def build_proxy(prefill_url: str, decode_url: str, post: PostFn | None = None) -
             kvp = await _prefill(body)
         except Exception as e:  # noqa: BLE001
             return JSONResponse({"error": f"prefill failed: {e}"}, status_code=502)
-        db = dict(body, kv_transfer_params=kvp)
+        wants_kv_back = bool((body.get("kv_transfer_params") or {}).get("return_kv"))
+        db = dict(body, kv_transfer_params={**kvp, "return_kv": True} if wants_kv_back else kvp)
         if body.get("stream"):
             import aiohttp
 

@@ -47,6 +47,9 @@ class HostStagedConnector:
         os.makedirs(self.store, exist_ok=True)
         self.timeout_s = float(extra.get("timeout_s", 30.0))
         self.ttl_s = float(extra.get("ttl_s", 600.0))  # exported transfers older than this are removed
+        # decode -> prefill exports of multi-turn chats live shorter: the next turn either comes
+        # soon or never, and every export holds host (/dev/shm) or pool memory meanwhile
+        self.return_ttl_s = float(extra.get("return_ttl_s", 60.0))
         self.cleanup_on_shutdown = bool(extra.get("cleanup_on_shutdown", False))
         self.kv = kv_caches
         self.h0, self.nh = kv_head_range
@@ -55,7 +58,7 @@ class HostStagedConnector:
         self.engine_id = engine_id
         self.role = role
         self.extra = extra
-        self.exported: list[str] = []
+        self.exported: list[tuple[str, float]] = []  # (transfer id, expiry time)
         self.stats = {"exported": 0, "loaded": 0, "failed": 0, "bytes": 0}
 
     @property
@@ -73,9 +76,10 @@ class HostStagedConnector:
         return [(i, kv) for i, kv in enumerate(self.kv) if kv is not None]
 
     # ----------------------------------------------------------------- producer
-    def export(self, request_id: str, block_ids: list[int], num_tokens: int) -> dict:
+    def export(self, request_id: str, block_ids: list[int], num_tokens: int, ttl_s: float | None = None) -> dict:
         """Write this rank's KV of positions [0, num_tokens) and return the params the
-        decode engine needs."""
+        decode engine needs.  The export is removed after ``ttl_s`` (default: the
+        connector's ``ttl_s``) unless read earlier."""
         tid = f"{self.engine_id}-{request_id}"
         self._gc()
         nb = -(-num_tokens // self.bs)
@@ -89,7 +93,7 @@ class HostStagedConnector:
         tmp = self._path(tid, self.rank) + f".tmp{os.getpid()}"
         torch.save({"num_tokens": num_tokens, "heads": (self.h0, self.nh), "layers": layers}, tmp)
         os.replace(tmp, self._path(tid, self.rank))
-        self.exported.append((tid, time.monotonic()))
+        self.exported.append((tid, time.monotonic() + (self.ttl_s if ttl_s is None else ttl_s)))
         self.stats["exported"] += 1
         return {"do_remote_prefill": True, "transfer_id": tid, "num_tokens": num_tokens,
                 "remote_tp_size": self.tp, "remote_engine_id": self.engine_id}
@@ -133,7 +137,7 @@ class HostStagedConnector:
         now = time.monotonic()
         keep = []
         for tid, t in self.exported:
-            if now - t > self.ttl_s:
+            if now > t:
                 try:
                     os.remove(self._path(tid, self.rank))
                 except OSError:
@@ -183,7 +187,7 @@ class B200IpcConnector(HostStagedConnector):
         self.layer_ids = [i for i, _ in layers]
         self.pool = None
         self.pool_bytes = int(float(self.extra.get("pool_mb", 1024)) * (1 << 20)) // 256 * 256
-        self.ranges: list[tuple[str, int, int, float]] = []  # (transfer id, offset, size, created)
+        self.ranges: list[tuple[str, int, int, float]] = []  # (transfer id, offset, size, expiry)
         self._peers: dict[tuple[str, int], int] = {}
         from ..ops import device_status
 
@@ -214,7 +218,7 @@ class B200IpcConnector(HostStagedConnector):
         now = time.monotonic()
         keep = []
         for tid, off, size, t in self.ranges:
-            if os.path.exists(self._ack_path(tid, self.rank)) or now - t > self.ttl_s:
+            if os.path.exists(self._ack_path(tid, self.rank)) or now > t:
                 for p in (self._ack_path(tid, self.rank), self._meta_path(tid, self.rank)):
                     try:
                         os.remove(p)
@@ -230,18 +234,18 @@ class B200IpcConnector(HostStagedConnector):
             cur = off + size
         return cur if self.pool_bytes - cur >= need else None
 
-    def export(self, request_id: str, block_ids: list[int], num_tokens: int) -> dict:
+    def export(self, request_id: str, block_ids: list[int], num_tokens: int, ttl_s: float | None = None) -> dict:
         need = (2 * len(self.layer_ids) * num_tokens * self.nh * self.row_bytes + 255) // 256 * 256
         off = self._reserve(need) if self.pool is not None else None
         if off is None:
-            return {**super().export(request_id, block_ids, num_tokens), "transport": "host"}
+            return {**super().export(request_id, block_ids, num_tokens, ttl_s), "transport": "host"}
         tid = f"{self.engine_id}-{request_id}"
         nb = -(-num_tokens // self.bs)
         blocks = torch.tensor(block_ids[:nb], dtype=torch.int32, device=self.device)
         torch.ops.b200.kv_export(self.pool0 + off, self.kptr, self.vptr, blocks, num_tokens, self.nh,
                                  self.row_bytes, self.bs)
         torch.cuda.current_stream(self.device).synchronize()  # the consumer reads from another process
-        self.ranges.append((tid, off, need, time.monotonic()))
+        self.ranges.append((tid, off, need, time.monotonic() + (self.ttl_s if ttl_s is None else ttl_s)))
         meta = {"offset": off, "num_tokens": num_tokens, "heads": (self.h0, self.nh), "layers": self.layer_ids,
                 "row_bytes": self.row_bytes}
         tmp = self._meta_path(tid, self.rank) + f".tmp{os.getpid()}"
@@ -341,7 +345,7 @@ class DecodeBenchConnector:
         self.std = float(extra.get("fill_std", 1.0))
         self.stats = {"exported": 0, "loaded": 0, "failed": 0, "bytes": 0}
 
-    def export(self, request_id: str, block_ids: list[int], num_tokens: int) -> dict:
+    def export(self, request_id: str, block_ids: list[int], num_tokens: int, ttl_s: float | None = None) -> dict:
         return {}
 
     def load(self, params: dict, block_ids: list[int], num_tokens: int) -> None:

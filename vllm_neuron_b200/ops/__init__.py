@@ -26,7 +26,8 @@ _STATUS: dict = {}
 
 def device_status(device: torch.device) -> torch.Tensor:
     """Per-device int32 status word that kernels with bounded waits or index checks
-    write (0 = ok; see ``csrc/common.cuh`` StatusCode).  Read it with
+    write (0 = ok; codes 1001.. as in ``csrc/common.cuh`` StatusCode, so they never
+    collide with a ``cudaError_t``).  Read it with
     :func:`check_device_status` between steps."""
     key = str(device)
     t = _STATUS.get(key)
@@ -44,7 +45,8 @@ def check_device_status(device: torch.device) -> int:
     code, where, value, _ = t.tolist()
     if code:
         t.zero_()
-        names = {1: "index out of range", 2: "device wait timed out", 3: "bad shape", 4: "bad alignment"}
+        names = {1001: "index out of range", 1002: "device wait timed out", 1003: "bad shape",
+                 1004: "bad alignment", 1005: "scratch too small"}
         raise RuntimeError(f"kernel status {code} ({names.get(code, 'unknown')}) at check {where}, value {value}")
     return 0
 

@@ -73,9 +73,14 @@ def hierarchical_all_to_all(t: torch.Tensor, node_group, peer_group) -> torch.Te
     rest = tuple(t.shape[1:])
     # [dest node, dest local, ...] -> [dest local, dest node, ...]: one chunk per local peer
     send1 = t.reshape((N, P) + rest).transpose(0, 1).contiguous()
-    recv1 = torch.empty_like(send1)  # [src local, dest node, ...]
-    dist.all_to_all_single(recv1, send1, group=node_group.device_group)
+    if P == 1:  # one rank per node: nothing to exchange inside the node (its group is this rank)
+        recv1 = send1
+    else:
+        recv1 = torch.empty_like(send1)  # [src local, dest node, ...]
+        dist.all_to_all_single(recv1, send1, group=node_group.device_group)
     send2 = recv1.transpose(0, 1).contiguous()  # [dest node, src local, ...]
+    if N == 1:  # a single node: the first hop already delivered everything
+        return send2.reshape((W,) + rest)
     recv2 = torch.empty_like(send2)  # [src node, src local, ...]
     dist.all_to_all_single(recv2, send2, group=peer_group.device_group)
     return recv2.reshape((W,) + rest)

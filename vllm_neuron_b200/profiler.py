@@ -4,7 +4,8 @@
 
 * ``activities``: any of "cpu", "cuda" (default both; the reference's "device_profile" and
   "system_profile" map to "cuda" and "cpu");
-* ``output_dir``: where traces are written (default ``./b200_profiles``);
+* ``output_dir``: where traces are written (default ``<tmpdir>/vllm_b200_profiles``, outside
+  any source tree);
 * ``record_shapes``, ``with_stack``: passed to ``torch.profiler``;
 * ``max_steps``: stop automatically after this many engine steps (0 = until stopped).
 
@@ -18,6 +19,7 @@ attribution, not for reporting throughput.
 from __future__ import annotations
 
 import os
+import tempfile
 import time
 from dataclasses import dataclass, field
 
@@ -27,7 +29,7 @@ _ALIASES = {"device_profile": "cuda", "system_profile": "cpu"}
 @dataclass
 class ProfilerConfig:
     activities: list = field(default_factory=lambda: ["cpu", "cuda"])
-    output_dir: str = os.path.join(".", "b200_profiles")
+    output_dir: str = field(default_factory=lambda: os.path.join(tempfile.gettempdir(), "vllm_b200_profiles"))
     record_shapes: bool = False
     with_stack: bool = False
     max_steps: int = 0
