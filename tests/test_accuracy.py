@@ -367,3 +367,22 @@ def test_deterministic_replay_bitwise(llama, tmp_path):
     for b in l0:
         assert sorted(l0[b]) == sorted(l1[b])
         assert all(torch.equal(l0[b][p], l1[b][p]) for p in l0[b])
+
+
+def test_greedy_logit_gaps_zero_for_identical_engines(tmp_path):
+    """The end-to-end greedy checker: an engine checked against itself has no gaps."""
+    from vllm_neuron_b200 import LLM, SamplingParams
+    from vllm_neuron_b200.accuracy.testing import greedy_logit_gaps, write_tiny_gpt_oss_checkpoint
+
+    path = str(tmp_path / "ck")
+    write_tiny_gpt_oss_checkpoint(path)
+    llm = LLM(model=path, dtype="float32", device="cpu", max_model_len=256, max_num_seqs=2, block_size=16,
+              additional_config={"neuron_config": {"quantization": "mxfp4"}})
+    try:
+        prompts = [[5, 6, 7, 8], list(range(100, 140))]
+        outs = llm.generate(prompt_token_ids=prompts,
+                            sampling_params=SamplingParams(temperature=0.0, max_tokens=4, ignore_eos=True))
+        res = greedy_logit_gaps(llm.engine, prompts, [list(o.outputs[0].token_ids) for o in outs])
+    finally:
+        llm.shutdown()
+    assert res.n_tokens == 8 and res.max_gap < 1e-4 and res.exact_fraction == 1.0

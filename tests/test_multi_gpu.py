@@ -214,3 +214,109 @@ def test_fused_ep_all2all_two_gpus():
             if e > 2e-2:  # bf16 expert outputs summed over two ranks
                 bad.append(f"rank {rank} {kind} T={T} rel err {e}")
     assert not bad, bad
+
+
+def _nvls_worker(rank, world, port, q):
+    """Row-parallel GEMM + all-reduce + bias + residual + RMSNorm through
+    ``GroupCoordinator.linear_all_reduce_add_rmsnorm`` (the NVLS GEMM when the group has a
+    multicast mapping, else GEMM + fused all-reduce), against NCCL + fp32 math; eager over
+    varying token counts (parity flips), then inside a CUDA graph replayed with new inputs."""
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        import torch.distributed as dist
+
+        from vllm_neuron_b200.parallel import state as ps
+        from vllm_neuron_b200.parallel.communicator import attach_communicators, attach_reducers
+
+        torch.cuda.set_device(rank)
+        ps.init_distributed_environment(world, rank, backend="nccl", local_rank=rank, timeout_s=120)
+        st = ps.initialize_parallel_state(tp=world, backend="nccl", timeout_s=120)
+        dev = torch.device("cuda", rank)
+        attach_communicators(st, dev)
+        attach_reducers(st, dev)
+        g = st.tp
+        path = "nvls" if g.reducer is not None else "gemm+fused_ar"
+        H, Kr, eps = 2880, 512, 1e-5
+        torch.manual_seed(5 + rank)
+        W = (torch.randn(H, Kr, device=dev) * 0.05).bfloat16()
+
+        def ref(x, res, nw, bias):
+            p = x.float() @ W.float().t()
+            dist.all_reduce(p)
+            s = (p + bias.float()).bfloat16().float()
+            r = (s + res.float()).bfloat16()
+            rf = r.float()
+            return rf * torch.rsqrt(rf.pow(2).mean(-1, keepdim=True) + eps) * nw, r
+
+        errs = []
+        for call, T in enumerate([64, 1, 17, 64, 200, 3]):
+            torch.manual_seed(100 + call * 7 + rank)
+            x = torch.randn(T, Kr, device=dev).bfloat16()
+            torch.manual_seed(999 + call)  # identical on every rank
+            res = torch.randn(T, H, device=dev).bfloat16()
+            nw = torch.rand(H, device=dev) + 0.5
+            bias = (torch.randn(H, device=dev) * 0.1).bfloat16()
+            want, want_res = ref(x, res, nw, bias)
+            out, res_out = g.linear_all_reduce_add_rmsnorm(x, W, res.clone(), nw, eps, bias)
+            errs.append(("norm", (out.float() - want).abs().max().item(), want.abs().max().item()))
+            errs.append(("res", (res_out.float() - want_res.float()).abs().max().item(),
+                         want_res.float().abs().max().item()))
+        # CUDA graph: two chained boundaries captured once, replayed with new inputs
+        T = 64
+        x = torch.zeros(T, Kr, device=dev, dtype=torch.bfloat16)
+        res = torch.zeros(T, H, device=dev, dtype=torch.bfloat16)
+        nw = torch.ones(H, device=dev)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            g.linear_all_reduce_add_rmsnorm(x, W, res.clone(), nw, eps, None)
+        torch.cuda.current_stream().wait_stream(s)
+        res_g = res.clone()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            y1, _ = g.linear_all_reduce_add_rmsnorm(x, W, res_g, nw, eps, None)
+            y2, _ = g.linear_all_reduce_add_rmsnorm(y1[:, :Kr].contiguous(), W, res_g, nw, eps, None)
+        for rep in range(3):
+            torch.manual_seed(300 + rep * 11 + rank)
+            x.copy_(torch.randn(T, Kr, device=dev).bfloat16())
+            torch.manual_seed(400 + rep)
+            r0 = torch.randn(T, H, device=dev).bfloat16()
+            res_g.copy_(r0)
+            graph.replay()
+            torch.cuda.synchronize()
+            w1, r1 = ref(x, r0, nw, torch.zeros(H, device=dev))
+            w2, _ = ref(y1[:, :Kr].contiguous(), r1, nw, torch.zeros(H, device=dev))
+            errs.append(("graph1", (y1.float() - w1).abs().max().item(), w1.abs().max().item()))
+            errs.append(("graph2", (y2.float() - w2).abs().max().item(), w2.abs().max().item()))
+        torch.cuda.synchronize()
+        from vllm_neuron_b200 import ops
+
+        st_code = int(ops.device_status(dev)[0].item())
+        del graph
+        ps.destroy_parallel_state()
+        dist.destroy_process_group()
+        q.put((rank, errs, st_code, path, None))
+    except Exception:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, [], -1, None, traceback.format_exc()))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_gemm_allreduce_two_gpus():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_nvls_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, errs, code, path, tb in res:
+        assert tb is None, tb
+        assert code == 0, f"rank {rank} status {code}"
+        print(f"rank {rank}: path {path}")
+        for kind, e, mag in errs:
+            # bf16 outputs; the fp32 sums of the GEMM arrive in a different order than NCCL's
+            assert e <= 0.02 * max(1.0, mag), f"rank {rank} {kind}: max err {e} (magnitude {mag})"

@@ -110,3 +110,82 @@ def assert_close_three_way(reference: torch.Tensor, baseline: torch.Tensor, actu
     if not r.passed:
         raise AssertionError(r.summary())
     return r
+
+
+# ---------------------------------------------------------------------------------------
+# End-to-end greedy check of an engine against a reference engine (teacher forcing)
+# ---------------------------------------------------------------------------------------
+TINY_GPT_OSS_D64 = {
+    "architectures": ["GptOssForCausalLM"], "model_type": "gpt_oss", "vocab_size": 4096, "hidden_size": 256,
+    "num_hidden_layers": 2, "num_attention_heads": 8, "num_key_value_heads": 2, "head_dim": 64,
+    "intermediate_size": 256, "num_local_experts": 8, "num_experts_per_tok": 2, "sliding_window": 128,
+    "layer_types": ["sliding_attention", "full_attention"], "rope_theta": 150000.0,
+    "rope_scaling": {"rope_type": "yarn", "factor": 32.0, "beta_fast": 32.0, "beta_slow": 1.0,
+                     "original_max_position_embeddings": 4096},
+    "rms_norm_eps": 1e-5, "swiglu_limit": 7.0, "attention_bias": True, "max_position_embeddings": 4096,
+}
+
+
+def write_tiny_gpt_oss_checkpoint(path: str, config: dict | None = None, seed: int = 0) -> dict:
+    """A random GPT-OSS-architecture HF checkpoint (safetensors + config.json) for end-to-end
+    checks: HF ``GptOssForCausalLM`` initialisation (seed), every bias and sink given a
+    non-trivial value.  Returns the config written."""
+    from transformers import GptOssConfig, GptOssForCausalLM
+
+    from ..utils.checkpoints import save_state_dict
+
+    cfg_d = dict(config or TINY_GPT_OSS_D64)
+    torch.manual_seed(seed)
+    hf_cfg = GptOssConfig(**{k: v for k, v in cfg_d.items() if k != "architectures"})
+    m = GptOssForCausalLM(hf_cfg).eval().float()
+    g = torch.Generator().manual_seed(seed + 1)
+    with torch.no_grad():
+        for n, p in m.named_parameters():
+            if n.endswith("bias") or "sinks" in n:
+                p.copy_(torch.randn(p.shape, generator=g) * 0.02)
+    out_cfg = m.config.to_dict()
+    out_cfg["architectures"] = ["GptOssForCausalLM"]
+    save_state_dict({k: v.detach().clone() for k, v in m.state_dict().items()}, path, out_cfg)
+    return out_cfg
+
+
+@dataclass
+class GreedyGapResult:
+    n_tokens: int
+    n_exact: int
+    max_gap: float
+    worst: tuple  # (prompt index, position, gap, row std)
+    gaps: list  # (gap, row std) per generated position
+
+    @property
+    def exact_fraction(self) -> float:
+        return self.n_exact / max(1, self.n_tokens)
+
+    def outliers(self, abs_tol: float = 0.05, rel_tol: float = 0.2) -> int:
+        """Positions whose gap exceeds max(abs_tol, rel_tol * row std).  A rare isolated
+        outlier is a discrete flip (e.g. a router top-k near tie ordered differently in
+        bf16 and fp32), not a numerical error of the kernels."""
+        return sum(1 for g, sd in self.gaps if g > max(abs_tol, rel_tol * sd))
+
+
+def greedy_logit_gaps(reference_engine, prompts: list[list[int]], generated: list[list[int]]) -> GreedyGapResult:
+    """Teacher-forced check of greedy generations: the reference engine scores prompt +
+    generation, and at every generated position the gap between its largest logit and the
+    logit of the token the engine under test chose is measured (0 when they agree).  Near
+    ties can legitimately flip under a different precision; a wrong kernel gives large gaps."""
+    n = exact = 0
+    gaps = []
+    max_gap, worst = 0.0, (-1, -1, 0.0, 0.0)
+    for i, (p, gen) in enumerate(zip(prompts, generated)):
+        if not gen:
+            continue
+        logits = reference_engine.score(list(p) + list(gen[:-1])).float()
+        for j, tok in enumerate(gen):
+            row = logits[len(p) - 1 + j]
+            gap = float(row.max() - row[tok])
+            n += 1
+            gaps.append((gap, float(row.std())))
+            exact += int(int(row.argmax()) == int(tok) or gap == 0.0)
+            if gap > max_gap:
+                max_gap, worst = gap, (i, j, gap, float(row.std()))
+    return GreedyGapResult(n, exact, max_gap, worst, gaps)

@@ -3,8 +3,8 @@
     torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m vllm_neuron_b200.benchmarks.collectives
     torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m vllm_neuron_b200.benchmarks.collectives --op ep
 
-``--op ep`` times the EP all-to-all (see ``_ep``); the default is the layer-boundary
-all-reduce:
+``--op ep`` times the EP all-to-all (see ``_ep``); ``--op gemm_ar`` the row-parallel GEMM
+fused with the all-reduce (see ``_gemm_ar``); the default is the layer-boundary all-reduce:
 
 For each token count T (hidden 2880, bf16) it times, with CUDA events after warm-up and as
 the maximum over ranks:
@@ -102,9 +102,88 @@ def _ep(a, rank, world, dev, ps) -> None:
     fused.close()
 
 
+def _gemm_ar(a, rank, world, dev, ps) -> None:
+    """Row-parallel projection + layer boundary (GPT-OSS o_proj: [T, 4096 / world] x
+    [2880, 4096 / world]^T, then all-reduce + bias + residual + RMSNorm), CUDA graph of
+    ``--iters`` calls, max over ranks:
+    * ``nvls``: the tcgen05 GEMM adds its fp32 output tiles into every rank's accumulator
+      with multimem reductions (NVSwitch), one finish kernel normalises;
+    * ``gemm+fused_ar``: the same GEMM storing bf16, then the one-shot NVLink all-reduce
+      kernel fused with the norm;
+    * ``cublas+nccl``: library GEMM, NCCL all-reduce, add + RMSNorm kernel (baseline).
+    Roofline: the slower of the weight stream at the measured HBM bandwidth, the GEMM at the
+    measured bf16 peak and the bytes each rank must push (fp32 rows once through the switch
+    for nvls, bf16 rows to every peer otherwise) at 770 GB/s."""
+    import torch.nn.functional as F
+
+    from vllm_neuron_b200 import ops
+
+    tp = ps.tp
+    H, Kr = a.hidden, 4096 // world
+    hbm, peak = 6537.0, 1667.1
+    try:
+        with open(os.path.join(os.path.dirname(__file__), "..", "..", "MEASURED_PEAKS.json")) as f:
+            mp_ = json.load(f)
+            hbm, peak = float(mp_["hbm_gbs"]), float(mp_["bf16_tflops"])
+    except (OSError, ValueError, KeyError):
+        pass
+    nw = torch.ones(H, device=dev)
+    torch.manual_seed(7 + rank)
+    W = (torch.randn(H, Kr, device=dev) * 0.02).bfloat16()
+    for T in [int(t) for t in a.tokens.split(",")]:
+        x = torch.randn(T, Kr, device=dev).bfloat16()
+        res = torch.randn(T, H, device=dev).bfloat16()
+        bias = torch.zeros(H, device=dev).bfloat16()
+        paths = (["nvls"] if tp.reducer is not None else []) + ["gemm+fused_ar", "cublas+nccl"]
+        for path in paths:
+            def step():
+                if path == "nvls":
+                    return tp.reducer.linear_add_rmsnorm(x, W, res, nw, 1e-5, bias)
+                if path == "gemm+fused_ar":
+                    return tp.communicator.all_reduce_add_rmsnorm(ops.linear(x, W), res, nw, 1e-5, bias)
+                y = F.linear(x, W)
+                dist.all_reduce(y, group=tp.device_group)
+                return ops.fused_add_rms_norm(y + bias, res, nw, 1e-5)
+
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                for _ in range(3):
+                    step()
+            torch.cuda.current_stream().wait_stream(s)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(a.iters):
+                    step()
+            for _ in range(3):
+                g.replay()
+            dist.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            t = torch.tensor([e0.elapsed_time(e1) * 1000.0 / a.iters], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            us = t.item()
+            link_bytes = T * H * 4 if path == "nvls" else (world - 1) * T * H * 2
+            t_link = link_bytes / (LINK_GBS * 1e3)
+            t_hbm = H * Kr * 2 / (hbm * 1e3)
+            t_mma = 2.0 * T * H * Kr / (peak * 1e6)
+            target = max(t_link, t_hbm, t_mma)
+            if rank == 0:
+                print(json.dumps({"op": "gemm_allreduce_rmsnorm", "path": path, "world": world, "T": T, "H": H,
+                                  "K_per_rank": Kr, "us": round(us, 2), "target_us": round(target, 2),
+                                  "bound": ["nvlink", "hbm", "mma"][[t_link, t_hbm, t_mma].index(target)],
+                                  "frac_of_roofline": round(target / us, 3)}), flush=True)
+            del g
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", choices=["allreduce", "ep"], default="allreduce")
+    ap.add_argument("--op", choices=["allreduce", "ep", "gemm_ar"], default="allreduce")
     ap.add_argument("--hidden", type=int, default=2880)
     ap.add_argument("--tokens", default="1,16,64,256")
     ap.add_argument("--experts", type=int, default=128)
@@ -112,7 +191,7 @@ def main() -> None:
     a = ap.parse_args()
     from vllm_neuron_b200 import ops
     from vllm_neuron_b200.parallel import state as pstate
-    from vllm_neuron_b200.parallel.communicator import attach_communicators
+    from vllm_neuron_b200.parallel.communicator import attach_communicators, attach_reducers
 
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -127,6 +206,13 @@ def main() -> None:
         dist.destroy_process_group()
         return
     attach_communicators(ps, dev)
+    if a.op == "gemm_ar":
+        attach_reducers(ps, dev)
+        _gemm_ar(a, rank, world, dev, ps)
+        torch.cuda.synchronize()
+        pstate.destroy_parallel_state()
+        dist.destroy_process_group()
+        return
     tp = ps.tp
     H = a.hidden
     w = torch.ones(H, device=dev)

@@ -254,6 +254,9 @@ void register_comm_impls(torch::Library& m);
 void register_comm_cpu_impls(torch::Library& m);
 void register_deltanet_ops(torch::Library& m);
 void register_deltanet_impls(torch::Library& m);
+void register_gemm_ops(torch::Library& m);
+void register_gemm_impls(torch::Library& m);
+void register_gemm_cpu_impls(torch::Library& m);
 
 TORCH_LIBRARY(b200, m) {
   m.def("rms_norm(Tensor(a!) out, Tensor x, Tensor w, float eps) -> ()");
@@ -291,10 +294,14 @@ TORCH_LIBRARY(b200, m) {
   register_moe_ops(m);
   register_comm_ops(m);
   register_deltanet_ops(m);
+  register_gemm_ops(m);
 }
 
 // ops without tensor arguments (pointer plumbing) dispatch through CompositeExplicitAutograd
-TORCH_LIBRARY_IMPL(b200, CompositeExplicitAutograd, m) { register_comm_cpu_impls(m); }
+TORCH_LIBRARY_IMPL(b200, CompositeExplicitAutograd, m) {
+  register_comm_cpu_impls(m);
+  register_gemm_cpu_impls(m);
+}
 
 TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("rms_norm", &rms_norm);
@@ -313,6 +320,7 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   register_moe_impls(m);
   register_comm_impls(m);
   register_deltanet_impls(m);
+  register_gemm_impls(m);
 }
 
 // Python module entry so `import vllm_neuron_b200._C` loads the library.

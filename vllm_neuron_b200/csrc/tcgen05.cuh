@@ -59,6 +59,65 @@ B200_D bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, uint64_t limi
   return false;
 }
 
+// ---------------------------------------------------------------- thread-block clusters
+B200_D uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+B200_D uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+B200_D uint32_t ncluster_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// Shared-memory address of the same variable in CTA `rank` of this cluster (DSMEM).
+B200_D uint32_t mapa(uint32_t local_smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem_addr), "r"(rank));
+  return r;
+}
+B200_D void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+// Arrive on an mbarrier of another CTA of the cluster; orders this thread's earlier
+// (cumulatively observed) memory operations before the arrival at cluster scope.
+B200_D void mbar_arrive_remote(uint32_t remote_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
+}
+B200_D bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for arrivals made by other CTAs of the cluster (acquire at cluster scope).
+B200_D bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* status, uint64_t limit_ns = kDefaultWaitNs) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((i & 1023) == 0) {
+      if (status && *reinterpret_cast<volatile int*>(status) != 0) return false;
+      if (globaltimer_ns() - t0 > limit_ns) break;
+    }
+  }
+  if (status) atomicCAS(status, 0, kWaitTimeout);
+  return false;
+}
+// Every thread of every CTA of the cluster (hardware barrier; memory ordered at cluster scope).
+B200_D void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release;\n barrier.cluster.wait.acquire;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- TMA (no multicast)
 B200_D void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(

@@ -80,9 +80,10 @@ class Worker:
             vision_tp=self.cfg.vision_neuron_config.tp_size, vision_dp=self.cfg.vision_neuron_config.dp_size,
             timeout_s=float(envs.VLLM_B200_BARRIER_TIMEOUT), sampling_dp=self._sampling_dp())
         if self.device.type == "cuda" and self.world_size > 1 and envs.VLLM_B200_FUSED_COLLECTIVES:
-            from ..parallel.communicator import attach_communicators
+            from ..parallel.communicator import attach_communicators, attach_reducers
 
             attach_communicators(self.ps, self.device)
+            attach_reducers(self.ps, self.device)
         self._t_start = t0
 
     def load_model(self) -> None:

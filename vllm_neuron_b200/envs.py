@@ -60,6 +60,12 @@ _REGISTRY: dict[str, tuple[Callable[[str], Any], str | None, str | None]] = {
     "VLLM_B200_GOLDEN_CACHE_DIR": (str, "", "VLLM_NEURON_GOLDEN_CACHE_DIR"),
     # Use the fused in-kernel NVLink collectives (else NCCL).
     "VLLM_B200_FUSED_COLLECTIVES": (_bool, "1", None),
+    # Row-parallel GEMMs reduce their output tiles through NVSwitch (multimem) when the group
+    # has a multicast object (else the GEMM and the fused all-reduce kernel run separately).
+    "VLLM_B200_GEMM_ALLREDUCE": (_bool, "1", None),
+    # Dense layers through the library GEMM (torch / cuBLAS) instead of the tcgen05 kernel:
+    # the NCCL + cuBLAS baseline-of-record configuration, never the default.
+    "VLLM_B200_LIBRARY_GEMM": (_bool, "0", None),
     # Spin-wait bound (iterations) for device-side flag waits in fused collectives.
     "VLLM_B200_DEVICE_WAIT_LIMIT": (int, "20000000", None),
     # Prometheus multiprocess directory (set automatically when unset).

@@ -183,6 +183,13 @@ class GptOssAttention(nn.Module):
 
     def forward(self, positions: torch.Tensor, x: torch.Tensor, meta, kv: tuple, cos_sin: torch.Tensor
                 ) -> torch.Tensor:
+        """This rank's partial output projection (reduced by the caller)."""
+        o = self.attend(positions, x, meta, kv, cos_sin)
+        return ops.linear(o, self.o_proj.weight, None)
+
+    def attend(self, positions: torch.Tensor, x: torch.Tensor, meta, kv: tuple, cos_sin: torch.Tensor
+               ) -> torch.Tensor:
+        """QKV projection, RoPE + KV write, attention: [T, nq * d], the o_proj input."""
         qkv = ops.linear(x, self.qkv_weight, self.qkv_bias)
         k_cache, v_cache = kv
         # under attention DP the slot mapping covers every replica's rows (-1 outside this
@@ -195,9 +202,7 @@ class GptOssAttention(nn.Module):
                           self.v_scale)
         if self.adp is not None:
             o = self.adp.all_to_all(o, scatter_dim=1, gather_dim=0)  # every row, this rank's q shard
-        # partial output projection of this rank's heads; the all-reduce, bias, residual add
-        # and the next RMSNorm happen in one fused step in the decoder layer
-        return ops.linear(o.reshape(o.shape[0], self.nq * self.d), self.o_proj.weight, None)
+        return o.reshape(o.shape[0], self.nq * self.d)
 
 
 class GptOssExperts(nn.Module):
@@ -314,9 +319,13 @@ class GptOssDecoderLayer(nn.Module):
             x = self.input_layernorm(h)
         else:
             x, residual = self.moe_group.all_reduce_add_rmsnorm(h, residual, self.input_layernorm.weight, self.eps)
-        a = self.self_attn(positions, x, meta, kv, cos_sin)
-        x, residual = self.tp.all_reduce_add_rmsnorm(a, residual, self.post_attention_layernorm.weight, self.eps,
-                                                     self.self_attn.o_proj.bias)
+        # the output projection of this rank's heads, the all-reduce, bias, residual add and the
+        # next RMSNorm: a GEMM that reduces through NVSwitch + one finish kernel, or the GEMM +
+        # one fused all-reduce kernel
+        a = self.self_attn.attend(positions, x, meta, kv, cos_sin)
+        x, residual = self.tp.linear_all_reduce_add_rmsnorm(a, self.self_attn.o_proj.weight, residual,
+                                                            self.post_attention_layernorm.weight, self.eps,
+                                                            self.self_attn.o_proj.bias)
         return self.mlp(x), residual
 
 

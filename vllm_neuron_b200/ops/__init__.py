@@ -55,12 +55,52 @@ def check_device_status(device: torch.device) -> int:
 # ---------------------------------------------------------------------------
 
 
-def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None) -> torch.Tensor:
-    """Plain GEMM (cuBLAS on GPU).  Fused GEMM+collective paths live in
-    :mod:`vllm_neuron_b200.parallel.communicator`."""
+_GEMM_WS: dict = {}
+_GEMM_MAX_SPLITS = 16
+
+
+def _gemm_workspace(device: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-device split-K scratch of the dense GEMM: fp32 sums [T, N] of a call whose output
+    tiles are fewer than the SMs (so at most one tile per SM) and one arrival counter per
+    tile and epilogue warp; both are zero between calls (each call clears what it used).
+    Allocated once, before any capture."""
+    key = str(device)
+    ws = _GEMM_WS.get(key)
+    if ws is None:
+        sms = torch.cuda.get_device_properties(device).multi_processor_count
+        ws = (torch.zeros(sms * 128 * 256, dtype=torch.float32, device=device),
+              torch.zeros(4 * max(256, sms), dtype=torch.int32, device=device))
+        _GEMM_WS[key] = ws
+    return ws
+
+
+def _gemm_ok(x: torch.Tensor, w: torch.Tensor) -> bool:
+    from .. import envs
+
+    return (use_kernel(x) and w.dtype == torch.bfloat16 and w.dim() == 2 and w.is_contiguous()
+            and w.shape[1] % 8 == 0 and w.shape[0] % 8 == 0 and not envs.VLLM_B200_LIBRARY_GEMM)
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None,
+           out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """y = x . w^T + b.  bf16 on a GPU: the tcgen05 GEMM of ``csrc/gemm.cu`` (split K when
+    the output tiles cannot fill the SMs); anything else: torch.  ``out_dtype=float32``
+    keeps the fp32 accumulator (router logits).  Row-parallel projections whose sum is
+    reduced across the TP group go through ``GroupCoordinator.linear_all_reduce_add_rmsnorm``."""
     if x.dtype != w.dtype:
         x = x.to(w.dtype)
-    return F.linear(x, w, b)
+    if _gemm_ok(x, w):
+        K, N = w.shape[1], w.shape[0]
+        x2 = x.reshape(-1, K)
+        if x2.stride(1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+            x2 = x2.contiguous()
+        y = torch.empty(x2.shape[0], N, dtype=out_dtype or w.dtype, device=x.device)
+        ws, cnt = _gemm_workspace(x.device)
+        bb = b.to(w.dtype).contiguous() if b is not None else None
+        _k().gemm_bf16(y, x2, w, bb, ws, cnt, _GEMM_MAX_SPLITS, device_status(x.device))
+        return y.reshape(*x.shape[:-1], N)
+    y = F.linear(x, w, b)
+    return y.to(out_dtype) if out_dtype is not None else y
 
 
 def linear_fp8(x: torch.Tensor, w_fp8: torch.Tensor, w_scale: torch.Tensor, in_scale: torch.Tensor | None,
@@ -257,16 +297,16 @@ def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqle
 def router_topk(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, top_k: int,
                 order: str = "topk_softmax") -> tuple[torch.Tensor, torch.Tensor]:
     """(topk_ids [T,k] int32, topk_weights [T,k] fp32)."""
-    if use_kernel(x) and order == "topk_softmax" and w.shape[0] <= 1024:
-        logits = F.linear(x.to(w.dtype), w, b)  # bf16 logits read directly by the top-k kernel
-        if logits.dtype not in (torch.bfloat16, torch.float32):
-            logits = logits.float()
+    if use_kernel(x) and order == "topk_softmax" and w.shape[0] <= 1024 and top_k <= 16:
+        # fp32 logits straight from the GEMM accumulator (the reference's router linear runs
+        # in fp32, model_mxfp4.py:949-955): bf16-rounded logits would reorder near ties
+        logits = linear(x, w, b, out_dtype=torch.float32)
         ids = torch.empty(x.shape[0], top_k, dtype=torch.int32, device=x.device)
         wts = torch.empty(x.shape[0], top_k, dtype=torch.float32, device=x.device)
         _k().topk_softmax(ids, wts, logits)
         return ids, wts
     if use_kernel(x):
-        logits = F.linear(x.to(w.dtype), w, b).float()
+        logits = linear(x, w, b, out_dtype=torch.float32)
         if order == "softmax_topk":
             wts, ids = torch.topk(torch.softmax(logits, -1), top_k, -1)
             wts = wts / wts.sum(-1, keepdim=True)

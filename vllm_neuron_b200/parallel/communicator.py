@@ -90,6 +90,109 @@ class FusedCommunicator:
         self._opened = []
 
 
+class NvlsReducer:
+    """Row-parallel GEMM fused with the all-reduce, through NVSwitch multicast (NVLS).
+
+    Owns one symmetric region per group (``torch.distributed._symmetric_memory`` allocates
+    it and binds every rank's copy to a multicast object; the kernels are this library's).
+    ``linear_add_rmsnorm`` runs two kernels (``csrc/gemm.cu``): the tcgen05 GEMM of this
+    rank's K slice adds each fp32 output tile into the accumulator of every rank at once
+    with ``multimem.red.add`` (the switch performs the additions) and counts the tile with a
+    multicast release; the finish kernel waits for all ranks' tiles, then applies bias,
+    residual and RMSNorm and clears the accumulator.  Decode-size token counts only
+    (``max_tokens``).  This replaces GEMM -> all-reduce + RMSNorm at the reference's
+    attention ``all_reduce`` (``model/gpt_oss/model_mxfp4.py:828``, ``nn/rpl.py:146-149``)."""
+
+    def __init__(self, group, device: torch.device, max_tokens: int = 256, max_hidden: int = 8192,
+                 max_splits: int = 8, num_blocks: int = 128):
+        from torch.distributed import _symmetric_memory as symm
+
+        from ..ops import _ext, device_status
+
+        _ext.load()
+        self.world = group.world_size
+        self.T_cap, self.H_cap = max_tokens, max_hidden
+        self.max_splits, self.num_blocks = max_splits, num_blocks
+        nbytes = int(torch.ops.b200.red_region_bytes(max_tokens, max_hidden))
+        gname = group.device_group.group_name
+        try:
+            symm.enable_symm_mem_for_group(gname)
+        except Exception:  # noqa: BLE001  (newer torch: nothing to enable)
+            pass
+        with torch.cuda.device(device):
+            self.buf = symm.empty(nbytes, dtype=torch.uint8, device=device)
+            self.buf.zero_()
+            self.hdl = symm.rendezvous(self.buf, gname)
+        # the multicast address is used only when it provably maps this tensor: a handle at
+        # offset 0 whose local buffer pointer is the tensor's own
+        off = int(getattr(self.hdl, "offset", 0))
+        ptrs = list(self.hdl.buffer_ptrs)
+        mc = int(self.hdl.multicast_ptr or 0)
+        if mc == 0 or off != 0 or int(ptrs[group.rank_in_group]) != self.buf.data_ptr():
+            raise RuntimeError(f"no usable NVLS multicast mapping (mc={mc:#x}, offset={off})")
+        self.uc, self.mc = self.buf.data_ptr(), mc
+        self.status = device_status(device)
+        torch.cuda.synchronize(device)
+        group.barrier()
+        logger.info("NVLS reducer for group %s: %d ranks, %.1f MB region", group.name, self.world, nbytes / 1e6)
+
+    def can(self, x: torch.Tensor, weight: torch.Tensor) -> bool:
+        T = x.numel() // x.shape[-1] if x.dim() else 0
+        return (x.is_cuda and x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and 0 < T <= self.T_cap
+                and weight.shape[0] <= self.H_cap and weight.shape[0] % 8 == 0 and weight.shape[1] % 8 == 0
+                and weight.is_contiguous())
+
+    def linear_add_rmsnorm(self, x: torch.Tensor, weight: torch.Tensor, residual: torch.Tensor, w: torch.Tensor,
+                           eps: float, bias: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        x2 = x.reshape(-1, x.shape[-1])
+        if x2.stride(1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+            x2 = x2.contiguous()
+        ops = torch.ops.b200
+        items = ops.gemm_bf16_allreduce(x2, weight, self.uc, self.mc, self.T_cap, self.H_cap, self.max_splits,
+                                        self.status)
+        out = torch.empty(x2.shape[0], weight.shape[0], dtype=x.dtype, device=x.device)
+        bb = bias.to(torch.bfloat16).contiguous() if bias is not None else None
+        ops.allreduce_finish(self.uc, self.T_cap, self.H_cap, items * self.world, out, residual, bb, w, eps,
+                             self.num_blocks, self.status)
+        return out, residual
+
+    def close(self) -> None:
+        self.hdl = None
+        self.buf = None
+
+
+def attach_reducers(ps, device) -> None:
+    """NVLS GEMM + all-reduce for the TP group (collective: every rank calls it).  Groups
+    without a usable multicast mapping keep the GEMM + fused all-reduce kernel pair."""
+    from .. import envs
+
+    if not envs.VLLM_B200_GEMM_ALLREDUCE:
+        return
+    seen = {}
+    for name in ("tp", "attn_tp"):
+        g = getattr(ps, name)
+        if g.world_size <= 1 or g.world_size > 8 or g.device_group is None:
+            continue
+        key = tuple(g.ranks)
+        if key not in seen:
+            red, err = None, None
+            try:
+                red = NvlsReducer(g, device)
+            except Exception as e:  # noqa: BLE001
+                err = e
+            # every rank of the group must take the same path: a rank waiting for tiles that a
+            # rank on the other path never adds would only end by its wait limit
+            ok = g.cpu_all_reduce_max([0 if red is not None else 1])[0] == 0
+            if not ok:
+                if red is not None:
+                    red.close()
+                red = None
+                logger.warning("group %s: NVLS GEMM + all-reduce unavailable (%s); using GEMM + NVLink all-reduce",
+                               g.name, err or "another rank has no multicast mapping")
+            seen[key] = red
+        g.reducer = seen[key]
+
+
 def attach_communicators(ps, device) -> None:
     """Create fused communicators for the groups whose all-reduces sit on the decode hot
     path (TP, and the MoE group when it differs).  Collective: every rank calls it."""

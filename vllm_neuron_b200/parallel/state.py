@@ -150,6 +150,7 @@ class GroupCoordinator:
     cpu_group: Any = None
     rank: int = 0
     communicator: Any = None  # fused NVLink collectives (parallel.communicator)
+    reducer: Any = None  # GEMM fused with the all-reduce through NVSwitch (parallel.communicator)
     sp_active: bool = False  # sequence parallelism at layer boundaries (set per prefill step)
 
     @property
@@ -189,6 +190,20 @@ class GroupCoordinator:
         if bias is not None:
             x = x + bias
         return ops.fused_add_rms_norm(x, residual, w, eps)
+
+    def linear_all_reduce_add_rmsnorm(self, x: torch.Tensor, weight: torch.Tensor, residual: torch.Tensor,
+                                      w: torch.Tensor, eps: float, bias: torch.Tensor | None = None
+                                      ) -> tuple[torch.Tensor, torch.Tensor]:
+        """Row-parallel projection and layer boundary: (RMSNorm(sum_ranks(x . weight^T) + bias
+        + residual) * w, the new residual).  With an NVLS reducer the GEMM's output tiles are
+        reduced through NVSwitch by the GEMM itself and one small kernel normalises; otherwise
+        the GEMM runs, then :meth:`all_reduce_add_rmsnorm`."""
+        from .. import ops
+
+        if (self.world_size > 1 and not self.sp_active and self.reducer is not None
+                and self.reducer.can(x, weight)):
+            return self.reducer.linear_add_rmsnorm(x, weight, residual, w, eps, bias)
+        return self.all_reduce_add_rmsnorm(ops.linear(x, weight, None), residual, w, eps, bias)
 
     def _sp_add_rmsnorm(self, x, residual, w, eps, bias):
         """Sequence-parallel layer boundary (prefill): reduce-scatter the partial sums over
@@ -571,5 +586,8 @@ def destroy_parallel_state() -> None:
                     g.communicator.close()
                 except Exception:  # pragma: no cover
                     pass
+            if isinstance(g, GroupCoordinator) and g.reducer is not None and id(g.reducer) not in seen:
+                seen.add(id(g.reducer))
+                g.reducer.close()
     _STATE = None
     _ALL_PGS.clear()
