@@ -58,6 +58,9 @@ GPT_OSS_120B = {
 GPT_OSS_20B = dict(GPT_OSS_120B, num_hidden_layers=24, num_local_experts=32,
                    layer_types=["sliding_attention" if i % 2 == 0 else "full_attention" for i in range(24)])
 METRIC = "output tok/s at fixed concurrency (GPT-OSS-120B, 8×B200); p50 TTFT / TPOT"
+# Device-timed value of ``--baseline-of-record`` on a B200 of this pool, per (model, GPUs),
+# the numbers BASELINE.md records (the reference publishes none); vs_baseline = value / it.
+BASELINE_OF_RECORD: dict = {}
 
 
 class ClockSampler:
@@ -214,10 +217,19 @@ def main() -> None:
     ap.add_argument("--output-len", type=int, default=512)
     ap.add_argument("--profile-dir", default=None,
                     help="also write a per-kernel table of one profiled serving period (rank 0)")
+    ap.add_argument("--baseline-of-record", action="store_true",
+                    help="the baseline of record: library GEMMs (cuBLAS) and NCCL collectives instead of the "
+                         "tcgen05 GEMMs and fused NVLink / NVSwitch kernels (attention and MoE stay on this "
+                         "framework's kernels: the reference's PyTorch MoE needs the experts dequantized to "
+                         "bf16, ~234 GB for GPT-OSS-120B, which no single B200 holds)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
         return
+    if args.baseline_of_record:
+        os.environ["VLLM_B200_LIBRARY_GEMM"] = "1"
+        os.environ["VLLM_B200_FUSED_COLLECTIVES"] = "0"
+        os.environ["VLLM_B200_GEMM_ALLREDUCE"] = "0"
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
 
@@ -330,11 +342,12 @@ def main() -> None:
             f.write(f"# one serving period: {ours} launches of this library's kernels, {total} kernels in total\n")
             f.write(table)
     value = tokens / (dev_ms / 1000.0)
+    base = BASELINE_OF_RECORD.get((args.model, N)) if not args.baseline_of_record else None
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": N, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None,
+            "scaling": "strong", "vs_baseline": round(value / base, 3) if base else None,
             "dtype": "bf16 (experts MXFP4 weights, MXFP8 activations)",
             "data": "synthetic random prompt tokens; random-init weights (GPT-OSS-120B architecture)",
             "config": {"model": args.model, "global_batch": C, "seq_len": P, "output_len": O,
@@ -355,6 +368,8 @@ def main() -> None:
             "gpu_launches": launches,
             "clocks": clk,
         }
+        if args.baseline_of_record:
+            line["impl"] = "baseline-of-record (cuBLAS GEMMs + NCCL collectives)"
         print(json.dumps(line))
         sys.stdout.flush()
     # Graphs that captured NCCL calls are freed before the process group is destroyed

@@ -10,13 +10,14 @@ import torch
 
 V = 512
 TOKS = [str(d) for d in range(10)] + list('{}":, ') + [chr(ord("a") + i) for i in range(26)] + ["true", "false", "null"]
+TOKS += ["[", "]"]
 TOKS += [f"<x{i}>" for i in range(V - len(TOKS) - 2)] + ["<unk>", "</s>"]
 EOS = V - 1
 
 
 @pytest.fixture(scope="module")
 def ckpt(tmp_path_factory):
-    from tokenizers import Tokenizer, models
+    from tokenizers import Tokenizer, decoders, models
     from transformers import LlamaConfig, LlamaForCausalLM, PreTrainedTokenizerFast
 
     from vllm_neuron_b200.utils.checkpoints import save_state_dict
@@ -31,6 +32,7 @@ def ckpt(tmp_path_factory):
     d["architectures"] = ["LlamaForCausalLM"]
     save_state_dict({k: v.detach().clone().contiguous() for k, v in m.state_dict().items()}, str(path), d)
     tk = Tokenizer(models.WordLevel({t: i for i, t in enumerate(TOKS)}, unk_token="<unk>"))
+    tk.decoder = decoders.Fuse()  # detokenised text joins the tokens as they are
     PreTrainedTokenizerFast(tokenizer_object=tk, eos_token="</s>", unk_token="<unk>").save_pretrained(str(path))
     return str(path)
 
@@ -133,3 +135,68 @@ def test_stop_strings_cut_generation(ckpt, include):
     p = text.find(stop)
     assert cut.finish_reason == "stop" and len(cut.token_ids) <= 6
     assert cut.text == text[:p + (len(stop) if include else 0)]
+
+
+def test_tool_calls_required_and_named_through_the_server(ckpt):
+    """tool_choice="required" constrains the output to a list of {name, parameters} over the
+    declared tools; a named tool constrains it to that tool's arguments.  Both come back as
+    message.tool_calls with finish_reason "tool_calls"."""
+    from fastapi.testclient import TestClient
+
+    from vllm_neuron_b200.engine.async_engine import AsyncLLM
+    from vllm_neuron_b200.entrypoints.openai_server import build_app
+
+    tools = [{"type": "function", "function": {"name": "ab", "parameters": {
+        "type": "object", "properties": {"x": {"type": "integer"}}, "required": ["x"]}}},
+             {"type": "function", "function": {"name": "cd", "parameters": {
+                 "type": "object", "properties": {"y": {"type": "boolean"}}, "required": ["y"]}}}]
+    eng = AsyncLLM(model=ckpt, dtype="float32", max_model_len=128, max_num_seqs=4, max_num_batched_tokens=64,
+                   block_size=16, device="cpu", additional_config={"neuron_config": {"enable_structured_outputs": True}})
+    try:
+        with TestClient(build_app(eng, "so")) as c:
+            msgs = [{"role": "user", "content": "a b c"}]
+            r = c.post("/v1/chat/completions", json={"model": "so", "messages": msgs, "tools": tools,
+                                                     "tool_choice": "required", "max_tokens": 60,
+                                                     "temperature": 0}).json()
+            ch = r["choices"][0]
+            if ch["finish_reason"] == "tool_calls":
+                calls = ch["message"]["tool_calls"]
+                assert calls and all(t["function"]["name"] in ("ab", "cd") for t in calls)
+                for t in calls:
+                    args = json.loads(t["function"]["arguments"])
+                    assert ("x" in args) if t["function"]["name"] == "ab" else ("y" in args)
+            else:
+                # a random model may keep appending calls until max_tokens (the array is
+                # unbounded, as in vLLM); every item it wrote still follows the tool schemas
+                assert ch["finish_reason"] == "length", ch
+                item = r'\{"name": "(ab|cd)", "parameters": \{("x": -?\d+|"y": (true|false))\}\}'
+                assert re.match(r"\[" + item + r"(, " + item + r")*", ch["message"]["content"]), ch
+            r = c.post("/v1/chat/completions", json={"model": "so", "messages": msgs, "tools": tools,
+                                                     "tool_choice": {"type": "function", "function": {"name": "cd"}},
+                                                     "max_tokens": 40, "temperature": 0}).json()
+            call = r["choices"][0]["message"]["tool_calls"][0]
+            assert call["function"]["name"] == "cd" and isinstance(json.loads(call["function"]["arguments"])["y"], bool)
+            bad = c.post("/v1/chat/completions", json={"model": "so", "messages": msgs, "tools": tools,
+                                                       "tool_choice": {"type": "function", "function": {"name": "zz"}}})
+            assert bad.status_code == 400
+    finally:
+        eng.shutdown()
+
+
+def test_tool_call_parsers():
+    """auto tool choice: calls read back from GPT-OSS harmony text, Hermes blocks and bare JSON."""
+    from vllm_neuron_b200.entrypoints.tool_calls import parse_tool_calls
+
+    tools = [{"type": "function", "function": {"name": "get_weather", "parameters": {}}}]
+    harmony = ('I will check.<|start|>assistant<|channel|>commentary to=functions.get_weather '
+               '<|constrain|>json<|message|>{"location": "Seattle"}<|call|>')
+    content, calls = parse_tool_calls(harmony, tools)
+    assert content == "I will check." and calls[0]["function"]["name"] == "get_weather"
+    assert json.loads(calls[0]["function"]["arguments"]) == {"location": "Seattle"}
+    content, calls = parse_tool_calls('ok <tool_call>{"name": "get_weather", "arguments": {"q": 1}}</tool_call>', tools)
+    assert content == "ok" and json.loads(calls[0]["function"]["arguments"]) == {"q": 1}
+    content, calls = parse_tool_calls('{"name": "get_weather", "parameters": {"q": 2}}', tools)
+    assert content is None and json.loads(calls[0]["function"]["arguments"]) == {"q": 2}
+    content, calls = parse_tool_calls('{"name": "other", "arguments": {}}', tools)  # unknown tool: plain text
+    assert calls == [] and content.startswith("{")
+    assert parse_tool_calls("just text", tools) == ("just text", [])

@@ -41,7 +41,11 @@ class AsyncLLM:
                     kind, payload = self._in.get_nowait()
                     if kind == "add":
                         rid, ids, sp, mm, kvp = payload
-                        self.engine.add_request(rid, ids, sp, mm_inputs=mm, kv_transfer_params=kvp)
+                        try:
+                            self.engine.add_request(rid, ids, sp, mm_inputs=mm, kv_transfer_params=kvp)
+                        except Exception as e:  # noqa: BLE001  (this request only: the engine keeps serving)
+                            logger.error("request %s refused: %s", rid, e)
+                            self._fail(rid, e)
                     elif kind == "abort":
                         self.engine.abort_request(payload)
                     elif kind == "call":
@@ -78,6 +82,13 @@ class AsyncLLM:
                     if o.finished:
                         with self._lock:
                             self._streams.pop(o.request_id, None)
+
+    def _fail(self, rid: str, e: Exception) -> None:
+        with self._lock:
+            ent = self._streams.pop(rid, None)
+        if ent is not None:
+            loop, q = ent
+            loop.call_soon_threadsafe(q.put_nowait, e if isinstance(e, ValueError) else RuntimeError(str(e)))
 
     async def generate(self, prompt_token_ids: list[int], sampling_params: SamplingParams,
                        request_id: str | None = None, mm_inputs: list | None = None,

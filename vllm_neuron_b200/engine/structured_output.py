@@ -31,6 +31,7 @@ class StructuredOutputsParams:
     choice: list[str] | None = None
     grammar: str | None = None  # EBNF
     json_object: bool = False   # any JSON object
+    disable_any_whitespace: bool = False  # JSON without free whitespace between tokens (compact)
     extra: dict = field(default_factory=dict)
 
     @classmethod
@@ -39,14 +40,16 @@ class StructuredOutputsParams:
             return obj
         get = obj.get if isinstance(obj, dict) else (lambda k, d=None: getattr(obj, k, d))
         p = cls(json=get("json"), regex=get("regex"), choice=get("choice"), grammar=get("grammar"),
-                json_object=bool(get("json_object", False)))
+                json_object=bool(get("json_object", False)),
+                disable_any_whitespace=bool(get("disable_any_whitespace", False)))
         if sum(x is not None and x is not False for x in (p.json, p.regex, p.choice, p.grammar, p.json_object)) != 1:
             raise ValueError("structured outputs need exactly one of json, regex, choice, grammar, json_object")
         return p
 
     def key(self) -> tuple:
         j = self.json if isinstance(self.json, str) or self.json is None else json.dumps(self.json, sort_keys=True)
-        return (j, self.regex, tuple(self.choice) if self.choice else None, self.grammar, self.json_object)
+        return (j, self.regex, tuple(self.choice) if self.choice else None, self.grammar, self.json_object,
+                self.disable_any_whitespace)
 
 
 class StructuredOutputManager:
@@ -73,7 +76,8 @@ class StructuredOutputManager:
         if g is None:
             c = self.compiler
             if p.json is not None:
-                g = c.compile_json_schema(p.json if isinstance(p.json, str) else json.dumps(p.json))
+                g = c.compile_json_schema(p.json if isinstance(p.json, str) else json.dumps(p.json),
+                                          any_whitespace=not p.disable_any_whitespace)
             elif p.json_object:
                 g = c.compile_builtin_json_grammar()
             elif p.regex is not None:

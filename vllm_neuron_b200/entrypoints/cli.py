@@ -65,6 +65,10 @@ def main(argv=None) -> None:
     _engine_args(s)
     s.add_argument("--host", default="127.0.0.1")
     s.add_argument("--port", type=int, default=8000)
+    s.add_argument("--tool-call-parser", default="auto", choices=["auto", "openai", "hermes", "json"],
+                   help="how tool calls are read from text when tool_choice is auto")
+    s.add_argument("--enable-auto-tool-choice", action="store_true",
+                   help="accepted for compatibility (auto tool choice is always available)")
     b = sub.add_parser("bench", help="serving benchmark client (random prompts)")
     b.add_argument("--base-url", default="http://127.0.0.1:8000")
     b.add_argument("--num-prompts", type=int, default=64)
@@ -85,7 +89,7 @@ def main(argv=None) -> None:
     elif a.cmd == "serve":
         from .openai_server import serve
 
-        serve(engine_kwargs(a), a.host, a.port, a.served_model_name)
+        serve(engine_kwargs(a), a.host, a.port, a.served_model_name, a.tool_call_parser)
     else:
         from .bench_client import run_bench
 

@@ -21,6 +21,7 @@ from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
 from ..engine.async_engine import AsyncLLM
 from ..engine.sampling_params import SamplingParams
 from ..logging_config import init_logger
+from .tool_calls import ToolChoiceError, message_with_tools, tool_constraint, tools_prompt
 
 logger = init_logger(__name__)
 
@@ -75,7 +76,7 @@ def _logprobs_payload(token_ids, entries, detok, chat: bool) -> dict | None:
             "top_logprobs": [{detok([i]): v for i, v in e.items()} for e in entries]}
 
 
-def build_app(engine: AsyncLLM, served_name: str):
+def build_app(engine: AsyncLLM, served_name: str, tool_parser: str = "auto"):
     app = FastAPI(title="vllm_neuron_b200")
     state = {"prof": None}
 
@@ -86,8 +87,8 @@ def build_app(engine: AsyncLLM, served_name: str):
         return tok.encode(prompt), prompt
 
     def detok(ids):
-        try:
-            return engine.llm.get_tokenizer().decode(ids)
+        try:  # the end-of-sequence token (kept in token_ids) is not part of the text
+            return engine.llm.get_tokenizer().decode(ids, skip_special_tokens=True)
         except Exception:  # noqa: BLE001
             return ""
 
@@ -121,18 +122,40 @@ def build_app(engine: AsyncLLM, served_name: str):
             return JSONResponse({"error": str(e)}, status_code=400)
         return {"status": "stopped", **res}
 
-    async def _complete(ids, sp, stream: bool, chat: bool, rid: str, kvp: dict | None = None):
+    async def _complete(ids, sp, stream: bool, chat: bool, rid: str, kvp: dict | None = None,
+                        tools: tuple | None = None):
+        """``tools``: (tools, tool_choice, parser) of a chat request that declared functions."""
         created = int(time.time())
         obj = "chat.completion" if chat else "text_completion"
 
         def choice(text, token_ids, finish):
             if chat:
-                return {"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": finish,
+                msg, called = {"role": "assistant", "content": text}, False
+                if tools is not None:
+                    msg, called = message_with_tools(text, *tools)
+                return {"index": 0, "message": msg, "finish_reason": "tool_calls" if called else finish,
                         "token_ids": token_ids}
             return {"index": 0, "text": text, "finish_reason": finish, "token_ids": token_ids}
 
         if stream and sp.n > 1:
             return JSONResponse({"error": "n > 1 is not supported with stream=true"}, status_code=400)
+        if stream and tools is not None:
+            # tool calls are parsed from the whole generation: one delta with the message
+            async def gen_tools():
+                final = None
+                async for o in engine.generate(ids, sp, rid, kv_transfer_params=kvp):
+                    final = o
+                c0 = final.outputs[0]
+                ch = choice(c0.text if isinstance(c0.stop_reason, str) else detok(c0.token_ids), c0.token_ids,
+                            c0.finish_reason)
+                delta = {k: v for k, v in ch["message"].items() if v is not None}
+                chunk = {"id": rid, "object": obj + ".chunk", "created": created, "model": served_name,
+                         "choices": [{"index": 0, "delta": delta, "finish_reason": ch["finish_reason"],
+                                      "token_ids": c0.token_ids}]}
+                yield "data: " + json.dumps(chunk) + "\n\n"
+                yield "data: [DONE]\n\n"
+
+            return StreamingResponse(gen_tools(), media_type="text/event-stream")
         if stream:
             async def gen():
                 sent = 0
@@ -188,6 +211,10 @@ def build_app(engine: AsyncLLM, served_name: str):
             resp["kv_transfer_params"] = final.kv_transfer_params
         return resp
 
+    @app.exception_handler(ValueError)
+    async def refused(_req: Request, e: ValueError):  # a request the engine refused (shape, grammar, ...)
+        return JSONResponse({"error": str(e)}, status_code=400)
+
     @app.post("/v1/completions")
     async def completions(req: Request):
         body = await req.json()
@@ -199,23 +226,41 @@ def build_app(engine: AsyncLLM, served_name: str):
     async def chat(req: Request):
         body = await req.json()
         msgs = body["messages"]
+        tools = body.get("tools") or None
+        tool_choice = body.get("tool_choice", "auto" if tools else None)
+        if tool_choice == "none":
+            tools = None
+        try:
+            constraint = tool_constraint(tools, tool_choice)
+        except ToolChoiceError as e:
+            return JSONResponse({"error": str(e)}, status_code=400)
+        if constraint is not None:
+            if _structured_from(body) is not None:
+                return JSONResponse({"error": "tool_choice and response_format cannot be combined"},
+                                    status_code=400)
+            body = dict(body, structured_outputs=constraint)
+        sp = _sampling_from(body)
         tok = engine.llm.get_tokenizer()
         if getattr(tok, "chat_template", None):
-            ids = tok.apply_chat_template(msgs, add_generation_prompt=True, tokenize=True)
+            ids = tok.apply_chat_template(msgs, tools=tools, add_generation_prompt=True, tokenize=True)
         else:
-            ids = tok.encode("\n".join(f"{m['role']}: {m['content']}" for m in msgs) + "\nassistant:")
-        return await _complete(list(ids), _sampling_from(body), bool(body.get("stream", False)), True,
-                               f"chatcmpl-{uuid.uuid4().hex}")
+            head = tools_prompt(tools) + "\n" if tools else ""
+            ids = tok.encode(head + "\n".join(f"{m['role']}: {m.get('content') or ''}" for m in msgs)
+                             + "\nassistant:")
+        spec = (tools, tool_choice, tool_parser) if tools else None
+        return await _complete(list(ids), sp, bool(body.get("stream", False)), True,
+                               f"chatcmpl-{uuid.uuid4().hex}", tools=spec)
 
     return app
 
 
-def serve(engine_kwargs: dict, host: str = "127.0.0.1", port: int = 8000, served_name: str | None = None) -> None:
+def serve(engine_kwargs: dict, host: str = "127.0.0.1", port: int = 8000, served_name: str | None = None,
+          tool_parser: str = "auto") -> None:
     import uvicorn
 
     engine = AsyncLLM(**engine_kwargs)
     name = served_name or str(engine_kwargs.get("model") or "model")
-    app = build_app(engine, name)
+    app = build_app(engine, name, tool_parser)
     try:
         uvicorn.run(app, host=host, port=port, log_level="warning")
     finally:
