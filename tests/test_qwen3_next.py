@@ -60,7 +60,7 @@ def test_qwen3_next_greedy_matches_hf(ckpt, tp, chunk, dp, a2a):
             want.append(g[0, len(p):].tolist())
     llm = LLM(model=path, dtype="float32", max_model_len=256, max_num_seqs=4, max_num_batched_tokens=chunk,
               block_size=16, device="cpu", tensor_parallel_size=tp, data_parallel_size=dp,
-              all2all_backend=a2a or "allgather_reducescatter")
+              all2all_backend=a2a or "allgather_reducescatter", enable_expert_parallel=a2a is not None)
     try:
         outs = llm.generate(prompt_token_ids=prompts,
                             sampling_params=SamplingParams(temperature=0, max_tokens=8, ignore_eos=True))

@@ -282,6 +282,16 @@ class EngineConfig:
             return "cpu"
         return "cuda"
 
+    def expert_parallel_degree(self) -> int:
+        """Expert partitions (``neuron_worker.py:88`` resolve_ep_degree): an explicit
+        ``neuron_config.ep_degree`` > 1 (variable EP: the ranks of a partition split the
+        intermediate dimension), else every rank with ``enable_expert_parallel`` (the
+        default EP = TP x DP), else 1 (MoE tensor parallelism over every rank)."""
+        nc = self.neuron_config
+        if nc.ep_degree > 1:
+            return nc.ep_degree
+        return self.world_size if self.enable_expert_parallel else 1
+
     def validate(self) -> None:
         """Checks mirrored from ``NeuronPlatform.check_and_update_config`` (``platform.py:278-393``)."""
         if self.block_size <= 0 or self.block_size & (self.block_size - 1):
@@ -297,6 +307,10 @@ class EngineConfig:
 
         if self.all2all_backend not in A2A_BACKENDS:
             raise ValueError(f"all2all_backend must be one of {A2A_BACKENDS}, got {self.all2all_backend!r}")
+        if (self.all2all_backend != "allgather_reducescatter" and self.world_size > 1
+                and self.expert_parallel_degree() != self.world_size):
+            raise ValueError("the EP all-to-all needs every rank to own whole experts: enable expert "
+                             "parallelism over all ranks (enable_expert_parallel, or ep_degree = world size)")
         if self.decode_context_parallel_size > 1 and self.tensor_parallel_size % self.decode_context_parallel_size:
             raise ValueError("decode_context_parallel_size must divide tensor_parallel_size")
         if self.kv_cache_dtype not in ("auto", "bf16", "bfloat16", "fp8", "fp8_e4m3"):

@@ -74,7 +74,7 @@ class Worker:
         nc = self.cfg.neuron_config
         self.ps = pstate.initialize_parallel_state(
             tp=self.cfg.tensor_parallel_size, dp=self.cfg.data_parallel_size,
-            ep_degree=nc.ep_degree, attention_dp_size=nc.attention_dp_size,
+            ep_degree=self.cfg.expert_parallel_degree(), attention_dp_size=nc.attention_dp_size,
             embedding_dp_size=nc.embedding_dp_size, lm_head_dp_size=nc.lm_head_dp_size,
             mlp_dp_size=nc.mlp_dp_size, dcp=self.cfg.decode_context_parallel_size,
             vision_tp=self.cfg.vision_neuron_config.tp_size, vision_dp=self.cfg.vision_neuron_config.dp_size,

@@ -100,6 +100,17 @@ def _param(shape, dtype, device) -> nn.Parameter:
     return nn.Parameter(torch.empty(shape, dtype=dtype, device=device), requires_grad=False)
 
 
+def _pad_narrow(t: torch.Tensor, dim: int, full: int, padded: int, start: int, length: int) -> torch.Tensor:
+    """``t`` (size ``full`` along ``dim``) zero-padded to ``padded``, then [start, start+length)."""
+    if t.shape[dim] != full:
+        raise ValueError(f"expected {full} entries along dim {dim}, got {t.shape[dim]}")
+    if padded > full:
+        shape = list(t.shape)
+        shape[dim] = padded - full
+        t = torch.cat([t, torch.zeros(shape, dtype=t.dtype, device=t.device)], dim)
+    return t.narrow(dim, start, length)
+
+
 def _attention_dp(ps: ParallelState) -> GroupCoordinator | None:
     """The attention-DP group (DP replicas at one TP position) when attention DP is on."""
     g = getattr(ps, "attn_dp", None)
@@ -207,9 +218,18 @@ class GptOssAttention(nn.Module):
 
 class GptOssExperts(nn.Module):
     """This rank's experts.  MXFP4: w13 [E_l, 2I, H/2] u8 + s13 [E_l, 2I, H/32] u8,
-    w2 [E_l, H, I/2] + s2 [E_l, H, I/32]; bf16: w13 [E_l, 2I, H], w2 [E_l, H, I]."""
+    w2 [E_l, H, I/2] + s2 [E_l, H, I/32]; bf16: w13 [E_l, 2I, H], w2 [E_l, H, I].
 
-    def __init__(self, cfg: GptOssConfig, ep_rank: int, ep_size: int, dtype, device):
+    Sharding (``model_mxfp4.py:879-911``, variable EP ``neuron_parallel_state.py:153-167``):
+    ``ep_size`` partitions of ``E / ep_size`` experts; inside a partition the intermediate
+    dimension is split over ``mtp_size`` ranks (MoE tensor parallelism), I padded with zero
+    channels to a multiple of ``mtp_size`` x 32 (one MX scale block; 2880 -> 3072 at 8 ranks,
+    the padding the reference uses) so every slice is whole scale blocks.  A zero channel
+    contributes nothing: its gate and up are 0, SwiGLU(0, 0) = 0.  The down-projection bias
+    is added by slice 0 only, so the partial sums over the ranks add it once."""
+
+    def __init__(self, cfg: GptOssConfig, ep_rank: int, ep_size: int, dtype, device, mtp_rank: int = 0,
+                 mtp_size: int = 1):
         super().__init__()
         E, H, I = cfg.num_local_experts, cfg.hidden_size, cfg.intermediate_size
         if E % ep_size:
@@ -218,22 +238,43 @@ class GptOssExperts(nn.Module):
         self.offset = ep_rank * self.E_local
         self.quant = cfg.quantization
         self.alpha, self.limit = cfg.swiglu_alpha, cfg.swiglu_limit
-        self.H, self.I = H, I
+        self.mtp_rank, self.mtp_size = mtp_rank, mtp_size
+        unit = (32 if self.quant == "mxfp4" else 8) * mtp_size
+        self.I_full = I
+        self.I_pad = round_up(I, unit) if mtp_size > 1 else I
+        I_loc = self.I_pad // mtp_size
+        self.i0 = mtp_rank * I_loc
+        self.H, self.I = H, I_loc
         if self.quant == "mxfp4":
-            if H % 32 or I % 32:
-                raise ValueError("MXFP4 needs hidden and intermediate sizes divisible by 32")
+            if H % 32 or I_loc % 32:
+                raise ValueError("MXFP4 needs hidden and (per-rank) intermediate sizes divisible by 32")
             # kernel layout (ops/mx_layout.py): 128x128 value tiles stored contiguously,
             # scales in 512-byte atoms
-            k1, k2 = round_up(H, 128), round_up(I, 128)
-            self.w13 = _param(tiled_shape(self.E_local, 2 * I, H), torch.uint8, device)
-            self.s13 = _param((self.E_local, -(-2 * I // 128), k1 // 128, 512), torch.uint8, device)
-            self.w2 = _param(tiled_shape(self.E_local, H, I), torch.uint8, device)
+            k1, k2 = round_up(H, 128), round_up(I_loc, 128)
+            self.w13 = _param(tiled_shape(self.E_local, 2 * I_loc, H), torch.uint8, device)
+            self.s13 = _param((self.E_local, -(-2 * I_loc // 128), k1 // 128, 512), torch.uint8, device)
+            self.w2 = _param(tiled_shape(self.E_local, H, I_loc), torch.uint8, device)
             self.s2 = _param((self.E_local, -(-H // 128), k2 // 128, 512), torch.uint8, device)
         else:
-            self.w13 = _param((self.E_local, 2 * I, H), dtype, device)
-            self.w2 = _param((self.E_local, H, I), dtype, device)
-        self.b13 = _param((self.E_local, 2 * I), torch.float32, device)
+            self.w13 = _param((self.E_local, 2 * I_loc, H), dtype, device)
+            self.w2 = _param((self.E_local, H, I_loc), dtype, device)
+        self.b13 = _param((self.E_local, 2 * I_loc), torch.float32, device)
         self.b2 = _param((self.E_local, H), torch.float32, device)
+
+    # -- slices of the (experts x intermediate) checkpoint tensors this rank holds ------------
+    def slice_13(self, t: torch.Tensor, dim: int = 1) -> torch.Tensor:
+        """Gate/up rows (interleaved 2i gate, 2i+1 up) of this rank's intermediate slice,
+        zero rows for the padding."""
+        if self.mtp_size == 1:
+            return t
+        return _pad_narrow(t, dim, 2 * self.I_full, 2 * self.I_pad, 2 * self.i0, 2 * self.I)
+
+    def slice_2(self, t: torch.Tensor, dim: int, per: int = 1) -> torch.Tensor:
+        """Down-projection K entries (``per`` elements each: 1 for values, 32 for MX blocks)
+        of this rank's intermediate slice, zeros for the padding."""
+        if self.mtp_size == 1:
+            return t
+        return _pad_narrow(t, dim, self.I_full // per, self.I_pad // per, self.i0 // per, self.I // per)
 
     def local(self, full: torch.Tensor) -> torch.Tensor:
         return full[self.offset:self.offset + self.E_local]
@@ -267,11 +308,16 @@ class GptOssMLP(nn.Module):
         # replica's tokens are already there, so no gather over DP)
         self.dp = ps.dp if rows_group is None else _single_group()
         self.tp = rows_group or ps.tp
-        ep_rank = ps.dp.rank_in_group * ps.tp.world_size + ps.tp.rank_in_group
-        ep_size = ps.tp.world_size * ps.dp.world_size
+        # expert partitions over the EP group, intermediate slices over the EP-TP group (ranks
+        # of one partition); rank r = partition * (world / ep) + slice
+        world = ps.tp.world_size * ps.dp.world_size
+        ep_size = int(ps.degrees.get("ep", world)) if world > 1 else 1
+        mtp_size = world // ep_size
+        r = ps.dp.rank_in_group * ps.tp.world_size + ps.tp.rank_in_group
+        ep_rank, mtp_rank = r // mtp_size, r % mtp_size
         self.router_weight = _param((cfg.num_local_experts, cfg.hidden_size), dtype, device)
         self.router_bias = _param((cfg.num_local_experts,), dtype, device)
-        self.experts = GptOssExperts(cfg, ep_rank, ep_size, dtype, device)
+        self.experts = GptOssExperts(cfg, ep_rank, ep_size, dtype, device, mtp_rank, mtp_size)
         # EP all-to-all (``parallel/all2all.py``), attached by the worker when
         # ``all2all_backend`` asks for one; None: all-gather / reduce-scatter over DP
         self.a2a = None
@@ -438,9 +484,10 @@ class GptOssForCausalLM(nn.Module):
         elif rest == "mlp.router.bias":
             mlp.router_bias.data.copy_(t.to(mlp.router_bias.dtype))
         elif rest == "mlp.experts.gate_up_proj_bias":
-            ex.b13.data.copy_(ex.local(t).float())
+            ex.b13.data.copy_(ex.slice_13(ex.local(t).float(), 1))
         elif rest == "mlp.experts.down_proj_bias":
-            ex.b2.data.copy_(ex.local(t).float())
+            # added once: by the first intermediate slice of each partition
+            ex.b2.data.copy_(ex.local(t).float() if ex.mtp_rank == 0 else torch.zeros_like(ex.b2))
         elif rest == "mlp.experts.gate_up_proj_blocks":
             self._load_mx(ex, "13", "blocks", t)
         elif rest == "mlp.experts.gate_up_proj_scales":
@@ -450,15 +497,18 @@ class GptOssForCausalLM(nn.Module):
         elif rest == "mlp.experts.down_proj_scales":
             self._load_mx(ex, "2", "scales", t)
         elif rest == "mlp.experts.gate_up_proj":  # bf16 [E, H, 2I]
-            self._load_dense(ex, "13", ex.local(t).transpose(1, 2))
+            self._load_dense(ex, "13", ex.slice_13(ex.local(t).transpose(1, 2), 1))
         elif rest == "mlp.experts.down_proj":  # bf16 [E, I, H]
-            self._load_dense(ex, "2", ex.local(t).transpose(1, 2))
+            self._load_dense(ex, "2", ex.slice_2(ex.local(t).transpose(1, 2), 2))
         else:
             raise KeyError(f"unexpected GPT-OSS weight {rest}")
 
     @staticmethod
     def _load_mx(ex: GptOssExperts, which: str, kind: str, t: torch.Tensor) -> None:
         loc = ex.local(t)
+        # blocks [E, rows, K/32, 16], scales [E, rows, K/32]: gate/up rows or down K blocks
+        # of this rank's intermediate slice
+        loc = ex.slice_13(loc, 1) if which == "13" else ex.slice_2(loc, 2, 32)
         K = ex.H if which == "13" else ex.I
         if ex.quant == "mxfp4":
             if kind == "blocks":
