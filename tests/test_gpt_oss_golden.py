@@ -144,3 +144,33 @@ def test_moe_tp_mxfp4_pads_intermediate():
     want = full(x, ids, wts)
     got = parts[0](x, ids, wts) + parts[1](x, ids, wts)
     assert torch.allclose(got, want, atol=1e-5, rtol=1e-4), (got - want).abs().max()
+
+
+def test_long_prompts_with_sliding_window_kv_group(ckpt):
+    """Prompts several windows long, prefilled in chunks: the sliding-window layers read their
+    own KV group, whose blocks behind the window are returned while the request runs, and the
+    greedy tokens still match HF."""
+    from vllm_neuron_b200 import LLM, SamplingParams
+
+    path, hf = ckpt
+    prompts = workload(n=2, lo=300, hi=420, seed=3)
+    want = _hf_greedy(hf, prompts, 8)
+    llm = LLM(model=path, dtype="float32", max_model_len=512, max_num_seqs=4, max_num_batched_tokens=128,
+              block_size=16, device="cpu", additional_config={"neuron_config": {"quantization": "bf16"}})
+    try:
+        kv = llm.engine.kv
+        assert kv.swa_pool is not None and kv.window == 128
+        seen = []
+        orig = kv._trim_window
+
+        def spy(req):
+            orig(req)
+            seen.append(req.swa_freed)
+
+        kv._trim_window = spy
+        outs = llm.generate(prompt_token_ids=prompts,
+                            sampling_params=SamplingParams(temperature=0, max_tokens=8, ignore_eos=True))
+    finally:
+        llm.shutdown()
+    assert max(seen) >= 10  # blocks behind the window were returned during prefill and decode
+    assert [o.outputs[0].token_ids for o in outs] == want

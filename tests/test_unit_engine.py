@@ -190,3 +190,33 @@ def test_parallel_sampling_n(tmp_path):
     assert [c.index for c in outs[0].outputs] == [0, 1, 2, 3]
     assert len({tuple(c.token_ids) for c in outs[0].outputs}) > 1
     assert outs[1].outputs[0].token_ids == outs[1].outputs[1].token_ids
+
+
+def test_sliding_window_kv_group_frees_blocks_behind_the_window():
+    """Hybrid KV groups: the windowed layers' table returns every block wholly behind the
+    window of the step's first query (keys j > p - W stay visible) to its own pool, so a long
+    sequence holds about W / block_size + 1 windowed blocks while the full-attention table
+    keeps the whole context."""
+    from vllm_neuron_b200.engine.block_manager import KVCacheManager
+    from vllm_neuron_b200.engine.request import Request
+    from vllm_neuron_b200.engine.sampling_params import SamplingParams
+
+    bs, W = 16, 128
+    kv = KVCacheManager(200, bs, False, sliding_window=W, swa_blocks=40)
+    req = Request("r", list(range(300)), SamplingParams(max_tokens=500))
+    assert kv.allocate_slots(req, 300)  # prefill: every block of the prompt in both groups
+    assert len(req.block_ids) == len(req.swa_block_ids) == 19 and kv.swa_pool.num_free == 40 - 1 - 19
+    req.num_computed_tokens = 300
+    for _ in range(200):  # decode: one token per step
+        assert kv.allocate_slots(req, 1)
+        p = req.num_computed_tokens
+        live = [b for b in req.swa_block_ids if b != 0]
+        first_visible = p - W + 1  # the query at p sees keys > p - W
+        # every block holding a visible key is live, every freed one is wholly behind the window
+        assert all(req.swa_block_ids[j] != 0 for j in range(first_visible // bs, -(-(p + 1) // bs)))
+        assert all((j + 1) * bs <= first_visible for j, b in enumerate(req.swa_block_ids) if b == 0)
+        assert len(live) <= W // bs + 2
+        req.num_computed_tokens += 1
+    assert len(req.block_ids) == -(-500 // bs)  # the full group keeps everything
+    kv.free(req)
+    assert kv.swa_pool.num_free == 39 and kv.pool.num_free == 199 and req.swa_block_ids == []

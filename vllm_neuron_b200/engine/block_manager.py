@@ -101,13 +101,27 @@ class BlockPool:
 
 
 class KVCacheManager:
+    """Blocks of the full-attention layers (``pool``) and, for models that mix sliding-window
+    and full-attention layers, a second group for the windowed layers (``swa_pool``, the
+    reference's hybrid KV-cache groups, ``neuron_model_runner.py:3787,3966-3986``).  A
+    request's windowed-layer table keeps one entry per logical block; before a step, the
+    entries wholly behind the window of its first query (keys j > p - W stay visible to
+    query p) are returned to the pool and become the null block, so a windowed layer holds
+    about W / block_size + 1 blocks per sequence instead of the whole context.  Kernels read
+    no block before the window.  Prefix caching applies to the full-attention group only,
+    and is off whenever the windowed group is kept apart."""
+
     def __init__(self, num_blocks: int, block_size: int, enable_caching: bool = False,
-                 sliding_window: int | None = None):
+                 sliding_window: int | None = None, swa_blocks: int = 0):
         self.block_size = block_size
         self.pool = BlockPool(num_blocks, enable_caching)
         self.enable_caching = enable_caching
         self._hashes: dict[str, list[bytes]] = {}
         self._registered: dict[str, int] = {}  # leading blocks already registered per request
+        self.window = sliding_window if swa_blocks else None
+        self.swa_pool = BlockPool(swa_blocks, False) if swa_blocks else None
+        if self.swa_pool is not None and enable_caching:
+            raise ValueError("prefix caching with a separate sliding-window KV group is not supported")
 
     # -------------------------------------------------------------- prefix cache
     def _block_hashes(self, req: Request, upto_tokens: int) -> list[bytes]:
@@ -146,8 +160,27 @@ class KVCacheManager:
     def can_allocate(self, n: int, watermark: int = 0) -> bool:
         return self.pool.num_free - n >= watermark
 
+    def _trim_window(self, req: Request) -> None:
+        """Return the windowed-layer blocks no query from ``num_computed_tokens`` on can see."""
+        first_key = req.num_computed_tokens - self.window + 1
+        n_dead = max(0, first_key) // self.block_size
+        n_dead = min(n_dead, len(req.swa_block_ids))
+        if n_dead > req.swa_freed:
+            dead = req.swa_block_ids[req.swa_freed:n_dead]
+            self.swa_pool.free_blocks(dead)
+            req.swa_block_ids[req.swa_freed:n_dead] = [0] * (n_dead - req.swa_freed)
+            req.swa_freed = n_dead
+
     def allocate_slots(self, req: Request, num_new_tokens: int, computed_blocks: list[int] | None = None) -> bool:
-        if not computed_blocks and req.num_computed_tokens + num_new_tokens <= len(req.block_ids) * self.block_size:
+        total = req.num_computed_tokens + num_new_tokens
+        if self.swa_pool is not None:
+            self._trim_window(req)
+            n_swa = max(0, -(-total // self.block_size) - len(req.swa_block_ids))
+            if n_swa > self.swa_pool.num_free:
+                return False
+        else:
+            n_swa = 0
+        if not computed_blocks and total <= len(req.block_ids) * self.block_size:
             return True  # the common decode case: the current block has room
         computed_blocks = computed_blocks or []
         n = self.blocks_needed(req, num_new_tokens, len(computed_blocks))
@@ -159,6 +192,8 @@ class KVCacheManager:
             self.pool.touch(b)
         req.block_ids.extend(computed_blocks)
         req.block_ids.extend(self.pool.allocate(n))
+        if n_swa:
+            req.swa_block_ids.extend(self.swa_pool.allocate(n_swa))
         return True
 
     def cache_full_blocks(self, req: Request) -> None:
@@ -177,6 +212,10 @@ class KVCacheManager:
     def free(self, req: Request) -> None:
         self.pool.free_blocks(req.block_ids)
         req.block_ids = []
+        if self.swa_pool is not None:
+            self.swa_pool.free_blocks(req.swa_block_ids)  # null entries are skipped
+            req.swa_block_ids = []
+            req.swa_freed = 0
         self._hashes.pop(req.request_id, None)
         self._registered.pop(req.request_id, None)
 

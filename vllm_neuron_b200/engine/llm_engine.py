@@ -79,8 +79,13 @@ class LLMEngine:
             logger.info("prefix caching disabled: recurrent (linear-attention) layers keep per-request state")
         # with decode context parallelism a block-table entry covers block_size tokens on each
         # of the dcp ranks
+        n_swa = getattr(self.worker, "num_swa_blocks", 0)
         self.kv = KVCacheManager(n_blocks, cfg.block_size * cfg.decode_context_parallel_size,
-                                 cfg.enable_prefix_caching and not hybrid)
+                                 cfg.enable_prefix_caching and not hybrid,
+                                 sliding_window=self.worker.swa_group_window() if n_swa else None, swa_blocks=n_swa)
+        if n_swa:
+            logger.info("sliding-window layers use their own KV group: %d blocks (full-attention layers: %d)",
+                        n_swa, n_blocks)
         k = cfg.speculative_config.num_speculative_tokens if cfg.speculative_config else 0
         self.scheduler = Scheduler(self.kv, cfg.max_num_seqs, cfg.max_num_batched_tokens, cfg.max_model_len,
                                    cfg.max_num_prefills_per_step, cfg.enable_chunked_prefill, k)

@@ -145,6 +145,10 @@ class ModelRunner:
         self.d_topp = torch.ones(B, dtype=torch.float32, device=d)
         self.d_unif = torch.zeros(B, dtype=torch.float32, device=d)
         self.d_out = torch.zeros(B * (1 + self._num_spec()), dtype=torch.int64, device=d)
+        # sliding-window KV group (set up by initialize_kv_cache when the windowed layers get
+        # their own, smaller block pool): its block table and slot mapping
+        self.swa_blocks = 0
+        self.h_bt_swa = self.h_slot_swa = self.d_bt_swa = self.d_slot_swa = None
         # asynchronous decode: input rows taken from the previous step's sampled ids, and two
         # host buffers so one step's D2H never overwrites the ids being read for the last one
         self.h_src = mk(B, torch.int64)
@@ -238,14 +242,25 @@ class ModelRunner:
         return sc.num_speculative_tokens if sc is not None else 0
 
     # ------------------------------------------------------------------ KV cache
-    def initialize_kv_cache(self, num_blocks: int) -> None:
+    def initialize_kv_cache(self, num_blocks: int, swa_blocks: int = 0) -> None:
+        """KV caches of every attention layer: ``num_blocks`` blocks, or ``swa_blocks`` for the
+        sliding-window layers when they form their own KV group (``swa_blocks`` > 0)."""
         spec = self.model.get_kv_spec()
         self.kv_caches = []
+        self.swa_blocks = swa_blocks
+        if swa_blocks:
+            T, B = self.max_tokens, max(self.cfg.max_num_seqs, 1)
+            pin = self.device.type == "cuda"
+            self.h_bt_swa = torch.zeros((B, self.max_blocks), dtype=torch.int32, pin_memory=pin)
+            self.h_slot_swa = torch.zeros(T, dtype=torch.int64, pin_memory=pin)
+            self.d_bt_swa = torch.zeros(B, self.max_blocks, dtype=torch.int32, device=self.device)
+            self.d_slot_swa = torch.full((T,), -1, dtype=torch.int64, device=self.device)
         for l in spec.layers:
             if l.kind != "attention":
                 self.kv_caches.append(self.state_caches[len(self.kv_caches)] if self.state_caches else None)
                 continue
-            shape = B200AttentionBackend.get_kv_cache_shape(num_blocks, self.bs, l.num_kv_heads, l.head_dim)[1:]
+            nb = swa_blocks if (swa_blocks and l.sliding_window) else num_blocks
+            shape = B200AttentionBackend.get_kv_cache_shape(nb, self.bs, l.num_kv_heads, l.head_dim)[1:]
             self.kv_caches.append((torch.zeros(shape, dtype=l.dtype, device=self.device),
                                    torch.zeros(shape, dtype=l.dtype, device=self.device)))
         self.num_blocks = num_blocks
@@ -341,6 +356,9 @@ class ModelRunner:
         sl = self.h_seqlen.numpy()
         bt = self.h_bt.numpy()
         lidx = self.h_lidx.numpy()
+        swa = self.swa_blocks > 0
+        if swa:
+            bt_s, slot_s = self.h_bt_swa.numpy(), self.h_slot_swa.numpy()
         t = 0
         qsl[0] = 0
         max_q, max_s = 1, 1
@@ -357,12 +375,17 @@ class ModelRunner:
             # bounds every kernel), so rows are not cleared
             bt[i, :nb] = s.block_ids
             sl[i] = s.seq_len
+            sw_ids = s.swa_block_ids if s.swa_block_ids is not None else s.block_ids
+            if swa:
+                bt_s[i, :len(sw_ids)] = sw_ids
             if plain_decode:  # one token: scalar work only
                 p0 = s.start_pos
                 ids[t] = s.token_ids[0]
                 delta = req.mrope_delta if req is not None else 0
                 pos[t] = p0 + delta
                 slot[t] = s.block_ids[p0 // vbs] * bs + p0 % bs if (p0 // bs) % cp == cpr else -1
+                if swa:
+                    slot_s[t] = sw_ids[p0 // bs] * bs + p0 % bs
                 lidx[n_sel] = t
                 n_sel += 1
                 t += 1
@@ -376,6 +399,8 @@ class ModelRunner:
             if req is not None and req.mrope_positions is not None and so.kind == "prefill":
                 has_mrope = True
             blocks = np.asarray(s.block_ids, dtype=np.int64)
+            if swa:
+                slot_s[t:t + k] = np.asarray(sw_ids, dtype=np.int64)[p // bs] * bs + p % bs
             if cp == 1:
                 slot[t:t + k] = blocks[p // bs] * bs + p % bs
             else:  # only the owning DCP rank writes a token
@@ -398,6 +423,9 @@ class ModelRunner:
             slot[T:T + k] = -1
             sl[n] = k
             bt[n] = 0
+            if swa:
+                slot_s[T:T + k] = -1
+                bt_s[n] = 0
             qsl[n + 1] = T + k
             max_q, max_s = max(max_q, k), max(max_s, k)
             T += k
@@ -407,6 +435,9 @@ class ModelRunner:
             slot[T:T + (B - n)] = -1
             sl[n:B] = 0
             bt[n:B] = 0
+            if swa:
+                slot_s[T:T + (B - n)] = -1
+                bt_s[n:B] = 0
             for j in range(n, B):
                 qsl[j + 1] = qsl[j] + 1
                 lidx[n_sel] = T + (j - n)
@@ -444,13 +475,18 @@ class ModelRunner:
             max_nb = max(max_nb, math.ceil(int(sl[n]) / vbs))
         self.d_bt[:B, :max_nb].copy_(self.h_bt[:B, :max_nb], non_blocking=True)
         nb_ += B * max_nb * 4
+        if swa:
+            self.d_bt_swa[:B, :max_nb].copy_(self.h_bt_swa[:B, :max_nb], non_blocking=True)
+            self.d_slot_swa[:T].copy_(self.h_slot_swa[:T], non_blocking=True)
+            nb_ += B * max_nb * 4 + T * 8
         self.h2d_bytes_last = nb_
         meta = AttentionMetadata(
             num_tokens=T, num_seqs=B, is_decode=(so.kind == "decode" and max_q == 1),
             query_start_loc=self.d_qsl[:B + 1], seq_lens=self.d_seqlen[:B], block_tables=self.d_bt[:B],
             slot_mapping=self.d_slot[:T], logits_indices=self.d_lidx[:n_sel], max_query_len=max_q,
             max_seq_len=max_s, workspace=self.workspace, num_splits=self.num_splits_for(B), extras=extras,
-            cp_group=self.cp_group)
+            cp_group=self.cp_group, block_tables_swa=self.d_bt_swa[:B] if swa else None,
+            slot_mapping_swa=self.d_slot_swa[:T] if swa else None)
         if spec:
             extras["spec"] = True
         if extras_so is not None:

@@ -36,6 +36,10 @@ class Request:
     status: RequestStatus = RequestStatus.WAITING
     output_token_ids: list[int] = field(default_factory=list)
     block_ids: list[int] = field(default_factory=list)
+    # sliding-window KV group: logical block table of the windowed layers; entries that fell
+    # behind the window are returned to their pool and replaced by the null block 0
+    swa_block_ids: list[int] = field(default_factory=list)
+    swa_freed: int = 0  # leading entries of swa_block_ids already returned
     num_computed_tokens: int = 0
     num_cached_tokens: int = 0  # prefix-cache hit length at first schedule
     spec_token_ids: list[int] = field(default_factory=list)

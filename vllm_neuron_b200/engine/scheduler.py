@@ -55,6 +55,7 @@ class ScheduledSeq:
     sample_seq: int = 0
     mm_inputs: list | None = None
     request: Request | None = None
+    swa_block_ids: list[int] | None = None  # the windowed layers' table (separate KV group)
 
     @property
     def seq_len(self) -> int:
@@ -230,7 +231,7 @@ class Scheduler:
                 done = s + n >= req.num_tokens
                 seqs.append(ScheduledSeq(req.request_id, req.all_token_ids[s:s + n], s, req.block_ids, done,
                                          sampling_params=req.sampling_params, sample_seq=req.sample_seq,
-                                         mm_inputs=req.mm_inputs, request=req))
+                                         mm_inputs=req.mm_inputs, request=req, swa_block_ids=self._swa(req)))
             if seqs:
                 return SchedulerOutput("prefill", seqs, finished=finished)
         if kind == "prefill":
@@ -257,7 +258,8 @@ class Scheduler:
             s = req.num_computed_tokens
             toks = [req.token_at(s)] + spec if s < req.num_tokens else spec
             seqs.append(ScheduledSeq(req.request_id, toks, s, req.block_ids, True, spec_token_ids=spec,
-                                     sampling_params=req.sampling_params, sample_seq=req.sample_seq, request=req))
+                                     sampling_params=req.sampling_params, sample_seq=req.sample_seq, request=req,
+                                     swa_block_ids=self._swa(req)))
         if not seqs:
             return SchedulerOutput("idle", [], preempted, finished)
         return SchedulerOutput("decode", seqs, preempted, finished)
@@ -281,9 +283,12 @@ class Scheduler:
             s = req.num_computed_tokens + 1
             seqs.append(ScheduledSeq(req.request_id, [0], s, req.block_ids, True,
                                      sampling_params=req.sampling_params, sample_seq=req.sample_seq + 1,
-                                     request=req))
+                                     request=req, swa_block_ids=self._swa(req)))
         finished, self._finished_ids = self._finished_ids, []
         return SchedulerOutput("decode", seqs, finished=finished)
+
+    def _swa(self, req: Request) -> list[int] | None:
+        return req.swa_block_ids if self.kv.swa_pool is not None else None
 
     def _remote_prefill_tokens(self, req: Request) -> int:
         """Prompt positions whose KV comes from the remote engine: all but the last prompt

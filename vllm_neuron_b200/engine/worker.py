@@ -164,9 +164,38 @@ class Worker:
             raise ValueError(f"decode_context_parallel_size {dcp} needs (tp // kv_heads) % dcp == 0 "
                              f"(tp={tp}, kv_heads={hkv})")
 
+    def swa_group_window(self) -> int | None:
+        """The sliding window when the windowed layers get their own KV block pool (models
+        mixing sliding-window and full-attention layers; not with prefix caching, DCP, KV
+        transfer, speculative decoding, attention DP or recurrent layers, whose block tables
+        are shared by every layer)."""
+        c = self.cfg
+        if not envs.VLLM_B200_SWA_KV_GROUP or c.enable_prefix_caching or c.decode_context_parallel_size > 1:
+            return None
+        if c.kv_transfer_config or c.speculative_config is not None or c.neuron_config.attention_dp_size > 1:
+            return None
+        if self.runner is not None and self.runner.state_caches is not None:
+            return None
+        return self.model.get_kv_spec().sliding_window
+
+    def swa_blocks_for(self) -> int:
+        """Blocks of the sliding-window group: every running sequence holds at most its window
+        plus one partial block on each side, and each prefill step's chunk adds its tokens."""
+        w = self.swa_group_window()
+        if not w:
+            return 0
+        bs, c = self.cfg.block_size, self.cfg
+        per_seq = -(-w // bs) + 2
+        chunk = -(-c.max_num_batched_tokens // bs) + 1
+        return c.max_num_seqs * per_seq + max(1, c.max_num_prefills_per_step) * chunk + 1
+
     def determine_num_blocks(self) -> int:
+        """Blocks of the full-attention group (``self.num_swa_blocks`` is set for the
+        sliding-window group when it is kept apart)."""
         spec = self.model.get_kv_spec()
-        per_block = max(1, spec.bytes_per_block(self.cfg.block_size))
+        self.num_swa_blocks = self.swa_blocks_for()
+        per_block = max(1, spec.bytes_per_block(self.cfg.block_size, False if self.num_swa_blocks else None))
+        swa_bytes = self.num_swa_blocks * spec.bytes_per_block(self.cfg.block_size, True) if self.num_swa_blocks else 0
         # a (virtual) block of a DCP rank holds block_size of its group's bs * dcp tokens
         vbs = self.cfg.block_size * self.cfg.decode_context_parallel_size
         need = self.cfg.max_num_seqs * math.ceil(self.cfg.max_model_len / vbs) + 1
@@ -176,7 +205,7 @@ class Worker:
             free, total = torch.cuda.mem_get_info(self.device)
             used = total - free
             reserve = (3 << 30) + self.runner.max_tokens * (getattr(self.model_cfg, "hidden_size", 4096) * 64)
-            budget = total * self.cfg.gpu_memory_utilization - used - reserve
+            budget = total * self.cfg.gpu_memory_utilization - used - reserve - swa_bytes
             min_b = envs.VLLM_B200_MIN_KV_BUDGET_GIB * (1 << 30)
             if budget < min_b:
                 raise RuntimeError(f"KV budget {budget / 2**30:.2f} GiB below the minimum "
@@ -192,7 +221,7 @@ class Worker:
         return max(n, 2)
 
     def initialize_cache(self, num_blocks: int) -> None:
-        self.runner.initialize_kv_cache(num_blocks)
+        self.runner.initialize_kv_cache(num_blocks, getattr(self, "num_swa_blocks", 0))
 
     def warmup(self) -> None:
         t0 = time.time()

@@ -23,13 +23,27 @@ class LayerSpec:
 class KVSpec:
     layers: list[LayerSpec]
 
-    def bytes_per_block(self, block_size: int) -> int:
+    def bytes_per_block(self, block_size: int, windowed: bool | None = None) -> int:
+        """KV bytes one block holds across the attention layers (``windowed``: only the
+        sliding-window layers / only the others; None: all)."""
         tot = 0
         for l in self.layers:
             if l.kind != "attention":
                 continue
+            if windowed is not None and bool(l.sliding_window) != windowed:
+                continue
             tot += 2 * block_size * l.num_kv_heads * l.head_dim * torch.empty(0, dtype=l.dtype).element_size()
         return tot
+
+    @property
+    def sliding_window(self) -> int | None:
+        """The window of the sliding-window layers when the model mixes them with
+        full-attention layers (one window), else None."""
+        att = [l for l in self.layers if l.kind == "attention"]
+        wins = {l.sliding_window for l in att if l.sliding_window}
+        if len(wins) == 1 and any(not l.sliding_window for l in att):
+            return wins.pop()
+        return None
 
 
 def component(ps, name: str) -> dict:

@@ -201,6 +201,7 @@ class GptOssAttention(nn.Module):
     def attend(self, positions: torch.Tensor, x: torch.Tensor, meta, kv: tuple, cos_sin: torch.Tensor
                ) -> torch.Tensor:
         """QKV projection, RoPE + KV write, attention: [T, nq * d], the o_proj input."""
+        meta = meta.for_layer(self.window)  # sliding-window layers: their own KV group's tables
         qkv = ops.linear(x, self.qkv_weight, self.qkv_bias)
         k_cache, v_cache = kv
         # under attention DP the slot mapping covers every replica's rows (-1 outside this

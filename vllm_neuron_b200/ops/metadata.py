@@ -37,6 +37,21 @@ class AttentionMetadata:
     # decode context parallelism: the DCP group (ranks that hold the same KV heads and
     # split the tokens of every sequence block by block); None without DCP
     cp_group: object = None
+    # sliding-window KV group (hybrid KV cache): block tables / slot mapping of the windowed
+    # layers, whose blocks behind the window have been returned; None when the windowed
+    # layers share the full-attention tables
+    block_tables_swa: torch.Tensor | None = None
+    slot_mapping_swa: torch.Tensor | None = None
+
+    def for_layer(self, window: int | None) -> "AttentionMetadata":
+        """The metadata a layer reads: the sliding-window group's tables for a windowed
+        layer when the KV cache keeps the two groups apart."""
+        if window and self.block_tables_swa is not None:
+            import dataclasses
+
+            return dataclasses.replace(self, block_tables=self.block_tables_swa, slot_mapping=self.slot_mapping_swa,
+                                       block_tables_swa=None, slot_mapping_swa=None)
+        return self
 
 
 class B200AttentionBackend:
