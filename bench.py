@@ -60,7 +60,7 @@ GPT_OSS_20B = dict(GPT_OSS_120B, num_hidden_layers=24, num_local_experts=32,
 METRIC = "output tok/s at fixed concurrency (GPT-OSS-120B, 8×B200); p50 TTFT / TPOT"
 # Device-timed value of ``--baseline-of-record`` on a B200 of this pool, per (model, GPUs),
 # the numbers BASELINE.md records (the reference publishes none); vs_baseline = value / it.
-BASELINE_OF_RECORD: dict = {}
+BASELINE_OF_RECORD: dict = {("gpt-oss-120b", 1): 3325.27}
 
 
 class ClockSampler:

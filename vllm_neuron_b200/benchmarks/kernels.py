@@ -18,6 +18,9 @@ layer shapes at TP=4):
   gdn_prefill  8192-token prompt, 4 key / 8 value heads of 128 (Qwen3-Next TP=4)
   gdn_decode   64 sequences, 8 value heads of 128
   kv_transfer  one 2048-token GPT-OSS-120B request: device export + import (disaggregated serving)
+  gemm         y[T, N] = x[T, K] W^T (+ fp32 out with --fp32-out): the tcgen05 dense GEMM of every
+               linear layer; --library times torch.nn.functional.linear (cuBLAS) on the same shape.
+               Default 64 x 5120 x 2880 (GPT-OSS QKV at TP=1); LM head: --T 64 --N 201088 --K 2880
 """
 
 from __future__ import annotations
@@ -160,7 +163,7 @@ def _attn_prefill(args):
     from vllm_neuron_b200 import ops
     from vllm_neuron_b200.ops.metadata import AttentionMetadata
 
-    L, hq, hkv, d = args.L or 2048, 64, 8, 64
+    L, hq, hkv, d = args.L or 2048, args.hq or 64, args.hkv or 8, 64
     kc, vc, bt, sl = _paged(1, L, hq, hkv, d)
     q = torch.randn(L, hq, d, device="cuda").bfloat16()
     qsl = torch.tensor([0, L], dtype=torch.int32, device="cuda")
@@ -169,6 +172,23 @@ def _attn_prefill(args):
     flops = 2 * hq * L * L * d  # causal: half of 4*L*L*d per head
     fn = lambda: ops.attention(q, kc, vc, meta, d ** -0.5)  # noqa: E731
     return fn, nbytes, flops, {"L": L, "hq": hq, "hkv": hkv, "d": d}
+
+
+def _gemm(args):
+    import torch.nn.functional as F
+
+    from vllm_neuron_b200 import ops
+
+    T, N, K = args.T or 64, args.N or 5120, args.K or 2880
+    x = torch.randn(T, K, device="cuda").bfloat16()
+    w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+    out_dtype = torch.float32 if args.fp32_out else None
+    if args.library:
+        fn = lambda: F.linear(x, w)  # noqa: E731
+    else:
+        fn = lambda: ops.linear(x, w, None, out_dtype)  # noqa: E731
+    nbytes = N * K * 2 + T * K * 2 + T * N * (4 if args.fp32_out else 2)
+    return fn, nbytes, 2 * T * N * K, {"T": T, "N": N, "K": K, "impl": "cublas" if args.library else "tcgen05"}
 
 
 def _gdn(args, decode: bool):
@@ -245,6 +265,7 @@ OPS = {
     "moe_bf16": _moe_bf16,
     "attn_decode": _attn_decode,
     "attn_prefill": _attn_prefill,
+    "gemm": _gemm,
     "gdn_prefill": lambda a: _gdn(a, False),
     "gdn_decode": lambda a: _gdn(a, True),
 }
@@ -259,8 +280,12 @@ def main() -> None:
     ap.add_argument("--E", type=int, default=0, help="experts")
     ap.add_argument("--L", type=int, default=0, help="context / prompt length")
     ap.add_argument("--splits", type=int, default=0, help="split-KV factor for attn_decode (0 = heuristic)")
-    ap.add_argument("--hq", type=int, default=0, help="query heads (attn_decode; default 64)")
-    ap.add_argument("--hkv", type=int, default=0, help="kv heads (attn_decode; default 8)")
+    ap.add_argument("--hq", type=int, default=0, help="query heads (attention ops; default 64)")
+    ap.add_argument("--hkv", type=int, default=0, help="kv heads (attention ops; default 8)")
+    ap.add_argument("--N", type=int, default=0, help="gemm output features")
+    ap.add_argument("--K", type=int, default=0, help="gemm input features")
+    ap.add_argument("--fp32-out", action="store_true", help="gemm with fp32 output (router logits)")
+    ap.add_argument("--library", action="store_true", help="gemm through cuBLAS instead of the tcgen05 kernel")
     ap.add_argument("--eager", action="store_true", help="time eager launches instead of a CUDA-graph replay")
     args = ap.parse_args()
     peaks = _peaks()

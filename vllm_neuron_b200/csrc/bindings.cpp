@@ -129,6 +129,16 @@ void paged_attention_decode(Tensor out, Tensor q, Tensor k_cache, Tensor v_cache
            "paged_attention_decode");
 }
 
+// VLLM_B200_TC_PREFILL=0 keeps prefill attention on the warp-MMA kernel (comparison runs).
+bool tc_prefill_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("VLLM_B200_TC_PREFILL");
+    v = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 void paged_attention_prefill(Tensor out, Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_tables,
                              Tensor seq_lens, Tensor qsl, c10::optional<Tensor> sinks, int64_t window, double scale,
                              double k_scale, double v_scale, int64_t max_query_len) {
@@ -141,6 +151,18 @@ void paged_attention_prefill(Tensor out, Tensor q, Tensor k_cache, Tensor v_cach
               "int32 metadata");
   const int B = seq_lens.size(0);
   c10::cuda::CUDAGuard g(q.device());
+  if (tc_prefill_enabled() && k_cache.is_contiguous() && v_cache.is_contiguous() &&
+      b200_prefill_tc_supported(d, dt(q), dt(k_cache), k_cache.size(2))) {
+    // tcgen05 / TMEM flash attention (csrc/fa_prefill.cu)
+    check_rc(b200_paged_attention_prefill_tc(
+                 out.data_ptr(), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.size(0),
+                 block_tables.data_ptr<int>(), seq_lens.data_ptr<int>(), qsl.data_ptr<int>(),
+                 sinks.has_value() ? sinks->data_ptr<float>() : nullptr, B, q.size(1), k_cache.size(1), d,
+                 q.stride(0), k_cache.size(2), block_tables.stride(0), window, (float)scale, (float)k_scale,
+                 (float)v_scale, max_query_len, dt(q), dt(k_cache), nullptr, stream()),
+             "paged_attention_prefill_tc");
+    return;
+  }
   check_rc(b200_paged_attention_prefill(out.data_ptr(), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
                                         block_tables.data_ptr<int>(), seq_lens.data_ptr<int>(), qsl.data_ptr<int>(),
                                         sinks.has_value() ? sinks->data_ptr<float>() : nullptr, B, q.size(0),

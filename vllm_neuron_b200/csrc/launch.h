@@ -57,6 +57,16 @@ int b200_paged_attention_prefill_cp(void* out, float* lse, const void* q, const 
                                     float scale, float k_scale, float v_scale, int max_query_len, int cp_rank,
                                     int cp_size, int dtype, int cache_dtype, cudaStream_t s);
 
+int b200_prefill_tc_supported(int d, int dtype, int cache_dtype, int block_size);
+
+// Prefill attention on the tensor cores (tcgen05 / TMEM / TMA): head dim 64, bf16 queries and
+// cache; num_blocks is the cache's block count (the TMA maps' extent).
+int b200_paged_attention_prefill_tc(void* out, const void* q, const void* k_cache, const void* v_cache, int num_blocks,
+                                    const int* block_tables, const int* seq_lens, const int* query_start_loc,
+                                    const float* sinks, int B, int nq, int nkv, int d, int q_stride, int block_size,
+                                    int max_blocks, int window, float scale, float k_scale, float v_scale,
+                                    int max_query_len, int dtype, int cache_dtype, int* status, cudaStream_t s);
+
 int b200_varlen_attention(void* out, const void* q, const void* k, const void* v, const int* cu_seqlens, int B,
                           int T, int nq, int nkv, int d, float scale, int causal, int max_seqlen, int dtype,
                           cudaStream_t s);
