@@ -503,7 +503,11 @@ class ModelRunner:
     def _grammar_mask(self, seqs, n_sel: int) -> torch.Tensor | None:
         """Packed allowed-token bitmask [n_sel, words] of this step's sampled rows (one row per
         sequence, in order; rows of unconstrained sequences and padding allow everything), or
-        None when no sequence carries a grammar."""
+        None when no sequence carries a grammar.  A mask set by the caller in
+        ``external_bitmask`` (an outer engine's grammar, already in this layout) is used once."""
+        ext = self.__dict__.pop("external_bitmask", None)
+        if ext is not None:
+            return ext.to(self.device, non_blocking=True)
         if not any(s.request is not None and s.request.grammar is not None for s in seqs):
             return None
         from .structured_output import fill_bitmask

@@ -44,8 +44,13 @@ def build_model(cfg: EngineConfig, ps, device: torch.device, hf: dict | None = N
 
 
 class Worker:
-    def __init__(self, cfg: EngineConfig, rank: int = 0, world_size: int = 1, local_rank: int = 0):
+    def __init__(self, cfg: EngineConfig, rank: int = 0, world_size: int = 1, local_rank: int = 0,
+                 init_method: str | None = None):
         self.cfg = cfg
+        self.init_method = init_method  # process-group rendezvous (None: file store / env://)
+        # the windowed layers may get their own block pool (off when an outer KV manager,
+        # such as vLLM's, owns a single block table per request)
+        self.swa_group_allowed = True
         self.rank = rank
         self.world_size = world_size
         self.local_rank = local_rank
@@ -69,7 +74,8 @@ class Worker:
                 cpus = bind_to_gpu_numa(self.device_index)
                 logger.info("rank %d pinned to %s CPUs of its GPU's NUMA node", self.rank,
                             len(cpus) if cpus else "no (node unknown)")
-        pstate.init_distributed_environment(self.world_size, self.rank, local_rank=self.device_index,
+        pstate.init_distributed_environment(self.world_size, self.rank, init_method=self.init_method,
+                                            local_rank=self.device_index,
                                             timeout_s=float(envs.VLLM_B200_BARRIER_TIMEOUT))
         nc = self.cfg.neuron_config
         self.ps = pstate.initialize_parallel_state(
@@ -170,6 +176,8 @@ class Worker:
         transfer, speculative decoding, attention DP or recurrent layers, whose block tables
         are shared by every layer)."""
         c = self.cfg
+        if not self.swa_group_allowed:
+            return None
         if not envs.VLLM_B200_SWA_KV_GROUP or c.enable_prefix_caching or c.decode_context_parallel_size > 1:
             return None
         if c.kv_transfer_config or c.speculative_config is not None or c.neuron_config.attention_dp_size > 1:
