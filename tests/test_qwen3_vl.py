@@ -193,3 +193,58 @@ def test_vl_interfaces_and_vision_warmup():
         assert p.shape == (3, 6) and delta == int(p.max()) + 1 - 6
     finally:
         llm.shutdown()
+
+
+def test_embed_images_block_packing_matches_single_image_calls(models):
+    """Several images encoded together (first-fit-decreasing blocks of at most
+    vision_block_size patches, one varlen vision-tower call per block) give each image the
+    same rows as encoding it alone."""
+    hf, ours = models
+    g = torch.Generator().manual_seed(3)
+    imgs = [torch.rand(3, h, w, generator=g) * 255 for h, w in ((64, 96), (128, 160), (64, 64), (96, 64))]
+    want = []
+    with torch.no_grad():
+        for im in imgs:
+            mm = ours.embed_multimodal(im)
+            want.append(torch.cat([mm["embeds"]] + list(mm["deepstack"]), dim=-1))
+        old = ours.vision_block_size
+        ours.vision_block_size = 96  # patches: 24, 80, 16, 24 -> blocks [80, 16], [24, 24]
+        try:
+            n0 = ours.encoder_calls
+            got = ours.embed_images(imgs)
+            calls = ours.encoder_calls - n0
+        finally:
+            ours.vision_block_size = old
+    assert calls == 2
+    for a, b in zip(got, want):
+        assert a.shape == b.shape and torch.allclose(a, b, atol=1e-4, rtol=1e-4)
+
+
+def test_vision_data_parallel_generation_matches_single_rank(models, tmp_path):
+    """Vision DP = 2 over gloo (vision TP 1, text TP 2): each rank encodes its share of the
+    packed blocks and one all-gather gives both ranks every image; greedy tokens of a prompt
+    with three images equal the single-rank engine's."""
+    from vllm_neuron_b200 import LLM, SamplingParams
+    from vllm_neuron_b200.utils.checkpoints import save_state_dict
+
+    hf, ours = models
+    cfg = hf.config.to_dict()
+    cfg["architectures"] = ["Qwen3VLForConditionalGeneration"]
+    path = str(tmp_path / "vl")
+    save_state_dict({k: v.detach().clone().contiguous() for k, v in hf.state_dict().items()}, path, cfg)
+    g = torch.Generator().manual_seed(5)
+    imgs = [torch.rand(3, h, w, generator=g) * 255 for h, w in ((64, 96), (96, 64), (64, 64))]
+    prompt = [5, 1001, 1000, 1002, 6, 1001, 1000, 1002, 1001, 1000, 1002, 7]
+    outs = []
+    for extra in ({}, {"tensor_parallel_size": 2,
+                       "additional_config": {"vision_neuron_config": {"tp_size": 1, "dp_size": 2,
+                                                                      "vision_attention_block_size": 32}}}):
+        llm = LLM(model=path, dtype="float32", max_model_len=256, max_num_seqs=2, max_num_batched_tokens=256,
+                  block_size=16, device="cpu", **extra)
+        try:
+            o = llm.generate([{"prompt_token_ids": prompt, "multi_modal_data": {"image": imgs}}],
+                             SamplingParams(temperature=0, max_tokens=6, ignore_eos=True))
+            outs.append(list(o[0].outputs[0].token_ids))
+        finally:
+            llm.shutdown()
+    assert outs[0] == outs[1] and len(outs[0]) == 6

@@ -521,6 +521,29 @@ class ModelRunner:
         images on first use), their token indices, and [3, T] multimodal positions."""
         model = self.model
         H = model.cfg.hidden_size
+        # every image this step needs that is not cached yet: one batched (block-packed,
+        # vision-DP) encoder pass; every rank runs the same step, so the collectives match
+        todo = []
+        for s in so.seqs:
+            req = s.request
+            if req is None or req.mrope_positions is None:
+                continue
+            k = len(s.token_ids)
+            for it_i, it in enumerate(req.mm_items or []):
+                if max(s.start_pos, it["offset"]) < min(s.start_pos + k, it["offset"] + it["n"]) and \
+                        not self.encoder_cache.has(req.request_id, it_i):
+                    todo.append((req.request_id, it_i, it["pixels"]))
+        if todo:
+            with torch.inference_mode():
+                if hasattr(model, "embed_images"):
+                    fats = model.embed_images([px for _, _, px in todo])
+                else:
+                    fats = []
+                    for _, _, px in todo:
+                        mm = model.embed_multimodal(px)
+                        fats.append(torch.cat([mm["embeds"]] + list(mm["deepstack"]), dim=-1))
+            for (rid, it_i, _), fat in zip(todo, fats):
+                self.encoder_cache.put(rid, it_i, fat)
         p3_parts, idx, rows = [], [], []
         t = 0
         for s in so.seqs:
@@ -537,11 +560,6 @@ class ModelRunner:
                     hi = min(s.start_pos + k, it["offset"] + it["n"])
                     if lo >= hi:
                         continue
-                    if not self.encoder_cache.has(req.request_id, it_i):
-                        with torch.inference_mode():
-                            mm = model.embed_multimodal(it["pixels"])
-                        fat = torch.cat([mm["embeds"]] + list(mm["deepstack"]), dim=-1)
-                        self.encoder_cache.put(req.request_id, it_i, fat)
                     r = torch.arange(lo - it["offset"], hi - it["offset"], device=self.device)
                     rows.append(self.encoder_cache.gather(req.request_id, it_i, r))
                     idx.append(torch.arange(t + lo - s.start_pos, t + hi - s.start_pos))

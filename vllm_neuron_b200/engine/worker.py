@@ -109,6 +109,8 @@ class Worker:
         for m in model.modules():  # kernel weight layouts (e.g. grouped-GEMM tiles)
             if hasattr(m, "process_weights_after_loading"):
                 m.process_weights_after_loading()
+        if hasattr(model, "vision_block_size"):
+            model.vision_block_size = int(self.cfg.vision_neuron_config.vision_attention_block_size)
         self.model = model.eval()
         self.model_cfg = mcfg
         self.hf = hf

@@ -260,7 +260,10 @@ class Qwen3VLForConditionalGeneration(LlamaForCausalLM):
         super().__init__(cfg.text, ps, dtype, device, kv_dtype)
         self.vl_cfg = cfg
         self.visual = Qwen3VLVisionModel(cfg.vision, ps.vision_tp, dtype, device)
+        self.vision_dp = ps.vision_dp
+        self.vision_block_size = 2048  # patches per packed encoder call (vision_attention_block_size)
         self.inv = cfg.text.inv_freq()[0]
+        self.encoder_calls = 0
 
     # ------------------------------------------------------------ multimodal helpers
     def embed_multimodal(self, pixels: torch.Tensor) -> dict:
@@ -270,6 +273,64 @@ class Qwen3VLForConditionalGeneration(LlamaForCausalLM):
         dev = self.visual.patch_w.device
         emb, deep = self.visual(patches.to(dev), [grid])
         return {"embeds": emb, "deepstack": deep, "grid": grid}
+
+    def embed_images(self, pixels: list[torch.Tensor]) -> list[torch.Tensor]:
+        """Every image of a step at once (``vision_encoder_bf16.py:806-862`` of the reference:
+        block packing, DP scatter, DP gather).  The images' patch sequences are packed first-fit
+        decreasing into blocks of at most ``vision_block_size`` patches; one vision-tower call
+        per block runs its images as one varlen batch.  With vision data parallelism the blocks
+        are dealt to the ranks of the ``vision_dp`` group (largest first, to the least-loaded
+        rank), each rank encodes its blocks with its vision-TP peers, and one all-gather of the
+        padded results gives every rank every image.  Returns per image the "fat" rows
+        [tokens, hidden x (1 + deepstack levels)]."""
+        from ..utils.vision_utils import pack_sequences
+
+        vc = self.vl_cfg.vision
+        pre = [preprocess_image(px, vc) for px in pixels]
+        lens = [p.shape[0] for p, _ in pre]
+        m2 = vc.spatial_merge_size ** 2
+        blocks = pack_sequences(lens, self.vision_block_size)
+        g = self.vision_dp
+        dp = g.world_size if g is not None else 1
+        me = g.rank_in_group if g is not None else 0
+        load = [0] * dp
+        owner = []
+        for blk in blocks:  # pack_sequences returns the blocks largest first
+            r = min(range(dp), key=lambda i: (load[i], i))
+            owner.append(r)
+            load[r] += sum(lens[i] for i in blk)
+        dev = self.visual.patch_w.device
+        out: list[torch.Tensor | None] = [None] * len(pixels)
+        mine: list[int] = []
+        for blk, r in zip(blocks, owner):
+            if r != me:
+                continue
+            patches = torch.cat([pre[i][0] for i in blk]).to(dev)
+            emb, deep = self.visual(patches, [pre[i][1] for i in blk])
+            self.encoder_calls += 1
+            fat = torch.cat([emb] + list(deep), dim=-1)
+            off = 0
+            for i in blk:
+                n = lens[i] // m2
+                out[i] = fat[off:off + n]
+                off += n
+                mine.append(i)
+        if dp > 1:
+            width = (1 + len(vc.deepstack_visual_indexes)) * vc.out_hidden_size
+            per_rank = [[i for blk, r in zip(blocks, owner) if r == q for i in blk] for q in range(dp)]
+            rows = [sum(lens[i] // m2 for i in ids) for ids in per_rank]
+            buf = torch.zeros(max(rows), width, dtype=self.visual.patch_w.dtype, device=dev)
+            if mine:
+                local = torch.cat([out[i] for i in mine])
+                buf[:local.shape[0]] = local
+            allb = g.all_gather(buf[None], dim=0)  # [dp, max_rows, width]
+            for q, ids in enumerate(per_rank):
+                off = 0
+                for i in ids:
+                    n = lens[i] // m2
+                    out[i] = allb[q, off:off + n]
+                    off += n
+        return out  # type: ignore[return-value]
 
     # ------------------------------------------------ capabilities (models/interfaces.py)
     @classmethod
