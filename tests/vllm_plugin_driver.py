@@ -19,10 +19,12 @@ def main() -> None:
     from vllm import SamplingParams
     from vllm.inputs import TokensPrompt
 
-    kw = dict(model=args["model"], skip_tokenizer_init=True, max_model_len=256, max_num_seqs=args.get("max_num_seqs", 4),
-              max_num_batched_tokens=args.get("max_num_batched_tokens", 128), block_size=16, dtype="float32",
-              enforce_eager=True, gpu_memory_utilization=0.5, enable_prefix_caching=args.get("prefix", False),
+    kw = dict(model=args["model"], skip_tokenizer_init=True, max_model_len=args.get("max_model_len", 256), max_num_seqs=args.get("max_num_seqs", 4),
+              max_num_batched_tokens=args.get("max_num_batched_tokens", 128), block_size=args.get("block_size", 16),
+              dtype=args.get("dtype", "float32"), enforce_eager=args.get("enforce_eager", True), gpu_memory_utilization=0.5, enable_prefix_caching=args.get("prefix", False),
               seed=0)
+    if args.get("additional_config"):
+        kw["additional_config"] = args["additional_config"]
     if args.get("num_gpu_blocks_override"):
         kw["num_gpu_blocks_override"] = args["num_gpu_blocks_override"]
     llm = vllm.LLM(**kw)

@@ -19,9 +19,10 @@ CUDA graphs; ``engine/model_runner.py``: input staging, forward, sampling):
   ``[num_computed, num_computed + num_scheduled)``; a step of single-token requests that
   all sample is a decode step (graph replay), anything else the varlen path.  A partial
   prefill chunk samples nothing.
-* Structured output: when the step has grammar-constrained requests, ``execute_model``
-  returns None and ``sample_tokens`` runs the step with vLLM's packed bitmask (rows of
-  unconstrained requests allow every token).
+* Execution: ``execute_model`` books the step and returns None; ``sample_tokens`` (which
+  vLLM calls next, with the grammar bitmask of the step's structured-output requests) runs
+  the forward pass and sampling, applying vLLM's packed bitmask (rows of unconstrained
+  requests allow every token).
 
 Not routed through this worker: speculative decoding, multimodal inputs, LoRA and pooling
 (they run on this framework's own engine, ``vllm-b200 serve``); requests that need them
@@ -163,10 +164,10 @@ class B200VllmWorker(_base()):
         return set()
 
     def profile(self, is_start: bool = True, profile_prefix: str | None = None) -> None:
-        from ..profiler import Profiler
+        from ..profiler import Profiler, ProfilerConfig
 
         if is_start:
-            self._profiler = Profiler(self.cfg.profiler_config)
+            self._profiler = Profiler(ProfilerConfig.from_dict(self.cfg.profiler_config), rank=self.rank)
             self._profiler.start()
         elif getattr(self, "_profiler", None) is not None:
             self._profiler.stop()
@@ -264,12 +265,16 @@ class B200VllmWorker(_base()):
 
     @torch.inference_mode()
     def execute_model(self, scheduler_output):
+        """Books the step; the forward and sampling run in ``sample_tokens``, which vLLM's
+        engine calls next with the grammar bitmask (its batch-queue loop always takes the
+        step's output from ``sample_tokens``).  An empty step returns its output here."""
         self._update_states(scheduler_output)
         ours = self._schedule(scheduler_output)
-        if getattr(scheduler_output, "has_structured_output_requests", False) and ours.seqs:
-            self._pending = (scheduler_output, ours)
-            return None
-        return self._run(scheduler_output, ours, None)
+        if not ours.seqs:
+            self._pending = None
+            return self._run(scheduler_output, ours, None)
+        self._pending = (scheduler_output, ours)
+        return None
 
     @torch.inference_mode()
     def sample_tokens(self, grammar_output):
