@@ -159,7 +159,7 @@ void paged_attention_prefill(Tensor out, Tensor q, Tensor k_cache, Tensor v_cach
                  block_tables.data_ptr<int>(), seq_lens.data_ptr<int>(), qsl.data_ptr<int>(),
                  sinks.has_value() ? sinks->data_ptr<float>() : nullptr, B, q.size(1), k_cache.size(1), d,
                  q.stride(0), k_cache.size(2), block_tables.stride(0), window, (float)scale, (float)k_scale,
-                 (float)v_scale, max_query_len, dt(q), dt(k_cache), nullptr, stream()),
+                 (float)v_scale, max_query_len, (int)q.size(0), dt(q), dt(k_cache), nullptr, stream()),
              "paged_attention_prefill_tc");
     return;
   }

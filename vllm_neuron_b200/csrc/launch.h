@@ -65,7 +65,7 @@ int b200_paged_attention_prefill_tc(void* out, const void* q, const void* k_cach
                                     const int* block_tables, const int* seq_lens, const int* query_start_loc,
                                     const float* sinks, int B, int nq, int nkv, int d, int q_stride, int block_size,
                                     int max_blocks, int window, float scale, float k_scale, float v_scale,
-                                    int max_query_len, int dtype, int cache_dtype, int* status, cudaStream_t s);
+                                    int max_query_len, int num_tokens, int dtype, int cache_dtype, int* status, cudaStream_t s);
 
 int b200_varlen_attention(void* out, const void* q, const void* k, const void* v, const int* cu_seqlens, int B,
                           int T, int nq, int nkv, int d, float scale, int causal, int max_seqlen, int dtype,
