@@ -215,6 +215,8 @@ def main() -> None:
     ap.add_argument("--concurrency", type=int, default=64)
     ap.add_argument("--prompt-len", type=int, default=2048)
     ap.add_argument("--output-len", type=int, default=512)
+    ap.add_argument("--mixed-prefill-tokens", type=int, default=0,
+                    help="prompt tokens per decode step (mixed steps); 0: separate prefill steps")
     ap.add_argument("--profile-dir", default=None,
                     help="also write a per-kernel table of one profiled serving period (rank 0)")
     ap.add_argument("--baseline-of-record", action="store_true",
@@ -248,6 +250,7 @@ def main() -> None:
     llm = LLM(hf_config=hf, load_format="dummy", dtype="bfloat16", tensor_parallel_size=N,
               max_model_len=max_len, max_num_seqs=C, max_num_batched_tokens=4096, block_size=32,
               max_num_prefills_per_step=2, spmd=N > 1, seed=0, async_scheduling=True,
+              mixed_prefill_tokens=args.mixed_prefill_tokens,
               additional_config={"neuron_config": {"ep_degree": N, "quantization": "mxfp4",
                                                    "num_seqs_buckets": [C]}})
     eng = llm.engine
@@ -355,6 +358,9 @@ def main() -> None:
                        "phase": f"steady-state closed loop at concurrency {C}: each step is one serving period "
                                 f"(a finished request replaced by a new {P}-token prompt, its prefill, and the "
                                 f"decode steps until the next completion)",
+                       "prefill_policy": (f"prompt chunks of <= {args.mixed_prefill_tokens} tokens inside the decode "
+                                          f"steps (mixed steps)" if args.mixed_prefill_tokens
+                                          else "separate prefill steps"),
                        "l2": "weights (~60 GB) and KV exceed L2 every engine step; no flush",
                        "output_tokens": tokens, "engine_steps": n_engine_steps,
                        "ttft_p50_ms": round(1000 * ttfts[len(ttfts) // 2], 2) if ttfts else None,

@@ -77,3 +77,27 @@ def test_tc_prefill_without_sinks_and_exact_tile_edges():
         want = ref.paged_attention(q.float(), kc.float(), vc.float(), bt, sl, qsl, 0.125, None, window or None)
         err = (got.float() - want).abs()
         assert (err > 2e-2 + 3e-2 * want.abs()).sum().item() == 0, f"window {window}: max err {err.max().item()}"
+
+
+@pytest.mark.parametrize("window", [0, 128])
+def test_mixed_step_attention_matches_reference(window):
+    """A mixed step: single-token decode sequences first (decode kernel on their rows), then
+    prompt chunks (tensor-core prefill kernel), in one ops.attention call."""
+    from vllm_neuron_b200 import ops
+    from vllm_neuron_b200.ops import reference as ref
+    from vllm_neuron_b200.ops.metadata import AttentionMetadata
+
+    seq_lens = [300, 1500, 77, 1024, 640, 200]
+    q_lens = [1, 1, 1, 1, 256, 200]
+    q, kc, vc, bt, sl, qsl = _setup(seq_lens, q_lens, 8, 1, 32, seed=21 + window)
+    sinks = torch.randn(8, device=DEV)
+    splits = 4
+    ws = torch.empty(len(seq_lens) * 8 * splits * 65, device=DEV)
+    meta = AttentionMetadata(sum(q_lens), len(seq_lens), False, qsl, sl, bt, None, None, max(q_lens),
+                             max(seq_lens), workspace=ws, num_splits=splits, num_decode_seqs=4)
+    got = ops.attention(q, kc, vc, meta, 0.125, sinks, window)
+    torch.cuda.synchronize()
+    want = ref.paged_attention(q.float(), kc.float(), vc.float(), bt, sl, qsl, 0.125, sinks, window or None)
+    err = (got.float() - want).abs()
+    assert (err > 2e-2 + 3e-2 * want.abs()).sum().item() == 0, f"max err {err.max().item()}"
+    assert ops.check_device_status(q.device) == 0

@@ -104,3 +104,47 @@ def test_sequence_parallel_prefill_counts(ckpt, monkeypatch):
         llm.shutdown()
     assert [o.outputs[0].token_ids for o in outs] == want
     assert calls["sp"] > 0
+
+
+def test_fp8_modelopt_checkpoint_close_to_dequantized_hf(tmp_path):
+    """A static-FP8 (ModelOpt layout: e4m3 weights, per-tensor weight_scale and input_scale per
+    projection; separate q / k / v and gate / up scales fused into per-row scales) checkpoint
+    on the CPU path: logits close to HF fp32 with the dequantised weights (the remaining
+    difference is the e4m3 rounding of the activations)."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from vllm_neuron_b200 import LLM
+    from vllm_neuron_b200.utils.checkpoints import save_state_dict
+
+    torch.manual_seed(0)
+    cfg = LlamaConfig(vocab_size=2048, hidden_size=128, intermediate_size=256, num_hidden_layers=2,
+                      num_attention_heads=8, num_key_value_heads=2, max_position_embeddings=1024,
+                      tie_word_embeddings=False)
+    m = LlamaForCausalLM(cfg).eval().float()
+    sd, deq = {}, {}
+    for k, v in m.state_dict().items():
+        if k.endswith("proj.weight"):
+            s = v.abs().amax() / 448 * (1.5 if "k_proj" in k or "up_proj" in k else 1.0)
+            q = (v / s).clamp(-448, 448).to(torch.float8_e4m3fn)
+            sd[k] = q
+            sd[k.replace("weight", "weight_scale")] = s.reshape(())
+            sd[k.replace("weight", "input_scale")] = torch.tensor(0.01)
+            deq[k] = q.float() * s
+        else:
+            sd[k] = v.detach().clone().contiguous()
+    m.load_state_dict({**m.state_dict(), **deq})
+    d = cfg.to_dict()
+    d["architectures"] = ["LlamaForCausalLM"]
+    d["quantization_config"] = {"quant_method": "modelopt", "quant_algo": "FP8"}
+    save_state_dict(sd, str(tmp_path), d)
+    ids = torch.randint(1, 2000, (40,), generator=torch.Generator().manual_seed(1)).tolist()
+    llm = LLM(model=str(tmp_path), dtype="float32", device="cpu", max_model_len=256, max_num_seqs=2,
+              max_num_batched_tokens=128, block_size=16)
+    try:
+        got = llm.engine.score(ids).float()
+    finally:
+        llm.shutdown()
+    with torch.no_grad():
+        want = m(torch.tensor([ids])).logits[0].float()
+    cos = torch.nn.functional.cosine_similarity(got, want, dim=-1)
+    assert cos.min().item() > 0.99, cos.min().item()

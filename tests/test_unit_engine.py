@@ -220,3 +220,45 @@ def test_sliding_window_kv_group_frees_blocks_behind_the_window():
     assert len(req.block_ids) == -(-500 // bs)  # the full group keeps everything
     kv.free(req)
     assert kv.swa_pool.num_free == 39 and kv.pool.num_free == 199 and req.swa_block_ids == []
+
+
+def test_mixed_prefill_decode_steps_keep_greedy_tokens(monkeypatch):
+    """With mixed_prefill_tokens, prompt chunks ride along in the decode steps of running
+    requests ("mixed" steps: decodes first, then chunks of at most that many prompt tokens);
+    greedy tokens equal the separate-steps engine's."""
+    from tiny_configs import workload
+
+    from vllm_neuron_b200 import LLM, SamplingParams
+    from vllm_neuron_b200.accuracy.testing import TINY_GPT_OSS_D64
+    from vllm_neuron_b200.engine import model_runner
+
+    kinds, launched = [], []
+    orig, orig_launch = model_runner.ModelRunner.execute, model_runner.ModelRunner.launch
+
+    def spy(self, so, *a, **k):
+        kinds.append((so.kind, so.num_decode, sum(len(s.token_ids) for s in so.seqs[so.num_decode:])))
+        return orig(self, so, *a, **k)
+
+    def spy_launch(self, so, *a, **k):
+        launched.append(so.kind)
+        return orig_launch(self, so, *a, **k)
+
+    monkeypatch.setattr(model_runner.ModelRunner, "execute", spy)
+    monkeypatch.setattr(model_runner.ModelRunner, "launch", spy_launch)
+    cfg = dict(TINY_GPT_OSS_D64)
+    cfg["architectures"] = ["GptOssForCausalLM"]
+    outs = []
+    for mixed, async_ in ((0, False), (32, False), (32, True)):
+        llm = LLM(hf_config=dict(cfg), load_format="dummy", dtype="float32", device="cpu", max_model_len=512,
+                  max_num_seqs=4, max_num_batched_tokens=128, block_size=16, seed=2, mixed_prefill_tokens=mixed,
+                  async_scheduling=async_)
+        try:
+            o = llm.generate(prompt_token_ids=workload(n=7, lo=20, hi=150, vocab=4000, seed=3),
+                             sampling_params=SamplingParams(temperature=0, max_tokens=10, ignore_eos=True))
+            outs.append([x.outputs[0].token_ids for x in o])
+        finally:
+            llm.shutdown()
+    mixed_steps = [k for k in kinds if k[0] == "mixed"]
+    assert mixed_steps and all(d > 0 and 0 < n <= 32 for _, d, n in mixed_steps), kinds
+    assert outs[0] == outs[1] == outs[2]
+    assert "mixed" in launched, launched  # asynchronous mixed steps

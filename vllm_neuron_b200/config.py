@@ -223,6 +223,9 @@ class EngineConfig:
     enable_prefix_caching: bool = False
     enable_chunked_prefill: bool = True
     max_num_prefills_per_step: int = 1
+    # > 0: prompt chunks of at most this many tokens join the decode steps while requests are
+    # decoding (mixed steps); 0: prefill and decode always run as separate steps
+    mixed_prefill_tokens: int = 0
     enforce_eager: bool = False
     async_scheduling: bool = False
     device: str = "auto"

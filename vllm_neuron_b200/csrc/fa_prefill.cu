@@ -304,6 +304,18 @@ __global__ void __launch_bounds__(kThreads, 1) fa_prefill_kernel(const __grid_co
         }
         tc::fence_after_sync();
         const int key0 = it.key_lo + j * kBK;
+        // a tile no row of this warp can see (the other query tile's diagonal or window edge):
+        // P = 0 without reading S; the row statistics are unchanged
+        if (__all_sync(0xffffffffu, key0 > hi_vis || key0 + kBK - 1 < lo_vis)) {
+#pragma unroll
+          for (int ch = 0; ch < 16; ++ch)
+            *reinterpret_cast<uint4*>(pbuf + (ch >> 3) * (kBQ * 128) + sw128(r, ch & 7)) = make_uint4(0, 0, 0, 0);
+          fence_async_smem();
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&p_full[x]);
+          continue;
+        }
         float sv[kBK];
 #pragma unroll
         for (int cc = 0; cc < kBK; cc += 32)

@@ -83,6 +83,8 @@ struct Args {
   int ldy;
   int m_tiles, n_tiles, splits, k_stages, sps;
   const __nv_bfloat16* bias;  // [N] or null (kStore)
+  const float* alpha;         // fp8 operands: dequantisation factor, per tensor ([1]) or per feature ([N])
+  int alpha_n;                // 0 (none), 1 or N
   void* y;                    // kStore: [T, ldy], bf16 (or fp32 when out_f32)
   int out_f32;
   float* ws;                  // kStore, splits > 1: fp32 sums [T, N], zero between calls
@@ -124,7 +126,10 @@ B200_D float4 ld_cg_f4(const float* p) {
 B200_D void store8(const Args& a, int t, int f, const float* v) {
   float o[8];
 #pragma unroll
-  for (int h = 0; h < 8; ++h) o[h] = v[h] + (a.bias != nullptr ? __bfloat162float(a.bias[f + h]) : 0.f);
+  for (int h = 0; h < 8; ++h) {
+    const float sc = a.alpha_n == 0 ? 1.f : a.alpha[a.alpha_n == 1 ? 0 : f + h];
+    o[h] = v[h] * sc + (a.bias != nullptr ? __bfloat162float(a.bias[f + h]) : 0.f);
+  }
   if (a.out_f32) {
     float* y = static_cast<float*>(a.y) + (size_t)t * a.ldy + f;
     *reinterpret_cast<float4*>(y) = make_float4(o[0], o[1], o[2], o[3]);
@@ -179,7 +184,9 @@ B200_D Item item_of(const Args& a, int w, int cl_split = -1) {
   return it;
 }
 
-template <int NT, int EPI, bool CL>
+// F8: both operands e4m3 (tcgen05 kind::f8f6f4, 128 K elements per 128-byte stage row),
+// else bf16 (kind::f16, 64 K elements per stage row); the shared-memory layout is the same.
+template <int NT, int EPI, bool CL, bool F8 = false>
 __global__ void __launch_bounds__(256, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmW,
                                                       const __grid_constant__ CUtensorMap tmX, Args a) {
   if (threadIdx.x == 0) stamp(a, 0);
@@ -258,8 +265,9 @@ __global__ void __launch_bounds__(256, 1) gemm_kernel(const __grid_constant__ CU
           }
           tc::mbar_arrive_expect_tx(&full[s], C::kStage);
           uint8_t* st = smem + s * C::kStage;
-          tc::tma_load_2d(st, &tmW, kt * kBK, wi.m0, &full[s]);
-          tc::tma_load_2d(st + C::kA, &tmX, kt * kBK, wi.n0 * NT, &full[s]);
+          constexpr int kEB = F8 ? 2 * kBK : kBK;  // K elements per 128-byte stage row
+          tc::tma_load_2d(st, &tmW, kt * kEB, wi.m0, &full[s]);
+          tc::tma_load_2d(st + C::kA, &tmX, kt * kEB, wi.n0 * NT, &full[s]);
           if (it == 0) stamp(a, 2);
         }
       }
@@ -267,7 +275,7 @@ __global__ void __launch_bounds__(256, 1) gemm_kernel(const __grid_constant__ CU
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      const uint32_t idesc = tc::idesc_f16_bf16(kBM, NT);
+      const uint32_t idesc = F8 ? tc::idesc_f8f6f4_e4m3(kBM, NT) : tc::idesc_f16_bf16(kBM, NT);
       int it = 0, local = 0;
       bool ok = true;
       for (int w = first; w < W && ok; w += step) {
@@ -287,8 +295,12 @@ __global__ void __launch_bounds__(256, 1) gemm_kernel(const __grid_constant__ CU
           const uint64_t ad = tc::desc_sw128(st);
           const uint64_t bd = tc::desc_sw128(st + C::kA);
 #pragma unroll
-          for (int kb = 0; kb < 4; ++kb)  // 4 x K=16 per 128-byte stage (+32 bytes each)
-            tc::mma_f16(t_d, ad + 2 * kb, bd + 2 * kb, idesc, (kt > wi.ks0 || kb > 0) ? 1u : 0u);
+          for (int kb = 0; kb < 4; ++kb) {  // 4 x (K=16 bf16 or K=32 e4m3) per 128-byte stage (+32 bytes each)
+            if constexpr (F8)
+              tc::mma_f8f6f4(t_d, ad + 2 * kb, bd + 2 * kb, idesc, (kt > wi.ks0 || kb > 0) ? 1u : 0u);
+            else
+              tc::mma_f16(t_d, ad + 2 * kb, bd + 2 * kb, idesc, (kt > wi.ks0 || kb > 0) ? 1u : 0u);
+          }
           tc::mma_commit(&empty[s]);
           if (it == 0) stamp(a, 3);
         }
@@ -620,15 +632,16 @@ static PFN_cuTensorMapEncodeTiled_v12000 encoder() {
   return fn;
 }
 
-// Row-major bf16 [rows, K] with row stride ld elements; box 64 x box_rows, 128-byte swizzle.
-static int make_map(CUtensorMap* m, const void* p, int rows, int K, int ld, int box_rows) {
+// Row-major [rows, K] (bf16, or e4m3 when f8) with row stride ld elements; box of one
+// 128-byte row (64 bf16 / 128 e4m3) x box_rows, 128-byte swizzle.
+static int make_map(CUtensorMap* m, const void* p, int rows, int K, int ld, int box_rows, bool f8 = false) {
   auto enc = encoder();
   if (!enc) return kBadShape;
   cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * (f8 ? 1 : 2)};
+  cuuint32_t box[2] = {(cuuint32_t)(f8 ? 2 * kBK : kBK), (cuuint32_t)box_rows};
   cuuint32_t es[2] = {1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(p), dims, strides, box, es,
+  CUresult r = enc(m, f8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(p), dims, strides, box, es,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : kTensorMapErrorBase + (int)r;
@@ -654,12 +667,12 @@ struct Plan {
 // split: for decode widths (NT <= 64) across a cluster of 2 / 4 / 8 CTAs that reduce over
 // DSMEM, chosen by a small cost model (rounds of tiles x stages per split, plus a reduction
 // cost); for wider tiles with vector atomics (at least 8 stages per split, at most 4 splits).
-static Plan make_plan(int T, int N, int K, int max_splits, bool allow_cluster = true) {
+static Plan make_plan(int T, int N, int K, int max_splits, bool allow_cluster = true, bool f8 = false) {
   Plan p;
   p.nt = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
   p.m_tiles = cdiv(N, kBM);
   p.n_tiles = cdiv(T, p.nt);
-  p.k_stages = cdiv(K, kBK);
+  p.k_stages = cdiv(K, f8 ? 2 * kBK : kBK);
   p.cluster = false;
   const int tiles = p.m_tiles * p.n_tiles;
   const int sms = sm_count();
@@ -691,15 +704,15 @@ static Plan make_plan(int T, int N, int K, int max_splits, bool allow_cluster = 
 
 static unsigned long long* g_trace = nullptr;  // set by b200_gemm_set_trace (analysis only)
 
-template <int NT, int EPI, bool CL>
+template <int NT, int EPI, bool CL, bool F8 = false>
 static int launch(const Plan& p, const void* x, int ldx, const void* w, Args a, cudaStream_t s) {
   using C = Cfg<NT, CL>;
   a.trace = g_trace;
   CUtensorMap tw, tx;
   int rc;
-  if ((rc = make_map(&tw, w, a.N, a.K, a.K, kBM))) return rc;
-  if ((rc = make_map(&tx, x, a.T, a.K, ldx, NT))) return rc;
-  auto kern = gemm_kernel<NT, EPI, CL>;
+  if ((rc = make_map(&tw, w, a.N, a.K, a.K, kBM, F8))) return rc;
+  if ((rc = make_map(&tx, x, a.T, a.K, ldx, NT, F8))) return rc;
+  auto kern = gemm_kernel<NT, EPI, CL, F8>;
   static bool attr = false;
   static int max_clusters[9] = {0};
   if (!attr) {
@@ -735,21 +748,21 @@ static int launch(const Plan& p, const void* x, int ldx, const void* w, Args a, 
   return (int)cudaGetLastError();
 }
 
-template <int EPI>
+template <int EPI, bool F8 = false>
 static int dispatch(const Plan& p, const void* x, int ldx, const void* w, const Args& a, cudaStream_t s) {
   if (p.cluster) {
     switch (p.nt) {
-      case 16: return launch<16, EPI, true>(p, x, ldx, w, a, s);
-      case 32: return launch<32, EPI, true>(p, x, ldx, w, a, s);
-      default: return launch<64, EPI, true>(p, x, ldx, w, a, s);
+      case 16: return launch<16, EPI, true, F8>(p, x, ldx, w, a, s);
+      case 32: return launch<32, EPI, true, F8>(p, x, ldx, w, a, s);
+      default: return launch<64, EPI, true, F8>(p, x, ldx, w, a, s);
     }
   }
   switch (p.nt) {
-    case 16: return launch<16, EPI, false>(p, x, ldx, w, a, s);
-    case 32: return launch<32, EPI, false>(p, x, ldx, w, a, s);
-    case 64: return launch<64, EPI, false>(p, x, ldx, w, a, s);
-    case 128: return launch<128, EPI, false>(p, x, ldx, w, a, s);
-    default: return launch<256, EPI, false>(p, x, ldx, w, a, s);
+    case 16: return launch<16, EPI, false, F8>(p, x, ldx, w, a, s);
+    case 32: return launch<32, EPI, false, F8>(p, x, ldx, w, a, s);
+    case 64: return launch<64, EPI, false, F8>(p, x, ldx, w, a, s);
+    case 128: return launch<128, EPI, false, F8>(p, x, ldx, w, a, s);
+    default: return launch<256, EPI, false, F8>(p, x, ldx, w, a, s);
   }
 }
 
@@ -803,6 +816,37 @@ extern "C" int b200_gemm_bf16(void* y, int ldy, int out_f32, const void* x, int 
     a.counters = counters;
   }
   return dispatch<kStore>(p, x, ldx, w, a, s);
+}
+
+// FP8 GEMM: Y[T, N] = (X[T, K] . W[N, K]^T) * alpha + bias with X and W e4m3 (row strides ldx
+// and K bytes), alpha an fp32 dequantisation factor per tensor (alpha_n = 1) or per output
+// feature (alpha_n = N), bias bf16 or null; Y bf16 (or fp32).  Workspace as b200_gemm_bf16.
+extern "C" int b200_gemm_fp8(void* y, int ldy, int out_f32, const void* x, int ldx, const void* w, const void* bias,
+                             const float* alpha, int alpha_n, int T, int N, int K, float* ws, int64_t ws_floats,
+                             int* counters, int64_t n_counters, int max_splits, int* status, cudaStream_t s) {
+  if (T < 0 || N <= 0 || K <= 0 || K % 16 || ldx % 16 || ldx < K) return kBadShape;
+  if (misaligned_host(x) || misaligned_host(w)) return kBadAlignment;
+  if (ldy % 8 || ldy < N || N % 8 || alpha == nullptr || (alpha_n != 1 && alpha_n != N)) return kBadShape;
+  if (T == 0) return 0;
+  const Plan p = make_plan(T, N, K, max_splits, true, true);
+  Args a{};
+  a.T = T, a.N = N, a.K = K, a.ldy = ldy;
+  a.m_tiles = p.m_tiles, a.n_tiles = p.n_tiles, a.splits = p.splits, a.k_stages = p.k_stages, a.sps = p.sps;
+  a.bias = static_cast<const __nv_bfloat16*>(bias);
+  a.alpha = alpha;
+  a.alpha_n = alpha_n;
+  a.y = y;
+  a.out_f32 = out_f32;
+  a.status = status;
+  if (misaligned_host(y) || (out_f32 && ldy % 4)) return kBadAlignment;
+  if (p.splits > 1 && !p.cluster) {
+    const int64_t tiles = (int64_t)p.m_tiles * p.n_tiles;
+    if (ws == nullptr || counters == nullptr || ws_floats < (int64_t)T * N || n_counters < 4 * tiles)
+      return kScratchTooSmall;
+    a.ws = ws;
+    a.counters = counters;
+  }
+  return dispatch<kStore, true>(p, x, ldx, w, a, s);
 }
 
 extern "C" size_t b200_red_region_bytes(int T_cap, int H_cap) { return red_region_bytes(T_cap, H_cap); }

@@ -9,6 +9,13 @@ void b200_gemm_workspace(int T, int N, int K, int max_splits, int64_t* ws_floats
 int b200_gemm_bf16(void* y, int ldy, int out_f32, const void* x, int ldx, const void* w, const void* bias, int T,
                    int N, int K, float* ws, int64_t ws_floats, int* counters, int64_t n_counters, int max_splits,
                    int* status, cudaStream_t s);
+int b200_gemm_fp8(void* y, int ldy, int out_f32, const void* x, int ldx, const void* w, const void* bias,
+                  const float* alpha, int alpha_n, int T, int N, int K, float* ws, int64_t ws_floats, int* counters,
+                  int64_t n_counters, int max_splits, int* status, cudaStream_t s);
+int b200_fp8_quant(void* q, int ldq, const void* x, int ldx, int rows, int H, const float* scale, unsigned* amax_ws,
+                   const float* w_scale, float* alpha, int alpha_n, cudaStream_t s);
+int b200_rms_norm_fp8(void* q, const void* x, void* residual, const float* w, int rows, int H, float eps,
+                      const float* scale, cudaStream_t s);
 size_t b200_red_region_bytes(int T_cap, int H_cap);
 void b200_gemm_set_trace(void* buf);
 int b200_gemm_bf16_allreduce(const void* x, int ldx, const void* w, int T, int N, int K, void* red_uc, void* red_mc,
@@ -52,6 +59,76 @@ void gemm_bf16(Tensor y, Tensor x, Tensor w, c10::optional<Tensor> bias, Tensor 
                                 status.has_value() ? status->data_ptr<int>() : nullptr,
                                 at::cuda::getCurrentCUDAStream().stream());
   TORCH_CHECK(rc == 0, "b200::gemm_bf16 failed with code ", rc);
+}
+
+void gemm_fp8(Tensor y, Tensor x, Tensor w, c10::optional<Tensor> bias, Tensor alpha, Tensor ws, Tensor counters,
+              int64_t max_splits, c10::optional<Tensor> status) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda(), "gemm_fp8: CUDA tensors required");
+  TORCH_CHECK(x.scalar_type() == at::kFloat8_e4m3fn && w.scalar_type() == at::kFloat8_e4m3fn, "gemm_fp8: e4m3 x and w");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "gemm_fp8: x [T, K], w [N, K]");
+  TORCH_CHECK(x.stride(1) == 1 && w.is_contiguous(), "gemm_fp8: x rows and w must be contiguous");
+  const int T = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK((y.scalar_type() == at::kBFloat16 || y.scalar_type() == at::kFloat) && y.dim() == 2 &&
+                  y.size(0) == T && y.size(1) == N && y.stride(1) == 1,
+              "gemm_fp8: y [T, N] bf16 or fp32 with contiguous rows");
+  TORCH_CHECK(alpha.is_cuda() && alpha.scalar_type() == at::kFloat && alpha.is_contiguous() &&
+                  (alpha.numel() == 1 || alpha.numel() == N),
+              "gemm_fp8: fp32 alpha [1] or [N]");
+  if (bias.has_value())
+    TORCH_CHECK(bias->scalar_type() == at::kBFloat16 && bias->numel() == N && bias->is_contiguous(), "gemm_fp8: bias");
+  TORCH_CHECK(ws.scalar_type() == at::kFloat && counters.scalar_type() == at::kInt, "gemm_fp8: workspace dtypes");
+  c10::cuda::CUDAGuard g(x.device());
+  const int rc = b200_gemm_fp8(y.data_ptr(), y.stride(0), y.scalar_type() == at::kFloat, x.data_ptr(), x.stride(0),
+                               w.data_ptr(), bias.has_value() ? bias->data_ptr() : nullptr, alpha.data_ptr<float>(),
+                               (int)alpha.numel(), T, N, K, ws.data_ptr<float>(), ws.numel(), counters.data_ptr<int>(),
+                               counters.numel(), max_splits, status.has_value() ? status->data_ptr<int>() : nullptr,
+                               at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(rc == 0, "b200::gemm_fp8 failed with code ", rc);
+}
+
+void fp8_quant(Tensor q, Tensor x, c10::optional<Tensor> scale, c10::optional<Tensor> amax_ws,
+               c10::optional<Tensor> w_scale, c10::optional<Tensor> alpha) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "fp8_quant: bf16 x");
+  TORCH_CHECK(q.scalar_type() == at::kFloat8_e4m3fn && q.dim() == 2 && q.size(0) == x.size(0) &&
+                  q.size(1) == x.size(1) && q.stride(1) == 1,
+              "fp8_quant: e4m3 q like x");
+  auto fptr = [](const c10::optional<Tensor>& t) -> float* {
+    if (!t.has_value()) return nullptr;
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat, "fp8_quant: fp32 device scalars");
+    return t->data_ptr<float>();
+  };
+  unsigned* aw = nullptr;
+  if (amax_ws.has_value()) {
+    TORCH_CHECK(amax_ws->is_cuda() && amax_ws->scalar_type() == at::kInt, "fp8_quant: int32 amax scratch");
+    aw = reinterpret_cast<unsigned*>(amax_ws->data_ptr<int>());
+  }
+  int alpha_n = 0;
+  if (alpha.has_value()) {
+    alpha_n = (int)alpha->numel();
+    TORCH_CHECK(!w_scale.has_value() || w_scale->numel() == alpha_n, "fp8_quant: w_scale like alpha");
+  }
+  c10::cuda::CUDAGuard g(x.device());
+  const int rc = b200_fp8_quant(q.data_ptr(), q.stride(0), x.data_ptr(), x.stride(0), x.size(0), x.size(1),
+                                fptr(scale), aw, fptr(w_scale), fptr(alpha), alpha_n,
+                                at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(rc == 0, "b200::fp8_quant failed with code ", rc);
+}
+
+void rms_norm_fp8(Tensor q, Tensor x, c10::optional<Tensor> residual, Tensor w, double eps, Tensor scale) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 2,
+              "rms_norm_fp8: bf16 x [T, H]");
+  TORCH_CHECK(q.scalar_type() == at::kFloat8_e4m3fn && q.is_contiguous() && q.numel() == x.numel(), "rms_norm_fp8: q");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && w.numel() == x.size(1), "rms_norm_fp8: fp32 w [H]");
+  TORCH_CHECK(scale.is_cuda() && scale.scalar_type() == at::kFloat, "rms_norm_fp8: fp32 scale");
+  if (residual.has_value())
+    TORCH_CHECK(residual->scalar_type() == at::kBFloat16 && residual->is_contiguous() &&
+                    residual->numel() == x.numel(),
+                "rms_norm_fp8: bf16 residual like x");
+  c10::cuda::CUDAGuard g(x.device());
+  const int rc = b200_rms_norm_fp8(q.data_ptr(), x.data_ptr(), residual.has_value() ? residual->data_ptr() : nullptr,
+                                   w.data_ptr<float>(), x.size(0), x.size(1), (float)eps, scale.data_ptr<float>(),
+                                   at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(rc == 0, "b200::rms_norm_fp8 failed with code ", rc);
 }
 
 int64_t red_region_bytes(int64_t T_cap, int64_t H_cap) { return (int64_t)b200_red_region_bytes(T_cap, H_cap); }
@@ -102,6 +179,12 @@ void register_gemm_ops(torch::Library& m) {
   m.def(
       "gemm_bf16(Tensor(a!) y, Tensor x, Tensor w, Tensor? bias, Tensor(b!) ws, Tensor(c!) counters, "
       "int max_splits, Tensor? status) -> ()");
+  m.def(
+      "gemm_fp8(Tensor(a!) y, Tensor x, Tensor w, Tensor? bias, Tensor alpha, Tensor(b!) ws, Tensor(c!) counters, "
+      "int max_splits, Tensor? status) -> ()");
+  m.def(
+      "fp8_quant(Tensor(a!) q, Tensor x, Tensor? scale, Tensor(b!)? amax_ws, Tensor? w_scale, Tensor(c!)? alpha) -> ()");
+  m.def("rms_norm_fp8(Tensor(a!) q, Tensor x, Tensor(b!)? residual, Tensor w, float eps, Tensor scale) -> ()");
   m.def("red_region_bytes(int T_cap, int H_cap) -> int");
   m.def("gemm_set_trace(int buf) -> ()");
   m.def(
@@ -114,6 +197,9 @@ void register_gemm_ops(torch::Library& m) {
 
 void register_gemm_impls(torch::Library& m) {
   m.impl("gemm_bf16", &gemm_bf16);
+  m.impl("gemm_fp8", &gemm_fp8);
+  m.impl("fp8_quant", &fp8_quant);
+  m.impl("rms_norm_fp8", &rms_norm_fp8);
   m.impl("gemm_bf16_allreduce", &gemm_bf16_allreduce);
   m.impl("allreduce_finish", &allreduce_finish);
 }

@@ -202,6 +202,15 @@ B200_HD uint32_t idesc_f16_bf16(int M, int N) {
   d |= (uint32_t)((M >> 4) & 0x1F) << 24;
   return d;
 }
+// Instruction descriptor for kind::f8f6f4 with e4m3 A and B (same type on both sides), fp32
+// accumulator, both K-major.
+B200_HD uint32_t idesc_f8f6f4_e4m3(int M, int N) {
+  uint32_t d = 0;
+  d |= 1u << 4;                           // D format F32; A and B format E4M3 = 0
+  d |= (uint32_t)((N >> 3) & 0x3F) << 17;
+  d |= (uint32_t)((M >> 4) & 0x1F) << 24;
+  return d;
+}
 B200_HD uint32_t idesc_with_sf_ids(uint32_t base, uint32_t a_sf_id, uint32_t b_sf_id) {
   return base | ((b_sf_id & 3) << 4) | ((a_sf_id & 3) << 29);
 }
@@ -221,6 +230,12 @@ B200_D void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t id
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+B200_D void mma_f8f6f4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 B200_D void mma_commit(uint64_t* bar) {

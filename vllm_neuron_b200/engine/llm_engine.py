@@ -87,8 +87,13 @@ class LLMEngine:
             logger.info("sliding-window layers use their own KV group: %d blocks (full-attention layers: %d)",
                         n_swa, n_blocks)
         k = cfg.speculative_config.num_speculative_tokens if cfg.speculative_config else 0
+        # mixed prefill + decode steps need no lockstep step kinds (data parallelism), no
+        # speculation and no context-parallel attention
+        mixed = cfg.mixed_prefill_tokens if (cfg.data_parallel_size == 1 and k == 0
+                                             and cfg.decode_context_parallel_size == 1) else 0
         self.scheduler = Scheduler(self.kv, cfg.max_num_seqs, cfg.max_num_batched_tokens, cfg.max_model_len,
-                                   cfg.max_num_prefills_per_step, cfg.enable_chunked_prefill, k)
+                                   cfg.max_num_prefills_per_step, cfg.enable_chunked_prefill, k,
+                                   mixed_prefill_tokens=mixed)
         if self.worker.runner.encoder_cache is not None:
             self.scheduler.on_finish.append(self.worker.runner.encoder_cache.release)
         if self.worker.runner.debug_logits is not None:
@@ -336,8 +341,7 @@ class LLMEngine:
             if nxt is not None:
                 cur = runner.launch(nxt, prev)
                 self._count_async("lookahead")
-                for s in nxt.seqs:
-                    s.request.num_inflight += 1
+                self._mark_inflight(nxt, 1)
             outs = self._commit(prev)
             self._inflight = cur
             return outs
@@ -349,8 +353,7 @@ class LLMEngine:
         if runner.can_launch_async(so):
             self._inflight = runner.launch(so)
             self._count_async("launched")
-            for s in so.seqs:
-                s.request.num_inflight += 1
+            self._mark_inflight(so, 1)
             return failed
         self._count_async("sync_fallback")
         return failed + self._run(so)
@@ -363,10 +366,19 @@ class LLMEngine:
         self.async_stats[mode] += 1
         ASYNC_STEPS.labels(model_name=self.cfg.served_model_name or "model", mode=mode).inc()
 
+    @staticmethod
+    def _mark_inflight(so, sign: int) -> None:
+        """Launched (+1) or committed (-1): decode tokens count in num_inflight, prompt chunks
+        of mixed steps in num_inflight_prefill."""
+        for i, s in enumerate(so.seqs):
+            if so.kind == "mixed" and i >= so.num_decode:
+                s.request.num_inflight_prefill += sign * len(s.token_ids)
+            else:
+                s.request.num_inflight += sign
+
     def _commit(self, step) -> list[RequestOutput]:
         sampled = self.worker.runner.commit(step)
-        for s in step.so.seqs:
-            s.request.num_inflight -= 1
+        self._mark_inflight(step.so, -1)
         finished = self.scheduler.update_from_output(step.so, sampled, time.monotonic())
         fin = {r.request_id for r in finished}
         return [self._make_output(s.request, s.request.status.finished) for s in step.so.seqs

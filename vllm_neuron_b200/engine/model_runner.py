@@ -395,8 +395,9 @@ class ModelRunner:
             ids[t:t + k] = s.token_ids
             p = np.arange(s.start_pos, s.start_pos + k)
             delta = req.mrope_delta if req is not None else 0
-            pos[t:t + k] = p + delta if (delta and so.kind == "decode") else p
-            if req is not None and req.mrope_positions is not None and so.kind == "prefill":
+            dec_seq = so.kind == "decode" or (so.kind == "mixed" and i < so.num_decode)
+            pos[t:t + k] = p + delta if (delta and dec_seq) else p
+            if req is not None and req.mrope_positions is not None and not dec_seq:
                 has_mrope = True
             blocks = np.asarray(s.block_ids, dtype=np.int64)
             if swa:
@@ -486,7 +487,8 @@ class ModelRunner:
             slot_mapping=self.d_slot[:T], logits_indices=self.d_lidx[:n_sel], max_query_len=max_q,
             max_seq_len=max_s, workspace=self.workspace, num_splits=self.num_splits_for(B), extras=extras,
             cp_group=self.cp_group, block_tables_swa=self.d_bt_swa[:B] if swa else None,
-            slot_mapping_swa=self.d_slot_swa[:T] if swa else None)
+            slot_mapping_swa=self.d_slot_swa[:T] if swa else None,
+            num_decode_seqs=so.num_decode if so.kind == "mixed" else 0)
         if spec:
             extras["spec"] = True
         if extras_so is not None:
@@ -774,11 +776,19 @@ class ModelRunner:
 
     # ---------------------------------------------------------- async decode steps
     def can_launch_async(self, so: SchedulerOutput) -> bool:
-        return (so.kind == "decode" and bool(so.seqs) and self.capture is None and self.replacer is None
-                and self.debug_logits is None
-                and all(len(s.token_ids) == 1 and not s.spec_token_ids for s in so.seqs)
-                and not any(s.request is not None and (s.request.sampling_params.logprobs is not None
-                                                       or s.request.grammar is not None) for s in so.seqs))
+        """Plain decode steps and mixed steps (decodes + prompt chunks) without per-token host
+        work (logprobs, grammars, debug dumps, tensor capture / replacement)."""
+        if so.kind not in ("decode", "mixed") or not so.seqs:
+            return False
+        if self.capture is not None or self.replacer is not None or self.debug_logits is not None:
+            return False
+        if so.kind == "mixed" and self.state_caches is not None:
+            return False  # recurrent-state models keep their mixed steps synchronous
+        dec = so.seqs[:so.num_decode] if so.kind == "mixed" else so.seqs
+        if not all(len(s.token_ids) == 1 and not s.spec_token_ids for s in dec):
+            return False
+        return not any(s.request is not None and (s.request.sampling_params.logprobs is not None
+                                                  or s.request.grammar is not None) for s in so.seqs)
 
     def _span_start(self):
         if self.step_spans is None or self.device.type != "cuda":
@@ -809,20 +819,22 @@ class ModelRunner:
         self.step_count += 1
         span0 = self._span_start()
         n = len(so.seqs)
-        pad_to = get_bucket_for_count(n, self.decode_buckets) if self.use_graphs else n
+        graphed = self.use_graphs and so.kind == "decode"
+        pad_to = get_bucket_for_count(n, self.decode_buckets) if graphed else n
         NUM_SEQS_PADDING.labels(model_name=self.cfg.served_model_name or "model").observe(pad_to - n)
-        meta, T, n_sel, greedy = self._prepare(so, pad_to)
+        meta, T, n_sel, greedy = self._prepare(so, pad_to if so.kind == "decode" else None)
         if prev is not None:
             src = self.h_src.numpy()
             src[:pad_to] = -1
-            for i, s in enumerate(so.seqs):
+            # decode sequences come first, one token row each; prompt chunks keep their host tokens
+            for i, s in enumerate(so.seqs[:so.num_decode] if so.kind == "mixed" else so.seqs):
                 src[i] = prev.row_of.get(s.req_id, -1)
             self.d_src[:pad_to].copy_(self.h_src[:pad_to], non_blocking=True)
             idx = self.d_src[:pad_to]
             prev_ids = self.d_out[:pad_to].index_select(0, idx.clamp(min=0))
             self.d_ids[:pad_to] = torch.where(idx >= 0, prev_ids, self.d_ids[:pad_to])
         self._h2d_done = self._event()  # the staging buffers are free again after this point
-        if self.use_graphs:
+        if graphed:
             key = (pad_to, greedy)
             entry = self.graphs.get(key)
             if entry is None:

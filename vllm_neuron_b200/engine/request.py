@@ -51,6 +51,7 @@ class Request:
     mrope_delta: int = 0  # decode rope position = cache position + delta
     kv_transfer_params_out: dict | None = None  # set by a KV-producer engine when the request finishes
     num_inflight: int = 0  # decode steps launched whose token is not yet known (async scheduling)
+    num_inflight_prefill: int = 0  # prompt tokens of a launched, not yet committed step (async mixed steps)
     grammar: object = None  # structured-output matcher (xgrammar), fed every sampled token
     logprobs: list = field(default_factory=list)  # per output token {token id: logprob} (SamplingParams.logprobs)
     stop_checker: object = None  # stop strings: callable(request) -> True when one appeared

@@ -64,10 +64,12 @@ class ScheduledSeq:
 
 @dataclass
 class SchedulerOutput:
-    kind: str  # "prefill" | "decode" | "idle"
+    kind: str  # "prefill" | "decode" | "mixed" | "idle"
     seqs: list[ScheduledSeq]
     preempted: list[str] = field(default_factory=list)
     finished: list[str] = field(default_factory=list)
+    # "mixed": the first num_decode seqs are single-token decodes, the rest prefill chunks
+    num_decode: int = 0
 
     @property
     def num_tokens(self) -> int:
@@ -77,8 +79,12 @@ class SchedulerOutput:
 class Scheduler:
     def __init__(self, kv: KVCacheManager, max_num_seqs: int, max_num_batched_tokens: int, max_model_len: int,
                  max_num_prefills_per_step: int = 1, enable_chunked_prefill: bool = True,
-                 num_spec_tokens: int = 0):
+                 num_spec_tokens: int = 0, mixed_prefill_tokens: int = 0):
         self.kv = kv
+        # > 0: while requests are decoding, prompt work rides along in their steps, at most this
+        # many prompt tokens per step (a decode step streams every expert weight anyway, so a
+        # prompt chunk adds little); 0: prefill and decode run as separate steps
+        self.mixed_prefill_tokens = mixed_prefill_tokens
         self.max_num_seqs = max_num_seqs
         self.max_num_batched_tokens = max_num_batched_tokens
         self.max_model_len = max_model_len
@@ -173,7 +179,12 @@ class Scheduler:
     def schedule(self, kind: str | None = None) -> SchedulerOutput:
         """Next step.  ``kind`` ("prefill" | "decode") restricts the step type; data-parallel
         replicas use it to run the same kind of step in lockstep (a replica with nothing of
-        that kind gets an idle output and runs a padding batch)."""
+        that kind gets an idle output and runs a padding batch).  With ``mixed_prefill_tokens``
+        a step that has both decoding requests and prompt work is one "mixed" step."""
+        if kind is None and self.mixed_prefill_tokens > 0 and not self.num_spec_tokens:
+            decoders = [r for r in self.running if not self._is_prefill(r)]
+            if decoders and self.has_prefill_work():
+                return self._schedule_mixed(decoders)
         finished, self._finished_ids = self._finished_ids, []
         # 1) ongoing segmented prefills first
         pre = [r for r in self.running if self._is_prefill(r)] if kind != "decode" else []
@@ -237,9 +248,34 @@ class Scheduler:
         if kind == "prefill":
             return SchedulerOutput("idle", [], [], finished)
         # 3) decode step over every running request
+        seqs, preempted = self._decode_seqs(list(self.running))
+        if not seqs:
+            return SchedulerOutput("idle", [], preempted, finished)
+        return SchedulerOutput("decode", seqs, preempted, finished)
+
+    def _schedule_mixed(self, decoders: list[Request]) -> SchedulerOutput:
+        """Every decoding request (one token each; their KV slots are secured first, preempting
+        the newest if needed) followed by prompt chunks within ``mixed_prefill_tokens``."""
+        finished, self._finished_ids = self._finished_ids, []
+        dec, preempted = self._decode_seqs(decoders)
+        saved = self.max_num_batched_tokens
+        self.max_num_batched_tokens = self.mixed_prefill_tokens
+        try:
+            pre = self.schedule("prefill")
+        finally:
+            self.max_num_batched_tokens = saved
+        seqs = dec + (pre.seqs if pre.kind == "prefill" else [])
+        if not seqs:
+            return SchedulerOutput("idle", [], preempted, finished)
+        if not dec:
+            return SchedulerOutput("prefill", seqs, preempted, finished)
+        if len(seqs) == len(dec):
+            return SchedulerOutput("decode", seqs, preempted, finished)
+        return SchedulerOutput("mixed", seqs, preempted, finished, num_decode=len(dec))
+
+    def _decode_seqs(self, running: list[Request]) -> tuple[list[ScheduledSeq], list[str]]:
         seqs, preempted = [], []
         k = self.num_spec_tokens
-        running = list(self.running)
         i = 0
         while i < len(running):
             req = running[i]
@@ -260,32 +296,55 @@ class Scheduler:
             seqs.append(ScheduledSeq(req.request_id, toks, s, req.block_ids, True, spec_token_ids=spec,
                                      sampling_params=req.sampling_params, sample_seq=req.sample_seq, request=req,
                                      swa_block_ids=self._swa(req)))
-        if not seqs:
-            return SchedulerOutput("idle", [], preempted, finished)
-        return SchedulerOutput("decode", seqs, preempted, finished)
+        return seqs, preempted
 
     def schedule_lookahead(self) -> SchedulerOutput | None:
-        """Asynchronous scheduling: the next decode step while the previous one is still on
-        the GPU.  Every running request feeds the token that the in-flight step is sampling
-        (the runner takes it from device memory), at position num_computed + num_inflight.
-        Returns None when that is not possible (prefill work waiting, speculation, a request
-        at its token limit, no free KV block): the caller then drains the pipeline."""
-        if self.num_spec_tokens or self.waiting or not self.running:
+        """Asynchronous scheduling: the next step while the previous one is still on the GPU.
+        Every decoding request feeds the token that the in-flight step is sampling (the runner
+        takes it from device memory), at position num_computed + num_inflight.  With mixed
+        steps, a prompt whose chunk is in flight continues with its next chunk (its tokens are
+        known on the host).  Returns None when that is not possible (a prompt to admit, a
+        prompt whose last chunk is in flight, speculation, a request at its token limit, no
+        free KV block): the caller then drains the pipeline."""
+        if self.num_spec_tokens or not self.running:
             return None
-        seqs = []
+        mixed = self.mixed_prefill_tokens > 0
+        if self.waiting and (not mixed or self.can_admit()):
+            return None
+        dec, pre = [], []
+        budget = self.mixed_prefill_tokens
         for req in self.running:
-            if self._is_prefill(req) or req.num_inflight != 1:
+            if self._is_prefill(req):
+                start = req.num_computed_tokens + req.num_inflight_prefill
+                if not mixed or req.num_inflight or start >= req.num_prompt_tokens:
+                    return None  # no chunk in flight yet, or the last one is: decide after it lands
+                n = min(req.num_prompt_tokens - start, budget)
+                if n <= 0:
+                    continue
+                if not self.kv.allocate_slots(req, req.num_inflight_prefill + n):
+                    return None
+                budget -= n
+                pre.append(ScheduledSeq(req.request_id, req.prompt_token_ids[start:start + n], start,
+                                        req.block_ids, start + n >= req.num_tokens,
+                                        sampling_params=req.sampling_params, sample_seq=req.sample_seq,
+                                        mm_inputs=req.mm_inputs, request=req, swa_block_ids=self._swa(req)))
+                continue
+            if req.num_inflight != 1:
                 return None
             if len(req.output_token_ids) + 1 >= req.max_tokens:
                 return None  # the in-flight token ends this request: nothing to run ahead
             if not self.kv.allocate_slots(req, 2):  # in-flight token + the new one
                 return None
             s = req.num_computed_tokens + 1
-            seqs.append(ScheduledSeq(req.request_id, [0], s, req.block_ids, True,
-                                     sampling_params=req.sampling_params, sample_seq=req.sample_seq + 1,
-                                     request=req, swa_block_ids=self._swa(req)))
+            dec.append(ScheduledSeq(req.request_id, [0], s, req.block_ids, True,
+                                    sampling_params=req.sampling_params, sample_seq=req.sample_seq + 1,
+                                    request=req, swa_block_ids=self._swa(req)))
+        if not dec:
+            return None
         finished, self._finished_ids = self._finished_ids, []
-        return SchedulerOutput("decode", seqs, finished=finished)
+        if pre:
+            return SchedulerOutput("mixed", dec + pre, finished=finished, num_decode=len(dec))
+        return SchedulerOutput("decode", dec, finished=finished)
 
     def _swa(self, req: Request) -> list[int] | None:
         return req.swa_block_ids if self.kv.swa_pool is not None else None
@@ -344,7 +403,7 @@ class Scheduler:
             req = self.requests.get(s.req_id)
             if req is None:
                 continue
-            if out.kind == "prefill":
+            if out.kind in ("prefill", "mixed"):
                 req.num_computed_tokens += len(s.token_ids)
             if not s.sample:
                 self.kv.cache_full_blocks(req)

@@ -85,6 +85,8 @@ def random_init_(module: nn.Module, seed: int = 0, std: float = 0.02) -> None:
             p.data.fill_(1.0)
         elif name.endswith("bias"):
             p.data.zero_()
+        elif name.endswith("weight_scale") or name.endswith("input_scale"):  # FP8 dequantisation scales
+            p.data.fill_(1.0 if name.endswith("weight_scale") else 0.05)
         else:
             _fill_chunked(p, lambda n: torch.randn(n, generator=g, dtype=torch.float32) * std)
 
@@ -113,5 +115,9 @@ def random_init_device_(module: nn.Module, seed: int = 0, std: float = 0.02) -> 
             p.data.fill_(1.0)
         elif name.endswith("bias"):
             p.data.zero_()
+        elif name.endswith("weight_scale") or name.endswith("input_scale"):
+            p.data.fill_(1.0 if name.endswith("weight_scale") else 0.05)
+        elif p.dtype == torch.float8_e4m3fn:
+            p.data.copy_(torch.empty(p.shape, device=p.device).normal_(0.0, std, generator=g).to(p.dtype))
         else:
             p.data.normal_(0.0, std, generator=g)

@@ -86,23 +86,43 @@ def _param(shape, dtype, device) -> nn.Parameter:
 
 
 class Linear(nn.Module):
-    """A local (already sharded) linear layer, bf16 or static FP8."""
+    """A local (already sharded) linear layer, bf16 or static FP8.  FP8: e4m3 weight, an fp32
+    weight scale per output feature (a per-tensor checkpoint scale is broadcast over the rows
+    of its segment, so the q / k / v or gate / up parts of a fused weight keep their own
+    scales) and one activation scale (the largest of the fused parts', which quantise the same
+    input)."""
 
     def __init__(self, out_f: int, in_f: int, bias: bool, dtype, device, fp8: bool = False):
         super().__init__()
         self.fp8 = fp8
+        self.dtype = dtype
         if fp8:
             self.weight = _param((out_f, in_f), torch.float8_e4m3fn, device)
-            self.weight_scale = _param((1,), torch.float32, device)
-            self.input_scale = _param((1,), torch.float32, device)
+            self.weight_scale = nn.Parameter(torch.ones(out_f, dtype=torch.float32, device=device), requires_grad=False)
+            self.input_scale = nn.Parameter(torch.zeros(1, dtype=torch.float32, device=device), requires_grad=False)
+            self.register_buffer("alpha", torch.ones(out_f, dtype=torch.float32, device=device), persistent=False)
         else:
             self.weight = _param((out_f, in_f), dtype, device)
         self.bias = _param((out_f,), dtype, device) if bias else None
 
-    def forward(self, x: torch.Tensor, with_bias: bool = True) -> torch.Tensor:
+    def load_scale(self, kind: str, full: torch.Tensor, rows: slice | None = None) -> None:
+        """A checkpoint scale for the output rows ``rows`` (all rows when None)."""
+        v = full.float().reshape(-1).to(self.weight_scale.device)
+        if kind == "input_scale":
+            self.input_scale.data.copy_(torch.maximum(self.input_scale.data, v[:1]))
+            return
+        tgt = self.weight_scale.data if rows is None else self.weight_scale.data[rows]
+        tgt.copy_(v[0].expand_as(tgt) if v.numel() == 1 else v[:tgt.numel()])
+
+    def process_weights_after_loading(self) -> None:
+        if self.fp8:
+            self.alpha.copy_(self.input_scale.float() * self.weight_scale.float())
+
+    def forward(self, x: torch.Tensor, with_bias: bool = True, x_q: torch.Tensor | None = None) -> torch.Tensor:
         b = self.bias if with_bias else None
         if self.fp8:
-            return ops.linear_fp8(x, self.weight, self.weight_scale, self.input_scale, b)
+            return ops.linear_fp8(x, self.weight, self.weight_scale, self.input_scale, b, x_q=x_q, alpha=self.alpha,
+                                  out_dtype=self.dtype)
         return ops.linear(x, self.weight, b)
 
 
@@ -129,7 +149,13 @@ class DenseAttention(nn.Module):
     def load_qkv(self, which: str, kind: str, full: torch.Tensor) -> None:
         d, r = self.d, self.tp.rank_in_group
         if kind in ("weight_scale", "input_scale"):
-            getattr(self.qkv, kind).data.copy_(full.float().reshape(-1)[:1])
+            nq, nkv = self.nq * d, self.nkv * d
+            seg = {"q": slice(0, nq), "k": slice(nq, nq + nkv), "v": slice(nq + nkv, nq + 2 * nkv)}[which]
+            if kind == "weight_scale" and full.numel() > 1:  # per-channel: this rank's rows
+                rows = slice(r * nq, (r + 1) * nq) if which == "q" else slice(self.kv_start * d,
+                                                                              (self.kv_start + self.nkv) * d)
+                full = full.reshape(-1)[rows]
+            self.qkv.load_scale(kind, full, seg)
             return
         if which == "q":
             rows = slice(r * self.nq * d, (r + 1) * self.nq * d)
@@ -141,8 +167,8 @@ class DenseAttention(nn.Module):
         tgt = self.qkv.weight if kind == "weight" else self.qkv.bias
         tgt.data[dst].copy_(full[rows].to(tgt.dtype))
 
-    def forward(self, positions, x, meta, kv, cos_sin) -> torch.Tensor:
-        qkv = self.qkv(x)
+    def forward(self, positions, x, meta, kv, cos_sin, x_q=None) -> torch.Tensor:
+        qkv = self.qkv(x, x_q=x_q)
         k_cache, v_cache = kv
         q = ops.rope_and_cache(qkv, positions, cos_sin, k_cache, v_cache, meta.slot_mapping, self.nq, self.nkv,
                                self.d, self.k_scale, self.v_scale, self.q_norm, self.k_norm, self.eps)
@@ -169,8 +195,14 @@ class DenseMLP(nn.Module):
 
     def load(self, which: str, kind: str, full: torch.Tensor) -> None:
         if kind in ("weight_scale", "input_scale"):
-            lin = self.down if which == "down" else self.gate_up
-            getattr(lin, kind).data.copy_(full.float().reshape(-1)[:1])
+            if which == "down":
+                self.down.load_scale(kind, full)
+                return
+            seg = slice(0, self.I_local) if which == "gate" else slice(self.I_local, 2 * self.I_local)
+            if kind == "weight_scale" and full.numel() > 1:
+                s0, e0 = shard_range(full.numel(), self.tp.rank_in_group, self.tp.world_size)
+                full = full.reshape(-1)[s0:e0]
+            self.gate_up.load_scale(kind, full, seg)
             return
         r, w = self.tp.rank_in_group, self.tp.world_size
         if which == "down":
@@ -185,11 +217,11 @@ class DenseMLP(nn.Module):
         tgt = self.gate_up.weight if kind == "weight" else self.gate_up.bias
         tgt.data[off:off + self.I_local].copy_(full[s:e].to(tgt.dtype))
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, x_q: torch.Tensor | None = None) -> torch.Tensor:
         if self.dp_group is not None:
             xa = self.dp_group.all_gather(x, dim=0)
             return self.dp_group.reduce_scatter(self.down(ops.silu_and_mul(self.gate_up(xa)), with_bias=False), dim=0)
-        return self.down(ops.silu_and_mul(self.gate_up(x)), with_bias=False)  # partial sum
+        return self.down(ops.silu_and_mul(self.gate_up(x, x_q=x_q)), with_bias=False)  # partial sum
 
 
 class DenseDecoderLayer(nn.Module):
@@ -203,9 +235,29 @@ class DenseDecoderLayer(nn.Module):
         mlp_g, mlp_dp = ps.component("mlp")
         self.mlp = DenseMLP(cfg, mlp_g, dtype, device, dp_group=mlp_dp)
 
+    def _fp8_fused(self) -> bool:
+        """Static-FP8 layer on one rank: the norms write e4m3 rows for the FP8 GEMMs directly
+        (fused RMSNorm + quantisation) instead of bf16 rows that the GEMM call re-reads."""
+        qkv, gu = self.self_attn.qkv, self.mlp.gate_up
+        return qkv.fp8 and gu.fp8 and self.tp.world_size == 1 and self.mlp.dp_group is None and \
+            not getattr(self.tp, "sp_active", False)
+
     def forward(self, positions, h, residual, meta, kv, cos_sin, in_bias=None):
         """``h``: the embedding (layer 0) or the previous layer's MLP partial sum, whose
         bias ``in_bias`` is added once after the reduction."""
+        if self._fp8_fused():
+            at, mlp = self.self_attn, self.mlp
+            if in_bias is not None:
+                h = h + in_bias
+            x_q, residual = ops.rms_norm_fp8(h, self.input_layernorm.weight, self.eps, at.qkv.input_scale, residual)
+            if residual is None:
+                residual = h
+            a = at(positions, None, meta, kv, cos_sin, x_q=x_q)
+            if at.o_proj.bias is not None:
+                a = a + at.o_proj.bias
+            x_q, residual = ops.rms_norm_fp8(a, self.post_attention_layernorm.weight, self.eps,
+                                             mlp.gate_up.input_scale, residual)
+            return mlp(None, x_q=x_q), residual
         if residual is None:
             residual = h
             x = self.input_layernorm(h)
@@ -309,8 +361,8 @@ class LlamaForCausalLM(nn.Module):
                 at.o_proj.weight.data.copy_(t[:, s:e].to(at.o_proj.weight.dtype))
             elif p[2] == "bias":
                 at.o_proj.bias.data.copy_(t.to(at.o_proj.bias.dtype))
-            else:
-                getattr(at.o_proj, p[2]).data.copy_(t.float().reshape(-1)[:1])
+            elif p[2] in ("weight_scale", "input_scale"):
+                at.o_proj.load_scale(p[2], t)
         elif p[0] == "self_attn" and p[1] in ("q_norm", "k_norm"):
             getattr(at, p[1]).data.copy_(t.float())
         elif p[0] == "mlp" and p[1] in ("gate_proj", "up_proj", "down_proj"):

@@ -104,19 +104,66 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None,
 
 
 def linear_fp8(x: torch.Tensor, w_fp8: torch.Tensor, w_scale: torch.Tensor, in_scale: torch.Tensor | None,
-               b: torch.Tensor | None = None) -> torch.Tensor:
-    """Static per-tensor FP8 linear (ModelOpt checkpoints, ``model/llama3/quantization.py:176``):
-    y = (q(x / s_in) @ W_fp8^T) * s_in * s_w, q = e4m3 with saturation.  Dynamic per-tensor
-    activation scale when ``in_scale`` is None."""
+               b: torch.Tensor | None = None, x_q: torch.Tensor | None = None,
+               alpha: torch.Tensor | None = None, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """Static FP8 linear (ModelOpt checkpoints, ``model/llama3/quantization.py:176``):
+    y = (q(x / s_in) @ W_fp8^T) * s_in * s_w, q = e4m3 with saturation; ``w_scale`` per
+    tensor ([1]) or per output feature ([N], e.g. the q / k / v segments of a fused QKV).
+    Dynamic per-tensor activation scale when ``in_scale`` is None.  On a GPU: the e4m3
+    quantisation kernel (``csrc/fp8.cu``, which also writes alpha = s_in * s_w on the device)
+    and the tcgen05 kind::f8f6f4 GEMM of ``csrc/gemm.cu``, which scales its fp32 accumulator
+    by alpha.  ``x_q``: activations already quantised with ``in_scale`` (the fused RMSNorm +
+    quantisation); ``alpha``: s_in * s_w precomputed for a static ``in_scale``."""
+    K, N = w_fp8.shape[1], w_fp8.shape[0]
+    ws_n = w_scale.numel()
+    if (use_kernel(w_fp8) and w_fp8.dtype == torch.float8_e4m3fn and w_fp8.is_contiguous() and K % 16 == 0
+            and N % 8 == 0 and ws_n in (1, N) and (x_q is not None or x.dtype == torch.bfloat16)):
+        lead = (x_q if x_q is not None else x).shape[:-1]
+        if x_q is None:
+            x2 = x.reshape(-1, K)
+            if x2.stride(1) != 1 or x2.stride(0) % 16 or x2.data_ptr() % 16:
+                x2 = x2.contiguous()
+            xq = torch.empty(x2.shape, dtype=torch.float8_e4m3fn, device=x.device)
+            if in_scale is not None and alpha is not None:
+                _k().fp8_quant(xq, x2, in_scale.float().reshape(1), None, None, None)
+            else:
+                alpha = torch.empty(ws_n, dtype=torch.float32, device=x.device)
+                amax = None if in_scale is not None else torch.empty(1, dtype=torch.int32, device=x.device)
+                _k().fp8_quant(xq, x2, in_scale.float().reshape(1) if in_scale is not None else None, amax,
+                               w_scale.float().reshape(-1), alpha)
+        else:
+            xq = x_q.reshape(-1, K)
+            if alpha is None:
+                alpha = in_scale.float().reshape(1) * w_scale.float().reshape(-1)
+        y = torch.empty(xq.shape[0], N, dtype=torch.bfloat16, device=w_fp8.device)
+        wsp, cnt = _gemm_workspace(w_fp8.device)
+        bb = b.to(torch.bfloat16).contiguous() if b is not None else None
+        _k().gemm_fp8(y, xq, w_fp8, bb, alpha.reshape(-1), wsp, cnt, _GEMM_MAX_SPLITS, device_status(w_fp8.device))
+        return y.reshape(*lead, N)
+    if x_q is not None:
+        x = (x_q.float() * in_scale.float()).to(out_dtype or torch.bfloat16)
     xs = in_scale if in_scale is not None else (x.abs().amax().float().clamp_min(1e-12) / 448.0).reshape(1)
-    xq = (x.float() / xs).clamp(-448, 448).to(torch.float8_e4m3fn)
-    if x.is_cuda and hasattr(torch, "_scaled_mm"):
-        y = torch._scaled_mm(xq, w_fp8.t(), scale_a=xs.float().reshape(()), scale_b=w_scale.float().reshape(()),
-                             out_dtype=torch.bfloat16)
-    else:
-        y = (xq.float() @ w_fp8.float().t()) * (xs.float() * w_scale.float())
+    xq = (x.float() / xs.float()).clamp(-448, 448).to(torch.float8_e4m3fn)
+    y = (xq.float() @ w_fp8.float().t()) * (xs.float() * w_scale.float().reshape(-1))
     y = y.to(x.dtype)
     return y + b if b is not None else y
+
+
+def rms_norm_fp8(x: torch.Tensor, w: torch.Tensor, eps: float, in_scale: torch.Tensor,
+                 residual: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """The reference's rmsnorm_quant: (residual + x), its RMSNorm * w quantised to e4m3 with
+    the static ``in_scale``.  Returns (e4m3 rows for ``linear_fp8(x_q=...)``, the new residual;
+    on a GPU the residual buffer is updated in place)."""
+    if use_kernel(x) and x.dtype == torch.bfloat16 and x.shape[-1] % 8 == 0 and x.shape[-1] <= 8192:
+        x2 = x.reshape(-1, x.shape[-1]).contiguous()
+        q = torch.empty(x2.shape, dtype=torch.float8_e4m3fn, device=x.device)
+        _k().rms_norm_fp8(q, x2, residual, w.float().contiguous(), eps, in_scale.float().reshape(1))
+        return q.reshape(x.shape), residual
+    if residual is not None:
+        residual = (x.float() + residual.float()).to(residual.dtype)
+        x = residual
+    y = (x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(x.dtype)
+    return (y.float() / in_scale.float()).clamp(-448, 448).to(torch.float8_e4m3fn), residual
 
 
 def silu_and_mul(gu: torch.Tensor) -> torch.Tensor:
@@ -240,6 +287,15 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, met
         if meta.is_decode:
             _k().paged_attention_decode(out, q, k_cache, v_cache, meta.block_tables, meta.seq_lens, sinks, win,
                                         scale, k_scale, v_scale, meta.workspace, meta.num_splits)
+        elif 0 < meta.num_decode_seqs < meta.num_seqs:
+            # mixed step: the decode kernel for the single-token sequences (rows 0 .. D-1), the
+            # prefill kernel for the prompt chunks (their query-start offsets index q directly)
+            D = meta.num_decode_seqs
+            _k().paged_attention_decode(out[:D], q[:D], k_cache, v_cache, meta.block_tables[:D], meta.seq_lens[:D],
+                                        sinks, win, scale, k_scale, v_scale, meta.workspace, meta.num_splits)
+            _k().paged_attention_prefill(out, q, k_cache, v_cache, meta.block_tables[D:], meta.seq_lens[D:],
+                                         meta.query_start_loc[D:], sinks, win, scale, k_scale, v_scale,
+                                         meta.max_query_len)
         else:
             _k().paged_attention_prefill(out, q, k_cache, v_cache, meta.block_tables, meta.seq_lens,
                                          meta.query_start_loc, sinks, win, scale, k_scale, v_scale,

@@ -42,6 +42,9 @@ class AttentionMetadata:
     # layers share the full-attention tables
     block_tables_swa: torch.Tensor | None = None
     slot_mapping_swa: torch.Tensor | None = None
+    # mixed steps: the first num_decode_seqs sequences are single-token decodes (their query
+    # rows are rows 0 .. num_decode_seqs - 1), the rest prompt chunks
+    num_decode_seqs: int = 0
 
     def for_layer(self, window: int | None) -> "AttentionMetadata":
         """The metadata a layer reads: the sliding-window group's tables for a windowed
