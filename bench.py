@@ -215,6 +215,8 @@ def main() -> None:
     ap.add_argument("--concurrency", type=int, default=64)
     ap.add_argument("--prompt-len", type=int, default=2048)
     ap.add_argument("--output-len", type=int, default=512)
+    ap.add_argument("--all2all", default="allgather_reducescatter",
+                    help="EP token exchange at N > 1 (EngineConfig.all2all_backend)")
     ap.add_argument("--mixed-prefill-tokens", type=int, default=0,
                     help="prompt tokens per decode step (mixed steps); 0: separate prefill steps")
     ap.add_argument("--profile-dir", default=None,
@@ -250,7 +252,7 @@ def main() -> None:
     llm = LLM(hf_config=hf, load_format="dummy", dtype="bfloat16", tensor_parallel_size=N,
               max_model_len=max_len, max_num_seqs=C, max_num_batched_tokens=4096, block_size=32,
               max_num_prefills_per_step=2, spmd=N > 1, seed=0, async_scheduling=True,
-              mixed_prefill_tokens=args.mixed_prefill_tokens,
+              mixed_prefill_tokens=args.mixed_prefill_tokens, all2all_backend=args.all2all,
               additional_config={"neuron_config": {"ep_degree": N, "quantization": "mxfp4",
                                                    "num_seqs_buckets": [C]}})
     eng = llm.engine
@@ -355,6 +357,7 @@ def main() -> None:
             "data": "synthetic random prompt tokens; random-init weights (GPT-OSS-120B architecture)",
             "config": {"model": args.model, "global_batch": C, "seq_len": P, "output_len": O,
                        "parallelism": f"tp{N}-ep{N}" if N > 1 else "single",
+                       "ep_exchange": args.all2all if N > 1 else None,
                        "phase": f"steady-state closed loop at concurrency {C}: each step is one serving period "
                                 f"(a finished request replaced by a new {P}-token prompt, its prefill, and the "
                                 f"decode steps until the next completion)",
