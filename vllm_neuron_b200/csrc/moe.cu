@@ -256,7 +256,11 @@ struct GemmSmem {
   static constexpr int kOffSfa = kOffB + STAGES * kB;
   static constexpr int kOffSfb = kOffSfa + STAGES * kSfAtom;
   static constexpr int kOffBar = kOffSfb + STAGES * kSfAtom;
-  static constexpr int kBytes = kOffBar + (2 * STAGES + 4) * 8 + 16;
+  // epilogue staging: per epilogue warp one 16-token x (its 32 rows) bf16 block, so the
+  // output leaves in 16-byte row segments instead of 2-byte scattered stores
+  static constexpr int kOffStage = ((kOffBar + (2 * STAGES + 4) * 8 + 16 + 127) / 128) * 128;
+  static constexpr int kStageBytes = 4 * 1024;
+  static constexpr int kBytes = kOffStage + kStageBytes;
   static constexpr int kAlloc = kBytes + 1024;  // slack to align the base to 1024
   static constexpr int kTmemNeed = 2 * NT + 8;  // two accumulators + SFA + SFB columns
   static constexpr uint32_t kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64 : kTmemNeed <= 128 ? 128
@@ -426,32 +430,58 @@ __global__ void __launch_bounds__(256, (NT <= 32 ? 2 : 1)) moe_gemm_kernel(const
       const int gm = wi.mt * 128 + m;
       const float b = gm < M ? bias[(size_t)wi.e * M + gm] : 0.f;
       const uint32_t lane_addr = tmem + acc * NT + ((uint32_t)(ew * 32) << 16);
+      uint8_t* stg = smem + L::kOffStage + ew * 1024;  // this warp's staging block
       for (int c = 0; c < NT; c += 16) {
         if (c >= nvalid) break;
         uint32_t r[16];
         tc::tmem_ld_32x32b_x16(lane_addr + c, r);
         tc::tmem_ld_wait();
+        __syncwarp();  // the previous chunk's staged rows were copied out
+        if constexpr (EPI == kEpiSwiglu) {
+          // rows 2i (gate) and 2i+1 (up) sit in lanes m and m^1: the pair splits the 16 tokens,
+          // the even lane taking the even ones and the odd lane the odd ones, and swaps the
+          // other half of its values with its partner (every lane computes)
+          const int odd = m & 1;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int j = c + i;
-          const float v = __uint_as_float(r[i]) + b;
-          if constexpr (EPI == kEpiSwiglu) {
-            const float other = __shfl_xor_sync(0xffffffffu, v, 1);
-            if (!(m & 1) && j < nvalid && gm < M) {
-              float g = v, u = other, a;
-              if (limit > 0.f) {
-                g = fminf(g, limit);
-                u = fminf(fmaxf(u, -limit), limit);
-                a = g / (1.f + __expf(-alpha * g)) * (u + 1.f);
-              } else {
-                a = g / (1.f + __expf(-g)) * u;
-              }
-              out[(size_t)(wi.row0 + j) * ld_out + (gm >> 1)] = __float2bfloat16(a);
+          for (int i2 = 0; i2 < 8; ++i2) {
+            const float keep = __uint_as_float(r[2 * i2 + odd]) + b;
+            const float send = __uint_as_float(r[2 * i2 + (odd ^ 1)]) + b;
+            const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
+            float g = odd ? recv : keep, u = odd ? keep : recv, a;
+            if (limit > 0.f) {
+              g = fminf(g, limit);
+              u = fminf(fmaxf(u, -limit), limit);
+              a = __fdividef(g, 1.f + __expf(-alpha * g)) * (u + 1.f);
+            } else {
+              a = __fdividef(g, 1.f + __expf(-g)) * u;
             }
-          } else {
-            if (j < nvalid && gm < M) {
+            // staged [16 tokens][16 features of this warp] bf16, 32 bytes per token
+            *reinterpret_cast<__nv_bfloat16*>(stg + (2 * i2 + odd) * 32 + (lane >> 1) * 2) = __float2bfloat16(a);
+          }
+          __syncwarp();
+          const int row = lane >> 1, j = c + row;
+          const int f = wi.mt * 64 + ew * 16 + (lane & 1) * 8;  // output feature of this 16-byte segment
+          if (j < nvalid && f < (M >> 1))
+            *reinterpret_cast<uint4*>(out + (size_t)(wi.row0 + j) * ld_out + f) =
+                *reinterpret_cast<const uint4*>(stg + row * 32 + (lane & 1) * 16);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int j = c + i;
+            const float v = __uint_as_float(r[i]) + b;
+            const float wt = j < nvalid ? topk_w[ws.row_route[wi.row0 + j]] : 0.f;
+            // staged [16 routes][32 features of this warp] bf16, 64 bytes per route
+            *reinterpret_cast<__nv_bfloat16*>(stg + i * 64 + lane * 2) = __float2bfloat16(v * wt);
+          }
+          __syncwarp();
+#pragma unroll
+          for (int k2 = 0; k2 < 2; ++k2) {
+            const int q = lane + 32 * k2, row = q >> 2, ch = q & 3, j = c + row;
+            const int f = wi.mt * 128 + ew * 32 + ch * 8;
+            if (j < nvalid && f < M) {
               const int route = ws.row_route[wi.row0 + j];
-              out[(size_t)route * ld_out + gm] = __float2bfloat16(v * topk_w[route]);
+              *reinterpret_cast<uint4*>(out + (size_t)route * ld_out + f) =
+                  *reinterpret_cast<const uint4*>(stg + row * 64 + ch * 16);
             }
           }
         }
@@ -573,6 +603,8 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const uint8
                        int ld_out, float alpha, float limit, int max_tiles, int E_local, int R_max, int atoms_max,
                        int* status, cudaStream_t s) {
   using L = GemmSmem<NT, STAGES>;
+  // the epilogue writes 16-byte segments of 8 features
+  if (M % 16 || ld_out % 8 || (reinterpret_cast<uintptr_t>(out) & 15)) return kBadShape;
   auto kern = moe_gemm_kernel<NT, STAGES, FMT, EPI>;
   static bool attr = false;
   if (!attr) {
