@@ -228,7 +228,8 @@ def _moe_reference(x, ids, wts, w13f, b13, w2f, b2, off, alpha, limit, emulate_f
                                                         (64, 32, 2880, 2880, 4, 0, 32, 0),
                                                         (200, 32, 2880, 2880, 4, 0, 32, 1),
                                                         (300, 16, 2880, 2880, 4, 16, 128, 0),
-                                                        (1200, 8, 2880, 2880, 4, 0, 8, 1)])
+                                                        (1200, 8, 2880, 2880, 4, 0, 8, 1),
+                                                        (4200, 8, 512, 512, 4, 0, 8, 1)])
 def test_moe_mxfp4(T, E, H, I, k, off, E_total, skew):
     """skew=1 concentrates the routing so single experts get several N tiles."""
     from vllm_neuron_b200.ops.mx_layout import scales_to_atoms, tile_values
