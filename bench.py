@@ -145,6 +145,53 @@ def _count_our_kernels(fn) -> tuple[int, int, str]:
     return ours, total, table
 
 
+def _collective_check(eng, H: int, T: int = 64) -> dict:
+    """At N > 1, before timing: the fused layer-boundary collectives on the benchmark's shapes
+    against NCCL + the plain kernels (same inputs on every rank), as max |difference| of the
+    normalised output and of the new residual.  Every rank runs the same calls."""
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    from vllm_neuron_b200 import ops
+
+    tp = eng.worker.ps.tp
+    dev = eng.worker.device
+    g = torch.Generator(device=dev).manual_seed(100 + dist.get_rank())
+    res = {}
+    x = torch.randn(T, H, device=dev, generator=g).bfloat16()
+    r0 = torch.randn(T, H, device=dev, generator=torch.Generator(device=dev).manual_seed(7)).bfloat16()
+    w = torch.ones(H, device=dev)
+    ref_sum = x.float().clone()
+    dist.all_reduce(ref_sum, group=tp.device_group)
+    want_out, want_res = ops.fused_add_rms_norm(ref_sum.bfloat16(), r0.clone(), w, 1e-5)
+    if tp.communicator is not None and tp.communicator.can_all_reduce(x):
+        out, rr = tp.communicator.all_reduce_add_rmsnorm(x, r0.clone(), w, 1e-5)
+        res["fused_allreduce_rmsnorm_max_err"] = max((out.float() - want_out.float()).abs().max().item(),
+                                                     (rr.float() - want_res.float()).abs().max().item())
+    if tp.reducer is not None:
+        K = 4096 // tp.world_size
+        a = torch.randn(T, K, device=dev, generator=g).bfloat16()
+        wt = (torch.randn(H, K, device=dev, generator=torch.Generator(device=dev).manual_seed(9)) * 0.02).bfloat16()
+        y = F.linear(a, wt).float()
+        dist.all_reduce(y, group=tp.device_group)
+        want_out, want_res = ops.fused_add_rms_norm(y.bfloat16(), r0.clone(), w, 1e-5)
+        out, rr = tp.reducer.linear_add_rmsnorm(a, wt, r0.clone(), w, 1e-5, None)
+        res["nvls_gemm_allreduce_rmsnorm_max_err"] = max((out.float() - want_out.float()).abs().max().item(),
+                                                         (rr.float() - want_res.float()).abs().max().item())
+    torch.cuda.synchronize()
+    errs = torch.tensor([res.get(k, 0.0) for k in ("fused_allreduce_rmsnorm_max_err",
+                                                  "nvls_gemm_allreduce_rmsnorm_max_err")], device=dev)
+    dist.all_reduce(errs, op=dist.ReduceOp.MAX)
+    out = {}
+    if "fused_allreduce_rmsnorm_max_err" in res:
+        out["fused_allreduce_rmsnorm_max_err"] = round(errs[0].item(), 5)
+    if "nvls_gemm_allreduce_rmsnorm_max_err" in res:
+        out["nvls_gemm_allreduce_rmsnorm_max_err"] = round(errs[1].item(), 5)
+    out["reference"] = "NCCL all-reduce + fused_add_rms_norm kernel, [64, hidden] bf16, max over ranks"
+    return out
+
+
 class ClosedLoop:
     """Keeps ``C`` requests in flight through the public engine API: every finished request
     is replaced by a new prompt at once.  Records arrival / token timestamps per request."""
@@ -265,6 +312,7 @@ def main() -> None:
             dist.barrier()
         torch.cuda.synchronize()
 
+    coll_check = _collective_check(eng, hf["hidden_size"]) if N > 1 else None
     loop = ClosedLoop(eng, hf["vocab_size"], C, P, O)
     # ---- fill: C prompts prefilled back to back (the burst at the start of a serving run) ----
     loop.fill()
@@ -358,6 +406,7 @@ def main() -> None:
             "config": {"model": args.model, "global_batch": C, "seq_len": P, "output_len": O,
                        "parallelism": f"tp{N}-ep{N}" if N > 1 else "single",
                        "ep_exchange": args.all2all if N > 1 else None,
+                       "collective_check": coll_check,
                        "phase": f"steady-state closed loop at concurrency {C}: each step is one serving period "
                                 f"(a finished request replaced by a new {P}-token prompt, its prefill, and the "
                                 f"decode steps until the next completion)",

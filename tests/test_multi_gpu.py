@@ -70,6 +70,20 @@ def _worker(rank, world, port, q):
             s1 = sum(r + 1 + rep for r in range(world))
             errs.append(("graph", max((y1.float() - s1).abs().max().item(), (y2.float() - s1 * world).abs().max().item())))
         torch.cuda.synchronize()
+        # deterministic replay: the same inputs twice give bit-identical results (a race in the
+        # flag / slot protocol would show as a difference)
+        torch.manual_seed(5 + rank)
+        xr = torch.randn(64, 2880, device=dev).bfloat16()
+        torch.manual_seed(6)
+        rr = torch.randn(64, 2880, device=dev).bfloat16()
+        wr = torch.rand(2880, device=dev) + 0.5
+        runs = []
+        for _ in range(2):
+            o, r_ = g.communicator.all_reduce_add_rmsnorm(xr, rr.clone(), wr, 1e-5)
+            runs.append((o.clone(), r_.clone()))
+        errs.append(("replay", float(not (torch.equal(runs[0][0], runs[1][0]) and torch.equal(runs[0][1], runs[1][1])))))
+        # guard bytes after every receive area are untouched
+        errs.append(("canary", float(not g.communicator.check_canaries())))
         st_code = int(ops.device_status(dev)[0].item())
         del graph
         ps.destroy_parallel_state()

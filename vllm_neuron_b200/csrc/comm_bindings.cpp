@@ -38,6 +38,20 @@ int64_t comm_alloc(int64_t slot_bytes) {
 
 void comm_free(int64_t p) { b200_comm_free(reinterpret_cast<void*>(p)); }
 
+// Guard ("canary") bytes of device regions: fill a byte range with a pattern, read it back.
+void device_fill(int64_t p, int64_t nbytes, int64_t value) {
+  const cudaError_t e = cudaMemset(reinterpret_cast<void*>(p), (int)value, (size_t)nbytes);
+  TORCH_CHECK(e == cudaSuccess, "device_fill: ", cudaGetErrorString(e));
+}
+
+Tensor device_read(int64_t p, int64_t nbytes) {
+  Tensor out = at::empty({nbytes}, at::TensorOptions().dtype(at::kByte));
+  const cudaError_t e = cudaMemcpy(out.data_ptr(), reinterpret_cast<const void*>(p), (size_t)nbytes,
+                                   cudaMemcpyDeviceToHost);
+  TORCH_CHECK(e == cudaSuccess, "device_read: ", cudaGetErrorString(e));
+  return out;
+}
+
 Tensor ipc_get_handle(int64_t p) {
   Tensor h = at::empty({64}, at::TensorOptions().dtype(at::kByte));
   const int rc = b200_ipc_get_handle(reinterpret_cast<void*>(p), h.data_ptr());
@@ -168,6 +182,8 @@ void ep_combine(at::IntArrayRef bases, int64_t rank, int64_t slot_bytes, int64_t
 void register_comm_ops(torch::Library& m) {
   m.def("comm_alloc(int slot_bytes) -> int");
   m.def("comm_free(int ptr) -> ()");
+  m.def("device_fill(int ptr, int nbytes, int value) -> ()");
+  m.def("device_read(int ptr, int nbytes) -> Tensor");
   m.def("ipc_get_handle(int ptr) -> Tensor");
   m.def("ipc_open_handle(Tensor handle) -> int");
   m.def("ipc_close(int ptr) -> ()");
@@ -200,6 +216,8 @@ void register_comm_impls(torch::Library& m) {
 void register_comm_cpu_impls(torch::Library& m) {
   m.impl("comm_alloc", &comm_alloc);
   m.impl("comm_free", &comm_free);
+  m.impl("device_fill", &device_fill);
+  m.impl("device_read", &device_read);
   m.impl("ipc_get_handle", &ipc_get_handle);
   m.impl("ipc_open_handle", &ipc_open_handle);
   m.impl("ipc_close", &ipc_close);

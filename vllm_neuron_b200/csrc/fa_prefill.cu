@@ -59,7 +59,7 @@ constexpr int kOffV = kOffK + kStages * kTileBytes;
 constexpr int kOffP = kOffV + kStages * kTileBytes;  // kQT x [128 q][128 keys]: two 64-key atoms each
 constexpr int kPBuf = kBQ * kBK * 2;
 constexpr int kOffBar = kOffP + kQT * kPBuf;
-constexpr int kNumBars = 2 * kStages + 2 + 4 * kQT;
+constexpr int kNumBars = 2 * kStages + 2 + 6 * kQT;
 constexpr int kSmem = kOffBar + kNumBars * 8 + 16 + 1024;
 static_assert(kSmem <= 232448, "shared memory");
 constexpr uint32_t kTmemCols = 512;  // S_A, S_B: 128 columns each; O_A, O_B: 64 each
@@ -88,6 +88,29 @@ B200_D float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// three-input maximum (one instruction)
+B200_D float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// (r0, r1) = (x0, x1) * s + (o, o) on the packed f32x2 pipe (one instruction for two lanes' worth)
+B200_D void ffma2(float& r0, float& r1, float x0, float x1, float s, float o) {
+  asm("{\n .reg .b64 a, b, c;\n mov.b64 a, {%2, %3};\n mov.b64 b, {%4, %4};\n mov.b64 c, {%5, %5};\n"
+      " fma.rn.f32x2 a, a, b, c;\n mov.b64 {%0, %1}, a;\n}"
+      : "=f"(r0), "=f"(r1)
+      : "f"(x0), "f"(x1), "f"(s), "f"(o));
+}
+
+// (a0, a1) += (b0, b1) on the packed f32x2 pipe
+B200_D void fadd2(float& a0, float& a1, float b0, float b1) {
+  asm("{\n .reg .b64 a, b;\n mov.b64 a, {%0, %1};\n mov.b64 b, {%2, %3};\n add.rn.f32x2 a, a, b;\n"
+      " mov.b64 {%0, %1}, a;\n}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(b0), "f"(b1));
 }
 
 B200_D void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -137,9 +160,11 @@ __global__ void __launch_bounds__(kThreads, 1) fa_prefill_kernel(const __grid_co
   uint64_t* kv_empty = bars + kStages;     // [kStages] every MMA reading the stage is done
   uint64_t* q_full = bars + 2 * kStages;   // the item's Q tiles landed
   uint64_t* q_empty = q_full + 1;          // every S MMA of the item is done (Q may be replaced)
-  uint64_t* s_full = q_empty + 1;          // [kQT] S_X(j) is in TMEM (and PV_X(j-1) is complete)
-  uint64_t* p_full = s_full + kQT;         // [kQT] P_X(j) is in shared memory, S_X(j) was read, O_X rescaled
-  uint64_t* o_done = p_full + kQT;         // [kQT] the item's last PV_X is complete
+  uint64_t* s_full = q_empty + 1;          // [kQT] S_X(j) is in TMEM
+  uint64_t* s_free = s_full + kQT;         // [kQT] the softmax has read S_X(j) into registers
+  uint64_t* p_full = s_free + kQT;         // [kQT] P_X(j) is in shared memory, O_X rescaled
+  uint64_t* pv_done = p_full + kQT;        // [kQT] PV_X(j) is complete (P_X free, O_X current)
+  uint64_t* o_done = pv_done + kQT;        // [kQT] the item's last PV_X is complete
   uint64_t* o_free = o_done + kQT;         // [kQT] the item's O_X was read out
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -153,7 +178,9 @@ __global__ void __launch_bounds__(kThreads, 1) fa_prefill_kernel(const __grid_co
     tc::mbar_init(q_empty, 1);
     for (int x = 0; x < kQT; ++x) {
       tc::mbar_init(&s_full[x], 1);
-      tc::mbar_init(&p_full[x], 4);  // one arrive per softmax warp
+      tc::mbar_init(&s_free[x], 4);  // one arrive per softmax warp
+      tc::mbar_init(&p_full[x], 4);
+      tc::mbar_init(&pv_done[x], 1);
       tc::mbar_init(&o_done[x], 1);
       tc::mbar_init(&o_free[x], 4);
     }
@@ -227,46 +254,59 @@ __global__ void __launch_bounds__(kThreads, 1) fa_prefill_kernel(const __grid_co
           tc::mma_f16(tmem + kColO + x * kD, tc::desc_sw128(pt + (ks >> 2) * (kBQ * 128) + (ks & 3) * 32),
                       tc::desc_sw128(vt + ks * 2048), id_o, (acc || ks > 0) ? 1u : 0u);
       };
+      auto s_mma = [&](int x, int stage) {  // S_X = Q_X K^T
+        const uint8_t* kt = smem + kOffK + stage * kTileBytes;
+        const uint8_t* qx = smem + kOffQ + x * kTileBytes;
+#pragma unroll
+        for (int ks = 0; ks < kD / 16; ++ks)
+          tc::mma_f16(tmem + x * kBK, tc::desc_sw128(qx + ks * 32), tc::desc_sw128(kt + ks * 32), id_s,
+                      ks > 0 ? 1u : 0u);
+        tc::mma_commit(&s_full[x]);
+      };
+      // Order per key tile j: S_X(j+1) as soon as the softmax has read S_X(j) (it then overlaps
+      // that softmax's exponentials), PV_X(j) once P_X(j) is written.
       for (int k = blockIdx.x; k < a.num_items && ok; k += gridDim.x) {
         Item it;
         if (!item_at(a, k, it) || it.n == 0) continue;
         if (!tc::mbar_wait(q_full, items & 1, a.status)) break;
+        if (!tc::mbar_wait(&kv_full[g % kStages], (g / kStages) & 1, a.status)) break;
         tc::fence_after_sync();
-        for (int j = 0; j <= it.n && ok; ++j) {
-          const int s = (g + j) % kStages, sp = (g + j - 1) % kStages;
-          if (j < it.n && !tc::mbar_wait(&kv_full[s], ((g + j) / kStages) & 1, a.status)) {
+        for (int x = 0; x < kQT; ++x) s_mma(x, g % kStages);
+        if (it.n == 1) tc::mma_commit(q_empty);
+        for (int j = 0; j < it.n && ok; ++j) {
+          const int s = (g + j) % kStages, sn = (g + j + 1) % kStages;
+          const bool more = j + 1 < it.n;
+          if (more && !tc::mbar_wait(&kv_full[sn], ((g + j + 1) / kStages) & 1, a.status)) {
             ok = false;
             break;
           }
-          tc::fence_after_sync();
-          for (int x = 0; x < kQT; ++x) {
-            if (j > 0) {  // PV_X(j-1): P_X(j-1) written, O_X rescaled
-              if (!tc::mbar_wait(&p_full[x], (c + j - 1) & 1, a.status)) {
-                ok = false;
-                break;
-              }
-              // the first PV of an item overwrites O_X: the previous item's O_X must be read out
-              if (j == 1 && items > 0 && !tc::mbar_wait(&o_free[x], (items - 1) & 1, a.status)) {
-                ok = false;
-                break;
-              }
-              tc::fence_after_sync();
-              pv(x, sp, j > 1);
-              if (j == it.n) tc::mma_commit(&o_done[x]);
+          for (int x = 0; x < kQT && ok && more; ++x) {
+            if (!tc::mbar_wait(&s_free[x], (c + j) & 1, a.status)) {
+              ok = false;
+              break;
             }
-            if (j < it.n) {  // S_X(j) = Q_X K(j)^T
-              const uint8_t* kt = smem + kOffK + s * kTileBytes;
-              const uint8_t* qx = smem + kOffQ + x * kTileBytes;
-#pragma unroll
-              for (int ks = 0; ks < kD / 16; ++ks)
-                tc::mma_f16(tmem + x * kBK, tc::desc_sw128(qx + ks * 32), tc::desc_sw128(kt + ks * 32), id_s,
-                            ks > 0 ? 1u : 0u);
-              tc::mma_commit(&s_full[x]);
-            }
+            tc::fence_after_sync();
+            s_mma(x, sn);
           }
           if (!ok) break;
-          if (j == it.n - 1) tc::mma_commit(q_empty);  // every S MMA of the item issued
-          if (j > 0) tc::mma_commit(&kv_empty[sp]);    // S(j-1) and PV(j-1) of both tiles issued
+          if (j + 1 == it.n - 1) tc::mma_commit(q_empty);  // every S MMA of the item issued
+          for (int x = 0; x < kQT; ++x) {
+            if (!tc::mbar_wait(&p_full[x], (c + j) & 1, a.status)) {
+              ok = false;
+              break;
+            }
+            // the first PV of an item overwrites O_X: the previous item's O_X must be read out
+            if (j == 0 && items > 0 && !tc::mbar_wait(&o_free[x], (items - 1) & 1, a.status)) {
+              ok = false;
+              break;
+            }
+            tc::fence_after_sync();
+            pv(x, s, j > 0);
+            tc::mma_commit(&pv_done[x]);
+            if (j == it.n - 1) tc::mma_commit(&o_done[x]);
+          }
+          if (!ok) break;
+          tc::mma_commit(&kv_empty[s]);  // S(j) and PV(j) of both tiles issued
         }
         g += it.n;
         c += it.n;
@@ -297,6 +337,13 @@ __global__ void __launch_bounds__(kThreads, 1) fa_prefill_kernel(const __grid_co
       const int lo_vis = a.window > 0 ? p - a.window + 1 : 0;
       const int hi_vis = a.causal ? min(p, it.L - 1) : it.L - 1;
       float m = -INFINITY, l = 0.f;
+      // PV_X of the previous key tile (phase c - 1) must be complete before P_X is rewritten
+      // or O_X rescaled; it was issued after this warpgroup's previous p_full arrive
+      auto wait_pv = [&](int cc_) -> bool {
+        if (!tc::mbar_wait(&pv_done[x], (cc_ - 1) & 1, a.status)) return false;
+        tc::fence_after_sync();
+        return true;
+      };
       for (int j = 0; j < it.n; ++j, ++c) {
         if (!tc::mbar_wait(&s_full[x], c & 1, a.status)) {
           ok = false;
@@ -307,6 +354,13 @@ __global__ void __launch_bounds__(kThreads, 1) fa_prefill_kernel(const __grid_co
         // a tile no row of this warp can see (the other query tile's diagonal or window edge):
         // P = 0 without reading S; the row statistics are unchanged
         if (__all_sync(0xffffffffu, key0 > hi_vis || key0 + kBK - 1 < lo_vis)) {
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&s_free[x]);
+          if (j > 0 && !wait_pv(c)) {
+            ok = false;
+            break;
+          }
 #pragma unroll
           for (int ch = 0; ch < 16; ++ch)
             *reinterpret_cast<uint4*>(pbuf + (ch >> 3) * (kBQ * 128) + sw128(r, ch & 7)) = make_uint4(0, 0, 0, 0);
@@ -321,6 +375,10 @@ __global__ void __launch_bounds__(kThreads, 1) fa_prefill_kernel(const __grid_co
         for (int cc = 0; cc < kBK; cc += 32)
           tc::tmem_ld_32x32b_x32(s_addr + cc, *reinterpret_cast<uint32_t(*)[32]>(sv + cc));
         tc::tmem_ld_wait();
+        // S_X is in registers: the tensor core may compute the next tile's S_X meanwhile
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&s_free[x]);
         if (key0 < lo_vis || key0 + kBK - 1 > hi_vis) {  // the tile crosses this row's visible range
 #pragma unroll
           for (int t = 0; t < kBK; ++t) {
@@ -330,46 +388,57 @@ __global__ void __launch_bounds__(kThreads, 1) fa_prefill_kernel(const __grid_co
         }
         float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int t = 0; t < kBK; ++t) mx[t & 3] = fmaxf(mx[t & 3], sv[t]);
-        const float tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * a.scale_log2;
+        for (int t = 0; t < kBK; t += 8) {  // four independent chains of three-input maxima
+          mx[0] = max3(mx[0], sv[t], sv[t + 1]);
+          mx[1] = max3(mx[1], sv[t + 2], sv[t + 3]);
+          mx[2] = max3(mx[2], sv[t + 4], sv[t + 5]);
+          mx[3] = max3(mx[3], sv[t + 6], sv[t + 7]);
+        }
+        const float tmax = max3(mx[0], mx[1], fmaxf(mx[2], mx[3])) * a.scale_log2;
         // lazy rescaling: move the reference maximum only when the row maximum grew by > 2^8
         const bool grow = tmax > m + kRescaleLog2 || (m == -INFINITY && tmax > -INFINITY);
         const float m_new = grow ? tmax : m;
         const float corr = grow ? ex2(m - m_new) : 1.f;  // m = -inf gives 0
-        if (j > 0 && __any_sync(0xffffffffu, grow)) {
-          // O_X holds PV through j-1 (complete: S_X(j) was committed after it); rescale it
-#pragma unroll
-          for (int cc = 0; cc < kD; cc += 16) {
-            uint32_t ov[16];
-            tc::tmem_ld_32x32b_x16(o_addr + cc, ov);
-            tc::tmem_ld_wait();
-#pragma unroll
-            for (int t = 0; t < 16; ++t) ov[t] = __float_as_uint(__uint_as_float(ov[t]) * corr);
-            tc::tmem_st_32x32b_x16(o_addr + cc, ov);
-          }
-          tc::tmem_st_wait();
-        }
         const float mref = m_new == -INFINITY ? 0.f : m_new;  // a fully masked row so far: P = 0
-        float rs[4] = {0.f, 0.f, 0.f, 0.f};
+        // P of the whole row into registers (bf16 pairs), overlapping PV_X(j-1) on the tensor core
+        float rs[4] = {0.f, 0.f, 0.f, 0.f};  // two packed (f32x2) row-sum chains
+        uint32_t pk[kBK / 2];
 #pragma unroll
-        for (int cc = 0; cc < kBK; cc += 32) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int t = 0; t < 32; t += 2) {
-            const float e0 = ex2(fmaf(sv[cc + t], a.scale_log2, -mref));
-            const float e1 = ex2(fmaf(sv[cc + t + 1], a.scale_log2, -mref));
-            rs[(t >> 1) & 3] += e0 + e1;
-            const __nv_bfloat162 pr = __floats2bfloat162_rn(e0, e1);
-            pk[t >> 1] = *reinterpret_cast<const uint32_t*>(&pr);
+        for (int t = 0; t < kBK; t += 2) {
+          float x0, x1;
+          ffma2(x0, x1, sv[t], sv[t + 1], a.scale_log2, -mref);
+          const float e0 = ex2(x0);
+          const float e1 = ex2(x1);
+          if ((t >> 1) & 1)
+            fadd2(rs[2], rs[3], e0, e1);
+          else
+            fadd2(rs[0], rs[1], e0, e1);
+          const __nv_bfloat162 pr = __floats2bfloat162_rn(e0, e1);
+          pk[t >> 1] = *reinterpret_cast<const uint32_t*>(&pr);
+        }
+        if (j > 0) {
+          if (!wait_pv(c)) {
+            ok = false;
+            break;
           }
-          const int atom = cc >> 6;  // 64 keys (128 bytes) per swizzle atom
+          if (__any_sync(0xffffffffu, grow)) {
+            // O_X holds PV through j-1 (complete): rescale it before PV_X(j) accumulates
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            const int chunk = ((cc & 63) >> 3) + q4;  // 16-byte chunk (8 keys) within the atom row
-            *reinterpret_cast<uint4*>(pbuf + atom * (kBQ * 128) + sw128(r, chunk)) =
-                make_uint4(pk[q4 * 4], pk[q4 * 4 + 1], pk[q4 * 4 + 2], pk[q4 * 4 + 3]);
+            for (int cc = 0; cc < kD; cc += 16) {
+              uint32_t ov[16];
+              tc::tmem_ld_32x32b_x16(o_addr + cc, ov);
+              tc::tmem_ld_wait();
+#pragma unroll
+              for (int t = 0; t < 16; ++t) ov[t] = __float_as_uint(__uint_as_float(ov[t]) * corr);
+              tc::tmem_st_32x32b_x16(o_addr + cc, ov);
+            }
+            tc::tmem_st_wait();
           }
         }
+#pragma unroll
+        for (int ch = 0; ch < 16; ++ch)  // 16-byte chunk ch = keys 8ch .. 8ch+7; 64 keys per swizzle atom
+          *reinterpret_cast<uint4*>(pbuf + (ch >> 3) * (kBQ * 128) + sw128(r, ch & 7)) =
+              make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
         l = l * corr + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
         m = m_new;
         fence_async_smem();  // P stores visible to the tensor cores

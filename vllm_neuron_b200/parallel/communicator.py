@@ -24,6 +24,10 @@ logger = init_logger(__name__)
 
 
 class FusedCommunicator:
+    CANARY_BYTES = 256
+    CANARY_VALUE = 0xA5
+    HEADER_BYTES = 64 * 1024  # flags + counters before the two slots (csrc/comm.cu)
+
     def __init__(self, group, device: torch.device, max_tokens: int = 256, max_hidden: int = 8192,
                  num_blocks: int = 64):
         from ..ops import _ext
@@ -35,12 +39,16 @@ class FusedCommunicator:
         self.world = group.world_size
         self.num_blocks = num_blocks
         self.max_hidden = max_hidden
-        # one receive area per source rank in each of the two slots
-        self.slot_bytes = group.world_size * max_tokens * max_hidden * 2
+        # one receive area per source rank in each of the two slots, each followed by a guard
+        # of CANARY_BYTES that no kernel writes (a pattern checked by check_canaries)
+        self.area_bytes = max_tokens * max_hidden * 2
+        self.slot_bytes = group.world_size * (self.area_bytes + self.CANARY_BYTES)
         self.max_elems = max_tokens * max_hidden
         ops = torch.ops.b200
         with torch.cuda.device(device):
             self.local = ops.comm_alloc(self.slot_bytes)
+            for off in self._canary_offsets():
+                ops.device_fill(self.local + off, self.CANARY_BYTES, self.CANARY_VALUE)
             handle = ops.ipc_get_handle(self.local).numpy().tobytes()
         handles = [None] * self.world
         dist.all_gather_object(handles, handle, group=group.cpu_group)
@@ -60,6 +68,20 @@ class FusedCommunicator:
         self.status = device_status(device)
         logger.info("fused communicator for group %s: %d ranks, %.1f MB slots", group.name, self.world,
                     self.slot_bytes / 1e6)
+
+    def _canary_offsets(self) -> list[int]:
+        part = self.area_bytes + self.CANARY_BYTES
+        return [self.HEADER_BYTES + slot * self.slot_bytes + p * part + self.area_bytes
+                for slot in (0, 1) for p in range(self.world)]
+
+    def check_canaries(self) -> bool:
+        """Every guard after a receive area of this rank's region still holds its pattern (no
+        kernel wrote past the rows it owns).  Synchronises the device."""
+        ops = torch.ops.b200
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize()
+            return all(bool((ops.device_read(self.local + off, self.CANARY_BYTES) == self.CANARY_VALUE).all())
+                       for off in self._canary_offsets())
 
     def can_all_reduce(self, x: torch.Tensor) -> bool:
         return (x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.dim() >= 1
