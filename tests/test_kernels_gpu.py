@@ -181,6 +181,10 @@ def test_router_topk_and_argmax(T, E, H, k):
     assert (got >= kth - 0.02).all(), "selected an expert outside the top-k"
     assert (ids.long().sort(-1).values.diff(dim=-1) > 0).all(), "duplicate expert"
     _close(wt, torch.softmax(got, -1), 1e-2, 1e-2, "router weights")
+    # softmax over all experts, top-k, no renormalisation (Qwen3-Next without norm_topk_prob)
+    ids_u, wt_u = ops.router_topk(x, w, b, k, "softmax_topk_unnormalized")
+    assert torch.equal(ids_u, ids)
+    _close(wt_u, torch.softmax(ref_logits, -1).gather(1, ids_u.long()), 1e-2, 1e-2, "unnormalised router weights")
     lg = torch.randn(64, 25136, device=DEV, dtype=torch.bfloat16)
     val, idx = ops.argmax(lg)
     assert torch.equal(idx, lg.float().argmax(-1))

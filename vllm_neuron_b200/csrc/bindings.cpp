@@ -235,14 +235,14 @@ void varlen_attention(Tensor out, Tensor q, Tensor k, Tensor v, Tensor cu, doubl
            "varlen_attention");
 }
 
-void topk_softmax(Tensor ids, Tensor weights, Tensor logits) {
+void topk_softmax(Tensor ids, Tensor weights, Tensor logits, int64_t full) {
   check_cuda(logits, "logits");
   TORCH_CHECK((logits.scalar_type() == at::kFloat || logits.scalar_type() == at::kBFloat16) &&
                   logits.is_contiguous(),
               "fp32 / bf16 contiguous logits");
   c10::cuda::CUDAGuard g(logits.device());
   check_rc(b200_topk_softmax(ids.data_ptr<int>(), weights.data_ptr<float>(), logits.data_ptr(), logits.size(0),
-                             logits.size(1), ids.size(1), dt(logits), stream()),
+                             logits.size(1), ids.size(1), dt(logits), (int)full, stream()),
            "topk_softmax");
 }
 
@@ -308,7 +308,7 @@ TORCH_LIBRARY(b200, m) {
   m.def(
       "varlen_attention(Tensor(a!) out, Tensor q, Tensor k, Tensor v, Tensor cu_seqlens, float scale, bool causal, "
       "int max_seqlen) -> ()");
-  m.def("topk_softmax(Tensor(a!) ids, Tensor(b!) weights, Tensor logits) -> ()");
+  m.def("topk_softmax(Tensor(a!) ids, Tensor(b!) weights, Tensor logits, int full=0) -> ()");
   m.def("argmax(Tensor(a!) vals, Tensor(b!) idx, Tensor logits) -> ()");
   m.def(
       "sample(Tensor(a!) out, Tensor logits, Tensor temperature, Tensor top_k, Tensor top_p, Tensor uniform, "

@@ -71,7 +71,8 @@ int b200_varlen_attention(void* out, const void* q, const void* k, const void* v
                           int T, int nq, int nkv, int d, float scale, int causal, int max_seqlen, int dtype,
                           cudaStream_t s);
 
-int b200_topk_softmax(int* ids, float* weights, const void* logits, int T, int E, int k, int dtype, cudaStream_t s);
+int b200_topk_softmax(int* ids, float* weights, const void* logits, int T, int E, int k, int dtype, int full,
+                      cudaStream_t s);
 
 int b200_argmax(float* vals, int64_t* idx, const void* logits, int B, int V, int dtype, cudaStream_t s);
 

@@ -1,7 +1,9 @@
 // Router top-k softmax, argmax and on-device sampling.
 //
 // topk_softmax: per token, the k largest router logits (ties -> lower expert id) and a
-//   softmax over those k values (GPT-OSS order, functional/moe/router.py:300-566).
+//   softmax over those k values (GPT-OSS order, functional/moe/router.py:300-566); with
+//   `full`, the softmax over all E logits taken at the k selected experts, not renormalised
+//   (softmax -> top-k routers without norm_topk_prob).
 // argmax: per row (max value, lowest index of the max).
 // sample: per row, temperature -> top-k (<= max_top_k <= 1024) -> softmax -> top-p ->
 //   inverse-CDF draw with a host-supplied uniform; temperature <= 0 is greedy
@@ -15,7 +17,7 @@ namespace b200 {
 
 template <typename LT>
 __global__ void topk_softmax_kernel(int* __restrict__ ids, float* __restrict__ w, const LT* __restrict__ logits,
-                                    int T, int E, int k) {
+                                    int T, int E, int k, int full) {
   pdl_wait();  // predecessor output visible (programmatic dependent launch)
   pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -29,6 +31,20 @@ __global__ void topk_softmax_kernel(int* __restrict__ ids, float* __restrict__ w
   for (int i = 0; i < kMaxPer; ++i) {
     const int e = i * 32 + lane;
     v[i] = (i < per && e < E) ? to_float(row[e]) : -INFINITY;
+  }
+  float denom_all = 0.f;  // full: sum over all experts of exp(l - max)
+  if (full) {
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) mx = fmaxf(mx, v[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sm = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) sm += v[i] == -INFINITY ? 0.f : __expf(v[i] - mx);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+    denom_all = sm;
   }
   float sel_v[16];
   int sel_i[16];
@@ -62,6 +78,7 @@ __global__ void topk_softmax_kernel(int* __restrict__ ids, float* __restrict__ w
     const float m = sel_v[0];
     float s = 0.f;
     for (int j = 0; j < k; ++j) s += __expf(sel_v[j] - m);
+    if (full) s = denom_all;  // m is the row maximum (the first selected logit)
     for (int j = 0; j < k; ++j) {
       ids[(size_t)warp * k + j] = sel_i[j];
       w[(size_t)warp * k + j] = __expf(sel_v[j] - m) / s;
@@ -296,16 +313,16 @@ __global__ void __launch_bounds__(1024) sample_kernel(int64_t* __restrict__ out,
 using namespace b200;
 
 extern "C" int b200_topk_softmax(int* ids, float* weights, const void* logits, int T, int E, int k, int dtype,
-                                 cudaStream_t s) {
+                                 int full, cudaStream_t s) {
   if (E > 1024 || k > 16 || k > E) return kBadShape;
   if (T == 0) return 0;
   const int warps_per_block = 4;
   if (dtype == kBF16)
     launch_k(topk_softmax_kernel<__nv_bfloat16>, dim3(cdiv(T, warps_per_block)), dim3(32 * warps_per_block), 0, s,
-             ids, weights, (const __nv_bfloat16*)logits, T, E, k);
+             ids, weights, (const __nv_bfloat16*)logits, T, E, k, full);
   else if (dtype == kF32)
     launch_k(topk_softmax_kernel<float>, dim3(cdiv(T, warps_per_block)), dim3(32 * warps_per_block), 0, s, ids,
-             weights, (const float*)logits, T, E, k);
+             weights, (const float*)logits, T, E, k, full);
   else
     return kBadShape;
   return (int)cudaGetLastError();

@@ -275,9 +275,7 @@ class SparseMoE(nn.Module):
         if self.cfg.norm_topk_prob:
             # softmax -> top-k -> renormalise == softmax over the top-k logits
             return ops.router_topk(x, self.router, None, k)
-        p = torch.softmax(ops.linear(x, self.router).float(), -1)
-        wts, ids = torch.topk(p, k, -1)
-        return ids.to(torch.int32), wts
+        return ops.router_topk(x, self.router, None, k, "softmax_topk_unnormalized")
 
     def _experts(self, x: torch.Tensor, ids: torch.Tensor, wts: torch.Tensor) -> torch.Tensor:
         H, I = self.cfg.hidden_size, self.cfg.moe_intermediate_size

@@ -353,24 +353,21 @@ def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqle
 def router_topk(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, top_k: int,
                 order: str = "topk_softmax") -> tuple[torch.Tensor, torch.Tensor]:
     """(topk_ids [T,k] int32, topk_weights [T,k] fp32)."""
-    if use_kernel(x) and order == "topk_softmax" and w.shape[0] <= 1024 and top_k <= 16:
+    if use_kernel(x) and order in ("topk_softmax", "softmax_topk", "softmax_topk_unnormalized") \
+            and w.shape[0] <= 1024 and top_k <= 16:
         # fp32 logits straight from the GEMM accumulator (the reference's router linear runs
-        # in fp32, model_mxfp4.py:949-955): bf16-rounded logits would reorder near ties
+        # in fp32, model_mxfp4.py:949-955): bf16-rounded logits would reorder near ties.
+        # softmax -> top-k -> renormalise selects and weighs exactly as top-k -> softmax (the
+        # softmax is monotonic and the renormalisation cancels its denominator); without the
+        # renormalisation the kernel divides by the softmax denominator over all experts.
         logits = linear(x, w, b, out_dtype=torch.float32)
         ids = torch.empty(x.shape[0], top_k, dtype=torch.int32, device=x.device)
         wts = torch.empty(x.shape[0], top_k, dtype=torch.float32, device=x.device)
-        _k().topk_softmax(ids, wts, logits)
+        _k().topk_softmax(ids, wts, logits, 1 if order == "softmax_topk_unnormalized" else 0)
         return ids, wts
-    if use_kernel(x):
-        logits = linear(x, w, b, out_dtype=torch.float32)
-        if order == "softmax_topk":
-            wts, ids = torch.topk(torch.softmax(logits, -1), top_k, -1)
-            wts = wts / wts.sum(-1, keepdim=True)
-        else:
-            ids, wts, _ = ref.router_topk(x, w, b, top_k, order)
-        return ids.to(torch.int32), wts
-    ids, wts, _ = ref.router_topk(x, w, b, top_k, order)
-    return ids, wts
+    ref_order, renorm = ("softmax_topk", False) if order == "softmax_topk_unnormalized" else (order, True)
+    ids, wts, _ = ref.router_topk(x, w, b, top_k, ref_order, renormalize=renorm)
+    return ids.to(torch.int32), wts
 
 
 def moe_mxfp4(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, w13: torch.Tensor,
