@@ -82,6 +82,18 @@ def _worker(rank, world, port, q):
             o, r_ = g.communicator.all_reduce_add_rmsnorm(xr, rr.clone(), wr, 1e-5)
             runs.append((o.clone(), r_.clone()))
         errs.append(("replay", float(not (torch.equal(runs[0][0], runs[1][0]) and torch.equal(runs[0][1], runs[1][1])))))
+        # MoE boundary with the route sum inside the all-reduce kernel == route-sum kernel, then the
+        # plain fused all-reduce (bit for bit: the same fp32 sums rounded to bf16)
+        torch.manual_seed(11 + rank)
+        k, E_local, e_off = 4, 8, 8 * rank
+        ids = torch.randint(0, 8 * world, (64, k), device=dev, dtype=torch.int32)
+        yr = torch.randn(64 * k, 2880, device=dev).bfloat16()
+        summed = torch.empty(64, 2880, device=dev, dtype=torch.bfloat16)
+        torch.ops.b200.moe_route_sum(summed, yr, ids, E_local, e_off)
+        o1, r1 = g.communicator.all_reduce_add_rmsnorm(summed, rr.clone(), wr, 1e-5)
+        o2, r2 = g.communicator.all_reduce_routes_add_rmsnorm(yr, ids, E_local, e_off, rr.clone(), wr, 1e-5)
+        errs.append(("routes", max((o1.float() - o2.float()).abs().max().item(),
+                                   (r1.float() - r2.float()).abs().max().item())))
         # guard bytes after every receive area are untouched
         errs.append(("canary", float(not g.communicator.check_canaries())))
         st_code = int(ops.device_status(dev)[0].item())
@@ -113,7 +125,8 @@ def test_fused_allreduce_two_gpus():
         for kind, e in errs:
             # bf16 results: a couple of ulps at magnitudes up to ~16 (rounding order of the
             # fused sum + bias differs from all-reduce-then-add)
-            tol = {"sum": 0.125, "norm": 0.13, "res": 0.13, "graph": 0.0}[kind]
+            tol = {"sum": 0.125, "norm": 0.13, "res": 0.13, "graph": 0.0, "replay": 0.0, "routes": 0.0,
+                   "canary": 0.0}[kind]
             if e > tol:
                 bad.append(f"rank {rank} {kind} err {e}")
     assert not bad, bad

@@ -72,8 +72,13 @@ B200_D uint64_t now_ns() {
 
 // One CTA per group of rows; rows r = blockIdx.x, blockIdx.x + gridDim.x, ...
 // H % 8 == 0; bf16 data.  kNorm: add bias + residual and RMSNorm; else plain sum.
+// Route mode (topk_ids != null): `in` holds per-route rows [T * k, H] of an MoE layer and the
+// partial pushed for token r is their sum over the routes to this rank's experts
+// [eoff, eoff + E_local) (fp32 sum rounded to bf16, as a separate reduction kernel would store).
 template <bool kNorm>
 __global__ void __launch_bounds__(256) allreduce_fused_kernel(CommPeers peers, const __nv_bfloat16* __restrict__ in,
+                                                              const int* __restrict__ topk_ids, int k, int E_local,
+                                                              int eoff,
                                                               __nv_bfloat16* __restrict__ out,
                                                               __nv_bfloat16* __restrict__ residual,
                                                               const __nv_bfloat16* __restrict__ bias,
@@ -97,8 +102,29 @@ __global__ void __launch_bounds__(256) allreduce_fused_kernel(CommPeers peers, c
   // 2. push my rows into every rank's receive area for me
   for (int r = b; r < T; r += gridDim.x) {
     const uint4* src = reinterpret_cast<const uint4*>(in + (size_t)r * H);
+    int loc[16];
+    int nl = 0;
+    if (topk_ids != nullptr)
+      for (int j = 0; j < k && j < 16; ++j) {
+        const int e = topk_ids[r * k + j] - eoff;
+        if (e >= 0 && e < E_local) loc[nl++] = j;
+      }
     for (int c = threadIdx.x; c < nchunk; c += blockDim.x) {
-      const uint4 v = src[c];
+      uint4 v;
+      if (topk_ids != nullptr) {
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int i = 0; i < nl; ++i) {
+          const uint4 u = reinterpret_cast<const uint4*>(in + (size_t)(r * k + loc[i]) * H)[c];
+          const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(hb[q]);
+        }
+        __nv_bfloat16* vb = reinterpret_cast<__nv_bfloat16*>(&v);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) vb[q] = __float2bfloat16(acc[q]);
+      } else {
+        v = src[c];
+      }
       const size_t off = (size_t)peers.rank * part + ((size_t)r * nchunk + c) * 16;
       for (int p = 0; p < peers.world; ++p)
         *reinterpret_cast<uint4*>(slot_of(peers.base[p], slot, peers.slot_bytes) + off) = v;
@@ -225,7 +251,9 @@ extern "C" int b200_ipc_close(void* p) { return (int)cudaIpcCloseMemHandle(p); }
 // wait_ns: limit of each CTA's wait for its peers (0 = kDefaultWaitNs).
 extern "C" int b200_allreduce_fused(void* const* bases, int rank, int world, size_t slot_bytes, const void* in,
                                     void* out, void* residual, const void* bias, const float* w, float eps, int T,
-                                    int H, int num_blocks, unsigned long long wait_ns, int* status, cudaStream_t s) {
+                                    int H, int num_blocks, unsigned long long wait_ns, int* status, cudaStream_t s,
+                                    const int* topk_ids, int k, int E_local, int eoff) {
+  if (topk_ids != nullptr && (k < 1 || k > 16)) return kBadShape;
   if (wait_ns == 0) wait_ns = kDefaultWaitNs;
   if (world > kMaxRanks || world < 1 || H % 8 || H > 8192 || T < 0) return kBadShape;
   if ((size_t)T * H * 2 * world > slot_bytes || (slot_bytes / world) % 16) return kBadShape;
@@ -237,11 +265,13 @@ extern "C" int b200_allreduce_fused(void* const* bases, int rank, int world, siz
   peers.world = world;
   peers.slot_bytes = slot_bytes;
   if (w != nullptr)
-    launch_k(allreduce_fused_kernel<true>, dim3(num_blocks), dim3(256), 0, s, peers, (const __nv_bfloat16*)in, (__nv_bfloat16*)out,
+    launch_k(allreduce_fused_kernel<true>, dim3(num_blocks), dim3(256), 0, s, peers, (const __nv_bfloat16*)in, topk_ids, k,
+             E_local, eoff, (__nv_bfloat16*)out,
                                                            (__nv_bfloat16*)residual, (const __nv_bfloat16*)bias, w,
                                                            eps, T, H, wait_ns, status);
   else
-    launch_k(allreduce_fused_kernel<false>, dim3(num_blocks), dim3(256), 0, s, peers, (const __nv_bfloat16*)in, (__nv_bfloat16*)out,
+    launch_k(allreduce_fused_kernel<false>, dim3(num_blocks), dim3(256), 0, s, peers, (const __nv_bfloat16*)in, topk_ids,
+             k, E_local, eoff, (__nv_bfloat16*)out,
                                                             nullptr, nullptr, nullptr, eps, T, H, wait_ns, status);
   return (int)cudaGetLastError();
 }

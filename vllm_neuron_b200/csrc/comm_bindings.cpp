@@ -12,7 +12,8 @@ int b200_ipc_open_handle(const void* handle64, void** out);
 int b200_ipc_close(void* p);
 int b200_allreduce_fused(void* const* bases, int rank, int world, size_t slot_bytes, const void* in, void* out,
                          void* residual, const void* bias, const float* w, float eps, int T, int H, int num_blocks,
-                         unsigned long long wait_ns, int* status, cudaStream_t s);
+                         unsigned long long wait_ns, int* status, cudaStream_t s, const int* topk_ids, int k,
+                         int E_local, int eoff);
 int b200_kv_export(void* dst, const int64_t* kptr, const int64_t* vptr, int n_layers, const int* blocks, int T, int nh,
                    int row_bytes, int bs, cudaStream_t s);
 int b200_kv_import(const void* const* part_base, const int* part_h0, const int* part_nh, int n_parts,
@@ -71,12 +72,22 @@ void ipc_close(int64_t p) { b200_ipc_close(reinterpret_cast<void*>(p)); }
 
 void allreduce_fused(at::IntArrayRef bases, int64_t rank, int64_t slot_bytes, Tensor input, Tensor out,
                      c10::optional<Tensor> residual, c10::optional<Tensor> bias, c10::optional<Tensor> w, double eps,
-                     int64_t num_blocks, c10::optional<Tensor> status, int64_t wait_ns) {
+                     int64_t num_blocks, c10::optional<Tensor> status, int64_t wait_ns,
+                     c10::optional<Tensor> topk_ids, int64_t e_local, int64_t e_off) {
   TORCH_CHECK(input.is_cuda() && input.scalar_type() == at::kBFloat16 && input.is_contiguous(), "bf16 input");
   TORCH_CHECK(out.is_contiguous() && out.scalar_type() == at::kBFloat16, "bf16 out");
   TORCH_CHECK(bases.size() >= 1 && bases.size() <= 8, "1..8 ranks");
   const int H = input.size(-1);
-  const int T = input.numel() / H;
+  int T = input.numel() / H, k = 0;
+  if (topk_ids.has_value()) {  // route mode: input holds [T * k, H] per-route rows
+    TORCH_CHECK(topk_ids->is_cuda() && topk_ids->scalar_type() == at::kInt && topk_ids->is_contiguous() &&
+                    topk_ids->dim() == 2,
+                "topk_ids: contiguous int32 [T, k]");
+    k = topk_ids->size(1);
+    TORCH_CHECK((int64_t)topk_ids->size(0) * k == T, "input rows must be T * k");
+    T = topk_ids->size(0);
+  }
+  TORCH_CHECK(out.numel() == (int64_t)T * H, "out must be [T, H]");
   void* ptrs[8];
   for (size_t i = 0; i < bases.size(); ++i) ptrs[i] = reinterpret_cast<void*>(bases[i]);
   if (w.has_value()) {
@@ -90,7 +101,8 @@ void allreduce_fused(at::IntArrayRef bases, int64_t rank, int64_t slot_bytes, Te
       residual.has_value() ? residual->data_ptr() : nullptr, bias.has_value() ? bias->data_ptr() : nullptr,
       w.has_value() ? w->data_ptr<float>() : nullptr, (float)eps, T, H, num_blocks,
       wait_ns > 0 ? (unsigned long long)wait_ns : 0ull, status.has_value() ? status->data_ptr<int>() : nullptr,
-      at::cuda::getCurrentCUDAStream().stream());
+      at::cuda::getCurrentCUDAStream().stream(), topk_ids.has_value() ? topk_ids->data_ptr<int>() : nullptr, k,
+      (int)e_local, (int)e_off);
   TORCH_CHECK(rc == 0, "b200::allreduce_fused failed with code ", rc);
 }
 void kv_export(int64_t dst, Tensor kptr, Tensor vptr, Tensor blocks, int64_t num_tokens, int64_t nh,
@@ -189,7 +201,8 @@ void register_comm_ops(torch::Library& m) {
   m.def("ipc_close(int ptr) -> ()");
   m.def(
       "allreduce_fused(int[] bases, int rank, int slot_bytes, Tensor input, Tensor(a!) out, Tensor(b!)? residual, "
-      "Tensor? bias, Tensor? w, float eps, int num_blocks, Tensor? status, int wait_ns=0) -> ()");
+      "Tensor? bias, Tensor? w, float eps, int num_blocks, Tensor? status, int wait_ns=0, Tensor? topk_ids=None, "
+      "int e_local=0, int e_off=0) -> ()");
   m.def(
       "ep_dispatch(int[] bases, int rank, int slot_bytes, int cpd, int Tc, int E_local, int t_begin, int t_end, "
       "Tensor x, Tensor ids, Tensor w, Tensor(a!) x_recv, Tensor(b!) ids_recv, Tensor(c!) w_recv, "

@@ -724,6 +724,7 @@ extern "C" int b200_moe_mx_forward(void* out, const void* x, const int* topk_ids
                                              max_tiles, atoms_max, status, s);
   }
   if (rc) return rc;
+  if (out == nullptr) return (int)cudaGetLastError();  // the caller reduces the per-route rows of ws.y
   launch_k(moe_reduce_kernel, dim3(sh.T), dim3(128), 0, s, (__nv_bfloat16*)out, (const __nv_bfloat16*)ws.y, topk_ids, sh.k,
                                          sh.E_local, sh.expert_offset, sh.H);
   return (int)cudaGetLastError();
@@ -758,5 +759,16 @@ extern "C" int b200_moe_bf16_forward(void* out, const void* x, const int* topk_i
   if (rc) return rc;
   launch_k(moe_reduce_kernel, dim3(sh.T), dim3(128), 0, s, (__nv_bfloat16*)out, (const __nv_bfloat16*)ws.y, topk_ids, sh.k,
                                          sh.E_local, sh.expert_offset, sh.H);
+  return (int)cudaGetLastError();
+}
+
+// out[t] = sum of y[t * k + j] over the slots j routed to experts [off, off + E) (the reduction
+// a caller defers when it fuses it into the layer-boundary all-reduce and cannot here).
+extern "C" int b200_moe_route_sum(void* out, const void* y, const int* topk_ids, int T, int k, int E, int off, int H,
+                                  cudaStream_t s) {
+  if (k > 16 || H % 8) return kBadShape;
+  if (T == 0) return 0;
+  launch_k(moe_reduce_kernel, dim3(T), dim3(128), 0, s, (__nv_bfloat16*)out, (const __nv_bfloat16*)y, topk_ids, k, E,
+           off, H);
   return (int)cudaGetLastError();
 }

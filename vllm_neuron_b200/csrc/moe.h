@@ -43,6 +43,11 @@ int b200_moe_mx_forward(void* out, const void* x, const int* topk_ids, const flo
                         const b200::MoeShape* shape, float alpha, float limit, const b200::MoeWorkspace* ws,
                         int* status, cudaStream_t s);
 
+// out null: stop after GEMM2, leaving the per-route rows [T*k, H] in ws->y.
+// Per-token sum of per-route rows over the local experts (the final step of the forward).
+int b200_moe_route_sum(void* out, const void* y, const int* topk_ids, int T, int k, int E, int off, int H,
+                       cudaStream_t s);
+
 // bf16 experts: route -> gather -> GEMM1 (+bias, SwiGLU) -> GEMM2 (+bias, x affinity) -> sum.
 // Weights are 128-row x 64-element tiles [E, ceil(rows/128), Kp/64, 128, 64]; shape.K1p /
 // K2p are H / I rounded up to 64; shape.a_fp4 = 2.

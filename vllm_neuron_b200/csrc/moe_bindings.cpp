@@ -12,7 +12,7 @@ using at::Tensor;
 
 void moe_mx(Tensor out, Tensor x, Tensor topk_ids, Tensor topk_w, Tensor w13, Tensor sf13, Tensor b13, Tensor w2,
             Tensor sf2, Tensor b2, int64_t expert_offset, int64_t H, int64_t I, bool a_fp4, double alpha,
-            double limit, c10::optional<Tensor> status) {
+            double limit, c10::optional<Tensor> status, c10::optional<Tensor> y_routes) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "x: contiguous bf16 CUDA");
   TORCH_CHECK(out.is_contiguous() && out.scalar_type() == at::kBFloat16, "out: contiguous bf16");
   TORCH_CHECK(topk_ids.scalar_type() == at::kInt && topk_ids.is_contiguous(), "topk_ids: contiguous int32");
@@ -66,8 +66,14 @@ void moe_mx(Tensor out, Tensor x, Tensor topk_ids, Tensor topk_w, Tensor w13, Te
   ws.aq = base + offs[9];
   ws.sf2 = base + offs[10];
   ws.y = reinterpret_cast<uint16_t*>(base + offs[11]);
+  if (y_routes.has_value()) {  // per-route rows for the caller (no per-token sum here)
+    TORCH_CHECK(y_routes->is_contiguous() && y_routes->scalar_type() == at::kBFloat16 &&
+                    y_routes->numel() == (int64_t)sh.T * sh.k * H,
+                "y_routes: contiguous bf16 [T * k, H]");
+    ws.y = reinterpret_cast<uint16_t*>(y_routes->data_ptr());
+  }
   int* st = status.has_value() ? status->data_ptr<int>() : nullptr;
-  const int rc = b200_moe_mx_forward(out.data_ptr(), x.data_ptr(), topk_ids.data_ptr<int>(), topk_w.data_ptr<float>(),
+  const int rc = b200_moe_mx_forward(y_routes.has_value() ? nullptr : out.data_ptr(), x.data_ptr(), topk_ids.data_ptr<int>(), topk_w.data_ptr<float>(),
                                      w13.data_ptr(), sf13.data_ptr<uint8_t>(), b13.data_ptr<float>(), w2.data_ptr(),
                                      sf2.data_ptr<uint8_t>(), b2.data_ptr<float>(), &sh, (float)alpha, (float)limit,
                                      &ws, st, at::cuda::getCurrentCUDAStream().stream());
@@ -130,6 +136,17 @@ void moe_bf16(Tensor out, Tensor x, Tensor topk_ids, Tensor topk_w, Tensor w13, 
                                        at::cuda::getCurrentCUDAStream().stream());
   TORCH_CHECK(rc == 0, "b200::moe_bf16 failed with code ", rc);
 }
+void moe_route_sum(Tensor out, Tensor y, Tensor topk_ids, int64_t e_local, int64_t e_off) {
+  TORCH_CHECK(out.is_contiguous() && y.is_contiguous() && out.scalar_type() == at::kBFloat16 &&
+                  y.scalar_type() == at::kBFloat16 && topk_ids.scalar_type() == at::kInt && topk_ids.is_contiguous(),
+              "moe_route_sum: bf16 out [T, H], y [T * k, H], int32 topk_ids [T, k]");
+  const int T = out.size(0), H = out.size(1), k = topk_ids.size(1);
+  TORCH_CHECK(y.numel() == (int64_t)T * k * H, "moe_route_sum: y rows");
+  c10::cuda::CUDAGuard g(out.device());
+  const int rc = b200_moe_route_sum(out.data_ptr(), y.data_ptr(), topk_ids.data_ptr<int>(), T, k, (int)e_local,
+                                    (int)e_off, H, at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(rc == 0, "b200::moe_route_sum failed with code ", rc);
+}
 }  // namespace
 
 void register_moe_ops(torch::Library& m) {
@@ -139,10 +156,12 @@ void register_moe_ops(torch::Library& m) {
   m.def(
       "moe_mx(Tensor(a!) out, Tensor x, Tensor topk_ids, Tensor topk_w, Tensor w13, Tensor sf13, Tensor b13, "
       "Tensor w2, Tensor sf2, Tensor b2, int expert_offset, int H, int I, bool a_fp4, float alpha, float limit, "
-      "Tensor? status) -> ()");
+      "Tensor? status, Tensor(b!)? y_routes=None) -> ()");
+  m.def("moe_route_sum(Tensor(a!) out, Tensor y, Tensor topk_ids, int e_local, int e_off) -> ()");
 }
 
 void register_moe_impls(torch::Library& m) {
   m.impl("moe_mx", &moe_mx);
+  m.impl("moe_route_sum", &moe_route_sum);
   m.impl("moe_bf16", &moe_bf16);
 }

@@ -62,7 +62,8 @@ _REGISTRY: dict[str, tuple[Callable[[str], Any], str | None, str | None]] = {
     "VLLM_B200_FUSED_COLLECTIVES": (_bool, "1", None),
     # Row-parallel GEMMs reduce their output tiles through NVSwitch (multimem) when the group
     # has a multicast object (else the GEMM and the fused all-reduce kernel run separately).
-    "VLLM_B200_GEMM_ALLREDUCE": (_bool, "1", None),
+    "VLLM_B200_GEMM_ALLREDUCE": (_bool, "0", None),
+    "VLLM_B200_FUSE_MOE_ROUTE_SUM": (_bool, "1", None),
     # Sliding-window layers keep their own KV block pool (blocks behind the window are freed).
     "VLLM_B200_SWA_KV_GROUP": (_bool, "1", None),
     # Dense layers through the library GEMM (torch / cuBLAS) instead of the tcgen05 kernel:

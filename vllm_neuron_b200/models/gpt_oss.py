@@ -26,11 +26,11 @@ from typing import Iterable
 import torch
 import torch.nn as nn
 
-from .. import ops
+from .. import envs, ops
 from ..nn.linear import ParallelLMHead, RMSNorm, RowParallelLinear, VocabParallelEmbedding
 from ..ops import reference as ref
 from ..ops.mx_layout import round_up, scales_to_atoms, tile_values, tiled_shape
-from ..parallel.state import GroupCoordinator, ParallelState
+from ..parallel.state import GroupCoordinator, ParallelState, RoutePartial
 from .base import KVSpec, LayerSpec, component, kv_head_sharding
 
 
@@ -338,8 +338,21 @@ class GptOssMLP(nn.Module):
         if self.dp.world_size > 1:
             x = self.dp.all_gather(x, dim=0)
         ids, w = ops.router_topk(x, self.router_weight, self.router_bias, self.cfg.num_experts_per_tok)
+        if self._defer_route_sum(x):
+            # the per-token sum over routes happens inside the layer-boundary all-reduce kernel
+            ex = self.experts
+            y = torch.empty(x.shape[0] * ids.shape[1], x.shape[1], dtype=x.dtype, device=x.device)
+            ops.moe_mxfp4(x, ids, w, ex.w13, ex.s13, ex.b13, ex.w2, ex.s2, ex.b2, ex.offset, ex.alpha, ex.limit,
+                          ex.H, ex.I, y_routes=y)
+            return RoutePartial(y, ids, ex.E_local, ex.offset)
         y = self.experts(x, ids, w)
         return self.dp.reduce_scatter(y, dim=0) if self.dp.world_size > 1 else y
+
+    def _defer_route_sum(self, x: torch.Tensor) -> bool:
+        comm = self.tp.communicator
+        return (envs.VLLM_B200_FUSE_MOE_ROUTE_SUM and x.is_cuda and self.dp.world_size == 1
+                and self.tp.world_size > 1 and comm is not None and not self.tp.sp_active
+                and self.experts.quant == "mxfp4" and comm.can_all_reduce(x))
 
 
 class GptOssDecoderLayer(nn.Module):
@@ -426,6 +439,8 @@ class GptOssForCausalLM(nn.Module):
         aux = []
         for i, layer in enumerate(self.layers):
             if i in self.aux_hidden_layers:  # hidden state entering layer i (reduced partial + residual)
+                if isinstance(h, RoutePartial):
+                    h = h.materialize()
                 aux.append(h if residual is None else self.tp.all_reduce(h.clone()) + residual)
             h, residual = layer(positions, h, residual, meta, kv_caches[i], self.cos_sin)
         h, _ = self.tp.all_reduce_add_rmsnorm(h, residual, self.norm.weight, self.cfg.rms_norm_eps)

@@ -373,21 +373,24 @@ def router_topk(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, top_k:
 def moe_mxfp4(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, w13: torch.Tensor,
               s13: torch.Tensor, b13: torch.Tensor | None, w2: torch.Tensor, s2: torch.Tensor,
               b2: torch.Tensor | None, expert_offset: int, alpha: float, limit: float, H: int, I: int,
-              status: torch.Tensor | None = None, fp4: bool = True) -> torch.Tensor:
+              status: torch.Tensor | None = None, fp4: bool = True,
+              y_routes: torch.Tensor | None = None) -> torch.Tensor:
     """Routed experts with packed MX weights in the kernel layout (``ops/mx_layout.py``):
     w13 tiles [E_local, 2I/128, K1p/128, 128, 64] u8 (gate/up interleaved rows) + s13
     scale atoms, w2 tiles [E_local, H/128, K2p/128, 128, 64] + s2 atoms; biases fp32
     [E_local, 2I] / [E_local, H].
-    Returns this rank's partial sum over its experts, [T, H] in x.dtype."""
+    Returns this rank's partial sum over its experts, [T, H] in x.dtype; with ``y_routes``
+    ([T * k, H] bf16, GPU only) the per-route rows are left there unsummed and it is returned
+    (the layer-boundary all-reduce sums them)."""
     E = w13.shape[0]
     if use_kernel(x) and x.dtype == torch.bfloat16:
-        out = torch.empty_like(x)
+        out = torch.empty_like(x) if y_routes is None else x
         b13_ = b13 if b13 is not None else torch.zeros(E, 2 * I, dtype=torch.float32, device=x.device)
         b2_ = b2 if b2 is not None else torch.zeros(E, H, dtype=torch.float32, device=x.device)
         st = status if status is not None else device_status(x.device)
         _k().moe_mx(out, x.contiguous(), topk_ids.to(torch.int32).contiguous(), topk_w.float().contiguous(), w13,
-                    s13, b13_, w2, s2, b2_, expert_offset, H, I, fp4, alpha, limit, st)
-        return out
+                    s13, b13_, w2, s2, b2_, expert_offset, H, I, fp4, alpha, limit, st, y_routes)
+        return out if y_routes is None else y_routes
     from .mx_layout import atoms_to_scales, untile_values
 
     if fp4:

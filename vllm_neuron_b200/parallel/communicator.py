@@ -93,6 +93,18 @@ class FusedCommunicator:
                                        self.num_blocks, self.status)
         return out
 
+    def all_reduce_routes_add_rmsnorm(self, y: torch.Tensor, topk_ids: torch.Tensor, e_local: int, e_off: int,
+                                      residual: torch.Tensor, w: torch.Tensor, eps: float,
+                                      bias: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """The MoE layer boundary in one kernel: per token, the sum of its per-route expert
+        rows ``y`` [T * k, H] over this rank's experts is the partial that is all-reduced, then
+        bias, residual and RMSNorm as ``all_reduce_add_rmsnorm``."""
+        T, H = topk_ids.shape[0], y.shape[-1]
+        out = torch.empty(T, H, dtype=y.dtype, device=y.device)
+        torch.ops.b200.allreduce_fused(self.bases, self.rank, self.slot_bytes, y, out, residual, bias, w, eps,
+                                       self.num_blocks, self.status, 0, topk_ids, e_local, e_off)
+        return out, residual
+
     def all_reduce_add_rmsnorm(self, x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float,
                                bias: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
         out = torch.empty_like(x)

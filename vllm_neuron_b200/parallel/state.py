@@ -141,6 +141,26 @@ def node_of(rank: int, world_size: int, nnodes: int) -> int:
 
 
 @dataclass
+class RoutePartial:
+    """An MoE layer's output before its per-token route sum: ``y`` [T * k, H] per-route
+    expert rows (the routes to this rank's experts [e_off, e_off + e_local) written), summed
+    by the layer-boundary all-reduce kernel itself; ``materialize`` sums them here."""
+    y: torch.Tensor
+    topk_ids: torch.Tensor
+    e_local: int
+    e_off: int
+
+    @property
+    def shape(self) -> torch.Size:
+        return torch.Size((self.topk_ids.shape[0], self.y.shape[-1]))
+
+    def materialize(self) -> torch.Tensor:
+        out = torch.empty(self.shape, dtype=self.y.dtype, device=self.y.device)
+        torch.ops.b200.moe_route_sum(out, self.y, self.topk_ids, self.e_local, self.e_off)
+        return out
+
+
+@dataclass
 class GroupCoordinator:
     """A device group plus a CPU group over the same ranks."""
 
@@ -181,6 +201,12 @@ class GroupCoordinator:
         fused add+norm op."""
         from .. import ops
 
+        if isinstance(x, RoutePartial):
+            comm = self.communicator
+            if (self.world_size > 1 and comm is not None and not self.sp_active
+                    and comm.can_all_reduce(residual)):
+                return comm.all_reduce_routes_add_rmsnorm(x.y, x.topk_ids, x.e_local, x.e_off, residual, w, eps, bias)
+            x = x.materialize()
         if self.sp_active and self.world_size > 1 and x.shape[0] % self.world_size == 0:
             return self._sp_add_rmsnorm(x, residual, w, eps, bias)
         if self.world_size > 1 and self.communicator is not None and self.communicator.can_all_reduce(x):
