@@ -179,16 +179,34 @@ def _collective_check(eng, H: int, T: int = 64) -> dict:
         out, rr = tp.reducer.linear_add_rmsnorm(a, wt, r0.clone(), w, 1e-5, None)
         res["nvls_gemm_allreduce_rmsnorm_max_err"] = max((out.float() - want_out.float()).abs().max().item(),
                                                          (rr.float() - want_res.float()).abs().max().item())
+    sc = tp.sp_comm
+    Tp = 2048
+    if sc is not None and sc.can(Tp, H):
+        # prefill SP boundary on the prompt's shape: the scatter GEMM + the boundary kernel
+        # against cuBLAS + NCCL reduce-scatter + norm + NCCL all-gather
+        K = 4096 // tp.world_size
+        Ts, r = Tp // tp.world_size, tp.rank_in_group
+        a = torch.randn(Tp, K, device=dev, generator=g).bfloat16()
+        wt = (torch.randn(H, K, device=dev, generator=torch.Generator(device=dev).manual_seed(9)) * 0.02).bfloat16()
+        rp = torch.randn(Tp, H, device=dev, generator=torch.Generator(device=dev).manual_seed(8)).bfloat16()
+        y = F.linear(a, wt).float()
+        dist.all_reduce(y, group=tp.device_group)
+        want_out, want_res = ops.fused_add_rms_norm(y[r * Ts:(r + 1) * Ts].bfloat16(),
+                                                    rp[r * Ts:(r + 1) * Ts].clone(), w, 1e-5)
+        want_full = torch.empty(Tp, H, device=dev, dtype=torch.bfloat16)
+        dist.all_gather_into_tensor(want_full, want_out.contiguous(), group=tp.device_group)
+        rr = rp[r * Ts:(r + 1) * Ts].clone()
+        ops.linear_scatter(a, wt, sc.scatter_targets(Tp, H), H)
+        out = sc.boundary(None, Tp, rr, w, 1e-5)
+        res["sp_gemm_boundary_max_err"] = max((out.float() - want_full.float()).abs().max().item(),
+                                              (rr.float() - want_res.float()).abs().max().item())
     torch.cuda.synchronize()
-    errs = torch.tensor([res.get(k, 0.0) for k in ("fused_allreduce_rmsnorm_max_err",
-                                                  "nvls_gemm_allreduce_rmsnorm_max_err")], device=dev)
+    keys = ("fused_allreduce_rmsnorm_max_err", "nvls_gemm_allreduce_rmsnorm_max_err", "sp_gemm_boundary_max_err")
+    errs = torch.tensor([res.get(k, 0.0) for k in keys], device=dev)
     dist.all_reduce(errs, op=dist.ReduceOp.MAX)
-    out = {}
-    if "fused_allreduce_rmsnorm_max_err" in res:
-        out["fused_allreduce_rmsnorm_max_err"] = round(errs[0].item(), 5)
-    if "nvls_gemm_allreduce_rmsnorm_max_err" in res:
-        out["nvls_gemm_allreduce_rmsnorm_max_err"] = round(errs[1].item(), 5)
-    out["reference"] = "NCCL all-reduce + fused_add_rms_norm kernel, [64, hidden] bf16, max over ranks"
+    out = {k: round(errs[i].item(), 5) for i, k in enumerate(keys) if k in res}
+    out["reference"] = ("NCCL all-reduce + fused_add_rms_norm kernel, [64, hidden] bf16; SP boundary: cuBLAS + "
+                        "NCCL all-reduce, norm of this rank's rows, NCCL all-gather, [2048, hidden]; max over ranks")
     return out
 
 

@@ -347,3 +347,111 @@ def test_gemm_allreduce_two_gpus():
         for kind, e, mag in errs:
             # bf16 outputs; the fp32 sums of the GEMM arrive in a different order than NCCL's
             assert e <= 0.02 * max(1.0, mag), f"rank {rank} {kind}: max err {e} (magnitude {mag})"
+
+
+def _sp_worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        import torch.distributed as dist
+
+        from vllm_neuron_b200 import ops
+        from vllm_neuron_b200.parallel import state as ps
+        from vllm_neuron_b200.parallel.communicator import attach_sp_communicator
+
+        torch.cuda.set_device(rank)
+        ps.init_distributed_environment(world, rank, backend="nccl", local_rank=rank, timeout_s=120)
+        st = ps.initialize_parallel_state(tp=world, backend="nccl", timeout_s=120)
+        dev = torch.device("cuda", rank)
+        H, K = 2880, 512
+        attach_sp_communicator(st, dev, 4096, H)
+        sc = st.tp.sp_comm
+        assert sc is not None
+        errs = []
+        for call, T in enumerate([64, 2, 2048, 6, 4096, 128]):
+            Ts = T // world
+            rows = slice(rank * Ts, (rank + 1) * Ts)
+            torch.manual_seed(300 + call * 7 + rank)  # per-rank partials
+            a = torch.randn(T, K, device=dev).bfloat16()
+            wgt = (torch.randn(H, K, device=dev) * 0.05).bfloat16()
+            x = ops.linear(a, wgt)
+            torch.manual_seed(900 + call)  # residual, norm weight, bias: the same on every rank
+            res = torch.randn(T, H, device=dev).bfloat16()
+            w = torch.rand(H, device=dev) + 0.5
+            bias = (torch.randn(H, device=dev) * 0.1).bfloat16()
+            # unfused reference: NCCL sum, bias, residual add + RMSNorm of my rows, all-gather
+            ref = x.float().clone()
+            dist.all_reduce(ref)
+            want_res = res[rows].clone()
+            want, want_res = ops.fused_add_rms_norm(ref[rows].bfloat16() + bias, want_res, w, 1e-5)
+            want_full = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
+            dist.all_gather_into_tensor(want_full, want.contiguous())
+            r1 = res[rows].clone()
+            out1 = sc.boundary(x, T, r1, w, 1e-5, bias).clone()
+            errs.append(("sp_norm", (out1.float() - want_full.float()).abs().max().item()))
+            errs.append(("sp_res", (r1.float() - want_res.float()).abs().max().item()))
+            # GEMM -> reduce-scatter fused: the GEMM stores its rows in the owners' receive areas
+            r2 = res[rows].clone()
+            ops.linear_scatter(a, wgt, sc.scatter_targets(T, H), H)
+            out2 = sc.boundary(None, T, r2, w, 1e-5, bias).clone()
+            errs.append(("sp_scatter", max((out2.float() - out1.float()).abs().max().item(),
+                                           (r2.float() - r1.float()).abs().max().item())))
+            # MoE boundary: the route sum inside the kernel == the route-sum kernel, then the boundary
+            k, E_local, e_off = 4, 8, 8 * rank
+            ids = torch.randint(0, 8 * world, (T, k), device=dev, dtype=torch.int32)
+            yr = torch.randn(T * k, H, device=dev).bfloat16()
+            summed = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
+            torch.ops.b200.moe_route_sum(summed, yr, ids, E_local, e_off)
+            r3, r4 = res[rows].clone(), res[rows].clone()
+            o3 = sc.boundary(summed, T, r3, w, 1e-5).clone()
+            o4 = sc.boundary(yr, T, r4, w, 1e-5, None, (ids, E_local, e_off)).clone()
+            errs.append(("sp_routes", max((o3.float() - o4.float()).abs().max().item(),
+                                          (r3.float() - r4.float()).abs().max().item())))
+        # the output of a call stays valid through the next call (the slots alternate)
+        T = 256
+        torch.manual_seed(40 + rank)
+        xa, xb = torch.randn(T, H, device=dev).bfloat16(), torch.randn(T, H, device=dev).bfloat16()
+        torch.manual_seed(41)
+        res = torch.randn(T // world, H, device=dev).bfloat16()
+        w = torch.rand(H, device=dev) + 0.5
+        oa = sc.boundary(xa, T, res.clone(), w, 1e-5)
+        keep = oa.clone()
+        sc.boundary(xb, T, res.clone(), w, 1e-5)
+        errs.append(("sp_alive", float(not torch.equal(oa, keep))))
+        # deterministic replay: the same inputs twice give bit-identical outputs
+        runs = [sc.boundary(xa, T, res.clone(), w, 1e-5).clone() for _ in range(2)]
+        errs.append(("sp_replay", float(not torch.equal(runs[0], runs[1]))))
+        errs.append(("sp_canary", float(not sc.check_canaries())))
+        st_code = int(ops.device_status(dev)[0].item())
+        ps.destroy_parallel_state()
+        dist.destroy_process_group()
+        q.put((rank, errs, st_code, None))
+    except Exception:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, [], -1, traceback.format_exc()))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_sp_boundary_two_gpus():
+    """Sequence-parallel prefill boundary (reduce-scatter + bias + residual + RMSNorm +
+    all-gather in one NVLink kernel) against NCCL + the unfused ops; the scatter GEMM and the
+    route-sum mode against the plain kernel (bit for bit)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_sp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    bad = []
+    for rank, errs, code, tb in res:
+        assert tb is None, tb
+        assert code == 0, f"rank {rank} status {code}"
+        for kind, e in errs:
+            # the scatter GEMM may split K with atomics (last-bit differences before the norm)
+            tol = {"sp_norm": 0.13, "sp_res": 0.13, "sp_scatter": 0.13}.get(kind, 0.0)
+            if e > tol:
+                bad.append(f"rank {rank} {kind} err {e}")
+    assert not bad, bad

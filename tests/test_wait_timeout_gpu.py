@@ -14,7 +14,10 @@ pytestmark = pytest.mark.gpu
 WAIT_TIMEOUT = 1002  # kWaitTimeout, csrc/common.cuh
 
 
-def test_allreduce_wait_runs_out_and_host_raises():
+@pytest.mark.parametrize("ll", [0, 1])
+def test_allreduce_wait_runs_out_and_host_raises(ll):
+    """ll=0: the wait for the peer's release flag runs out; ll=1: the polls of the peer's LL
+    units (data with the epoch inside) run out."""
     from vllm_neuron_b200.ops import check_device_status, device_status
     from vllm_neuron_b200.ops._ext import load
 
@@ -22,7 +25,7 @@ def test_allreduce_wait_runs_out_and_host_raises():
     ops = torch.ops.b200
     dev = torch.device("cuda", torch.cuda.current_device())
     T, H, world, blocks = 4, 256, 2, 4
-    slot_bytes = world * T * H * 2
+    slot_bytes = world * T * H * (4 if ll else 2)
     mine = ops.comm_alloc(slot_bytes)
     silent_peer = ops.comm_alloc(slot_bytes)  # nobody ever raises this rank's flags
     try:
@@ -33,7 +36,7 @@ def test_allreduce_wait_runs_out_and_host_raises():
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
         ops.allreduce_fused([mine, silent_peer], 0, slot_bytes, x, out, None, None, None, 0.0, blocks, status,
-                            1_000_000)
+                            1_000_000, None, 0, 0, ll)
         end.record()
         torch.cuda.synchronize()
         assert int(status[0].item()) == WAIT_TIMEOUT

@@ -4,7 +4,8 @@
     torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m vllm_neuron_b200.benchmarks.collectives --op ep
 
 ``--op ep`` times the EP all-to-all (see ``_ep``); ``--op gemm_ar`` the row-parallel GEMM
-fused with the all-reduce (see ``_gemm_ar``); the default is the layer-boundary all-reduce:
+fused with the all-reduce (see ``_gemm_ar``); ``--op sp --tokens 512,2048,4096`` the
+sequence-parallel prefill boundary (see ``_sp``); the default is the layer-boundary all-reduce:
 
 For each token count T (hidden 2880, bf16) it times, with CUDA events after warm-up and as
 the maximum over ranks:
@@ -181,9 +182,105 @@ def _gemm_ar(a, rank, world, dev, ps) -> None:
             del g
 
 
+def _sp(a, rank, world, dev, ps) -> None:
+    """Sequence-parallel prefill boundary after the row-parallel o_proj (GPT-OSS: [T, 4096 /
+    world] x [2880, 4096 / world]^T, then reduce-scatter + bias + residual + RMSNorm +
+    all-gather), CUDA graph of ``--iters`` calls, max over ranks:
+    * ``gemm_scatter+sp``: the tcgen05 GEMM stores each partial row block straight into its
+      owner's receive area (peer stores from the epilogue), then the boundary kernel reduces,
+      normalises and pushes the rows to every rank;
+    * ``gemm+sp``: the GEMM into local memory, then the boundary kernel with both push phases;
+    * ``cublas+nccl``: library GEMM, NCCL reduce-scatter, bias add, add + RMSNorm kernel, NCCL
+      all-gather (baseline);
+    * ``sp`` / ``nccl``: the collective part alone on a precomputed partial.
+    Roofline: every rank must send (world - 1) / world of the T x H bf16 partial (the
+    reduce-scatter) and of the normalised rows (the all-gather) over NVLink at 770 GB/s; with
+    the GEMM, the slower of that, the weight stream at HBM bandwidth and the MMA at the bf16 peak."""
+    import torch.nn.functional as F
+
+    from vllm_neuron_b200 import ops
+    from vllm_neuron_b200.parallel.communicator import attach_sp_communicator
+
+    tp = ps.tp
+    H, Kr = a.hidden, 4096 // world
+    toks = [int(t) for t in a.tokens.split(",")]
+    attach_sp_communicator(ps, dev, max(toks), H)
+    sc = tp.sp_comm
+    hbm, peak = 6537.0, 1667.1
+    try:
+        with open(os.path.join(os.path.dirname(__file__), "..", "..", "MEASURED_PEAKS.json")) as f:
+            mp_ = json.load(f)
+            hbm, peak = float(mp_["hbm_gbs"]), float(mp_["bf16_tflops"])
+    except (OSError, ValueError, KeyError):
+        pass
+    nw = torch.ones(H, device=dev)
+    torch.manual_seed(7 + rank)
+    W = (torch.randn(H, Kr, device=dev) * 0.02).bfloat16()
+    for T in toks:
+        Ts = T // world
+        x = torch.randn(T, Kr, device=dev).bfloat16()
+        part = ops.linear(x, W)
+        res = torch.randn(Ts, H, device=dev).bfloat16()
+        bias = torch.zeros(H, device=dev).bfloat16()
+        for path in ("gemm_scatter+sp", "gemm+sp", "cublas+nccl", "sp", "nccl"):
+            def step():
+                if path == "gemm_scatter+sp":
+                    ops.linear_scatter(x, W, sc.scatter_targets(T, H), H)
+                    return sc.boundary(None, T, res, nw, 1e-5, bias)
+                if path in ("gemm+sp", "sp"):
+                    return sc.boundary(ops.linear(x, W) if path == "gemm+sp" else part, T, res, nw, 1e-5, bias)
+                y = F.linear(x, W) if path == "cublas+nccl" else part
+                ys = torch.empty(Ts, H, device=dev, dtype=y.dtype)
+                dist.reduce_scatter_tensor(ys, y, group=tp.device_group)
+                o, _ = ops.fused_add_rms_norm(ys + bias, res, nw, 1e-5)
+                full = torch.empty(T, H, device=dev, dtype=o.dtype)
+                dist.all_gather_into_tensor(full, o, group=tp.device_group)
+                return full
+
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                for _ in range(3):
+                    step()
+            torch.cuda.current_stream().wait_stream(s)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(a.iters):
+                    step()
+            for _ in range(3):
+                g.replay()
+            dist.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            t = torch.tensor([e0.elapsed_time(e1) * 1000.0 / a.iters], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            us = t.item()
+            link_bytes = 2 * (world - 1) * Ts * H * 2
+            t_link = link_bytes / (LINK_GBS * 1e3)
+            gemm = path not in ("sp", "nccl")
+            t_hbm = H * Kr * 2 / (hbm * 1e3) if gemm else 0.0
+            t_mma = 2.0 * T * H * Kr / (peak * 1e6) if gemm else 0.0
+            target = max(t_link, t_hbm, t_mma)
+            if rank == 0:
+                print(json.dumps({"op": "sp_boundary", "path": path, "world": world, "T": T, "H": H,
+                                  "K_per_rank": Kr, "us": round(us, 2), "nvlink_bytes_per_rank": link_bytes,
+                                  "target_us": round(target, 2),
+                                  "bound": ["nvlink", "hbm", "mma"][[t_link, t_hbm, t_mma].index(target)],
+                                  "frac_of_roofline": round(target / us, 3)}), flush=True)
+            del g
+    ok = sc.check_canaries()
+    if rank == 0:
+        print(json.dumps({"op": "sp_boundary", "guards_intact": ok}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", choices=["allreduce", "ep", "gemm_ar"], default="allreduce")
+    ap.add_argument("--op", choices=["allreduce", "ep", "gemm_ar", "sp"], default="allreduce")
     ap.add_argument("--hidden", type=int, default=2880)
     ap.add_argument("--tokens", default="1,16,64,256")
     ap.add_argument("--experts", type=int, default=128)
@@ -201,6 +298,12 @@ def main() -> None:
     ps = pstate.initialize_parallel_state(tp=world, timeout_s=120)
     if a.op == "ep":
         _ep(a, rank, world, dev, ps)
+        torch.cuda.synchronize()
+        pstate.destroy_parallel_state()
+        dist.destroy_process_group()
+        return
+    if a.op == "sp":
+        _sp(a, rank, world, dev, ps)
         torch.cuda.synchronize()
         pstate.destroy_parallel_state()
         dist.destroy_process_group()

@@ -13,7 +13,11 @@ int b200_ipc_close(void* p);
 int b200_allreduce_fused(void* const* bases, int rank, int world, size_t slot_bytes, const void* in, void* out,
                          void* residual, const void* bias, const float* w, float eps, int T, int H, int num_blocks,
                          unsigned long long wait_ns, int* status, cudaStream_t s, const int* topk_ids, int k,
-                         int E_local, int eoff);
+                         int E_local, int eoff, int ll);
+int b200_sp_boundary(void* const* bases, int rank, int world, size_t slot_bytes, size_t area_bytes, size_t guard_bytes,
+                     int slot, const void* in, void* residual, const void* bias, const float* w, float eps, int T, int H,
+                     int num_blocks, unsigned long long wait_ns, int* status, cudaStream_t s, const int* topk_ids,
+                     int k, int E_local, int eoff);
 int b200_kv_export(void* dst, const int64_t* kptr, const int64_t* vptr, int n_layers, const int* blocks, int T, int nh,
                    int row_bytes, int bs, cudaStream_t s);
 int b200_kv_import(const void* const* part_base, const int* part_h0, const int* part_nh, int n_parts,
@@ -73,7 +77,7 @@ void ipc_close(int64_t p) { b200_ipc_close(reinterpret_cast<void*>(p)); }
 void allreduce_fused(at::IntArrayRef bases, int64_t rank, int64_t slot_bytes, Tensor input, Tensor out,
                      c10::optional<Tensor> residual, c10::optional<Tensor> bias, c10::optional<Tensor> w, double eps,
                      int64_t num_blocks, c10::optional<Tensor> status, int64_t wait_ns,
-                     c10::optional<Tensor> topk_ids, int64_t e_local, int64_t e_off) {
+                     c10::optional<Tensor> topk_ids, int64_t e_local, int64_t e_off, int64_t ll) {
   TORCH_CHECK(input.is_cuda() && input.scalar_type() == at::kBFloat16 && input.is_contiguous(), "bf16 input");
   TORCH_CHECK(out.is_contiguous() && out.scalar_type() == at::kBFloat16, "bf16 out");
   TORCH_CHECK(bases.size() >= 1 && bases.size() <= 8, "1..8 ranks");
@@ -102,9 +106,60 @@ void allreduce_fused(at::IntArrayRef bases, int64_t rank, int64_t slot_bytes, Te
       w.has_value() ? w->data_ptr<float>() : nullptr, (float)eps, T, H, num_blocks,
       wait_ns > 0 ? (unsigned long long)wait_ns : 0ull, status.has_value() ? status->data_ptr<int>() : nullptr,
       at::cuda::getCurrentCUDAStream().stream(), topk_ids.has_value() ? topk_ids->data_ptr<int>() : nullptr, k,
-      (int)e_local, (int)e_off);
+      (int)e_local, (int)e_off, (int)ll);
   TORCH_CHECK(rc == 0, "b200::allreduce_fused failed with code ", rc);
 }
+// Sequence-parallel layer boundary (csrc/comm.cu, sp_boundary_kernel); the output is the AG
+// area of `slot` (read through comm_view).  input: [T, H] partial, [T * k, H] route rows with
+// topk_ids, or None when gemm_scatter has stored the partial rows already.
+void sp_boundary(at::IntArrayRef bases, int64_t rank, int64_t slot_bytes, int64_t area_bytes, int64_t guard_bytes,
+                 int64_t slot, c10::optional<Tensor> input, Tensor residual, c10::optional<Tensor> bias, Tensor w,
+                 double eps, int64_t T, int64_t num_blocks, c10::optional<Tensor> status, int64_t wait_ns,
+                 c10::optional<Tensor> topk_ids, int64_t e_local, int64_t e_off) {
+  const int world = bases.size();
+  TORCH_CHECK(world >= 1 && world <= 8, "1..8 ranks");
+  TORCH_CHECK(residual.is_cuda() && residual.scalar_type() == at::kBFloat16 && residual.is_contiguous() &&
+                  residual.dim() == 2 && residual.size(0) * world == T,
+              "residual: this rank's contiguous bf16 [T / world, H] rows");
+  const int H = residual.size(1);
+  TORCH_CHECK(w.scalar_type() == at::kFloat && w.numel() == H, "norm weight fp32 [H]");
+  if (bias.has_value())
+    TORCH_CHECK(bias->scalar_type() == at::kBFloat16 && bias->numel() == H && bias->is_contiguous(), "bias [H] bf16");
+  int k = 0;
+  if (input.has_value()) {
+    TORCH_CHECK(input->scalar_type() == at::kBFloat16 && input->is_contiguous() && input->size(-1) == H, "bf16 input");
+    if (topk_ids.has_value()) {
+      TORCH_CHECK(topk_ids->scalar_type() == at::kInt && topk_ids->is_contiguous() && topk_ids->dim() == 2 &&
+                      topk_ids->size(0) == T,
+                  "topk_ids: contiguous int32 [T, k]");
+      k = topk_ids->size(1);
+      TORCH_CHECK(input->numel() == (int64_t)T * k * H, "route rows must be [T * k, H]");
+    } else {
+      TORCH_CHECK(input->numel() == T * H, "input must be [T, H]");
+    }
+  } else {
+    TORCH_CHECK(!topk_ids.has_value(), "route mode needs the route rows");
+  }
+  void* ptrs[8];
+  for (int i = 0; i < world; ++i) ptrs[i] = reinterpret_cast<void*>(bases[i]);
+  c10::cuda::CUDAGuard g(residual.device());
+  const int rc = b200_sp_boundary(
+      ptrs, rank, world, (size_t)slot_bytes, (size_t)area_bytes, (size_t)guard_bytes, slot,
+      input.has_value() ? input->data_ptr() : nullptr, residual.data_ptr(), bias.has_value() ? bias->data_ptr() : nullptr,
+      w.data_ptr<float>(), (float)eps, T, H, num_blocks, wait_ns > 0 ? (unsigned long long)wait_ns : 0ull,
+      status.has_value() ? status->data_ptr<int>() : nullptr, at::cuda::getCurrentCUDAStream().stream(),
+      topk_ids.has_value() ? topk_ids->data_ptr<int>() : nullptr, k, (int)e_local, (int)e_off);
+  TORCH_CHECK(rc == 0, "b200::sp_boundary failed with code ", rc);
+}
+
+// A bf16 [rows, cols] tensor over device memory this library owns (a communicator region), on
+// the device of `like`; the region outlives every view the communicator hands out.
+Tensor comm_view(int64_t ptr, int64_t rows, int64_t cols, Tensor like) {
+  TORCH_CHECK(like.is_cuda(), "comm_view: a CUDA tensor gives the device");
+  return at::from_blob(reinterpret_cast<void*>(ptr), {rows, cols},
+                       at::TensorOptions().dtype(at::kBFloat16).device(like.device()));
+}
+
 void kv_export(int64_t dst, Tensor kptr, Tensor vptr, Tensor blocks, int64_t num_tokens, int64_t nh,
                int64_t row_bytes, int64_t bs) {
   TORCH_CHECK(kptr.is_cuda() && kptr.scalar_type() == at::kLong && vptr.scalar_type() == at::kLong &&
@@ -193,6 +248,11 @@ void ep_combine(at::IntArrayRef bases, int64_t rank, int64_t slot_bytes, int64_t
 
 void register_comm_ops(torch::Library& m) {
   m.def("comm_alloc(int slot_bytes) -> int");
+  m.def(
+      "sp_boundary(int[] bases, int rank, int slot_bytes, int area_bytes, int guard_bytes, int slot, Tensor? input, "
+      "Tensor(a!) residual, Tensor? bias, Tensor w, float eps, int T, int num_blocks, Tensor? status, int wait_ns=0, "
+      "Tensor? topk_ids=None, int e_local=0, int e_off=0) -> ()");
+  m.def("comm_view(int ptr, int rows, int cols, Tensor like) -> Tensor");
   m.def("comm_free(int ptr) -> ()");
   m.def("device_fill(int ptr, int nbytes, int value) -> ()");
   m.def("device_read(int ptr, int nbytes) -> Tensor");
@@ -202,7 +262,7 @@ void register_comm_ops(torch::Library& m) {
   m.def(
       "allreduce_fused(int[] bases, int rank, int slot_bytes, Tensor input, Tensor(a!) out, Tensor(b!)? residual, "
       "Tensor? bias, Tensor? w, float eps, int num_blocks, Tensor? status, int wait_ns=0, Tensor? topk_ids=None, "
-      "int e_local=0, int e_off=0) -> ()");
+      "int e_local=0, int e_off=0, int ll=0) -> ()");
   m.def(
       "ep_dispatch(int[] bases, int rank, int slot_bytes, int cpd, int Tc, int E_local, int t_begin, int t_end, "
       "Tensor x, Tensor ids, Tensor w, Tensor(a!) x_recv, Tensor(b!) ids_recv, Tensor(c!) w_recv, "
@@ -220,6 +280,8 @@ void register_comm_ops(torch::Library& m) {
 
 void register_comm_impls(torch::Library& m) {
   m.impl("allreduce_fused", &allreduce_fused);
+  m.impl("sp_boundary", &sp_boundary);
+  m.impl("comm_view", &comm_view);
   m.impl("ep_dispatch", &ep_dispatch);
   m.impl("ep_combine", &ep_combine);
   m.impl("kv_export", &kv_export);

@@ -92,6 +92,11 @@ struct Args {
   uint8_t* red_uc;            // kReduce: this rank's region (unicast)
   uint8_t* red_mc;            // kReduce: multicast mapping of the region (null: local atomics)
   int H_cap, T_cap;           // kReduce accumulator geometry (row stride H_cap)
+  // kStore scatter (dst_rows > 0): token row t goes to ydst[t / dst_rows] at row t % dst_rows
+  // (row stride ldy, bf16), e.g. the reduce-scatter receive areas of a sequence-parallel
+  // boundary on the peer GPUs (plain 16-byte stores over NVLink)
+  uint8_t* ydst[8];
+  int dst_rows;
   int* status;
   // optional per-CTA timeline (%globaltimer ns, 8 slots per CTA) for latency analysis:
   // entry, setup done, first TMA issued, first MMA issued, first accumulator ready, first
@@ -139,7 +144,14 @@ B200_D void store8(const Args& a, int t, int f, const float* v) {
     __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&u);
 #pragma unroll
     for (int h = 0; h < 4; ++h) ob[h] = __floats2bfloat162_rn(o[2 * h], o[2 * h + 1]);
-    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.y) + (size_t)t * a.ldy + f) = u;
+    __nv_bfloat16* yrow;
+    if (a.dst_rows > 0) {
+      const int q = t / a.dst_rows;
+      yrow = reinterpret_cast<__nv_bfloat16*>(a.ydst[q]) + (size_t)(t - q * a.dst_rows) * a.ldy;
+    } else {
+      yrow = static_cast<__nv_bfloat16*>(a.y) + (size_t)t * a.ldy;
+    }
+    *reinterpret_cast<uint4*>(yrow + f) = u;
   }
 }
 
@@ -502,6 +514,9 @@ __global__ void __launch_bounds__(256, 1) gemm_kernel(const __grid_constant__ CU
       if (ew == 0 && lane == 0) stamp(a, local == 0 ? 5 : 6);
       ++local;
     }
+    // scattered rows may sit in other GPUs' memory: complete them at system scope before the
+    // kernel ends (the collective that follows releases its flags after this kernel)
+    if (a.dst_rows > 0) __threadfence_system();
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -671,11 +686,21 @@ static Plan make_plan(int T, int N, int K, int max_splits, bool allow_cluster = 
   Plan p;
   p.nt = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
   p.m_tiles = cdiv(N, kBM);
+  const int sms = sm_count();
+  // Wide token tiles that leave SMs idle (fewer tiles than SMs): halve the tile while that
+  // lowers the busiest SM's share (waves x tile width); K is split only after that, since a
+  // split of a wide tile reduces through global atomics.  A projection of a 512-token prefill
+  // chunk at N = 2880 thus runs 92 tiles of 128 tokens instead of 46 tiles split three ways.
+  while (p.nt > 64 && p.m_tiles * cdiv(T, p.nt) < sms) {
+    const int half = p.nt / 2;
+    if ((long long)cdiv(p.m_tiles * cdiv(T, half), sms) * half >= (long long)cdiv(p.m_tiles * cdiv(T, p.nt), sms) * p.nt)
+      break;
+    p.nt = half;
+  }
   p.n_tiles = cdiv(T, p.nt);
   p.k_stages = cdiv(K, f8 ? 2 * kBK : kBK);
   p.cluster = false;
   const int tiles = p.m_tiles * p.n_tiles;
-  const int sms = sm_count();
   int splits = 1;
   if (p.nt <= 64 && allow_cluster && max_splits > 1) {
     double best = (double)cdiv(tiles, sms) * (p.k_stages + 1.0);
@@ -847,6 +872,37 @@ extern "C" int b200_gemm_fp8(void* y, int ldy, int out_f32, const void* x, int l
     a.counters = counters;
   }
   return dispatch<kStore, true>(p, x, ldx, w, a, s);
+}
+
+// Y = X . W^T (bf16, no bias) with token row t stored at dst[t / (T / n_dst)] + (t % (T / n_dst))
+// rows of ldd elements: the producer of a reduce-scatter writes every row block straight into
+// its owner's receive area (n_dst ranks, T % n_dst == 0; dst pointers may be peer memory,
+// which only the epilogue's plain stores touch).  Workspace as b200_gemm_bf16.
+extern "C" int b200_gemm_bf16_scatter(void* const* dst, int n_dst, int ldd, const void* x, int ldx, const void* w,
+                                      int T, int N, int K, float* ws, int64_t ws_floats, int* counters,
+                                      int64_t n_counters, int max_splits, int* status, cudaStream_t s) {
+  int rc = check_common(x, ldx, w, T, N, K);
+  if (rc) return rc;
+  if (n_dst < 1 || n_dst > 8 || T % n_dst || ldd % 8 || ldd < N || N % 8) return kBadShape;
+  for (int q = 0; q < n_dst; ++q)
+    if (dst[q] == nullptr || misaligned_host(dst[q])) return kBadAlignment;
+  if (T == 0) return 0;
+  const Plan p = make_plan(T, N, K, max_splits);
+  Args a{};
+  a.T = T, a.N = N, a.K = K, a.ldy = ldd;
+  a.m_tiles = p.m_tiles, a.n_tiles = p.n_tiles, a.splits = p.splits, a.k_stages = p.k_stages, a.sps = p.sps;
+  a.y = dst[0];
+  for (int q = 0; q < n_dst; ++q) a.ydst[q] = static_cast<uint8_t*>(dst[q]);
+  a.dst_rows = T / n_dst;
+  a.status = status;
+  if (p.splits > 1 && !p.cluster) {
+    const int64_t tiles = (int64_t)p.m_tiles * p.n_tiles;
+    if (ws == nullptr || counters == nullptr || ws_floats < (int64_t)T * N || n_counters < 4 * tiles)
+      return kScratchTooSmall;
+    a.ws = ws;
+    a.counters = counters;
+  }
+  return dispatch<kStore>(p, x, ldx, w, a, s);
 }
 
 extern "C" size_t b200_red_region_bytes(int T_cap, int H_cap) { return red_region_bytes(T_cap, H_cap); }

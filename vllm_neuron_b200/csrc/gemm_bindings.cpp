@@ -9,6 +9,9 @@ void b200_gemm_workspace(int T, int N, int K, int max_splits, int64_t* ws_floats
 int b200_gemm_bf16(void* y, int ldy, int out_f32, const void* x, int ldx, const void* w, const void* bias, int T,
                    int N, int K, float* ws, int64_t ws_floats, int* counters, int64_t n_counters, int max_splits,
                    int* status, cudaStream_t s);
+int b200_gemm_bf16_scatter(void* const* dst, int n_dst, int ldd, const void* x, int ldx, const void* w, int T, int N,
+                           int K, float* ws, int64_t ws_floats, int* counters, int64_t n_counters, int max_splits,
+                           int* status, cudaStream_t s);
 int b200_gemm_fp8(void* y, int ldy, int out_f32, const void* x, int ldx, const void* w, const void* bias,
                   const float* alpha, int alpha_n, int T, int N, int K, float* ws, int64_t ws_floats, int* counters,
                   int64_t n_counters, int max_splits, int* status, cudaStream_t s);
@@ -59,6 +62,24 @@ void gemm_bf16(Tensor y, Tensor x, Tensor w, c10::optional<Tensor> bias, Tensor 
                                 status.has_value() ? status->data_ptr<int>() : nullptr,
                                 at::cuda::getCurrentCUDAStream().stream());
   TORCH_CHECK(rc == 0, "b200::gemm_bf16 failed with code ", rc);
+}
+
+// Y = X . W^T with row block q (T / len(dst) rows) stored at the device address dst[q] (rows of
+// ldd elements): the producer side of a sequence-parallel reduce-scatter.
+void gemm_scatter(at::IntArrayRef dst, int64_t ldd, Tensor x, Tensor w, Tensor ws, Tensor counters,
+                  int64_t max_splits, c10::optional<Tensor> status) {
+  check_x_w(x, w);
+  const int T = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(dst.size() >= 1 && dst.size() <= 8, "gemm_scatter: 1..8 destinations");
+  TORCH_CHECK(ws.scalar_type() == at::kFloat && counters.scalar_type() == at::kInt, "gemm: workspace dtypes");
+  void* ptrs[8];
+  for (size_t i = 0; i < dst.size(); ++i) ptrs[i] = reinterpret_cast<void*>(dst[i]);
+  c10::cuda::CUDAGuard g(x.device());
+  const int rc = b200_gemm_bf16_scatter(ptrs, dst.size(), ldd, x.data_ptr(), x.stride(0), w.data_ptr(), T, N, K,
+                                        ws.data_ptr<float>(), ws.numel(), counters.data_ptr<int>(), counters.numel(),
+                                        max_splits, status.has_value() ? status->data_ptr<int>() : nullptr,
+                                        at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(rc == 0, "b200::gemm_scatter failed with code ", rc);
 }
 
 void gemm_fp8(Tensor y, Tensor x, Tensor w, c10::optional<Tensor> bias, Tensor alpha, Tensor ws, Tensor counters,
@@ -180,6 +201,9 @@ void register_gemm_ops(torch::Library& m) {
       "gemm_bf16(Tensor(a!) y, Tensor x, Tensor w, Tensor? bias, Tensor(b!) ws, Tensor(c!) counters, "
       "int max_splits, Tensor? status) -> ()");
   m.def(
+      "gemm_scatter(int[] dst, int ldd, Tensor x, Tensor w, Tensor(a!) ws, Tensor(b!) counters, int max_splits, "
+      "Tensor? status) -> ()");
+  m.def(
       "gemm_fp8(Tensor(a!) y, Tensor x, Tensor w, Tensor? bias, Tensor alpha, Tensor(b!) ws, Tensor(c!) counters, "
       "int max_splits, Tensor? status) -> ()");
   m.def(
@@ -198,6 +222,7 @@ void register_gemm_ops(torch::Library& m) {
 void register_gemm_impls(torch::Library& m) {
   m.impl("gemm_bf16", &gemm_bf16);
   m.impl("gemm_fp8", &gemm_fp8);
+  m.impl("gemm_scatter", &gemm_scatter);
   m.impl("fp8_quant", &fp8_quant);
   m.impl("rms_norm_fp8", &rms_norm_fp8);
   m.impl("gemm_bf16_allreduce", &gemm_bf16_allreduce);

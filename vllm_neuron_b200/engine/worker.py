@@ -96,6 +96,11 @@ class Worker:
         t0 = time.time()
         torch.manual_seed(self.cfg.seed)
         model, mcfg, hf = build_model(self.cfg, self.ps, self.device)
+        if (self.device.type == "cuda" and self.world_size > 1 and envs.VLLM_B200_FUSED_COLLECTIVES
+                and hasattr(mcfg, "hidden_size")):
+            from ..parallel.communicator import attach_sp_communicator
+
+            attach_sp_communicator(self.ps, self.device, self.cfg.max_num_batched_tokens, mcfg.hidden_size)
         if self.cfg.load_format == "dummy" or self.cfg.model is None:
             if self.device.type == "cuda":
                 random_init_device_(model, self.cfg.seed)

@@ -63,7 +63,14 @@ _REGISTRY: dict[str, tuple[Callable[[str], Any], str | None, str | None]] = {
     # Row-parallel GEMMs reduce their output tiles through NVSwitch (multimem) when the group
     # has a multicast object (else the GEMM and the fused all-reduce kernel run separately).
     "VLLM_B200_GEMM_ALLREDUCE": (_bool, "0", None),
+    # The decode all-reduce kernel sends LL units (data with the call's epoch in every 16-byte
+    # store) instead of data + one release flag per peer.
+    "VLLM_B200_AR_LL": (_bool, "1", None),
+    # The MoE layer's per-token route sum runs inside the layer-boundary collective kernel.
     "VLLM_B200_FUSE_MOE_ROUTE_SUM": (_bool, "1", None),
+    # Sequence-parallel prefill boundaries as one NVLink kernel (reduce-scatter + norm +
+    # all-gather), fed by the row-parallel GEMM's scattered stores (else NCCL + the norm).
+    "VLLM_B200_FUSED_SP": (_bool, "1", None),
     # Sliding-window layers keep their own KV block pool (blocks behind the window are freed).
     "VLLM_B200_SWA_KV_GROUP": (_bool, "1", None),
     # Dense layers through the library GEMM (torch / cuBLAS) instead of the tcgen05 kernel:

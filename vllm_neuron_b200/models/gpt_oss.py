@@ -349,10 +349,14 @@ class GptOssMLP(nn.Module):
         return self.dp.reduce_scatter(y, dim=0) if self.dp.world_size > 1 else y
 
     def _defer_route_sum(self, x: torch.Tensor) -> bool:
+        if not (envs.VLLM_B200_FUSE_MOE_ROUTE_SUM and x.is_cuda and self.dp.world_size == 1
+                and self.tp.world_size > 1 and self.experts.quant == "mxfp4"):
+            return False
+        if self.tp.sp_active:  # the SP boundary kernel sums the routes while it scatters
+            sc = self.tp.sp_comm
+            return sc is not None and sc.can(x.shape[0], x.shape[1])
         comm = self.tp.communicator
-        return (envs.VLLM_B200_FUSE_MOE_ROUTE_SUM and x.is_cuda and self.dp.world_size == 1
-                and self.tp.world_size > 1 and comm is not None and not self.tp.sp_active
-                and self.experts.quant == "mxfp4" and comm.can_all_reduce(x))
+        return comm is not None and comm.can_all_reduce(x)
 
 
 class GptOssDecoderLayer(nn.Module):

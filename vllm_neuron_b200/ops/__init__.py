@@ -103,6 +103,25 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None,
     return y.to(out_dtype) if out_dtype is not None else y
 
 
+def gemm_available(x: torch.Tensor, w: torch.Tensor) -> bool:
+    """The bf16 tcgen05 GEMM takes these operands (``linear`` would not fall back to torch)."""
+    return x.dtype == torch.bfloat16 and _gemm_ok(x, w)
+
+
+def linear_scatter(x: torch.Tensor, w: torch.Tensor, dst: list[int], ldd: int) -> None:
+    """x . w^T (bf16, no bias) with the rows split into ``len(dst)`` equal blocks, block q
+    stored from device address ``dst[q]`` with a row stride of ``ldd`` elements: the tcgen05
+    GEMM of ``csrc/gemm.cu`` writing a sequence-parallel reduce-scatter's partial rows straight
+    into their owners' receive areas (peer memory, plain stores from the epilogue)."""
+    if not _gemm_ok(x, w) or x.dtype != torch.bfloat16:
+        raise RuntimeError("linear_scatter needs the bf16 tcgen05 GEMM")
+    x2 = x.reshape(-1, w.shape[1])
+    if x2.stride(1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    ws, cnt = _gemm_workspace(x.device)
+    _k().gemm_scatter(list(dst), ldd, x2, w, ws, cnt, _GEMM_MAX_SPLITS, device_status(x.device))
+
+
 def linear_fp8(x: torch.Tensor, w_fp8: torch.Tensor, w_scale: torch.Tensor, in_scale: torch.Tensor | None,
                b: torch.Tensor | None = None, x_q: torch.Tensor | None = None,
                alpha: torch.Tensor | None = None, out_dtype: torch.dtype | None = None) -> torch.Tensor:

@@ -171,6 +171,7 @@ class GroupCoordinator:
     rank: int = 0
     communicator: Any = None  # fused NVLink collectives (parallel.communicator)
     reducer: Any = None  # GEMM fused with the all-reduce through NVSwitch (parallel.communicator)
+    sp_comm: Any = None  # sequence-parallel prefill boundary over NVLink (parallel.communicator)
     sp_active: bool = False  # sequence parallelism at layer boundaries (set per prefill step)
 
     @property
@@ -203,6 +204,9 @@ class GroupCoordinator:
 
         if isinstance(x, RoutePartial):
             comm = self.communicator
+            T = x.shape[0]
+            if self.sp_active and self.world_size > 1 and self.sp_comm is not None and self.sp_comm.can(T, x.shape[1]):
+                return self._sp_boundary(x.y, T, residual, w, eps, bias, (x.topk_ids, x.e_local, x.e_off))
             if (self.world_size > 1 and comm is not None and not self.sp_active
                     and comm.can_all_reduce(residual)):
                 return comm.all_reduce_routes_add_rmsnorm(x.y, x.topk_ids, x.e_local, x.e_off, residual, w, eps, bias)
@@ -229,16 +233,34 @@ class GroupCoordinator:
         if (self.world_size > 1 and not self.sp_active and self.reducer is not None
                 and self.reducer.can(x, weight)):
             return self.reducer.linear_add_rmsnorm(x, weight, residual, w, eps, bias)
+        sc = self.sp_comm
+        T = x.shape[0] if x.dim() == 2 else -1
+        if (self.sp_active and self.world_size > 1 and sc is not None and sc.can(T, weight.shape[0])
+                and ops.gemm_available(x, weight)):
+            # GEMM -> reduce-scatter fused: the GEMM stores each partial row block in its
+            # owner's receive area; the boundary kernel reduces, normalises and all-gathers
+            ops.linear_scatter(x, weight, sc.scatter_targets(T, weight.shape[0]), weight.shape[0])
+            return self._sp_boundary(None, T, residual, w, eps, bias)
         return self.all_reduce_add_rmsnorm(ops.linear(x, weight, None), residual, w, eps, bias)
+
+    def _sp_boundary(self, x, T, residual, w, eps, bias, routes=None):
+        """The SP boundary in one NVLink kernel (``SpCommunicator.boundary``); the residual
+        becomes this rank's T / tp rows at the first boundary."""
+        if residual.shape[0] == T:  # first boundary after the (replicated) embedding
+            residual = residual.chunk(self.world_size, dim=0)[self.rank_in_group].contiguous()
+        return self.sp_comm.boundary(x, T, residual, w, eps, bias, routes), residual
 
     def _sp_add_rmsnorm(self, x, residual, w, eps, bias):
         """Sequence-parallel layer boundary (prefill): reduce-scatter the partial sums over
         tokens, add bias and this rank's residual rows, normalise the shard, all-gather the
         normalised rows for the next GEMM.  The residual stays sharded (T / tp rows)
-        between boundaries (``model_mxfp4.py:464,685``: AG before, RS after each block)."""
+        between boundaries (``model_mxfp4.py:464,685``: AG before, RS after each block).
+        One NVLink kernel when an ``SpCommunicator`` is attached, else NCCL + the norm."""
         from .. import ops
 
         T = x.shape[0]
+        if self.sp_comm is not None and x.is_cuda and x.dtype == torch.bfloat16 and self.sp_comm.can(T, x.shape[-1]):
+            return self._sp_boundary(x.contiguous(), T, residual, w, eps, bias)
         xs = self.reduce_scatter(x, dim=0)
         if residual.shape[0] == T:  # first boundary after the (replicated) embedding
             residual = residual.chunk(self.world_size, dim=0)[self.rank_in_group].contiguous()
@@ -615,5 +637,8 @@ def destroy_parallel_state() -> None:
             if isinstance(g, GroupCoordinator) and g.reducer is not None and id(g.reducer) not in seen:
                 seen.add(id(g.reducer))
                 g.reducer.close()
+            if isinstance(g, GroupCoordinator) and g.sp_comm is not None and id(g.sp_comm) not in seen:
+                seen.add(id(g.sp_comm))
+                g.sp_comm.close()
     _STATE = None
     _ALL_PGS.clear()
