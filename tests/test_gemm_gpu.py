@@ -29,7 +29,9 @@ def _close(got, want, what):
 
 @pytest.mark.parametrize("T,N,K", [(1, 128, 64), (5, 640, 2880), (16, 2880, 512), (33, 5120, 2880),
                                    (64, 2880, 4096), (64, 25136, 2880), (100, 1000, 360), (300, 2048, 1024),
-                                   (2048, 2880, 2880), (130, 136, 4104)])
+                                   (2048, 2880, 2880), (130, 136, 4104),
+                                   # token tiles of 160 / 224 / 192 from the wave-balancing planner
+                                   (900, 2880, 1024), (1200, 2880, 512), (1500, 2048, 640)])
 def test_gemm_matches_fp32(T, N, K):
     from vllm_neuron_b200 import ops
 

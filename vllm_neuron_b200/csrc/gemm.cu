@@ -34,6 +34,7 @@
 //     plain global atomics on the local accumulator.  No TMA and no library kernel ever
 //     touches another GPU's memory; the only cross-GPU traffic is multimem reductions.
 #include <algorithm>
+#include <cstdlib>
 
 #include "launch.h"
 #include "launch_pdl.h"
@@ -51,7 +52,7 @@ template <int NT, bool CL>
 struct Cfg {
   static constexpr int kA = kBM * kBK * 2;  // 16 KB
   static constexpr int kB = NT * kBK * 2;
-  static constexpr int kStages = CL ? (NT >= 64 ? 6 : 8) : (NT <= 64 ? 8 : (NT == 128 ? 6 : 4));
+  static constexpr int kStages = CL ? (NT >= 64 ? 6 : 8) : (NT <= 64 ? 8 : NT == 128 ? 6 : NT <= 192 ? 5 : 4);
   static constexpr int kStage = kA + kB;
   static constexpr int kOffEpi = kStages * kStage;
   static constexpr int kEpiBytes = 4 * 16 * 36 * 4;  // per epilogue warp: 16 tokens x 36 floats
@@ -678,6 +679,24 @@ struct Plan {
   bool cluster;  // the K splits of a tile are one thread-block cluster (DSMEM reduction)
 };
 
+// A forced token tile width for non-cluster plans (tile-size measurements): VLLM_B200_GEMM_NT
+// at the first call, or b200_gemm_force_nt; 0 = the planner's choice.
+static int g_forced_nt = -1;
+static int valid_nt(int v) {
+  return (v == 16 || v == 32 || v == 64 || v == 128 || v == 160 || v == 192 || v == 224 || v == 256) ? v : 0;
+}
+static int forced_nt() {
+  if (g_forced_nt < 0) {
+    const char* e = std::getenv("VLLM_B200_GEMM_NT");
+    g_forced_nt = valid_nt(e != nullptr ? std::atoi(e) : 0);
+  }
+  return g_forced_nt;
+}
+
+// Relative cost of one token of a tile of width nt against a 256-wide tile (the per-tile
+// epilogue and the shared-memory traffic per MMA grow as the tile narrows).
+static double tile_cost(int nt) { return 1.0 + 0.5 * (256 - nt) / 128.0; }
+
 // Tile width from the token count.  When the output tiles cannot occupy every SM, K is
 // split: for decode widths (NT <= 64) across a cluster of 2 / 4 / 8 CTAs that reduce over
 // DSMEM, chosen by a small cost model (rounds of tiles x stages per split, plus a reduction
@@ -687,11 +706,25 @@ static Plan make_plan(int T, int N, int K, int max_splits, bool allow_cluster = 
   p.nt = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
   p.m_tiles = cdiv(N, kBM);
   const int sms = sm_count();
+  if (p.nt == 256) {
+    // wide tiles: the width whose busiest SM does the least work (waves x width x the width's
+    // relative cost), so the last wave is not left mostly idle (184 tiles of 256 tokens on 148
+    // SMs run two waves, the second a quarter full)
+    double best = 1e30;
+    for (int nt : {256, 224, 192, 160, 128}) {
+      const double cost = (double)cdiv(p.m_tiles * cdiv(T, nt), sms) * nt * tile_cost(nt);
+      if (cost < best - 1e-9) {
+        best = cost;
+        p.nt = nt;
+      }
+    }
+  }
+  if (forced_nt() > 0) p.nt = forced_nt();
   // Wide token tiles that leave SMs idle (fewer tiles than SMs): halve the tile while that
   // lowers the busiest SM's share (waves x tile width); K is split only after that, since a
   // split of a wide tile reduces through global atomics.  A projection of a 512-token prefill
   // chunk at N = 2880 thus runs 92 tiles of 128 tokens instead of 46 tiles split three ways.
-  while (p.nt > 64 && p.m_tiles * cdiv(T, p.nt) < sms) {
+  while ((p.nt == 256 || p.nt == 128) && forced_nt() == 0 && p.m_tiles * cdiv(T, p.nt) < sms) {
     const int half = p.nt / 2;
     if ((long long)cdiv(p.m_tiles * cdiv(T, half), sms) * half >= (long long)cdiv(p.m_tiles * cdiv(T, p.nt), sms) * p.nt)
       break;
@@ -787,6 +820,9 @@ static int dispatch(const Plan& p, const void* x, int ldx, const void* w, const 
     case 32: return launch<32, EPI, false, F8>(p, x, ldx, w, a, s);
     case 64: return launch<64, EPI, false, F8>(p, x, ldx, w, a, s);
     case 128: return launch<128, EPI, false, F8>(p, x, ldx, w, a, s);
+    case 160: return launch<160, EPI, false, F8>(p, x, ldx, w, a, s);
+    case 192: return launch<192, EPI, false, F8>(p, x, ldx, w, a, s);
+    case 224: return launch<224, EPI, false, F8>(p, x, ldx, w, a, s);
     default: return launch<256, EPI, false, F8>(p, x, ldx, w, a, s);
   }
 }
@@ -906,6 +942,9 @@ extern "C" int b200_gemm_bf16_scatter(void* const* dst, int n_dst, int ldd, cons
 }
 
 extern "C" size_t b200_red_region_bytes(int T_cap, int H_cap) { return red_region_bytes(T_cap, H_cap); }
+
+// Force the token tile width of later non-cluster plans (0 restores the planner's choice).
+extern "C" void b200_gemm_force_nt(int nt) { g_forced_nt = valid_nt(nt); }
 
 // Latency analysis: every later GEMM launch writes 8 %globaltimer stamps per CTA to `buf`
 // (device memory of grid x 8 u64; null turns it off).

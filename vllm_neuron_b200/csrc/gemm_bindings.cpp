@@ -9,6 +9,7 @@ void b200_gemm_workspace(int T, int N, int K, int max_splits, int64_t* ws_floats
 int b200_gemm_bf16(void* y, int ldy, int out_f32, const void* x, int ldx, const void* w, const void* bias, int T,
                    int N, int K, float* ws, int64_t ws_floats, int* counters, int64_t n_counters, int max_splits,
                    int* status, cudaStream_t s);
+void b200_gemm_force_nt(int nt);
 int b200_gemm_bf16_scatter(void* const* dst, int n_dst, int ldd, const void* x, int ldx, const void* w, int T, int N,
                            int K, float* ws, int64_t ws_floats, int* counters, int64_t n_counters, int max_splits,
                            int* status, cudaStream_t s);
@@ -81,6 +82,8 @@ void gemm_scatter(at::IntArrayRef dst, int64_t ldd, Tensor x, Tensor w, Tensor w
                                         at::cuda::getCurrentCUDAStream().stream());
   TORCH_CHECK(rc == 0, "b200::gemm_scatter failed with code ", rc);
 }
+
+void gemm_force_nt(int64_t nt) { b200_gemm_force_nt((int)nt); }
 
 void gemm_fp8(Tensor y, Tensor x, Tensor w, c10::optional<Tensor> bias, Tensor alpha, Tensor ws, Tensor counters,
               int64_t max_splits, c10::optional<Tensor> status) {
@@ -211,6 +214,7 @@ void register_gemm_ops(torch::Library& m) {
   m.def("rms_norm_fp8(Tensor(a!) q, Tensor x, Tensor(b!)? residual, Tensor w, float eps, Tensor scale) -> ()");
   m.def("red_region_bytes(int T_cap, int H_cap) -> int");
   m.def("gemm_set_trace(int buf) -> ()");
+  m.def("gemm_force_nt(int nt) -> ()");
   m.def(
       "gemm_bf16_allreduce(Tensor x, Tensor w, int red_uc, int red_mc, int T_cap, int H_cap, int max_splits, "
       "Tensor? status) -> int");
@@ -233,4 +237,5 @@ void register_gemm_cpu_impls(torch::Library& m) {
   m.impl("gemm_workspace", &gemm_workspace);
   m.impl("red_region_bytes", &red_region_bytes);
   m.impl("gemm_set_trace", &gemm_set_trace);
+  m.impl("gemm_force_nt", &gemm_force_nt);
 }
