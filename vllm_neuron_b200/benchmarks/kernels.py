@@ -159,6 +159,24 @@ def _attn_decode(args):
     return fn, nbytes, flops, {"B": B, "L": L, "hq": hq, "hkv": hkv, "d": d, "splits": splits}
 
 
+def _mla_decode(args):
+    """MLA decode (absorbed): B sequences of L tokens, hq heads (default 16: 128 heads over
+    TP 8), latent cache rows of 576 bf16 in 64-token blocks."""
+    from vllm_neuron_b200 import ops
+
+    B, L, hq, bs = args.T or 64, args.L or 2048, args.hq or 16, 64
+    nb = -(-L // bs)
+    cache = (torch.randn(B * nb, bs, 576, device="cuda") * 0.5).bfloat16()
+    bt = torch.randperm(B * nb, device="cuda").to(torch.int32).reshape(B, nb)
+    sl = torch.full((B,), L, dtype=torch.int32, device="cuda")
+    q = torch.randn(B, hq, 576, device="cuda").bfloat16()
+    splits = args.splits or None
+    nbytes = B * L * 576 * 2 + B * hq * (576 + 512) * 2
+    flops = 2 * B * hq * L * (576 + 512)
+    fn = lambda: ops.mla_decode(q, cache, bt, sl, 192 ** -0.5, num_splits=splits, max_seq_len=L)  # noqa: E731
+    return fn, nbytes, flops, {"B": B, "L": L, "hq": hq, "block": bs, "splits": splits or "auto"}
+
+
 def _attn_prefill(args):
     from vllm_neuron_b200 import ops
     from vllm_neuron_b200.ops.metadata import AttentionMetadata
@@ -264,6 +282,7 @@ OPS = {
     "moe_mxfp4": _moe_mxfp4,
     "moe_bf16": _moe_bf16,
     "attn_decode": _attn_decode,
+    "mla_decode": _mla_decode,
     "attn_prefill": _attn_prefill,
     "gemm": _gemm,
     "gdn_prefill": lambda a: _gdn(a, False),

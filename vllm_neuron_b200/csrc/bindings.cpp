@@ -277,6 +277,8 @@ void register_comm_cpu_impls(torch::Library& m);
 void register_deltanet_ops(torch::Library& m);
 void register_deltanet_impls(torch::Library& m);
 void register_gemm_ops(torch::Library& m);
+void register_mla_ops(torch::Library& m);
+void register_mla_impls(torch::Library& m);
 void register_gemm_impls(torch::Library& m);
 void register_gemm_cpu_impls(torch::Library& m);
 
@@ -317,6 +319,7 @@ TORCH_LIBRARY(b200, m) {
   register_comm_ops(m);
   register_deltanet_ops(m);
   register_gemm_ops(m);
+  register_mla_ops(m);
 }
 
 // ops without tensor arguments (pointer plumbing) dispatch through CompositeExplicitAutograd
@@ -343,6 +346,7 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   register_comm_impls(m);
   register_deltanet_impls(m);
   register_gemm_impls(m);
+  register_mla_impls(m);
 }
 
 // Python module entry so `import vllm_neuron_b200._C` loads the library.

@@ -285,6 +285,32 @@ def build_cos_sin_cache(inv_freq: torch.Tensor, max_pos: int, attn_factor: float
 # ---------------------------------------------------------------------------
 
 
+def mla_decode(q: torch.Tensor, cache: torch.Tensor, block_tables: torch.Tensor, seq_lens: torch.Tensor,
+               scale: float, num_splits: int | None = None, max_seq_len: int | None = None) -> torch.Tensor:
+    """Multi-head latent attention decode (absorbed form): q [B, Hq, 576] against the paged
+    latent cache [num_blocks, block_size, 576] (512 latent + 64 rope dims, shared by all
+    heads), output [B, Hq, 512].  On a GPU: the tcgen05 kernel of ``csrc/mla_decode.cu``
+    (keys as the MMA's 128-row dimension, S and O in tensor memory, split-KV with a
+    log-sum-exp merge); elsewhere the fp32 reference.  ``num_splits`` defaults to enough
+    splits of each sequence's 128-key tiles to put one CTA on every SM (``max_seq_len``, if
+    given, caps it without reading ``seq_lens`` on the host)."""
+    B, Hq = q.shape[0], q.shape[1]
+    if not (use_kernel(q) and q.dtype == torch.bfloat16 and cache.dtype == torch.bfloat16):
+        return ref.attention.mla_decode(q, cache, block_tables, seq_lens, scale)
+    if num_splits is None:
+        sms = torch.cuda.get_device_properties(q.device).multi_processor_count
+        groups = -(-Hq // 64) if Hq > 32 else 1
+        num_splits = max(1, min(64, sms // max(1, B * groups)))
+        if max_seq_len is not None:
+            num_splits = max(1, min(num_splits, -(-max_seq_len // 128)))
+    q = q.contiguous()
+    out = torch.empty(B, Hq, 512, dtype=torch.bfloat16, device=q.device)
+    ws = torch.empty(B * Hq * num_splits * 513, dtype=torch.float32, device=q.device) if num_splits > 1 else None
+    _k().mla_decode(out, q, cache.contiguous(), block_tables.to(torch.int32).contiguous(),
+                    seq_lens.to(torch.int32).contiguous(), float(scale), ws, num_splits, device_status(q.device))
+    return out
+
+
 def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, meta: AttentionMetadata,
               scale: float, sinks: torch.Tensor | None = None, window: int | None = None,
               k_scale: float = 1.0, v_scale: float = 1.0, out: torch.Tensor | None = None) -> torch.Tensor:

@@ -191,3 +191,24 @@ def lse_merge(outs: list[torch.Tensor], lses: list[torch.Tensor],
     denom = torch.exp(Lall - m).sum(0)
     acc = sum(o.float() * (wi / denom).transpose(0, 1)[..., None] for o, wi in zip(outs, w))
     return acc.to(outs[0].dtype)
+
+
+def mla_decode(q: torch.Tensor, cache: torch.Tensor, block_tables: torch.Tensor, seq_lens: torch.Tensor,
+               scale: float, v_dim: int = 512) -> torch.Tensor:
+    """Multi-head latent attention for one new token per sequence (absorbed form, fp32): the
+    paged cache [num_blocks, block_size, d_qk] holds one latent row per token shared by every
+    head; s = scale * q . c, p = softmax over the sequence's tokens, o = p . c[:, :v_dim].
+    q [B, Hq, d_qk] -> o [B, Hq, v_dim] in q's dtype."""
+    B, Hq, _ = q.shape
+    bs = cache.shape[1]
+    out = torch.zeros(B, Hq, v_dim, dtype=torch.float32, device=q.device)
+    for b in range(B):
+        L = int(seq_lens[b])
+        if L <= 0:
+            continue
+        nblk = -(-L // bs)
+        rows = cache[block_tables[b, :nblk].long()].reshape(nblk * bs, -1)[:L].float()
+        s = (q[b].float() @ rows.t()) * scale
+        p = torch.softmax(s, dim=-1)
+        out[b] = p @ rows[:, :v_dim]
+    return out.to(q.dtype)
