@@ -44,8 +44,15 @@ constexpr int kQkStages = 5;     // chunks (0,1) (2,3) (4,5) (6,7) (8)
 constexpr int kPvStages = 4;     // value chunks (0,1) .. (6,7): one 128-dim O tile each
 constexpr int kStagesPerTile = kQkStages + kPvStages;
 constexpr int kThreads = 256;
-constexpr int kColS = 0;         // TMEM: S^T at columns [0, NH), O^T tile i at 64 + i * NH
-constexpr int kColO = 64;
+constexpr int kColS = 0;         // TMEM: S^T of tile j at columns 64 (j & 1) + [0, NH), O^T tile i at 128 + i * NH
+constexpr int kColO = 128;
+
+// P^T as the MN-major B operand (a key's row of 64 heads is one 128-byte line, written with
+// 16-byte stores) when the head tile is 64 wide; K-major (2-byte stores) for 16 / 32 heads.
+template <int NH>
+constexpr bool kPMnMajor() {
+  return NH == 64;
+}
 
 template <int NH>
 struct Smem {
@@ -60,7 +67,7 @@ struct Smem {
   static constexpr int kOffL = kOffFac + NH * 4;               // float [NH] final row sums
   static constexpr int kOffFlag = kOffL + NH * 4;              // int [2] rescale flag per tile parity
   static constexpr int kOffBar = (kOffFlag + 8 + 7) / 8 * 8;
-  static constexpr int kNumBars = 2 * kRing + 4;               // full, empty, q_full, s_full, p_full, pv_done
+  static constexpr int kNumBars = 2 * kRing + 7;  // full, empty, q_full, s_full[2], p_full, pv_done, pv_landed, pv_zeroed
   static constexpr int kBytes = kOffBar + kNumBars * 8 + 16;
   static constexpr int kAlloc = kBytes + 1024;
   static constexpr uint32_t kTmemCols = kColO + 4 * NH <= 128 ? 128 : kColO + 4 * NH <= 256 ? 256 : 512;
@@ -81,6 +88,50 @@ B200_D uint64_t desc_sw128_mn(const void* smem, uint32_t lbo) {
 }
 
 B200_D void named_bar_softmax() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+B200_D uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&p);
+}
+
+// Reduce N per-lane values (lane = key) across the warp's 32 lanes with a transposing
+// butterfly: at each step a lane keeps half of its values and trades the other half with its
+// partner, so N = 64 costs 62 shuffles instead of 320.  Afterwards lane l holds the results
+// for heads 2l, 2l + 1 (N = 64) in a[0..1], head l (N = 32) or head l / 2 (N = 16) in a[0].
+template <int N, bool kMax>
+B200_D void lane_reduce(float (&a)[N], int lane) {
+#pragma unroll
+  for (int s = 0; s < 5; ++s) {
+    const int off = 16 >> s;
+    const int n = N >> s;  // values still held per lane
+    if (n > 1) {
+      const bool upper = (lane & off) != 0;
+#pragma unroll
+      for (int i = 0; i < n / 2; ++i) {
+        const float send = upper ? a[i] : a[i + n / 2];
+        const float keep = upper ? a[i + n / 2] : a[i];
+        const float recv = __shfl_xor_sync(0xffffffffu, send, off);
+        a[i] = kMax ? fmaxf(keep, recv) : keep + recv;
+      }
+    } else {
+      const float recv = __shfl_xor_sync(0xffffffffu, a[0], off);
+      a[0] = kMax ? fmaxf(a[0], recv) : a[0] + recv;
+    }
+  }
+}
+
+// Store lane_reduce's per-head results of this warp to dst[0 .. N).
+template <int N>
+B200_D void store_lane_result(float* dst, const float (&a)[N], int lane) {
+  if constexpr (N == 64) {
+    dst[2 * lane] = a[0];
+    dst[2 * lane + 1] = a[1];
+  } else if constexpr (N == 32) {
+    dst[lane] = a[0];
+  } else {
+    if ((lane & 1) == 0) dst[lane >> 1] = a[0];
+  }
+}
 
 // Grid (num_splits, head groups, B).  Warp 0: TMA; warp 1: TMEM owner and MMA issuer;
 // warps 4..7: softmax and epilogue.
@@ -108,10 +159,12 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
   uint64_t* empty = full + R;
   uint64_t* q_full = empty + R;
-  uint64_t* s_full = q_full + 1;
-  uint64_t* p_full = s_full + 1;
+  uint64_t* s_full = q_full + 1;  // [2]: one per S buffer
+  uint64_t* p_full = s_full + 2;
   uint64_t* pv_done = p_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 1);
+  uint64_t* pv_landed = pv_done + 1;  // the split's partial last tile: its P.V stages are in
+  uint64_t* pv_zeroed = pv_landed + 1;  // ... and the softmax warps have zeroed the rows past the end
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_zeroed + 1);
 
   const int split = blockIdx.x, grp = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -130,9 +183,12 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(
       tc::mbar_init(&empty[s], 1);
     }
     tc::mbar_init(q_full, 1);
-    tc::mbar_init(s_full, 1);
+    tc::mbar_init(&s_full[0], 1);
+    tc::mbar_init(&s_full[1], 1);
     tc::mbar_init(p_full, 128);
     tc::mbar_init(pv_done, 1);
+    tc::mbar_init(pv_landed, 1);
+    tc::mbar_init(pv_zeroed, 128);
     tc::fence_barrier_init();
     tc::prefetch_tmap(&tmQ);
     tc::prefetch_tmap(&tmC);
@@ -151,12 +207,14 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(
   if (warp == 0) {
     if (lane == 0 && ntiles > 0) {
       // ---------------- TMA producer ----------------
+      // ring order: S stages of tile 0, then per tile j: S stages of tile j + 1, P.V stages of
+      // tile j (the MMA issuer consumes in the same order, so S(j + 1) overlaps softmax(j))
       tc::mbar_arrive_expect_tx(q_full, kChunks * L::kQChunk);
       for (int c = 0; c < kChunks; ++c) tc::tma_load_3d(sQ + c * L::kQChunk, &tmQ, c * 64, grp * NH, b, q_full);
       const int nb = kKeys >> bs_log;  // cache blocks per tile (bs >= 16: at most 8)
       int it = 0;
       bool ok = true;
-      for (int j = 0; j < ntiles && ok; ++j) {
+      auto load_stages = [&](int j, bool qk) {
         const int key0 = (t_begin + j) * kKeys;
         int blk[8];
         for (int r = 0; r < nb; ++r) {
@@ -169,32 +227,38 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(
           }
           blk[r] = id;
         }
-        for (int st = 0; st < kStagesPerTile; ++st, ++it) {
+        const int nst = qk ? kQkStages : kPvStages;
+        for (int st = 0; st < nst && ok; ++st, ++it) {
           const int slot = it % R, use = it / R;
           if (it >= R && !tc::mbar_wait(&empty[slot], (use - 1) & 1, status)) {
             ok = false;
             break;
           }
-          const bool qk = st < kQkStages;
-          const int c0 = qk ? 2 * st : 2 * (st - kQkStages);
           const int nch = (qk && st == kQkStages - 1) ? 1 : 2;
           tc::mbar_arrive_expect_tx(&full[slot], nch * kChunkBytes);
           for (int cc = 0; cc < nch; ++cc)
             for (int r = 0; r < nb; ++r)
               tc::tma_load_2d(ring + slot * kStageBytes + cc * kChunkBytes + (r << bs_log) * 128, &tmC,
-                              (c0 + cc) * 64, blk[r] << bs_log, &full[slot]);
+                              (2 * st + cc) * 64, blk[r] << bs_log, &full[slot]);
         }
+      };
+      load_stages(0, true);
+      for (int j = 0; j < ntiles && ok; ++j) {
+        if (j + 1 < ntiles) load_stages(j + 1, true);
+        load_stages(j, false);
       }
     }
   } else if (warp == 1) {
     if (lane == 0 && ntiles > 0) {
       // ---------------- MMA issuer ----------------
       const uint32_t id_s = tc::idesc_f16_bf16(kKeys, NH);
-      const uint32_t id_o = tc::idesc_f16_bf16(kKeys, NH) | (1u << 15);  // A (V^T) MN-major
+      // A = V^T MN-major; B = P^T MN-major (heads contiguous) when a P row is one 128-byte line
+      const uint32_t id_o = tc::idesc_f16_bf16(kKeys, NH) | (1u << 15) | (kPMnMajor<NH>() ? (1u << 16) : 0u);
       bool ok = tc::mbar_wait(q_full, 0, status);
       tc::fence_after_sync();
       int it = 0;
-      for (int j = 0; j < ntiles && ok; ++j) {
+      auto qk = [&](int j) {
+        const uint32_t t_s = tmem + kColS + (j & 1) * 64;
         for (int st = 0; st < kQkStages && ok; ++st, ++it) {
           const int slot = it % R, use = it / R;
           if (!tc::mbar_wait(&full[slot], use & 1, status)) {
@@ -209,15 +273,26 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(
             uint8_t* bq = sQ + c * L::kQChunk;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              tc::mma_f16(tmem + kColS, tc::desc_sw128(a + kk * 32), tc::desc_sw128(bq + kk * 32), id_s,
+              tc::mma_f16(t_s, tc::desc_sw128(a + kk * 32), tc::desc_sw128(bq + kk * 32), id_s,
                           (c | kk) != 0 ? 1u : 0u);
           }
           tc::mma_commit(&empty[slot]);
         }
-        if (!ok) break;
-        tc::mma_commit(s_full);
-        if (!tc::mbar_wait(p_full, j & 1, status)) break;
+        if (ok) tc::mma_commit(&s_full[j & 1]);
+      };
+      if (ok) qk(0);
+      for (int j = 0; j < ntiles && ok; ++j) {
+        if (j + 1 < ntiles) qk(j + 1);  // S(j + 1) into the other buffer while softmax(j) runs
+        if (!ok || !tc::mbar_wait(p_full, j & 1, status)) break;
         tc::fence_after_sync();
+        if ((t_begin + j + 1) * kKeys > key_end) {  // partial last tile: rows past the end get zeroed first
+          for (int i = 0; i < kPvStages && ok; ++i)
+            ok = tc::mbar_wait(&full[(it + i) % R], ((it + i) / R) & 1, status);
+          if (!ok) break;
+          tc::mbar_arrive(pv_landed);
+          if (!tc::mbar_wait(pv_zeroed, 0, status)) break;
+          tc::fence_after_sync();
+        }
         for (int i = 0; i < kPvStages && ok; ++i, ++it) {
           const int slot = it % R, use = it / R;
           if (!tc::mbar_wait(&full[slot], use & 1, status)) {
@@ -227,10 +302,12 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(
           tc::fence_after_sync();
           uint8_t* v = ring + slot * kStageBytes;
 #pragma unroll
-          for (int ks = 0; ks < kKeys / 16; ++ks)
-            tc::mma_f16(tmem + kColO + i * NH, desc_sw128_mn(v + ks * 2048, kChunkBytes),
-                        tc::desc_sw128(sP + (ks >> 2) * L::kQChunk + (ks & 3) * 32), id_o,
+          for (int ks = 0; ks < kKeys / 16; ++ks) {
+            const uint64_t bp = kPMnMajor<NH>() ? tc::desc_sw128(sP + ks * 2048)
+                                                : tc::desc_sw128(sP + (ks >> 2) * L::kQChunk + (ks & 3) * 32);
+            tc::mma_f16(tmem + kColO + i * NH, desc_sw128_mn(v + ks * 2048, kChunkBytes), bp, id_o,
                         (j > 0 || ks > 0) ? 1u : 0u);
+          }
           tc::mma_commit(&empty[slot]);
         }
         if (!ok) break;
@@ -249,25 +326,28 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(
     // thread runs the same sequence of named barriers and warp-collective TMEM accesses; the
     // waits after a recorded error return at once.
     bool ok = true;
+    float v[NH];
     for (int j = 0; j < ntiles; ++j) {
       const int key0 = (t_begin + j) * kKeys;
       const int nvalid = min(kKeys, key_end - key0);
-      ok = tc::mbar_wait(s_full, j & 1, status) && ok;
+      ok = tc::mbar_wait(&s_full[j & 1], (j >> 1) & 1, status) && ok;
       tc::fence_after_sync();
-      float v[NH];
 #pragma unroll
       for (int c16 = 0; c16 < NH / 16; ++c16) {
         uint32_t r[16];
-        tc::tmem_ld_32x32b_x16(tmem + lane_base + kColS + c16 * 16, r);
+        tc::tmem_ld_32x32b_x16(tmem + lane_base + kColS + (j & 1) * 64 + c16 * 16, r);
         tc::tmem_ld_wait();
 #pragma unroll
         for (int e = 0; e < 16; ++e) v[c16 * 16 + e] = t < nvalid ? __uint_as_float(r[e]) * scale_log2 : -INFINITY;
       }
-      // per-head maximum of the tile over the 128 keys (lanes)
+      // per-head maximum of the tile over the 128 keys (lanes): transposing butterfly in the
+      // warp, then the four warps through shared memory
+      {
+        float a[NH];
 #pragma unroll
-      for (int h = 0; h < NH; ++h) {
-        const float mx = warp_max(v[h]);
-        if (lane == 0) red[q4 * NH + h] = mx;
+        for (int h = 0; h < NH; ++h) a[h] = v[h];
+        lane_reduce<NH, true>(a, lane);
+        store_lane_result<NH>(red + q4 * NH, a, lane);
       }
       named_bar_softmax();
       if (t < NH) {
@@ -285,6 +365,13 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(
       named_bar_softmax();
       const bool resc = flag[j & 1] != 0;
       if (t == 0) flag[(j + 1) & 1] = 0;  // read by nobody until the next tile's barrier
+      // exponentials (in place) while the previous tile's P.V may still run
+#pragma unroll
+      for (int h = 0; h < NH; ++h) {
+        const float p = v[h] == -INFINITY ? 0.f : exp2f(v[h] - m_used[h]);
+        lp[h] = lp[h] * fac[h] + p;
+        v[h] = p;
+      }
       // P.V of the previous tile must be done before P or O change
       if (j > 0) {
         ok = tc::mbar_wait(pv_done, (j - 1) & 1, status) && ok;
@@ -306,44 +393,56 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(
           tc::tmem_st_wait();
         }
       }
-      // P (bf16) into the K-major B operand: row h, key t of chunk t / 64
-      uint8_t* pc = sP + (t >> 6) * L::kQChunk;
-      const int kc = t & 63;
+      if constexpr (kPMnMajor<NH>()) {
+        // P^T MN-major: key t's row holds its 64 heads (one 128-byte line, 16-byte units
+        // swizzled by t % 8)
+        uint8_t* row = sP + t * 128;
 #pragma unroll
-      for (int h = 0; h < NH; ++h) {
-        const float mh = m_used[h];
-        const float p = v[h] == -INFINITY ? 0.f : exp2f(v[h] - mh);
-        lp[h] = lp[h] * fac[h] + p;
-        const __nv_bfloat16 pb = __float2bfloat16(p);
-        *reinterpret_cast<__nv_bfloat16*>(pc + h * 128 + ((((kc >> 3) ^ (h & 7))) << 4) + (kc & 7) * 2) = pb;
-      }
-      if (nvalid < kKeys) {
-        // keys past the sequence: zero their value rows so that 0 x (stale cache bytes) cannot
-        // turn into NaN in P.V
-        for (int i = 0; i < kPvStages; ++i) {
-          const int itv = j * kStagesPerTile + kQkStages + i;
-          const int slot = itv % R, use = itv / R;
-          ok = tc::mbar_wait(&full[slot], use & 1, status) && ok;
-          if (t >= nvalid) {
-            uint4* row0 = reinterpret_cast<uint4*>(ring + slot * kStageBytes + t * 128);
-            uint4* row1 = reinterpret_cast<uint4*>(ring + slot * kStageBytes + kChunkBytes + t * 128);
-#pragma unroll
-            for (int u = 0; u < 8; ++u) row0[u] = row1[u] = make_uint4(0u, 0u, 0u, 0u);
-          }
+        for (int u = 0; u < 8; ++u) {
+          uint4 w;
+          w.x = pack_bf16x2(v[8 * u + 0], v[8 * u + 1]);
+          w.y = pack_bf16x2(v[8 * u + 2], v[8 * u + 3]);
+          w.z = pack_bf16x2(v[8 * u + 4], v[8 * u + 5]);
+          w.w = pack_bf16x2(v[8 * u + 6], v[8 * u + 7]);
+          *reinterpret_cast<uint4*>(row + ((u ^ (t & 7)) << 4)) = w;
         }
+      } else {
+        // P^T K-major: row h, key t of chunk t / 64
+        uint8_t* pc = sP + (t >> 6) * L::kQChunk;
+        const int kc = t & 63;
+#pragma unroll
+        for (int h = 0; h < NH; ++h)
+          *reinterpret_cast<__nv_bfloat16*>(pc + h * 128 + ((((kc >> 3) ^ (h & 7))) << 4) + (kc & 7) * 2) =
+              __float2bfloat16(v[h]);
       }
       tc::fence_proxy_async();  // generic shared-memory writes -> the tensor core's async proxy
       tc::fence_before_sync();
       tc::mbar_arrive(p_full);
+      if (nvalid < kKeys) {
+        // the split's last tile ends inside it: once the MMA issuer reports its P.V stages
+        // landed, zero the value rows of the keys past the end (0 x stale cache bytes could be
+        // NaN in P.V); happens once per CTA, so the barriers see a single phase
+        ok = tc::mbar_wait(pv_landed, 0, status) && ok;
+        if (t >= nvalid) {
+          const int itv = kQkStages + j * kStagesPerTile + (j + 1 < ntiles ? kQkStages : 0);
+#pragma unroll 1
+          for (int i = 0; i < kPvStages; ++i) {
+            uint8_t* st = ring + ((itv + i) % R) * kStageBytes;
+            uint4* row0 = reinterpret_cast<uint4*>(st + t * 128);
+            uint4* row1 = reinterpret_cast<uint4*>(st + kChunkBytes + t * 128);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) row0[u] = row1[u] = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+        tc::fence_proxy_async();
+        tc::mbar_arrive(pv_zeroed);
+      }
     }
     // ---- epilogue ----
     if (ok && ntiles > 0) ok = tc::mbar_wait(pv_done, (ntiles - 1) & 1, status);
     tc::fence_after_sync();
-#pragma unroll
-    for (int h = 0; h < NH; ++h) {
-      const float s = warp_sum(lp[h]);
-      if (lane == 0) red[q4 * NH + h] = s;
-    }
+    lane_reduce<NH, false>(lp, lane);
+    store_lane_result<NH>(red + q4 * NH, lp, lane);
     named_bar_softmax();
     if (t < NH) lsum[t] = red[t] + red[NH + t] + red[2 * NH + t] + red[3 * NH + t];
     named_bar_softmax();
