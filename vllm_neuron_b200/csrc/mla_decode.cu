@@ -43,7 +43,7 @@ constexpr int kStageBytes = 2 * kChunkBytes;
 constexpr int kQkStages = 5;     // chunks (0,1) (2,3) (4,5) (6,7) (8)
 constexpr int kPvStages = 4;     // value chunks (0,1) .. (6,7): one 128-dim O tile each
 constexpr int kStagesPerTile = kQkStages + kPvStages;
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;  // warp 0 TMA, warp 1 MMA, warps 4-11 softmax (two groups)
 constexpr int kColS = 0;         // TMEM: S^T of tile j at columns 64 (j & 1) + [0, NH), O^T tile i at 128 + i * NH
 constexpr int kColO = 128;
 
@@ -87,7 +87,7 @@ B200_D uint64_t desc_sw128_mn(const void* smem, uint32_t lbo) {
   return d;
 }
 
-B200_D void named_bar_softmax() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+B200_D void named_bar_softmax() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 B200_D uint32_t pack_bf16x2(float lo, float hi) {
   const __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
@@ -120,16 +120,58 @@ B200_D void lane_reduce(float (&a)[N], int lane) {
   }
 }
 
-// Store lane_reduce's per-head results of this warp to dst[0 .. N).
+// Store lane_reduce's per-head results of this warp to dst[0 .. N): lane l holds heads 2l and
+// 2l + 1 for N = 64, head l / (32 / N) for N <= 32 (its first lane writes it).
 template <int N>
 B200_D void store_lane_result(float* dst, const float (&a)[N], int lane) {
   if constexpr (N == 64) {
     dst[2 * lane] = a[0];
     dst[2 * lane + 1] = a[1];
-  } else if constexpr (N == 32) {
-    dst[lane] = a[0];
   } else {
-    if ((lane & 1) == 0) dst[lane >> 1] = a[0];
+    constexpr int per = 32 / N;
+    if (lane % per == 0) dst[lane / per] = a[0];
+  }
+}
+
+// N consecutive fp32 TMEM columns of this warp's 32 lanes (N = 8, 16 or 32), waited.
+template <int N>
+B200_D void tmem_ld_cols(uint32_t taddr, float (&v)[N]) {
+  if constexpr (N == 8) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+    tc::tmem_ld_wait();
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(r[e]);
+  } else {
+#pragma unroll
+    for (int c = 0; c < N / 16; ++c) {
+      uint32_t r[16];
+      tc::tmem_ld_32x32b_x16(taddr + c * 16, r);
+      tc::tmem_ld_wait();
+#pragma unroll
+      for (int e = 0; e < 16; ++e) v[c * 16 + e] = __uint_as_float(r[e]);
+    }
+  }
+}
+
+// Store N fp32 columns back (the caller waits with tmem_st_wait).
+template <int N>
+B200_D void tmem_st_cols(uint32_t taddr, const float (&v)[N]) {
+  if constexpr (N == 8) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+                 "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+                 "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+                 "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])));
+  } else {
+#pragma unroll
+    for (int c = 0; c < N / 16; ++c) {
+      uint32_t r[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(v[c * 16 + e]);
+      tc::tmem_st_32x32b_x16(taddr + c * 16, r);
+    }
   }
 }
 
@@ -185,16 +227,16 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(
     tc::mbar_init(q_full, 1);
     tc::mbar_init(&s_full[0], 1);
     tc::mbar_init(&s_full[1], 1);
-    tc::mbar_init(p_full, 128);
+    tc::mbar_init(p_full, 256);
     tc::mbar_init(pv_done, 1);
     tc::mbar_init(pv_landed, 1);
-    tc::mbar_init(pv_zeroed, 128);
+    tc::mbar_init(pv_zeroed, 256);
     tc::fence_barrier_init();
     tc::prefetch_tmap(&tmQ);
     tc::prefetch_tmap(&tmC);
     flag[0] = flag[1] = 0;
   }
-  if (threadIdx.x >= 128 && threadIdx.x < 128 + NH) m_used[threadIdx.x - 128] = -INFINITY;
+  if (threadIdx.x >= 128 && threadIdx.x < 128 + NH) m_used[threadIdx.x - 128] = -INFINITY;  // softmax threads
   if (warp == 1) {
     tc::tmem_alloc(tmem_slot, L::kTmemCols);
     tc::tmem_relinquish();
@@ -315,61 +357,62 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(
       }
     }
   } else if (warp >= 4) {
-    // ---------------- softmax / epilogue (thread t = TMEM lane t) ----------------
+    // ---------------- softmax / epilogue ----------------
+    // Two warpgroups, each owning half of the tile's heads (HH = NH / 2); thread t of a group =
+    // TMEM lane t (key t for S, value dim t of a 128-dim tile for O).
+    constexpr int HH = NH / 2;
+    const int ts = threadIdx.x - 128;     // 0 .. 255
+    const int g = ts >> 7;                // head half
     const int q4 = warp & 3, t = q4 * 32 + lane;
+    const int h0 = g * HH;
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
-    float lp[NH];
+    float lp[HH];
 #pragma unroll
-    for (int h = 0; h < NH; ++h) lp[h] = 0.f;
+    for (int h = 0; h < HH; ++h) lp[h] = 0.f;
     named_bar_softmax();  // m_used initialised
     // A failed (timed-out) wait sets ok = false but never leaves the loop: every softmax
     // thread runs the same sequence of named barriers and warp-collective TMEM accesses; the
     // waits after a recorded error return at once.
     bool ok = true;
-    float v[NH];
+    float v[HH];
     for (int j = 0; j < ntiles; ++j) {
       const int key0 = (t_begin + j) * kKeys;
       const int nvalid = min(kKeys, key_end - key0);
       ok = tc::mbar_wait(&s_full[j & 1], (j >> 1) & 1, status) && ok;
       tc::fence_after_sync();
-#pragma unroll
-      for (int c16 = 0; c16 < NH / 16; ++c16) {
-        uint32_t r[16];
-        tc::tmem_ld_32x32b_x16(tmem + lane_base + kColS + (j & 1) * 64 + c16 * 16, r);
-        tc::tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 16; ++e) v[c16 * 16 + e] = t < nvalid ? __uint_as_float(r[e]) * scale_log2 : -INFINITY;
-      }
+      const uint32_t s_addr = tmem + lane_base + kColS + (j & 1) * 64 + h0;
       // per-head maximum of the tile over the 128 keys (lanes): transposing butterfly in the
-      // warp, then the four warps through shared memory
-      {
-        float a[NH];
+      // warp, then the four warps through shared memory (the butterfly consumes its copy; the
+      // scores are read from TMEM again below, which costs less than keeping both live)
+      tmem_ld_cols<HH>(s_addr, v);
 #pragma unroll
-        for (int h = 0; h < NH; ++h) a[h] = v[h];
-        lane_reduce<NH, true>(a, lane);
-        store_lane_result<NH>(red + q4 * NH, a, lane);
-      }
+      for (int h = 0; h < HH; ++h) v[h] = t < nvalid ? v[h] * scale_log2 : -INFINITY;
+      lane_reduce<HH, true>(v, lane);
+      store_lane_result<HH>(red + q4 * NH + h0, v, lane);
       named_bar_softmax();
-      if (t < NH) {
-        const float tm = fmaxf(fmaxf(red[t], red[NH + t]), fmaxf(red[2 * NH + t], red[3 * NH + t]));
-        const float mo = m_used[t];
+      if (ts < NH) {
+        const float tm = fmaxf(fmaxf(red[ts], red[NH + ts]), fmaxf(red[2 * NH + ts], red[3 * NH + ts]));
+        const float mo = m_used[ts];
         float mn = mo, f = 1.f;
         if (tm > mo + 8.f) {  // lazy rescale: exponentials stay below 2^8 otherwise
           mn = tm;
           f = mo == -INFINITY ? 0.f : exp2f(mo - mn);
           flag[j & 1] = 1;
         }
-        m_used[t] = mn;
-        fac[t] = f;
+        m_used[ts] = mn;
+        fac[ts] = f;
       }
       named_bar_softmax();
       const bool resc = flag[j & 1] != 0;
-      if (t == 0) flag[(j + 1) & 1] = 0;  // read by nobody until the next tile's barrier
+      if (ts == 0) flag[(j + 1) & 1] = 0;  // read by nobody until the next tile's barrier
       // exponentials (in place) while the previous tile's P.V may still run
+      tmem_ld_cols<HH>(s_addr, v);
 #pragma unroll
-      for (int h = 0; h < NH; ++h) {
-        const float p = v[h] == -INFINITY ? 0.f : exp2f(v[h] - m_used[h]);
-        lp[h] = lp[h] * fac[h] + p;
+      for (int h = 0; h < HH; ++h) v[h] = t < nvalid ? v[h] * scale_log2 : -INFINITY;
+#pragma unroll
+      for (int h = 0; h < HH; ++h) {
+        const float p = v[h] == -INFINITY ? 0.f : exp2f(v[h] - m_used[h0 + h]);
+        lp[h] = lp[h] * fac[h0 + h] + p;
         v[h] = p;
       }
       // P.V of the previous tile must be done before P or O change
@@ -377,17 +420,17 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(
         ok = tc::mbar_wait(pv_done, (j - 1) & 1, status) && ok;
         tc::fence_after_sync();
         if (resc) {
+          constexpr int CW = HH < 16 ? HH : 16;  // columns per TMEM round trip
 #pragma unroll 1
           for (int i = 0; i < 4; ++i) {
+#pragma unroll 1
+            for (int c = 0; c < HH; c += CW) {
+              float o[CW];
+              const uint32_t addr = tmem + lane_base + kColO + i * NH + h0 + c;
+              tmem_ld_cols<CW>(addr, o);
 #pragma unroll
-            for (int c16 = 0; c16 < NH / 16; ++c16) {
-              uint32_t r[16];
-              const uint32_t addr = tmem + lane_base + kColO + i * NH + c16 * 16;
-              tc::tmem_ld_32x32b_x16(addr, r);
-              tc::tmem_ld_wait();
-#pragma unroll
-              for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * fac[c16 * 16 + e]);
-              tc::tmem_st_32x32b_x16(addr, r);
+              for (int h = 0; h < CW; ++h) o[h] *= fac[h0 + c + h];
+              tmem_st_cols<CW>(addr, o);
             }
           }
           tc::tmem_st_wait();
@@ -395,25 +438,28 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(
       }
       if constexpr (kPMnMajor<NH>()) {
         // P^T MN-major: key t's row holds its 64 heads (one 128-byte line, 16-byte units
-        // swizzled by t % 8)
+        // swizzled by t % 8); this group writes units 4g .. 4g + 3
         uint8_t* row = sP + t * 128;
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < HH / 8; ++u) {
           uint4 w;
           w.x = pack_bf16x2(v[8 * u + 0], v[8 * u + 1]);
           w.y = pack_bf16x2(v[8 * u + 2], v[8 * u + 3]);
           w.z = pack_bf16x2(v[8 * u + 4], v[8 * u + 5]);
           w.w = pack_bf16x2(v[8 * u + 6], v[8 * u + 7]);
-          *reinterpret_cast<uint4*>(row + ((u ^ (t & 7)) << 4)) = w;
+          const int uu = g * (HH / 8) + u;
+          *reinterpret_cast<uint4*>(row + ((uu ^ (t & 7)) << 4)) = w;
         }
       } else {
         // P^T K-major: row h, key t of chunk t / 64
         uint8_t* pc = sP + (t >> 6) * L::kQChunk;
         const int kc = t & 63;
 #pragma unroll
-        for (int h = 0; h < NH; ++h)
+        for (int hh = 0; hh < HH; ++hh) {
+          const int h = h0 + hh;
           *reinterpret_cast<__nv_bfloat16*>(pc + h * 128 + ((((kc >> 3) ^ (h & 7))) << 4) + (kc & 7) * 2) =
-              __float2bfloat16(v[h]);
+              __float2bfloat16(v[hh]);
+        }
       }
       tc::fence_proxy_async();  // generic shared-memory writes -> the tensor core's async proxy
       tc::fence_before_sync();
@@ -427,11 +473,9 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(
           const int itv = kQkStages + j * kStagesPerTile + (j + 1 < ntiles ? kQkStages : 0);
 #pragma unroll 1
           for (int i = 0; i < kPvStages; ++i) {
-            uint8_t* st = ring + ((itv + i) % R) * kStageBytes;
-            uint4* row0 = reinterpret_cast<uint4*>(st + t * 128);
-            uint4* row1 = reinterpret_cast<uint4*>(st + kChunkBytes + t * 128);
+            uint4* row = reinterpret_cast<uint4*>(ring + ((itv + i) % R) * kStageBytes + g * kChunkBytes + t * 128);
 #pragma unroll
-            for (int u = 0; u < 8; ++u) row0[u] = row1[u] = make_uint4(0u, 0u, 0u, 0u);
+            for (int u = 0; u < 8; ++u) row[u] = make_uint4(0u, 0u, 0u, 0u);
           }
         }
         tc::fence_proxy_async();
@@ -441,35 +485,31 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(
     // ---- epilogue ----
     if (ok && ntiles > 0) ok = tc::mbar_wait(pv_done, (ntiles - 1) & 1, status);
     tc::fence_after_sync();
-    lane_reduce<NH, false>(lp, lane);
-    store_lane_result<NH>(red + q4 * NH, lp, lane);
+    lane_reduce<HH, false>(lp, lane);
+    store_lane_result<HH>(red + q4 * NH + h0, lp, lane);
     named_bar_softmax();
-    if (t < NH) lsum[t] = red[t] + red[NH + t] + red[2 * NH + t] + red[3 * NH + t];
+    if (ts < NH) lsum[ts] = red[ts] + red[NH + ts] + red[2 * NH + ts] + red[3 * NH + ts];
     named_bar_softmax();
     const bool have = __all_sync(0xffffffffu, ok && ntiles > 0);  // uniform per warp (tcgen05.ld is collective)
+    constexpr int CW = HH < 16 ? HH : 16;  // columns per TMEM load
 #pragma unroll 1
-    for (int i = 0; i < 4; ++i) {
+    for (int ic = 0; ic < 4 * (HH / CW); ++ic) {
+      const int i = ic / (HH / CW), c = (ic % (HH / CW)) * CW;
+      float o[CW];
+      if (have) tmem_ld_cols<CW>(tmem + lane_base + kColO + i * NH + h0 + c, o);
 #pragma unroll
-      for (int c16 = 0; c16 < NH / 16; ++c16) {
-        uint32_t r[16];
-        if (have) {
-          tc::tmem_ld_32x32b_x16(tmem + lane_base + kColO + i * NH + c16 * 16, r);
-          tc::tmem_ld_wait();
-        }
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int h = c16 * 16 + e, head = grp * NH + h;
-          if (head >= Hq) continue;
-          const float l = lsum[h];
-          const float o = (have && l > 0.f) ? __uint_as_float(r[e]) / l : 0.f;
-          const int dim = i * 128 + t;
-          if (num_splits == 1) {
-            out[((size_t)b * Hq + head) * kDv + dim] = __float2bfloat16(o);
-          } else {
-            float* w = ws + (((size_t)b * Hq + head) * num_splits + split) * (kDv + 1);
-            w[dim] = o;
-            if (dim == 0) w[kDv] = (have && l > 0.f) ? m_used[h] + log2f(l) : -INFINITY;
-          }
+      for (int hc = 0; hc < CW; ++hc) {
+        const int hh = c + hc, h = h0 + hh, head = grp * NH + h;
+        if (head >= Hq) continue;
+        const float l = lsum[h];
+        const float val = (have && l > 0.f) ? o[hc] / l : 0.f;
+        const int dim = i * 128 + t;
+        if (num_splits == 1) {
+          out[((size_t)b * Hq + head) * kDv + dim] = __float2bfloat16(val);
+        } else {
+          float* w = ws + (((size_t)b * Hq + head) * num_splits + split) * (kDv + 1);
+          w[dim] = val;
+          if (dim == 0) w[kDv] = (have && l > 0.f) ? m_used[h] + log2f(l) : -INFINITY;
         }
       }
     }
