@@ -18,11 +18,12 @@
 //   * TMA (no multicast) brings one cache block per box into a ring of 32 KB stages: per
 //     128-key tile, five stages of 128 latent dims for S, then four stages of the 512 value
 //     dims again for P.V (the second read of a tile comes from L2);
-//   * one thread issues TMA, one issues MMAs, four softmax warps own the 128 TMEM lanes
-//     (lane = key for S, lane = value dim for O): per-head maxima are reduced across lanes
-//     with warp shuffles and shared memory, O is rescaled lazily (only when a head's running
-//     maximum grows by more than 2^8, FlashAttention-4's rule), P goes to shared memory as the
-//     K-major B operand of the P.V MMA;
+//   * one thread issues TMA, one issues MMAs (S of the next tile while the softmax of this one
+//     runs, from a second S buffer), two softmax warpgroups own the 128 TMEM lanes (lane = key
+//     for S, lane = value dim for O), each for half of the tile's heads: per-head maxima are
+//     reduced across lanes with a transposing warp butterfly and shared memory, O is rescaled
+//     lazily (only when a head's running maximum grows by more than 2^8, FlashAttention-4's
+//     rule), P goes to shared memory as the B operand of the P.V MMA (MN-major for 64 heads);
 //   * split-KV over 128-key tiles, merged by a log-sum-exp combine kernel.
 // Every mbarrier wait is bounded and records kWaitTimeout in `status`.
 #include <algorithm>
