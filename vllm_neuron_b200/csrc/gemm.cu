@@ -701,11 +701,12 @@ static double tile_cost(int nt) { return 1.0 + 0.5 * (256 - nt) / 128.0; }
 // split: for decode widths (NT <= 64) across a cluster of 2 / 4 / 8 CTAs that reduce over
 // DSMEM, chosen by a small cost model (rounds of tiles x stages per split, plus a reduction
 // cost); for wider tiles with vector atomics (at least 8 stages per split, at most 4 splits).
-static Plan make_plan(int T, int N, int K, int max_splits, bool allow_cluster = true, bool f8 = false) {
+static Plan make_plan(int T, int N, int K, int max_splits, bool allow_cluster = true, bool f8 = false,
+                      int sms_override = 0) {
   Plan p;
   p.nt = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
   p.m_tiles = cdiv(N, kBM);
-  const int sms = sm_count();
+  const int sms = sms_override > 0 ? sms_override : sm_count();
   if (p.nt == 256) {
     // wide tiles: the width whose busiest SM does the least work (waves x width x the width's
     // relative cost), so the last wave is not left mostly idle (184 tiles of 256 tokens on 148
@@ -758,6 +759,10 @@ static Plan make_plan(int T, int N, int K, int max_splits, bool allow_cluster = 
     p.splits = cdiv(p.k_stages, p.sps);
   }
   return p;
+}
+
+static Plan make_plan_on(int T, int N, int K, int max_splits, int sms) {
+  return make_plan(T, N, K, max_splits, true, false, sms);
 }
 
 static unsigned long long* g_trace = nullptr;  // set by b200_gemm_set_trace (analysis only)
@@ -942,6 +947,17 @@ extern "C" int b200_gemm_bf16_scatter(void* const* dst, int n_dst, int ldd, cons
 }
 
 extern "C" size_t b200_red_region_bytes(int T_cap, int H_cap) { return red_region_bytes(T_cap, H_cap); }
+
+// The planner's decision for a bf16 GEMM of this shape on `sms` SMs (0: the current device's count):
+// out[0..4] = token tile width, output tiles, K splits, cluster split (0/1), k stages per split.
+extern "C" void b200_gemm_plan(int T, int N, int K, int max_splits, int sms, int* out) {
+  const Plan p = make_plan_on(T, N, K, max_splits, sms);
+  out[0] = p.nt;
+  out[1] = p.m_tiles * p.n_tiles;
+  out[2] = p.splits;
+  out[3] = p.cluster ? 1 : 0;
+  out[4] = p.sps;
+}
 
 // Force the token tile width of later non-cluster plans (0 restores the planner's choice).
 extern "C" void b200_gemm_force_nt(int nt) { g_forced_nt = valid_nt(nt); }

@@ -10,6 +10,7 @@ int b200_gemm_bf16(void* y, int ldy, int out_f32, const void* x, int ldx, const 
                    int N, int K, float* ws, int64_t ws_floats, int* counters, int64_t n_counters, int max_splits,
                    int* status, cudaStream_t s);
 void b200_gemm_force_nt(int nt);
+void b200_gemm_plan(int T, int N, int K, int max_splits, int sms, int* out);
 int b200_gemm_bf16_scatter(void* const* dst, int n_dst, int ldd, const void* x, int ldx, const void* w, int T, int N,
                            int K, float* ws, int64_t ws_floats, int* counters, int64_t n_counters, int max_splits,
                            int* status, cudaStream_t s);
@@ -84,6 +85,13 @@ void gemm_scatter(at::IntArrayRef dst, int64_t ldd, Tensor x, Tensor w, Tensor w
 }
 
 void gemm_force_nt(int64_t nt) { b200_gemm_force_nt((int)nt); }
+
+// The planner's decision: [token tile width, output tiles, K splits, cluster split, k stages per split].
+std::vector<int64_t> gemm_plan(int64_t T, int64_t N, int64_t K, int64_t max_splits, int64_t sms) {
+  int o[5];
+  b200_gemm_plan(T, N, K, max_splits, sms, o);
+  return {o[0], o[1], o[2], o[3], o[4]};
+}
 
 void gemm_fp8(Tensor y, Tensor x, Tensor w, c10::optional<Tensor> bias, Tensor alpha, Tensor ws, Tensor counters,
               int64_t max_splits, c10::optional<Tensor> status) {
@@ -215,6 +223,7 @@ void register_gemm_ops(torch::Library& m) {
   m.def("red_region_bytes(int T_cap, int H_cap) -> int");
   m.def("gemm_set_trace(int buf) -> ()");
   m.def("gemm_force_nt(int nt) -> ()");
+  m.def("gemm_plan(int T, int N, int K, int max_splits, int sms) -> int[]");
   m.def(
       "gemm_bf16_allreduce(Tensor x, Tensor w, int red_uc, int red_mc, int T_cap, int H_cap, int max_splits, "
       "Tensor? status) -> int");
@@ -238,4 +247,5 @@ void register_gemm_cpu_impls(torch::Library& m) {
   m.impl("red_region_bytes", &red_region_bytes);
   m.impl("gemm_set_trace", &gemm_set_trace);
   m.impl("gemm_force_nt", &gemm_force_nt);
+  m.impl("gemm_plan", &gemm_plan);
 }
