@@ -114,12 +114,16 @@ class ClockSampler:
 def run_reference(args) -> None:
     """The reference is a Trainium plugin: its model and functional packages import the
     Neuron SDK (``nki``) at module level and its package init hides every CUDA device."""
-    sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    sys.path.insert(0, ref_dir)
     reason = None
+    if not os.path.isdir(os.path.join(ref_dir, "vllm_neuron")):
+        reason = ("the reference is not installed in baseline/_ref on this machine (pip install --no-deps "
+                  "--target baseline/_ref of the reference tree); it targets AWS Trainium and cannot run on B200")
     try:
         import vllm_neuron.functional  # noqa: F401
     except Exception as e:  # noqa: BLE001
-        reason = (f"the reference installs (baseline/_ref) but cannot run on B200: "
+        reason = reason or (f"the reference installs (baseline/_ref) but cannot run on B200: "
                   f"importing vllm_neuron.functional fails ({type(e).__name__}: {e}); it targets AWS Trainium "
                   f"(NKI kernels, neuronx-cc) and sets CUDA_VISIBLE_DEVICES='' at import")
     rank = int(os.environ.get("RANK", "0"))
