@@ -58,8 +58,9 @@ GPT_OSS_120B = {
 GPT_OSS_20B = dict(GPT_OSS_120B, num_hidden_layers=24, num_local_experts=32,
                    layer_types=["sliding_attention" if i % 2 == 0 else "full_attention" for i in range(24)])
 METRIC = "output tok/s at fixed concurrency (GPT-OSS-120B, 8×B200); p50 TTFT / TPOT"
-# Device-timed value of ``--baseline-of-record`` on a B200 of this pool, per (model, GPUs),
-# the numbers BASELINE.md records (the reference publishes none); vs_baseline = value / it.
+# Device-timed value of ``--baseline-of-record`` (this framework with cuBLAS dense layers and NCCL
+# collectives) measured on a B200, per (model, GPUs); the reference publishes no number for this
+# configuration.  vs_baseline = value / it.
 BASELINE_OF_RECORD: dict = {("gpt-oss-120b", 1): 3325.27}
 
 

@@ -3,7 +3,7 @@
 A background thread owns the :class:`LLMEngine` and loops ``step()`` while requests are
 in flight; API handlers submit requests through a thread-safe queue and receive
 per-request outputs on asyncio queues.  This is the role vLLM's AsyncLLM / EngineCore
-play for the Trainium plugin, collapsed into one process since the
+play for the Trainium plugin (its engine-core loop), collapsed into one process since the
 scheduler is deterministic and SPMD across ranks.
 """
 
